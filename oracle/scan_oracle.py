@@ -1,0 +1,372 @@
+"""CPU oracle for the Mamba-3 scan hot path (test infrastructure only).
+
+This module is the checker, never the product: only ``tests/``, ``__graft_entry__.smoke()``
+and ``bench.py``'s CPU-baseline leg may import it. It restates, in float64 numpy, the
+algorithm of the upstream package Aiyoniganmaaiya/mamba3-ssm v0.2.1:
+
+* ``siso_scan_fwd``  -- ``mamba3_ssm/ops.py:142-177`` (decay/dt/sigmoid precompute at
+  ``ops.py:146-148``, the per-timestep blend/update/readout loop at ``ops.py:166-175``).
+* ``mimo_scan_fwd``  -- ``mamba3_ssm/ops.py:202-242``.
+* ``siso_scan_bwd`` / ``mimo_scan_bwd`` -- the exact adjoints of the two loops above. The
+  reference has no backward kernel; its gradients come from autograd through the loops,
+  and the golden fixtures record those gradients.
+* ``rmsnorm`` (``ops.py:96-104``), ``apply_rope`` (``ops.py:116-119``).
+* ``mamba3_forward`` (``mamba3_ssm/layer.py:168-266``), ``mamba3_step``
+  (``layer.py:272-374``), ``allocate_inference_cache`` (``layer.py:380-412``).
+* ``lm_forward`` / ``lm_step`` (``mamba3_ssm/block.py:93-139``).
+
+Parity pin: every function here is checked against fixtures recorded from the reference
+itself (``tests/golden/make_golden.py`` runs the reference's CPU loops and autograd and
+writes ``tests/golden/*.npz``; ``tests/test_oracle_golden.py`` compares).
+
+Notation: B batch, L seqlen, H heads, P headdim, D d_state, R mimo rank, S rope angles.
+All arrays are float64 numpy arrays in the reference layouts: x (B,L,H,P); SISO B/C
+(B,L,H,D); MIMO B/C (B,L,R,H,D); ADT/DT/trap (B,L,H); D (H); mimo_x/mimo_o (H,R,P).
+"""
+
+import numpy as np
+
+f64 = np.float64
+
+
+def sigmoid(v):
+    return 1.0 / (1.0 + np.exp(-v))
+
+
+def softplus(v):
+    """torch.nn.functional.softplus with beta=1, threshold=20."""
+    v = np.asarray(v, dtype=f64)
+    return np.where(v > 20.0, v, np.log1p(np.exp(np.minimum(v, 20.0))))
+
+
+def _coeffs(ADT, DT, trap):
+    """decay a_t = exp(ADT) and the blend weights of ops.py:171-173 written as
+    h_t = a_t h_{t-1} + beta_t u_t + gamma_t u_{t-1}, u_t = x_t (x) B_t:
+    beta = dt (1 - tr) + dt tr / 2, gamma = dt tr / 2, tr = sigmoid(trap)."""
+    a = np.exp(ADT.astype(f64))
+    dt = DT.astype(f64)
+    tr = sigmoid(trap.astype(f64))
+    beta = dt * (1.0 - tr) + 0.5 * dt * tr
+    gamma = 0.5 * dt * tr
+    return a, dt, tr, beta, gamma
+
+
+# ----------------------------------------------------------------------------------
+# SISO
+# ----------------------------------------------------------------------------------
+
+def siso_scan_fwd(x, B, C, ADT, DT, trap, D, h0=None, bx0=None):
+    """ops.py:161-177. Returns (y (B,L,H,P), h_last (B,H,P,D), bx_last (B,H,P,D)).
+    ``h0``/``bx0`` are the optional carried states (the reference starts from zeros)."""
+    x = x.astype(f64); B = B.astype(f64); C = C.astype(f64)
+    Bn, L, H, P = x.shape
+    Ds = B.shape[-1]
+    a, dt, tr, _, _ = _coeffs(ADT, DT, trap)
+    h = np.zeros((Bn, H, P, Ds)) if h0 is None else h0.astype(f64).copy()
+    bxp = np.zeros((Bn, H, P, Ds)) if bx0 is None else bx0.astype(f64).copy()
+    y = np.empty((Bn, L, H, P))
+    Dw = D.astype(f64)[None, :, None]
+    for t in range(L):
+        xt = x[:, t]
+        bx = xt[..., :, None] * B[:, t][..., None, :]
+        trt = tr[:, t][..., None, None]
+        blend = (1.0 - trt) * bx + trt * 0.5 * (bx + bxp)
+        h = a[:, t][..., None, None] * h + dt[:, t][..., None, None] * blend
+        y[:, t] = np.einsum("bhd,bhpd->bhp", C[:, t], h) + Dw * xt
+        bxp = bx
+    return y, h, bxp
+
+
+def siso_scan_bwd(x, B, C, ADT, DT, trap, D, dy, h0=None, bx0=None):
+    """Adjoint of ``siso_scan_fwd`` (the gradients autograd returns through
+    ops.py:166-175). Stores every state, so keep it to small cases.
+    Returns dict dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0."""
+    x = x.astype(f64); B = B.astype(f64); C = C.astype(f64); dy = dy.astype(f64)
+    Bn, L, H, P = x.shape
+    Ds = B.shape[-1]
+    a, dt, tr, beta, gamma = _coeffs(ADT, DT, trap)
+    hs = np.empty((L + 1, Bn, H, P, Ds))
+    us = np.empty((L + 1, Bn, H, P, Ds))
+    hs[0] = 0.0 if h0 is None else h0
+    us[0] = 0.0 if bx0 is None else bx0
+    for t in range(L):
+        u = x[:, t][..., :, None] * B[:, t][..., None, :]
+        us[t + 1] = u
+        hs[t + 1] = (a[:, t][..., None, None] * hs[t] + beta[:, t][..., None, None] * u
+                     + gamma[:, t][..., None, None] * us[t])
+    dx = np.empty_like(x); dB = np.empty_like(B); dC = np.empty_like(C)
+    dADT = np.empty((Bn, L, H)); dDT = np.empty((Bn, L, H)); dtrap = np.empty((Bn, L, H))
+    dD = np.zeros(H)
+    g_next = np.zeros((Bn, H, P, Ds))
+    a_next = np.zeros((Bn, H))
+    gam_next = np.zeros((Bn, H))
+    for t in range(L - 1, -1, -1):
+        g = a_next[..., None, None] * g_next + dy[:, t][..., :, None] * C[:, t][..., None, :]
+        dC[:, t] = np.einsum("bhp,bhpd->bhd", dy[:, t], hs[t + 1])
+        v = beta[:, t][..., None, None] * g + gam_next[..., None, None] * g_next
+        dx[:, t] = D[None, :, None] * dy[:, t] + np.einsum("bhpd,bhd->bhp", v, B[:, t])
+        dB[:, t] = np.einsum("bhpd,bhp->bhd", v, x[:, t])
+        dbeta = np.einsum("bhpd,bhpd->bh", g, us[t + 1])
+        dgam = np.einsum("bhpd,bhpd->bh", g, us[t])
+        da = np.einsum("bhpd,bhpd->bh", g, hs[t])
+        dADT[:, t] = da * a[:, t]
+        trt = tr[:, t]
+        dDT[:, t] = dbeta * (1.0 - 0.5 * trt) + dgam * 0.5 * trt
+        dtrap[:, t] = 0.5 * dt[:, t] * (dgam - dbeta) * trt * (1.0 - trt)
+        dD += np.einsum("bhp,bhp->h", dy[:, t], x[:, t])
+        g_next = g
+        a_next = a[:, t]
+        gam_next = gamma[:, t]
+    dh0 = a_next[..., None, None] * g_next
+    dbx0 = gam_next[..., None, None] * g_next
+    return dict(dx=dx, dB=dB, dC=dC, dADT=dADT, dDT=dDT, dtrap=dtrap, dD=dD,
+                dh0=dh0, dbx0=dbx0)
+
+
+# ----------------------------------------------------------------------------------
+# MIMO
+# ----------------------------------------------------------------------------------
+
+def mimo_scan_fwd(x, B, C, ADT, DT, trap, D, mimo_x, mimo_o, h0=None, bx0=None):
+    """ops.py:222-242. B/C are (B,L,R,H,D); the state is one scalar per (b,h,d).
+    Returns (y (B,L,H,P), h_last (B,H,D), bx_last (B,H,D))."""
+    x = x.astype(f64); B = B.astype(f64); C = C.astype(f64)
+    mx = mimo_x.astype(f64); mo = mimo_o.astype(f64)
+    Bn, L, H, P = x.shape
+    Ds = B.shape[-1]
+    a, dt, tr, _, _ = _coeffs(ADT, DT, trap)
+    h = np.zeros((Bn, H, Ds)) if h0 is None else h0.astype(f64).copy()
+    bxp = np.zeros((Bn, H, Ds)) if bx0 is None else bx0.astype(f64).copy()
+    y = np.empty((Bn, L, H, P))
+    Dw = D.astype(f64)
+    for t in range(L):
+        xr = np.einsum("bhp,hrp->bhr", x[:, t], mx)
+        bx = np.einsum("bhr,brhd->bhd", xr, B[:, t])
+        trt = tr[:, t][..., None]
+        blend = (1.0 - trt) * bx + trt * 0.5 * (bx + bxp)
+        h = a[:, t][..., None] * h + dt[:, t][..., None] * blend
+        yr = np.einsum("brhd,bhd->bhr", C[:, t], h) + Dw[None, :, None] * xr
+        y[:, t] = np.einsum("bhr,hrp->bhp", yr, mo)
+        bxp = bx
+    return y, h, bxp
+
+
+def mimo_scan_bwd(x, B, C, ADT, DT, trap, D, mimo_x, mimo_o, dy, h0=None, bx0=None):
+    """Adjoint of ``mimo_scan_fwd``. Returns dict dx, dB, dC, dADT, dDT, dtrap, dD,
+    dmimo_x, dmimo_o, dh0, dbx0."""
+    x = x.astype(f64); B = B.astype(f64); C = C.astype(f64); dy = dy.astype(f64)
+    mx = mimo_x.astype(f64); mo = mimo_o.astype(f64)
+    Bn, L, H, P = x.shape
+    Ds = B.shape[-1]
+    a, dt, tr, beta, gamma = _coeffs(ADT, DT, trap)
+    xr = np.einsum("blhp,hrp->blhr", x, mx)
+    bx = np.einsum("blhr,blrhd->blhd", xr, B)
+    hs = np.empty((L + 1, Bn, H, Ds))
+    us = np.empty((L + 1, Bn, H, Ds))
+    hs[0] = 0.0 if h0 is None else h0
+    us[0] = 0.0 if bx0 is None else bx0
+    for t in range(L):
+        us[t + 1] = bx[:, t]
+        hs[t + 1] = (a[:, t][..., None] * hs[t] + beta[:, t][..., None] * bx[:, t]
+                     + gamma[:, t][..., None] * us[t])
+    Dw = D.astype(f64)
+    yr = np.einsum("blrhd,lbhd->blhr", C, hs[1:]) + Dw[None, None, :, None] * xr
+    dmo = np.einsum("blhr,blhp->hrp", yr, dy)
+    dyr = np.einsum("blhp,hrp->blhr", dy, mo)
+    dD = np.einsum("blhr,blhr->h", dyr, xr)
+    dC = np.einsum("blhr,lbhd->blrhd", dyr, hs[1:])
+    dxr = Dw[None, None, :, None] * dyr
+    dB = np.empty_like(B)
+    dADT = np.empty((Bn, L, H)); dDT = np.empty((Bn, L, H)); dtrap = np.empty((Bn, L, H))
+    g_next = np.zeros((Bn, H, Ds))
+    a_next = np.zeros((Bn, H))
+    gam_next = np.zeros((Bn, H))
+    for t in range(L - 1, -1, -1):
+        g = a_next[..., None] * g_next + np.einsum("bhr,brhd->bhd", dyr[:, t], C[:, t])
+        v = beta[:, t][..., None] * g + gam_next[..., None] * g_next
+        dxr[:, t] += np.einsum("bhd,brhd->bhr", v, B[:, t])
+        dB[:, t] = np.einsum("bhr,bhd->brhd", xr[:, t], v)
+        dbeta = np.einsum("bhd,bhd->bh", g, us[t + 1])
+        dgam = np.einsum("bhd,bhd->bh", g, us[t])
+        da = np.einsum("bhd,bhd->bh", g, hs[t])
+        dADT[:, t] = da * a[:, t]
+        trt = tr[:, t]
+        dDT[:, t] = dbeta * (1.0 - 0.5 * trt) + dgam * 0.5 * trt
+        dtrap[:, t] = 0.5 * dt[:, t] * (dgam - dbeta) * trt * (1.0 - trt)
+        g_next = g
+        a_next = a[:, t]
+        gam_next = gamma[:, t]
+    dx = np.einsum("blhr,hrp->blhp", dxr, mx)
+    dmx = np.einsum("blhr,blhp->hrp", dxr, x)
+    return dict(dx=dx, dB=dB, dC=dC, dADT=dADT, dDT=dDT, dtrap=dtrap, dD=dD,
+                dmimo_x=dmx, dmimo_o=dmo,
+                dh0=a_next[..., None] * g_next, dbx0=gam_next[..., None] * g_next)
+
+
+# ----------------------------------------------------------------------------------
+# Layer / LM restatement
+# ----------------------------------------------------------------------------------
+
+def rmsnorm(x, w, eps=1e-5):
+    """ops.py:102-104."""
+    x = x.astype(f64)
+    rms = np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
+    return x / rms * w.astype(f64)
+
+
+def apply_rope(x, ang):
+    """ops.py:116-119: rotate interleaved pairs (x[0::2], x[1::2]) by ``ang``."""
+    c, s = np.cos(ang), np.sin(ang)
+    x1, x2 = x[..., 0::2], x[..., 1::2]
+    out = np.empty_like(x, dtype=f64)
+    out[..., 0::2] = x1 * c - x2 * s
+    out[..., 1::2] = x1 * s + x2 * c
+    return out
+
+
+class LayerDims:
+    """Dimension bookkeeping of layer.py:82-115."""
+
+    def __init__(self, d_model, d_state=128, expand=2, headdim=64, ngroups=1,
+                 rope_fraction=0.5, is_mimo=False, mimo_rank=4, A_floor=1e-4, **_):
+        self.d_model = int(d_model)
+        self.d_state = int(d_state)
+        self.headdim = int(headdim)
+        self.ngroups = int(ngroups)
+        self.is_mimo = bool(is_mimo)
+        self.R = int(mimo_rank) if self.is_mimo else 1
+        self.d_inner = int(expand * d_model)
+        self.H = self.d_inner // self.headdim
+        split = int(self.d_state * float(rope_fraction))
+        if split % 2:
+            split -= 1
+        self.split = split
+        self.S = split // 2
+        self.A_floor = float(A_floor)
+        self.d_in_proj = 2 * self.d_inner + 2 * self.d_state * self.ngroups * self.R + 3 * self.H + self.S
+
+    def split_proj(self, zxbc):
+        """torch.split order [z | x | B | C | dt | A | trap | angle] (layer.py:182-191)."""
+        sizes = [self.d_inner, self.d_inner, self.d_state * self.ngroups * self.R,
+                 self.d_state * self.ngroups * self.R, self.H, self.H, self.H, self.S]
+        out, o = [], 0
+        for s in sizes:
+            out.append(zxbc[..., o:o + s])
+            o += s
+        return out
+
+
+def _bc_heads(dims, raw, norm_w, bias, lead):
+    """RMSNorm over D per (r, g), broadcast groups to heads, add per-head bias
+    (layer.py:214-225). raw (..., R*G*D) -> (..., R, H, D)."""
+    R, G, Ds, H = dims.R, dims.ngroups, dims.d_state, dims.H
+    r = raw.reshape(*lead, R, G, Ds)
+    n = rmsnorm(r, norm_w)
+    n = np.broadcast_to(n, (*lead, R, H, Ds)) if G == 1 else np.repeat(n, H // G, axis=-2)
+    return n + np.swapaxes(bias.astype(f64), 0, 1)  # bias (H,R,D) -> (R,H,D)
+
+
+def _rope_bc(dims, bc, ang):
+    """Rotate the first split dims of (..., R, H, D) by angles (..., H, S) (layer.py:236-244)."""
+    a = np.broadcast_to(ang[..., None, :, :], (*bc.shape[:-1], dims.S))
+    out = bc.copy()
+    out[..., :dims.split] = apply_rope(bc[..., :dims.split], a)
+    return out
+
+
+def mamba3_forward(w, dims, u):
+    """layer.py:168-266 in float64. ``w`` maps state_dict names to arrays."""
+    u = u.astype(f64)
+    Bn, L, _ = u.shape
+    allp = u @ w["in_proj.weight"].astype(f64).T
+    z, x, Braw, Craw, ddt, dA, trap, angr = dims.split_proj(allp)
+    z = z.reshape(Bn, L, dims.H, dims.headdim)
+    x = x.reshape(Bn, L, dims.H, dims.headdim)
+    # layer.py:207 reads -(softplus(dd_A).clamp(max=-A_floor)); since softplus > 0 the
+    # clamp always yields -A_floor, so A == +A_floor for every input (kept as written).
+    A = -np.minimum(softplus(dA), -dims.A_floor)
+    DT = softplus(ddt + w["dt_bias"].astype(f64))
+    ADT = A * DT
+    Bh = _bc_heads(dims, Braw, w["B_norm.weight"], w["B_bias"], (Bn, L))
+    Ch = _bc_heads(dims, Craw, w["C_norm.weight"], w["C_bias"], (Bn, L))
+    ang = np.cumsum(angr[:, :, None, :] * DT[..., None], axis=1)  # (B,L,H,S)
+    Bp = _rope_bc(dims, Bh, ang)
+    Cp = _rope_bc(dims, Ch, ang)
+    if dims.is_mimo:
+        y, _, _ = mimo_scan_fwd(x, Bp, Cp, ADT, DT, trap, w["D"], w["mimo_x"], w["mimo_o"])
+    else:
+        y, _, _ = siso_scan_fwd(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, w["D"])
+    y = y * (z * sigmoid(z))
+    y = y.reshape(Bn, L, dims.d_inner)
+    return y @ w["out_proj.weight"].astype(f64).T
+
+
+def allocate_inference_cache(dims, batch):
+    """layer.py:380-412."""
+    ang = np.zeros((batch, dims.H, dims.S))
+    if dims.is_mimo:
+        return ang, np.zeros((batch, dims.H, dims.d_state)), np.zeros((batch, dims.H, dims.d_state))
+    shp = (batch, dims.H, dims.headdim, dims.d_state)
+    return ang, np.zeros(shp), np.zeros(shp)
+
+
+def mamba3_step(w, dims, u, angle, ssm, bxp):
+    """layer.py:272-374 in float64. Returns (out, angle, ssm, bx_prev), new arrays."""
+    u = u.astype(f64)
+    Bn = u.shape[0]
+    allp = u @ w["in_proj.weight"].astype(f64).T
+    z, x, Braw, Craw, ddt, dA, trap, angr = dims.split_proj(allp)
+    z = z.reshape(Bn, dims.H, dims.headdim)
+    x = x.reshape(Bn, dims.H, dims.headdim)
+    A = -np.minimum(softplus(dA), -dims.A_floor)  # layer.py:317, same clamp as forward
+    DT = softplus(ddt + w["dt_bias"].astype(f64))
+    tr = sigmoid(trap)
+    Bh = _bc_heads(dims, Braw, w["B_norm.weight"], w["B_bias"], (Bn,))
+    Ch = _bc_heads(dims, Craw, w["C_norm.weight"], w["C_bias"], (Bn,))
+    angle = angle.astype(f64) + angr[:, None, :] * DT[..., None]
+    Bp = _rope_bc(dims, Bh, angle)
+    Cp = _rope_bc(dims, Ch, angle)
+    decay = np.exp(A * DT)
+    if dims.is_mimo:
+        xr = np.einsum("bhp,hrp->bhr", x, w["mimo_x"].astype(f64))
+        bx = np.einsum("bhr,brhd->bhd", xr, Bp)
+        tre = tr[..., None]
+        blend = (1.0 - tre) * bx + tre * 0.5 * (bx + bxp)
+        ssm = decay[..., None] * ssm + DT[..., None] * blend
+        yr = np.einsum("brhd,bhd->brh", Cp, ssm) + w["D"].astype(f64)[None, None, :] * np.swapaxes(xr, 1, 2)
+        y = np.einsum("brh,hrp->bhp", yr, w["mimo_o"].astype(f64))
+    else:
+        bx = x[..., :, None] * Bp[:, 0][..., None, :]
+        tre = tr[..., None, None]
+        blend = (1.0 - tre) * bx + tre * 0.5 * (bx + bxp)
+        ssm = decay[..., None, None] * ssm + DT[..., None, None] * blend
+        y = np.einsum("bhd,bhpd->bhp", Cp[:, 0], ssm) + w["D"].astype(f64)[None, :, None] * x
+    y = y * (z * sigmoid(z))
+    out = y.reshape(Bn, dims.d_inner) @ w["out_proj.weight"].astype(f64).T
+    return out, angle, ssm, bx
+
+
+def _layer_weights(w, i):
+    pre = f"layers.{i}.mixer."
+    return {k[len(pre):]: v for k, v in w.items() if k.startswith(pre)}
+
+
+def lm_forward(w, dims, n_layer, ids):
+    """block.py:93-101 (tied lm_head, d_intermediate = 0)."""
+    x = w["embedding.weight"].astype(f64)[ids]
+    for i in range(n_layer):
+        x = x + mamba3_forward(_layer_weights(w, i), dims, rmsnorm(x, w[f"layers.{i}.norm.weight"]))
+    x = rmsnorm(x, w["norm_f.weight"])
+    return x @ w["lm_head.weight"].astype(f64).T
+
+
+def lm_step(w, dims, n_layer, ids, cache):
+    """block.py:110-139. ``cache`` is a list of (angle, ssm, bx) per layer."""
+    x = w["embedding.weight"].astype(f64)[ids.reshape(-1)]
+    new = []
+    for i in range(n_layer):
+        out, a, s, b = mamba3_step(_layer_weights(w, i), dims, rmsnorm(x, w[f"layers.{i}.norm.weight"]), *cache[i])
+        x = x + out
+        new.append((a, s, b))
+    x = rmsnorm(x, w["norm_f.weight"])
+    return x @ w["lm_head.weight"].astype(f64).T, new
