@@ -1,0 +1,356 @@
+"""Benchmark of the Mamba-3 scan hot path on B200.
+
+Headline workload (one "step"): the raw SISO scan op ``ssm_scan_siso`` forward at long
+context, bf16 I/O: B=16, H=64, P=64, D=128, L=32768 (x, B, C ~ N(0,1); dt =
+clamp(softplus(N(-3, 0.5)), 1e-3, 0.1); A = -exp(U(0, ln 16)) per head; ADT = A dt;
+trap = sigmoid(N(0,1)) passed as the op's logit; B and C rotated by RoPE with angles
+cumsum(dt) * 10000^(-2i/D) on the first D/2 dims). Synthetic inputs, seeded per rank.
+The batch is sharded across ranks (one process per GPU, torchrun), so the total work is
+fixed as N grows; no collective runs inside the scan.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0. ``value`` = tokens (B*L positions, all heads) per second
+for the whole job, timed on the device with CUDA events (max over ranks); ``e2e`` is the
+same metric through the public API with the inputs copied from pinned host memory and y
+copied back every step; ``roofline`` relates the scan kernel's algorithmic bytes to the
+measured HBM copy bandwidth; ``cpu_baseline`` times the fp32 C restatement of the
+reference's CPU loop on a bounded sample (rank 0, N=1).
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mamba3-ssm_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.nn.functional as F  # noqa: E402
+
+C5 = dict(batch=16, seqlen=32768, nheads=64, headdim=64, dstate=128)
+METRIC = "scan tokens/s (SISO scan fwd, B=16 H=64 P=64 D=128 L=32768, bf16)"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algorithmic_bytes_per_unit(e=2, P=64, D=128):
+    """Bytes one (b, l, h) position must move: x, y (P each), B, C (D each) in the I/O
+    dtype, plus ADT, DT, trap in fp32."""
+    return e * (2 * P + 2 * D) + 12
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ----------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ----------------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.idx = ",".join(str(i) for i in gpu_indices)
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.idx, "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.th.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------
+# inputs
+# ----------------------------------------------------------------------------------
+def make_inputs(batch, L, H, P, D, device, seed):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    bf = torch.bfloat16
+    x = torch.empty(batch, L, H, P, dtype=bf, device=device)
+    Bm = torch.empty(batch, L, H, D, dtype=bf, device=device)
+    Cm = torch.empty(batch, L, H, D, dtype=bf, device=device)
+    dt = F.softplus(torch.randn(batch, L, H, generator=g, device=device) * 0.5 - 3.0).clamp(1e-3, 0.1)
+    A = -torch.exp(torch.rand(H, generator=g, device=device) * math.log(16.0))
+    ADT = (A * dt).contiguous()
+    trap = torch.sigmoid(torch.randn(batch, L, H, generator=g, device=device))
+    Dw = torch.randn(H, generator=g, device=device) * 0.5 + 1.0
+    S = D // 4
+    theta = 10000.0 ** (-2.0 * torch.arange(S, device=device, dtype=torch.float32) / D)
+    for b in range(batch):
+        x[b] = torch.randn(L, H, P, generator=g, device=device).to(bf)
+        ang = torch.cumsum(dt[b], dim=0).unsqueeze(-1) * theta  # (L, H, S)
+        c, s = torch.cos(ang), torch.sin(ang)
+        for dst in (Bm, Cm):
+            v = torch.randn(L, H, D, generator=g, device=device)
+            v1, v2 = v[..., 0:2 * S:2].clone(), v[..., 1:2 * S:2].clone()
+            v[..., 0:2 * S:2] = v1 * c - v2 * s
+            v[..., 1:2 * S:2] = v1 * s + v2 * c
+            dst[b] = v.to(bf)
+    return x, Bm, Cm, ADT, dt.contiguous(), trap.contiguous(), Dw
+
+
+# ----------------------------------------------------------------------------------
+# CPU baseline: fp32 C restatement of the reference loop, bounded sample
+# ----------------------------------------------------------------------------------
+def cpu_sample(L_sample, nb=1, H=64, P=64, D=128, seed=7):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((nb, L_sample, H, P), dtype=np.float32)
+    Bm = rng.standard_normal((nb, L_sample, H, D), dtype=np.float32)
+    Cm = rng.standard_normal((nb, L_sample, H, D), dtype=np.float32)
+    dt = np.clip(np.log1p(np.exp(rng.normal(-3, 0.5, (nb, L_sample, H)))), 1e-3, 0.1).astype(np.float32)
+    A = -np.exp(rng.uniform(0, np.log(16), H)).astype(np.float32)
+    trap = (1 / (1 + np.exp(-rng.standard_normal((nb, L_sample, H))))).astype(np.float32)
+    return x, Bm, Cm, (A * dt).astype(np.float32), dt, trap, np.ones(H, np.float32)
+
+
+def cpu_baseline(target_s=8.0):
+    from oracle import cpu_ref
+    cores = cpu_ref.max_threads()
+    L_s = 64
+    while True:
+        args = cpu_sample(L_s)
+        t0 = time.perf_counter()
+        cpu_ref.siso_fwd(*args, nthreads=cores)
+        dt = time.perf_counter() - t0
+        if dt >= target_s or L_s >= C5["seqlen"]:
+            break
+        L_s = min(C5["seqlen"], L_s * max(2, int(target_s / max(dt, 1e-3) * 0.8)))
+    tok_s = L_s / dt  # one batch row over all 64 heads: L_s token positions
+    return {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"fp32 C restatement of the reference loop (oracle/scan_ref.c), OpenMP over (b,h); "
+                      f"1 batch row x 64 heads x {L_s} positions (P=64, D=128) of the long-context "
+                      f"workload in {dt:.2f} s"}, L_s
+
+
+def workload_config(world):
+    return {"workload": "raw SISO scan op forward, long context (ssm_scan_siso)", "batch": C5["batch"],
+            "seq_len": C5["seqlen"], "nheads": C5["nheads"], "headdim": C5["headdim"], "d_state": C5["dstate"],
+            "parallelism": f"batch-sharded x{world}", "l2": "inputs (26 GB) larger than L2"}
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import cpu_ref
+    cores = cpu_ref.max_threads()
+    # size one step to about 2 s of CPU work
+    base, L_s = cpu_baseline(target_s=2.0)
+    sample = cpu_sample(L_s)
+    for _ in range(args.warmup):
+        cpu_ref.siso_fwd(*sample, nthreads=cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_ref.siso_fwd(*sample, nthreads=cores)
+    el = time.perf_counter() - t0
+    v = args.steps * L_s / el
+    base["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": workload_config(world),
+            "cpu_baseline": base,
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py: no CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+
+    from mamba3_ssm import ssm_scan_siso
+    from mamba3_ssm import _lib
+    _lib.load()
+
+    Bt, L, H, P, D = C5["batch"], C5["seqlen"], C5["nheads"], C5["headdim"], C5["dstate"]
+    if Bt % world:
+        raise SystemExit("bench.py: batch 16 must divide by the number of GPUs")
+    Bl = Bt // world
+    x, Bm, Cm, ADT, DT, trap, Dw = make_inputs(Bl, L, H, P, D, dev, 1234 + rank)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    def step():
+        return ssm_scan_siso(x, Bm, Cm, ADT, DT, trap, Dw)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    K = args.steps
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    t_beg, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    t_beg.record()
+    for i in range(K):
+        evs[i][0].record()
+        y = step()
+        evs[i][1].record()
+    t_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    total_ms = t_beg.elapsed_time(t_end)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    tt = torch.tensor([total_ms, kern_ms], device=dev, dtype=torch.float64)
+    if pg is not None:
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+    total_ms, kern_ms = float(tt[0]), float(tt[1])
+    ms_step = total_ms / K
+    tokens = Bt * L
+    value = tokens / (ms_step / 1e3)
+
+    hbm, peak_kind = peaks()
+    unit_bytes = algorithmic_bytes_per_unit()
+    launch_bytes = unit_bytes * Bl * L * H
+    achieved = launch_bytes / (kern_ms / 1e3) / 1e9
+    tr = measured_traffic().get("siso_scan_fwd")
+    traffic = tr["bytes_per_unit"] * Bl * L * H if tr else None
+
+    # e2e through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hosts = []
+        for t in (x, Bm, Cm, ADT, DT, trap):
+            h_ = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            h_.copy_(t)
+            hosts.append(h_)
+        y_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        h2d = sum(h.numel() * h.element_size() for h in hosts)
+        d2h = y_host.numel() * y_host.element_size()
+        Ke = min(K, 3)
+        devs = (x, Bm, Cm, ADT, DT, trap)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(Ke):
+            for d_, h_ in zip(devs, hosts):
+                d_.copy_(h_, non_blocking=True)
+            yy = ssm_scan_siso(x, Bm, Cm, ADT, DT, trap, Dw)
+            y_host.copy_(yy, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        et = torch.tensor([e0.elapsed_time(e1) / Ke], device=dev, dtype=torch.float64)
+        if pg is not None:
+            pg.all_reduce(et, op=pg.ReduceOp.MAX)
+        e2e = {"value": tokens / (float(et[0]) / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+               "d2h_bytes_per_step": d2h * world, "steps": Ke}
+        del hosts, y_host
+
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base, _ = cpu_baseline()
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+                "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": workload_config(world),
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                             "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
+                             "algorithmic_bytes_per_launch": launch_bytes, "kernel_ms": kern_ms},
+                "cpu_baseline": base, "e2e": e2e, "gpu_launches": K, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,170 @@
+/*
+ * mamba3_b200.h -- C ABI of the B200 (sm_100a) Mamba-3 scan library (libmamba3_b200.so).
+ *
+ * Every entry point takes plain device pointers wrapped in m3_tensor descriptors (shape +
+ * element strides), launches on the caller's CUDA stream and returns an m3_status; the
+ * text of the last error on the calling thread is available from m3_last_error_string().
+ * Nothing here allocates device memory: the caller owns every input, output and
+ * workspace buffer. Host (CPU) pointers are rejected; there is no CPU fallback.
+ *
+ * Reference interfaces replaced (upstream Aiyoniganmaaiya/mamba3-ssm v0.2.1):
+ *   - the pybind functions siso_scan / mimo_state built by load_inline
+ *     (mamba3_ssm/cuda_backend.py:319-356) and their raw launchers
+ *     (cuda_backend.py:236-301), reached from ssm_scan_siso / ssm_scan_mimo
+ *     (mamba3_ssm/ops.py:126-242);
+ *   - the per-token recurrence written in PyTorch inside Mamba3.step
+ *     (mamba3_ssm/layer.py:296-371), which has no native boundary upstream.
+ *
+ * Layout conventions (reference layouts, innermost dimension contiguous):
+ *   x, y, dx, dy     (B, L, H, P)        f32 / bf16 / f16
+ *   SISO B, C        (B, L, H, D)        f32 / bf16 / f16
+ *   MIMO B, C        (B, L, R, H, D)     f32 / bf16 / f16
+ *   ADT, DT, trap    (B, L, H)           f32, any strides (trap is a logit: the kernels
+ *                                        apply the sigmoid, as ops.py:148 does)
+ *   D                (H)                 f32
+ *   mimo_x, mimo_o   (H, R, P)           f32 / bf16
+ *   SISO states      (B, H, P, D)        f32 contiguous
+ *   MIMO states      (B, H, D)           f32 contiguous
+ */
+#ifndef MAMBA3_B200_H
+#define MAMBA3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define M3_ABI_VERSION 1
+#define M3_MAX_DIMS 6
+
+typedef enum m3_dtype {
+  M3_FLOAT32 = 0,
+  M3_BFLOAT16 = 1,
+  M3_FLOAT16 = 2
+} m3_dtype;
+
+typedef enum m3_status {
+  M3_OK = 0,
+  M3_ERR_INVALID_ARGUMENT = 1, /* shape, stride, dtype or pointer problem            */
+  M3_ERR_UNSUPPORTED = 2,      /* valid request outside the compiled kernel variants  */
+  M3_ERR_CUDA = 3,             /* a CUDA runtime call or kernel launch failed         */
+  M3_ERR_WORKSPACE = 4         /* workspace missing or too small                      */
+} m3_status;
+
+/* A strided view of device memory. data == NULL marks an absent optional argument. */
+typedef struct m3_tensor {
+  void* data;
+  int32_t dtype; /* m3_dtype */
+  int32_t ndim;
+  int64_t shape[M3_MAX_DIMS];
+  int64_t stride[M3_MAX_DIMS]; /* in elements */
+} m3_tensor;
+
+/* Dimensions of one Mamba3 mixer (mamba3_ssm/layer.py:82-115). */
+typedef struct m3_layer_dims {
+  int32_t d_model;
+  int32_t d_inner;         /* expand * d_model                                */
+  int32_t nheads;          /* H = d_inner / headdim                            */
+  int32_t headdim;         /* P                                                */
+  int32_t d_state;         /* D                                                */
+  int32_t ngroups;         /* G (B/C groups broadcast to heads)                */
+  int32_t mimo_rank;       /* R (1 for SISO)                                   */
+  int32_t num_rope_angles; /* S = split / 2                                    */
+  int32_t rope_split;      /* leading state dims that rotate (even)            */
+  float A_floor;           /* layer.py:207                                     */
+  float norm_eps;          /* RMSNorm eps of B_norm / C_norm (ops.py:97)       */
+} m3_layer_dims;
+
+/* ---------------------------------------------------------------------------------
+ * Library information
+ * ------------------------------------------------------------------------------- */
+int m3_abi_version(void);
+const char* m3_last_error_string(void);
+
+/* ---------------------------------------------------------------------------------
+ * SISO scan, forward.  Replaces siso_scan(x, B, C, decay, dt, tr, D)
+ * (cuda_backend.py:319-336 -> siso_scan_launcher :236-267 -> siso_scan_kernel :35-111)
+ * as called by ssm_scan_siso (ops.py:126-177); unlike the reference it takes ADT and
+ * the trap logit and applies exp / sigmoid itself (ops.py:146-148).
+ *   y[b,t,h,:] = h_t C_t + D[h] x_t,  h_t = e^{ADT} h_{t-1} + DT*blend(x_t B_t, x_{t-1}B_{t-1})
+ * h0, bx0      optional initial state / previous B*x (B,H,P,D) f32; absent = zeros.
+ * h_last, bx_last  optional outputs (B,H,P,D) f32: state and B*x after the last step
+ *              (the decode-cache pair of layer.py:284-285).
+ * ------------------------------------------------------------------------------- */
+int m3_siso_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                     const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,
+                     const m3_tensor* D, const m3_tensor* h0, const m3_tensor* bx0,
+                     m3_tensor* y, m3_tensor* h_last, m3_tensor* bx_last, void* stream);
+
+/* SISO scan, backward. The reference has no backward kernel (its CUDA tier drops the
+ * gradient; cuda_backend.py:327); this returns the gradients autograd produces through
+ * the loop of ops.py:166-175.
+ * workspace: f32 buffer of at least m3_siso_scan_bwd_workspace_size() bytes.
+ * dD (H) f32 is overwritten. dh0 / dbx0 optional (B,H,P,D) f32 outputs. */
+size_t m3_siso_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads,
+                                       int64_t headdim, int64_t dstate);
+int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                     const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,
+                     const m3_tensor* D, const m3_tensor* h0, const m3_tensor* bx0,
+                     const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB, m3_tensor* dC,
+                     m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD,
+                     m3_tensor* dh0, m3_tensor* dbx0, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * MIMO scan, forward.  Replaces mimo_state_cuda (cuda_backend.py:419-463: einsum ->
+ * mimo_state(x_mixed, ...) :339-356 -> mimo_state_kernel :123-204 -> einsum) as called
+ * by ssm_scan_mimo (ops.py:184-242). The rank-R projections through mimo_x / mimo_o
+ * and the D skip are fused into the same kernel.
+ * ------------------------------------------------------------------------------- */
+int m3_mimo_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                     const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,
+                     const m3_tensor* D, const m3_tensor* mimo_x, const m3_tensor* mimo_o,
+                     const m3_tensor* h0, const m3_tensor* bx0, m3_tensor* y,
+                     m3_tensor* h_last, m3_tensor* bx_last, void* stream);
+
+/* MIMO scan, backward (gradients of ops.py:226-240). dD, dmimo_x, dmimo_o are f32 and
+ * overwritten. */
+size_t m3_mimo_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads,
+                                       int64_t headdim, int64_t dstate, int64_t rank);
+int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                     const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,
+                     const m3_tensor* D, const m3_tensor* mimo_x, const m3_tensor* mimo_o,
+                     const m3_tensor* h0, const m3_tensor* bx0, const m3_tensor* dy,
+                     m3_tensor* dx, m3_tensor* dB, m3_tensor* dC, m3_tensor* dADT,
+                     m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dmimo_x,
+                     m3_tensor* dmimo_o, m3_tensor* dh0, m3_tensor* dbx0, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Single-token decode step of one Mamba3 mixer, everything between in_proj and out_proj
+ * of Mamba3.step (layer.py:298-371) in one kernel: split of the in_proj row, softplus /
+ * clamp / sigmoid, RMSNorm + bias of B and C, angle update and RoPE, the state update,
+ * the C.h readout, the D skip, (MIMO) the rank projections, and the silu(z) gate.
+ *   zxbcdt      (batch, d_in_proj) in_proj output, f32 / bf16 / f16
+ *   dt_bias (H) f32;  B_bias, C_bias (H, R, D) f32;  B_norm_w, C_norm_w (D) f32;  Dskip (H) f32
+ *   mimo_x, mimo_o (H, R, P) (MIMO only)
+ *   angle_in/out (batch, H, S) f32;  ssm_in/out, bx_in/out: SISO (batch,H,P,D), MIMO (batch,H,D) f32
+ *               (an output may alias its input: the update is then in place)
+ *   y_gated     (batch, d_inner), dtype of zxbcdt: y * silu(z), the out_proj input.
+ * ------------------------------------------------------------------------------- */
+int m3_siso_step(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
+                 const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                 const m3_tensor* C_norm_w, const m3_tensor* Dskip, const m3_tensor* angle_in,
+                 const m3_tensor* ssm_in, const m3_tensor* bx_in, m3_tensor* angle_out,
+                 m3_tensor* ssm_out, m3_tensor* bx_out, m3_tensor* y_gated, void* stream);
+
+int m3_mimo_step(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
+                 const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                 const m3_tensor* C_norm_w, const m3_tensor* Dskip, const m3_tensor* mimo_x,
+                 const m3_tensor* mimo_o, const m3_tensor* angle_in, const m3_tensor* ssm_in,
+                 const m3_tensor* bx_in, m3_tensor* angle_out, m3_tensor* ssm_out,
+                 m3_tensor* bx_out, m3_tensor* y_gated, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA3_B200_H */

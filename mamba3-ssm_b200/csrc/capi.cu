@@ -1,0 +1,460 @@
+// extern "C" entry points of libmamba3_b200: argument validation, dispatch to the
+// kernels, and the thread-local error string. Nothing here allocates device memory.
+#include <cstdio>
+#include <string>
+
+#include "decode_step.cuh"
+#include "m3_common.cuh"
+#include "mimo_scan.cuh"
+#include "siso_chunk.cuh"
+#include "siso_scan.cuh"
+
+namespace m3 {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return M3_OK;
+}
+
+namespace {
+
+constexpr unsigned kAnyFloat = (1u << M3_FLOAT32) | (1u << M3_BFLOAT16) | (1u << M3_FLOAT16);
+constexpr unsigned kF32 = 1u << M3_FLOAT32;
+
+std::string shape_str(const m3_tensor* t) {
+  std::string s = "(";
+  for (int i = 0; i < t->ndim; ++i) s += std::to_string(t->shape[i]) + (i + 1 < t->ndim ? "," : "");
+  return s + ")";
+}
+
+bool present(const m3_tensor* t) { return t != nullptr && t->data != nullptr; }
+
+int check_device_ptr(const void* p, const char* name) {
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": not a CUDA pointer (" + cudaGetErrorString(e) + ")");
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+    return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": host memory is not accepted (no CPU path)");
+  return M3_OK;
+}
+
+// shape must match `shape` (entries < 0 are free); dtype in `mask`; innermost stride 1
+// unless the dim has extent 1; `contig` requires the full row-major layout.
+int check(const m3_tensor* t, const char* name, int ndim, const int64_t* shape, unsigned mask,
+          bool contig, bool optional, bool devcheck) {
+  if (!present(t)) {
+    if (optional) return M3_OK;
+    return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": missing");
+  }
+  if (t->ndim != ndim)
+    return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": expected " + std::to_string(ndim) +
+                                             " dims, got " + std::to_string(t->ndim));
+  for (int i = 0; i < ndim; ++i)
+    if (shape[i] >= 0 && t->shape[i] != shape[i]) {
+      std::string want = "(";
+      for (int j = 0; j < ndim; ++j) want += (shape[j] >= 0 ? std::to_string(shape[j]) : std::string("*")) + (j + 1 < ndim ? "," : "");
+      return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": shape " + shape_str(t) + " != " + want + ")");
+    }
+  if (t->dtype < 0 || t->dtype > 2 || !(mask & (1u << t->dtype)))
+    return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": unsupported dtype " + std::to_string(t->dtype));
+  if (ndim > 0 && t->shape[ndim - 1] > 1 && t->stride[ndim - 1] != 1)
+    return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": innermost dimension must be contiguous");
+  if (contig) {
+    int64_t st = 1;
+    for (int i = ndim - 1; i >= 0; --i) {
+      if (t->shape[i] > 1 && t->stride[i] != st)
+        return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": must be contiguous");
+      st *= t->shape[i];
+    }
+  }
+  for (int i = 0; i < ndim; ++i)
+    if (t->stride[i] < 0) return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": negative stride");
+  if (devcheck) return check_device_ptr(t->data, name);
+  return M3_OK;
+}
+
+// strides of dims (0,1,2) of a 4-d view
+Str3 s3(const m3_tensor* t) { return Str3{t->stride[0], t->stride[1], t->stride[2]}; }
+Str3 s3_scal(const m3_tensor* t) { return Str3{t->stride[0], t->stride[1], t->stride[2]}; }
+Str4 s4(const m3_tensor* t) { return Str4{t->stride[0], t->stride[1], t->stride[2], t->stride[3]}; }
+
+int64_t numel(const m3_tensor* t) {
+  int64_t n = 1;
+  for (int i = 0; i < t->ndim; ++i) n *= t->shape[i];
+  return n;
+}
+
+template <typename T>
+T* fptr(const m3_tensor* t) { return present(t) ? reinterpret_cast<T*>(t->data) : nullptr; }
+
+int memset_async(void* p, size_t bytes, cudaStream_t s, const char* what) {
+  if (!p || bytes == 0) return M3_OK;
+  cudaError_t e = cudaMemsetAsync(p, 0, bytes, s);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return M3_OK;
+}
+
+int copy_or_zero(void* dst, const void* src, size_t bytes, cudaStream_t s, const char* what) {
+  if (!dst || bytes == 0) return M3_OK;
+  cudaError_t e = src ? cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s) : cudaMemsetAsync(dst, 0, bytes, s);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return M3_OK;
+}
+
+// Shared checks of the scan operands. bc_ndim 4 (SISO) or 5 (MIMO).
+int check_scan_inputs(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                      const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, int bc_ndim,
+                      int64_t* Bn, int64_t* L, int64_t* H, int64_t* P, int64_t* Ds, int64_t* R) {
+  if (!present(x)) return fail(M3_ERR_INVALID_ARGUMENT, "x: missing");
+  if (x->ndim != 4) return fail(M3_ERR_INVALID_ARGUMENT, "x: expected (B, L, H, P)");
+  *Bn = x->shape[0]; *L = x->shape[1]; *H = x->shape[2]; *P = x->shape[3];
+  if (!present(B) || B->ndim != bc_ndim) return fail(M3_ERR_INVALID_ARGUMENT, bc_ndim == 4 ? "B: expected (B, L, H, D)" : "B: expected (B, L, R, H, D)");
+  *Ds = B->shape[bc_ndim - 1];
+  *R = bc_ndim == 5 ? B->shape[2] : 1;
+  const bool empty = (*Bn) * (*L) * (*H) * (*P) == 0;
+  const int64_t xs[4] = {*Bn, *L, *H, *P};
+  M3_TRY(check(x, "x", 4, xs, kAnyFloat, false, false, !empty));
+  if (bc_ndim == 4) {
+    const int64_t bs[4] = {*Bn, *L, *H, *Ds};
+    M3_TRY(check(B, "B", 4, bs, kAnyFloat, false, false, !empty));
+    M3_TRY(check(C, "C", 4, bs, 1u << B->dtype, false, false, !empty));
+  } else {
+    const int64_t bs[5] = {*Bn, *L, *R, *H, *Ds};
+    M3_TRY(check(B, "B", 5, bs, kAnyFloat, false, false, !empty));
+    M3_TRY(check(C, "C", 5, bs, 1u << B->dtype, false, false, !empty));
+  }
+  const int64_t ss[3] = {*Bn, *L, *H};
+  M3_TRY(check(ADT, "ADT", 3, ss, kF32, false, false, false));
+  M3_TRY(check(DT, "DT", 3, ss, kF32, false, false, false));
+  M3_TRY(check(trap, "trap", 3, ss, kF32, false, false, false));
+  const int64_t hs[1] = {*H};
+  if (!present(D) || D->ndim != 1 || D->shape[0] != *H || D->dtype != M3_FLOAT32)
+    return fail(M3_ERR_INVALID_ARGUMENT, "D: expected (H) float32");
+  (void)hs;
+  if (*Ds <= 0 && !empty) return fail(M3_ERR_INVALID_ARGUMENT, "B: d_state must be positive");
+  return M3_OK;
+}
+
+}  // namespace
+}  // namespace m3
+
+using namespace m3;
+
+extern "C" {
+
+int m3_abi_version(void) { return M3_ABI_VERSION; }
+
+const char* m3_last_error_string(void) { return g_last_error.c_str(); }
+
+int m3_siso_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                     const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* h0,
+                     const m3_tensor* bx0, m3_tensor* y, m3_tensor* h_last, m3_tensor* bx_last, void* stream) {
+  int64_t Bn, L, H, P, Ds, R;
+  M3_TRY(check_scan_inputs(x, B, C, ADT, DT, trap, D, 4, &Bn, &L, &H, &P, &Ds, &R));
+  const int64_t xs[4] = {Bn, L, H, P}, st[4] = {Bn, H, P, Ds};
+  const bool empty = Bn * L * H * P == 0;
+  M3_TRY(check(y, "y", 4, xs, 1u << x->dtype, false, false, !empty));
+  M3_TRY(check(h0, "h0", 4, st, kF32, true, true, false));
+  M3_TRY(check(bx0, "bx0", 4, st, kF32, true, true, false));
+  M3_TRY(check(h_last, "h_last", 4, st, kF32, true, true, false));
+  M3_TRY(check(bx_last, "bx_last", 4, st, kF32, true, true, false));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (Bn * H * P * Ds == 0) return M3_OK;
+  if (L == 0) {
+    const size_t bytes = sizeof(float) * Bn * H * P * Ds;
+    M3_TRY(copy_or_zero(fptr<void>(h_last), fptr<void>(h0), bytes, s, "h_last"));
+    return copy_or_zero(fptr<void>(bx_last), fptr<void>(bx0), bytes, s, "bx_last");
+  }
+  if (Bn > INT32_MAX || L > INT32_MAX || H > INT32_MAX || P > 65535)
+    return fail(M3_ERR_UNSUPPORTED, "siso scan: dimension too large");
+  SisoParams p{};
+  p.Bn = (int)Bn; p.L = (int)L; p.H = (int)H; p.P = (int)P; p.D = (int)Ds;
+  p.x = x->data; p.sx = s3(x);
+  p.Bm = B->data; p.sB = s3(B);
+  p.Cm = C->data; p.sC = s3(C);
+  p.adt = fptr<const float>(ADT); p.sadt = s3_scal(ADT);
+  p.dt = fptr<const float>(DT); p.sdt = s3_scal(DT);
+  p.trap = fptr<const float>(trap); p.strap = s3_scal(trap);
+  p.Dskip = fptr<const float>(D); p.sD = D->stride[0];
+  p.h0 = fptr<const float>(h0); p.bx0 = fptr<const float>(bx0);
+  p.y = y->data; p.sy = s3(y);
+  p.h_last = fptr<float>(h_last); p.bx_last = fptr<float>(bx_last);
+  if (siso_chunk_supported(p, x->dtype, B->dtype)) return launch_siso_fwd_chunked(p, x->dtype, B->dtype, s);
+  return launch_siso_fwd_recurrent(p, x->dtype, B->dtype, s);
+}
+
+size_t m3_siso_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                                       int64_t dstate) {
+  (void)headdim; (void)dstate;
+  return sizeof(float) * (size_t)(batch * nheads * seqlen);
+}
+
+int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                     const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* h0,
+                     const m3_tensor* bx0, const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB, m3_tensor* dC,
+                     m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dh0,
+                     m3_tensor* dbx0, void* workspace, size_t workspace_bytes, void* stream) {
+  int64_t Bn, L, H, P, Ds, R;
+  M3_TRY(check_scan_inputs(x, B, C, ADT, DT, trap, D, 4, &Bn, &L, &H, &P, &Ds, &R));
+  const bool empty = Bn * L * H * P == 0;
+  const int64_t xs[4] = {Bn, L, H, P}, bs[4] = {Bn, L, H, Ds}, st[4] = {Bn, H, P, Ds}, ss[3] = {Bn, L, H}, hs[1] = {H};
+  M3_TRY(check(h0, "h0", 4, st, kF32, true, true, false));
+  M3_TRY(check(bx0, "bx0", 4, st, kF32, true, true, false));
+  M3_TRY(check(dy, "dy", 4, xs, 1u << x->dtype, false, false, !empty));
+  M3_TRY(check(dx, "dx", 4, xs, 1u << x->dtype, false, false, !empty));
+  M3_TRY(check(dB, "dB", 4, bs, 1u << B->dtype, false, false, !empty));
+  M3_TRY(check(dC, "dC", 4, bs, 1u << B->dtype, false, false, !empty));
+  M3_TRY(check(dADT, "dADT", 3, ss, kF32, false, false, false));
+  M3_TRY(check(dDT, "dDT", 3, ss, kF32, false, false, false));
+  M3_TRY(check(dtrap, "dtrap", 3, ss, kF32, false, false, false));
+  M3_TRY(check(dD, "dD", 1, hs, kF32, true, false, false));
+  M3_TRY(check(dh0, "dh0", 4, st, kF32, true, true, false));
+  M3_TRY(check(dbx0, "dbx0", 4, st, kF32, true, true, false));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  M3_TRY(memset_async(dD->data, sizeof(float) * H, s, "dD"));
+  if (Bn * H * P * Ds == 0) return M3_OK;
+  if (L == 0) {
+    const size_t bytes = sizeof(float) * Bn * H * P * Ds;
+    M3_TRY(copy_or_zero(fptr<void>(dh0), nullptr, bytes, s, "dh0"));
+    return copy_or_zero(fptr<void>(dbx0), nullptr, bytes, s, "dbx0");
+  }
+  const size_t need = m3_siso_scan_bwd_workspace_size(Bn, L, H, P, Ds);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(M3_ERR_WORKSPACE, "siso backward: workspace of " + std::to_string(need) + " bytes required");
+  SisoParams p{};
+  p.Bn = (int)Bn; p.L = (int)L; p.H = (int)H; p.P = (int)P; p.D = (int)Ds;
+  p.x = x->data; p.sx = s3(x);
+  p.Bm = B->data; p.sB = s3(B);
+  p.Cm = C->data; p.sC = s3(C);
+  p.adt = fptr<const float>(ADT); p.sadt = s3_scal(ADT);
+  p.dt = fptr<const float>(DT); p.sdt = s3_scal(DT);
+  p.trap = fptr<const float>(trap); p.strap = s3_scal(trap);
+  p.Dskip = fptr<const float>(D); p.sD = D->stride[0];
+  p.h0 = fptr<const float>(h0); p.bx0 = fptr<const float>(bx0);
+  p.dy = dy->data; p.sdy = s3(dy);
+  p.dx = dx->data; p.sdx = s3(dx);
+  p.dB = dB->data; p.sdB = s3(dB);
+  p.dC = dC->data; p.sdC = s3(dC);
+  p.dadt = fptr<float>(dADT); p.sdadt = s3_scal(dADT);
+  p.ddt = fptr<float>(dDT); p.sddt = s3_scal(dDT);
+  p.dtrap = fptr<float>(dtrap); p.sdtrap = s3_scal(dtrap);
+  p.dD = fptr<float>(dD);
+  p.dh0 = fptr<float>(dh0); p.dbx0 = fptr<float>(dbx0);
+  p.q = reinterpret_cast<float*>(workspace);
+  return launch_siso_bwd_recurrent(p, x->dtype, B->dtype, s);
+}
+
+static int fill_mimo(MimoParams& p, const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                     const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D,
+                     const m3_tensor* mimo_x, const m3_tensor* mimo_o, const m3_tensor* h0,
+                     const m3_tensor* bx0, int64_t* dims) {
+  int64_t Bn, L, H, P, Ds, R;
+  M3_TRY(check_scan_inputs(x, B, C, ADT, DT, trap, D, 5, &Bn, &L, &H, &P, &Ds, &R));
+  const int64_t ms[3] = {H, R, P}, st[3] = {Bn, H, Ds};
+  M3_TRY(check(mimo_x, "mimo_x", 3, ms, kF32, false, false, false));
+  M3_TRY(check(mimo_o, "mimo_o", 3, ms, kF32, false, false, false));
+  M3_TRY(check(h0, "h0", 3, st, kF32, true, true, false));
+  M3_TRY(check(bx0, "bx0", 3, st, kF32, true, true, false));
+  if (Bn > INT32_MAX || L > INT32_MAX || H > INT32_MAX || P > 65535 || R > 8)
+    return fail(M3_ERR_UNSUPPORTED, "mimo scan: dimension too large (rank must be <= 8)");
+  p.Bn = (int)Bn; p.L = (int)L; p.H = (int)H; p.P = (int)P; p.D = (int)Ds; p.R = (int)R;
+  p.x = x->data; p.sx = s3(x);
+  p.Bm = B->data; p.sB = s4(B);
+  p.Cm = C->data; p.sC = s4(C);
+  p.adt = fptr<const float>(ADT); p.sadt = s3_scal(ADT);
+  p.dt = fptr<const float>(DT); p.sdt = s3_scal(DT);
+  p.trap = fptr<const float>(trap); p.strap = s3_scal(trap);
+  p.Dskip = fptr<const float>(D); p.sD = D->stride[0];
+  p.mimo_x = fptr<const float>(mimo_x); p.smx_h = mimo_x->stride[0]; p.smx_r = mimo_x->stride[1];
+  p.mimo_o = fptr<const float>(mimo_o); p.smo_h = mimo_o->stride[0]; p.smo_r = mimo_o->stride[1];
+  p.h0 = fptr<const float>(h0); p.bx0 = fptr<const float>(bx0);
+  dims[0] = Bn; dims[1] = L; dims[2] = H; dims[3] = P; dims[4] = Ds; dims[5] = R;
+  return M3_OK;
+}
+
+int m3_mimo_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                     const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* mimo_x,
+                     const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, m3_tensor* y,
+                     m3_tensor* h_last, m3_tensor* bx_last, void* stream) {
+  MimoParams p{};
+  int64_t d[6];
+  M3_TRY(fill_mimo(p, x, B, C, ADT, DT, trap, D, mimo_x, mimo_o, h0, bx0, d));
+  const int64_t xs[4] = {d[0], d[1], d[2], d[3]}, st[3] = {d[0], d[2], d[4]};
+  const bool empty = d[0] * d[1] * d[2] * d[3] == 0;
+  M3_TRY(check(y, "y", 4, xs, 1u << x->dtype, false, false, !empty));
+  M3_TRY(check(h_last, "h_last", 3, st, kF32, true, true, false));
+  M3_TRY(check(bx_last, "bx_last", 3, st, kF32, true, true, false));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (d[0] * d[2] * d[4] == 0) return M3_OK;
+  if (d[1] == 0 || d[3] == 0) {
+    const size_t bytes = sizeof(float) * d[0] * d[2] * d[4];
+    if (d[1] == 0) {
+      M3_TRY(copy_or_zero(fptr<void>(h_last), fptr<void>(h0), bytes, s, "h_last"));
+      return copy_or_zero(fptr<void>(bx_last), fptr<void>(bx0), bytes, s, "bx_last");
+    }
+  }
+  p.y = y->data; p.sy = s3(y);
+  p.h_last = fptr<float>(h_last); p.bx_last = fptr<float>(bx_last);
+  return launch_mimo(p, x->dtype, B->dtype, false, s);
+}
+
+size_t m3_mimo_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                                       int64_t dstate, int64_t rank) {
+  return sizeof(float) * mimo_bwd_workspace_floats(batch, seqlen, nheads, headdim, dstate, rank);
+}
+
+int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                     const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* mimo_x,
+                     const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, const m3_tensor* dy,
+                     m3_tensor* dx, m3_tensor* dB, m3_tensor* dC, m3_tensor* dADT, m3_tensor* dDT,
+                     m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dmimo_x, m3_tensor* dmimo_o, m3_tensor* dh0,
+                     m3_tensor* dbx0, void* workspace, size_t workspace_bytes, void* stream) {
+  MimoParams p{};
+  int64_t d[6];
+  M3_TRY(fill_mimo(p, x, B, C, ADT, DT, trap, D, mimo_x, mimo_o, h0, bx0, d));
+  const int64_t Bn = d[0], L = d[1], H = d[2], P = d[3], Ds = d[4], R = d[5];
+  const bool empty = Bn * L * H * P == 0;
+  const int64_t xs[4] = {Bn, L, H, P}, bs[5] = {Bn, L, R, H, Ds}, ss[3] = {Bn, L, H}, hs[1] = {H},
+                ms[3] = {H, R, P}, st[3] = {Bn, H, Ds};
+  M3_TRY(check(dy, "dy", 4, xs, 1u << x->dtype, false, false, !empty));
+  M3_TRY(check(dx, "dx", 4, xs, 1u << x->dtype, false, false, !empty));
+  M3_TRY(check(dB, "dB", 5, bs, 1u << B->dtype, false, false, !empty));
+  M3_TRY(check(dC, "dC", 5, bs, 1u << B->dtype, false, false, !empty));
+  M3_TRY(check(dADT, "dADT", 3, ss, kF32, false, false, false));
+  M3_TRY(check(dDT, "dDT", 3, ss, kF32, false, false, false));
+  M3_TRY(check(dtrap, "dtrap", 3, ss, kF32, false, false, false));
+  M3_TRY(check(dD, "dD", 1, hs, kF32, true, false, false));
+  M3_TRY(check(dmimo_x, "dmimo_x", 3, ms, kF32, true, false, false));
+  M3_TRY(check(dmimo_o, "dmimo_o", 3, ms, kF32, true, false, false));
+  M3_TRY(check(dh0, "dh0", 3, st, kF32, true, true, false));
+  M3_TRY(check(dbx0, "dbx0", 3, st, kF32, true, true, false));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  M3_TRY(memset_async(dD->data, sizeof(float) * H, s, "dD"));
+  M3_TRY(memset_async(dmimo_x->data, sizeof(float) * H * R * P, s, "dmimo_x"));
+  M3_TRY(memset_async(dmimo_o->data, sizeof(float) * H * R * P, s, "dmimo_o"));
+  if (Bn * H * Ds == 0) return M3_OK;
+  if (L == 0) {
+    const size_t bytes = sizeof(float) * Bn * H * Ds;
+    M3_TRY(copy_or_zero(fptr<void>(dh0), nullptr, bytes, s, "dh0"));
+    return copy_or_zero(fptr<void>(dbx0), nullptr, bytes, s, "dbx0");
+  }
+  const size_t need = m3_mimo_scan_bwd_workspace_size(Bn, L, H, P, Ds, R);
+  if (need == 0) return fail(M3_ERR_UNSUPPORTED, "mimo backward: shapes too large for shared memory");
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(M3_ERR_WORKSPACE, "mimo backward: workspace of " + std::to_string(need) + " bytes required");
+  p.dy = dy->data; p.sdy = s3(dy);
+  p.dx = dx->data; p.sdx = s3(dx);
+  p.dB = dB->data; p.sdB = s4(dB);
+  p.dC = dC->data; p.sdC = s4(dC);
+  p.dadt = fptr<float>(dADT); p.sdadt = s3_scal(dADT);
+  p.ddt = fptr<float>(dDT); p.sddt = s3_scal(dDT);
+  p.dtrap = fptr<float>(dtrap); p.sdtrap = s3_scal(dtrap);
+  p.dD = fptr<float>(dD);
+  p.dmx = fptr<float>(dmimo_x); p.dmo = fptr<float>(dmimo_o);
+  p.dh0 = fptr<float>(dh0); p.dbx0 = fptr<float>(dbx0);
+  p.work = reinterpret_cast<float*>(workspace);
+  return launch_mimo(p, x->dtype, B->dtype, true, s);
+}
+
+static int step_common(bool mimo, const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
+                       const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                       const m3_tensor* C_norm_w, const m3_tensor* Dskip, const m3_tensor* mimo_x,
+                       const m3_tensor* mimo_o, const m3_tensor* angle_in, const m3_tensor* ssm_in,
+                       const m3_tensor* bx_in, m3_tensor* angle_out, m3_tensor* ssm_out, m3_tensor* bx_out,
+                       m3_tensor* y_gated, void* stream) {
+  if (!dims) return fail(M3_ERR_INVALID_ARGUMENT, "dims: missing");
+  const int64_t H = dims->nheads, P = dims->headdim, Ds = dims->d_state, G = dims->ngroups,
+                R = mimo ? dims->mimo_rank : 1, S = dims->num_rope_angles, di = dims->d_inner;
+  if (H <= 0 || P <= 0 || Ds <= 0 || G <= 0 || R <= 0 || S < 0 || di != H * P || dims->rope_split != 2 * S ||
+      dims->rope_split > Ds || (G != 1 && G != H))
+    return fail(M3_ERR_INVALID_ARGUMENT, "dims: inconsistent layer dimensions");
+  if (!mimo && dims->mimo_rank != 1) return fail(M3_ERR_INVALID_ARGUMENT, "dims: SISO step needs mimo_rank 1");
+  if (!present(zxbcdt) || zxbcdt->ndim != 2) return fail(M3_ERR_INVALID_ARGUMENT, "zxbcdt: expected (batch, d_in_proj)");
+  const int64_t Bn = zxbcdt->shape[0];
+  const int64_t dproj = 2 * di + 2 * Ds * G * R + 3 * H + S;
+  const int64_t zs[2] = {Bn, dproj}, ys[2] = {Bn, di}, h1[1] = {H}, hrd[3] = {H, R, Ds}, d1[1] = {Ds},
+                hrp[3] = {H, R, P}, as[3] = {Bn, H, S};
+  M3_TRY(check(zxbcdt, "zxbcdt", 2, zs, kAnyFloat, false, false, Bn > 0));
+  M3_TRY(check(y_gated, "y_gated", 2, ys, 1u << zxbcdt->dtype, false, false, false));
+  M3_TRY(check(dt_bias, "dt_bias", 1, h1, kF32, true, false, false));
+  M3_TRY(check(B_bias, "B_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(C_bias, "C_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(B_norm_w, "B_norm_w", 1, d1, kF32, true, false, false));
+  M3_TRY(check(C_norm_w, "C_norm_w", 1, d1, kF32, true, false, false));
+  M3_TRY(check(Dskip, "D", 1, h1, kF32, true, false, false));
+  if (mimo) {
+    M3_TRY(check(mimo_x, "mimo_x", 3, hrp, kF32, true, false, false));
+    M3_TRY(check(mimo_o, "mimo_o", 3, hrp, kF32, true, false, false));
+  }
+  if (S > 0) {
+    M3_TRY(check(angle_in, "angle_in", 3, as, kF32, true, false, false));
+    M3_TRY(check(angle_out, "angle_out", 3, as, kF32, true, false, false));
+  }
+  if (mimo) {
+    const int64_t st[3] = {Bn, H, Ds};
+    M3_TRY(check(ssm_in, "ssm_in", 3, st, kF32, true, false, false));
+    M3_TRY(check(bx_in, "bx_in", 3, st, kF32, true, false, false));
+    M3_TRY(check(ssm_out, "ssm_out", 3, st, kF32, true, false, false));
+    M3_TRY(check(bx_out, "bx_out", 3, st, kF32, true, false, false));
+  } else {
+    const int64_t st[4] = {Bn, H, P, Ds};
+    M3_TRY(check(ssm_in, "ssm_in", 4, st, kF32, true, false, false));
+    M3_TRY(check(bx_in, "bx_in", 4, st, kF32, true, false, false));
+    M3_TRY(check(ssm_out, "ssm_out", 4, st, kF32, true, false, false));
+    M3_TRY(check(bx_out, "bx_out", 4, st, kF32, true, false, false));
+  }
+  if (Bn == 0) return M3_OK;
+  if (!mimo) {
+    for (const m3_tensor* t : {ssm_in, bx_in, (const m3_tensor*)ssm_out, (const m3_tensor*)bx_out})
+      if (reinterpret_cast<uintptr_t>(t->data) % 16 != 0)
+        return fail(M3_ERR_INVALID_ARGUMENT, "siso step: state buffers must be 16-byte aligned");
+  }
+  StepParams p{};
+  p.Bn = (int)Bn; p.H = (int)H; p.P = (int)P; p.D = (int)Ds; p.R = (int)R; p.G = (int)G; p.S = (int)S;
+  p.split = dims->rope_split; p.d_inner = (int)di; p.A_floor = dims->A_floor; p.eps = dims->norm_eps;
+  p.zxbcdt = zxbcdt->data; p.s_row = zxbcdt->stride[0];
+  p.dt_bias = fptr<const float>(dt_bias);
+  p.B_bias = fptr<const float>(B_bias); p.C_bias = fptr<const float>(C_bias);
+  p.B_norm_w = fptr<const float>(B_norm_w); p.C_norm_w = fptr<const float>(C_norm_w);
+  p.Dskip = fptr<const float>(Dskip);
+  p.mimo_x = mimo ? fptr<const float>(mimo_x) : nullptr;
+  p.mimo_o = mimo ? fptr<const float>(mimo_o) : nullptr;
+  p.angle_in = S > 0 ? fptr<const float>(angle_in) : nullptr;
+  p.angle_out = S > 0 ? fptr<float>(angle_out) : nullptr;
+  p.ssm_in = fptr<const float>(ssm_in); p.ssm_out = fptr<float>(ssm_out);
+  p.bx_in = fptr<const float>(bx_in); p.bx_out = fptr<float>(bx_out);
+  p.y = y_gated->data; p.s_y = y_gated->stride[0];
+  return launch_step(p, zxbcdt->dtype, mimo, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int m3_siso_step(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias, const m3_tensor* B_bias,
+                 const m3_tensor* C_bias, const m3_tensor* B_norm_w, const m3_tensor* C_norm_w, const m3_tensor* Dskip,
+                 const m3_tensor* angle_in, const m3_tensor* ssm_in, const m3_tensor* bx_in, m3_tensor* angle_out,
+                 m3_tensor* ssm_out, m3_tensor* bx_out, m3_tensor* y_gated, void* stream) {
+  return step_common(false, dims, zxbcdt, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, Dskip, nullptr, nullptr,
+                     angle_in, ssm_in, bx_in, angle_out, ssm_out, bx_out, y_gated, stream);
+}
+
+int m3_mimo_step(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias, const m3_tensor* B_bias,
+                 const m3_tensor* C_bias, const m3_tensor* B_norm_w, const m3_tensor* C_norm_w, const m3_tensor* Dskip,
+                 const m3_tensor* mimo_x, const m3_tensor* mimo_o, const m3_tensor* angle_in, const m3_tensor* ssm_in,
+                 const m3_tensor* bx_in, m3_tensor* angle_out, m3_tensor* ssm_out, m3_tensor* bx_out,
+                 m3_tensor* y_gated, void* stream) {
+  return step_common(true, dims, zxbcdt, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, Dskip, mimo_x, mimo_o,
+                     angle_in, ssm_in, bx_in, angle_out, ssm_out, bx_out, y_gated, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,223 @@
+// Fused single-token decode step of one Mamba3 mixer: everything Mamba3.step
+// (mamba3_ssm/layer.py:298-371) does between in_proj and out_proj, in one kernel.
+// One CTA per (b, h). The prologue (split of the in_proj row, softplus / clamp /
+// sigmoid, RMSNorm + bias of B and C, angle update and RoPE) runs once per CTA in shared
+// memory; the state update and readout then stream the fp32 state exactly once
+// (read old state, write new state), which is what bounds the step on HBM.
+#include "m3_common.cuh"
+#include "decode_step.cuh"
+
+namespace m3 {
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kMaxRD = 2048;  // R * D
+
+struct StepSmem {
+  float Bp[kMaxRD];
+  float Cp[kMaxRD];
+  float ss[2 * 8];  // sum of squares per (B|C, r)
+  float ang[256];
+  float xr[8];
+  float yr[8];
+  float scal[4];    // DT, decay, tr, D
+};
+
+// Prologue shared by SISO and MIMO: fills Bp/Cp (R x D, normed + bias + RoPE) and the
+// per-head scalars, writes angle_out.
+template <typename TZ>
+__device__ void step_prologue(const StepParams& a, int b, int h, StepSmem& s) {
+  const int tid = threadIdx.x, D = a.D, R = a.R, G = a.G, H = a.H;
+  const TZ* row = reinterpret_cast<const TZ*>(a.zxbcdt) + (int64_t)b * a.s_row;
+  const int g = (int)(((int64_t)h * G) / H);
+  const int off_B = 2 * a.d_inner, off_C = off_B + D * G * R, off_dt = off_C + D * G * R;
+  const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
+  if (tid == 0) {
+    const float DT = softplusf_(to_f32(row[off_dt + h]) + a.dt_bias[h]);
+    const float A = -fminf(softplusf_(to_f32(row[off_A + h])), -a.A_floor);  // layer.py:317
+    s.scal[0] = DT;
+    s.scal[1] = expf(A * DT);
+    s.scal[2] = sigmoidf_(to_f32(row[off_tr + h]));
+    s.scal[3] = a.Dskip[h];
+  }
+  for (int i = tid; i < R * D; i += blockDim.x) {
+    const int r = i / D, d = i - r * D;
+    s.Bp[i] = to_f32(row[off_B + (r * G + g) * D + d]);
+    s.Cp[i] = to_f32(row[off_C + (r * G + g) * D + d]);
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  for (int j = warp; j < 2 * R; j += nw) {
+    const float* v = (j < R) ? (s.Bp + j * D) : (s.Cp + (j - R) * D);
+    float acc = 0.f;
+    for (int d = lane; d < D; d += 32) acc = fmaf(v[d], v[d], acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) s.ss[j] = acc;
+  }
+  const float DT = s.scal[0];
+  for (int i = tid; i < a.S; i += blockDim.x) {
+    const int64_t ai = ((int64_t)b * H + h) * a.S + i;
+    const float an = a.angle_in[ai] + to_f32(row[off_ang + i]) * DT;
+    s.ang[i] = an;
+    a.angle_out[ai] = an;
+  }
+  __syncthreads();
+  // normalise + bias, then rotate pairs of the first rope_split dims
+  const int npair = a.split / 2;
+  const int per_r = npair + (D - a.split);
+  for (int i = tid; i < R * per_r; i += blockDim.x) {
+    const int r = i / per_r, k = i - r * per_r;
+    // RMSNorm (ops.py:102-104): x / sqrt(mean(x^2) + eps) * weight
+    const float rb = sqrtf(s.ss[r] / D + a.eps);
+    const float rc = sqrtf(s.ss[R + r] / D + a.eps);
+    const float* bb = a.B_bias + ((int64_t)h * R + r) * D;
+    const float* cb = a.C_bias + ((int64_t)h * R + r) * D;
+    float* Bv = s.Bp + r * D;
+    float* Cv = s.Cp + r * D;
+    if (k < npair) {
+      const int d0 = 2 * k, d1 = d0 + 1;
+      const float b0 = Bv[d0] / rb * a.B_norm_w[d0] + bb[d0];
+      const float b1 = Bv[d1] / rb * a.B_norm_w[d1] + bb[d1];
+      const float c0 = Cv[d0] / rc * a.C_norm_w[d0] + cb[d0];
+      const float c1 = Cv[d1] / rc * a.C_norm_w[d1] + cb[d1];
+      float sn, cs;
+      sincosf(s.ang[k], &sn, &cs);
+      Bv[d0] = b0 * cs - b1 * sn;
+      Bv[d1] = b0 * sn + b1 * cs;
+      Cv[d0] = c0 * cs - c1 * sn;
+      Cv[d1] = c0 * sn + c1 * cs;
+    } else {
+      const int d = a.split + (k - npair);
+      Bv[d] = Bv[d] / rb * a.B_norm_w[d] + bb[d];
+      Cv[d] = Cv[d] / rc * a.C_norm_w[d] + cb[d];
+    }
+  }
+  __syncthreads();
+}
+
+template <typename TZ>
+__global__ void __launch_bounds__(kThreads) siso_step_kernel(StepParams a) {
+  __shared__ StepSmem s;
+  const int b = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  step_prologue<TZ>(a, b, h, s);
+  const int D = a.D, P = a.P, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const TZ* row = reinterpret_cast<const TZ*>(a.zxbcdt) + (int64_t)b * a.s_row;
+  const float DT = s.scal[0], decay = s.scal[1], tr = s.scal[2], Dk = s.scal[3];
+  const int LPR = D / 4 < 32 ? D / 4 : 32;  // lanes per state row (float4 each)
+  const int RPW = 32 / LPR;                  // rows per warp pass
+  const int li = lane % LPR, rw = lane / LPR;
+  const int64_t base = ((int64_t)b * a.H + h) * P * D;
+  for (int p0 = warp * RPW; p0 < P; p0 += (blockDim.x >> 5) * RPW) {
+    const int p = p0 + rw;
+    const bool pv = p < P;
+    const float xv = pv ? to_f32(row[a.d_inner + h * P + p]) : 0.f;
+    float acc = 0.f;
+    for (int d4 = li; 4 * d4 < D; d4 += LPR) {
+      const int d = 4 * d4;
+      if (pv) {
+        const float4 hs = *reinterpret_cast<const float4*>(a.ssm_in + base + (int64_t)p * D + d);
+        const float4 bp = *reinterpret_cast<const float4*>(a.bx_in + base + (int64_t)p * D + d);
+        const float hk[4] = {hs.x, hs.y, hs.z, hs.w};
+        const float pk[4] = {bp.x, bp.y, bp.z, bp.w};
+        float ho[4], bo[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float bxc = xv * s.Bp[d + k];
+          const float blend = (1.0f - tr) * bxc + tr * 0.5f * (bxc + pk[k]);  // layer.py:362
+          ho[k] = decay * hk[k] + DT * blend;                                  // layer.py:363-366
+          bo[k] = bxc;
+          acc = fmaf(s.Cp[d + k], ho[k], acc);
+        }
+        *reinterpret_cast<float4*>(a.ssm_out + base + (int64_t)p * D + d) = make_float4(ho[0], ho[1], ho[2], ho[3]);
+        *reinterpret_cast<float4*>(a.bx_out + base + (int64_t)p * D + d) = make_float4(bo[0], bo[1], bo[2], bo[3]);
+      }
+    }
+    for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (pv && li == 0) {
+      const float y = acc + Dk * xv;
+      const float z = to_f32(row[h * P + p]);
+      st(reinterpret_cast<TZ*>(a.y) + (int64_t)b * a.s_y + h * P + p, y * (z * sigmoidf_(z)));
+    }
+  }
+}
+
+template <typename TZ>
+__global__ void __launch_bounds__(kThreads) mimo_step_kernel(StepParams a) {
+  __shared__ StepSmem s;
+  __shared__ float sx[1024];
+  const int b = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  step_prologue<TZ>(a, b, h, s);
+  const int D = a.D, P = a.P, R = a.R, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const TZ* row = reinterpret_cast<const TZ*>(a.zxbcdt) + (int64_t)b * a.s_row;
+  const float DT = s.scal[0], decay = s.scal[1], tr = s.scal[2], Dk = s.scal[3];
+  for (int p = tid; p < P; p += blockDim.x) sx[p] = to_f32(row[a.d_inner + h * P + p]);
+  __syncthreads();
+  // xr = mimo_x x   (layer.py:346)
+  for (int r = warp; r < R; r += blockDim.x >> 5) {
+    float acc = 0.f;
+    for (int p = lane; p < P; p += 32) acc = fmaf(sx[p], a.mimo_x[((int64_t)h * R + r) * P + p], acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) s.xr[r] = acc;
+  }
+  __syncthreads();
+  // state update; y_r partial sums via shared atomics
+  if (tid < R) s.yr[tid] = 0.f;
+  __syncthreads();
+  const int64_t base = ((int64_t)b * a.H + h) * D;
+  float yacc[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) yacc[r] = 0.f;
+  for (int d = tid; d < D; d += blockDim.x) {
+    float bxc = 0.f;
+    for (int r = 0; r < R; ++r) bxc = fmaf(s.xr[r], s.Bp[r * D + d], bxc);  // layer.py:347
+    const float blend = (1.0f - tr) * bxc + tr * 0.5f * (bxc + a.bx_in[base + d]);
+    const float hn = decay * a.ssm_in[base + d] + DT * blend;
+    a.ssm_out[base + d] = hn;
+    a.bx_out[base + d] = bxc;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < R) yacc[r] = fmaf(s.Cp[r * D + d], hn, yacc[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    if (r < R) {
+      float v = yacc[r];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) atomicAdd(&s.yr[r], v);
+    }
+  }
+  __syncthreads();
+  // y = mimo_o^T (y_r + D xr), gated (layer.py:352-356)
+  for (int p = tid; p < P; p += blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < R; ++r)
+      acc = fmaf(s.yr[r] + Dk * s.xr[r], a.mimo_o[((int64_t)h * R + r) * P + p], acc);
+    const float z = to_f32(row[h * P + p]);
+    st(reinterpret_cast<TZ*>(a.y) + (int64_t)b * a.s_y + h * P + p, acc * (z * sigmoidf_(z)));
+  }
+}
+
+}  // namespace
+
+int launch_step(const StepParams& p, int zdt, bool mimo, cudaStream_t s) {
+  if (p.R * p.D > kMaxRD || p.R > 8 || p.S > 256) return fail(M3_ERR_UNSUPPORTED, "step: mimo_rank*d_state above 2048, rank above 8 or more than 256 angles");
+  if (mimo && p.P > 1024) return fail(M3_ERR_UNSUPPORTED, "step: headdim above 1024");
+  if (!mimo && (p.D % 16 != 0 || (p.D & (p.D - 1)) != 0)) return fail(M3_ERR_UNSUPPORTED, "siso step: d_state must be a power of two >= 16");
+  const dim3 grid(p.Bn * p.H);
+#define M3_STEP_LAUNCH(T)                                                          \
+  do {                                                                             \
+    if (mimo) mimo_step_kernel<T><<<grid, kThreads, 0, s>>>(p);                    \
+    else siso_step_kernel<T><<<grid, kThreads, 0, s>>>(p);                         \
+  } while (0)
+  if (zdt == M3_FLOAT32) M3_STEP_LAUNCH(float);
+  else if (zdt == M3_BFLOAT16) M3_STEP_LAUNCH(__nv_bfloat16);
+  else if (zdt == M3_FLOAT16) M3_STEP_LAUNCH(__half);
+  else return fail(M3_ERR_UNSUPPORTED, "step: unsupported dtype");
+#undef M3_STEP_LAUNCH
+  return check_launch(mimo ? "mimo_step_kernel" : "siso_step_kernel");
+}
+
+}  // namespace m3

@@ -1,0 +1,63 @@
+// Shared device/host helpers of libmamba3_b200: element loads/stores for the three I/O
+// dtypes, the thread-local error string, and argument checks for m3_tensor views.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "mamba3_b200.h"
+
+namespace m3 {
+
+// ------------------------------------------------------------------------------------
+// element conversion
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+template <typename T> __device__ __forceinline__ float ld(const T* p) { return to_f32(*p); }
+template <typename T> __device__ __forceinline__ void st(T* p, float v) { *p = from_f32<T>(v); }
+
+__device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + expf(-v)); }
+// torch.nn.functional.softplus, beta = 1, threshold = 20
+__device__ __forceinline__ float softplusf_(float v) { return v > 20.0f ? v : log1pf(expf(v)); }
+
+template <typename T> struct DT_;
+template <> struct DT_<float> { static constexpr int id = M3_FLOAT32; };
+template <> struct DT_<__nv_bfloat16> { static constexpr int id = M3_BFLOAT16; };
+template <> struct DT_<__half> { static constexpr int id = M3_FLOAT16; };
+
+// ------------------------------------------------------------------------------------
+// host-side error handling
+// ------------------------------------------------------------------------------------
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int check_launch(const char* what);
+
+inline size_t dtype_size(int dt) { return dt == M3_FLOAT32 ? 4 : 2; }
+
+// Strided view passed by value to kernels (inner dimension contiguous).
+struct View4 {
+  const void* p;
+  int64_t s0, s1, s2;  // strides of dims 0..2 in elements (dim 3 is contiguous)
+};
+
+}  // namespace m3
+
+#define M3_TRY(expr)                  \
+  do {                                \
+    int _rc = (expr);                 \
+    if (_rc != M3_OK) return _rc;     \
+  } while (0)

@@ -1,0 +1,48 @@
+// Parameters of the MIMO scan kernels. Element strides; innermost dims contiguous.
+#pragma once
+#include <stdint.h>
+
+#include "siso_scan.cuh"
+
+namespace m3 {
+
+struct Str4 {
+  int64_t b, l, r, h;
+};
+
+struct MimoParams {
+  int Bn, L, H, P, D, R;
+  const void* x;    Str3 sx;
+  const void* Bm;   Str4 sB;
+  const void* Cm;   Str4 sC;
+  const float* adt; Str3 sadt;
+  const float* dt;  Str3 sdt;
+  const float* trap; Str3 strap;
+  const float* Dskip; int64_t sD;
+  const float* mimo_x; int64_t smx_h, smx_r;  // (H, R, P) f32
+  const float* mimo_o; int64_t smo_h, smo_r;
+  const float* h0;   // (B,H,D) contiguous or null
+  const float* bx0;
+  void* y; Str3 sy;
+  float* h_last;
+  float* bx_last;
+  // backward
+  const void* dy; Str3 sdy;
+  void* dx; Str3 sdx;
+  void* dB; Str4 sdB;
+  void* dC; Str4 sdC;
+  float* dadt; Str3 sdadt;
+  float* ddt; Str3 sddt;
+  float* dtrap; Str3 sdtrap;
+  float* dD;    // (H) pre-zeroed
+  float* dmx;   // (H,R,P) contiguous, pre-zeroed
+  float* dmo;
+  float* dh0;
+  float* dbx0;
+  float* work;  // checkpoints
+};
+
+size_t mimo_bwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t P, int64_t D, int64_t R);
+int launch_mimo(const MimoParams& p, int xdt, int bcdt, bool bwd, cudaStream_t s);
+
+}  // namespace m3

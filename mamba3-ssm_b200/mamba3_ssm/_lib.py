@@ -1,0 +1,121 @@
+"""ctypes binding of libmamba3_b200.so (declared in include/mamba3_b200.h).
+
+The library is built in-tree by ``mamba3-ssm_b200/build_lib.py`` and loaded from this
+directory. There is deliberately no fallback: if the library is missing or a call fails,
+a RuntimeError is raised with the library's own error text.
+"""
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmamba3_b200.so")
+MAX_DIMS = 6
+
+M3_FLOAT32, M3_BFLOAT16, M3_FLOAT16 = 0, 1, 2
+_DTYPE_CODE = {torch.float32: M3_FLOAT32, torch.bfloat16: M3_BFLOAT16, torch.float16: M3_FLOAT16}
+_STATUS = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "workspace"}
+
+
+class M3Tensor(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("dtype", ctypes.c_int32),
+        ("ndim", ctypes.c_int32),
+        ("shape", ctypes.c_int64 * MAX_DIMS),
+        ("stride", ctypes.c_int64 * MAX_DIMS),
+    ]
+
+
+class M3LayerDims(ctypes.Structure):
+    _fields_ = [
+        ("d_model", ctypes.c_int32),
+        ("d_inner", ctypes.c_int32),
+        ("nheads", ctypes.c_int32),
+        ("headdim", ctypes.c_int32),
+        ("d_state", ctypes.c_int32),
+        ("ngroups", ctypes.c_int32),
+        ("mimo_rank", ctypes.c_int32),
+        ("num_rope_angles", ctypes.c_int32),
+        ("rope_split", ctypes.c_int32),
+        ("A_floor", ctypes.c_float),
+        ("norm_eps", ctypes.c_float),
+    ]
+
+
+_P = ctypes.POINTER(M3Tensor)
+_SIGS = {
+    "m3_abi_version": ([], ctypes.c_int),
+    "m3_last_error_string": ([], ctypes.c_char_p),
+    "m3_siso_scan_fwd": ([_P] * 12 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_siso_scan_bwd_workspace_size": ([ctypes.c_int64] * 5, ctypes.c_size_t),
+    "m3_siso_scan_bwd": ([_P] * 19 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+    "m3_mimo_scan_fwd": ([_P] * 14 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_mimo_scan_bwd_workspace_size": ([ctypes.c_int64] * 6, ctypes.c_size_t),
+    "m3_mimo_scan_bwd": ([_P] * 23 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+    "m3_siso_step": ([ctypes.POINTER(M3LayerDims)] + [_P] * 14 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_mimo_step": ([ctypes.POINTER(M3LayerDims)] + [_P] * 16 + [ctypes.c_void_p], ctypes.c_int),
+}
+
+_lib = None
+
+
+def load():
+    """Load the library once and attach the C signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is not built; run `python mamba3-ssm_b200/build_lib.py` (nvcc, sm_100a). "
+            "There is no CPU or PyTorch fallback.")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (args, res) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    if lib.m3_abi_version() != 1:
+        raise RuntimeError("libmamba3_b200.so ABI version mismatch")
+    _lib = lib
+    return lib
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def tensor(t):
+    """m3_tensor view of a torch tensor (None -> absent optional argument)."""
+    m = M3Tensor()
+    if t is None:
+        m.data = None
+        m.ndim = 0
+        return m
+    if t.dim() > MAX_DIMS:
+        raise ValueError("tensor has too many dimensions for the C ABI")
+    code = _DTYPE_CODE.get(t.dtype)
+    if code is None:
+        raise TypeError(f"dtype {t.dtype} is not supported by libmamba3_b200")
+    m.data = t.data_ptr() if t.numel() > 0 else (t.data_ptr() or 1)
+    m.dtype = code
+    m.ndim = t.dim()
+    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
+        m.shape[i] = s
+        m.stride[i] = st
+    return m
+
+
+def ref(m):
+    return ctypes.byref(m) if m is not None else None
+
+
+def check(rc, what):
+    if rc != 0:
+        msg = load().m3_last_error_string().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({_STATUS.get(rc, rc)}): {msg}")
+
+
+def stream_of(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)

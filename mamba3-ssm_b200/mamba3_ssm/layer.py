@@ -1,0 +1,197 @@
+"""Mamba3 mixer with the constructor, parameters (names, shapes, init order), forward,
+step and allocate_inference_cache of the reference's ``mamba3_ssm/layer.py`` (:61-412).
+
+* ``forward`` keeps the reference's prologue (in_proj split, softplus/clamp, RMSNorm + bias
+  of B/C, cumulative RoPE angles) and epilogue (silu gate, out_proj) and runs the scan
+  through ``ops.ssm_scan_siso`` / ``ops.ssm_scan_mimo`` (sm_100a kernels, with backward).
+* ``step`` runs everything between in_proj and out_proj of one decode step
+  (layer.py:298-371) as a single fused kernel (``m3_siso_step`` / ``m3_mimo_step``).
+  Like the reference it returns new state tensors and leaves its inputs untouched.
+"""
+
+import math
+from typing import Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib as L
+from .ops import RMSNorm, apply_rope, ssm_scan_mimo, ssm_scan_siso
+
+
+class _StepNoGrad(torch.autograd.Function):
+    """Marks the outputs of the fused decode step: running it under grad mode is fine
+    (generation loops often do), but differentiating through it is not supported."""
+
+    @staticmethod
+    def forward(ctx, runner, *tensors):
+        return runner()
+
+    @staticmethod
+    def backward(ctx, *grads):
+        raise RuntimeError("Mamba3.step is inference-only in the B200 build: its fused kernel has no "
+                           "backward. Differentiate through Mamba3.forward instead.")
+
+
+class Mamba3(nn.Module):
+    def __init__(self, d_model: int, d_state: int = 128, expand: int = 2, headdim: int = 64,
+                 ngroups: int = 1, rope_fraction: float = 0.5, dt_min: float = 0.001,
+                 dt_max: float = 0.1, dt_init_floor: float = 1e-4, A_floor: float = 1e-4,
+                 is_mimo: bool = False, mimo_rank: int = 4, device=None, dtype=None):
+        factory_kwargs = {"device": device, "dtype": dtype}
+        super().__init__()
+        self.d_model = d_model
+        self.d_state = d_state
+        self.expand = expand
+        self.headdim = headdim
+        self.A_floor = A_floor
+        self.is_mimo = is_mimo
+        self.mimo_rank = mimo_rank if is_mimo else 1
+        self.num_bc_heads = ngroups
+        self.d_inner = int(expand * d_model)
+        assert self.d_inner % headdim == 0, f"d_inner ({self.d_inner}) must be divisible by headdim ({headdim})"
+        self.nheads = self.d_inner // headdim
+        assert rope_fraction in (0.5, 1.0), "rope_fraction must be 0.5 or 1.0"
+        split = int(d_state * rope_fraction)
+        self.split_tensor_size = split - (split % 2)
+        self.num_rope_angles = self.split_tensor_size // 2
+        assert self.num_rope_angles > 0
+        d_in_proj = (2 * self.d_inner + 2 * d_state * ngroups * self.mimo_rank + 3 * self.nheads
+                     + self.num_rope_angles)
+        # Parameter creation order matches the reference (in_proj init, then one
+        # torch.rand(nheads) draw for dt_bias, then out_proj init), so the same seed gives
+        # the same weights.
+        self.in_proj = nn.Linear(d_model, d_in_proj, bias=False, **factory_kwargs)
+        dt = torch.exp(torch.rand(self.nheads, dtype=torch.float32) * (math.log(dt_max) - math.log(dt_min))
+                       + math.log(dt_min)).clamp(min=dt_init_floor)
+        self.dt_bias = nn.Parameter(dt + torch.log(-torch.expm1(-dt)))  # inverse softplus
+        self.dt_bias._no_weight_decay = True
+        self.B_bias = nn.Parameter(torch.ones(self.nheads, self.mimo_rank, d_state, dtype=torch.float32))
+        self.C_bias = nn.Parameter(torch.ones(self.nheads, self.mimo_rank, d_state, dtype=torch.float32))
+        self.B_bias._no_weight_decay = True
+        self.C_bias._no_weight_decay = True
+        self.B_norm = RMSNorm(d_state)
+        self.C_norm = RMSNorm(d_state)
+        if self.is_mimo:
+            self.mimo_x = nn.Parameter(torch.ones(self.nheads, self.mimo_rank, headdim, **factory_kwargs)
+                                       / self.mimo_rank)
+            self.mimo_o = nn.Parameter(torch.ones(self.nheads, self.mimo_rank, headdim, **factory_kwargs)
+                                       / self.mimo_rank)
+        self.D = nn.Parameter(torch.ones(self.nheads, **factory_kwargs))
+        self.D._no_weight_decay = True
+        self.out_proj = nn.Linear(self.d_inner, d_model, bias=False, **factory_kwargs)
+        self._splits = [self.d_inner, self.d_inner, d_state * ngroups * self.mimo_rank,
+                        d_state * ngroups * self.mimo_rank, self.nheads, self.nheads, self.nheads,
+                        self.num_rope_angles]
+        self._f32_cache = None
+
+    # ------------------------------------------------------------------------------
+    def _bc(self, raw, norm, bias):
+        """RMSNorm over d_state, broadcast groups to heads, add the per-head bias."""
+        n = norm(raw.float())
+        n = n.expand(*n.shape[:-2], self.nheads, self.d_state)
+        return n + bias.transpose(0, 1)  # (H,R,D) -> (R,H,D)
+
+    def forward(self, u: torch.Tensor) -> torch.Tensor:
+        batch, Ln, _ = u.shape
+        R, G, Ds, H, P = self.mimo_rank, self.num_bc_heads, self.d_state, self.nheads, self.headdim
+        z, x, B_raw, C_raw, dd_dt, dd_A, trap_raw, angle_raw = torch.split(self.in_proj(u), self._splits, dim=-1)
+        z = z.unflatten(-1, (H, P))
+        x = x.unflatten(-1, (H, P))
+        B_raw = B_raw.unflatten(-1, (R, G, Ds))
+        C_raw = C_raw.unflatten(-1, (R, G, Ds))
+        A = -F.softplus(dd_A.float()).clamp(max=-self.A_floor)
+        DT = F.softplus(dd_dt.float() + self.dt_bias)
+        ADT = A * DT
+        Bh = self._bc(B_raw, self.B_norm, self.B_bias)
+        Ch = self._bc(C_raw, self.C_norm, self.C_bias)
+        ang = torch.cumsum(angle_raw.float().unsqueeze(2) * DT.unsqueeze(-1), dim=1)  # (B,L,H,S)
+        ang = ang.unsqueeze(2).expand(batch, Ln, R, H, self.num_rope_angles)
+        k = self.split_tensor_size
+        B_proj = torch.cat([apply_rope(Bh[..., :k], ang), Bh[..., k:]], dim=-1)
+        C_proj = torch.cat([apply_rope(Ch[..., :k], ang), Ch[..., k:]], dim=-1)
+        if self.is_mimo:
+            y = ssm_scan_mimo(x, B_proj, C_proj, ADT, DT, trap_raw.float(), self.D, self.mimo_x, self.mimo_o)
+        else:
+            y = ssm_scan_siso(x, B_proj[:, :, 0], C_proj[:, :, 0], ADT, DT, trap_raw.float(), self.D)
+        y = y * F.silu(z.float())
+        return self.out_proj(y.flatten(-2).to(x.dtype))
+
+    # ------------------------------------------------------------------------------
+    def _dims(self):
+        d = L.M3LayerDims()
+        d.d_model, d.d_inner, d.nheads, d.headdim = self.d_model, self.d_inner, self.nheads, self.headdim
+        d.d_state, d.ngroups, d.mimo_rank = self.d_state, self.num_bc_heads, self.mimo_rank
+        d.num_rope_angles, d.rope_split = self.num_rope_angles, self.split_tensor_size
+        d.A_floor, d.norm_eps = float(self.A_floor), float(self.B_norm.eps)
+        return d
+
+    def _step_params(self):
+        """fp32 contiguous views of the per-head parameters the step kernel reads, cached
+        until a parameter changes (in-place update, new tensor or new device)."""
+        ps = [self.dt_bias, self.B_bias, self.C_bias, self.B_norm.weight, self.C_norm.weight, self.D]
+        if self.is_mimo:
+            ps += [self.mimo_x, self.mimo_o]
+        key = tuple((p.data_ptr(), p._version, p.dtype, p.device) for p in ps)
+        if self._f32_cache is None or self._f32_cache[0] != key:
+            with torch.no_grad():
+                vals = [p.detach().float().contiguous() for p in ps]
+            self._f32_cache = (key, vals)
+        return self._f32_cache[1]
+
+    def step(self, u: torch.Tensor, angle_state: torch.Tensor, ssm_state: torch.Tensor,
+             bx_prev_state: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        zxbcdt = self.in_proj(u)
+        if not zxbcdt.is_cuda:
+            raise RuntimeError("Mamba3.step: the B200 build runs on CUDA tensors only (no CPU path)")
+        if zxbcdt.stride(-1) != 1:
+            zxbcdt = zxbcdt.contiguous()
+        batch = zxbcdt.shape[0]
+        dev = zxbcdt.device
+        params = self._step_params()
+        ang_in = angle_state.float().contiguous()
+        ssm_in = ssm_state.float().contiguous()
+        bx_in = bx_prev_state.float().contiguous()
+
+        def run():
+            ang_out = torch.empty_like(ang_in)
+            ssm_out = torch.empty_like(ssm_in)
+            bx_out = torch.empty_like(bx_in)
+            y = torch.empty((batch, self.d_inner), dtype=zxbcdt.dtype, device=dev)
+            dims = self._dims()
+            lib = L.load()
+            if self.is_mimo:
+                dtb, bb, cb, bw, cw, dd, mx, mo = params
+                args = [zxbcdt, dtb, bb, cb, bw, cw, dd, mx, mo, ang_in, ssm_in, bx_in, ang_out, ssm_out, bx_out, y]
+                fn, name = lib.m3_mimo_step, "m3_mimo_step"
+            else:
+                dtb, bb, cb, bw, cw, dd = params
+                args = [zxbcdt, dtb, bb, cb, bw, cw, dd, ang_in, ssm_in, bx_in, ang_out, ssm_out, bx_out, y]
+                fn, name = lib.m3_siso_step, "m3_siso_step"
+            ms = [L.tensor(t) for t in args]
+            with torch.cuda.device(dev):
+                L.check(fn(L.ref(dims), *[L.ref(m) for m in ms], L.stream_of(zxbcdt)), name)
+            return y, ang_out, ssm_out, bx_out
+
+        if torch.is_grad_enabled() and zxbcdt.requires_grad:
+            y, ang_out, ssm_out, bx_out = _StepNoGrad.apply(run, zxbcdt)
+        else:
+            y, ang_out, ssm_out, bx_out = run()
+        out = self.out_proj(y.to(u.dtype))
+        return out, ang_out, ssm_out, bx_out
+
+    def allocate_inference_cache(self, batch_size: int, device=None, dtype=None):
+        """Zero decode states (layer.py:380-412): angle (B,H,S), ssm and bx_prev
+        (B,H,P,D) for SISO or (B,H,D) for MIMO, all fp32."""
+        device = device or self.in_proj.weight.device
+        angle_state = torch.zeros(batch_size, self.nheads, self.num_rope_angles, device=device, dtype=torch.float32)
+        shape = (batch_size, self.nheads, self.d_state) if self.is_mimo else \
+            (batch_size, self.nheads, self.headdim, self.d_state)
+        return (angle_state, torch.zeros(shape, device=device, dtype=torch.float32),
+                torch.zeros(shape, device=device, dtype=torch.float32))
+
+    def extra_repr(self) -> str:
+        return (f"d_model={self.d_model}, d_state={self.d_state}, d_inner={self.d_inner}, "
+                f"nheads={self.nheads}, headdim={self.headdim}, is_mimo={self.is_mimo}, "
+                f"mimo_rank={self.mimo_rank}")

@@ -1,0 +1,113 @@
+"""CPU-only checks of the boundary: the C-ABI library loads without a GPU, exports every
+entry point include/mamba3_b200.h declares, rejects bad arguments on the host, and the
+Python drop-in keeps the reference's parameter names, shapes and init order."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT, load_golden
+
+HEADER = os.path.join(ROOT, "include", "mamba3_b200.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(m3_\w+)\s*\(", src, re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from mamba3_ssm import _lib
+    return _lib.load()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from mamba3_ssm import _lib
+    names = _declared()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) <= set(_lib.exported_symbols()) | {"m3_abi_version", "m3_last_error_string"}
+    assert lib.m3_abi_version() == 1
+
+
+def test_workspace_size_queries(lib):
+    assert lib.m3_siso_scan_bwd_workspace_size(2, 100, 3, 64, 128) == 4 * 2 * 100 * 3
+    assert lib.m3_mimo_scan_bwd_workspace_size(2, 100, 3, 32, 64, 4) > 0
+
+
+def test_host_validation_errors(lib):
+    from mamba3_ssm import _lib
+    null = _lib.M3Tensor()
+    rc = lib.m3_siso_scan_fwd(*([ctypes.byref(null)] * 12), None)
+    assert rc == 1
+    assert b"x: missing" in lib.m3_last_error_string()
+    x = _lib.M3Tensor()
+    x.data = 16
+    x.ndim = 3
+    rc = lib.m3_siso_scan_fwd(ctypes.byref(x), *([ctypes.byref(null)] * 11), None)
+    assert rc == 1 and b"x: expected" in lib.m3_last_error_string()
+    dims = _lib.M3LayerDims()
+    rc = lib.m3_siso_step(ctypes.byref(dims), *([ctypes.byref(null)] * 14), None)
+    assert rc == 1 and b"dims" in lib.m3_last_error_string()
+
+
+def test_cpu_tensors_are_rejected():
+    from mamba3_ssm import ssm_scan_siso, ssm_scan_mimo
+    x = torch.randn(1, 4, 2, 8)
+    B = torch.randn(1, 4, 2, 16)
+    s = torch.randn(1, 4, 2)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        ssm_scan_siso(x, B, B, s, s, s, torch.ones(2))
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        ssm_scan_mimo(x, B.unsqueeze(2), B.unsqueeze(2), s, s, s, torch.ones(2), torch.ones(2, 1, 8),
+                      torch.ones(2, 1, 8))
+
+
+@pytest.mark.parametrize("name", ["layer_c1_siso_f32", "layer_siso_f32_grad", "layer_siso_rope1_f32",
+                                  "layer_mimo_f32_grad", "layer_c2_mimo_bf16", "layer_siso_bf16"])
+def test_layer_init_matches_reference(name):
+    """Same seed -> bit-identical parameters and state_dict keys (layer.py:107-162)."""
+    from mamba3_ssm import Mamba3
+    g = load_golden(name)
+    cfg = {k[4:]: g[k].item() for k in g if k.startswith("cfg.")}
+    seed = {"layer_c1_siso_f32": 0, "layer_siso_f32_grad": 7, "layer_siso_rope1_f32": 8,
+            "layer_mimo_f32_grad": 9, "layer_c2_mimo_bf16": 0, "layer_siso_bf16": 3}[name]
+    torch.manual_seed(seed)
+    m = Mamba3(**cfg)
+    if str(g["dtype"]) == "bfloat16":
+        m = m.to(torch.bfloat16)
+    sd = m.state_dict()
+    assert sorted(sd) == sorted(k[2:] for k in g if k.startswith("w."))
+    for k, v in sd.items():
+        assert np.array_equal(v.float().numpy(), g["w." + k]), k
+
+
+def test_lm_init_matches_reference():
+    from mamba3_ssm import MambaConfig, MambaLMHeadModel
+    g = load_golden("lm_mimo_f32")
+    ssm = {k[4:]: g[k].item() for k in g if k.startswith("ssm.")}
+    cfg = MambaConfig(d_model=int(g["cfg.d_model"]), n_layer=int(g["cfg.n_layer"]),
+                      vocab_size=int(g["cfg.vocab_size"]), ssm_cfg=ssm)
+    torch.manual_seed(6)
+    m = MambaLMHeadModel(cfg)
+    sd = m.state_dict()
+    assert m.vocab_size == 296  # padded to a multiple of 8 (block.py:61-66)
+    for k, v in sd.items():
+        assert np.array_equal(v.numpy(), g["w." + k]), k
+
+
+def test_allocate_inference_cache_shapes():
+    from mamba3_ssm import Mamba3
+    m = Mamba3(d_model=1536, d_state=64, headdim=64, is_mimo=True, mimo_rank=4)
+    a, s, b = m.allocate_inference_cache(256)
+    assert a.shape == (256, 48, 16) and s.shape == (256, 48, 64) and b.shape == (256, 48, 64)
+    assert a.dtype == s.dtype == b.dtype == torch.float32
+    m = Mamba3(d_model=128, d_state=32, headdim=32)
+    a, s, b = m.allocate_inference_cache(3)
+    assert s.shape == (3, 8, 32, 32) and b.shape == s.shape and a.shape == (3, 8, 8)

@@ -1,0 +1,113 @@
+"""Parity of the drop-in Mamba3 layer and MambaLMHeadModel on the GPU with the
+reference's own outputs (golden fixtures recorded from layer.py / block.py on the CPU):
+forward, backward (every parameter gradient and du), the fused decode step replayed
+token by token, and the reference's invariant step == forward (tests.py:67-108).
+
+Tolerances: rel 1e-4 in fp32, rel 2e-2 in bf16 (max|a - ref| / max|ref|)."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, rel_err
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _t(g, k):
+    a = torch.from_numpy(np.ascontiguousarray(g[k]))
+    return a.to(torch.bfloat16 if k in g["bf16"] else a.dtype).to(DEV)
+
+
+def _layer(g):
+    from mamba3_ssm import Mamba3
+    cfg = {k[4:]: g[k].item() for k in g if k.startswith("cfg.")}
+    m = Mamba3(**cfg)
+    if str(g["dtype"]) == "bfloat16":
+        m = m.to(torch.bfloat16)
+    m.load_state_dict({k[2:]: _t(g, k) for k in g if k.startswith("w.")})
+    return m.to(DEV)
+
+
+LAYERS = ["layer_c1_siso_f32", "layer_siso_f32_grad", "layer_siso_rope1_f32", "layer_mimo_f32_grad",
+          "layer_c2_mimo_bf16", "layer_siso_bf16"]
+
+
+@pytest.mark.parametrize("name", LAYERS)
+def test_layer_forward_backward_step(name):
+    g = load_golden(name)
+    m = _layer(g)
+    bf = str(g["dtype"]) == "bfloat16"
+    tol = 2e-2 if bf else 1e-4
+    u = _t(g, "u").requires_grad_("du" in g)
+    y = m(u)
+    assert y.shape == u.shape and y.dtype == u.dtype
+    assert rel_err(y.float().detach().cpu().numpy(), g["y"]) < tol
+    if "du" in g:
+        y.backward(_t(g, "dy"))
+        assert rel_err(u.grad.float().cpu().numpy(), g["du"]) < tol
+        for k, p in m.named_parameters():
+            gk = "g." + k
+            if gk in g:
+                assert rel_err(p.grad.float().cpu().numpy(), g[gk]) < tol * 5, k
+    n = g["step_y"].shape[1]
+    with torch.no_grad():
+        a, s, b = m.allocate_inference_cache(u.shape[0])
+        ys = []
+        for t in range(n):
+            o, a2, s2, b2 = m.step(u[:, t].detach(), a, s, b)
+            assert a2 is not a and s2 is not s  # out-of-place, like the reference
+            a, s, b = a2, s2, b2
+            ys.append(o)
+    st = torch.stack(ys, 1).float().cpu().numpy()
+    assert rel_err(st, g["step_y"]) < tol
+    assert rel_err(s.cpu().numpy(), g["step_ssm"]) < tol
+    assert rel_err(b.cpu().numpy(), g["step_bx"]) < tol
+    assert rel_err(a.cpu().numpy(), g["step_angle"]) < tol
+    assert rel_err(st, y[:, :n].float().detach().cpu().numpy()) < max(tol, 1e-4)
+
+
+def test_step_under_grad_mode_is_inference_only():
+    g = load_golden("layer_siso_f32_grad")
+    m = _layer(g)
+    u = _t(g, "u")
+    a, s, b = m.allocate_inference_cache(u.shape[0])
+    o, a, s, b = m.step(u[:, 0], a, s, b)  # grad mode on, parameters require grad
+    assert o.requires_grad
+    with pytest.raises(RuntimeError, match="inference-only"):
+        o.sum().backward()
+
+
+def _lm(g):
+    from mamba3_ssm import MambaConfig, MambaLMHeadModel
+    ssm = {k[4:]: g[k].item() for k in g if k.startswith("ssm.")}
+    cfg = MambaConfig(d_model=int(g["cfg.d_model"]), n_layer=int(g["cfg.n_layer"]),
+                      vocab_size=int(g["cfg.vocab_size"]), ssm_cfg=ssm)
+    m = MambaLMHeadModel(cfg)
+    if str(g["dtype"]) == "bfloat16":
+        m = m.to(torch.bfloat16)
+    m.load_state_dict({k[2:]: _t(g, k) for k in g if k.startswith("w.")})
+    return m.to(DEV)
+
+
+@pytest.mark.parametrize("name", ["lm_siso_f32", "lm_mimo_f32", "lm_mimo_bf16"])
+def test_lm_forward_and_step(name):
+    g = load_golden(name)
+    m = _lm(g)
+    tol = 2e-2 if str(g["dtype"]) == "bfloat16" else 1e-4
+    ids = torch.from_numpy(g["ids"]).to(DEV)
+    with torch.no_grad():
+        lo = m(ids)
+        assert rel_err(lo.float().cpu().numpy(), g["logits"]) < tol
+        cache = m.allocate_inference_cache(ids.shape[0])
+        lg = []
+        for t in range(g["step_logits"].shape[1]):
+            x = ids[:, t] if t % 2 else ids[:, t:t + 1]  # (B,) and (B, 1) both accepted
+            out, cache = m.step(x, cache)
+            lg.append(out)
+    assert rel_err(torch.stack(lg, 1).float().cpu().numpy(), g["step_logits"]) < tol
+    for i, (a, s, b) in enumerate(cache):
+        assert rel_err(s.cpu().numpy(), g[f"cache{i}.ssm"]) < tol
+        assert rel_err(b.cpu().numpy(), g[f"cache{i}.bx"]) < tol
+        assert rel_err(a.cpu().numpy(), g[f"cache{i}.angle"]) < tol

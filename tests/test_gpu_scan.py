@@ -1,0 +1,176 @@
+"""Parity of the CUDA scan kernels (through the drop-in ops and the C ABI) with the
+reference's own outputs (golden fixtures) and with the float64 oracle.
+
+Tolerances (max|a - ref| / max|ref| per tensor): rel 1e-4 for fp32 I/O, rel 2e-2 for bf16
+I/O, the bars of the parity target; parameter-like gradients that sum over the whole
+sequence (dADT, dDT, dtrap, dD) get 5x that.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, rel_err
+from oracle import scan_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _t(g, k, dtype=None):
+    a = torch.from_numpy(np.ascontiguousarray(g[k]))
+    if dtype is None:
+        dtype = torch.bfloat16 if k in g["bf16"] else torch.float32
+    return a.to(dtype).to(DEV)
+
+
+def _tol(dtype):
+    return 2e-2 if dtype == torch.bfloat16 else 1e-4
+
+
+SISO = ["siso_op_f32", "siso_op_f32_ragged", "siso_op_f32_d128", "siso_op_bf16", "siso_op_f32_l1"]
+MIMO = ["mimo_op_f32", "mimo_op_f32_r2", "mimo_op_bf16", "mimo_op_f32_r1", "mimo_op_f32_r8"]
+
+
+@pytest.mark.parametrize("name", SISO)
+def test_siso_fwd_bwd_matches_reference(name):
+    from mamba3_ssm import ssm_scan_siso
+    g = load_golden(name)
+    ins = [_t(g, k).requires_grad_(True) for k in ("x", "B", "C", "ADT", "DT", "trap", "D")]
+    y = ssm_scan_siso(*ins)
+    tol = _tol(ins[0].dtype)
+    assert y.dtype == ins[0].dtype and y.shape == ins[0].shape
+    assert rel_err(y.float().cpu().numpy(), g["y"]) < tol
+    y.backward(_t(g, "dy"))
+    for k, t in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
+        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
+        assert t.grad.dtype == t.dtype
+        assert rel_err(t.grad.float().cpu().numpy(), g[k]) < tol * f, k
+
+
+@pytest.mark.parametrize("name", MIMO)
+def test_mimo_fwd_bwd_matches_reference(name):
+    from mamba3_ssm import ssm_scan_mimo
+    g = load_golden(name)
+    ins = [_t(g, k).requires_grad_(True) for k in ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")]
+    y = ssm_scan_mimo(*ins)
+    tol = _tol(ins[0].dtype)
+    assert rel_err(y.float().cpu().numpy(), g["y"]) < tol
+    y.backward(_t(g, "dy"))
+    for k, t in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
+        f = 5 if k in ("dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o") else 1
+        assert rel_err(t.grad.float().cpu().numpy(), g[k]) < tol * f, k
+
+
+def _inputs(seed, Bn, L, H, P, D, R=None, dtype=torch.float32):
+    rng = np.random.default_rng(seed)
+    bc = (Bn, L, H, D) if R is None else (Bn, L, R, H, D)
+    x = rng.standard_normal((Bn, L, H, P))
+    Bm = rng.standard_normal(bc)
+    C = rng.standard_normal(bc)
+    dt = np.clip(np.log1p(np.exp(rng.normal(-3, 0.5, (Bn, L, H)))), 1e-3, 0.1)
+    A = -np.exp(rng.uniform(0, np.log(16), H))
+    ADT = A * dt
+    trap = 1 / (1 + np.exp(-rng.standard_normal((Bn, L, H))))
+    Dw = rng.standard_normal(H) * 0.5 + 1.0
+    arrs = dict(x=x, B=Bm, C=C, ADT=ADT, DT=dt, trap=trap, D=Dw)
+    if R is not None:
+        arrs["mimo_x"] = rng.standard_normal((H, R, P)) * 0.3 + 1.0 / R
+        arrs["mimo_o"] = rng.standard_normal((H, R, P)) * 0.3 + 1.0 / R
+    tens = {}
+    for k, v in arrs.items():
+        dt_ = dtype if k in ("x", "B", "C") else torch.float32
+        tens[k] = torch.tensor(v, dtype=torch.float32).to(dt_).to(DEV)
+        arrs[k] = tens[k].double().cpu().numpy()  # oracle sees the rounded values
+    return arrs, tens
+
+
+@pytest.mark.parametrize("D", [16, 32, 64, 128])
+@pytest.mark.parametrize("P,L", [(16, 33), (64, 70), (128, 40)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_siso_sweep_against_oracle(D, P, L, dtype):
+    from mamba3_ssm import ssm_scan_siso
+    arrs, t = _inputs(D * 1000 + P + L, 2, L, 3, P, D, dtype=dtype)
+    ins = [t[k].requires_grad_(True) for k in ("x", "B", "C", "ADT", "DT", "trap", "D")]
+    y = ssm_scan_siso(*ins)
+    yo, _, _ = O.siso_scan_fwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
+    tol = _tol(dtype)
+    assert rel_err(y.double().cpu().numpy(), yo) < tol
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    go = O.siso_scan_bwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")], dy.double().cpu().numpy())
+    for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
+        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
+        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < tol * f, k
+
+
+@pytest.mark.parametrize("R,D,P", [(1, 16, 16), (2, 32, 64), (4, 64, 32), (8, 128, 64), (4, 64, 64)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mimo_sweep_against_oracle(R, D, P, dtype):
+    from mamba3_ssm import ssm_scan_mimo
+    arrs, t = _inputs(R * 100 + D + P, 2, 77, 3, P, D, R=R, dtype=dtype)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")
+    ins = [t[k].requires_grad_(True) for k in keys]
+    y = ssm_scan_mimo(*ins)
+    yo, _, _ = O.mimo_scan_fwd(*[arrs[k] for k in keys])
+    tol = _tol(dtype)
+    assert rel_err(y.double().cpu().numpy(), yo) < tol
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    go = O.mimo_scan_bwd(*[arrs[k] for k in keys], dy.double().cpu().numpy())
+    for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
+        f = 5 if k in ("dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o") else 1
+        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < tol * f, k
+
+
+def test_siso_strided_views_and_state_continuation():
+    """B/C as (B, L, R, H, D)[:, :, 0] views (layer.py:256-257) and a scan split in two
+    halves with the carried (ssm_state, bx_prev) equal one full scan."""
+    from mamba3_ssm import ssm_scan_siso
+    from mamba3_ssm.ops import ssm_scan_siso_states
+    arrs, t = _inputs(7, 2, 96, 4, 32, 64)
+    B5 = torch.randn(2, 96, 2, 4, 64, device=DEV)
+    C5 = torch.randn(2, 96, 2, 4, 64, device=DEV)
+    y = ssm_scan_siso(t["x"], B5[:, :, 0], C5[:, :, 0], t["ADT"], t["DT"], t["trap"], t["D"])
+    yo, ho, bo = O.siso_scan_fwd(arrs["x"], B5[:, :, 0].double().cpu().numpy(), C5[:, :, 0].double().cpu().numpy(),
+                                 arrs["ADT"], arrs["DT"], arrs["trap"], arrs["D"])
+    assert rel_err(y.double().cpu().numpy(), yo) < 1e-4
+    Bc, Cc = B5[:, :, 0].contiguous(), C5[:, :, 0].contiguous()
+    a = slice(0, 41)
+    b = slice(41, 96)
+    y1, h1, b1 = ssm_scan_siso_states(t["x"][:, a], Bc[:, a], Cc[:, a], t["ADT"][:, a], t["DT"][:, a],
+                                      t["trap"][:, a], t["D"])
+    y2, h2, b2 = ssm_scan_siso_states(t["x"][:, b], Bc[:, b], Cc[:, b], t["ADT"][:, b], t["DT"][:, b],
+                                      t["trap"][:, b], t["D"], h1, b1)
+    assert rel_err(torch.cat([y1, y2], 1).double().cpu().numpy(), yo) < 1e-4
+    assert rel_err(h2.double().cpu().numpy(), ho) < 1e-4
+    assert rel_err(b2.double().cpu().numpy(), bo) < 1e-4
+
+
+def test_empty_and_single_token_inputs():
+    from mamba3_ssm import ssm_scan_siso, ssm_scan_mimo
+    for L in (0, 1):
+        arrs, t = _inputs(3, 2, L, 2, 16, 32)
+        y = ssm_scan_siso(*[t[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
+        assert y.shape == (2, L, 2, 16)
+        if L:
+            yo, _, _ = O.siso_scan_fwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
+            assert rel_err(y.double().cpu().numpy(), yo) < 1e-4
+        arrs, t = _inputs(4, 2, L, 2, 16, 32, R=2)
+        y = ssm_scan_mimo(*[t[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")])
+        assert y.shape == (2, L, 2, 16)
+    x = torch.zeros(0, 5, 2, 16, device=DEV)
+    B = torch.zeros(0, 5, 2, 32, device=DEV)
+    s = torch.zeros(0, 5, 2, device=DEV)
+    assert ssm_scan_siso(x, B, B, s, s, s, torch.ones(2, device=DEV)).shape == (0, 5, 2, 16)
+
+
+def test_long_sequence_slices_against_oracle():
+    """Long-context shape per (b, h) (H=2 of the 64 heads, full L = 32768, P=64, D=128,
+    bf16 I/O) against the float64 oracle."""
+    from mamba3_ssm import ssm_scan_siso
+    arrs, t = _inputs(11, 1, 32768, 2, 64, 128, dtype=torch.bfloat16)
+    y = ssm_scan_siso(*[t[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
+    yo, _, _ = O.siso_scan_fwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
+    assert rel_err(y.double().cpu().numpy(), yo) < 2e-2

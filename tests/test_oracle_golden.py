@@ -129,3 +129,13 @@ def test_oracle_bwd_matches_finite_difference():
             m = base.copy(); m[i] -= e
             fd[i] = (loss(**{**args, k: p}) - loss(**{**args, k: m})) / (2 * e)
         assert rel_err(grads[gk], fd) < 1e-6, k
+
+
+@pytest.mark.parametrize("name", ["siso_op_f32", "siso_op_f32_ragged", "siso_op_f32_d128", "siso_op_f32_l1",
+                                  "siso_op_bf16"])
+def test_c_restatement_matches_reference(name):
+    """oracle/scan_ref.c (the CPU baseline) against the reference's own outputs."""
+    from oracle import cpu_ref
+    g = load_golden(name)
+    y = cpu_ref.siso_fwd(*[g[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
+    assert rel_err(y, g["y"]) < (2e-2 if str(g["dtype"]) == "bfloat16" else 1e-5)
