@@ -70,6 +70,9 @@ int check(const m3_tensor* t, const char* name, int ndim, const int64_t* shape, 
     }
   if (t->dtype < 0 || t->dtype > 2 || !(mask & (1u << t->dtype)))
     return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": unsupported dtype " + std::to_string(t->dtype));
+  int64_t n = 1;
+  for (int i = 0; i < ndim; ++i) n *= t->shape[i];
+  if (n == 0) return M3_OK;  // empty views carry arbitrary strides and are never dereferenced
   if (ndim > 0 && t->shape[ndim - 1] > 1 && t->stride[ndim - 1] != 1)
     return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": innermost dimension must be contiguous");
   if (contig) {

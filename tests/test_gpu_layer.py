@@ -46,11 +46,11 @@ def test_layer_forward_backward_step(name):
     assert rel_err(y.float().detach().cpu().numpy(), g["y"]) < tol
     if "du" in g:
         y.backward(_t(g, "dy"))
-        assert rel_err(u.grad.float().cpu().numpy(), g["du"]) < tol
+        assert rel_err(u.grad.detach().float().cpu().numpy(), g["du"]) < tol
         for k, p in m.named_parameters():
             gk = "g." + k
             if gk in g:
-                assert rel_err(p.grad.float().cpu().numpy(), g[gk]) < tol * 5, k
+                assert rel_err(p.grad.detach().float().cpu().numpy(), g[gk]) < tol * 5, k
     n = g["step_y"].shape[1]
     with torch.no_grad():
         a, s, b = m.allocate_inference_cache(u.shape[0])
@@ -60,11 +60,11 @@ def test_layer_forward_backward_step(name):
             assert a2 is not a and s2 is not s  # out-of-place, like the reference
             a, s, b = a2, s2, b2
             ys.append(o)
-    st = torch.stack(ys, 1).float().cpu().numpy()
+    st = torch.stack(ys, 1).detach().float().cpu().numpy()
     assert rel_err(st, g["step_y"]) < tol
-    assert rel_err(s.cpu().numpy(), g["step_ssm"]) < tol
-    assert rel_err(b.cpu().numpy(), g["step_bx"]) < tol
-    assert rel_err(a.cpu().numpy(), g["step_angle"]) < tol
+    assert rel_err(s.detach().cpu().numpy(), g["step_ssm"]) < tol
+    assert rel_err(b.detach().cpu().numpy(), g["step_bx"]) < tol
+    assert rel_err(a.detach().cpu().numpy(), g["step_angle"]) < tol
     assert rel_err(st, y[:, :n].float().detach().cpu().numpy()) < max(tol, 1e-4)
 
 
@@ -99,15 +99,15 @@ def test_lm_forward_and_step(name):
     ids = torch.from_numpy(g["ids"]).to(DEV)
     with torch.no_grad():
         lo = m(ids)
-        assert rel_err(lo.float().cpu().numpy(), g["logits"]) < tol
+        assert rel_err(lo.detach().float().cpu().numpy(), g["logits"]) < tol
         cache = m.allocate_inference_cache(ids.shape[0])
         lg = []
         for t in range(g["step_logits"].shape[1]):
             x = ids[:, t] if t % 2 else ids[:, t:t + 1]  # (B,) and (B, 1) both accepted
             out, cache = m.step(x, cache)
             lg.append(out)
-    assert rel_err(torch.stack(lg, 1).float().cpu().numpy(), g["step_logits"]) < tol
+    assert rel_err(torch.stack(lg, 1).detach().float().cpu().numpy(), g["step_logits"]) < tol
     for i, (a, s, b) in enumerate(cache):
-        assert rel_err(s.cpu().numpy(), g[f"cache{i}.ssm"]) < tol
-        assert rel_err(b.cpu().numpy(), g[f"cache{i}.bx"]) < tol
-        assert rel_err(a.cpu().numpy(), g[f"cache{i}.angle"]) < tol
+        assert rel_err(s.detach().cpu().numpy(), g[f"cache{i}.ssm"]) < tol
+        assert rel_err(b.detach().cpu().numpy(), g[f"cache{i}.bx"]) < tol
+        assert rel_err(a.detach().cpu().numpy(), g[f"cache{i}.angle"]) < tol

@@ -41,12 +41,12 @@ def test_siso_fwd_bwd_matches_reference(name):
     y = ssm_scan_siso(*ins)
     tol = _tol(ins[0].dtype)
     assert y.dtype == ins[0].dtype and y.shape == ins[0].shape
-    assert rel_err(y.float().cpu().numpy(), g["y"]) < tol
+    assert rel_err(y.detach().float().cpu().numpy(), g["y"]) < tol
     y.backward(_t(g, "dy"))
     for k, t in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
         f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
         assert t.grad.dtype == t.dtype
-        assert rel_err(t.grad.float().cpu().numpy(), g[k]) < tol * f, k
+        assert rel_err(t.grad.detach().float().cpu().numpy(), g[k]) < tol * f, k
 
 
 @pytest.mark.parametrize("name", MIMO)
@@ -56,11 +56,11 @@ def test_mimo_fwd_bwd_matches_reference(name):
     ins = [_t(g, k).requires_grad_(True) for k in ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")]
     y = ssm_scan_mimo(*ins)
     tol = _tol(ins[0].dtype)
-    assert rel_err(y.float().cpu().numpy(), g["y"]) < tol
+    assert rel_err(y.detach().float().cpu().numpy(), g["y"]) < tol
     y.backward(_t(g, "dy"))
     for k, t in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
         f = 5 if k in ("dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o") else 1
-        assert rel_err(t.grad.float().cpu().numpy(), g[k]) < tol * f, k
+        assert rel_err(t.grad.detach().float().cpu().numpy(), g[k]) < tol * f, k
 
 
 def _inputs(seed, Bn, L, H, P, D, R=None, dtype=torch.float32):
@@ -82,7 +82,7 @@ def _inputs(seed, Bn, L, H, P, D, R=None, dtype=torch.float32):
     for k, v in arrs.items():
         dt_ = dtype if k in ("x", "B", "C") else torch.float32
         tens[k] = torch.tensor(v, dtype=torch.float32).to(dt_).to(DEV)
-        arrs[k] = tens[k].double().cpu().numpy()  # oracle sees the rounded values
+        arrs[k] = tens[k].detach().double().cpu().numpy()  # oracle sees the rounded values
     return arrs, tens
 
 
@@ -96,13 +96,13 @@ def test_siso_sweep_against_oracle(D, P, L, dtype):
     y = ssm_scan_siso(*ins)
     yo, _, _ = O.siso_scan_fwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
     tol = _tol(dtype)
-    assert rel_err(y.double().cpu().numpy(), yo) < tol
+    assert rel_err(y.detach().double().cpu().numpy(), yo) < tol
     dy = torch.randn_like(y)
     y.backward(dy)
-    go = O.siso_scan_bwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")], dy.double().cpu().numpy())
+    go = O.siso_scan_bwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")], dy.detach().double().cpu().numpy())
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
         f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
-        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < tol * f, k
+        assert rel_err(tt.grad.detach().double().cpu().numpy(), go[k]) < tol * f, k
 
 
 @pytest.mark.parametrize("R,D,P", [(1, 16, 16), (2, 32, 64), (4, 64, 32), (8, 128, 64), (4, 64, 64)])
@@ -115,13 +115,13 @@ def test_mimo_sweep_against_oracle(R, D, P, dtype):
     y = ssm_scan_mimo(*ins)
     yo, _, _ = O.mimo_scan_fwd(*[arrs[k] for k in keys])
     tol = _tol(dtype)
-    assert rel_err(y.double().cpu().numpy(), yo) < tol
+    assert rel_err(y.detach().double().cpu().numpy(), yo) < tol
     dy = torch.randn_like(y)
     y.backward(dy)
-    go = O.mimo_scan_bwd(*[arrs[k] for k in keys], dy.double().cpu().numpy())
+    go = O.mimo_scan_bwd(*[arrs[k] for k in keys], dy.detach().double().cpu().numpy())
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
         f = 5 if k in ("dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o") else 1
-        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < tol * f, k
+        assert rel_err(tt.grad.detach().double().cpu().numpy(), go[k]) < tol * f, k
 
 
 def test_siso_strided_views_and_state_continuation():
@@ -133,9 +133,9 @@ def test_siso_strided_views_and_state_continuation():
     B5 = torch.randn(2, 96, 2, 4, 64, device=DEV)
     C5 = torch.randn(2, 96, 2, 4, 64, device=DEV)
     y = ssm_scan_siso(t["x"], B5[:, :, 0], C5[:, :, 0], t["ADT"], t["DT"], t["trap"], t["D"])
-    yo, ho, bo = O.siso_scan_fwd(arrs["x"], B5[:, :, 0].double().cpu().numpy(), C5[:, :, 0].double().cpu().numpy(),
+    yo, ho, bo = O.siso_scan_fwd(arrs["x"], B5[:, :, 0].detach().double().cpu().numpy(), C5[:, :, 0].detach().double().cpu().numpy(),
                                  arrs["ADT"], arrs["DT"], arrs["trap"], arrs["D"])
-    assert rel_err(y.double().cpu().numpy(), yo) < 1e-4
+    assert rel_err(y.detach().double().cpu().numpy(), yo) < 1e-4
     Bc, Cc = B5[:, :, 0].contiguous(), C5[:, :, 0].contiguous()
     a = slice(0, 41)
     b = slice(41, 96)
@@ -143,9 +143,9 @@ def test_siso_strided_views_and_state_continuation():
                                       t["trap"][:, a], t["D"])
     y2, h2, b2 = ssm_scan_siso_states(t["x"][:, b], Bc[:, b], Cc[:, b], t["ADT"][:, b], t["DT"][:, b],
                                       t["trap"][:, b], t["D"], h1, b1)
-    assert rel_err(torch.cat([y1, y2], 1).double().cpu().numpy(), yo) < 1e-4
-    assert rel_err(h2.double().cpu().numpy(), ho) < 1e-4
-    assert rel_err(b2.double().cpu().numpy(), bo) < 1e-4
+    assert rel_err(torch.cat([y1, y2], 1).detach().double().cpu().numpy(), yo) < 1e-4
+    assert rel_err(h2.detach().double().cpu().numpy(), ho) < 1e-4
+    assert rel_err(b2.detach().double().cpu().numpy(), bo) < 1e-4
 
 
 def test_empty_and_single_token_inputs():
@@ -156,7 +156,7 @@ def test_empty_and_single_token_inputs():
         assert y.shape == (2, L, 2, 16)
         if L:
             yo, _, _ = O.siso_scan_fwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
-            assert rel_err(y.double().cpu().numpy(), yo) < 1e-4
+            assert rel_err(y.detach().double().cpu().numpy(), yo) < 1e-4
         arrs, t = _inputs(4, 2, L, 2, 16, 32, R=2)
         y = ssm_scan_mimo(*[t[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")])
         assert y.shape == (2, L, 2, 16)
@@ -173,4 +173,4 @@ def test_long_sequence_slices_against_oracle():
     arrs, t = _inputs(11, 1, 32768, 2, 64, 128, dtype=torch.bfloat16)
     y = ssm_scan_siso(*[t[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
     yo, _, _ = O.siso_scan_fwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
-    assert rel_err(y.double().cpu().numpy(), yo) < 2e-2
+    assert rel_err(y.detach().double().cpu().numpy(), yo) < 2e-2
