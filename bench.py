@@ -226,6 +226,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the global batch (profiling runs on a smaller case)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -249,6 +251,8 @@ def main():
     from mamba3_ssm import _lib
     _lib.load()
 
+    if args.batch:
+        C5["batch"] = args.batch
     Bt, L, H, P, D = C5["batch"], C5["seqlen"], C5["nheads"], C5["headdim"], C5["dstate"]
     if Bt % world:
         raise SystemExit("bench.py: batch 16 must divide by the number of GPUs")

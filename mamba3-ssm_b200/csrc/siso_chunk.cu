@@ -9,20 +9,36 @@
 //   y_i     = e^{lambda_i} C_i k_c + sum_{j<i} e^{lambda_i - lambda_{j+1}} mu_j (C_i.B_j) x_j
 //             + (beta_i C_i.B_i + D) x_i
 //   k_{c+1} = e^{lambda_Q} k_c + sum_j e^{lambda_Q - lambda_{j+1}} mu_j x_j B_j^T
-// Four tcgen05 MMAs per chunk (M = 128, accumulators in TMEM):
-//   G   = C B^T                  (128 x 128, K = D)        A, B: K-major smem (TMA, SW128)
-//   Y1  = C k_c^T                (128 x 64,  K = D)        B: k_c^T in smem, MN-major
-//   Y2  = G' X                   (128 x 64,  K = Q)        A: G' in TMEM (bf16), B: X MN-major
-//   dK^T = B^T (w o X)           (128 x 64,  K = Q)        A: B tile read MN-major
-// where G' = G masked and scaled on the CUDA cores (exp2 of lambda differences), then
-// y = e^{lambda} Y1 + Y2 + D x and k^T = e^{lambda_Q} k^T + dK^T (fp32, in registers).
+// Four tcgen05 MMAs per chunk (M = 128, fp32 accumulators in TMEM):
+//   G    = C B^T        (128 x 128, K = D)   A, B: K-major smem tiles (TMA, 128B swizzle)
+//   Y1   = C k_c^T      (128 x 64,  K = D)   B: k_c^T (bf16) in smem, MN-major
+//   Y2   = G' X         (128 x 64,  K = Q)   A: G' (bf16) in TMEM, B: X tile MN-major
+//   dK^T = B^T (w o X)  (128 x 64,  K = Q)   A: the B tile read MN-major
+// G' is G masked to j <= i and scaled: G'_ij = G_ij e^{lambda_i - lambda_{j+1}} mu_j for
+// j < i, G'_ii = beta_i G_ii + D (the D skip rides on the diagonal). The decay factor is
+// split per 32-column block b as e^{lambda_i - lambda_{32b+1}} * e^{lambda_{32b+1} -
+// lambda_{j+1}}; a block whose exponents could leave the fp32 range falls back to one exp2
+// per element. Then y = e^{lambda} Y1 + Y2 and k^T = e^{lambda_Q} k^T + dK^T.
 //
-// One CTA (4 warps, 128 threads) owns one (b, h) and walks its chunks in order; thread i
-// owns TMEM lane i (row i of G, Y1, Y2; state row d = i of k^T). Shared memory holds one
-// 80 KB stage (C, B, X) plus a 16 KB buffer that carries k_c^T, then w o X, then k_{c+1}^T;
-// two CTAs fit on one SM (TMEM 2 x 256 columns), so one CTA's math overlaps the other's
-// loads. The next chunk's TMA is issued as soon as the last MMA reading the stage is done.
+// Warp-specialised, persistent CTA (one per SM, 16 warps), walking its (b, h) units
+// chunk by chunk:
+//   warp 0      TMA producer: C, B (2 x 64-column boxes each) and X of a chunk into a
+//               2-stage ring (80 KB per stage)
+//   warp 1      tcgen05 MMA issuer (one elected lane) and TMEM owner (512 columns:
+//               two buffer sets of G | dK, Y1, Y2 so consecutive chunks overlap)
+//   warps 2-3   per-chunk scalars (decay cumsum, mu, block factors, state weights) into a
+//               4-slot ring, even / odd chunks, running ahead of the consumers
+//   warps 4-7   even chunks: G -> G' in TMEM (in place, packed bf16), w o X into smem,
+//               then the epilogue y = e^{lambda} Y1 + Y2 -> global (bf16)
+//   warps 12-15 odd chunks: the same
+//   warps 8-11  state: k^T (fp32, registers) <- decay k^T + dK^T, bf16 copy for the next Y1
+// The TMA warp also streams the chunks 2-3 ahead into L2, so refilling a stage (which can
+// only start once the MMAs reading it are done) is served from L2.
+// All hand-offs are mbarriers with bounded waits; on a timeout the kernel records an error
+// and drains.
 #include <cudaTypedefs.h>
+
+#include <cstddef>
 
 #include "m3_common.cuh"
 #include "siso_chunk.cuh"
@@ -36,33 +52,55 @@ using namespace sm100;
 constexpr int Q = 128;
 constexpr int kP = 64;
 constexpr int kD = 128;
-constexpr int kThreads = 128;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t COL_G = 0, COL_DK = 64, COL_Y1 = 128, COL_Y2 = 192;
-constexpr uint32_t kTileBytes = Q * 64 * 2;           // one SW128 tile: 128 rows x 128 B
-constexpr uint32_t kStageBytes = 5 * kTileBytes;      // C(2) + B(2) + X
+constexpr int kThreads = 512;
+constexpr int NS = 2;    // TMA stages
+constexpr int NSC = 4;   // scalar slots
+constexpr int kPrefetch = 3;  // chunks streamed into L2 ahead of their TMA load
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTileBytes = Q * 64 * 2;       // one SW128 tile: 128 rows x 128 B
+constexpr uint32_t kStageBytes = 5 * kTileBytes;  // C(2) + B(2) + X
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kSafeExp2 = 120.f;
 
-struct __align__(1024) Smem {
-  uint8_t C[2][kTileBytes];   // C[t][d], d halves 0-63 / 64-127, K-major SW128
-  uint8_t Bt[2][kTileBytes];  // B[t][d], same layout
-  uint8_t X[kTileBytes];      // x[t][p], SW128
-  uint8_t S[kTileBytes];      // k_c^T[d][p] -> (w o x)[t][p] -> k_{c+1}^T[d][p]
-  float lam2[Q + 1];          // lambda_i * log2(e)
+// TMEM columns of buffer set p: G (128, G' packed in its first 64, dK in its last 64),
+// Y1 (64), Y2 (64).
+__device__ __forceinline__ uint32_t col_g(int p) { return 256u * p; }
+__device__ __forceinline__ uint32_t col_dk(int p) { return 256u * p + 64u; }
+__device__ __forceinline__ uint32_t col_y1(int p) { return 256u * p + 128u; }
+__device__ __forceinline__ uint32_t col_y2(int p) { return 256u * p + 192u; }
+
+struct __align__(16) ScalSlot {
+  float colf[Q];      // e^{lambda_{32b+1} - lambda_{j+1}} mu_j (read as float4)
   float mu[Q];
   float beta[Q];
-  float wgt[Q];               // state-update weights
-  float av[Q + 1];            // a_t of rows t0 .. t0+Q
-  float gv[Q + 1];            // gamma_t of rows t0 .. t0+Q
-  float warp_sum[4];
-  float adt_next;
+  float w[Q];         // state-update weights
+  float lam2[Q + 1];  // lambda_i * log2(e)
   float decay_end;
-  uint32_t tmem_base;
-  uint64_t bar_tma;
-  uint64_t bar_mma;
+  float dskip;        // D of the unit's head (added on the diagonal of G')
+  float a0, g0;       // a, gamma of the unit's first row (initial state)
+  int n;              // valid rows in the chunk
+  int flags;          // bit0 first chunk of unit, bit1 last, bits 4..7 block b factorisable
 };
 
-__device__ int g_chunk_error;  // set when a bounded wait gives up (diagnostics)
+struct __align__(1024) Smem {
+  uint8_t stage[NS][5][kTileBytes];  // C(d 0-63), C(d 64-127), B(0-63), B(64-127), X
+  uint8_t xs[2][kTileBytes];         // (w o x)[t][p]
+  uint8_t kbuf[kTileBytes];          // k_c^T[d][p]
+  ScalSlot sc[NSC];
+  float side_x[2][kP];               // last row of a unit (for the final B*x)
+  float side_b[2][kD];
+  uint64_t stage_full[NS], stage_empty[NS];
+  uint64_t g_full[2], gp_ready[2], g_free[2], dk_full[2], y_full[2], y_free[2];
+  uint64_t k_ready;
+  uint64_t scal_full[NSC], scal_empty[NSC];
+  uint32_t tmem_base;
+};
+
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory budget");
+static_assert(offsetof(ScalSlot, colf) % 16 == 0 && sizeof(ScalSlot) % 16 == 0 && offsetof(Smem, sc) % 16 == 0,
+              "float4 reads of the column factors need 16-byte alignment");
+
+__device__ int g_chunk_error;  // set when a bounded wait gives up
 
 struct ChunkArgs {
   int Bn, L, H;
@@ -77,337 +115,572 @@ struct ChunkArgs {
   float* bx_last;
 };
 
-__device__ __forceinline__ uint32_t tmem_lane_addr(uint32_t base, int warp, uint32_t col) {
-  return base + ((uint32_t)(warp * 32) << 16) + col;
+__device__ __forceinline__ uint32_t lane_addr(uint32_t base, int warp, uint32_t col) {
+  return base + ((uint32_t)((warp & 3) * 32) << 16) + col;
 }
-
-// element (row r, column c) of a 128-row SW128 tile of 64 bf16 per row
+// byte offset of (row r, element c) in a 128-row SW128 tile with 64 bf16 per row
 __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
   return (uint32_t)r * 128u + ((((uint32_t)c >> 3) ^ ((uint32_t)r & 7u)) << 4) + (((uint32_t)c & 7u) << 1);
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+struct ChunkPos {
+  int b, h, c, t0, n;
+  bool first, last;
+};
+__device__ __forceinline__ ChunkPos chunk_pos(const ChunkArgs& a, int g, int nch) {
+  ChunkPos q;
+  const int k = g / nch;
+  q.c = g - k * nch;
+  const int u = blockIdx.x + k * gridDim.x;
+  q.b = u / a.H;
+  q.h = u - q.b * a.H;
+  q.t0 = q.c * Q;
+  q.n = min(Q, a.L - q.t0);
+  q.first = q.c == 0;
+  q.last = q.c == nch - 1;
+  return q;
+}
+
+__device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity) {
+  if (mbar_wait(bar, parity, 1u << 24)) return true;
+  atomicExch(&g_chunk_error, 1);
+  return false;
+}
+
+__device__ __forceinline__ float ld_scal(const float* p, const Str3& s, int b, int t, int h) {
+  return p[(int64_t)b * s.b + (int64_t)t * s.l + (int64_t)h * s.h];
+}
+
+// ------------------------------------------------------------------------------------
+// warps 2 and 3: per-chunk scalars. Warp 2 takes the even chunks, warp 3 the odd ones;
+// each loads the raw ADT / DT / trap of its next chunk before computing the current one.
+// ------------------------------------------------------------------------------------
+struct RawScal {
+  float adt[4], dt[4], tr[4];  // rows lane + 32k
+  float adtQ, dtQ, trQ;        // row t0 + Q (lane 0)
+};
+
+__device__ __forceinline__ void load_raw(const ChunkArgs& a, const ChunkPos& cp, int lane, RawScal& r) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int t = cp.t0 + lane + 32 * k;
+    const bool v = t < a.L;
+    r.adt[k] = v ? ld_scal(a.adt, a.sadt, cp.b, t, cp.h) : 0.f;
+    r.dt[k] = v ? ld_scal(a.dt, a.sdt, cp.b, t, cp.h) : 0.f;
+    r.tr[k] = v ? ld_scal(a.trap, a.strap, cp.b, t, cp.h) : 0.f;
+  }
+  const int t = cp.t0 + Q;
+  const bool v = lane == 0 && t < a.L;
+  r.adtQ = v ? ld_scal(a.adt, a.sadt, cp.b, t, cp.h) : 0.f;
+  r.dtQ = v ? ld_scal(a.dt, a.sdt, cp.b, t, cp.h) : 0.f;
+  r.trQ = v ? ld_scal(a.trap, a.strap, cp.b, t, cp.h) : 0.f;
+}
+
+__device__ void scalar_role(const ChunkArgs& a, Smem& s, int G, int nch, int lane, int g_first) {
+  RawScal raw;
+  if (g_first < G) load_raw(a, chunk_pos(a, g_first, nch), lane, raw);
+  for (int g = g_first; g < G; g += 2) {
+    const int q = g % NSC;
+    const ChunkPos cp = chunk_pos(a, g, nch);
+    float adt[4], av[4], be[4], ga[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const bool v = cp.t0 + lane + 32 * k < a.L;
+      adt[k] = raw.adt[k];
+      const float dt = raw.dt[k];
+      const float tr = v ? sigmoidf_(raw.tr[k]) : 0.f;
+      be[k] = dt * (1.0f - tr) + 0.5f * dt * tr;
+      ga[k] = 0.5f * dt * tr;
+      av[k] = v ? exp2f(adt[k] * kLog2e) : 0.f;
+    }
+    float adtQ, aQ, gQ;
+    {
+      const bool v = cp.t0 + Q < a.L;
+      adtQ = __shfl_sync(0xffffffffu, raw.adtQ, 0);
+      aQ = v ? exp2f(adtQ * kLog2e) : 0.f;
+      const float trQ = v ? sigmoidf_(__shfl_sync(0xffffffffu, raw.trQ, 0)) : 0.f;
+      gQ = 0.5f * __shfl_sync(0xffffffffu, raw.dtQ, 0) * trQ;
+    }
+    if (g + 2 < G) load_raw(a, chunk_pos(a, g + 2, nch), lane, raw);  // next chunk of this warp
+    // lambda: inclusive scan of (r == 0 ? 0 : ADT_r) over r = lane + 32k
+    float lam[4];
+    float carry = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float v = (k == 0 && lane == 0) ? 0.f : adt[k];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      lam[k] = (v + carry) * kLog2e;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    const float lamQ = (carry + adtQ) * kLog2e;
+    // next-row values: a_{r+1}, gamma_{r+1}, lam2_{r+1}
+    float an[4], gn[4], ln[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float a1 = __shfl_down_sync(0xffffffffu, av[k], 1);
+      const float g1 = __shfl_down_sync(0xffffffffu, ga[k], 1);
+      const float l1 = __shfl_down_sync(0xffffffffu, lam[k], 1);
+      float aw, gw, lw;
+      if (k < 3) {
+        aw = __shfl_sync(0xffffffffu, av[k + 1 < 4 ? k + 1 : 3], 0);
+        gw = __shfl_sync(0xffffffffu, ga[k + 1 < 4 ? k + 1 : 3], 0);
+        lw = __shfl_sync(0xffffffffu, lam[k + 1 < 4 ? k + 1 : 3], 0);
+      } else {
+        aw = aQ; gw = gQ; lw = lamQ;
+      }
+      an[k] = lane < 31 ? a1 : aw;
+      gn[k] = lane < 31 ? g1 : gw;
+      ln[k] = lane < 31 ? l1 : lw;
+    }
+    const int e = cp.n - 1;  // last valid row
+    const int eg = (e >> 5) & 3;
+    const float lam_sel = eg == 0 ? lam[0] : (eg == 1 ? lam[1] : (eg == 2 ? lam[2] : lam[3]));
+    const float lam_e = __shfl_sync(0xffffffffu, lam_sel, e & 31);
+    const float lam_end = cp.last ? lam_e : lamQ;
+    // Split-exponent safety. Column factors span at most 32 steps, row factors at most
+    // 128: with |ADT| <= 2.5 and ADT <= 0.6 everywhere in the chunk all blocks are safe.
+    float amax = fabsf(adtQ), pmax = adtQ;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      amax = fmaxf(amax, fabsf(adt[k]));
+      pmax = fmaxf(pmax, adt[k]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, o));
+    }
+    const bool all_safe = amax <= 2.5f && pmax <= 0.6f;
+    int flags = (cp.first ? 1 : 0) | (cp.last ? 2 : 0);
+    ScalSlot& sl = s.sc[q];
+    if (!wait_or_flag(&s.scal_empty[q], ((g / NSC) & 1) ^ 1)) return;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = lane + 32 * k;
+      const float mu = an[k] * be[k] + gn[k];
+      const float ref = __shfl_sync(0xffffffffu, lam[k], 1);  // lambda_{32k+1}
+      const float ex = ref - ln[k];
+      sl.lam2[j] = lam[k];
+      sl.mu[j] = mu;
+      sl.beta[j] = be[k];
+      sl.colf[j] = exp2f(ex) * mu;
+      float wj;
+      if (!cp.last) wj = exp2f(lamQ - ln[k]) * mu;
+      else wj = (j < e) ? exp2f(lam_e - ln[k]) * mu : (j == e ? be[k] : 0.f);
+      sl.w[j] = wj;
+    }
+    if (all_safe) {
+      flags |= 0xF0;
+    } else {
+      // per block: |column exponents| bounded, and row factors bounded above
+      float gmax[4], mx_grp[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float v = lam[k], rm = lane >= 1 ? lam[k] : -INFINITY;
+        const float ref = __shfl_sync(0xffffffffu, lam[k], 1);
+        float m = fabsf(ref - ln[k]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+          rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, o));
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        }
+        gmax[k] = v;
+        mx_grp[k] = rm;
+        if (m <= kSafeExp2) flags |= 1 << (4 + k);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float mx = mx_grp[k];
+#pragma unroll
+        for (int k2 = k + 1; k2 < 4; ++k2) mx = fmaxf(mx, gmax[k2]);
+        const float ref = __shfl_sync(0xffffffffu, lam[k], 1);
+        if (!(mx - ref <= kSafeExp2)) flags &= ~(1 << (4 + k));
+      }
+    }
+    if (lane == 0) {
+      sl.lam2[Q] = lamQ;
+      sl.decay_end = exp2f(lam_end);
+      sl.dskip = a.Dskip[cp.h * a.sD];
+      sl.a0 = av[0];
+      sl.g0 = ga[0];
+      sl.n = cp.n;
+      sl.flags = flags;
+    }
+    mbar_arrive(&s.scal_full[q]);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// G -> G' (TMEM, in place) and w o X -> smem. Warps 4-7 take the even chunks, warps 12-15
+// the odd ones (each chunk parity has its own TMEM buffer set), so two chunks are masked
+// concurrently. Thread i owns row i. Warp r (rows 32r..32r+31) sees column blocks b < r
+// entirely below the diagonal, block r on it and blocks b > r above it (zeros, not read).
+// Blocks go in increasing order with the TMEM load of the next block issued before the
+// current one is converted; the packed bf16 G' of block b lands in columns 16b..16b+15,
+// which this thread has already read.
+// ------------------------------------------------------------------------------------
+// One 32-column block of row i: full (below the diagonal), diagonal and above-diagonal
+// blocks share one code path through the column limit il = i - 32 qd. When the block's
+// split exponents could leave the fp32 range (`exact`), the factor is one exp2 per element.
+__device__ __forceinline__ void mask_block(const uint32_t (&r)[32], uint32_t (&pk)[16], int qd, int i,
+                                           const ScalSlot& sl, float li, float bi, float dk, bool exact) {
+  const float rowf = exact ? 0.f : exp2f(li - sl.lam2[32 * qd + 1]);
+  const int il = i - 32 * qd;
+  const float4* cf4 = reinterpret_cast<const float4*>(sl.colf + 32 * qd);
+#pragma unroll
+  for (int e4 = 0; e4 < 8; ++e4) {
+    float cc[4];
+    if (!exact) {
+      const float4 c = cf4[e4];
+      cc[0] = c.x * rowf; cc[1] = c.y * rowf; cc[2] = c.z * rowf; cc[3] = c.w * rowf;
+    } else {
+#pragma unroll
+      for (int z = 0; z < 4; ++z) {
+        const int j = 32 * qd + 4 * e4 + z;
+        cc[z] = j < i ? exp2f(li - sl.lam2[j + 1]) * sl.mu[j] : 0.f;
+      }
+    }
+    float v[4];
+#pragma unroll
+    for (int z = 0; z < 4; ++z) {
+      const int jl = 4 * e4 + z;
+      const float gij = __uint_as_float(r[jl]);
+      const float off = jl == il ? fmaf(gij, bi, dk) : 0.f;
+      v[z] = jl < il ? gij * cc[z] : off;
+    }
+    pk[2 * e4] = pack_bf16(v[0], v[1]);
+    pk[2 * e4 + 1] = pack_bf16(v[2], v[3]);
+  }
+}
+
+__device__ __noinline__ void stash_last_row(Smem& s, int p, int st, int i) {
+  const uint8_t* xt = s.stage[st][4];
+  for (int pp = 0; pp < kP; ++pp)
+    s.side_x[p][pp] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(xt + sw128_off(i, pp)));
+  for (int d = 0; d < kD; ++d)
+    s.side_b[p][d] =
+        __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(s.stage[st][2 + (d >> 6)] + sw128_off(i, d & 63)));
+}
+
+// y = e^{lambda} Y1 + Y2 of chunk g, thread = row i
+__device__ __forceinline__ void epilogue(const ChunkArgs& a, Smem& s, uint32_t tbase, int g, int nch, int warp, int i) {
+  const int p = g & 1;
+  const ChunkPos cp = chunk_pos(a, g, nch);
+  const ScalSlot& sl = s.sc[g % NSC];
+  const float sc = exp2f(sl.lam2[i]);
+  const bool valid = i < cp.n;
+  uint4* dst = reinterpret_cast<uint4*>(a.y + (int64_t)cp.b * a.sy.b + (int64_t)(cp.t0 + (valid ? i : 0)) * a.sy.l +
+                                        (int64_t)cp.h * a.sy.h);
+#pragma unroll
+  for (int qt = 0; qt < 4; ++qt) {
+    uint32_t y1[16], y2[16];
+    tmem_ld16(lane_addr(tbase, warp, col_y1(p) + 16 * qt), y1);
+    tmem_ld16(lane_addr(tbase, warp, col_y2(p) + 16 * qt), y2);
+    tmem_wait_ld();
+    if (qt == 3) {
+      tc_fence_before();
+      mbar_arrive(&s.y_free[p]);
+    }
+    uint32_t outp[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      outp[e] = pack_bf16(fmaf(sc, __uint_as_float(y1[2 * e]), __uint_as_float(y2[2 * e])),
+                          fmaf(sc, __uint_as_float(y1[2 * e + 1]), __uint_as_float(y2[2 * e + 1])));
+    if (valid) {
+      dst[2 * qt] = make_uint4(outp[0], outp[1], outp[2], outp[3]);
+      dst[2 * qt + 1] = make_uint4(outp[4], outp[5], outp[6], outp[7]);
+    }
+  }
+}
+
+__device__ void mask_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, int nch, int warp, int i, int parity) {
+  const int wr = warp & 3;
+  for (int g = parity; g < G; g += 2) {
+    const int p = g & 1, q = g % NSC, st = g % NS;
+    if (!wait_or_flag(&s.scal_full[q], (g / NSC) & 1)) return;
+    if (!wait_or_flag(&s.g_full[p], (g >> 1) & 1)) return;
+    // the stage's phase is already complete (G was computed from it); this wait makes its
+    // TMA writes visible to this thread's X / B reads
+    if (!wait_or_flag(&s.stage_full[st], (g / NS) & 1)) return;
+    tc_fence_after();
+    const ScalSlot& sl = s.sc[q];
+    const float li = sl.lam2[i];
+    const float bi = sl.beta[i];
+    const float dk = sl.dskip;
+    const int flags = sl.flags;
+    // one block at a time; the packed store of block b lands on columns this thread read
+#pragma unroll 1
+    for (int qd = 0; qd <= wr; ++qd) {
+      uint32_t r[32];
+      tmem_ld32(lane_addr(tbase, warp, col_g(p) + 32 * qd), r);
+      tmem_wait_ld();
+      uint32_t pk[16];
+      mask_block(r, pk, qd, i, sl, li, bi, dk, !((flags >> (4 + qd)) & 1));
+      tmem_st16(lane_addr(tbase, warp, col_g(p) + 16 * qd), pk);
+    }
+    {
+      uint32_t z[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) z[e] = 0u;
+#pragma unroll 1
+      for (int qd = wr + 1; qd < 4; ++qd) tmem_st16(lane_addr(tbase, warp, col_g(p) + 16 * qd), z);
+    }
+    // (w o x) row i
+    {
+      const float wi = sl.w[i];
+      const uint8_t* xt = s.stage[st][4];
+      uint8_t* dst = s.xs[p];
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xt + sw128_off(i, 8 * cc));
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[e]));
+          o[e] = pack_bf16(f.x * wi, f.y * wi);
+        }
+        *reinterpret_cast<uint4*>(dst + sw128_off(i, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      if ((flags & 2) && a.bx_last && i == sl.n - 1) stash_last_row(s, p, st, i);
+    }
+    tmem_wait_st();
+    fence_proxy_async_smem();
+    tc_fence_before();
+    mbar_arrive(&s.gp_ready[p]);
+    // this chunk's outputs (Y1 and Y2 complete with dK at one commit point)
+    if (!wait_or_flag(&s.y_full[p], (g >> 1) & 1)) return;
+    tc_fence_after();
+    epilogue(a, s, tbase, g, nch, warp, i);
+    mbar_arrive(&s.scal_empty[q]);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// warps 8-11: carried state, thread = state row d
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void write_kbuf(Smem& s, int d, const float (&k)[kP]) {
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc) {
+    uint4 v;
+    v.x = pack_bf16(k[8 * cc + 0], k[8 * cc + 1]);
+    v.y = pack_bf16(k[8 * cc + 2], k[8 * cc + 3]);
+    v.z = pack_bf16(k[8 * cc + 4], k[8 * cc + 5]);
+    v.w = pack_bf16(k[8 * cc + 6], k[8 * cc + 7]);
+    *reinterpret_cast<uint4*>(s.kbuf + sw128_off(d, 8 * cc)) = v;
+  }
+}
+
+__device__ __forceinline__ void init_state(const ChunkArgs& a, const ChunkPos& cp, const ScalSlot& sl, int d,
+                                        float (&k)[kP]) {
+  const float a0 = sl.a0, g0 = sl.g0;
+  const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * kD;
+#pragma unroll
+  for (int pp = 0; pp < kP; ++pp) {
+    float v = 0.f;
+    if (a.h0) v = a0 * a.h0[sb + (int64_t)pp * kD + d];
+    if (a.bx0) v = fmaf(g0, a.bx0[sb + (int64_t)pp * kD + d], v);
+    k[pp] = v;
+  }
+}
+
+__device__ __forceinline__ void store_final(const ChunkArgs& a, const Smem& s, const ChunkPos& cp, int p, int d,
+                                         const float (&k)[kP]) {
+  const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * kD;
+  if (a.h_last)
+    for (int pp = 0; pp < kP; ++pp) a.h_last[sb + (int64_t)pp * kD + d] = k[pp];
+  if (a.bx_last) {
+    const float bd = s.side_b[p][d];
+    for (int pp = 0; pp < kP; ++pp) a.bx_last[sb + (int64_t)pp * kD + d] = s.side_x[p][pp] * bd;
+  }
+}
+
+__device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, int nch, int warp, int d) {
+  float k[kP];
+  for (int g = 0; g < G; ++g) {
+    const int p = g & 1, q = g % NSC;
+    const ChunkPos cp = chunk_pos(a, g, nch);
+    if (!wait_or_flag(&s.scal_full[q], (g / NSC) & 1)) return;
+    const ScalSlot& sl = s.sc[q];
+    if (cp.first) {
+      if (a.h0 || a.bx0) {
+        init_state(a, cp, sl, d, k);
+      } else {
+#pragma unroll
+        for (int pp = 0; pp < kP; ++pp) k[pp] = 0.f;
+      }
+      write_kbuf(s, d, k);
+      fence_proxy_async_smem();
+      mbar_arrive(&s.k_ready);
+    }
+    if (!wait_or_flag(&s.dk_full[p], (g >> 1) & 1)) return;
+    tc_fence_after();
+    const float dec = sl.decay_end;
+    const int flags = sl.flags;
+#pragma unroll
+    for (int qt = 0; qt < 4; ++qt) {
+      uint32_t r[16];
+      tmem_ld16(lane_addr(tbase, warp, col_dk(p) + 16 * qt), r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) k[16 * qt + e] = fmaf(dec, k[16 * qt + e], __uint_as_float(r[e]));
+    }
+    tc_fence_before();
+    mbar_arrive(&s.g_free[p]);
+    if (!(flags & 2)) {
+      write_kbuf(s, d, k);
+      fence_proxy_async_smem();
+      mbar_arrive(&s.k_ready);
+    } else if (a.h_last || a.bx_last) {
+      store_final(a, s, cp, p, d, k);
+    }
+    mbar_arrive(&s.scal_empty[q]);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1)
 siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_B,
                       const __grid_constant__ CUtensorMap tm_C, ChunkArgs a) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int b = blockIdx.x / a.H, h = blockIdx.x % a.H;
-  const int L = a.L;
-  const int nchunk = (L + Q - 1) / Q;
+  const int nch = (a.L + Q - 1) / Q;
+  const int units = a.Bn * a.H;
+  const int my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int G = my_units * nch;
 
   if (tid == 0) {
-    prefetch_tensormap(&tm_x);
-    prefetch_tensormap(&tm_B);
-    prefetch_tensormap(&tm_C);
-    mbar_init(&s.bar_tma, 1);
-    mbar_init(&s.bar_mma, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&s.stage_full[i], 1);
+      mbar_init(&s.stage_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.g_full[i], 1);
+      mbar_init(&s.gp_ready[i], 128);
+      mbar_init(&s.g_free[i], 128);
+      mbar_init(&s.dk_full[i], 1);
+      mbar_init(&s.y_full[i], 1);
+      mbar_init(&s.y_free[i], 128);
+    }
+    mbar_init(&s.k_ready, 128);
+    for (int i = 0; i < NSC; ++i) {
+      mbar_init(&s.scal_full[i], 32);
+      mbar_init(&s.scal_empty[i], 2 * 128);
+    }
     fence_barrier_init();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     tmem_alloc(&s.tmem_base, kTmemCols);
     tmem_relinquish();
   }
-  // initial carried state k_0^T[d][p] = a_0 h0[p][d] + gamma_0 bx0[p][d]   (thread = d)
-  float kst[kP];
-  {
-    const int d = tid;
-    float a0 = 0.f, g0 = 0.f;
-    if (a.h0 || a.bx0) {
-      a0 = expf(a.adt[(int64_t)b * a.sadt.b + (int64_t)h * a.sadt.h]);
-      const float dt0 = a.dt[(int64_t)b * a.sdt.b + (int64_t)h * a.sdt.h];
-      const float tr0 = sigmoidf_(a.trap[(int64_t)b * a.strap.b + (int64_t)h * a.strap.h]);
-      g0 = 0.5f * dt0 * tr0;
-    }
-    const int64_t sb = ((int64_t)b * a.H + h) * kP * kD;
-#pragma unroll
-    for (int p = 0; p < kP; ++p) {
-      float v = 0.f;
-      if (a.h0) v = a0 * a.h0[sb + (int64_t)p * kD + d];
-      if (a.bx0) v = fmaf(g0, a.bx0[sb + (int64_t)p * kD + d], v);
-      kst[p] = v;
-    }
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 v;
-      v.x = pack_bf16(kst[8 * c + 0], kst[8 * c + 1]);
-      v.y = pack_bf16(kst[8 * c + 2], kst[8 * c + 3]);
-      v.z = pack_bf16(kst[8 * c + 4], kst[8 * c + 5]);
-      v.w = pack_bf16(kst[8 * c + 6], kst[8 * c + 7]);
-      *reinterpret_cast<uint4*>(s.S + sw128_off(d, 8 * c)) = v;
-    }
-  }
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = s.tmem_base;
-  const float Dk = a.Dskip[h * a.sD];
 
-  if (tid == 0) {
-    mbar_expect_tx(&s.bar_tma, kStageBytes);
-    tma_load_4d(s.C[0], &tm_C, &s.bar_tma, 0, h, 0, b);
-    tma_load_4d(s.C[1], &tm_C, &s.bar_tma, 64, h, 0, b);
-    tma_load_4d(s.Bt[0], &tm_B, &s.bar_tma, 0, h, 0, b);
-    tma_load_4d(s.Bt[1], &tm_B, &s.bar_tma, 64, h, 0, b);
-    tma_load_4d(s.X, &tm_x, &s.bar_tma, 0, h, 0, b);
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&tm_x);
+      prefetch_tensormap(&tm_B);
+      prefetch_tensormap(&tm_C);
+      for (int g = 0; g < G; ++g) {
+        const int st = g % NS;
+        if (!wait_or_flag(&s.stage_empty[st], ((g / NS) & 1) ^ 1)) break;
+        const ChunkPos cp = chunk_pos(a, g, nch);
+        mbar_expect_tx(&s.stage_full[st], kStageBytes);
+        tma_load_4d(s.stage[st][0], &tm_C, &s.stage_full[st], 0, cp.h, cp.t0, cp.b);
+        tma_load_4d(s.stage[st][1], &tm_C, &s.stage_full[st], 64, cp.h, cp.t0, cp.b);
+        tma_load_4d(s.stage[st][2], &tm_B, &s.stage_full[st], 0, cp.h, cp.t0, cp.b);
+        tma_load_4d(s.stage[st][3], &tm_B, &s.stage_full[st], 64, cp.h, cp.t0, cp.b);
+        tma_load_4d(s.stage[st][4], &tm_x, &s.stage_full[st], 0, cp.h, cp.t0, cp.b);
+        // stream the following chunks into L2 so a stage refill is an L2 hit
+        for (int ahead = (g == 0 ? 1 : kPrefetch); ahead <= kPrefetch; ++ahead) {
+          if (g + ahead >= G) break;
+          const ChunkPos pf = chunk_pos(a, g + ahead, nch);
+          tma_prefetch_l2_4d(&tm_C, 0, pf.h, pf.t0, pf.b);
+          tma_prefetch_l2_4d(&tm_C, 64, pf.h, pf.t0, pf.b);
+          tma_prefetch_l2_4d(&tm_B, 0, pf.h, pf.t0, pf.b);
+          tma_prefetch_l2_4d(&tm_B, 64, pf.h, pf.t0, pf.b);
+          tma_prefetch_l2_4d(&tm_x, 0, pf.h, pf.t0, pf.b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t I_G = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t I_Y = idesc_bf16_f32(128, 64, false, true);
+      constexpr uint32_t I_DK = idesc_bf16_f32(128, 64, true, true);
+      const uint32_t a_kb = smem_u32(s.kbuf);
+      auto stage_addr = [&](int st, int t) { return smem_u32(s.stage[st][t]); };
+      auto issue_g = [&](int g) -> bool {
+        const int st = g % NS, p = g & 1;
+        if (!wait_or_flag(&s.stage_full[st], (g / NS) & 1)) return false;
+        if (!wait_or_flag(&s.g_free[p], ((g >> 1) & 1) ^ 1)) return false;
+        tc_fence_after();
+        const uint32_t c0 = stage_addr(st, 0), b0 = stage_addr(st, 2);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
+          mma_ss(tbase + col_g(p), sdesc_sw128(c0 + koff, 16, 1024), sdesc_sw128(b0 + koff, 16, 1024), I_G, kk > 0);
+        }
+        mma_commit(&s.g_full[p]);
+        return true;
+      };
+      auto issue_y1 = [&](int g) -> bool {
+        const int st = g % NS, p = g & 1;
+        if (!wait_or_flag(&s.k_ready, g & 1)) return false;
+        if (!wait_or_flag(&s.y_free[p], ((g >> 1) & 1) ^ 1)) return false;
+        tc_fence_after();
+        const uint32_t c0 = stage_addr(st, 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
+          mma_ss(tbase + col_y1(p), sdesc_sw128(c0 + koff, 16, 1024),
+                 sdesc_sw128(a_kb + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
+        }
+        return true;
+      };
+      bool ok = G == 0 || (issue_g(0) && issue_y1(0));
+      for (int g = 0; g < G && ok; ++g) {
+        const int st = g % NS, p = g & 1;
+        if (g + 1 < G && !issue_g(g + 1)) break;
+        if (!wait_or_flag(&s.gp_ready[p], (g >> 1) & 1)) break;
+        tc_fence_after();
+        const uint32_t xa = stage_addr(st, 4), ba = stage_addr(st, 2), xsa = smem_u32(s.xs[p]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_ts(tbase + col_y2(p), tbase + col_g(p) + 8u * kk, sdesc_sw128(xa + (uint32_t)kk * 2048u, kTileBytes, 1024),
+                 I_Y, kk > 0);
+          mma_ss(tbase + col_dk(p), sdesc_sw128(ba + (uint32_t)kk * 2048u, kTileBytes, 1024),
+                 sdesc_sw128(xsa + (uint32_t)kk * 2048u, kTileBytes, 1024), I_DK, kk > 0);
+        }
+        mma_commit(&s.y_full[p]);
+        mma_commit(&s.dk_full[p]);
+        mma_commit(&s.stage_empty[st]);
+        if (g + 1 < G && !issue_y1(g + 1)) break;
+      }
+    }
+  } else if (warp == 2 || warp == 3) {
+    scalar_role(a, s, G, nch, lane, warp - 2);
+  } else if (warp >= 4 && warp < 8) {
+    mask_role(a, s, tbase, G, nch, warp, tid - 128, 0);
+  } else if (warp >= 8 && warp < 12) {
+    state_role(a, s, tbase, G, nch, warp, tid - 256);
+  } else if (warp >= 12) {
+    mask_role(a, s, tbase, G, nch, warp, tid - 384, 1);
   }
-  constexpr uint32_t I_G = idesc_bf16_f32(128, 128, false, false);
-  constexpr uint32_t I_Y1 = idesc_bf16_f32(128, 64, false, true);
-  constexpr uint32_t I_Y2 = idesc_bf16_f32(128, 64, false, true);
-  constexpr uint32_t I_DK = idesc_bf16_f32(128, 64, true, true);
-  const uint32_t aC = smem_u32(s.C[0]), aB = smem_u32(s.Bt[0]), aX = smem_u32(s.X), aS = smem_u32(s.S);
-  uint32_t tma_phase = 0, mma_phase = 0;
-  bool ok = true;
-  bool tma_pending = true;
-
-  for (int c = 0; c < nchunk; ++c) {
-    const int t0 = c * Q;
-    const int n = min(Q, L - t0);
-    const bool last = (c == nchunk - 1);
-    // ---- per-row coefficients (overlap the TMA in flight)
-    const int t = t0 + tid;
-    float adt = 0.f, be = 0.f, ga = 0.f, av = 0.f;
-    if (t < L) {
-      adt = a.adt[(int64_t)b * a.sadt.b + (int64_t)t * a.sadt.l + (int64_t)h * a.sadt.h];
-      const float dt = a.dt[(int64_t)b * a.sdt.b + (int64_t)t * a.sdt.l + (int64_t)h * a.sdt.h];
-      const float tr = sigmoidf_(a.trap[(int64_t)b * a.strap.b + (int64_t)t * a.strap.l + (int64_t)h * a.strap.h]);
-      be = dt * (1.0f - tr) + 0.5f * dt * tr;
-      ga = 0.5f * dt * tr;
-      av = expf(adt);
-    }
-    s.av[tid] = av;
-    s.gv[tid] = ga;
-    s.beta[tid] = be;
-    float adt_next = 0.f;
-    if (tid == 0) {
-      const int tn = t0 + Q;
-      float an = 0.f, gn = 0.f;
-      if (tn < L) {
-        adt_next = a.adt[(int64_t)b * a.sadt.b + (int64_t)tn * a.sadt.l + (int64_t)h * a.sadt.h];
-        const float dt = a.dt[(int64_t)b * a.sdt.b + (int64_t)tn * a.sdt.l + (int64_t)h * a.sdt.h];
-        const float tr = sigmoidf_(a.trap[(int64_t)b * a.strap.b + (int64_t)tn * a.strap.l + (int64_t)h * a.strap.h]);
-        an = expf(adt_next);
-        gn = 0.5f * dt * tr;
-      }
-      s.av[Q] = an;
-      s.gv[Q] = gn;
-      s.adt_next = adt_next;
-    }
-    // inclusive scan of v_i = (i == 0 ? 0 : ADT_{t0+i})
-    float v = (tid == 0) ? 0.f : adt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float u = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += u;
-    }
-    if (lane == 31) s.warp_sum[warp] = v;
-    __syncthreads();
-    float off = 0.f;
-    for (int w = 0; w < warp; ++w) off += s.warp_sum[w];
-    const float lam = v + off;
-    s.lam2[tid] = lam * kLog2e;
-    if (tid == Q - 1) s.lam2[Q] = (lam + s.adt_next) * kLog2e;
-    __syncthreads();
-    // mu_j and the state-update weights w_j (the last chunk produces h_{L-1} instead of k)
-    {
-      const int j = tid;
-      const float muj = s.av[j + 1] * be + s.gv[j + 1];
-      s.mu[j] = muj;
-      float w;
-      if (!last) {
-        w = exp2f(s.lam2[Q] - s.lam2[j + 1]) * muj;
-      } else {
-        const int e = n - 1;
-        w = (j < e) ? exp2f(s.lam2[e] - s.lam2[j + 1]) * muj : (j == e ? be : 0.f);
-      }
-      s.wgt[j] = w;
-      if (tid == 0) s.decay_end = exp2f(last ? s.lam2[n - 1] : s.lam2[Q]);
-    }
-    // ---- wait for the stage, issue G and Y1
-    ok = __syncthreads_and(ok && mbar_wait(&s.bar_tma, tma_phase));
-    tma_phase ^= 1;
-    tma_pending = false;
-    if (!ok) break;
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
-        const uint64_t dc = sdesc_sw128(aC + koff, 16, 1024);
-        const uint64_t db = sdesc_sw128(aB + koff, 16, 1024);
-        mma_ss(tbase + COL_G, dc, db, I_G, kk > 0);
-        const uint64_t dk = sdesc_sw128(aS + (uint32_t)kk * 2048u, kTileBytes, 1024);
-        mma_ss(tbase + COL_Y1, dc, dk, I_Y1, kk > 0);
-      }
-      mma_commit(&s.bar_mma);
-    }
-    __syncthreads();
-    // my x row (kept for the epilogue) -- read before the stage is refilled
-    uint32_t xr[32];
-    {
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        const uint4 q = *reinterpret_cast<const uint4*>(s.X + sw128_off(tid, 8 * cc));
-        xr[4 * cc + 0] = q.x; xr[4 * cc + 1] = q.y; xr[4 * cc + 2] = q.z; xr[4 * cc + 3] = q.w;
-      }
-    }
-    ok = __syncthreads_and(mbar_wait(&s.bar_mma, mma_phase));
-    mma_phase ^= 1;
-    if (!ok) break;
-    tc_fence_after();
-    // ---- w o X into S (k_c^T no longer needed: Y1 is done), mask G -> G' (bf16) in TMEM
-    {
-      const float wj = s.wgt[tid];
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint4 q;
-        uint32_t* qq = reinterpret_cast<uint32_t*>(&q);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162*>(&xr[4 * cc + e]);
-          const float2 f = __bfloat1622float2(p2);
-          qq[e] = pack_bf16(f.x * wj, f.y * wj);
-        }
-        *reinterpret_cast<uint4*>(s.S + sw128_off(tid, 8 * cc)) = q;
-      }
-    }
-    {
-      const int i = tid;
-      const float li = s.lam2[i];
-      const float bi = s.beta[i];
-#pragma unroll
-      for (int qd = 0; qd < 4; ++qd) {
-        uint32_t g[32];
-        tmem_ld32(tmem_lane_addr(tbase, warp, COL_G + 32 * qd), g);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float vv[2];
-#pragma unroll
-          for (int z = 0; z < 2; ++z) {
-            const int j = 32 * qd + 2 * e + z;
-            const float gij = __uint_as_float(g[2 * e + z]);
-            float r = 0.f;
-            if (j < i) r = gij * exp2f(li - s.lam2[j + 1]) * s.mu[j];
-            else if (j == i) r = gij * bi;
-            vv[z] = r;
-          }
-          pk[e] = pack_bf16(vv[0], vv[1]);
-        }
-        tmem_st16(tmem_lane_addr(tbase, warp, COL_G + 16 * qd), pk);
-      }
-      tmem_wait_st();
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    // ---- Y2 = G' X ; dK^T = B^T (w o X)
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t dx = sdesc_sw128(aX + (uint32_t)kk * 2048u, kTileBytes, 1024);
-        mma_ts(tbase + COL_Y2, tbase + COL_G + 8u * kk, dx, I_Y2, kk > 0);
-        const uint64_t dbt = sdesc_sw128(aB + (uint32_t)kk * 2048u, kTileBytes, 1024);
-        const uint64_t dxs = sdesc_sw128(aS + (uint32_t)kk * 2048u, kTileBytes, 1024);
-        mma_ss(tbase + COL_DK, dbt, dxs, I_DK, kk > 0);
-      }
-      mma_commit(&s.bar_mma);
-    }
-    ok = __syncthreads_and(mbar_wait(&s.bar_mma, mma_phase));
-    mma_phase ^= 1;
-    if (!ok) break;
-    tc_fence_after();
-    // final B*x (last chunk only): bx_last[p][d] = x_{L-1}[p] * B_{L-1}[d], thread = d
-    if (last && a.bx_last) {
-      const int d = tid, e = n - 1;
-      const float bd = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(
-          s.Bt[d >> 6] + sw128_off(e, d & 63)));
-      const int64_t sb = ((int64_t)b * a.H + h) * kP * kD;
-      for (int p = 0; p < kP; ++p) {
-        const float xv = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(s.X + sw128_off(e, p)));
-        a.bx_last[sb + (int64_t)p * kD + d] = xv * bd;
-      }
-    }
-    __syncthreads();
-    // ---- stage free: prefetch the next chunk
-    if (c + 1 < nchunk) tma_pending = true;
-    if (tid == 0 && c + 1 < nchunk) {
-      const int tn = t0 + Q;
-      mbar_expect_tx(&s.bar_tma, kStageBytes);
-      tma_load_4d(s.C[0], &tm_C, &s.bar_tma, 0, h, tn, b);
-      tma_load_4d(s.C[1], &tm_C, &s.bar_tma, 64, h, tn, b);
-      tma_load_4d(s.Bt[0], &tm_B, &s.bar_tma, 0, h, tn, b);
-      tma_load_4d(s.Bt[1], &tm_B, &s.bar_tma, 64, h, tn, b);
-      tma_load_4d(s.X, &tm_x, &s.bar_tma, 0, h, tn, b);
-    }
-    // ---- state update: k^T = decay * k^T + dK^T  (thread = d), bf16 copy into S
-    {
-      const float dec = s.decay_end;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t r[32];
-        tmem_ld32(tmem_lane_addr(tbase, warp, COL_DK + 32 * half), r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) kst[32 * half + e] = fmaf(dec, kst[32 * half + e], __uint_as_float(r[e]));
-      }
-      if (!last) {
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          uint4 q;
-          q.x = pack_bf16(kst[8 * cc + 0], kst[8 * cc + 1]);
-          q.y = pack_bf16(kst[8 * cc + 2], kst[8 * cc + 3]);
-          q.z = pack_bf16(kst[8 * cc + 4], kst[8 * cc + 5]);
-          q.w = pack_bf16(kst[8 * cc + 6], kst[8 * cc + 7]);
-          *reinterpret_cast<uint4*>(s.S + sw128_off(tid, 8 * cc)) = q;
-        }
-      } else if (a.h_last) {
-        const int64_t sb = ((int64_t)b * a.H + h) * kP * kD;
-        for (int p = 0; p < kP; ++p) a.h_last[sb + (int64_t)p * kD + tid] = kst[p];
-      }
-    }
-    // ---- y = e^{lambda} Y1 + Y2 + D x   (thread = row i)
-    {
-      const int i = tid;
-      const float sc = exp2f(s.lam2[i]);
-      const bool valid = (t0 + i) < L;
-      __nv_bfloat16* yrow = a.y + (int64_t)b * a.sy.b + (int64_t)(t0 + i) * a.sy.l + (int64_t)h * a.sy.h;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t y1[32], y2[32];
-        tmem_ld32(tmem_lane_addr(tbase, warp, COL_Y1 + 32 * half), y1);
-        tmem_ld32(tmem_lane_addr(tbase, warp, COL_Y2 + 32 * half), y2);
-        tmem_wait_ld();
-        uint32_t outp[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float2 xf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xr[16 * half + e]));
-          const float o0 = fmaf(sc, __uint_as_float(y1[2 * e]), __uint_as_float(y2[2 * e])) + Dk * xf.x;
-          const float o1 = fmaf(sc, __uint_as_float(y1[2 * e + 1]), __uint_as_float(y2[2 * e + 1])) + Dk * xf.y;
-          outp[e] = pack_bf16(o0, o1);
-        }
-        if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(yrow + 32 * half);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            dst[q4] = make_uint4(outp[4 * q4], outp[4 * q4 + 1], outp[4 * q4 + 2], outp[4 * q4 + 3]);
-        }
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-  }
-  if (!ok) {
-    // a wait gave up: record it, let an in-flight stage load land (bounded), then release TMEM
-    if (tid == 0) atomicExch(&g_chunk_error, 1);
-    if (tma_pending) mbar_wait(&s.bar_tma, tma_phase, 1u << 20);
-  }
+  tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, kTmemCols);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
 }
 
 // ------------------------------------------------------------------------------------
@@ -445,6 +718,16 @@ int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t H, int64_t
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 bool strides_ok(const Str3& s) { return (s.b % 8 == 0) && (s.l % 8 == 0) && (s.h % 8 == 0); }
 
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      n = 148;
+  }
+  return n;
+}
+
 }  // namespace
 
 bool siso_chunk_supported(const SisoParams& p, int xdt, int bcdt) {
@@ -481,7 +764,9 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
     if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     attr_set = true;
   }
-  siso_chunk_fwd_kernel<<<p.Bn * p.H, kThreads, smem, s>>>(mx, mb, mc, a);
+  const int units = p.Bn * p.H;
+  const int grid = units < num_sms() ? units : num_sms();
+  siso_chunk_fwd_kernel<<<grid, kThreads, smem, s>>>(mx, mb, mc, a);
   return check_launch("siso_chunk_fwd_kernel");
 }
 
