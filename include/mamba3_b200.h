@@ -113,6 +113,27 @@ int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
                      m3_tensor* dh0, m3_tensor* dbx0, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* SISO scan, backward, without any device allocation by the caller or the library.
+ * No counterpart in the reference. Same arguments and results as m3_siso_scan_bwd, minus
+ * the workspace: the per-position workspace lives in a fixed device array inside this
+ * library (M3_NOALLOC_MAX_POSITIONS floats = 8 MiB, held by every GPU that loads the
+ * library until the process exits). For callers that may not allocate device memory at the
+ * point of the backward call, e.g. a host framework that owns a fixed device-memory budget
+ * and forbids side allocations by extensions.
+ *   - batch * seqlen * nheads above M3_NOALLOC_MAX_POSITIONS returns M3_ERR_WORKSPACE.
+ *   - The first call on a device looks up the array's device address (once per device,
+ *     with that device current); make that first call before any stream capture.
+ *   - Every call on a GPU shares the one array: calls whose kernels overlap on that GPU
+ *     (different streams, or host threads) race and produce wrong gradients. Serialise them.
+ *   - Nothing carries over between calls: each call writes every scratch entry it reads. */
+#define M3_NOALLOC_MAX_POSITIONS (2 * 1024 * 1024)
+int m3_siso_scan_bwd_noalloc(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                             const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,
+                             const m3_tensor* D, const m3_tensor* h0, const m3_tensor* bx0,
+                             const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB, m3_tensor* dC,
+                             m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD,
+                             m3_tensor* dh0, m3_tensor* dbx0, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * MIMO scan, forward.  Replaces mimo_state_cuda (cuda_backend.py:419-463: einsum ->
  * mimo_state(x_mixed, ...) :339-356 -> mimo_state_kernel :123-204 -> einsum) as called

@@ -1,6 +1,7 @@
 // extern "C" entry points of libmamba3_b200: argument validation, dispatch to the
 // kernels, and the thread-local error string. Nothing here allocates device memory.
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "decode_step.cuh"
@@ -25,6 +26,12 @@ int check_launch(const char* what) {
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
   return M3_OK;
 }
+
+// Fixed scratch of the allocation-free SISO backward (m3_siso_scan_bwd_noalloc): room for
+// the per-position workspace of up to M3_NOALLOC_MAX_POSITIONS (batch * heads * seqlen)
+// positions, 4 bytes each (8 MiB). Lives in every GPU that loads the library, for the
+// lifetime of the process, and is shared by all calls on that GPU.
+__device__ __align__(256) float g_noalloc_scratch[M3_NOALLOC_MAX_POSITIONS];
 
 namespace {
 
@@ -258,6 +265,51 @@ int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
   p.dh0 = fptr<float>(dh0); p.dbx0 = fptr<float>(dbx0);
   p.q = reinterpret_cast<float*>(workspace);
   return launch_siso_bwd_recurrent(p, x->dtype, B->dtype, s);
+}
+
+// Device address of g_noalloc_scratch, looked up once per device with that device
+// current (host code cannot use the symbol itself as a device pointer).
+static float* noalloc_scratch_for_current_device() {
+  static std::mutex mu;
+  static float* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      fail(M3_ERR_CUDA, std::string("cudaGetSymbolAddress(noalloc scratch): ") + cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = static_cast<float*>(p);
+  }
+  return addr[dev];
+}
+
+int m3_siso_scan_bwd_noalloc(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                             const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* h0,
+                             const m3_tensor* bx0, const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB,
+                             m3_tensor* dC, m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD,
+                             m3_tensor* dh0, m3_tensor* dbx0, void* stream) {
+  if (!present(x) || x->ndim != 4) return fail(M3_ERR_INVALID_ARGUMENT, "x: expected (B, L, H, P)");
+  const int64_t positions = x->shape[0] * x->shape[1] * x->shape[2];
+  if (positions > (int64_t)M3_NOALLOC_MAX_POSITIONS)
+    return fail(M3_ERR_WORKSPACE, "siso backward (no-alloc): batch*heads*seqlen = " + std::to_string(positions) +
+                                      " exceeds the fixed scratch of " + std::to_string(M3_NOALLOC_MAX_POSITIONS) +
+                                      " positions; use m3_siso_scan_bwd with a caller workspace");
+  float* scratch = nullptr;
+  if (positions > 0) {
+    scratch = noalloc_scratch_for_current_device();
+    if (!scratch) return M3_ERR_CUDA;
+  }
+  // every position of the scratch that the kernels read is written first in the same call,
+  // so nothing needs clearing between calls
+  return m3_siso_scan_bwd(x, B, C, ADT, DT, trap, D, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0,
+                          scratch, sizeof(float) * (size_t)M3_NOALLOC_MAX_POSITIONS, stream);
 }
 
 static int fill_mimo(MimoParams& p, const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
