@@ -166,23 +166,29 @@ def cpu_sample(L_sample, nb=1, H=64, P=64, D=128, seed=7):
     return x, Bm, Cm, (A * dt).astype(np.float32), dt, trap, np.ones(H, np.float32)
 
 
-def cpu_baseline(target_s=8.0):
+def cpu_baseline(target_s=12.0, L_s=4096):
+    """Time the fp32 C restatement of the reference loop on all host cores on a bounded
+    sample of the long-context workload: one batch row x 64 heads x L_s positions (about
+    0.4 GB of host arrays), run repeatedly until about target_s seconds have passed (the
+    per-position cost of the loop does not depend on the position). Returns
+    (baseline dict, (L_s, reps per step of about 2 s))."""
     from oracle import cpu_ref
     cores = cpu_ref.max_threads()
-    L_s = 64
+    args = cpu_sample(L_s)
+    cpu_ref.siso_fwd(*args, nthreads=cores)  # warm-up (page-in, thread pool)
+    reps, t0 = 0, time.perf_counter()
     while True:
-        args = cpu_sample(L_s)
-        t0 = time.perf_counter()
         cpu_ref.siso_fwd(*args, nthreads=cores)
+        reps += 1
         dt = time.perf_counter() - t0
-        if dt >= target_s or L_s >= C5["seqlen"]:
+        if dt >= target_s:
             break
-        L_s = min(C5["seqlen"], L_s * max(2, int(target_s / max(dt, 1e-3) * 0.8)))
-    tok_s = L_s / dt  # one batch row over all 64 heads: L_s token positions
+    tok_s = reps * L_s / dt
+    per_2s = max(1, int(round(2.0 * reps / dt)))
     return {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"fp32 C restatement of the reference loop (oracle/scan_ref.c), OpenMP over (b,h); "
-                      f"1 batch row x 64 heads x {L_s} positions (P=64, D=128) of the long-context "
-                      f"workload in {dt:.2f} s"}, L_s
+                      f"1 batch row x 64 heads x {L_s} positions (P=64, D=128) of the long-context workload, "
+                      f"run {reps} times in {dt:.1f} s"}, (L_s, per_2s)
 
 
 def workload_config(world):
@@ -196,18 +202,18 @@ def run_reference_arm(args, rank, world):
         return
     from oracle import cpu_ref
     cores = cpu_ref.max_threads()
-    # size one step to about 2 s of CPU work
-    base, L_s = cpu_baseline(target_s=2.0)
+    # one step = the sample run enough times for about 2 s of CPU work
+    base, (L_s, reps) = cpu_baseline(target_s=4.0)
     sample = cpu_sample(L_s)
     for _ in range(args.warmup):
         cpu_ref.siso_fwd(*sample, nthreads=cores)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(args.steps * reps):
         cpu_ref.siso_fwd(*sample, nthreads=cores)
     el = time.perf_counter() - t0
-    v = args.steps * L_s / el
+    v = args.steps * reps * L_s / el
     base["value"] = v
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
@@ -215,6 +221,72 @@ def run_reference_arm(args, rank, world):
             "cpu_baseline": base,
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------
+# secondary figures (one GPU): long-context forward + backward, and LM decode
+# ----------------------------------------------------------------------------------
+def measure_fwd_bwd(inputs, steps=2):
+    """ssm_scan_siso forward + backward through autograd on the long-context inputs."""
+    from mamba3_ssm import ssm_scan_siso
+    x, Bm, Cm, ADT, DT, trap, Dw = inputs
+    leaves = [t.detach().requires_grad_(True) for t in (x, Bm, Cm, ADT, DT, trap, Dw)]
+    dy = torch.randn_like(x)
+    for _ in range(1):
+        ssm_scan_siso(*leaves).backward(dy)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        for t in leaves:
+            t.grad = None
+        ssm_scan_siso(*leaves).backward(dy)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    tokens = x.shape[0] * x.shape[1]
+    return {"value": tokens / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+            "what": "ssm_scan_siso forward + backward (autograd) on the same workload"}
+
+
+def measure_decode(dev, steps=48, batch=256, prefill=16):
+    """Greedy decode through MambaLMHeadModel.step (block.py:110-139 interface) at the
+    medium preset: d_model 1536, 20 layers, MIMO rank 4, d_state 64, headdim 64,
+    vocab 50000, bf16, batch 256, random-init weights, uniform random prompt ids."""
+    from mamba3_ssm import MambaConfig, MambaLMHeadModel
+    torch.manual_seed(0)
+    cfg = MambaConfig(d_model=1536, n_layer=20, vocab_size=50000,
+                      ssm_cfg=dict(d_state=64, expand=2, headdim=64, is_mimo=True, mimo_rank=4))
+    model = MambaLMHeadModel(cfg, device=dev, dtype=torch.bfloat16).eval()
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    ids = torch.randint(0, 50000, (batch, prefill), device=dev, generator=g)
+    with torch.no_grad():
+        cache = model.allocate_inference_cache(batch)
+        for t in range(prefill):
+            logits, cache = model.step(ids[:, t], cache)
+        tok = logits.argmax(-1)
+        for _ in range(3):
+            logits, cache = model.step(tok, cache)
+            tok = logits.argmax(-1)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            logits, cache = model.step(tok, cache)
+            tok = logits.argmax(-1)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    H, D, S = 48, 64, 16
+    state_bytes = 20 * batch * 2 * 4 * (2 * H * D + H * S)
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    del model, cache
+    torch.cuda.empty_cache()
+    return {"value": batch / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "batch": batch, "layers": 20, "bytes_per_step_min": state_bytes + weight_bytes,
+            "what": "MambaLMHeadModel.step greedy decode, medium preset (d_model 1536, 20 layers, "
+                    "MIMO R=4), bf16, batch 256, after a 16-token prefill"}
 
 
 # ----------------------------------------------------------------------------------
@@ -226,6 +298,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the forward+backward and decode figures")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the global batch (profiling runs on a smaller case)")
     args = ap.parse_args()
@@ -337,6 +410,13 @@ def main():
                "d2h_bytes_per_step": d2h * world, "steps": Ke}
         del hosts, y_host
 
+    extra = {}
+    if world == 1 and not args.no_extra:
+        extra["fwd_bwd"] = measure_fwd_bwd((x, Bm, Cm, ADT, DT, trap, Dw))
+        del x, Bm, Cm, ADT, DT, trap, Dw, y
+        torch.cuda.empty_cache()
+        extra["decode"] = measure_decode(dev)
+
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base, _ = cpu_baseline()
@@ -349,7 +429,8 @@ def main():
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
                              "algorithmic_bytes_per_launch": launch_bytes, "kernel_ms": kern_ms},
-                "cpu_baseline": base, "e2e": e2e, "gpu_launches": K, "clocks": clocks}
+                "cpu_baseline": base, "e2e": e2e, "gpu_launches": K, "clocks": clocks,
+                "secondary": extra}
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()

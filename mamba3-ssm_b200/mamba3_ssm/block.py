@@ -63,6 +63,9 @@ class MambaLMHeadModel(nn.Module):
             self.mlp_layers = None
         self.norm_f = RMSNorm(config.d_model)
         self.lm_head = nn.Linear(config.d_model, v, bias=False, **f)
+        if device is not None:
+            for mod in [self.norm_f] + [blk.norm for blk in self.layers]:
+                mod.weight = nn.Parameter(mod.weight.data.to(device))
         if config.tie_embeddings:
             self.lm_head.weight = self.embedding.weight
 

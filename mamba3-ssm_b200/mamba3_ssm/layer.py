@@ -81,6 +81,15 @@ class Mamba3(nn.Module):
         self.D = nn.Parameter(torch.ones(self.nheads, **factory_kwargs))
         self.D._no_weight_decay = True
         self.out_proj = nn.Linear(self.d_inner, d_model, bias=False, **factory_kwargs)
+        if device is not None:
+            # the fp32 parameters above are drawn and filled on the CPU (same RNG stream as the
+            # reference); place them on the requested device
+            for mod in (self, self.B_norm, self.C_norm):
+                for name, prm in list(mod._parameters.items()):
+                    if prm is not None and prm.device != torch.device(device):
+                        mod._parameters[name] = nn.Parameter(prm.data.to(device), requires_grad=prm.requires_grad)
+            for prm_name in ("dt_bias", "B_bias", "C_bias", "D"):
+                getattr(self, prm_name)._no_weight_decay = True
         self._splits = [self.d_inner, self.d_inner, d_state * ngroups * self.mimo_rank,
                         d_state * ngroups * self.mimo_rank, self.nheads, self.nheads, self.nheads,
                         self.num_rope_angles]
