@@ -65,6 +65,27 @@ def measured_traffic():
 
 
 # ----------------------------------------------------------------------------------
+# multi-rank helpers (one process per GPU; the scan needs no exchange)
+# ----------------------------------------------------------------------------------
+def shard(total, world, rank):
+    """Contiguous share of `total` batch rows for `rank`: (first row, rows)."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad rank / world size")
+    base, rem = divmod(total, world)
+    start = rank * base + min(rank, rem)
+    return start, base + (1 if rank < rem else 0)
+
+
+def max_over_ranks(values, dist=None, device=None):
+    """Element-wise max of a list of floats over all ranks (the job's time is the slowest
+    rank's). With no process group the values are returned unchanged."""
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+# ----------------------------------------------------------------------------------
 # clocks sampled during the timed region
 # ----------------------------------------------------------------------------------
 class ClockSampler:
@@ -72,8 +93,8 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_indices):
-        self.idx = ",".join(str(i) for i in gpu_indices)
+    def __init__(self, gpu_ids):
+        self.idx = ",".join(str(i) for i in gpu_ids)
         self.lines = []
         self.proc = None
 
@@ -327,9 +348,7 @@ def main():
     if args.batch:
         C5["batch"] = args.batch
     Bt, L, H, P, D = C5["batch"], C5["seqlen"], C5["nheads"], C5["headdim"], C5["dstate"]
-    if Bt % world:
-        raise SystemExit("bench.py: batch 16 must divide by the number of GPUs")
-    Bl = Bt // world
+    _, Bl = shard(Bt, world, rank)
     x, Bm, Cm, ADT, DT, trap, Dw = make_inputs(Bl, L, H, P, D, dev, 1234 + rank)
     torch.cuda.synchronize()
 
@@ -346,7 +365,14 @@ def main():
     K = args.steps
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     t_beg, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    # every rank's GPU, named by UUID (nvidia-smi indices need not match CUDA ordinals)
+    uid = str(torch.cuda.get_device_properties(dev).uuid)
+    uid = uid if uid.startswith("GPU-") else "GPU-" + uid
+    uids = [uid]
+    if pg is not None:
+        uids = [None] * world
+        pg.all_gather_object(uids, uid)
+    sampler = ClockSampler(uids) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
@@ -363,10 +389,7 @@ def main():
     clocks = sampler.stop() if sampler else None
     total_ms = t_beg.elapsed_time(t_end)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    tt = torch.tensor([total_ms, kern_ms], device=dev, dtype=torch.float64)
-    if pg is not None:
-        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
-    total_ms, kern_ms = float(tt[0]), float(tt[1])
+    total_ms, kern_ms = max_over_ranks([total_ms, kern_ms], pg, dev)
     ms_step = total_ms / K
     tokens = Bt * L
     value = tokens / (ms_step / 1e3)
@@ -403,11 +426,10 @@ def main():
         e1.record()
         torch.cuda.synchronize()
         barrier()
-        et = torch.tensor([e0.elapsed_time(e1) / Ke], device=dev, dtype=torch.float64)
-        if pg is not None:
-            pg.all_reduce(et, op=pg.ReduceOp.MAX)
-        e2e = {"value": tokens / (float(et[0]) / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-               "d2h_bytes_per_step": d2h * world, "steps": Ke}
+        (e_ms,) = max_over_ranks([e0.elapsed_time(e1) / Ke], pg, dev)
+        h2d, d2h = max_over_ranks([h2d, d2h], pg, dev)  # equal shares: report the job total below
+        e2e = {"value": tokens / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d * world),
+               "d2h_bytes_per_step": int(d2h * world), "steps": Ke}
         del hosts, y_host
 
     extra = {}

@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the chunked scan uses: mbarriers,
-// TMA tensor loads (no multicast), tcgen05 TMEM allocation, MMA, commit, loads/stores,
+// TMA tensor loads (each CTA loads its own tiles), tcgen05 TMEM allocation, MMA, commit, loads/stores,
 // and the UMMA shared-memory / instruction descriptors.
 #pragma once
 #include <cuda.h>
