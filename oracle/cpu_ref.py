@@ -42,7 +42,13 @@ def load():
 
 
 def max_threads():
-    return load().m3_ref_max_threads()
+    """Host cores this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks;
+    the CPU baseline uses every core it is allowed to)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    return max(n, load().m3_ref_max_threads())
 
 
 def siso_fwd(x, B, C, ADT, DT, trap, D, nthreads=0):
