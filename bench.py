@@ -270,10 +270,19 @@ def measure_fwd_bwd(inputs, steps=2):
             "what": "ssm_scan_siso forward + backward (autograd) on the same workload"}
 
 
+def _state_bytes(mixer, batch):
+    """fp32 decode-state bytes of one layer: angle (B,H,S) + ssm and bx (B,H,D) MIMO or
+    (B,H,P,D) SISO."""
+    per = mixer.d_state if mixer.is_mimo else mixer.headdim * mixer.d_state
+    return batch * mixer.nheads * (mixer.num_rope_angles + 2 * per) * 4
+
+
 def measure_decode(dev, steps=48, batch=256, prefill=16):
-    """Greedy decode through MambaLMHeadModel.step (block.py:110-139 interface) at the
-    medium preset: d_model 1536, 20 layers, MIMO rank 4, d_state 64, headdim 64,
-    vocab 50000, bf16, batch 256, random-init weights, uniform random prompt ids."""
+    """Greedy decode of the medium preset (d_model 1536, 20 layers, MIMO rank 4, d_state 64,
+    headdim 64, vocab 50000), bf16, batch 256, random-init weights, uniform random prompt
+    ids, three ways: MambaLMHeadModel.step (block.py:110-139 interface, one launch per op),
+    the same step replayed as one CUDA graph (DecodeGraph), and the fused step kernel alone
+    (m3_mimo_step per layer, cycling the 20 layers' caches so the state exceeds L2)."""
     from mamba3_ssm import MambaConfig, MambaLMHeadModel
     torch.manual_seed(0)
     cfg = MambaConfig(d_model=1536, n_layer=20, vocab_size=50000,
@@ -282,7 +291,9 @@ def measure_decode(dev, steps=48, batch=256, prefill=16):
     g = torch.Generator(device=dev)
     g.manual_seed(4321)
     ids = torch.randint(0, 50000, (batch, prefill), device=dev, generator=g)
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     with torch.no_grad():
+        # (1) eager step()
         cache = model.allocate_inference_cache(batch)
         for t in range(prefill):
             logits, cache = model.step(ids[:, t], cache)
@@ -291,23 +302,78 @@ def measure_decode(dev, steps=48, batch=256, prefill=16):
             logits, cache = model.step(tok, cache)
             tok = logits.argmax(-1)
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = ev(), ev()
         e0.record()
         for _ in range(steps):
             logits, cache = model.step(tok, cache)
             tok = logits.argmax(-1)
         e1.record()
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    H, D, S = 48, 64, 16
-    state_bytes = 20 * batch * 2 * 4 * (2 * H * D + H * S)
+        ms_eager = e0.elapsed_time(e1) / steps
+        del cache, logits
+        # (2) CUDA-graph replay of the whole step (greedy argmax inside the graph)
+        dg = model.decode_graph(batch, greedy=True)
+        for t in range(prefill):
+            dg.feed(ids[:, t])
+        for _ in range(3):
+            dg.next()
+        torch.cuda.synchronize()
+        e0, e1 = ev(), ev()
+        e0.record()
+        for _ in range(steps):
+            dg.next()
+        e1.record()
+        torch.cuda.synchronize()
+        ms_graph = e0.elapsed_time(e1) / steps
+        del dg
+        # (3) the fused step kernel alone, one launch per layer
+        mixers = [blk.mixer for blk in model.layers]
+        u = torch.randn(batch, cfg.d_model, device=dev, dtype=torch.bfloat16)
+        zs = [m.in_proj(u).contiguous() for m in mixers]
+        caches = [m.allocate_inference_cache(batch) for m in mixers]
+        ys = [torch.empty(batch, m.d_inner, device=dev, dtype=torch.bfloat16) for m in mixers]
+        def sweep():
+            for m, z, c, y in zip(mixers, zs, caches, ys):
+                m._fused_step(z, *c, *c, y)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                sweep()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()  # replayed, so host-side binding cost is not timed
+        with torch.cuda.graph(graph):
+            sweep()
+        graph.replay()
+        torch.cuda.synchronize()
+        kreps = 10
+        e0, e1 = ev(), ev()
+        e0.record()
+        for _ in range(kreps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us_kernel = e0.elapsed_time(e1) * 1e3 / (kreps * len(mixers))
+        del graph
+    m0 = mixers[0]
+    kbytes = (2 * _state_bytes(m0, batch) + zs[0].numel() * zs[0].element_size()
+              + ys[0].numel() * ys[0].element_size())
+    k_gbs = kbytes / (us_kernel * 1e-6) / 1e9
+    peak = peaks()[0]
+    state_bytes = 20 * 2 * _state_bytes(m0, batch)
     weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
-    del model, cache
+    del model, caches, zs, ys
     torch.cuda.empty_cache()
-    return {"value": batch / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
-            "batch": batch, "layers": 20, "bytes_per_step_min": state_bytes + weight_bytes,
-            "what": "MambaLMHeadModel.step greedy decode, medium preset (d_model 1536, 20 layers, "
-                    "MIMO R=4), bf16, batch 256, after a 16-token prefill"}
+    return {"value": batch / (ms_graph / 1e3), "unit": "tokens/s", "ms_per_step": ms_graph,
+            "eager_step": {"value": batch / (ms_eager / 1e3), "ms_per_step": ms_eager},
+            "steps": steps, "batch": batch, "layers": 20, "bytes_per_step_min": state_bytes + weight_bytes,
+            "step_kernel": {"us_per_launch": us_kernel, "bytes_per_launch": kbytes, "achieved_gbs": k_gbs,
+                            "peak_gbs": peak, "frac": k_gbs / peak,
+                            "what": "m3_mimo_step, one layer at batch 256 (in-place state), 20 layers' "
+                                    "caches cycled, replayed from a CUDA graph"},
+            "what": "greedy decode, medium preset (d_model 1536, 20 layers, MIMO R=4), bf16, batch 256, "
+                    "after a 16-token prefill; value = DecodeGraph replay, eager_step = "
+                    "MambaLMHeadModel.step"}
 
 
 # ----------------------------------------------------------------------------------

@@ -162,9 +162,8 @@ __global__ void __launch_bounds__(kThreads) mimo_step_kernel(StepParams a) {
     if (lane == 0) s.xr[r] = acc;
   }
   __syncthreads();
-  // state update; y_r partial sums via shared atomics
-  if (tid < R) s.yr[tid] = 0.f;
-  __syncthreads();
+  // state update; y_r partial sums per warp, added in warp order (deterministic)
+  __shared__ float yw[kThreads / 32][8];
   const int64_t base = ((int64_t)b * a.H + h) * D;
   float yacc[8];
 #pragma unroll
@@ -186,8 +185,14 @@ __global__ void __launch_bounds__(kThreads) mimo_step_kernel(StepParams a) {
       float v = yacc[r];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) atomicAdd(&s.yr[r], v);
+      if (lane == 0) yw[warp][r] = v;
     }
+  }
+  __syncthreads();
+  if (tid < R) {
+    float v = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) v += yw[w][tid];
+    s.yr[tid] = v;
   }
   __syncthreads();
   // y = mimo_o^T (y_r + D xr), gated (layer.py:352-356)
@@ -200,6 +205,209 @@ __global__ void __launch_bounds__(kThreads) mimo_step_kernel(StepParams a) {
   }
 }
 
+// ------------------------------------------------------------------------------------
+// MIMO step, one warp per (b, h): 8 batch rows of one head per CTA. The head's parameters
+// (B/C bias and norm weights, mimo_x, mimo_o) are staged once per CTA in shared memory;
+// every per-row reduction is a warp shuffle. Lane l holds d = 32 k + l of each rank's
+// B / C row (DL = D / 32 values per rank) and p = l + 32 j of x. Templates: DL, RM (rank
+// rounded up to a power of two) and PJ (headdim / 32 rounded up), so the register
+// arrays match the shape. Used when D % 32 == 0, R * D <= 512 and P <= 256.
+// ------------------------------------------------------------------------------------
+constexpr int kWarpRows = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename TZ, int DL, int RM, int PJ>
+__global__ void __launch_bounds__(32 * kWarpRows) mimo_step_warp_kernel(StepParams a) {
+  constexpr int NK = RM * DL;  // B / C values per lane
+  constexpr int D = 32 * DL;
+  extern __shared__ float wsm[];
+  const int P = a.P, R = a.R, G = a.G, H = a.H;
+  float* sBb = wsm;            // (R, D)
+  float* sCb = sBb + R * D;    // (R, D)
+  float* sBw = sCb + R * D;    // (D)
+  float* sCw = sBw + D;        // (D)
+  float* smx = sCw + D;        // (R, P)
+  float* smo = smx + R * P;    // (R, P)
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  const int b = blockIdx.y * kWarpRows + (threadIdx.x >> 5);
+  const bool active = b < a.Bn;
+  const TZ* row = reinterpret_cast<const TZ*>(a.zxbcdt) + (int64_t)(active ? b : 0) * a.s_row;
+  const int g = (int)(((int64_t)h * G) / H);
+  const int off_B = 2 * a.d_inner, off_C = off_B + D * G * R, off_dt = off_C + D * G * R;
+  const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
+  // this row's operands: all loads independent, issued before the parameter barrier
+  float Bv[NK], Cv[NK], xv[PJ], zv[PJ], hs[DL], bp[DL];
+#pragma unroll
+  for (int k = 0; k < NK; ++k) {
+    const int r = k / DL, d = 32 * (k % DL) + lane;
+    const bool v = r < R;
+    Bv[k] = v ? to_f32(row[off_B + (r * G + g) * D + d]) : 0.f;
+    Cv[k] = v ? to_f32(row[off_C + (r * G + g) * D + d]) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < PJ; ++j) {
+    const int p = lane + 32 * j;
+    const bool v = p < P;
+    xv[j] = v ? to_f32(row[a.d_inner + h * P + p]) : 0.f;
+    zv[j] = v ? to_f32(row[h * P + p]) : 0.f;
+  }
+  const int64_t sbase = ((int64_t)(active ? b : 0) * H + h) * D;
+#pragma unroll
+  for (int k = 0; k < DL; ++k) {
+    hs[k] = active ? a.ssm_in[sbase + 32 * k + lane] : 0.f;
+    bp[k] = active ? a.bx_in[sbase + 32 * k + lane] : 0.f;
+  }
+  const float dt_raw = to_f32(row[off_dt + h]), A_raw = to_f32(row[off_A + h]), tr_raw = to_f32(row[off_tr + h]);
+  const int npair = a.split / 2;
+  const int64_t abase = ((int64_t)(active ? b : 0) * H + h) * a.S;
+  float ang_in[DL], ang_raw[DL];
+#pragma unroll
+  for (int k = 0; k < DL; ++k) {
+    const int i = (32 * k + lane) >> 1;  // angle of the pair holding d = 32 k + lane
+    ang_in[k] = i < npair && active ? a.angle_in[abase + i] : 0.f;
+    ang_raw[k] = i < npair ? to_f32(row[off_ang + i]) : 0.f;
+  }
+  // head parameters into shared memory
+  for (int i = threadIdx.x; i < R * D; i += blockDim.x) {
+    sBb[i] = a.B_bias[(int64_t)h * R * D + i];
+    sCb[i] = a.C_bias[(int64_t)h * R * D + i];
+  }
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    sBw[i] = a.B_norm_w[i];
+    sCw[i] = a.C_norm_w[i];
+  }
+  for (int i = threadIdx.x; i < R * P; i += blockDim.x) {
+    smx[i] = a.mimo_x[(int64_t)h * R * P + i];
+    smo[i] = a.mimo_o[(int64_t)h * R * P + i];
+  }
+  __syncthreads();
+  if (!active) return;
+
+  const float DT = softplusf_(dt_raw + a.dt_bias[h]);
+  const float A = -fminf(softplusf_(A_raw), -a.A_floor);  // layer.py:317
+  const float decay = expf(A * DT);
+  const float tr = sigmoidf_(tr_raw);
+  const float Dk = a.Dskip[h];
+  // RMSNorm per rank over D (ops.py:102-104), then bias
+  float rB[RM], rC[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) { rB[r] = 0.f; rC[r] = 0.f; }
+#pragma unroll
+  for (int k = 0; k < NK; ++k) {
+    rB[k / DL] = fmaf(Bv[k], Bv[k], rB[k / DL]);
+    rC[k / DL] = fmaf(Cv[k], Cv[k], rC[k / DL]);
+  }
+#pragma unroll
+  for (int r = 0; r < RM; ++r) {
+    rB[r] = 1.0f / sqrtf(warp_sum(rB[r]) / D + a.eps);
+    rC[r] = 1.0f / sqrtf(warp_sum(rC[r]) / D + a.eps);
+  }
+  // RoPE angle of this lane's pairs: one sincos per d slot, shared by every rank
+  float sn[DL], cs[DL];
+#pragma unroll
+  for (int k = 0; k < DL; ++k) {
+    const float an = ang_in[k] + ang_raw[k] * DT;
+    sincosf(an, &sn[k], &cs[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < NK; ++k) {
+    const int r = k / DL, kd = k % DL, d = 32 * kd + lane;
+    if (r < R) {
+      Bv[k] = Bv[k] * rB[r] * sBw[d] + sBb[r * D + d];
+      Cv[k] = Cv[k] * rC[r] * sCw[d] + sCb[r * D + d];
+    }
+    // pairs (2i, 2i+1), i < split / 2: the partner sits in lane ^ 1
+    const float pb = __shfl_xor_sync(0xffffffffu, Bv[k], 1);
+    const float pc = __shfl_xor_sync(0xffffffffu, Cv[k], 1);
+    if ((d >> 1) < npair) {
+      if (lane & 1) {
+        Bv[k] = pb * sn[kd] + Bv[k] * cs[kd];
+        Cv[k] = pc * sn[kd] + Cv[k] * cs[kd];
+      } else {
+        Bv[k] = Bv[k] * cs[kd] - pb * sn[kd];
+        Cv[k] = Cv[k] * cs[kd] - pc * sn[kd];
+      }
+    }
+  }
+  // angle update (layer.py:331-332); angle_out may alias angle_in, which every lane has read
+  __syncwarp();
+  for (int i = lane; i < a.S; i += 32) a.angle_out[abase + i] = a.angle_in[abase + i] + to_f32(row[off_ang + i]) * DT;
+  // xr = mimo_x x (layer.py:346)
+  float xr[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < PJ; ++j) {
+      const int p = lane + 32 * j;
+      if (r < R && p < P) acc = fmaf(smx[r * P + p], xv[j], acc);
+    }
+    xr[r] = warp_sum(acc);
+  }
+  // state update (layer.py:347-351) and y_r = C_r h
+  float yr[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) yr[r] = 0.f;
+#pragma unroll
+  for (int k = 0; k < DL; ++k) {
+    float bxc = 0.f;
+#pragma unroll
+    for (int r = 0; r < RM; ++r) bxc = fmaf(xr[r], Bv[r * DL + k], bxc);  // zero rows beyond R
+    const float blend = (1.0f - tr) * bxc + tr * 0.5f * (bxc + bp[k]);
+    const float hn = decay * hs[k] + DT * blend;
+    a.ssm_out[sbase + 32 * k + lane] = hn;
+    a.bx_out[sbase + 32 * k + lane] = bxc;
+#pragma unroll
+    for (int r = 0; r < RM; ++r) yr[r] = fmaf(Cv[r * DL + k], hn, yr[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < RM; ++r) yr[r] = warp_sum(yr[r]) + Dk * xr[r];
+  // y = mimo_o^T (y_r + D xr), gated by silu(z) (layer.py:352-356)
+  TZ* yo = reinterpret_cast<TZ*>(a.y) + (int64_t)b * a.s_y + h * P;
+#pragma unroll
+  for (int j = 0; j < PJ; ++j) {
+    const int p = lane + 32 * j;
+    if (p < P) {
+      float acc = 0.f;
+#pragma unroll
+      for (int r = 0; r < RM; ++r)
+        if (r < R) acc = fmaf(yr[r], smo[r * P + p], acc);
+      const float z = zv[j];
+      st(yo + p, acc * (z * sigmoidf_(z)));
+    }
+  }
+}
+
+template <typename TZ, int DL, int RM>
+void launch_warp_rm(const StepParams& p, cudaStream_t s) {
+  const dim3 grid(p.H, (p.Bn + kWarpRows - 1) / kWarpRows);
+  const size_t smem = sizeof(float) * (size_t)(2 * p.R * p.D + 2 * p.D + 2 * p.R * p.P);
+  if (p.P <= 64) mimo_step_warp_kernel<TZ, DL, RM, 2><<<grid, 32 * kWarpRows, smem, s>>>(p);
+  else mimo_step_warp_kernel<TZ, DL, RM, 8><<<grid, 32 * kWarpRows, smem, s>>>(p);
+}
+
+template <typename TZ, int DL>
+void launch_warp_dl(const StepParams& p, cudaStream_t s) {
+  if (p.R <= 1) launch_warp_rm<TZ, DL, 1>(p, s);
+  else if (p.R <= 2) launch_warp_rm<TZ, DL, 2>(p, s);
+  else if (p.R <= 4) launch_warp_rm<TZ, DL, 4>(p, s);
+  else if constexpr (DL <= 2) launch_warp_rm<TZ, DL, 8>(p, s);
+}
+
+template <typename TZ>
+void launch_warp(const StepParams& p, cudaStream_t s) {
+  const int dl = p.D / 32;
+  if (dl == 1) launch_warp_dl<TZ, 1>(p, s);
+  else if (dl == 2) launch_warp_dl<TZ, 2>(p, s);
+  else launch_warp_dl<TZ, 4>(p, s);
+}
+
 }  // namespace
 
 int launch_step(const StepParams& p, int zdt, bool mimo, cudaStream_t s) {
@@ -207,9 +415,15 @@ int launch_step(const StepParams& p, int zdt, bool mimo, cudaStream_t s) {
   if (mimo && p.P > 1024) return fail(M3_ERR_UNSUPPORTED, "step: headdim above 1024");
   if (!mimo && (p.D % 16 != 0 || (p.D & (p.D - 1)) != 0)) return fail(M3_ERR_UNSUPPORTED, "siso step: d_state must be a power of two >= 16");
   const dim3 grid(p.Bn * p.H);
+  // warp-per-(b, h) MIMO kernel where its register layout fits (shared memory: head
+  // parameters, at most 2*512 + 2*128 + 2*8*256 floats = 21.5 KB)
+  const int dl = p.D / 32;
+  const bool warp_mimo = mimo && p.D % 32 == 0 && (dl == 1 || dl == 2 || dl == 4) && p.R * dl <= 16 &&
+                         p.P <= 256 && p.split <= p.D;
 #define M3_STEP_LAUNCH(T)                                                          \
   do {                                                                             \
-    if (mimo) mimo_step_kernel<T><<<grid, kThreads, 0, s>>>(p);                    \
+    if (warp_mimo) launch_warp<T>(p, s);                                            \
+    else if (mimo) mimo_step_kernel<T><<<grid, kThreads, 0, s>>>(p);               \
     else siso_step_kernel<T><<<grid, kThreads, 0, s>>>(p);                         \
   } while (0)
   if (zdt == M3_FLOAT32) M3_STEP_LAUNCH(float);

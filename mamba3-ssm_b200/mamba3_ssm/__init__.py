@@ -9,7 +9,7 @@ libmamba3_b200.so. There is no CPU path.
 
 from .config import MambaConfig, SSMConfig
 from .layer import Mamba3
-from .block import MambaLMHeadModel, MambaBlock
+from .block import MambaLMHeadModel, MambaBlock, DecodeGraph
 from .ops import RMSNorm, apply_rope, ssm_scan_siso, ssm_scan_mimo
 
 __all__ = [
@@ -18,6 +18,7 @@ __all__ = [
     "Mamba3",
     "MambaLMHeadModel",
     "MambaBlock",
+    "DecodeGraph",
     "RMSNorm",
     "apply_rope",
     "ssm_scan_siso",

@@ -7,6 +7,7 @@ a RuntimeError is raised with the library's own error text.
 
 import ctypes
 import os
+import struct
 
 import torch
 
@@ -45,7 +46,10 @@ class M3LayerDims(ctypes.Structure):
     ]
 
 
-_P = ctypes.POINTER(M3Tensor)
+# tensor arguments are passed as plain addresses of m3_tensor records (see pack())
+_P = ctypes.c_void_p
+_REC = struct.Struct("<qii" + "q" * MAX_DIMS + "q" * MAX_DIMS)
+assert _REC.size == ctypes.sizeof(M3Tensor)
 _SIGS = {
     "m3_abi_version": ([], ctypes.c_int),
     "m3_last_error_string": ([], ctypes.c_char_p),
@@ -56,8 +60,8 @@ _SIGS = {
     "m3_mimo_scan_fwd": ([_P] * 14 + [ctypes.c_void_p], ctypes.c_int),
     "m3_mimo_scan_bwd_workspace_size": ([ctypes.c_int64] * 6, ctypes.c_size_t),
     "m3_mimo_scan_bwd": ([_P] * 23 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
-    "m3_siso_step": ([ctypes.POINTER(M3LayerDims)] + [_P] * 14 + [ctypes.c_void_p], ctypes.c_int),
-    "m3_mimo_step": ([ctypes.POINTER(M3LayerDims)] + [_P] * 16 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_siso_step": ([ctypes.c_void_p] + [_P] * 14 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_mimo_step": ([ctypes.c_void_p] + [_P] * 16 + [ctypes.c_void_p], ctypes.c_int),
 }
 
 _lib = None
@@ -99,13 +103,47 @@ def tensor(t):
     code = _DTYPE_CODE.get(t.dtype)
     if code is None:
         raise TypeError(f"dtype {t.dtype} is not supported by libmamba3_b200")
-    m.data = t.data_ptr() if t.numel() > 0 else (t.data_ptr() or 1)
+    n = t.dim()
+    m.data = t.data_ptr() or (1 if t.numel() == 0 else 0)
     m.dtype = code
-    m.ndim = t.dim()
-    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
-        m.shape[i] = s
-        m.stride[i] = st
+    m.ndim = n
+    m.shape[:n] = t.shape
+    m.stride[:n] = t.stride()
     return m
+
+
+class Packed:
+    """m3_tensor records of several tensors in one buffer (built with struct, which is
+    several times cheaper than filling ctypes structures). ``ptrs[i]`` is the address
+    of record i, or None for an absent optional argument; the object must stay alive
+    until the call returns."""
+
+    __slots__ = ("buf", "ptrs")
+
+    def __init__(self, ts):
+        n = len(ts)
+        self.buf = ctypes.create_string_buffer(_REC.size * n)
+        base = ctypes.addressof(self.buf)
+        ptrs = []
+        for i, t in enumerate(ts):
+            if t is None:
+                ptrs.append(None)
+                continue
+            code = _DTYPE_CODE.get(t.dtype)
+            if code is None:
+                raise TypeError(f"dtype {t.dtype} is not supported by libmamba3_b200")
+            nd = t.dim()
+            if nd > MAX_DIMS:
+                raise ValueError("tensor has too many dimensions for the C ABI")
+            pad = (0,) * (MAX_DIMS - nd)
+            ptr = t.data_ptr() or (1 if t.numel() == 0 else 0)
+            _REC.pack_into(self.buf, _REC.size * i, ptr, code, nd, *t.shape, *pad, *t.stride(), *pad)
+            ptrs.append(base + _REC.size * i)
+        self.ptrs = ptrs
+
+
+def pack(*ts):
+    return Packed(ts)
 
 
 def ref(m):

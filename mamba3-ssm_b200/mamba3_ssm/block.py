@@ -92,3 +92,71 @@ class MambaLMHeadModel(nn.Module):
             if self.mlp_layers is not None:
                 x = x + self.mlp_layers[i](self.mlp_norms[i](x))
         return self.lm_head(self.norm_f(x)), new_cache
+
+    # ------------------------------------------------------------------------------
+    def decode_graph(self, batch_size: int, greedy: bool = True) -> "DecodeGraph":
+        """A CUDA-graph decode loop for this model at a fixed batch size (see DecodeGraph).
+        Not part of the reference interface; step() keeps the reference's semantics."""
+        return DecodeGraph(self, batch_size, greedy)
+
+
+class DecodeGraph:
+    """Replays one whole decode step (embedding, every layer's norm / in_proj / fused step
+    kernel / out_proj / residual, norm_f, lm_head and, with ``greedy``, the argmax) as one
+    CUDA graph. The decode cache lives in static tensors updated in place; ``logits`` and
+    ``tokens`` are static buffers overwritten by every call.
+
+        g = model.decode_graph(batch)          # captures on the current device
+        g.reset()                              # zero cache
+        for t in prompt.T: g.feed(t)           # prefill token by token, like step()
+        for _ in range(n): tok = g.next()      # greedy: the argmax becomes the next input
+    """
+
+    def __init__(self, model: "MambaLMHeadModel", batch_size: int, greedy: bool = True):
+        dev = model.embedding.weight.device
+        if dev.type != "cuda":
+            raise RuntimeError("DecodeGraph needs the model on a CUDA device")
+        self.model = model
+        self.greedy = greedy
+        self.tokens = torch.zeros(batch_size, dtype=torch.long, device=dev)
+        self.cache = model.allocate_inference_cache(batch_size)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.no_grad():
+            for _ in range(2):  # warm the caching allocator and the libraries outside the graph
+                self._body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.reset()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph, capture_error_mode="relaxed"):
+            self.logits = self._body()
+        self.reset()
+
+    def _body(self):
+        m = self.model
+        x = m.embedding(self.tokens)
+        for i, blk in enumerate(m.layers):
+            x = x + blk.mixer.step_inplace(blk.norm(x), *self.cache[i])
+            if m.mlp_layers is not None:
+                x = x + m.mlp_layers[i](m.mlp_norms[i](x))
+        logits = m.lm_head(m.norm_f(x))
+        if self.greedy:
+            self.tokens.copy_(logits.argmax(-1))
+        return logits
+
+    def reset(self):
+        for a, s, b in self.cache:
+            a.zero_()
+            s.zero_()
+            b.zero_()
+
+    def feed(self, tokens: torch.Tensor) -> torch.Tensor:
+        """One step on the given tokens (B,) or (B, 1); returns the static logits."""
+        self.tokens.copy_(tokens.reshape(-1))
+        self.graph.replay()
+        return self.logits
+
+    def next(self) -> torch.Tensor:
+        """One greedy step on the previous step's argmax; returns the static token buffer."""
+        self.graph.replay()
+        return self.tokens

@@ -9,6 +9,7 @@ step and allocate_inference_cache of the reference's ``mamba3_ssm/layer.py`` (:6
   Like the reference it returns new state tensors and leaves its inputs untouched.
 """
 
+import ctypes
 import math
 from typing import Tuple
 
@@ -146,8 +147,22 @@ class Mamba3(nn.Module):
         if self._f32_cache is None or self._f32_cache[0] != key:
             with torch.no_grad():
                 vals = [p.detach().float().contiguous() for p in ps]
-            self._f32_cache = (key, vals)
+            self._f32_cache = (key, vals, L.pack(*vals), self._dims())
         return self._f32_cache[1]
+
+    def _fused_step(self, zxbcdt, ang_in, ssm_in, bx_in, ang_out, ssm_out, bx_out, y):
+        """One decode step of the fused kernel (m3_siso_step / m3_mimo_step). Outputs may
+        alias inputs (in-place state update)."""
+        self._step_params()
+        _, _, pp, dims = self._f32_cache
+        lib = L.load()
+        fn, name = (lib.m3_mimo_step, "m3_mimo_step") if self.is_mimo else (lib.m3_siso_step, "m3_siso_step")
+        dyn = L.pack(zxbcdt, ang_in, ssm_in, bx_in, ang_out, ssm_out, bx_out, y)
+        dev = zxbcdt.device
+        with torch.cuda.device(dev):
+            rc = fn(ctypes.byref(dims), dyn.ptrs[0], *pp.ptrs, *dyn.ptrs[1:],
+                    torch.cuda.current_stream(dev).cuda_stream)
+        L.check(rc, name)
 
     def step(self, u: torch.Tensor, angle_state: torch.Tensor, ssm_state: torch.Tensor,
              bx_prev_state: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
@@ -157,8 +172,6 @@ class Mamba3(nn.Module):
         if zxbcdt.stride(-1) != 1:
             zxbcdt = zxbcdt.contiguous()
         batch = zxbcdt.shape[0]
-        dev = zxbcdt.device
-        params = self._step_params()
         ang_in = angle_state.float().contiguous()
         ssm_in = ssm_state.float().contiguous()
         bx_in = bx_prev_state.float().contiguous()
@@ -167,20 +180,8 @@ class Mamba3(nn.Module):
             ang_out = torch.empty_like(ang_in)
             ssm_out = torch.empty_like(ssm_in)
             bx_out = torch.empty_like(bx_in)
-            y = torch.empty((batch, self.d_inner), dtype=zxbcdt.dtype, device=dev)
-            dims = self._dims()
-            lib = L.load()
-            if self.is_mimo:
-                dtb, bb, cb, bw, cw, dd, mx, mo = params
-                args = [zxbcdt, dtb, bb, cb, bw, cw, dd, mx, mo, ang_in, ssm_in, bx_in, ang_out, ssm_out, bx_out, y]
-                fn, name = lib.m3_mimo_step, "m3_mimo_step"
-            else:
-                dtb, bb, cb, bw, cw, dd = params
-                args = [zxbcdt, dtb, bb, cb, bw, cw, dd, ang_in, ssm_in, bx_in, ang_out, ssm_out, bx_out, y]
-                fn, name = lib.m3_siso_step, "m3_siso_step"
-            ms = [L.tensor(t) for t in args]
-            with torch.cuda.device(dev):
-                L.check(fn(L.ref(dims), *[L.ref(m) for m in ms], L.stream_of(zxbcdt)), name)
+            y = torch.empty((batch, self.d_inner), dtype=zxbcdt.dtype, device=zxbcdt.device)
+            self._fused_step(zxbcdt, ang_in, ssm_in, bx_in, ang_out, ssm_out, bx_out, y)
             return y, ang_out, ssm_out, bx_out
 
         if torch.is_grad_enabled() and zxbcdt.requires_grad:
@@ -189,6 +190,17 @@ class Mamba3(nn.Module):
             y, ang_out, ssm_out, bx_out = run()
         out = self.out_proj(y.to(u.dtype))
         return out, ang_out, ssm_out, bx_out
+
+    def step_inplace(self, u: torch.Tensor, angle_state: torch.Tensor, ssm_state: torch.Tensor,
+                     bx_prev_state: torch.Tensor) -> torch.Tensor:
+        """Like step(), but updates the (fp32, contiguous) state tensors in place and returns
+        only the output; allocation-stable, so it can be recorded in a CUDA graph."""
+        zxbcdt = self.in_proj(u)
+        if zxbcdt.stride(-1) != 1:
+            zxbcdt = zxbcdt.contiguous()
+        y = torch.empty((zxbcdt.shape[0], self.d_inner), dtype=zxbcdt.dtype, device=zxbcdt.device)
+        self._fused_step(zxbcdt, angle_state, ssm_state, bx_prev_state, angle_state, ssm_state, bx_prev_state, y)
+        return self.out_proj(y.to(u.dtype))
 
     def allocate_inference_cache(self, batch_size: int, device=None, dtype=None):
         """Zero decode states (layer.py:380-412): angle (B,H,S), ssm and bx_prev

@@ -81,9 +81,9 @@ class _SisoScanFn(torch.autograd.Function):
         if want_state:
             hl = _empty((Bn, H, P, Ds), torch.float32, x.device)
             bl = _empty((Bn, H, P, Ds), torch.float32, x.device)
-        a = [L.tensor(t) for t in (x, B, C, ADT, DT, trap, D, h0, bx0, y, hl, bl)]
+        a = L.pack(x, B, C, ADT, DT, trap, D, h0, bx0, y, hl, bl)
         with torch.cuda.device(x.device):
-            L.check(lib.m3_siso_scan_fwd(*[L.ref(m) for m in a], L.stream_of(x)), "m3_siso_scan_fwd")
+            L.check(lib.m3_siso_scan_fwd(*a.ptrs, L.stream_of(x)), "m3_siso_scan_fwd")
         ctx.save_for_backward(x, B, C, ADT, DT, trap, D, h0, bx0)
         ctx.mark_non_differentiable(*[t for t in (hl, bl) if t is not None])
         return y, hl, bl
@@ -109,10 +109,10 @@ class _SisoScanFn(torch.autograd.Function):
         dbx0 = _empty(bx0.shape, torch.float32, dev) if (bx0 is not None and ctx.needs_input_grad[8]) else None
         nbytes = lib.m3_siso_scan_bwd_workspace_size(Bn, Ln, H, P, Ds)
         ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
-        a = [L.tensor(t) for t in (x, B, C, ADT, DT, trap, D, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD,
-                                   dh0, dbx0)]
+        a = L.pack(x, B, C, ADT, DT, trap, D, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD,
+                    dh0, dbx0)
         with torch.cuda.device(dev):
-            L.check(lib.m3_siso_scan_bwd(*[L.ref(m) for m in a], ws.data_ptr(), ws.numel(), L.stream_of(x)),
+            L.check(lib.m3_siso_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)),
                     "m3_siso_scan_bwd")
         return dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0, None
 
@@ -128,9 +128,9 @@ class _MimoScanFn(torch.autograd.Function):
         if want_state:
             hl = _empty((Bn, H, Ds), torch.float32, x.device)
             bl = _empty((Bn, H, Ds), torch.float32, x.device)
-        a = [L.tensor(t) for t in (x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, y, hl, bl)]
+        a = L.pack(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, y, hl, bl)
         with torch.cuda.device(x.device):
-            L.check(lib.m3_mimo_scan_fwd(*[L.ref(m) for m in a], L.stream_of(x)), "m3_mimo_scan_fwd")
+            L.check(lib.m3_mimo_scan_fwd(*a.ptrs, L.stream_of(x)), "m3_mimo_scan_fwd")
         ctx.save_for_backward(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0)
         ctx.mark_non_differentiable(*[t for t in (hl, bl) if t is not None])
         return y, hl, bl
@@ -158,10 +158,10 @@ class _MimoScanFn(torch.autograd.Function):
         dbx0 = _empty(bx0.shape, torch.float32, dev) if (bx0 is not None and ctx.needs_input_grad[10]) else None
         nbytes = lib.m3_mimo_scan_bwd_workspace_size(Bn, Ln, H, P, Ds, R)
         ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
-        a = [L.tensor(t) for t in (x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap,
-                                   dD, dmx, dmo, dh0, dbx0)]
+        a = L.pack(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap,
+                    dD, dmx, dmo, dh0, dbx0)
         with torch.cuda.device(dev):
-            L.check(lib.m3_mimo_scan_bwd(*[L.ref(m) for m in a], ws.data_ptr(), ws.numel(), L.stream_of(x)),
+            L.check(lib.m3_mimo_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)),
                     "m3_mimo_scan_bwd")
         return dx, dB, dC, dADT, dDT, dtrap, dD, dmx, dmo, dh0, dbx0, None
 
