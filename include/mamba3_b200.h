@@ -184,6 +184,21 @@ int m3_mimo_step(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_te
                  const m3_tensor* bx_in, m3_tensor* angle_out, m3_tensor* ssm_out,
                  m3_tensor* bx_out, m3_tensor* y_gated, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * RMSNorm with an optional fused residual add: the reference's RMSNorm.forward
+ * (mamba3_ssm/ops.py:94-102, x.float() / sqrt(mean(x^2) + eps) * weight, returned in
+ * x.dtype), used by MambaBlock (block.py:20-29, x + mixer(norm(x))), the B / C norms of
+ * Mamba3 (layer.py:215-225) and norm_f (block.py:78-80).
+ *   x, residual, out, residual_out: (..., d), one dtype (f32 / bf16 / f16), innermost
+ *   stride 1, leading dims collapsible into rows of one stride
+ *   weight (d) f32 / bf16 / f16
+ * With residual: h = x + residual (rounded to x.dtype like the eager add) is written to
+ * residual_out (optional; may alias x) and normalised. out may alias x or residual, not
+ * residual_out. Stream-ordered; the reference has no native counterpart (plain PyTorch).
+ * ------------------------------------------------------------------------------- */
+int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* weight, float eps,
+               m3_tensor* out, m3_tensor* residual_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,6 +7,7 @@
 #include "decode_step.cuh"
 #include "m3_common.cuh"
 #include "mimo_scan.cuh"
+#include "rmsnorm.cuh"
 #include "siso_chunk.cuh"
 #include "siso_scan.cuh"
 
@@ -510,6 +511,46 @@ int m3_mimo_step(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_te
                  m3_tensor* y_gated, void* stream) {
   return step_common(true, dims, zxbcdt, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, Dskip, mimo_x, mimo_o,
                      angle_in, ssm_in, bx_in, angle_out, ssm_out, bx_out, y_gated, stream);
+}
+
+
+int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* weight, float eps,
+               m3_tensor* out, m3_tensor* residual_out, void* stream) {
+  if (!present(x) || x->ndim < 1) return fail(M3_ERR_INVALID_ARGUMENT, "x: missing or 0-d");
+  const int nd = x->ndim;
+  const int64_t d = x->shape[nd - 1];
+  int64_t rows = 1;
+  for (int i = 0; i < nd - 1; ++i) rows *= x->shape[i];
+  const bool empty = rows * d == 0;
+  // every operand: (..., d) whose leading dims collapse into rows of one stride
+  auto rows_of = [&](const m3_tensor* t, const char* name, bool optional, unsigned mask, int64_t* srow) -> int {
+    if (!present(t)) {
+      if (optional) return M3_OK;
+      return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": missing");
+    }
+    M3_TRY(check(t, name, nd, x->shape, mask, false, false, !empty));
+    if (empty) return M3_OK;
+    for (int i = 0; i + 2 < nd; ++i)
+      if (t->shape[i] > 1 && t->stride[i] != t->stride[i + 1] * t->shape[i + 1])
+        return fail(M3_ERR_INVALID_ARGUMENT, std::string(name) + ": leading dims must collapse into rows");
+    *srow = nd >= 2 ? t->stride[nd - 2] : d;
+    return M3_OK;
+  };
+  NormParams p{};
+  p.rows = rows; p.d = d; p.eps = eps;
+  M3_TRY(rows_of(x, "x", false, kAnyFloat, &p.sx));
+  M3_TRY(rows_of(residual, "residual", true, 1u << x->dtype, &p.sres));
+  M3_TRY(rows_of(out, "out", false, 1u << x->dtype, &p.sout));
+  M3_TRY(rows_of(residual_out, "residual_out", true, 1u << x->dtype, &p.shout));
+  const int64_t ws[1] = {d};
+  M3_TRY(check(weight, "weight", 1, ws, kAnyFloat, true, false, !empty));
+  if (present(residual_out) && !present(residual))
+    return fail(M3_ERR_INVALID_ARGUMENT, "residual_out: given without residual");
+  if (present(residual_out) && present(out) && residual_out->data == out->data && !empty)
+    return fail(M3_ERR_INVALID_ARGUMENT, "out: must not alias residual_out");
+  p.x = x->data; p.res = present(residual) ? residual->data : nullptr;
+  p.w = weight->data; p.out = out->data; p.hout = present(residual_out) ? residual_out->data : nullptr;
+  return launch_rmsnorm(p, x->dtype, weight->dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -221,6 +221,34 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Warp totals of N values at once (N a power of two <= 32), every lane receiving all N.
+// Each butterfly step halves the values a lane carries: the lane whose `o` bit is set
+// keeps the upper half and the partner the lower half, so N values cost
+// N-1 + log2(32/N) shuffles plus N broadcasts instead of 5 N. Value k ends in the lanes
+// whose top log2(N) bits spell k, i.e. lane k * 32 / N.
+template <int N>
+__device__ __forceinline__ void warp_sum_n(float (&v)[N], int lane) {
+  if constexpr (N == 1) {
+    v[0] = warp_sum(v[0]);
+  } else {
+#pragma unroll
+    for (int n = N, o = 16; n > 1; n >>= 1, o >>= 1) {
+      const bool up = lane & o;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = up ? v[i] : v[i + n / 2];
+        const float keep = up ? v[i + n / 2] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    float t = v[0];
+#pragma unroll
+    for (int o = 16 / N; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+#pragma unroll
+    for (int k = 0; k < N; ++k) v[k] = __shfl_sync(0xffffffffu, t, k * (32 / N));
+  }
+}
+
 template <typename TZ, int DL, int RM, int PJ>
 __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_warp_kernel(StepParams a) {
   constexpr int NK = RM * DL;  // B / C values per lane
@@ -303,10 +331,16 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_warp_kernel(StepPara
     rB[k / DL] = fmaf(Bv[k], Bv[k], rB[k / DL]);
     rC[k / DL] = fmaf(Cv[k], Cv[k], rC[k / DL]);
   }
+  {
+    float ss[2 * RM];
 #pragma unroll
-  for (int r = 0; r < RM; ++r) {
-    rB[r] = 1.0f / sqrtf(warp_sum(rB[r]) / D + a.eps);
-    rC[r] = 1.0f / sqrtf(warp_sum(rC[r]) / D + a.eps);
+    for (int r = 0; r < RM; ++r) { ss[r] = rB[r]; ss[RM + r] = rC[r]; }
+    warp_sum_n<2 * RM>(ss, lane);
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+      rB[r] = rsqrtf(ss[r] / D + a.eps);
+      rC[r] = rsqrtf(ss[RM + r] / D + a.eps);
+    }
   }
   // RoPE angle of this lane's pairs: one sincos per d slot, shared by every rank
   float sn[DL], cs[DL];
@@ -348,8 +382,9 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_warp_kernel(StepPara
       const int p = lane + 32 * j;
       if (r < R && p < P) acc = fmaf(smx[r * P + p], xv[j], acc);
     }
-    xr[r] = warp_sum(acc);
+    xr[r] = acc;
   }
+  warp_sum_n<RM>(xr, lane);
   // state update (layer.py:347-351) and y_r = C_r h
   float yr[RM];
 #pragma unroll
@@ -367,7 +402,9 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_warp_kernel(StepPara
     for (int r = 0; r < RM; ++r) yr[r] = fmaf(Cv[r * DL + k], hn, yr[r]);
   }
 #pragma unroll
-  for (int r = 0; r < RM; ++r) yr[r] = warp_sum(yr[r]) + Dk * xr[r];
+  warp_sum_n<RM>(yr, lane);
+#pragma unroll
+  for (int r = 0; r < RM; ++r) yr[r] += Dk * xr[r];
   // y = mimo_o^T (y_r + D xr), gated by silu(z) (layer.py:352-356)
   TZ* yo = reinterpret_cast<TZ*>(a.y) + (int64_t)b * a.s_y + h * P;
 #pragma unroll

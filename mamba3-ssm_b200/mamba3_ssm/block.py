@@ -11,7 +11,7 @@ import torch.nn.functional as F
 
 from .config import MambaConfig
 from .layer import Mamba3
-from .ops import RMSNorm
+from .ops import RMSNorm, rmsnorm
 
 
 class MambaBlock(nn.Module):
@@ -80,18 +80,33 @@ class MambaLMHeadModel(nn.Module):
     def allocate_inference_cache(self, batch_size: int) -> List[Tuple[torch.Tensor, ...]]:
         return [blk.mixer.allocate_inference_cache(batch_size) for blk in self.layers]
 
+    def _norms_after(self, i):
+        """The norm that follows layer i's mixer residual add: the MLP norm of layer i,
+        the next block's norm, or norm_f."""
+        if self.mlp_layers is not None:
+            return self.mlp_norms[i]
+        return self.layers[i + 1].norm if i + 1 < len(self.layers) else self.norm_f
+
     def step(self, input_ids: torch.Tensor, cache: List[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]]):
         if input_ids.dim() == 1:
             input_ids = input_ids.unsqueeze(-1)
         x = self.embedding(input_ids).squeeze(1)
         new_cache = []
+        h = self.layers[0].norm(x) if self.layers else self.norm_f(x)
         for i, block in enumerate(self.layers):
-            out, a, s, b = block.mixer.step(block.norm(x), *cache[i])
-            x = x + out
+            out, a, s, b = block.mixer.step(h, *cache[i])
             new_cache.append((a, s, b))
+            # x = x + out, then the next norm, in one kernel
+            nrm = self._norms_after(i)
+            x_new = torch.empty_like(x)
+            h = rmsnorm(x, nrm.weight, nrm.eps, residual=out, residual_out=x_new)
+            x = x_new
             if self.mlp_layers is not None:
-                x = x + self.mlp_layers[i](self.mlp_norms[i](x))
-        return self.lm_head(self.norm_f(x)), new_cache
+                nxt = self.layers[i + 1].norm if i + 1 < len(self.layers) else self.norm_f
+                x_new = torch.empty_like(x)
+                h = rmsnorm(x, nxt.weight, nxt.eps, residual=self.mlp_layers[i](h), residual_out=x_new)
+                x = x_new
+        return self.lm_head(h), new_cache
 
     # ------------------------------------------------------------------------------
     def decode_graph(self, batch_size: int, greedy: bool = True) -> "DecodeGraph":
@@ -135,11 +150,15 @@ class DecodeGraph:
     def _body(self):
         m = self.model
         x = m.embedding(self.tokens)
+        h = m.layers[0].norm(x) if m.layers else m.norm_f(x)
         for i, blk in enumerate(m.layers):
-            x = x + blk.mixer.step_inplace(blk.norm(x), *self.cache[i])
+            out = blk.mixer.step_inplace(h, *self.cache[i])
+            nrm = m._norms_after(i)
+            h = rmsnorm(x, nrm.weight, nrm.eps, residual=out, residual_out=x)  # x += out; norm
             if m.mlp_layers is not None:
-                x = x + m.mlp_layers[i](m.mlp_norms[i](x))
-        logits = m.lm_head(m.norm_f(x))
+                nxt = m.layers[i + 1].norm if i + 1 < len(m.layers) else m.norm_f
+                h = rmsnorm(x, nxt.weight, nxt.eps, residual=m.mlp_layers[i](h), residual_out=x)
+        logits = m.lm_head(h)
         if self.greedy:
             self.tokens.copy_(logits.argmax(-1))
         return logits

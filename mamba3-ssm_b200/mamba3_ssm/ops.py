@@ -22,7 +22,8 @@ _PAIRS = {(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16), (tor
 
 
 class RMSNorm(nn.Module):
-    """x / sqrt(mean(x^2) + eps) * weight, computed in fp32 and returned in x.dtype."""
+    """x / sqrt(mean(x^2) + eps) * weight, computed in fp32 and returned in x.dtype: the
+    m3_rmsnorm kernel for inference, the eager formula when autograd needs a graph."""
 
     def __init__(self, d: int, eps: float = 1e-5):
         super().__init__()
@@ -30,9 +31,41 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(d))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        rms = xf.pow(2).mean(dim=-1, keepdim=True).add(self.eps).sqrt()
-        return (xf / rms * self.weight).to(x.dtype)
+        if torch.is_grad_enabled() and (x.requires_grad or self.weight.requires_grad):
+            # training: the reference's own formula, differentiated by autograd
+            xf = x.float()
+            rms = xf.pow(2).mean(dim=-1, keepdim=True).add(self.eps).sqrt()
+            return (xf / rms * self.weight).to(x.dtype)
+        return rmsnorm(x, self.weight, self.eps)
+
+
+def _rows_view(t: torch.Tensor) -> bool:
+    """Innermost stride 1 and the leading dims collapse into rows of one stride."""
+    st, sh = t.stride(), t.shape
+    if t.dim() and sh[-1] > 1 and st[-1] != 1:
+        return False
+    return all(sh[i] <= 1 or st[i] == st[i + 1] * sh[i + 1] for i in range(t.dim() - 2))
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor = None,
+            residual_out: torch.Tensor = None) -> torch.Tensor:
+    """RMSNorm (ops.py:94-102) on the m3_rmsnorm kernel. With ``residual``, normalises
+    h = x + residual (rounded to x.dtype) and, when ``residual_out`` is given, writes h
+    there (it may be x itself). Returns the normalised tensor in x.dtype."""
+    if not x.is_cuda:
+        raise RuntimeError("rmsnorm: the B200 build runs on CUDA tensors only (no CPU path)")
+    if not _rows_view(x):
+        x = x.contiguous()
+    if residual is not None and not _rows_view(residual):
+        residual = residual.contiguous()
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    lib = L.load()
+    a = L.pack(x, residual, weight, out, residual_out)
+    with torch.cuda.device(x.device):
+        rc = lib.m3_rmsnorm(a.ptrs[0], a.ptrs[1], a.ptrs[2], float(eps), a.ptrs[3], a.ptrs[4],
+                            torch.cuda.current_stream(x.device).cuda_stream)
+    L.check(rc, "m3_rmsnorm")
+    return out
 
 
 def build_rope_freqs(num_angles: int, device=None) -> torch.Tensor:
