@@ -107,6 +107,13 @@ class ClockSampler:
             self.th.start()
         except (OSError, ValueError):
             self.proc = None
+            return
+        # nvidia-smi's first query of the throttle reasons stalls the GPU for ~0.1 s: let it
+        # land before the timed region starts
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 10.0 and self.proc.poll() is None:
+            time.sleep(0.05)
+        time.sleep(0.3)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -441,7 +448,6 @@ def main():
     sampler = ClockSampler(uids) if rank == 0 else None
     if sampler:
         sampler.start()
-        time.sleep(0.3)
     barrier()
     torch.cuda.synchronize()
     t_beg.record()
@@ -453,6 +459,8 @@ def main():
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop() if sampler else None
+    if _lib.device_timeouts(reset=True):
+        raise RuntimeError("a bounded inter-warp wait gave up during the timed region; outputs invalid")
     total_ms = t_beg.elapsed_time(t_end)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     total_ms, kern_ms = max_over_ranks([total_ms, kern_ms], pg, dev)

@@ -199,6 +199,14 @@ int m3_mimo_step(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_te
 int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* weight, float eps,
                m3_tensor* out, m3_tensor* residual_out, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Health word of the warp-specialised kernels on the current device: *flag_out is
+ * nonzero once any bounded inter-warp wait gave up (the kernel then drained and its
+ * outputs are invalid); reset != 0 clears it. Synchronises the device. No reference
+ * counterpart (the reference checks no launch at all, cuda_backend.py:403-405).
+ * ------------------------------------------------------------------------------- */
+int m3_device_timeouts(int reset, int* flag_out);
+
 #ifdef __cplusplus
 }
 #endif

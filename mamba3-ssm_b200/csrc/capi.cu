@@ -553,4 +553,10 @@ int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* w
   return launch_rmsnorm(p, x->dtype, weight->dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
+
+int m3_device_timeouts(int reset, int* flag_out) {
+  if (!flag_out) return fail(M3_ERR_INVALID_ARGUMENT, "flag_out: missing");
+  return chunk_error_word(reset != 0, flag_out);
+}
+
 }  // extern "C"

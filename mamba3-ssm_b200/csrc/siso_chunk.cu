@@ -21,21 +21,28 @@
 // per element. Then y = e^{lambda} Y1 + Y2 and k^T = e^{lambda_Q} k^T + dK^T.
 //
 // Warp-specialised, persistent CTA (one per SM, 16 warps), walking its (b, h) units
-// chunk by chunk:
-//   warp 0      TMA producer: C, B (2 x 64-column boxes each) and X of a chunk into a
-//               2-stage ring (80 KB per stage)
-//   warp 1      tcgen05 MMA issuer (one elected lane) and TMEM owner (512 columns:
-//               two buffer sets of G | dK, Y1, Y2 so consecutive chunks overlap)
+// chunk by chunk. Shared-memory buffers are split by lifetime so that the large C / B
+// tiles are released as soon as the early MMAs have read them:
+//   C, B (64 KB)  2-stage ring; read by G, Y1 and dK, freed after dK (issued early)
+//   X    (16 KB)  3-stage ring; read by the state warps (w o X) and by Y2 after the mask
+//   w o X, k_c^T  one buffer each
+// Roles:
+//   warp 0      TMA producer (one thread polling the C/B ring and the X ring, plus the L2
+//               prefetch of later chunks)
+//   warp 1      tcgen05 MMA issuer (one thread polling two streams: G, Y1, dK fed by the
+//               loads and the state warps; Y2 gated by the mask) and TMEM owner (512
+//               columns: per chunk parity G (128, G' packed in place), Y1 (64), Y2 (64,
+//               shared with dK, which the state warps read before Y2 is written))
 //   warps 2-3   per-chunk scalars (decay cumsum, mu, block factors, state weights) into a
 //               4-slot ring, even / odd chunks, running ahead of the consumers
-//   warps 4-7   even chunks: G -> G' in TMEM (in place, packed bf16), w o X into smem,
-//               then the epilogue y = e^{lambda} Y1 + Y2 -> global (bf16)
+//   warps 4-7   even chunks: G -> G' in TMEM (in place, packed bf16), then the epilogue
+//               y = e^{lambda} Y1 + Y2 -> global (bf16)
 //   warps 12-15 odd chunks: the same
-//   warps 8-11  state: k^T (fp32, registers) <- decay k^T + dK^T, bf16 copy for the next Y1
-// The TMA warp also streams the chunks 2-3 ahead into L2, so refilling a stage (which can
-// only start once the MMAs reading it are done) is served from L2.
-// All hand-offs are mbarriers with bounded waits; on a timeout the kernel records an error
-// and drains.
+//   warps 8-11  state: w o X for dK, then k^T (fp32, registers) <- decay k^T + dK^T and
+//               its bf16 copy for the next Y1
+// All hand-offs are mbarriers; every wait is bounded (blocking waits by a poll count, the
+// polling producer and issuer by an idle count), and on a timeout the kernel records an
+// error and drains.
 #include <cudaTypedefs.h>
 
 #include <cstddef>
@@ -53,21 +60,22 @@ constexpr int Q = 128;
 constexpr int kP = 64;
 constexpr int kD = 128;
 constexpr int kThreads = 512;
-constexpr int NS = 2;    // TMA stages
+constexpr int NS = 2;    // C/B stages
+constexpr int NX = 3;    // X stages
 constexpr int NSC = 4;   // scalar slots
 constexpr int kPrefetch = 3;  // chunks streamed into L2 ahead of their TMA load
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTileBytes = Q * 64 * 2;       // one SW128 tile: 128 rows x 128 B
-constexpr uint32_t kStageBytes = 5 * kTileBytes;  // C(2) + B(2) + X
+constexpr uint32_t kCBBytes = 4 * kTileBytes;     // C(2) + B(2)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kSafeExp2 = 120.f;
+constexpr uint32_t kIdleLimit = 1u << 22;  // idle polls (~32 ns apart) before the producers give up
 
-// TMEM columns of buffer set p: G (128, G' packed in its first 64, dK in its last 64),
-// Y1 (64), Y2 (64).
+// TMEM columns of chunk parity p: G (128; G' packed into its first 64), Y1 (64), Y2 / dK (64).
 __device__ __forceinline__ uint32_t col_g(int p) { return 256u * p; }
-__device__ __forceinline__ uint32_t col_dk(int p) { return 256u * p + 64u; }
 __device__ __forceinline__ uint32_t col_y1(int p) { return 256u * p + 128u; }
 __device__ __forceinline__ uint32_t col_y2(int p) { return 256u * p + 192u; }
+__device__ __forceinline__ uint32_t col_dk(int p) { return 256u * p + 192u; }
 
 struct __align__(16) ScalSlot {
   float colf[Q];      // e^{lambda_{32b+1} - lambda_{j+1}} mu_j (read as float4)
@@ -83,15 +91,16 @@ struct __align__(16) ScalSlot {
 };
 
 struct __align__(1024) Smem {
-  uint8_t stage[NS][5][kTileBytes];  // C(d 0-63), C(d 64-127), B(0-63), B(64-127), X
-  uint8_t xs[2][kTileBytes];         // (w o x)[t][p]
+  uint8_t cb[NS][4][kTileBytes];     // C(d 0-63), C(d 64-127), B(0-63), B(64-127)
+  uint8_t xr[NX][kTileBytes];        // x[t][p]
+  uint8_t xs[kTileBytes];            // (w o x)[t][p]
   uint8_t kbuf[kTileBytes];          // k_c^T[d][p]
   ScalSlot sc[NSC];
-  float side_x[2][kP];               // last row of a unit (for the final B*x)
-  float side_b[2][kD];
-  uint64_t stage_full[NS], stage_empty[NS];
-  uint64_t g_full[2], gp_ready[2], g_free[2], dk_full[2], y_full[2], y_free[2];
-  uint64_t k_ready;
+  float side_x[kP];                  // last row of a unit (for the final B*x)
+  float side_b[kD];
+  uint64_t cb_full[NS], cb_empty[NS], x_full[NX], x_empty[NX];
+  uint64_t xs_full, xs_empty, k_ready;
+  uint64_t g_full[2], gp_ready[2], y_full[2], y_free[2], dk_full[2], dk_free[2];
   uint64_t scal_full[NSC], scal_empty[NSC];
   uint32_t tmem_base;
 };
@@ -316,35 +325,18 @@ __device__ void scalar_role(const ChunkArgs& a, Smem& s, int G, int nch, int lan
 }
 
 // ------------------------------------------------------------------------------------
-// G -> G' (TMEM, in place) and w o X -> smem. Warps 4-7 take the even chunks, warps 12-15
-// the odd ones (each chunk parity has its own TMEM buffer set), so two chunks are masked
-// concurrently. Thread i owns row i. Warp r (rows 32r..32r+31) sees column blocks b < r
-// entirely below the diagonal, block r on it and blocks b > r above it (zeros, not read).
-// Blocks go in increasing order with the TMEM load of the next block issued before the
-// current one is converted; the packed bf16 G' of block b lands in columns 16b..16b+15,
-// which this thread has already read.
-// ------------------------------------------------------------------------------------
 // One 32-column block of row i: full (below the diagonal), diagonal and above-diagonal
-// blocks share one code path through the column limit il = i - 32 qd. When the block's
-// split exponents could leave the fp32 range (`exact`), the factor is one exp2 per element.
+// blocks share one code path through the column limit il = i - 32 qd. The factor of
+// element j is the block's row factor times its column factor.
 __device__ __forceinline__ void mask_block(const uint32_t (&r)[32], uint32_t (&pk)[16], int qd, int i,
-                                           const ScalSlot& sl, float li, float bi, float dk, bool exact) {
-  const float rowf = exact ? 0.f : exp2f(li - sl.lam2[32 * qd + 1]);
+                                           const ScalSlot& sl, float li, float bi, float dk) {
+  const float rowf = exp2f(li - sl.lam2[32 * qd + 1]);
   const int il = i - 32 * qd;
   const float4* cf4 = reinterpret_cast<const float4*>(sl.colf + 32 * qd);
 #pragma unroll
   for (int e4 = 0; e4 < 8; ++e4) {
-    float cc[4];
-    if (!exact) {
-      const float4 c = cf4[e4];
-      cc[0] = c.x * rowf; cc[1] = c.y * rowf; cc[2] = c.z * rowf; cc[3] = c.w * rowf;
-    } else {
-#pragma unroll
-      for (int z = 0; z < 4; ++z) {
-        const int j = 32 * qd + 4 * e4 + z;
-        cc[z] = j < i ? exp2f(li - sl.lam2[j + 1]) * sl.mu[j] : 0.f;
-      }
-    }
+    const float4 c = cf4[e4];
+    const float cc[4] = {c.x * rowf, c.y * rowf, c.z * rowf, c.w * rowf};
     float v[4];
 #pragma unroll
     for (int z = 0; z < 4; ++z) {
@@ -358,14 +350,30 @@ __device__ __forceinline__ void mask_block(const uint32_t (&r)[32], uint32_t (&p
   }
 }
 
-__device__ __noinline__ void stash_last_row(Smem& s, int p, int st, int i) {
-  const uint8_t* xt = s.stage[st][4];
-  for (int pp = 0; pp < kP; ++pp)
-    s.side_x[p][pp] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(xt + sw128_off(i, pp)));
-  for (int d = 0; d < kD; ++d)
-    s.side_b[p][d] =
-        __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(s.stage[st][2 + (d >> 6)] + sw128_off(i, d & 63)));
+// The same block when its split exponents could leave the fp32 range: one exp2 per
+// element. Rare (chunks with |ADT| above 2.5 or ADT above 0.6), so it is kept out of line
+// and rolled; it reloads G from TMEM itself, so no register array crosses the call.
+__device__ __noinline__ void mask_block_exact(uint32_t taddr_in, uint32_t taddr_out, int qd, int i,
+                                              const ScalSlot& sl, float li, float bi, float dk) {
+  uint32_t r[32];
+  tmem_ld32(taddr_in, r);
+  tmem_wait_ld();
+  uint32_t pk[16];
+  const int il = i - 32 * qd;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    float v[2];
+#pragma unroll
+    for (int z = 0; z < 2; ++z) {
+      const int jl = 2 * e + z, j = 32 * qd + jl;
+      const float gij = __uint_as_float(r[jl]);
+      v[z] = jl < il ? gij * (exp2f(li - sl.lam2[j + 1]) * sl.mu[j]) : (jl == il ? fmaf(gij, bi, dk) : 0.f);
+    }
+    pk[e] = pack_bf16(v[0], v[1]);
+  }
+  tmem_st16(taddr_out, pk);
 }
+
 
 // y = e^{lambda} Y1 + Y2 of chunk g, thread = row i
 __device__ __forceinline__ void epilogue(const ChunkArgs& a, Smem& s, uint32_t tbase, int g, int nch, int warp, int i) {
@@ -398,30 +406,40 @@ __device__ __forceinline__ void epilogue(const ChunkArgs& a, Smem& s, uint32_t t
   }
 }
 
+// ------------------------------------------------------------------------------------
+// G -> G' (TMEM, in place), then the epilogue. Warps 4-7 take the even chunks, warps
+// 12-15 the odd ones (each chunk parity has its own TMEM columns), so two chunks are
+// masked concurrently. Thread i owns row i. Warp r (rows 32r..32r+31) sees column blocks
+// b < r entirely below the diagonal, block r on it and blocks b > r above it (zeros, not
+// read). The packed bf16 G' of block b lands in columns 16b..16b+15, which this thread has
+// already read.
+// ------------------------------------------------------------------------------------
 __device__ void mask_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, int nch, int warp, int i, int parity) {
   const int wr = warp & 3;
   for (int g = parity; g < G; g += 2) {
-    const int p = g & 1, q = g % NSC, st = g % NS;
+    const int p = g & 1, q = g % NSC;
     if (!wait_or_flag(&s.scal_full[q], (g / NSC) & 1)) return;
     if (!wait_or_flag(&s.g_full[p], (g >> 1) & 1)) return;
-    // the stage's phase is already complete (G was computed from it); this wait makes its
-    // TMA writes visible to this thread's X / B reads
-    if (!wait_or_flag(&s.stage_full[st], (g / NS) & 1)) return;
     tc_fence_after();
     const ScalSlot& sl = s.sc[q];
     const float li = sl.lam2[i];
     const float bi = sl.beta[i];
     const float dk = sl.dskip;
     const int flags = sl.flags;
-    // one block at a time; the packed store of block b lands on columns this thread read
 #pragma unroll 1
     for (int qd = 0; qd <= wr; ++qd) {
-      uint32_t r[32];
-      tmem_ld32(lane_addr(tbase, warp, col_g(p) + 32 * qd), r);
-      tmem_wait_ld();
-      uint32_t pk[16];
-      mask_block(r, pk, qd, i, sl, li, bi, dk, !((flags >> (4 + qd)) & 1));
-      tmem_st16(lane_addr(tbase, warp, col_g(p) + 16 * qd), pk);
+      const uint32_t tin = lane_addr(tbase, warp, col_g(p) + 32 * qd);
+      const uint32_t tout = lane_addr(tbase, warp, col_g(p) + 16 * qd);
+      if ((flags >> (4 + qd)) & 1) {
+        uint32_t r[32];
+        tmem_ld32(tin, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+        mask_block(r, pk, qd, i, sl, li, bi, dk);
+        tmem_st16(tout, pk);
+      } else {
+        mask_block_exact(tin, tout, qd, i, sl, li, bi, dk);
+      }
     }
     {
       uint32_t z[16];
@@ -430,30 +448,10 @@ __device__ void mask_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, in
 #pragma unroll 1
       for (int qd = wr + 1; qd < 4; ++qd) tmem_st16(lane_addr(tbase, warp, col_g(p) + 16 * qd), z);
     }
-    // (w o x) row i
-    {
-      const float wi = sl.w[i];
-      const uint8_t* xt = s.stage[st][4];
-      uint8_t* dst = s.xs[p];
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xt + sw128_off(i, 8 * cc));
-        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[e]));
-          o[e] = pack_bf16(f.x * wi, f.y * wi);
-        }
-        *reinterpret_cast<uint4*>(dst + sw128_off(i, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-      if ((flags & 2) && a.bx_last && i == sl.n - 1) stash_last_row(s, p, st, i);
-    }
     tmem_wait_st();
-    fence_proxy_async_smem();
     tc_fence_before();
     mbar_arrive(&s.gp_ready[p]);
-    // this chunk's outputs (Y1 and Y2 complete with dK at one commit point)
+    // this chunk's outputs (Y1 and Y2 complete at one commit point)
     if (!wait_or_flag(&s.y_full[p], (g >> 1) & 1)) return;
     tc_fence_after();
     epilogue(a, s, tbase, g, nch, warp, i);
@@ -462,7 +460,7 @@ __device__ void mask_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, in
 }
 
 // ------------------------------------------------------------------------------------
-// warps 8-11: carried state, thread = state row d
+// warps 8-11: w o X (thread = row t) and the carried state (thread = state row d)
 // ------------------------------------------------------------------------------------
 __device__ __forceinline__ void write_kbuf(Smem& s, int d, const float (&k)[kP]) {
 #pragma unroll
@@ -476,9 +474,8 @@ __device__ __forceinline__ void write_kbuf(Smem& s, int d, const float (&k)[kP])
   }
 }
 
-__device__ __forceinline__ void init_state(const ChunkArgs& a, const ChunkPos& cp, const ScalSlot& sl, int d,
-                                        float (&k)[kP]) {
-  const float a0 = sl.a0, g0 = sl.g0;
+__device__ __forceinline__ void init_state(const ChunkArgs& a, const ChunkPos& cp, float a0, float g0, int d,
+                                           float (&k)[kP]) {
   const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * kD;
 #pragma unroll
   for (int pp = 0; pp < kP; ++pp) {
@@ -489,56 +486,102 @@ __device__ __forceinline__ void init_state(const ChunkArgs& a, const ChunkPos& c
   }
 }
 
-__device__ __forceinline__ void store_final(const ChunkArgs& a, const Smem& s, const ChunkPos& cp, int p, int d,
-                                         const float (&k)[kP]) {
-  const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * kD;
+__device__ __forceinline__ void store_final(const ChunkArgs& a, const Smem& s, int b, int h, int d,
+                                            const float (&k)[kP]) {
+  const int64_t sb = ((int64_t)b * a.H + h) * kP * kD;
   if (a.h_last)
     for (int pp = 0; pp < kP; ++pp) a.h_last[sb + (int64_t)pp * kD + d] = k[pp];
   if (a.bx_last) {
-    const float bd = s.side_b[p][d];
-    for (int pp = 0; pp < kP; ++pp) a.bx_last[sb + (int64_t)pp * kD + d] = s.side_x[p][pp] * bd;
+    const float bd = s.side_b[d];
+    for (int pp = 0; pp < kP; ++pp) a.bx_last[sb + (int64_t)pp * kD + d] = s.side_x[pp] * bd;
+  }
+}
+
+__device__ __noinline__ void stash_last_row(Smem& s, const uint8_t* xt, const uint8_t* bt0, const uint8_t* bt1, int i) {
+  for (int pp = 0; pp < kP; ++pp)
+    s.side_x[pp] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(xt + sw128_off(i, pp)));
+  for (int d = 0; d < kD; ++d)
+    s.side_b[d] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>((d < 64 ? bt0 : bt1) + sw128_off(i, d & 63)));
+}
+
+// k = dec * k + dK(parity p), read in quarters
+__device__ __forceinline__ void add_dk(uint32_t tbase, int warp, int p, float dec, float (&k)[kP]) {
+#pragma unroll
+  for (int qt = 0; qt < 4; ++qt) {
+    uint32_t r[16];
+    tmem_ld16(lane_addr(tbase, warp, col_dk(p) + 16 * qt), r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) k[16 * qt + e] = fmaf(dec, k[16 * qt + e], __uint_as_float(r[e]));
   }
 }
 
 __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, int nch, int warp, int d) {
   float k[kP];
-  for (int g = 0; g < G; ++g) {
-    const int p = g & 1, q = g % NSC;
+  float prev_dec = 0.f;
+  int prev_b = 0, prev_h = 0, prev_last = 0;
+  for (int g = 0; g <= G; ++g) {
+    // (1) fold dK(g-1) into the carried state (or finish the unit that g-1 closed)
+    if (g > 0) {
+      const int pp = (g - 1) & 1;
+      if (!wait_or_flag(&s.dk_full[pp], ((g - 1) >> 1) & 1)) return;
+      tc_fence_after();
+      add_dk(tbase, warp, pp, prev_dec, k);
+      tc_fence_before();
+      mbar_arrive(&s.dk_free[pp]);
+      if (prev_last && (a.h_last || a.bx_last)) store_final(a, s, prev_b, prev_h, d, k);
+    }
+    if (g == G) break;
+    const int q = g % NSC, xi = g % NX;
     const ChunkPos cp = chunk_pos(a, g, nch);
     if (!wait_or_flag(&s.scal_full[q], (g / NSC) & 1)) return;
     const ScalSlot& sl = s.sc[q];
+    // (2) k_c for this chunk -> kbuf (its previous reader, Y1(g-1), finished before dK(g-1))
     if (cp.first) {
       if (a.h0 || a.bx0) {
-        init_state(a, cp, sl, d, k);
+        init_state(a, cp, sl.a0, sl.g0, d, k);
       } else {
 #pragma unroll
         for (int pp = 0; pp < kP; ++pp) k[pp] = 0.f;
       }
-      write_kbuf(s, d, k);
-      fence_proxy_async_smem();
-      mbar_arrive(&s.k_ready);
     }
-    if (!wait_or_flag(&s.dk_full[p], (g >> 1) & 1)) return;
-    tc_fence_after();
-    const float dec = sl.decay_end;
-    const int flags = sl.flags;
+    write_kbuf(s, d, k);
+    fence_proxy_async_smem();
+    mbar_arrive(&s.k_ready);
+    // (3) (w o x) row t = d of this chunk, for dK(g)
+    if (!wait_or_flag(&s.x_full[xi], (g / NX) & 1)) return;
+    if (!wait_or_flag(&s.xs_empty, (g & 1) ^ 1)) return;
+    {
+      const float wi = sl.w[d];
+      const uint8_t* xt = s.xr[xi];
 #pragma unroll
-    for (int qt = 0; qt < 4; ++qt) {
-      uint32_t r[16];
-      tmem_ld16(lane_addr(tbase, warp, col_dk(p) + 16 * qt), r);
-      tmem_wait_ld();
+      for (int cc = 0; cc < 8; ++cc) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xt + sw128_off(d, 8 * cc));
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) k[16 * qt + e] = fmaf(dec, k[16 * qt + e], __uint_as_float(r[e]));
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[e]));
+          o[e] = pack_bf16(f.x * wi, f.y * wi);
+        }
+        *reinterpret_cast<uint4*>(s.xs + sw128_off(d, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      // the C/B stage stays valid until dK(g), which waits for xs_full below; the other
+      // state threads read the stash after dK(g) (named barrier of warps 8-11)
+      if (cp.last && a.bx_last) {
+        if (d == sl.n - 1) {
+          const int st = g % NS;
+          stash_last_row(s, xt, s.cb[st][2], s.cb[st][3], d);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
     }
-    tc_fence_before();
-    mbar_arrive(&s.g_free[p]);
-    if (!(flags & 2)) {
-      write_kbuf(s, d, k);
-      fence_proxy_async_smem();
-      mbar_arrive(&s.k_ready);
-    } else if (a.h_last || a.bx_last) {
-      store_final(a, s, cp, p, d, k);
-    }
+    fence_proxy_async_smem();
+    mbar_arrive(&s.xs_full);
+    prev_dec = sl.decay_end;
+    prev_last = cp.last;
+    prev_b = cp.b;
+    prev_h = cp.h;
     mbar_arrive(&s.scal_empty[q]);
   }
 }
@@ -557,18 +600,24 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
 
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&s.stage_full[i], 1);
-      mbar_init(&s.stage_empty[i], 1);
+      mbar_init(&s.cb_full[i], 1);
+      mbar_init(&s.cb_empty[i], 1);
     }
+    for (int i = 0; i < NX; ++i) {
+      mbar_init(&s.x_full[i], 1);
+      mbar_init(&s.x_empty[i], 1);
+    }
+    mbar_init(&s.xs_full, 128);
+    mbar_init(&s.xs_empty, 1);
+    mbar_init(&s.k_ready, 128);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.g_full[i], 1);
       mbar_init(&s.gp_ready[i], 128);
-      mbar_init(&s.g_free[i], 128);
-      mbar_init(&s.dk_full[i], 1);
       mbar_init(&s.y_full[i], 1);
       mbar_init(&s.y_free[i], 128);
+      mbar_init(&s.dk_full[i], 1);
+      mbar_init(&s.dk_free[i], 128);
     }
-    mbar_init(&s.k_ready, 128);
     for (int i = 0; i < NSC; ++i) {
       mbar_init(&s.scal_full[i], 32);
       mbar_init(&s.scal_empty[i], 2 * 128);
@@ -585,85 +634,148 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
   const uint32_t tbase = s.tmem_base;
 
   if (warp == 0) {
+    // one producer thread polling two independent streams: the C/B ring (waits for dK of
+    // two chunks back) and the X ring with the L2 prefetch (waits for Y2 of three back)
     if (lane == 0) {
       prefetch_tensormap(&tm_x);
       prefetch_tensormap(&tm_B);
       prefetch_tensormap(&tm_C);
-      for (int g = 0; g < G; ++g) {
-        const int st = g % NS;
-        if (!wait_or_flag(&s.stage_empty[st], ((g / NS) & 1) ^ 1)) break;
-        const ChunkPos cp = chunk_pos(a, g, nch);
-        mbar_expect_tx(&s.stage_full[st], kStageBytes);
-        tma_load_4d(s.stage[st][0], &tm_C, &s.stage_full[st], 0, cp.h, cp.t0, cp.b);
-        tma_load_4d(s.stage[st][1], &tm_C, &s.stage_full[st], 64, cp.h, cp.t0, cp.b);
-        tma_load_4d(s.stage[st][2], &tm_B, &s.stage_full[st], 0, cp.h, cp.t0, cp.b);
-        tma_load_4d(s.stage[st][3], &tm_B, &s.stage_full[st], 64, cp.h, cp.t0, cp.b);
-        tma_load_4d(s.stage[st][4], &tm_x, &s.stage_full[st], 0, cp.h, cp.t0, cp.b);
-        // stream the following chunks into L2 so a stage refill is an L2 hit
-        for (int ahead = (g == 0 ? 1 : kPrefetch); ahead <= kPrefetch; ++ahead) {
-          if (g + ahead >= G) break;
-          const ChunkPos pf = chunk_pos(a, g + ahead, nch);
-          tma_prefetch_l2_4d(&tm_C, 0, pf.h, pf.t0, pf.b);
-          tma_prefetch_l2_4d(&tm_C, 64, pf.h, pf.t0, pf.b);
-          tma_prefetch_l2_4d(&tm_B, 0, pf.h, pf.t0, pf.b);
-          tma_prefetch_l2_4d(&tm_B, 64, pf.h, pf.t0, pf.b);
-          tma_prefetch_l2_4d(&tm_x, 0, pf.h, pf.t0, pf.b);
+      int gc = 0, gx = 0;
+      uint32_t idle = 0;
+      while (gc < G || gx < G) {
+        bool moved = false;
+        if (gc < G && mbar_test(&s.cb_empty[gc % NS], ((gc / NS) & 1) ^ 1)) {
+          const int st = gc % NS;
+          const ChunkPos cp = chunk_pos(a, gc, nch);
+          mbar_expect_tx(&s.cb_full[st], kCBBytes);
+          tma_load_4d(s.cb[st][0], &tm_C, &s.cb_full[st], 0, cp.h, cp.t0, cp.b);
+          tma_load_4d(s.cb[st][1], &tm_C, &s.cb_full[st], 64, cp.h, cp.t0, cp.b);
+          tma_load_4d(s.cb[st][2], &tm_B, &s.cb_full[st], 0, cp.h, cp.t0, cp.b);
+          tma_load_4d(s.cb[st][3], &tm_B, &s.cb_full[st], 64, cp.h, cp.t0, cp.b);
+          ++gc;
+          moved = true;
+        }
+        if (gx < G && mbar_test(&s.x_empty[gx % NX], ((gx / NX) & 1) ^ 1)) {
+          const int xi = gx % NX;
+          const ChunkPos cp = chunk_pos(a, gx, nch);
+          mbar_expect_tx(&s.x_full[xi], kTileBytes);
+          tma_load_4d(s.xr[xi], &tm_x, &s.x_full[xi], 0, cp.h, cp.t0, cp.b);
+          // stream the following chunks into L2 so the loads above are L2 hits
+          for (int ahead = (gx == 0 ? 1 : kPrefetch); ahead <= kPrefetch; ++ahead) {
+            if (gx + ahead >= G) break;
+            const ChunkPos pf = chunk_pos(a, gx + ahead, nch);
+            tma_prefetch_l2_4d(&tm_C, 0, pf.h, pf.t0, pf.b);
+            tma_prefetch_l2_4d(&tm_C, 64, pf.h, pf.t0, pf.b);
+            tma_prefetch_l2_4d(&tm_B, 0, pf.h, pf.t0, pf.b);
+            tma_prefetch_l2_4d(&tm_B, 64, pf.h, pf.t0, pf.b);
+            tma_prefetch_l2_4d(&tm_x, 0, pf.h, pf.t0, pf.b);
+          }
+          ++gx;
+          moved = true;
+        }
+        if (moved) {
+          idle = 0;
+        } else {
+          if (++idle > kIdleLimit) {
+            atomicExch(&g_chunk_error, 1);
+            break;
+          }
+          __nanosleep(32);
         }
       }
     }
   } else if (warp == 1) {
+    // one MMA issuer thread polling two streams: A = dK(g), G(g+1), Y1(g+1) (fed by loads
+    // and the state warps), B = Y2(g) (gated by the mask). The tensor pipe runs MMAs in
+    // issue order, so G(g+2) issued after Y2(g) never overwrites G'(g) before it is read,
+    // and the commit after Y2(g) also covers Y1(g) (always issued before: Y2(g) waits for
+    // the state to read dK(g), which comes after Y1(g) in stream A).
     if (lane == 0) {
       constexpr uint32_t I_G = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t I_Y = idesc_bf16_f32(128, 64, false, true);
       constexpr uint32_t I_DK = idesc_bf16_f32(128, 64, true, true);
-      const uint32_t a_kb = smem_u32(s.kbuf);
-      auto stage_addr = [&](int st, int t) { return smem_u32(s.stage[st][t]); };
-      auto issue_g = [&](int g) -> bool {
-        const int st = g % NS, p = g & 1;
-        if (!wait_or_flag(&s.stage_full[st], (g / NS) & 1)) return false;
-        if (!wait_or_flag(&s.g_free[p], ((g >> 1) & 1) ^ 1)) return false;
-        tc_fence_after();
-        const uint32_t c0 = stage_addr(st, 0), b0 = stage_addr(st, 2);
+      const uint32_t a_kb = smem_u32(s.kbuf), a_xs = smem_u32(s.xs);
+      auto cb_addr = [&](int st, int t) { return smem_u32(s.cb[st][t]); };
+      // stream A position: chunk ga, step sa (0: G(ga), 1: Y1(ga), 2: dK(ga))
+      int ga = 0, sa = 0, gb = 0;
+      uint32_t idle = 0;
+      while (ga < G || gb < G) {
+        bool moved = false;
+        if (ga < G) {
+          const int st = ga % NS, p = ga & 1;
+          if (sa == 0) {
+            // G(ga) = C B^T, over G'(ga-2): Y2(ga-2) must already be issued
+            if (gb >= ga - 1 && mbar_test(&s.cb_full[st], (ga / NS) & 1)) {
+              tc_fence_after();
+              const uint32_t c0 = cb_addr(st, 0), b0 = cb_addr(st, 2);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
-          mma_ss(tbase + col_g(p), sdesc_sw128(c0 + koff, 16, 1024), sdesc_sw128(b0 + koff, 16, 1024), I_G, kk > 0);
-        }
-        mma_commit(&s.g_full[p]);
-        return true;
-      };
-      auto issue_y1 = [&](int g) -> bool {
-        const int st = g % NS, p = g & 1;
-        if (!wait_or_flag(&s.k_ready, g & 1)) return false;
-        if (!wait_or_flag(&s.y_free[p], ((g >> 1) & 1) ^ 1)) return false;
-        tc_fence_after();
-        const uint32_t c0 = stage_addr(st, 0);
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
+                mma_ss(tbase + col_g(p), sdesc_sw128(c0 + koff, 16, 1024), sdesc_sw128(b0 + koff, 16, 1024), I_G,
+                       kk > 0);
+              }
+              mma_commit(&s.g_full[p]);
+              sa = 1;
+              moved = true;
+            }
+          } else if (sa == 1) {
+            // Y1(ga) = C k_c^T
+            if (mbar_test(&s.k_ready, ga & 1) && mbar_test(&s.y_free[p], ((ga >> 1) & 1) ^ 1)) {
+              tc_fence_after();
+              const uint32_t c0 = cb_addr(st, 0);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
-          mma_ss(tbase + col_y1(p), sdesc_sw128(c0 + koff, 16, 1024),
-                 sdesc_sw128(a_kb + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
-        }
-        return true;
-      };
-      bool ok = G == 0 || (issue_g(0) && issue_y1(0));
-      for (int g = 0; g < G && ok; ++g) {
-        const int st = g % NS, p = g & 1;
-        if (g + 1 < G && !issue_g(g + 1)) break;
-        if (!wait_or_flag(&s.gp_ready[p], (g >> 1) & 1)) break;
-        tc_fence_after();
-        const uint32_t xa = stage_addr(st, 4), ba = stage_addr(st, 2), xsa = smem_u32(s.xs[p]);
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
+                mma_ss(tbase + col_y1(p), sdesc_sw128(c0 + koff, 16, 1024),
+                       sdesc_sw128(a_kb + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
+              }
+              sa = 2;
+              moved = true;
+            }
+          } else {
+            // dK(ga) = B^T (w o X) into the Y2/dK columns of parity p
+            if (mbar_test(&s.xs_full, ga & 1) && mbar_test(&s.y_free[p], ((ga >> 1) & 1) ^ 1)) {
+              tc_fence_after();
+              const uint32_t ba = cb_addr(st, 2);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          mma_ts(tbase + col_y2(p), tbase + col_g(p) + 8u * kk, sdesc_sw128(xa + (uint32_t)kk * 2048u, kTileBytes, 1024),
-                 I_Y, kk > 0);
-          mma_ss(tbase + col_dk(p), sdesc_sw128(ba + (uint32_t)kk * 2048u, kTileBytes, 1024),
-                 sdesc_sw128(xsa + (uint32_t)kk * 2048u, kTileBytes, 1024), I_DK, kk > 0);
+              for (int kk = 0; kk < 8; ++kk)
+                mma_ss(tbase + col_dk(p), sdesc_sw128(ba + (uint32_t)kk * 2048u, kTileBytes, 1024),
+                       sdesc_sw128(a_xs + (uint32_t)kk * 2048u, kTileBytes, 1024), I_DK, kk > 0);
+              mma_commit(&s.dk_full[p]);
+              mma_commit(&s.xs_empty);
+              mma_commit(&s.cb_empty[st]);  // last reader of this C/B stage
+              sa = 0;
+              ++ga;
+              moved = true;
+            }
+          }
         }
-        mma_commit(&s.y_full[p]);
-        mma_commit(&s.dk_full[p]);
-        mma_commit(&s.stage_empty[st]);
-        if (g + 1 < G && !issue_y1(g + 1)) break;
+        if (gb < G) {
+          const int p = gb & 1, xi = gb % NX;
+          // Y2(gb) = G' X after the mask, over dK(gb) once the state warps have read it
+          if (mbar_test(&s.gp_ready[p], (gb >> 1) & 1) && mbar_test(&s.dk_free[p], (gb >> 1) & 1) &&
+              mbar_test(&s.x_full[xi], (gb / NX) & 1)) {
+            tc_fence_after();
+            const uint32_t xa = smem_u32(s.xr[xi]);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              mma_ts(tbase + col_y2(p), tbase + col_g(p) + 8u * kk,
+                     sdesc_sw128(xa + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
+            mma_commit(&s.y_full[p]);
+            mma_commit(&s.x_empty[xi]);
+            ++gb;
+            moved = true;
+          }
+        }
+        if (moved) {
+          idle = 0;
+        } else {
+          if (++idle > kIdleLimit) {
+            atomicExch(&g_chunk_error, 1);
+            break;
+          }
+          __nanosleep(32);
+        }
       }
     }
   } else if (warp == 2 || warp == 3) {
@@ -740,6 +852,18 @@ bool siso_chunk_supported(const SisoParams& p, int xdt, int bcdt) {
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
   return major == 10;
+}
+
+int chunk_error_word(bool reset, int* out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_chunk_error, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_chunk_error, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("chunk error word: ") + cudaGetErrorString(e));
+  *out = v;
+  return M3_OK;
 }
 
 int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t s) {

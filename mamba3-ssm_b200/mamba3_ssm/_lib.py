@@ -63,6 +63,7 @@ _SIGS = {
     "m3_siso_step": ([ctypes.c_void_p] + [_P] * 14 + [ctypes.c_void_p], ctypes.c_int),
     "m3_mimo_step": ([ctypes.c_void_p] + [_P] * 16 + [ctypes.c_void_p], ctypes.c_int),
     "m3_rmsnorm": ([_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_void_p], ctypes.c_int),
+    "m3_device_timeouts": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
 }
 
 _lib = None
@@ -159,3 +160,13 @@ def check(rc, what):
 
 def stream_of(t):
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def device_timeouts(reset=False, device=None):
+    """Nonzero once a bounded inter-warp wait of a kernel on this device gave up (outputs
+    of that launch are invalid). Synchronises the device."""
+    lib = load()
+    v = ctypes.c_int(0)
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        check(lib.m3_device_timeouts(1 if reset else 0, ctypes.byref(v)), "m3_device_timeouts")
+    return v.value

@@ -18,6 +18,14 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
+@pytest.fixture(autouse=True)
+def _no_kernel_timeouts():
+    """Every bounded inter-warp wait of the warp-specialised kernels completed."""
+    yield
+    from mamba3_ssm import _lib as L
+    assert L.device_timeouts(reset=True) == 0
+
+
 def _t(g, k, dtype=None):
     a = torch.from_numpy(np.ascontiguousarray(g[k]))
     if dtype is None:
@@ -195,3 +203,27 @@ def test_siso_bf16_headdim64_dstate128_against_oracle(L):
     assert rel_err(y2.detach().double().cpu().numpy(), yo2) < 2e-2
     assert rel_err(h2.detach().double().cpu().numpy(), ho2) < 2e-2
     assert rel_err(b2.detach().double().cpu().numpy(), bo2) < 2e-2
+
+
+@pytest.mark.parametrize("case", ["strong_decay", "mixed_sign"])
+def test_siso_bf16_chunked_exact_mask_path(case):
+    """Decays outside the split-exponent range of the chunked kernel: strong per-step decay
+    (ADT down to -13, so 32-step column factors leave fp32) and isolated growth steps
+    (ADT up to +0.7). Those mask blocks take the per-element path; results must still
+    match the oracle."""
+    from mamba3_ssm import ssm_scan_siso
+    arrs, t = _inputs(7 if case == "strong_decay" else 8, 2, 700, 3, 64, 128, dtype=torch.bfloat16)
+    rng = np.random.default_rng(99)
+    if case == "strong_decay":
+        adt = -rng.uniform(0.0, 13.0, arrs["ADT"].shape)
+    else:
+        adt = -rng.uniform(0.0, 3.0, arrs["ADT"].shape)
+        grow = rng.random(adt.shape) < 0.05
+        adt[grow] = rng.uniform(0.0, 0.7, grow.sum())
+    t["ADT"] = torch.tensor(adt, dtype=torch.float32, device=DEV)
+    arrs["ADT"] = t["ADT"].double().cpu().numpy()
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D")
+    y = ssm_scan_siso(*[t[k] for k in keys])
+    yo, _, _ = O.siso_scan_fwd(*[arrs[k] for k in keys])
+    assert np.isfinite(y.float().cpu().numpy()).all()
+    assert rel_err(y.detach().double().cpu().numpy(), yo) < 2e-2
