@@ -24,8 +24,8 @@
 // chunk by chunk. Shared-memory buffers are split by lifetime so that the large C / B
 // tiles are released as soon as the early MMAs have read them:
 //   C, B (64 KB)  2-stage ring; read by G, Y1 and dK, freed after dK (issued early)
-//   X    (16 KB)  3-stage ring; read by the state warps (w o X) and by Y2 after the mask
-//   w o X, k_c^T  one buffer each
+//   X    (16 KB)  per chunk parity; read by the scalar warps (w o X) and by Y2 after the mask
+//   w o X (16 KB) per chunk parity;  k_c^T (16 KB) one buffer
 // Roles:
 //   warp 0      TMA producer (one thread polling the C/B ring and the X ring, plus the L2
 //               prefetch of later chunks)
@@ -34,12 +34,13 @@
 //               columns: per chunk parity G (128, G' packed in place), Y1 (64), Y2 (64,
 //               shared with dK, which the state warps read before Y2 is written))
 //   warps 2-3   per-chunk scalars (decay cumsum, mu, block factors, state weights) into a
-//               4-slot ring, even / odd chunks, running ahead of the consumers
+//               4-slot ring, even / odd chunks, running ahead of the consumers; then the
+//               chunk's w o X tile for dK (lane l owns rows l + 32 k, whose w it holds)
 //   warps 4-7   even chunks: G -> G' in TMEM (in place, packed bf16), then the epilogue
 //               y = e^{lambda} Y1 + Y2 -> global (bf16)
 //   warps 12-15 odd chunks: the same
-//   warps 8-11  state: w o X for dK, then k^T (fp32, registers) <- decay k^T + dK^T and
-//               its bf16 copy for the next Y1
+//   warps 8-11  state: k^T (fp32, registers) <- decay k^T + dK^T and its bf16 copy for
+//               the next Y1
 // All hand-offs are mbarriers; every wait is bounded (blocking waits by a poll count, the
 // polling producer and issuer by an idle count), and on a timeout the kernel records an
 // error and drains.
@@ -61,7 +62,6 @@ constexpr int kP = 64;
 constexpr int kD = 128;
 constexpr int kThreads = 512;
 constexpr int NS = 2;    // C/B stages
-constexpr int NX = 3;    // X stages
 constexpr int NSC = 4;   // scalar slots
 constexpr int kPrefetch = 3;  // chunks streamed into L2 ahead of their TMA load
 constexpr uint32_t kTmemCols = 512;
@@ -92,14 +92,14 @@ struct __align__(16) ScalSlot {
 
 struct __align__(1024) Smem {
   uint8_t cb[NS][4][kTileBytes];     // C(d 0-63), C(d 64-127), B(0-63), B(64-127)
-  uint8_t xr[NX][kTileBytes];        // x[t][p]
-  uint8_t xs[kTileBytes];            // (w o x)[t][p]
+  uint8_t xr[2][kTileBytes];         // x[t][p], per chunk parity
+  uint8_t xs[2][kTileBytes];         // (w o x)[t][p], per chunk parity
   uint8_t kbuf[kTileBytes];          // k_c^T[d][p]
   ScalSlot sc[NSC];
   float side_x[kP];                  // last row of a unit (for the final B*x)
   float side_b[kD];
-  uint64_t cb_full[NS], cb_empty[NS], x_full[NX], x_empty[NX];
-  uint64_t xs_full, xs_empty, k_ready;
+  uint64_t cb_full[NS], cb_empty[NS], x_full[2], x_empty[2];
+  uint64_t xs_full[2], xs_empty[2], k_ready;
   uint64_t g_full[2], gp_ready[2], y_full[2], y_free[2], dk_full[2], dk_free[2];
   uint64_t scal_full[NSC], scal_empty[NSC];
   uint32_t tmem_base;
@@ -158,6 +158,35 @@ __device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity) {
 
 __device__ __forceinline__ float ld_scal(const float* p, const Str3& s, int b, int t, int h) {
   return p[(int64_t)b * s.b + (int64_t)t * s.l + (int64_t)h * s.h];
+}
+
+
+// xs[t][:] = w_t x[t][:] for the rows t = lane + 32 k
+__device__ __forceinline__ void write_xs_rows(const uint8_t* xt, uint8_t* xs, const float (&wk)[4], int lane) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int t = lane + 32 * k;
+    const float wt = wk[k];
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xt + sw128_off(t, 8 * cc));
+      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[e]));
+        o[e] = pack_bf16(f.x * wt, f.y * wt);
+      }
+      *reinterpret_cast<uint4*>(xs + sw128_off(t, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+__device__ __noinline__ void stash_last_row(Smem& s, const uint8_t* xt, const uint8_t* bt0, const uint8_t* bt1, int i) {
+  for (int pp = 0; pp < kP; ++pp)
+    s.side_x[pp] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(xt + sw128_off(i, pp)));
+  for (int d = 0; d < kD; ++d)
+    s.side_b[d] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>((d < 64 ? bt0 : bt1) + sw128_off(i, d & 63)));
 }
 
 // ------------------------------------------------------------------------------------
@@ -266,6 +295,7 @@ __device__ void scalar_role(const ChunkArgs& a, Smem& s, int G, int nch, int lan
     const bool all_safe = amax <= 2.5f && pmax <= 0.6f;
     int flags = (cp.first ? 1 : 0) | (cp.last ? 2 : 0);
     ScalSlot& sl = s.sc[q];
+    float wk[4];
     if (!wait_or_flag(&s.scal_empty[q], ((g / NSC) & 1) ^ 1)) return;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -281,6 +311,7 @@ __device__ void scalar_role(const ChunkArgs& a, Smem& s, int G, int nch, int lan
       if (!cp.last) wj = exp2f(lamQ - ln[k]) * mu;
       else wj = (j < e) ? exp2f(lam_e - ln[k]) * mu : (j == e ? be[k] : 0.f);
       sl.w[j] = wj;
+      wk[k] = wj;
     }
     if (all_safe) {
       flags |= 0xF0;
@@ -321,6 +352,18 @@ __device__ void scalar_role(const ChunkArgs& a, Smem& s, int G, int nch, int lan
       sl.flags = flags;
     }
     mbar_arrive(&s.scal_full[q]);
+    // (w o x) rows lane + 32 k of this chunk, for dK(g)
+    const int p = g & 1;
+    if (!wait_or_flag(&s.x_full[p], (g >> 1) & 1)) return;
+    if (!wait_or_flag(&s.xs_empty[p], ((g >> 1) & 1) ^ 1)) return;
+    write_xs_rows(s.xr[p], s.xs[p], wk, lane);
+    if (cp.last && a.bx_last && (e & 31) == lane) {
+      // the C/B stage stays valid until dK(g), which waits for xs_full below
+      const int st = g % NS;
+      stash_last_row(s, s.xr[p], s.cb[st][2], s.cb[st][3], e);
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(&s.xs_full[p]);
   }
 }
 
@@ -497,12 +540,6 @@ __device__ __forceinline__ void store_final(const ChunkArgs& a, const Smem& s, i
   }
 }
 
-__device__ __noinline__ void stash_last_row(Smem& s, const uint8_t* xt, const uint8_t* bt0, const uint8_t* bt1, int i) {
-  for (int pp = 0; pp < kP; ++pp)
-    s.side_x[pp] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(xt + sw128_off(i, pp)));
-  for (int d = 0; d < kD; ++d)
-    s.side_b[d] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>((d < 64 ? bt0 : bt1) + sw128_off(i, d & 63)));
-}
 
 // k = dec * k + dK(parity p), read in quarters
 __device__ __forceinline__ void add_dk(uint32_t tbase, int warp, int p, float dec, float (&k)[kP]) {
@@ -527,12 +564,17 @@ __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, i
       if (!wait_or_flag(&s.dk_full[pp], ((g - 1) >> 1) & 1)) return;
       tc_fence_after();
       add_dk(tbase, warp, pp, prev_dec, k);
+      if (prev_last && (a.h_last || a.bx_last)) {
+        // the scalar lane that stashed the last row released it with xs_full(g-1), whose
+        // phase cannot advance before this thread frees the dK columns below
+        if (!wait_or_flag(&s.xs_full[pp], ((g - 1) >> 1) & 1)) return;
+        store_final(a, s, prev_b, prev_h, d, k);
+      }
       tc_fence_before();
       mbar_arrive(&s.dk_free[pp]);
-      if (prev_last && (a.h_last || a.bx_last)) store_final(a, s, prev_b, prev_h, d, k);
     }
     if (g == G) break;
-    const int q = g % NSC, xi = g % NX;
+    const int q = g % NSC;
     const ChunkPos cp = chunk_pos(a, g, nch);
     if (!wait_or_flag(&s.scal_full[q], (g / NSC) & 1)) return;
     const ScalSlot& sl = s.sc[q];
@@ -548,36 +590,6 @@ __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, i
     write_kbuf(s, d, k);
     fence_proxy_async_smem();
     mbar_arrive(&s.k_ready);
-    // (3) (w o x) row t = d of this chunk, for dK(g)
-    if (!wait_or_flag(&s.x_full[xi], (g / NX) & 1)) return;
-    if (!wait_or_flag(&s.xs_empty, (g & 1) ^ 1)) return;
-    {
-      const float wi = sl.w[d];
-      const uint8_t* xt = s.xr[xi];
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xt + sw128_off(d, 8 * cc));
-        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[e]));
-          o[e] = pack_bf16(f.x * wi, f.y * wi);
-        }
-        *reinterpret_cast<uint4*>(s.xs + sw128_off(d, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-      // the C/B stage stays valid until dK(g), which waits for xs_full below; the other
-      // state threads read the stash after dK(g) (named barrier of warps 8-11)
-      if (cp.last && a.bx_last) {
-        if (d == sl.n - 1) {
-          const int st = g % NS;
-          stash_last_row(s, xt, s.cb[st][2], s.cb[st][3], d);
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      }
-    }
-    fence_proxy_async_smem();
-    mbar_arrive(&s.xs_full);
     prev_dec = sl.decay_end;
     prev_last = cp.last;
     prev_b = cp.b;
@@ -603,12 +615,12 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
       mbar_init(&s.cb_full[i], 1);
       mbar_init(&s.cb_empty[i], 1);
     }
-    for (int i = 0; i < NX; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s.x_full[i], 1);
       mbar_init(&s.x_empty[i], 1);
+      mbar_init(&s.xs_full[i], 32);
+      mbar_init(&s.xs_empty[i], 1);
     }
-    mbar_init(&s.xs_full, 128);
-    mbar_init(&s.xs_empty, 1);
     mbar_init(&s.k_ready, 128);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.g_full[i], 1);
@@ -655,8 +667,8 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
           ++gc;
           moved = true;
         }
-        if (gx < G && mbar_test(&s.x_empty[gx % NX], ((gx / NX) & 1) ^ 1)) {
-          const int xi = gx % NX;
+        if (gx < G && mbar_test(&s.x_empty[gx & 1], ((gx >> 1) & 1) ^ 1)) {
+          const int xi = gx & 1;
           const ChunkPos cp = chunk_pos(a, gx, nch);
           mbar_expect_tx(&s.x_full[xi], kTileBytes);
           tma_load_4d(s.xr[xi], &tm_x, &s.x_full[xi], 0, cp.h, cp.t0, cp.b);
@@ -694,7 +706,7 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
       constexpr uint32_t I_G = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t I_Y = idesc_bf16_f32(128, 64, false, true);
       constexpr uint32_t I_DK = idesc_bf16_f32(128, 64, true, true);
-      const uint32_t a_kb = smem_u32(s.kbuf), a_xs = smem_u32(s.xs);
+      const uint32_t a_kb = smem_u32(s.kbuf);
       auto cb_addr = [&](int st, int t) { return smem_u32(s.cb[st][t]); };
       // stream A position: chunk ga, step sa (0: G(ga), 1: Y1(ga), 2: dK(ga))
       int ga = 0, sa = 0, gb = 0;
@@ -734,15 +746,15 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
             }
           } else {
             // dK(ga) = B^T (w o X) into the Y2/dK columns of parity p
-            if (mbar_test(&s.xs_full, ga & 1) && mbar_test(&s.y_free[p], ((ga >> 1) & 1) ^ 1)) {
+            if (mbar_test(&s.xs_full[p], (ga >> 1) & 1) && mbar_test(&s.y_free[p], ((ga >> 1) & 1) ^ 1)) {
               tc_fence_after();
-              const uint32_t ba = cb_addr(st, 2);
+              const uint32_t ba = cb_addr(st, 2), xsa = smem_u32(s.xs[p]);
 #pragma unroll
               for (int kk = 0; kk < 8; ++kk)
                 mma_ss(tbase + col_dk(p), sdesc_sw128(ba + (uint32_t)kk * 2048u, kTileBytes, 1024),
-                       sdesc_sw128(a_xs + (uint32_t)kk * 2048u, kTileBytes, 1024), I_DK, kk > 0);
+                       sdesc_sw128(xsa + (uint32_t)kk * 2048u, kTileBytes, 1024), I_DK, kk > 0);
               mma_commit(&s.dk_full[p]);
-              mma_commit(&s.xs_empty);
+              mma_commit(&s.xs_empty[p]);
               mma_commit(&s.cb_empty[st]);  // last reader of this C/B stage
               sa = 0;
               ++ga;
@@ -751,10 +763,10 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
           }
         }
         if (gb < G) {
-          const int p = gb & 1, xi = gb % NX;
+          const int p = gb & 1, xi = p;
           // Y2(gb) = G' X after the mask, over dK(gb) once the state warps have read it
           if (mbar_test(&s.gp_ready[p], (gb >> 1) & 1) && mbar_test(&s.dk_free[p], (gb >> 1) & 1) &&
-              mbar_test(&s.x_full[xi], (gb / NX) & 1)) {
+              mbar_test(&s.x_full[xi], (gb >> 1) & 1)) {
             tc_fence_after();
             const uint32_t xa = smem_u32(s.xr[xi]);
 #pragma unroll
