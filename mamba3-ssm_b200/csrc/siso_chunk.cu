@@ -29,10 +29,10 @@
 // Roles:
 //   warp 0      TMA producer (one thread polling the C/B ring and the X ring, plus the L2
 //               prefetch of later chunks)
-//   warp 1      tcgen05 MMA issuer (one thread polling two streams: G, Y1, dK fed by the
-//               loads and the state warps; Y2 gated by the mask) and TMEM owner (512
-//               columns: per chunk parity G (128, G' packed in place), Y1 (64), Y2 (64,
-//               shared with dK, which the state warps read before Y2 is written))
+//   warp 1      tcgen05 MMA issuer (one thread polling three streams: G fed by the loads;
+//               dK and Y1 fed by the scalar and state warps; Y2 gated by the mask) and TMEM
+//               owner (512 columns: per chunk parity G (128, G' packed in place) and Y2
+//               (64); one Y1 (64) and one dK (64))
 //   warps 2-3   per-chunk scalars (decay cumsum, mu, block factors, state weights) into a
 //               4-slot ring, even / odd chunks, running ahead of the consumers; then the
 //               chunk's w o X tile for dK (lane l owns rows l + 32 k, whose w it holds)
@@ -71,11 +71,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kSafeExp2 = 120.f;
 constexpr uint32_t kIdleLimit = 1u << 22;  // idle polls (~32 ns apart) before the producers give up
 
-// TMEM columns of chunk parity p: G (128; G' packed into its first 64), Y1 (64), Y2 / dK (64).
-__device__ __forceinline__ uint32_t col_g(int p) { return 256u * p; }
-__device__ __forceinline__ uint32_t col_y1(int p) { return 256u * p + 128u; }
-__device__ __forceinline__ uint32_t col_y2(int p) { return 256u * p + 192u; }
-__device__ __forceinline__ uint32_t col_dk(int p) { return 256u * p + 192u; }
+// TMEM columns: per chunk parity p G (128; G' packed into its first 64) and Y2 (64); one
+// Y1 (64) and one dK (64), each consumed before the next chunk's is written.
+__device__ __forceinline__ uint32_t col_g(int p) { return 128u * p; }
+__device__ __forceinline__ uint32_t col_y2(int p) { return 256u + 64u * p; }
+constexpr uint32_t kColY1 = 384u;
+constexpr uint32_t kColDK = 448u;
 
 struct __align__(16) ScalSlot {
   float colf[Q];      // e^{lambda_{32b+1} - lambda_{j+1}} mu_j (read as float4)
@@ -100,7 +101,9 @@ struct __align__(1024) Smem {
   float side_b[kD];
   uint64_t cb_full[NS], cb_empty[NS], x_full[2], x_empty[2];
   uint64_t xs_full[2], xs_empty[2], k_ready;
-  uint64_t g_full[2], gp_ready[2], y_full[2], y_free[2], dk_full[2], dk_free[2];
+  uint64_t g_full[2], gp_ready[2], y_full[2], y2_free[2];
+  uint64_t y1_full[2], y1_free, dk_full, dk_free;  // y1_full per parity: its two waiters
+                                                   // are a chunk apart
   uint64_t scal_full[NSC], scal_empty[NSC];
   uint32_t tmem_base;
 };
@@ -357,10 +360,15 @@ __device__ void scalar_role(const ChunkArgs& a, Smem& s, int G, int nch, int lan
     if (!wait_or_flag(&s.x_full[p], (g >> 1) & 1)) return;
     if (!wait_or_flag(&s.xs_empty[p], ((g >> 1) & 1) ^ 1)) return;
     write_xs_rows(s.xr[p], s.xs[p], wk, lane);
-    if (cp.last && a.bx_last && (e & 31) == lane) {
-      // the C/B stage stays valid until dK(g), which waits for xs_full below
-      const int st = g % NS;
-      stash_last_row(s, s.xr[p], s.cb[st][2], s.cb[st][3], e);
+    if (cp.last && a.bx_last) {
+      // the C/B stage stays valid until Y1(g), which waits for the state warps; they read
+      // the stash after named barrier 2 + p (160 threads: this warp arrives, they sync)
+      if ((e & 31) == lane) {
+        const int st = g % NS;
+        stash_last_row(s, s.xr[p], s.cb[st][2], s.cb[st][3], e);
+      }
+      __syncwarp();
+      asm volatile("bar.arrive %0, 160;" ::"r"(2 + p) : "memory");
     }
     fence_proxy_async_smem();
     mbar_arrive(&s.xs_full[p]);
@@ -430,12 +438,13 @@ __device__ __forceinline__ void epilogue(const ChunkArgs& a, Smem& s, uint32_t t
 #pragma unroll
   for (int qt = 0; qt < 4; ++qt) {
     uint32_t y1[16], y2[16];
-    tmem_ld16(lane_addr(tbase, warp, col_y1(p) + 16 * qt), y1);
+    tmem_ld16(lane_addr(tbase, warp, kColY1 + 16 * qt), y1);
     tmem_ld16(lane_addr(tbase, warp, col_y2(p) + 16 * qt), y2);
     tmem_wait_ld();
     if (qt == 3) {
       tc_fence_before();
-      mbar_arrive(&s.y_free[p]);
+      mbar_arrive(&s.y1_free);
+      mbar_arrive(&s.y2_free[p]);
     }
     uint32_t outp[8];
 #pragma unroll
@@ -494,8 +503,9 @@ __device__ void mask_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, in
     tmem_wait_st();
     tc_fence_before();
     mbar_arrive(&s.gp_ready[p]);
-    // this chunk's outputs (Y1 and Y2 complete at one commit point)
+    // this chunk's outputs
     if (!wait_or_flag(&s.y_full[p], (g >> 1) & 1)) return;
+    if (!wait_or_flag(&s.y1_full[p], (g >> 1) & 1)) return;
     tc_fence_after();
     epilogue(a, s, tbase, g, nch, warp, i);
     mbar_arrive(&s.scal_empty[q]);
@@ -541,12 +551,12 @@ __device__ __forceinline__ void store_final(const ChunkArgs& a, const Smem& s, i
 }
 
 
-// k = dec * k + dK(parity p), read in quarters
-__device__ __forceinline__ void add_dk(uint32_t tbase, int warp, int p, float dec, float (&k)[kP]) {
+// k = dec * k + dK, read in quarters
+__device__ __forceinline__ void add_dk(uint32_t tbase, int warp, float dec, float (&k)[kP]) {
 #pragma unroll
   for (int qt = 0; qt < 4; ++qt) {
     uint32_t r[16];
-    tmem_ld16(lane_addr(tbase, warp, col_dk(p) + 16 * qt), r);
+    tmem_ld16(lane_addr(tbase, warp, kColDK + 16 * qt), r);
     tmem_wait_ld();
 #pragma unroll
     for (int e = 0; e < 16; ++e) k[16 * qt + e] = fmaf(dec, k[16 * qt + e], __uint_as_float(r[e]));
@@ -561,24 +571,22 @@ __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, i
     // (1) fold dK(g-1) into the carried state (or finish the unit that g-1 closed)
     if (g > 0) {
       const int pp = (g - 1) & 1;
-      if (!wait_or_flag(&s.dk_full[pp], ((g - 1) >> 1) & 1)) return;
+      if (!wait_or_flag(&s.dk_full, (g - 1) & 1)) return;
       tc_fence_after();
-      add_dk(tbase, warp, pp, prev_dec, k);
+      add_dk(tbase, warp, prev_dec, k);
       if (prev_last && (a.h_last || a.bx_last)) {
-        // the scalar lane that stashed the last row released it with xs_full(g-1), whose
-        // phase cannot advance before this thread frees the dK columns below
-        if (!wait_or_flag(&s.xs_full[pp], ((g - 1) >> 1) & 1)) return;
+        if (a.bx_last) asm volatile("bar.sync %0, 160;" ::"r"(2 + pp) : "memory");  // the stash of g-1
         store_final(a, s, prev_b, prev_h, d, k);
       }
       tc_fence_before();
-      mbar_arrive(&s.dk_free[pp]);
+      mbar_arrive(&s.dk_free);
     }
     if (g == G) break;
     const int q = g % NSC;
     const ChunkPos cp = chunk_pos(a, g, nch);
     if (!wait_or_flag(&s.scal_full[q], (g / NSC) & 1)) return;
     const ScalSlot& sl = s.sc[q];
-    // (2) k_c for this chunk -> kbuf (its previous reader, Y1(g-1), finished before dK(g-1))
+    // (2) k_c for this chunk -> kbuf
     if (cp.first) {
       if (a.h0 || a.bx0) {
         init_state(a, cp, sl.a0, sl.g0, d, k);
@@ -587,6 +595,8 @@ __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, i
         for (int pp = 0; pp < kP; ++pp) k[pp] = 0.f;
       }
     }
+    // kbuf's previous reader is Y1(g-1)
+    if (g > 0 && !wait_or_flag(&s.y1_full[(g - 1) & 1], ((g - 1) >> 1) & 1)) return;
     write_kbuf(s, d, k);
     fence_proxy_async_smem();
     mbar_arrive(&s.k_ready);
@@ -622,13 +632,16 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
       mbar_init(&s.xs_empty[i], 1);
     }
     mbar_init(&s.k_ready, 128);
+    mbar_init(&s.y1_full[0], 1);
+    mbar_init(&s.y1_full[1], 1);
+    mbar_init(&s.y1_free, 128);
+    mbar_init(&s.dk_full, 1);
+    mbar_init(&s.dk_free, 128);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.g_full[i], 1);
       mbar_init(&s.gp_ready[i], 128);
       mbar_init(&s.y_full[i], 1);
-      mbar_init(&s.y_free[i], 128);
-      mbar_init(&s.dk_full[i], 1);
-      mbar_init(&s.dk_free[i], 128);
+      mbar_init(&s.y2_free[i], 128);
     }
     for (int i = 0; i < NSC; ++i) {
       mbar_init(&s.scal_full[i], 32);
@@ -697,76 +710,76 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
       }
     }
   } else if (warp == 1) {
-    // one MMA issuer thread polling two streams: A = dK(g), G(g+1), Y1(g+1) (fed by loads
-    // and the state warps), B = Y2(g) (gated by the mask). The tensor pipe runs MMAs in
-    // issue order, so G(g+2) issued after Y2(g) never overwrites G'(g) before it is read,
-    // and the commit after Y2(g) also covers Y1(g) (always issued before: Y2(g) waits for
-    // the state to read dK(g), which comes after Y1(g) in stream A).
+    // one MMA issuer thread polling three streams, each in chunk order:
+    //   G  : G(c) = C B^T                 needs the C/B stage, and Y2(c-2) issued (G'(c-2)
+    //                                     read: the tensor pipe runs MMAs in issue order)
+    //   K  : dK(c) = B^T (w o X), then Y1(c) = C k_c^T
+    //        dK(c) needs w o X(c), the dK columns read (dK(c-1) consumed) and G(c) issued;
+    //        Y1(c) needs k_c and the Y1 columns read (epilogue of c-1); Y1(c) is the last
+    //        reader of the stage, so its commit frees it
+    //   Y2 : Y2(c) = G' X                 needs the mask of c, X(c) and w o X(c), the Y2
+    //                                     columns of c-2 read
     if (lane == 0) {
       constexpr uint32_t I_G = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t I_Y = idesc_bf16_f32(128, 64, false, true);
       constexpr uint32_t I_DK = idesc_bf16_f32(128, 64, true, true);
       const uint32_t a_kb = smem_u32(s.kbuf);
       auto cb_addr = [&](int st, int t) { return smem_u32(s.cb[st][t]); };
-      // stream A position: chunk ga, step sa (0: G(ga), 1: Y1(ga), 2: dK(ga))
-      int ga = 0, sa = 0, gb = 0;
+      int cg = 0, ck = 0, sk = 0, gb = 0;
       uint32_t idle = 0;
-      while (ga < G || gb < G) {
+      while (cg < G || ck < G || gb < G) {
         bool moved = false;
-        if (ga < G) {
-          const int st = ga % NS, p = ga & 1;
-          if (sa == 0) {
-            // G(ga) = C B^T, over G'(ga-2): Y2(ga-2) must already be issued
-            if (gb >= ga - 1 && mbar_test(&s.cb_full[st], (ga / NS) & 1)) {
-              tc_fence_after();
-              const uint32_t c0 = cb_addr(st, 0), b0 = cb_addr(st, 2);
+        if (cg < G && gb >= cg - 1 && mbar_test(&s.cb_full[cg % NS], (cg / NS) & 1)) {
+          const int st = cg % NS, p = cg & 1;
+          tc_fence_after();
+          const uint32_t c0 = cb_addr(st, 0), b0 = cb_addr(st, 2);
 #pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
-                mma_ss(tbase + col_g(p), sdesc_sw128(c0 + koff, 16, 1024), sdesc_sw128(b0 + koff, 16, 1024), I_G,
-                       kk > 0);
-              }
-              mma_commit(&s.g_full[p]);
-              sa = 1;
-              moved = true;
-            }
-          } else if (sa == 1) {
-            // Y1(ga) = C k_c^T
-            if (mbar_test(&s.k_ready, ga & 1) && mbar_test(&s.y_free[p], ((ga >> 1) & 1) ^ 1)) {
-              tc_fence_after();
-              const uint32_t c0 = cb_addr(st, 0);
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
-                mma_ss(tbase + col_y1(p), sdesc_sw128(c0 + koff, 16, 1024),
-                       sdesc_sw128(a_kb + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
-              }
-              sa = 2;
-              moved = true;
-            }
-          } else {
-            // dK(ga) = B^T (w o X) into the Y2/dK columns of parity p
-            if (mbar_test(&s.xs_full[p], (ga >> 1) & 1) && mbar_test(&s.y_free[p], ((ga >> 1) & 1) ^ 1)) {
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
+            mma_ss(tbase + col_g(p), sdesc_sw128(c0 + koff, 16, 1024), sdesc_sw128(b0 + koff, 16, 1024), I_G,
+                   kk > 0);
+          }
+          mma_commit(&s.g_full[p]);
+          ++cg;
+          moved = true;
+        }
+        if (ck < G) {
+          const int st = ck % NS, p = ck & 1;
+          if (sk == 0) {
+            if (cg > ck && mbar_test(&s.xs_full[p], (ck >> 1) & 1) && mbar_test(&s.dk_free, (ck & 1) ^ 1)) {
               tc_fence_after();
               const uint32_t ba = cb_addr(st, 2), xsa = smem_u32(s.xs[p]);
 #pragma unroll
               for (int kk = 0; kk < 8; ++kk)
-                mma_ss(tbase + col_dk(p), sdesc_sw128(ba + (uint32_t)kk * 2048u, kTileBytes, 1024),
+                mma_ss(tbase + kColDK, sdesc_sw128(ba + (uint32_t)kk * 2048u, kTileBytes, 1024),
                        sdesc_sw128(xsa + (uint32_t)kk * 2048u, kTileBytes, 1024), I_DK, kk > 0);
-              mma_commit(&s.dk_full[p]);
+              mma_commit(&s.dk_full);
               mma_commit(&s.xs_empty[p]);
-              mma_commit(&s.cb_empty[st]);  // last reader of this C/B stage
-              sa = 0;
-              ++ga;
+              sk = 1;
               moved = true;
             }
+          } else if (mbar_test(&s.k_ready, ck & 1) && mbar_test(&s.y1_free, (ck & 1) ^ 1)) {
+            tc_fence_after();
+            const uint32_t c0 = cb_addr(st, 0);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
+              mma_ss(tbase + kColY1, sdesc_sw128(c0 + koff, 16, 1024),
+                     sdesc_sw128(a_kb + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
+            }
+            mma_commit(&s.y1_full[p]);
+            mma_commit(&s.cb_empty[st]);  // last reader of this C/B stage
+            sk = 0;
+            ++ck;
+            moved = true;
           }
         }
         if (gb < G) {
           const int p = gb & 1, xi = p;
-          // Y2(gb) = G' X after the mask, over dK(gb) once the state warps have read it
-          if (mbar_test(&s.gp_ready[p], (gb >> 1) & 1) && mbar_test(&s.dk_free[p], (gb >> 1) & 1) &&
-              mbar_test(&s.x_full[xi], (gb >> 1) & 1)) {
+          // (w o X(gb) written implies the scalar warp is past its wait on X(gb), so X(gb+2)
+          // cannot land in this slot before that wait)
+          if (mbar_test(&s.gp_ready[p], (gb >> 1) & 1) && mbar_test(&s.x_full[xi], (gb >> 1) & 1) &&
+              mbar_test(&s.xs_full[p], (gb >> 1) & 1) && mbar_test(&s.y2_free[p], ((gb >> 1) & 1) ^ 1)) {
             tc_fence_after();
             const uint32_t xa = smem_u32(s.xr[xi]);
 #pragma unroll
