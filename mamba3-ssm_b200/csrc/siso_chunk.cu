@@ -63,7 +63,7 @@ constexpr int kD = 128;
 constexpr int kThreads = 512;
 constexpr int NS = 2;    // C/B stages
 constexpr int NSC = 4;   // scalar slots
-constexpr int kPrefetch = 3;  // chunks streamed into L2 ahead of their TMA load
+constexpr int kPrefetch = 2;  // chunks streamed into L2 ahead of their TMA load
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTileBytes = Q * 64 * 2;       // one SW128 tile: 128 rows x 128 B
 constexpr uint32_t kCBBytes = 4 * kTileBytes;     // C(2) + B(2)
