@@ -383,6 +383,95 @@ def measure_decode(dev, steps=48, batch=256, prefill=16):
                     "MambaLMHeadModel.step"}
 
 
+def _time(fn, steps, warm=2):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def measure_mimo(dev, steps=10):
+    """MIMO at the layer configuration the reference's tests use for bf16 MIMO (d_model 256,
+    H=16, P=32, D=64, R=4, batch 8 x 2048 tokens): the raw op ssm_scan_mimo forward on the
+    layer's operand types (x bf16, B/C fp32) with its HBM roofline, and Mamba3.forward +
+    backward through the whole layer (random-init weights, synthetic activations)."""
+    from mamba3_ssm import Mamba3, ssm_scan_mimo
+    torch.manual_seed(0)
+    Bn, L, H, P, D, R = 8, 2048, 16, 32, 64, 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)
+    x = torch.randn(Bn, L, H, P, device=dev, generator=g).to(torch.bfloat16)
+    Bm = torch.randn(Bn, L, R, H, D, device=dev, generator=g)
+    Cm = torch.randn(Bn, L, R, H, D, device=dev, generator=g)
+    dt = F.softplus(torch.randn(Bn, L, H, device=dev, generator=g) * 0.5 - 3.0).clamp(1e-3, 0.1)
+    ADT = (-torch.exp(torch.rand(H, device=dev, generator=g) * math.log(16.0)) * dt).contiguous()
+    trap = torch.randn(Bn, L, H, device=dev, generator=g)
+    Dw = torch.ones(H, device=dev)
+    mx = torch.randn(H, R, P, device=dev, generator=g) * 0.3 + 0.25
+    mo = torch.randn(H, R, P, device=dev, generator=g) * 0.3 + 0.25
+    with torch.no_grad():
+        op_ms = _time(lambda: ssm_scan_mimo(x, Bm, Cm, ADT, dt, trap, Dw, mx, mo), steps)
+    op_bytes = Bn * L * H * (2 * 2 * P + 2 * 4 * R * D + 12)
+    peak = peaks()[0]
+    layer = Mamba3(d_model=256, d_state=64, expand=2, headdim=32, is_mimo=True, mimo_rank=4,
+                   device=dev, dtype=torch.bfloat16)
+    u = torch.randn(Bn, L, 256, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(Bn, L, 256, device=dev, generator=g).to(torch.bfloat16)
+
+    def fb():
+        for p_ in layer.parameters():
+            p_.grad = None
+        u.grad = None
+        layer(u).backward(dy)
+    fb_ms = _time(fb, steps)
+    with torch.no_grad():
+        f_ms = _time(lambda: layer(u), steps)
+    del layer, u, dy, x, Bm, Cm
+    torch.cuda.empty_cache()
+    tok = Bn * L
+    return {"op_fwd": {"ms": op_ms, "tokens_per_s": tok / (op_ms / 1e3), "bytes": op_bytes,
+                       "achieved_gbs": op_bytes / (op_ms / 1e3) / 1e9, "frac_hbm": op_bytes / (op_ms / 1e3) / 1e9 / peak,
+                       "what": "ssm_scan_mimo forward, x bf16, B/C fp32 (B,L,R,H,D), R=4 H=16 P=32 D=64, 8 x 2048"},
+            "layer_fwd": {"ms": f_ms, "tokens_per_s": tok / (f_ms / 1e3)},
+            "layer_fwd_bwd": {"ms": fb_ms, "tokens_per_s": tok / (fb_ms / 1e3)},
+            "what": "Mamba3 MIMO layer (d_model 256, R=4, bf16), batch 8 x 2048 tokens"}
+
+
+def measure_lm_forward(dev, steps=5):
+    """MambaLMHeadModel forward at the SISO LM preset (d_model 1024, 16 layers, H=32, P=64,
+    D=64, vocab 50000), bf16, batch 32 x 512 tokens, random-init weights, uniform ids;
+    reported against the measured bf16 tensor peak (the forward is GEMM-bound)."""
+    from mamba3_ssm import MambaConfig, MambaLMHeadModel
+    torch.manual_seed(0)
+    cfg = MambaConfig(d_model=1024, n_layer=16, vocab_size=50000,
+                      ssm_cfg=dict(d_state=64, expand=2, headdim=64))
+    model = MambaLMHeadModel(cfg, device=dev, dtype=torch.bfloat16).eval()
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    ids = torch.randint(0, 50000, (32, 512), device=dev, generator=g)
+    with torch.no_grad():
+        ms = _time(lambda: model(ids), steps)
+    d_in_proj = model.layers[0].mixer.in_proj.weight.shape[0]
+    flops_tok = 2 * 16 * (1024 * d_in_proj + 2048 * 1024) + 2 * 1024 * model.vocab_size
+    tflops = flops_tok * ids.numel() / (ms / 1e3) / 1e12
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpk = float(json.load(f).get("bf16_tflops", 1590.0))
+    except (OSError, ValueError):
+        tpk = 1590.0
+    del model
+    torch.cuda.empty_cache()
+    return {"ms": ms, "tokens_per_s": ids.numel() / (ms / 1e3), "gemm_tflops": tflops,
+            "frac_bf16_peak": tflops / tpk, "flops_per_token": flops_tok,
+            "what": "MambaLMHeadModel.forward, SISO preset d_model 1024 x 16 layers, bf16, 32 x 512 tokens"}
+
+
 # ----------------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
@@ -512,6 +601,8 @@ def main():
         del x, Bm, Cm, ADT, DT, trap, Dw, y
         torch.cuda.empty_cache()
         extra["decode"] = measure_decode(dev)
+        extra["mimo"] = measure_mimo(dev)
+        extra["lm_forward"] = measure_lm_forward(dev)
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

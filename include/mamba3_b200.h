@@ -148,6 +148,20 @@ int m3_mimo_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
 
 /* MIMO scan, backward (gradients of ops.py:226-240). dD, dmimo_x, dmimo_o are f32 and
  * overwritten. */
+/* Chunk-parallel MIMO forward: same operands and results as m3_mimo_scan_fwd, plus a
+ * caller-provided device workspace (16-byte aligned) of at least
+ * m3_mimo_scan_fwd_workspace_size(...) bytes (per (b, h, 64-step chunk) one state and one
+ * decay: 4 * batch * nheads * ceil(seqlen / 64) * (dstate + 1) bytes). The time axis is cut
+ * into 64-step chunks processed in parallel (local states, a carry pass, then the outputs),
+ * instead of one serial walk per (b, h). Replaces the same reference path as
+ * m3_mimo_scan_fwd (cuda_backend.py:419-463, ops.py:226-240). */
+size_t m3_mimo_scan_fwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t dstate);
+int m3_mimo_scan_fwd_ws(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                        const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D,
+                        const m3_tensor* mimo_x, const m3_tensor* mimo_o, const m3_tensor* h0,
+                        const m3_tensor* bx0, m3_tensor* y, m3_tensor* h_last, m3_tensor* bx_last,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 size_t m3_mimo_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads,
                                        int64_t headdim, int64_t dstate, int64_t rank);
 int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,

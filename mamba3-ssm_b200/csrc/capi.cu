@@ -367,6 +367,43 @@ int m3_mimo_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
   return launch_mimo(p, x->dtype, B->dtype, false, s);
 }
 
+size_t m3_mimo_scan_fwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t dstate) {
+  if (batch < 0 || seqlen < 0 || nheads < 0 || dstate < 0) return 0;
+  return sizeof(float) * mimo_fwd_workspace_floats(batch, seqlen, nheads, dstate);
+}
+
+int m3_mimo_scan_fwd_ws(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                        const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* mimo_x,
+                        const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, m3_tensor* y,
+                        m3_tensor* h_last, m3_tensor* bx_last, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  MimoParams p{};
+  int64_t d[6];
+  M3_TRY(fill_mimo(p, x, B, C, ADT, DT, trap, D, mimo_x, mimo_o, h0, bx0, d));
+  const int64_t xs[4] = {d[0], d[1], d[2], d[3]}, st[3] = {d[0], d[2], d[4]};
+  const bool empty = d[0] * d[1] * d[2] * d[3] == 0;
+  M3_TRY(check(y, "y", 4, xs, 1u << x->dtype, false, false, !empty));
+  M3_TRY(check(h_last, "h_last", 3, st, kF32, true, true, false));
+  M3_TRY(check(bx_last, "bx_last", 3, st, kF32, true, true, false));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (d[0] * d[2] * d[4] == 0) return M3_OK;
+  if (d[1] == 0 || d[3] == 0) {
+    const size_t bytes = sizeof(float) * d[0] * d[2] * d[4];
+    if (d[1] == 0) {
+      M3_TRY(copy_or_zero(fptr<void>(h_last), fptr<void>(h0), bytes, s, "h_last"));
+      return copy_or_zero(fptr<void>(bx_last), fptr<void>(bx0), bytes, s, "bx_last");
+    }
+  }
+  const size_t need = sizeof(float) * mimo_fwd_workspace_floats(d[0], d[1], d[2], d[4]);
+  if (!workspace || workspace_bytes < need)
+    return fail(M3_ERR_WORKSPACE, "workspace: need " + std::to_string(need) + " bytes");
+  if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0) return fail(M3_ERR_INVALID_ARGUMENT, "workspace: not 16-byte aligned");
+  M3_TRY(check_device_ptr(workspace, "workspace"));
+  p.y = y->data; p.sy = s3(y);
+  p.h_last = fptr<float>(h_last); p.bx_last = fptr<float>(bx_last);
+  return launch_mimo_fwd_chunked(p, x->dtype, B->dtype, reinterpret_cast<float*>(workspace), s);
+}
+
 size_t m3_mimo_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
                                        int64_t dstate, int64_t rank) {
   return sizeof(float) * mimo_bwd_workspace_floats(batch, seqlen, nheads, headdim, dstate, rank);

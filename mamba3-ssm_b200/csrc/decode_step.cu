@@ -401,7 +401,6 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_warp_kernel(StepPara
 #pragma unroll
     for (int r = 0; r < RM; ++r) yr[r] = fmaf(Cv[r * DL + k], hn, yr[r]);
   }
-#pragma unroll
   warp_sum_n<RM>(yr, lane);
 #pragma unroll
   for (int r = 0; r < RM; ++r) yr[r] += Dk * xr[r];

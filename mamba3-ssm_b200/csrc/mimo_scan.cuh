@@ -44,5 +44,8 @@ struct MimoParams {
 
 size_t mimo_bwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t P, int64_t D, int64_t R);
 int launch_mimo(const MimoParams& p, int xdt, int bcdt, bool bwd, cudaStream_t s);
+// Chunk-parallel forward (mimo_chunked.cu): workspace of mimo_fwd_workspace_floats floats.
+size_t mimo_fwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t D);
+int launch_mimo_fwd_chunked(const MimoParams& p, int xdt, int bcdt, float* ws, cudaStream_t s);
 
 }  // namespace m3

@@ -162,8 +162,11 @@ class _MimoScanFn(torch.autograd.Function):
             hl = _empty((Bn, H, Ds), torch.float32, x.device)
             bl = _empty((Bn, H, Ds), torch.float32, x.device)
         a = L.pack(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, y, hl, bl)
+        nbytes = lib.m3_mimo_scan_fwd_workspace_size(Bn, Ln, H, Ds)
+        ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=x.device)
         with torch.cuda.device(x.device):
-            L.check(lib.m3_mimo_scan_fwd(*a.ptrs, L.stream_of(x)), "m3_mimo_scan_fwd")
+            L.check(lib.m3_mimo_scan_fwd_ws(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)),
+                    "m3_mimo_scan_fwd_ws")
         ctx.save_for_backward(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0)
         ctx.mark_non_differentiable(*[t for t in (hl, bl) if t is not None])
         return y, hl, bl

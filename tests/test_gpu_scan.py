@@ -227,3 +227,22 @@ def test_siso_bf16_chunked_exact_mask_path(case):
     yo, _, _ = O.siso_scan_fwd(*[arrs[k] for k in keys])
     assert np.isfinite(y.float().cpu().numpy()).all()
     assert rel_err(y.detach().double().cpu().numpy(), yo) < 2e-2
+
+
+@pytest.mark.parametrize("L", [1, 63, 64, 65, 300])
+@pytest.mark.parametrize("R,D,P", [(4, 64, 32), (8, 256, 16)])
+def test_mimo_chunked_forward_with_states(L, R, D, P):
+    """The chunk-parallel MIMO forward (64-step chunks: local states, carry pass, outputs)
+    on chunk-boundary lengths, with carried-in states h0 / bx0 and the returned h_last /
+    bx_last, against the fp64 oracle."""
+    from mamba3_ssm.ops import _MimoScanFn
+    arrs, t = _inputs(1000 + L + D, 2, L, 3, P, D, R=R, dtype=torch.float32)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")
+    rng = np.random.default_rng(L + 7)
+    h0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV)
+    b0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV)
+    y, hl, bl = _MimoScanFn.apply(*[t[k] for k in keys], h0, b0, True)
+    yo, ho, bo = O.mimo_scan_fwd(*[arrs[k] for k in keys], h0.double().cpu().numpy(), b0.double().cpu().numpy())
+    assert rel_err(y.detach().double().cpu().numpy(), yo) < 1e-4
+    assert rel_err(hl.double().cpu().numpy(), ho) < 1e-4
+    assert rel_err(bl.double().cpu().numpy(), bo) < 1e-4
