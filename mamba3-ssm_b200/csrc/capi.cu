@@ -448,6 +448,8 @@ int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
   if (need == 0) return fail(M3_ERR_UNSUPPORTED, "mimo backward: shapes too large for shared memory");
   if (workspace == nullptr || workspace_bytes < need)
     return fail(M3_ERR_WORKSPACE, "mimo backward: workspace of " + std::to_string(need) + " bytes required");
+  if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+    return fail(M3_ERR_INVALID_ARGUMENT, "mimo backward: workspace not 16-byte aligned");
   p.dy = dy->data; p.sdy = s3(dy);
   p.dx = dx->data; p.sdx = s3(dx);
   p.dB = dB->data; p.sdB = s4(dB);

@@ -3,8 +3,8 @@
 //
 // The MIMO state is one scalar per d, so the recurrence h_t = a_t h_{t-1} + beta_t Bx_t +
 // gamma_t Bx_{t-1} (Bx_t = sum_r xr_t[r] B_t[r, :], xr_t = mimo_x x_t) is D independent
-// first-order scans. Time is cut into chunks of kTc steps and every (b, h, chunk) gets its
-// own CTA:
+// first-order scans. Time is cut into chunks (64 steps forward, 32 backward) and every
+// (b, h, chunk) gets its own CTA:
 //   1. local:  the chunk's end state from a zero start, S_c, and its decay product A_c
 //   2. carry:  per (b, h, d), in chunk order, carry_c = A_{c-1} carry_{c-1} + S_{c-1}
 //              (carry_0 = h0), written over S; the last one is h_last
@@ -20,7 +20,8 @@
 namespace m3 {
 namespace {
 
-constexpr int kTc = 64;   // time steps per chunk
+constexpr int kTcF = 64;  // time steps per chunk, forward
+constexpr int kTcB = 32;  // time steps per chunk, backward (four per-step state arrays in smem)
 constexpr int kCT = 128;  // threads per CTA
 
 template <typename T>
@@ -43,22 +44,24 @@ struct CSmem {
   float *x, *xr, *a, *be, *ga, *mx, *mo, *H, *yr;
 };
 
+template <int TC>
 __host__ __device__ inline size_t csmem_floats(int P, int R, int D, bool out) {
-  size_t n = (size_t)(kTc + 1) * P + (size_t)(kTc + 1) * R + 3 * (size_t)kTc + 2 * (size_t)R * P;
-  if (out) n += (size_t)kTc * D + (size_t)kTc * R;
+  size_t n = (size_t)(TC + 1) * P + (size_t)(TC + 1) * R + 3 * (size_t)TC + 2 * (size_t)R * P;
+  if (out) n += (size_t)TC * D + (size_t)TC * R;
   return n;
 }
 
+template <int TC>
 __device__ inline CSmem ccarve(float* p, int P, int R, int D, bool out) {
   CSmem s;
-  s.x = p; p += (kTc + 1) * P;
-  s.xr = p; p += (kTc + 1) * R;
-  s.a = p; p += kTc;
-  s.be = p; p += kTc;
-  s.ga = p; p += kTc;
+  s.x = p; p += (TC + 1) * P;
+  s.xr = p; p += (TC + 1) * R;
+  s.a = p; p += TC;
+  s.be = p; p += TC;
+  s.ga = p; p += TC;
   s.mx = p; p += R * P;
   s.mo = p; p += R * P;
-  s.H = out ? p : nullptr; p += out ? kTc * D : 0;
+  s.H = out ? p : nullptr; p += out ? TC * D : 0;
   s.yr = out ? p : nullptr;
   return s;
 }
@@ -107,12 +110,12 @@ __device__ __forceinline__ float bx_before(const MimoParams& a, const CSmem& s, 
   return a.bx0 ? a.bx0[((int64_t)b * a.H + h) * a.D + d] : 0.f;
 }
 
-template <typename TX, typename TB>
+template <typename TX, typename TB, int TC>
 __global__ void __launch_bounds__(kCT) mimo_local_kernel(MimoParams a, float* S, float* Adec, int nch) {
   extern __shared__ float4 csm4[];
   const int c = blockIdx.x, u = blockIdx.y, b = u / a.H, h = u - b * a.H;
-  const int t0 = c * kTc, n = min(kTc, a.L - t0);
-  const CSmem s = ccarve(reinterpret_cast<float*>(csm4), a.P, a.R, a.D, false);
+  const int t0 = c * TC, n = min(TC, a.L - t0);
+  const CSmem s = ccarve<TC>(reinterpret_cast<float*>(csm4), a.P, a.R, a.D, false);
   stage<TX>(a, s, b, h, t0, n, false);
   for (int d = threadIdx.x; d < a.D; d += kCT) {
     float bxp = bx_before<TB>(a, s, b, h, t0, d);
@@ -132,7 +135,8 @@ __global__ void __launch_bounds__(kCT) mimo_local_kernel(MimoParams a, float* S,
   }
 }
 
-__global__ void __launch_bounds__(kCT) mimo_carry_kernel(MimoParams a, float* S, const float* Adec, int nch) {
+__global__ void __launch_bounds__(kCT) mimo_carry_kernel(MimoParams a, float* S, const float* Adec, int nch,
+                                                          bool write_last) {
   const int u = blockIdx.x;
   for (int d = threadIdx.x; d < a.D; d += kCT) {
     float run = a.h0 ? a.h0[(int64_t)u * a.D + d] : 0.f;
@@ -142,7 +146,7 @@ __global__ void __launch_bounds__(kCT) mimo_carry_kernel(MimoParams a, float* S,
       S[i] = run;
       run = fmaf(Adec[(int64_t)u * nch + c], run, loc);
     }
-    if (a.h_last) a.h_last[(int64_t)u * a.D + d] = run;
+    if (write_last && a.h_last) a.h_last[(int64_t)u * a.D + d] = run;
   }
 }
 
@@ -150,9 +154,9 @@ template <typename TX, typename TB>
 __global__ void __launch_bounds__(kCT) mimo_out_kernel(MimoParams a, const float* S, int nch) {
   extern __shared__ float4 csm4[];
   const int c = blockIdx.x, u = blockIdx.y, b = u / a.H, h = u - b * a.H;
-  const int t0 = c * kTc, n = min(kTc, a.L - t0);
+  const int t0 = c * kTcF, n = min(kTcF, a.L - t0);
   const int P = a.P, R = a.R, D = a.D, tid = threadIdx.x;
-  const CSmem s = ccarve(reinterpret_cast<float*>(csm4), P, R, D, true);
+  const CSmem s = ccarve<kTcF>(reinterpret_cast<float*>(csm4), P, R, D, true);
   stage<TX>(a, s, b, h, t0, n, true);
   // states of the chunk from its carry
   for (int d = tid; d < D; d += kCT) {
@@ -189,6 +193,309 @@ __global__ void __launch_bounds__(kCT) mimo_out_kernel(MimoParams a, const float
   }
 }
 
+// ------------------------------------------------------------------------------------
+// Backward. The adjoint of the state obeys the reverse recurrence
+//   g_t = a_{t+1} g_{t+1} + E_t,   E_t = sum_r dyr_t[r] C_t[r, :],   dyr_t = mimo_o dy_t
+// (D independent scans again), so it is chunked the same way in reverse:
+//   B1 local:  g at each chunk start from a zero adjoint after the chunk, and the decay
+//              product a_{t0+1} .. a_{t0+n} that carries the adjoint across the chunk
+//   B2 carry:  in reverse chunk order, the adjoint entering each chunk from the right
+//              (written over the local values); g_0 gives dh0 = a_0 g_0, dbx0 = gamma_0 g_0
+//   B3 full:   each chunk recomputes its forward states (from the forward carries) and
+//              its adjoints (from the backward carries) and emits dx, dB, dC, dDT, dtrap,
+//              the per-step terms of dADT with their chunk total, and partial sums of dD,
+//              dmimo_x, dmimo_o (atomics)
+//   B4:        dADT_r = sum_{s >= r} (q_s - beta_s dbeta_s - gamma_s dgamma_s), the
+//              suffix sums of B3's per-step terms across chunks (offsets in fp64)
+// ------------------------------------------------------------------------------------
+struct BSmem {
+  float *dy, *dyr, *an;  // dy rows t0..t0+n-1, their mimo_o projections, a_{t0+1}..a_{t0+n}
+};
+
+template <typename TX>
+__device__ void stage_dy(const MimoParams& a, const BSmem& s, const float* mo, int b, int h, int t0, int n) {
+  const int P = a.P, R = a.R, tid = threadIdx.x;
+  for (int i = tid; i < n * P; i += kCT) {
+    const int r = i / P, p = i - r * P;
+    s.dy[i] = ldxc<TX>(a.dy, a.sdy, b, t0 + r, h, p);
+  }
+  for (int r = tid; r < n; r += kCT) {
+    const int t = t0 + 1 + r;
+    s.an[r] = t < a.L ? expf(scalc(a.adt, a.sadt, b, t, h)) : 0.f;
+  }
+  __syncthreads();
+  for (int i = tid; i < n * R; i += kCT) {
+    const int r = i / R, k = i - r * R;
+    float acc = 0.f;
+    for (int p = 0; p < P; ++p) acc = fmaf(s.dy[r * P + p], mo[k * P + p], acc);
+    s.dyr[i] = acc;
+  }
+  __syncthreads();
+}
+
+template <typename TB>
+__device__ __forceinline__ float e_at(const MimoParams& a, const float* dyr_row, int b, int t, int h, int d) {
+  float acc = 0.f;
+  for (int r = 0; r < a.R; ++r) acc = fmaf(dyr_row[r], ldbcc<TB>(a.Cm, a.sC, b, t, r, h, d), acc);
+  return acc;
+}
+
+template <typename TX, typename TB>
+__global__ void __launch_bounds__(kCT) mimo_bwd_local_kernel(MimoParams a, float* Gl, float* Ab, int nch) {
+  extern __shared__ float4 csm4[];
+  const int c = blockIdx.x, u = blockIdx.y, b = u / a.H, h = u - b * a.H;
+  const int t0 = c * kTcB, n = min(kTcB, a.L - t0);
+  const int P = a.P, R = a.R, tid = threadIdx.x;
+  float* p = reinterpret_cast<float*>(csm4);
+  float* mo = p; p += R * P;
+  BSmem s;
+  s.dy = p; p += kTcB * P;
+  s.dyr = p; p += kTcB * R;
+  s.an = p;
+  for (int i = tid; i < R * P; i += kCT) {
+    const int r = i / P, q = i - r * P;
+    mo[i] = a.mimo_o[(int64_t)h * a.smo_h + (int64_t)r * a.smo_r + q];
+  }
+  __syncthreads();
+  stage_dy<TX>(a, s, mo, b, h, t0, n);
+  for (int d = tid; d < a.D; d += kCT) {
+    float gv = 0.f;
+#pragma unroll 4
+    for (int t = n - 1; t >= 0; --t) gv = fmaf(s.an[t], gv, e_at<TB>(a, s.dyr + t * R, b, t0 + t, h, d));
+    Gl[((int64_t)u * nch + c) * a.D + d] = gv;
+  }
+  if (tid == 0) {
+    float prod = 1.f;
+    for (int t = 0; t < n; ++t) prod *= s.an[t];
+    Ab[(int64_t)u * nch + c] = prod;
+  }
+}
+
+__global__ void __launch_bounds__(kCT) mimo_bwd_carry_kernel(MimoParams a, float* Gl, const float* Ab, int nch) {
+  const int u = blockIdx.x, b = u / a.H, h = u - b * a.H;
+  for (int d = threadIdx.x; d < a.D; d += kCT) {
+    float run = 0.f;
+    for (int c = nch - 1; c >= 0; --c) {
+      const int64_t i = ((int64_t)u * nch + c) * a.D + d;
+      const float loc = Gl[i];
+      Gl[i] = run;
+      run = fmaf(Ab[(int64_t)u * nch + c], run, loc);
+    }
+    if (a.dh0 || a.dbx0) {
+      const float a0 = expf(scalc(a.adt, a.sadt, b, 0, h));
+      const float dt0 = scalc(a.dt, a.sdt, b, 0, h);
+      const float tr0 = sigmoidf_(scalc(a.trap, a.strap, b, 0, h));
+      if (a.dh0) a.dh0[(int64_t)u * a.D + d] = a0 * run;
+      if (a.dbx0) a.dbx0[(int64_t)u * a.D + d] = 0.5f * dt0 * tr0 * run;
+    }
+  }
+}
+
+// B3 shared memory (floats), chunk of kTcB steps; row r of x / xr / scalars is t0 - 1 + r
+// for x, xr, and t0 + r for a, be, ga (row n = t0 + n); BX row r is Bx_{t0-1+r}; G row n is
+// the adjoint entering from the next chunk.
+__host__ __device__ inline size_t bsmem_floats(int P, int R, int D) {
+  constexpr int T = kTcB;
+  return 2 * (size_t)R * P + (size_t)(T + 1) * P + (size_t)(T + 1) * R + (size_t)T * P + 3 * (size_t)T * R +
+         3 * (size_t)(T + 1) + 2 * (size_t)T + (size_t)T * D + 2 * (size_t)(T + 1) * D + (size_t)T * D + 4 * (size_t)T;
+}
+
+template <typename TX, typename TB>
+__global__ void __launch_bounds__(kCT) mimo_bwd_full_kernel(MimoParams a, const float* Hc, const float* Gc,
+                                                            double* tot, int nch) {
+  extern __shared__ float4 csm4[];
+  constexpr int T = kTcB;
+  const int c = blockIdx.x, u = blockIdx.y, b = u / a.H, h = u - b * a.H;
+  const int t0 = c * T, n = min(T, a.L - t0);
+  const int P = a.P, R = a.R, D = a.D, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* p = reinterpret_cast<float*>(csm4);
+  float* mx = p; p += R * P;
+  float* mo = p; p += R * P;
+  float* xs = p; p += (T + 1) * P;
+  float* xr = p; p += (T + 1) * R;
+  float* dyv = p; p += T * P;
+  float* dyr = p; p += T * R;
+  float* dxr = p; p += T * R;
+  float* yr = p; p += T * R;
+  float* av = p; p += T + 1;
+  float* be = p; p += T + 1;
+  float* ga = p; p += T + 1;
+  float* trv = p; p += T;
+  float* dtv = p; p += T;
+  float* Hs = p; p += T * D;
+  float* BX = p; p += (T + 1) * D;
+  float* Gs = p; p += (T + 1) * D;
+  float* Es = p; p += T * D;
+  float* red = p;  // dbeta, dgamma, q, z per step
+  // ---- staging
+  for (int i = tid; i < R * P; i += kCT) {
+    const int r = i / P, q = i - r * P;
+    mx[i] = a.mimo_x[(int64_t)h * a.smx_h + (int64_t)r * a.smx_r + q];
+    mo[i] = a.mimo_o[(int64_t)h * a.smo_h + (int64_t)r * a.smo_r + q];
+  }
+  for (int i = tid; i < (n + 1) * P; i += kCT) {
+    const int r = i / P, q = i - r * P, t = t0 - 1 + r;
+    xs[i] = t >= 0 ? ldxc<TX>(a.x, a.sx, b, t, h, q) : 0.f;
+  }
+  for (int i = tid; i < n * P; i += kCT) {
+    const int r = i / P, q = i - r * P;
+    dyv[i] = ldxc<TX>(a.dy, a.sdy, b, t0 + r, h, q);
+  }
+  for (int r = tid; r <= n; r += kCT) {
+    const int t = t0 + r;
+    float A = 0.f, bb = 0.f, gg = 0.f, tr = 0.f, dt = 0.f;
+    if (t < a.L) {
+      dt = scalc(a.dt, a.sdt, b, t, h);
+      tr = sigmoidf_(scalc(a.trap, a.strap, b, t, h));
+      A = expf(scalc(a.adt, a.sadt, b, t, h));
+      bb = dt * (1.0f - tr) + 0.5f * dt * tr;
+      gg = 0.5f * dt * tr;
+    }
+    av[r] = A; be[r] = bb; ga[r] = gg;
+    if (r < n) { trv[r] = tr; dtv[r] = dt; }
+  }
+  __syncthreads();
+  for (int i = tid; i < (n + 1) * R; i += kCT) {
+    const int r = i / R, k = i - r * R;
+    float acc = 0.f;
+    for (int q = 0; q < P; ++q) acc = fmaf(xs[r * P + q], mx[k * P + q], acc);
+    xr[i] = acc;
+  }
+  for (int i = tid; i < n * R; i += kCT) {
+    const int r = i / R, k = i - r * R;
+    float acc = 0.f;
+    for (int q = 0; q < P; ++q) acc = fmaf(dyv[r * P + q], mo[k * P + q], acc);
+    dyr[i] = acc;
+  }
+  __syncthreads();
+  // ---- forward states from the carry, adjoints from the backward carry (thread = d)
+  for (int d = tid; d < D; d += kCT) {
+    float bxp = t0 > 0 ? bx_at<TB>(a, xr, b, t0 - 1, h, d)
+                       : (a.bx0 ? a.bx0[(int64_t)u * D + d] : 0.f);
+    float hv = Hc[((int64_t)u * nch + c) * D + d];
+    BX[d] = bxp;
+#pragma unroll 4
+    for (int t = 0; t < n; ++t) {
+      const float bx = bx_at<TB>(a, xr + (t + 1) * R, b, t0 + t, h, d);
+      hv = fmaf(av[t], hv, fmaf(be[t], bx, ga[t] * bxp));
+      Hs[t * D + d] = hv;
+      BX[(t + 1) * D + d] = bx;
+      bxp = bx;
+    }
+    float gv = Gc[((int64_t)u * nch + c) * D + d];
+    Gs[n * D + d] = gv;
+#pragma unroll 4
+    for (int t = n - 1; t >= 0; --t) {
+      const float e = e_at<TB>(a, dyr + t * R, b, t0 + t, h, d);
+      Es[t * D + d] = e;
+      gv = fmaf(av[t + 1], gv, e);
+      Gs[t * D + d] = gv;
+    }
+  }
+  __syncthreads();
+  // ---- per (t, r): readout yr and dC; dB and dxr (one warp per pair, lanes over d)
+  const float Dk = a.Dskip[h * a.sD];
+  for (int pr = warp; pr < n * R; pr += kCT / 32) {
+    const int t = pr / R, r = pr - t * R, tt = t0 + t;
+    const float dyv_r = dyr[pr], xr_r = xr[(t + 1) * R + r];
+    float acc = 0.f, accb = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const float hd = Hs[t * D + d];
+      acc = fmaf(ldbcc<TB>(a.Cm, a.sC, b, tt, r, h, d), hd, acc);
+      const float v = fmaf(be[t], Gs[t * D + d], ga[t + 1] * Gs[(t + 1) * D + d]);
+      accb = fmaf(ldbcc<TB>(a.Bm, a.sB, b, tt, r, h, d), v, accb);
+      st(reinterpret_cast<TB*>(a.dC) + (int64_t)b * a.sdC.b + (int64_t)tt * a.sdC.l + (int64_t)r * a.sdC.r +
+             (int64_t)h * a.sdC.h + d, dyv_r * hd);
+      st(reinterpret_cast<TB*>(a.dB) + (int64_t)b * a.sdB.b + (int64_t)tt * a.sdB.l + (int64_t)r * a.sdB.r +
+             (int64_t)h * a.sdB.h + d, xr_r * v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      accb += __shfl_xor_sync(0xffffffffu, accb, o);
+    }
+    if (lane == 0) {
+      yr[pr] = fmaf(Dk, xr_r, acc);
+      dxr[pr] = fmaf(Dk, dyv_r, accb);
+    }
+  }
+  // ---- per t: dbeta, dgamma, q (one warp per step)
+  for (int t = warp; t < n; t += kCT / 32) {
+    float db = 0.f, dg = 0.f, q = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const float g = Gs[t * D + d];
+      db = fmaf(g, BX[(t + 1) * D + d], db);
+      dg = fmaf(g, BX[t * D + d], dg);
+      q = fmaf(Es[t * D + d], Hs[t * D + d], q);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      db += __shfl_xor_sync(0xffffffffu, db, o);
+      dg += __shfl_xor_sync(0xffffffffu, dg, o);
+      q += __shfl_xor_sync(0xffffffffu, q, o);
+    }
+    if (lane == 0) {
+      const int tt = t0 + t;
+      const float tr = trv[t], dt = dtv[t];
+      red[t] = q - be[t] * db - ga[t] * dg;
+      a.ddt[(int64_t)b * a.sddt.b + (int64_t)tt * a.sddt.l + (int64_t)h * a.sddt.h] =
+          db * (1.0f - 0.5f * tr) + dg * 0.5f * tr;
+      a.dtrap[(int64_t)b * a.sdtrap.b + (int64_t)tt * a.sdtrap.l + (int64_t)h * a.sdtrap.h] =
+          0.5f * dt * (dg - db) * tr * (1.0f - tr);
+    }
+  }
+  __syncthreads();
+  // ---- within-chunk suffix sums of the dADT terms (fp64); the chunk total for B4
+  if (tid == 0) {
+    double cum = 0.0;
+    for (int t = n - 1; t >= 0; --t) {
+      cum += (double)red[t];
+      a.dadt[(int64_t)b * a.sdadt.b + (int64_t)(t0 + t) * a.sdadt.l + (int64_t)h * a.sdadt.h] = (float)cum;
+    }
+    tot[(int64_t)u * nch + c] = cum;
+  }
+  // ---- dx = mimo_x^T dxr
+  for (int i = tid; i < n * P; i += kCT) {
+    const int t = i / P, q = i - t * P;
+    float acc = 0.f;
+    for (int r = 0; r < R; ++r) acc = fmaf(dxr[t * R + r], mx[r * P + q], acc);
+    st(reinterpret_cast<TX*>(a.dx) + (int64_t)b * a.sdx.b + (int64_t)(t0 + t) * a.sdx.l + (int64_t)h * a.sdx.h + q, acc);
+  }
+  // ---- dmimo_x += dxr x^T, dmimo_o += yr dy^T, dD += <dyr, xr>
+  for (int i = tid; i < R * P; i += kCT) {
+    const int r = i / P, q = i - r * P;
+    float ax = 0.f, ao = 0.f;
+    for (int t = 0; t < n; ++t) {
+      ax = fmaf(dxr[t * R + r], xs[(t + 1) * P + q], ax);
+      ao = fmaf(yr[t * R + r], dyv[t * P + q], ao);
+    }
+    atomicAdd(a.dmx + (int64_t)h * R * P + i, ax);
+    atomicAdd(a.dmo + (int64_t)h * R * P + i, ao);
+  }
+  if (warp == 0) {
+    float v = 0.f;
+    for (int i = lane; i < n * R; i += 32) v = fmaf(dyr[i], xr[(i / R + 1) * R + i % R], v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) atomicAdd(a.dD + h, v);
+  }
+}
+
+// B4: add to every step's dADT the terms of all later chunks
+__global__ void __launch_bounds__(kCT) mimo_bwd_dadt_kernel(MimoParams a, const double* tot, int nch) {
+  const int u = blockIdx.x, b = u / a.H, h = u - b * a.H;
+  double off = 0.0;
+  for (int c = nch - 1; c >= 0; --c) {
+    const int t0 = c * kTcB, n = min(kTcB, a.L - t0);
+    if (c < nch - 1)
+      for (int t = threadIdx.x; t < n; t += kCT) {
+        float* q = a.dadt + (int64_t)b * a.sdadt.b + (int64_t)(t0 + t) * a.sdadt.l + (int64_t)h * a.sdadt.h;
+        *q = (float)((double)*q + off);
+      }
+    off += tot[(int64_t)u * nch + c];
+  }
+}
+
 template <typename K>
 int opt_in(K k, size_t smem) {
   if (smem <= 48 * 1024) return M3_OK;
@@ -199,33 +506,84 @@ int opt_in(K k, size_t smem) {
 
 template <typename TX, typename TB>
 int run_chunked(const MimoParams& p, float* ws, cudaStream_t s) {
-  const int nch = (p.L + kTc - 1) / kTc;
+  const int nch = (p.L + kTcF - 1) / kTcF;
   const int units = p.Bn * p.H;
   float* S = ws;
   float* Adec = ws + (size_t)units * nch * p.D;
-  const size_t sm_loc = csmem_floats(p.P, p.R, p.D, false) * sizeof(float);
-  const size_t sm_out = csmem_floats(p.P, p.R, p.D, true) * sizeof(float);
+  const size_t sm_loc = csmem_floats<kTcF>(p.P, p.R, p.D, false) * sizeof(float);
+  const size_t sm_out = csmem_floats<kTcF>(p.P, p.R, p.D, true) * sizeof(float);
   if (sm_out > 200 * 1024) return fail(M3_ERR_UNSUPPORTED, "mimo scan: shapes too large for shared memory");
-  M3_TRY(opt_in(mimo_local_kernel<TX, TB>, sm_loc));
+  M3_TRY(opt_in(mimo_local_kernel<TX, TB, kTcF>, sm_loc));
   M3_TRY(opt_in(mimo_out_kernel<TX, TB>, sm_out));
   const dim3 grid(nch, units);
-  mimo_local_kernel<TX, TB><<<grid, kCT, sm_loc, s>>>(p, S, Adec, nch);
+  mimo_local_kernel<TX, TB, kTcF><<<grid, kCT, sm_loc, s>>>(p, S, Adec, nch);
   M3_TRY(check_launch("mimo_local_kernel"));
-  mimo_carry_kernel<<<units, kCT, 0, s>>>(p, S, Adec, nch);
+  mimo_carry_kernel<<<units, kCT, 0, s>>>(p, S, Adec, nch, true);
   M3_TRY(check_launch("mimo_carry_kernel"));
   mimo_out_kernel<TX, TB><<<grid, kCT, sm_out, s>>>(p, S, nch);
   return check_launch("mimo_out_kernel");
 }
 
+template <typename TX, typename TB>
+int run_bwd_chunked(const MimoParams& p0, void* ws, cudaStream_t s) {
+  MimoParams p = p0;
+  const int nch = (p.L + kTcB - 1) / kTcB;
+  const int units = p.Bn * p.H;
+  double* tot = reinterpret_cast<double*>(ws);
+  float* Hc = reinterpret_cast<float*>(tot + (size_t)units * nch);
+  float* Af = Hc + (size_t)units * nch * p.D;
+  float* Gc = Af + (size_t)units * nch;
+  float* Ab = Gc + (size_t)units * nch * p.D;
+  const size_t sm_loc = csmem_floats<kTcB>(p.P, p.R, p.D, false) * sizeof(float);
+  const size_t sm_bl = ((size_t)p.R * p.P + (size_t)kTcB * p.P + (size_t)kTcB * p.R + kTcB) * sizeof(float);
+  const size_t sm_full = bsmem_floats(p.P, p.R, p.D) * sizeof(float);
+  M3_TRY(opt_in(mimo_local_kernel<TX, TB, kTcB>, sm_loc));
+  M3_TRY(opt_in(mimo_bwd_local_kernel<TX, TB>, sm_bl));
+  M3_TRY(opt_in(mimo_bwd_full_kernel<TX, TB>, sm_full));
+  const dim3 grid(nch, units);
+  // forward states at the chunk starts
+  mimo_local_kernel<TX, TB, kTcB><<<grid, kCT, sm_loc, s>>>(p, Hc, Af, nch);
+  M3_TRY(check_launch("mimo_local_kernel"));
+  mimo_carry_kernel<<<units, kCT, 0, s>>>(p, Hc, Af, nch, false);
+  M3_TRY(check_launch("mimo_carry_kernel"));
+  // adjoints entering each chunk from the right
+  mimo_bwd_local_kernel<TX, TB><<<grid, kCT, sm_bl, s>>>(p, Gc, Ab, nch);
+  M3_TRY(check_launch("mimo_bwd_local_kernel"));
+  mimo_bwd_carry_kernel<<<units, kCT, 0, s>>>(p, Gc, Ab, nch);
+  M3_TRY(check_launch("mimo_bwd_carry_kernel"));
+  mimo_bwd_full_kernel<TX, TB><<<grid, kCT, sm_full, s>>>(p, Hc, Gc, tot, nch);
+  M3_TRY(check_launch("mimo_bwd_full_kernel"));
+  mimo_bwd_dadt_kernel<<<units, kCT, 0, s>>>(p, tot, nch);
+  return check_launch("mimo_bwd_dadt_kernel");
+}
+
 }  // namespace
 
+bool mimo_bwd_chunked_fits(int P, int R, int D) { return bsmem_floats(P, R, D) * sizeof(float) <= 200 * 1024; }
+
+size_t mimo_bwd_chunked_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D) {
+  const int64_t nch = (L + kTcB - 1) / kTcB, cells = Bn * H * nch;
+  return (size_t)cells * sizeof(double) + sizeof(float) * (size_t)cells * (2 * D + 2);
+}
+
+int launch_mimo_bwd_chunked(const MimoParams& p, int xdt, int bcdt, void* ws, cudaStream_t s) {
+  if (p.L >= (int64_t)65535 * kTcB) return fail(M3_ERR_UNSUPPORTED, "mimo scan: sequence too long for the chunk grid");
+  if (xdt == M3_FLOAT32 && bcdt == M3_FLOAT32) return run_bwd_chunked<float, float>(p, ws, s);
+  if (xdt == M3_BFLOAT16 && bcdt == M3_BFLOAT16) return run_bwd_chunked<__nv_bfloat16, __nv_bfloat16>(p, ws, s);
+  if (xdt == M3_BFLOAT16 && bcdt == M3_FLOAT32) return run_bwd_chunked<__nv_bfloat16, float>(p, ws, s);
+  if (xdt == M3_FLOAT32 && bcdt == M3_BFLOAT16) return run_bwd_chunked<float, __nv_bfloat16>(p, ws, s);
+  if (xdt == M3_FLOAT16 && bcdt == M3_FLOAT16) return run_bwd_chunked<__half, __half>(p, ws, s);
+  if (xdt == M3_FLOAT16 && bcdt == M3_FLOAT32) return run_bwd_chunked<__half, float>(p, ws, s);
+  return fail(M3_ERR_UNSUPPORTED, "unsupported dtype combination for x / B,C");
+}
+
 size_t mimo_fwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t D) {
-  const int64_t nch = (L + kTc - 1) / kTc;
+  const int64_t nch = (L + kTcF - 1) / kTcF;
   return (size_t)(Bn * H * nch * (D + 1));
 }
 
 int launch_mimo_fwd_chunked(const MimoParams& p, int xdt, int bcdt, float* ws, cudaStream_t s) {
-  if (p.L >= (int64_t)65535 * kTc) return fail(M3_ERR_UNSUPPORTED, "mimo scan: sequence too long for the chunk grid");
+  if (p.L >= (int64_t)65535 * kTcF) return fail(M3_ERR_UNSUPPORTED, "mimo scan: sequence too long for the chunk grid");
   if (xdt == M3_FLOAT32 && bcdt == M3_FLOAT32) return run_chunked<float, float>(p, ws, s);
   if (xdt == M3_BFLOAT16 && bcdt == M3_BFLOAT16) return run_chunked<__nv_bfloat16, __nv_bfloat16>(p, ws, s);
   if (xdt == M3_BFLOAT16 && bcdt == M3_FLOAT32) return run_chunked<__nv_bfloat16, float>(p, ws, s);

@@ -425,6 +425,8 @@ int run(const MimoParams& p, bool bwd, cudaStream_t s) {
 }  // namespace
 
 size_t mimo_bwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t P, int64_t D, int64_t R) {
+  if (mimo_bwd_chunked_fits((int)P, (int)R, (int)D))
+    return (mimo_bwd_chunked_workspace_bytes(Bn, L, H, D) + sizeof(float) - 1) / sizeof(float);
   const int T = choose_T((int)P, (int)R, (int)D, true);
   if (T == 0) return 0;
   const int64_t nchunk = (L + T - 1) / T;
@@ -432,6 +434,9 @@ size_t mimo_bwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t P, in
 }
 
 int launch_mimo(const MimoParams& p, int xdt, int bcdt, bool bwd, cudaStream_t s) {
+  // the chunk-parallel backward where its shared-memory layout fits; the per-(b, h) sweep
+  // kernel otherwise
+  if (bwd && mimo_bwd_chunked_fits(p.P, p.R, p.D)) return launch_mimo_bwd_chunked(p, xdt, bcdt, p.work, s);
   if (xdt == M3_FLOAT32 && bcdt == M3_FLOAT32) return run<float, float>(p, bwd, s);
   if (xdt == M3_BFLOAT16 && bcdt == M3_BFLOAT16) return run<__nv_bfloat16, __nv_bfloat16>(p, bwd, s);
   if (xdt == M3_BFLOAT16 && bcdt == M3_FLOAT32) return run<__nv_bfloat16, float>(p, bwd, s);

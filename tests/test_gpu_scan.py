@@ -246,3 +246,28 @@ def test_mimo_chunked_forward_with_states(L, R, D, P):
     assert rel_err(y.detach().double().cpu().numpy(), yo) < 1e-4
     assert rel_err(hl.double().cpu().numpy(), ho) < 1e-4
     assert rel_err(bl.double().cpu().numpy(), bo) < 1e-4
+
+
+@pytest.mark.parametrize("L", [1, 31, 32, 33, 200])
+@pytest.mark.parametrize("R,D,P", [(4, 64, 32), (2, 128, 64)])
+def test_mimo_chunked_backward_with_states(L, R, D, P):
+    """The chunk-parallel MIMO backward (32-step chunks: forward carries, reverse adjoint
+    carries, per-chunk gradients, cross-chunk dADT suffix sums) on chunk-boundary lengths,
+    with initial states, against the fp64 adjoint of the oracle (all gradients incl.
+    dh0 / dbx0)."""
+    from mamba3_ssm.ops import _MimoScanFn
+    arrs, t = _inputs(2000 + L + D, 2, L, 3, P, D, R=R, dtype=torch.float32)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")
+    rng = np.random.default_rng(L + 11)
+    h0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV).requires_grad_(True)
+    b0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV).requires_grad_(True)
+    ins = [t[k].requires_grad_(True) for k in keys]
+    y, _, _ = _MimoScanFn.apply(*ins, h0, b0, False)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    go = O.mimo_scan_bwd(*[arrs[k] for k in keys], dy.double().cpu().numpy(),
+                         h0.detach().double().cpu().numpy(), b0.detach().double().cpu().numpy())
+    for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
+        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < 5e-4, k
+    assert rel_err(h0.grad.double().cpu().numpy(), go["dh0"]) < 5e-4
+    assert rel_err(b0.grad.double().cpu().numpy(), go["dbx0"]) < 5e-4
