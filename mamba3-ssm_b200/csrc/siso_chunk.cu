@@ -116,6 +116,8 @@ __device__ int g_chunk_error;  // set when a bounded wait gives up
 
 struct ChunkArgs {
   int Bn, L, H;
+  int D;     // d_state: 128, or 64 (the second halves of the C / B tiles then stay zero)
+  int nkd;   // K steps of 16 over d_state in G and Y1
   const float* adt; Str3 sadt;
   const float* dt; Str3 sdt;
   const float* trap; Str3 strap;
@@ -529,24 +531,26 @@ __device__ __forceinline__ void write_kbuf(Smem& s, int d, const float (&k)[kP])
 
 __device__ __forceinline__ void init_state(const ChunkArgs& a, const ChunkPos& cp, float a0, float g0, int d,
                                            float (&k)[kP]) {
-  const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * kD;
+  const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * a.D;
+  const bool dv = d < a.D;
 #pragma unroll
   for (int pp = 0; pp < kP; ++pp) {
     float v = 0.f;
-    if (a.h0) v = a0 * a.h0[sb + (int64_t)pp * kD + d];
-    if (a.bx0) v = fmaf(g0, a.bx0[sb + (int64_t)pp * kD + d], v);
+    if (a.h0 && dv) v = a0 * a.h0[sb + (int64_t)pp * a.D + d];
+    if (a.bx0 && dv) v = fmaf(g0, a.bx0[sb + (int64_t)pp * a.D + d], v);
     k[pp] = v;
   }
 }
 
 __device__ __forceinline__ void store_final(const ChunkArgs& a, const Smem& s, int b, int h, int d,
                                             const float (&k)[kP]) {
-  const int64_t sb = ((int64_t)b * a.H + h) * kP * kD;
+  if (d >= a.D) return;
+  const int64_t sb = ((int64_t)b * a.H + h) * kP * a.D;
   if (a.h_last)
-    for (int pp = 0; pp < kP; ++pp) a.h_last[sb + (int64_t)pp * kD + d] = k[pp];
+    for (int pp = 0; pp < kP; ++pp) a.h_last[sb + (int64_t)pp * a.D + d] = k[pp];
   if (a.bx_last) {
     const float bd = s.side_b[d];
-    for (int pp = 0; pp < kP; ++pp) a.bx_last[sb + (int64_t)pp * kD + d] = s.side_x[pp] * bd;
+    for (int pp = 0; pp < kP; ++pp) a.bx_last[sb + (int64_t)pp * a.D + d] = s.side_x[pp] * bd;
   }
 }
 
@@ -653,6 +657,15 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
     tmem_alloc(&s.tmem_base, kTmemCols);
     tmem_relinquish();
   }
+  if (a.D < kD) {
+    // d_state 64: the upper halves of the C / B tiles are never loaded; they read as zero
+    for (int i = tid; i < NS * 2 * (int)(kTileBytes / 16); i += kThreads) {
+      const int st = i / (2 * (kTileBytes / 16)), rem = i % (2 * (kTileBytes / 16));
+      const int t = rem < (int)(kTileBytes / 16) ? 1 : 3, off = rem % (kTileBytes / 16);
+      reinterpret_cast<uint4*>(s.cb[st][t])[off] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -672,11 +685,13 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
         if (gc < G && mbar_test(&s.cb_empty[gc % NS], ((gc / NS) & 1) ^ 1)) {
           const int st = gc % NS;
           const ChunkPos cp = chunk_pos(a, gc, nch);
-          mbar_expect_tx(&s.cb_full[st], kCBBytes);
+          mbar_expect_tx(&s.cb_full[st], a.D == kD ? kCBBytes : kCBBytes / 2);
           tma_load_4d(s.cb[st][0], &tm_C, &s.cb_full[st], 0, cp.h, cp.t0, cp.b);
-          tma_load_4d(s.cb[st][1], &tm_C, &s.cb_full[st], 64, cp.h, cp.t0, cp.b);
           tma_load_4d(s.cb[st][2], &tm_B, &s.cb_full[st], 0, cp.h, cp.t0, cp.b);
-          tma_load_4d(s.cb[st][3], &tm_B, &s.cb_full[st], 64, cp.h, cp.t0, cp.b);
+          if (a.D == kD) {
+            tma_load_4d(s.cb[st][1], &tm_C, &s.cb_full[st], 64, cp.h, cp.t0, cp.b);
+            tma_load_4d(s.cb[st][3], &tm_B, &s.cb_full[st], 64, cp.h, cp.t0, cp.b);
+          }
           ++gc;
           moved = true;
         }
@@ -733,8 +748,8 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
           const int st = cg % NS, p = cg & 1;
           tc_fence_after();
           const uint32_t c0 = cb_addr(st, 0), b0 = cb_addr(st, 2);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll 4
+          for (int kk = 0; kk < a.nkd; ++kk) {
             const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
             mma_ss(tbase + col_g(p), sdesc_sw128(c0 + koff, 16, 1024), sdesc_sw128(b0 + koff, 16, 1024), I_G,
                    kk > 0);
@@ -761,8 +776,8 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
           } else if (mbar_test(&s.k_ready, ck & 1) && mbar_test(&s.y1_free, (ck & 1) ^ 1)) {
             tc_fence_after();
             const uint32_t c0 = cb_addr(st, 0);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll 4
+            for (int kk = 0; kk < a.nkd; ++kk) {
               const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
               mma_ss(tbase + kColY1, sdesc_sw128(c0 + koff, 16, 1024),
                      sdesc_sw128(a_kb + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
@@ -869,7 +884,7 @@ int num_sms() {
 
 bool siso_chunk_supported(const SisoParams& p, int xdt, int bcdt) {
   if (xdt != M3_BFLOAT16 || bcdt != M3_BFLOAT16) return false;
-  if (p.P != kP || p.D != kD) return false;
+  if (p.P != kP || (p.D != kD && p.D != 64)) return false;
   if (!aligned16(p.x) || !aligned16(p.Bm) || !aligned16(p.Cm) || !aligned16(p.y)) return false;
   if (!strides_ok(p.sx) || !strides_ok(p.sB) || !strides_ok(p.sC) || !strides_ok(p.sy)) return false;
   if (!get_encode()) return false;
@@ -899,6 +914,7 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
   M3_TRY(make_map(&mc, p.Cm, p.D, p.H, p.L, p.Bn, p.sC));
   ChunkArgs a{};
   a.Bn = p.Bn; a.L = p.L; a.H = p.H;
+  a.D = p.D; a.nkd = p.D / 16;
   a.adt = p.adt; a.sadt = p.sadt;
   a.dt = p.dt; a.sdt = p.sdt;
   a.trap = p.trap; a.strap = p.strap;

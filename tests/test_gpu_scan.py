@@ -184,20 +184,21 @@ def test_long_sequence_slices_against_oracle():
     assert rel_err(y.detach().double().cpu().numpy(), yo) < 2e-2
 
 
+@pytest.mark.parametrize("Ds", [128, 64])
 @pytest.mark.parametrize("L", [1, 77, 128, 129, 300, 1000])
-def test_siso_bf16_headdim64_dstate128_against_oracle(L):
-    """The long-context shape class (bf16, P=64, D=128, run by the chunked tensor-core
-    kernel) on ragged lengths, with and without carried decode states."""
+def test_siso_bf16_headdim64_dstate128_against_oracle(L, Ds):
+    """The shape class of the chunked tensor-core kernel (bf16, P=64, d_state 128 or 64) on
+    ragged lengths, with and without carried decode states."""
     from mamba3_ssm import ssm_scan_siso
     from mamba3_ssm.ops import ssm_scan_siso_states
-    arrs, t = _inputs(100 + L, 2, L, 3, 64, 128, dtype=torch.bfloat16)
+    arrs, t = _inputs(100 + L + Ds, 2, L, 3, 64, Ds, dtype=torch.bfloat16)
     keys = ("x", "B", "C", "ADT", "DT", "trap", "D")
     y = ssm_scan_siso(*[t[k] for k in keys])
     yo, ho, bo = O.siso_scan_fwd(*[arrs[k] for k in keys])
     assert rel_err(y.detach().double().cpu().numpy(), yo) < 2e-2
     rng = np.random.default_rng(L)
-    h0 = torch.tensor(rng.standard_normal((2, 3, 64, 128)), dtype=torch.float32, device=DEV)
-    b0 = torch.tensor(rng.standard_normal((2, 3, 64, 128)), dtype=torch.float32, device=DEV)
+    h0 = torch.tensor(rng.standard_normal((2, 3, 64, Ds)), dtype=torch.float32, device=DEV)
+    b0 = torch.tensor(rng.standard_normal((2, 3, 64, Ds)), dtype=torch.float32, device=DEV)
     y2, h2, b2 = ssm_scan_siso_states(*[t[k] for k in keys], h0, b0)
     yo2, ho2, bo2 = O.siso_scan_fwd(*[arrs[k] for k in keys], h0.double().cpu().numpy(), b0.double().cpu().numpy())
     assert rel_err(y2.detach().double().cpu().numpy(), yo2) < 2e-2
