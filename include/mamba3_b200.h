@@ -214,6 +214,26 @@ int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* w
                m3_tensor* out, m3_tensor* residual_out, void* stream);
 
 /* ---------------------------------------------------------------------------------
+ * Fused forward prologue of Mamba3.forward (layer.py:180-244) for inference, from the
+ * in_proj output zxbcdt (batch, seqlen, d_in_proj) (innermost stride 1, any dtype):
+ *   DT = softplus(dd_dt + dt_bias), ADT = -min(softplus(dd_A), -A_floor) * DT, trap = the
+ *   logit in fp32 (all (batch, seqlen, nheads) fp32 contiguous); angles (batch, seqlen,
+ *   nheads, num_rope_angles) fp32 = cumsum over seqlen of angle_raw * DT; B_proj, C_proj
+ *   (batch, seqlen, mimo_rank, nheads, d_state) contiguous, f32 / bf16 / f16: RMSNorm
+ *   (eps = dims->norm_eps) * weight + bias per head, pairs (2i, 2i+1) with 2i < rope_split
+ *   rotated by angles. Parameters fp32 as in m3_siso_step. Replaces the PyTorch prologue
+ *   of the reference (layer.py:198-244), which materialises the per-head B / C in fp32.
+ * ------------------------------------------------------------------------------- */
+int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
+                      const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                      const m3_tensor* C_norm_w, m3_tensor* B_proj, m3_tensor* C_proj, m3_tensor* ADT,
+                      m3_tensor* DT, m3_tensor* trap, m3_tensor* angles, void* stream);
+
+/* out = y * silu(z), (B, L, H, P) views with innermost stride 1; the gate of
+ * Mamba3.forward between the scan and out_proj (layer.py:262-266). */
+int m3_silu_gate(const m3_tensor* y, const m3_tensor* z, m3_tensor* out, void* stream);
+
+/* ---------------------------------------------------------------------------------
  * Health word of the warp-specialised kernels on the current device: *flag_out is
  * nonzero once any bounded inter-warp wait gave up (the kernel then drained and its
  * outputs are invalid); reset != 0 clears it. Synchronises the device. No reference

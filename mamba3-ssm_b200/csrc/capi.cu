@@ -7,6 +7,7 @@
 #include "decode_step.cuh"
 #include "m3_common.cuh"
 #include "mimo_scan.cuh"
+#include "prologue.cuh"
 #include "rmsnorm.cuh"
 #include "siso_chunk.cuh"
 #include "siso_scan.cuh"
@@ -596,6 +597,64 @@ int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* w
 int m3_device_timeouts(int reset, int* flag_out) {
   if (!flag_out) return fail(M3_ERR_INVALID_ARGUMENT, "flag_out: missing");
   return chunk_error_word(reset != 0, flag_out);
+}
+
+
+int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
+                      const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                      const m3_tensor* C_norm_w, m3_tensor* B_proj, m3_tensor* C_proj, m3_tensor* ADT,
+                      m3_tensor* DT, m3_tensor* trap, m3_tensor* angles, void* stream) {
+  if (!dims) return fail(M3_ERR_INVALID_ARGUMENT, "dims: missing");
+  const int64_t H = dims->nheads, P = dims->headdim, Ds = dims->d_state, G = dims->ngroups,
+                R = dims->mimo_rank, S = dims->num_rope_angles, di = dims->d_inner;
+  if (H <= 0 || P <= 0 || Ds <= 0 || G <= 0 || R <= 0 || S < 0 || di != H * P || dims->rope_split != 2 * S ||
+      dims->rope_split > Ds || (G != 1 && G != H))
+    return fail(M3_ERR_INVALID_ARGUMENT, "dims: inconsistent layer dimensions");
+  if (!present(zxbcdt) || zxbcdt->ndim != 3) return fail(M3_ERR_INVALID_ARGUMENT, "zxbcdt: expected (batch, seqlen, d_in_proj)");
+  const int64_t Bn = zxbcdt->shape[0], L = zxbcdt->shape[1];
+  const int64_t dproj = 2 * di + 2 * Ds * G * R + 3 * H + S;
+  const bool empty = Bn * L == 0;
+  const int64_t zs[3] = {Bn, L, dproj}, bs[5] = {Bn, L, R, H, Ds}, ss[3] = {Bn, L, H}, as[4] = {Bn, L, H, S},
+                h1[1] = {H}, hrd[3] = {H, R, Ds}, d1[1] = {Ds};
+  M3_TRY(check(zxbcdt, "zxbcdt", 3, zs, kAnyFloat, false, false, !empty));
+  M3_TRY(check(B_proj, "B_proj", 5, bs, kAnyFloat, true, false, !empty));
+  M3_TRY(check(C_proj, "C_proj", 5, bs, 1u << B_proj->dtype, true, false, !empty));
+  M3_TRY(check(ADT, "ADT", 3, ss, kF32, true, false, false));
+  M3_TRY(check(DT, "DT", 3, ss, kF32, true, false, false));
+  M3_TRY(check(trap, "trap", 3, ss, kF32, true, false, false));
+  M3_TRY(check(angles, "angles", 4, as, kF32, true, S == 0, false));
+  M3_TRY(check(dt_bias, "dt_bias", 1, h1, kF32, true, false, false));
+  M3_TRY(check(B_bias, "B_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(C_bias, "C_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(B_norm_w, "B_norm_w", 1, d1, kF32, true, false, false));
+  M3_TRY(check(C_norm_w, "C_norm_w", 1, d1, kF32, true, false, false));
+  if (empty) return M3_OK;
+  if (Bn > INT32_MAX || L > INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "prologue: dimension too large");
+  PrologueParams p{};
+  p.Bn = (int)Bn; p.L = (int)L; p.H = (int)H; p.P = (int)P; p.D = (int)Ds; p.R = (int)R; p.G = (int)G;
+  p.S = (int)S; p.split = dims->rope_split; p.d_inner = (int)di; p.A_floor = dims->A_floor; p.eps = dims->norm_eps;
+  p.zx = zxbcdt->data; p.s_zb = zxbcdt->stride[0]; p.s_zl = zxbcdt->stride[1];
+  p.dt_bias = fptr<const float>(dt_bias);
+  p.B_bias = fptr<const float>(B_bias); p.C_bias = fptr<const float>(C_bias);
+  p.B_norm_w = fptr<const float>(B_norm_w); p.C_norm_w = fptr<const float>(C_norm_w);
+  p.Bp = B_proj->data; p.Cp = C_proj->data;
+  p.ADT = fptr<float>(ADT); p.DT = fptr<float>(DT); p.trap = fptr<float>(trap); p.angles = fptr<float>(angles);
+  return launch_prologue(p, zxbcdt->dtype, B_proj->dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int m3_silu_gate(const m3_tensor* y, const m3_tensor* z, m3_tensor* out, void* stream) {
+  if (!present(y) || y->ndim != 4) return fail(M3_ERR_INVALID_ARGUMENT, "y: expected (B, L, H, P)");
+  const int64_t* sh = y->shape;
+  const bool empty = sh[0] * sh[1] * sh[2] * sh[3] == 0;
+  M3_TRY(check(y, "y", 4, sh, kAnyFloat, false, false, !empty));
+  M3_TRY(check(z, "z", 4, sh, kAnyFloat, false, false, !empty));
+  M3_TRY(check(out, "out", 4, sh, kAnyFloat, false, false, !empty));
+  if (empty) return M3_OK;
+  if (sh[1] > INT32_MAX || sh[2] > INT32_MAX || sh[3] > INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "gate: dimension too large");
+  GateParams p{};
+  p.rows = sh[0] * sh[1] * sh[2]; p.L = (int)sh[1]; p.H = (int)sh[2]; p.P = (int)sh[3];
+  p.y = y->data; p.sy = s3(y); p.z = z->data; p.sz = s3(z); p.out = out->data; p.so = s3(out);
+  return launch_gate(p, y->dtype, z->dtype, out->dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

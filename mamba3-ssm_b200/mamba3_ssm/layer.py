@@ -104,6 +104,52 @@ class Mamba3(nn.Module):
         return n + bias.transpose(0, 1)  # (H,R,D) -> (R,H,D)
 
     def forward(self, u: torch.Tensor) -> torch.Tensor:
+        if not (torch.is_grad_enabled() and (u.requires_grad or any(p.requires_grad for p in self.parameters()))):
+            return self._forward_fused(u)
+        return self._forward_autograd(u)
+
+    def _forward_fused(self, u: torch.Tensor) -> torch.Tensor:
+        """Inference forward: in_proj, the fused prologue kernel (m3_layer_prologue: dt /
+        decay / trap, RMSNorm + bias + RoPE of B and C per head, the angle cumsum), the scan,
+        the fused silu gate (m3_silu_gate), out_proj. bf16 layers give the scan bf16 B / C
+        (the tensor-core path); other dtypes keep them in fp32."""
+        batch, Ln, _ = u.shape
+        R, Ds, H, P, S = self.mimo_rank, self.d_state, self.nheads, self.headdim, self.num_rope_angles
+        zx = self.in_proj(u)
+        if not zx.is_cuda:
+            raise RuntimeError("Mamba3.forward: the B200 build runs on CUDA tensors only (no CPU path)")
+        if zx.stride(-1) != 1:
+            zx = zx.contiguous()
+        vals = self._step_params()
+        dims = self._f32_cache[3]
+        dev = zx.device
+        op = torch.bfloat16 if zx.dtype == torch.bfloat16 else torch.float32
+        Bp = torch.empty(batch, Ln, R, H, Ds, dtype=op, device=dev)
+        Cp = torch.empty(batch, Ln, R, H, Ds, dtype=op, device=dev)
+        ADT, DT, trap = (torch.empty(batch, Ln, H, dtype=torch.float32, device=dev) for _ in range(3))
+        ang = torch.empty(batch, Ln, H, S, dtype=torch.float32, device=dev)
+        lib = L.load()
+        a = L.pack(zx, *vals[:5], Bp, Cp, ADT, DT, trap, ang)
+        with torch.cuda.device(dev):
+            rc = lib.m3_layer_prologue(ctypes.byref(dims), *a.ptrs, torch.cuda.current_stream(dev).cuda_stream)
+        L.check(rc, "m3_layer_prologue")
+        di = self.d_inner
+        z = zx[..., :di].unflatten(-1, (H, P))
+        x = zx[..., di:2 * di].unflatten(-1, (H, P))
+        if self.is_mimo:
+            y = ssm_scan_mimo(x, Bp, Cp, ADT, DT, trap, self.D, self.mimo_x, self.mimo_o)
+        else:
+            y = ssm_scan_siso(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, self.D)
+        g = torch.empty(batch, Ln, H, P, dtype=zx.dtype, device=dev)
+        a = L.pack(y, z, g)
+        with torch.cuda.device(dev):
+            rc = lib.m3_silu_gate(*a.ptrs, torch.cuda.current_stream(dev).cuda_stream)
+        L.check(rc, "m3_silu_gate")
+        return self.out_proj(g.flatten(-2))
+
+    def _forward_autograd(self, u: torch.Tensor) -> torch.Tensor:
+        """Training forward: the reference's PyTorch prologue (differentiated by autograd)
+        around the scan kernels."""
         batch, Ln, _ = u.shape
         R, G, Ds, H, P = self.mimo_rank, self.num_bc_heads, self.d_state, self.nheads, self.headdim
         z, x, B_raw, C_raw, dd_dt, dd_A, trap_raw, angle_raw = torch.split(self.in_proj(u), self._splits, dim=-1)
