@@ -2,12 +2,12 @@
 // everything between the in_proj GEMM and the scan, and the silu gate between the scan and
 // out_proj, read straight from the in_proj output.
 //
-//   angle kernel (one warp per (b, h), lane = rotary angle, walks the sequence):
+//   angle kernel (one CTA per (b, h), thread = step, block scans over tiles of 128 steps):
 //     DT = softplus(dd_dt + dt_bias), A = -min(softplus(dd_A), -A_floor) (layer.py:207),
 //     ADT = A DT, trap logit copied to fp32, angles[b,l,h,i] = sum_{l'<=l} angle_raw[b,l',i] DT
-//   bc kernel (one CTA per (b, l) row): RMSNorm over d_state of every (r, g) row of B and C
-//     (ops.py:94-102, once per group, not once per head), then per head the bias and the
-//     rotation of the pairs (2i, 2i+1), i < rope_split / 2, by angles[b,l,h,i]
+//   bc kernel (one warp per output row (b, l, B|C, r, h)): RMSNorm over d_state of the
+//     row's group (ops.py:94-102), the head's bias, and the rotation of the pairs
+//     (2i, 2i+1), i < rope_split / 2, by angles[b,l,h,i]
 //     (ops.py:116-119, layer.py:229-244), written as B_proj / C_proj (B, L, R, H, D) in the
 //     scan's operand dtype
 //   gate kernel: out = y * silu(z) in the dtype of out (layer.py:262-266)
@@ -17,106 +17,184 @@
 namespace m3 {
 namespace {
 
-constexpr int kWarps = 4;
+// one CTA per (b, h); the sequence in tiles of 128 steps, thread = step; the angle
+// cumsums are block-wide inclusive scans (warp shuffles, then the warp totals) carried
+// from tile to tile
+constexpr int kAT = 128;
 
 template <typename TZ>
-__global__ void __launch_bounds__(32 * kWarps) prologue_angle_kernel(PrologueParams a) {
-  const int lane = threadIdx.x & 31;
-  const int u = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (u >= a.Bn * a.H) return;
-  const int b = u / a.H, h = u - b * a.H;
+__global__ void __launch_bounds__(kAT) prologue_angle_kernel(PrologueParams a) {
+  __shared__ float wsum[kAT / 32][64];
+  __shared__ float carry[64];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int u = blockIdx.x, b = u / a.H, h = u - b * a.H;
   const int H = a.H, S = a.S;
   const int off_dt = 2 * a.d_inner + 2 * a.D * a.G * a.R;
   const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
   const float dtb = a.dt_bias[h];
-  float ang0 = 0.f, ang1 = 0.f;  // angles lane and lane + 32
   const TZ* base = reinterpret_cast<const TZ*>(a.zx) + (int64_t)b * a.s_zb;
-#pragma unroll 4
-  for (int l = 0; l < a.L; ++l) {
-    const TZ* row = base + (int64_t)l * a.s_zl;
-    const float dtv = softplusf_(to_f32(row[off_dt + h]) + dtb);
+  for (int s0 = tid; s0 < S; s0 += kAT) carry[s0] = 0.f;
+  __syncthreads();
+  for (int l0 = 0; l0 < a.L; l0 += kAT) {
+    const int l = l0 + tid;
+    const bool v = l < a.L;
+    const TZ* row = base + (int64_t)(v ? l : 0) * a.s_zl;
+    float dtv = 0.f;
     const int64_t o = ((int64_t)b * a.L + l) * H + h;
-    if (lane == 0) {
+    if (v) {
+      dtv = softplusf_(to_f32(row[off_dt + h]) + dtb);
       const float A = -fminf(softplusf_(to_f32(row[off_A + h])), -a.A_floor);
       a.DT[o] = dtv;
       a.ADT[o] = A * dtv;
       a.trap[o] = to_f32(row[off_tr + h]);
     }
-    if (lane < S) {
-      ang0 = fmaf(to_f32(row[off_ang + lane]), dtv, ang0);
-      a.angles[o * S + lane] = ang0;
-    }
-    if (lane + 32 < S) {
-      ang1 = fmaf(to_f32(row[off_ang + lane + 32]), dtv, ang1);
-      a.angles[o * S + lane + 32] = ang1;
-    }
-  }
-}
-
-template <typename TZ, typename TO>
-__global__ void __launch_bounds__(128) prologue_bc_kernel(PrologueParams a) {
-  extern __shared__ float psm[];
-  const int b = blockIdx.y, l = blockIdx.x;
-  const int R = a.R, G = a.G, D = a.D, H = a.H, S = a.S;
-  const int RGD = R * G * D;
-  float* raw = psm;              // [2][R][G][D]: B then C
-  float* inv = raw + 2 * RGD;    // [2][R][G]
-  const TZ* row = reinterpret_cast<const TZ*>(a.zx) + (int64_t)b * a.s_zb + (int64_t)l * a.s_zl;
-  const int off_B = 2 * a.d_inner;
-  for (int i = threadIdx.x; i < 2 * RGD; i += blockDim.x) raw[i] = to_f32(row[off_B + i]);
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int j = warp; j < 2 * R * G; j += blockDim.x >> 5) {
-    float ss = 0.f;
-    for (int d = lane; d < D; d += 32) ss = fmaf(raw[j * D + d], raw[j * D + d], ss);
+    for (int s0 = 0; s0 < S; ++s0) {
+      float x = v ? to_f32(row[off_ang + s0]) * dtv : 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) inv[j] = sqrtf(ss / (float)D + a.eps);
-  }
-  __syncthreads();
-  const int half = D / 2, npair = a.split / 2;
-  const int64_t rowo = ((int64_t)b * a.L + l);
-  const float* angr = a.angles + rowo * H * S;
-  // item = (m, r, h, pair): pair k covers d = 2k, 2k + 1
-  const int items = 2 * R * H * half;
-  for (int it = threadIdx.x; it < items; it += blockDim.x) {
-    const int k = it % half;
-    int rest = it / half;
-    const int h = rest % H;
-    rest /= H;
-    const int r = rest % R, m = rest / R;
-    const int g = (int)(((int64_t)h * G) / H);
-    const float* src = raw + ((m * R + r) * G + g) * D;
-    const float rs = inv[(m * R + r) * G + g];
-    const float* w = m ? a.C_norm_w : a.B_norm_w;
-    const float* bias = (m ? a.C_bias : a.B_bias) + ((int64_t)h * R + r) * D;
-    const int d0 = 2 * k, d1 = d0 + 1;
-    float v0 = src[d0] / rs * w[d0] + bias[d0];
-    float v1 = src[d1] / rs * w[d1] + bias[d1];
-    if (k < npair) {
-      float sn, cs;
-      sincosf(angr[h * S + k], &sn, &cs);
-      const float t0 = v0 * cs - v1 * sn;
-      v1 = v0 * sn + v1 * cs;
-      v0 = t0;
+      for (int k = 1; k < 32; k <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, x, k);
+        if (lane >= k) x += y;
+      }
+      if (lane == 31) wsum[warp][s0] = x;
+      __syncthreads();
+      float pre = carry[s0];
+      for (int w = 0; w < warp; ++w) pre += wsum[w][s0];
+      if (v) a.angles[o * S + s0] = pre + x;
+      __syncthreads();
+      if (tid == kAT - 1) carry[s0] = pre + x;
+      // the last thread's total (tile end) becomes the next tile's carry; readers of
+      // carry[s0] for this tile are past the barrier above
     }
-    TO* out = reinterpret_cast<TO*>(m ? a.Cp : a.Bp) + ((rowo * R + r) * H + h) * D;
-    out[d0] = from_f32<TO>(v0);
-    out[d1] = from_f32<TO>(v1);
+    __syncthreads();
   }
 }
 
-template <typename TY, typename TZ, typename TO>
+template <typename TO>
+__device__ __forceinline__ void st_pair(TO* p, float v0, float v1) {
+  p[0] = from_f32<TO>(v0);
+  p[1] = from_f32<TO>(v1);
+}
+template <>
+__device__ __forceinline__ void st_pair<__nv_bfloat16>(__nv_bfloat16* p, float v0, float v1) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v0, v1);
+}
+template <>
+__device__ __forceinline__ void st_pair<float>(float* p, float v0, float v1) {
+  *reinterpret_cast<float2*>(p) = make_float2(v0, v1);
+}
+
+// one warp per (b, l, r): lanes over the pairs (2k, 2k + 1) of d_state (PPL per lane). The
+// group rows of B and C are loaded and normalised once (G == 1) or per head (G == H), then
+// for every head: bias, one sin / cos per pair shared by B and C, rotate, store.
+template <typename TZ, typename TO, int PPL>
+__global__ void __launch_bounds__(256) prologue_bc_kernel(PrologueParams a) {
+  const int R = a.R, G = a.G, D = a.D, H = a.H, S = a.S;
+  const int half = D / 2, npair = a.split / 2, lane = threadIdx.x & 31;
+  const int rowo = blockIdx.x;  // b * L + l
+  const int r = blockIdx.y * 8 + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const int b = rowo / a.L, l = rowo - b * a.L;
+  const TZ* zrow = reinterpret_cast<const TZ*>(a.zx) + (int64_t)b * a.s_zb + (int64_t)l * a.s_zl + 2 * a.d_inner;
+  const int64_t RGD = (int64_t)R * G * D;
+  float wb0[PPL], wb1[PPL], wc0[PPL], wc1[PPL];
+#pragma unroll
+  for (int j = 0; j < PPL; ++j) {
+    const int k = min(lane + 32 * j, half - 1);
+    wb0[j] = a.B_norm_w[2 * k]; wb1[j] = a.B_norm_w[2 * k + 1];
+    wc0[j] = a.C_norm_w[2 * k]; wc1[j] = a.C_norm_w[2 * k + 1];
+  }
+  float b0[PPL], b1[PPL], c0[PPL], c1[PPL];  // normalised group rows
+  for (int h = 0; h < H; ++h) {
+    if (h == 0 || G != 1) {
+      const int g = G == 1 ? 0 : h;
+      const TZ* sb = zrow + (int64_t)(r * G + g) * D;
+      const TZ* sc = sb + RGD;
+      float ssb = 0.f, ssc = 0.f;
+#pragma unroll
+      for (int j = 0; j < PPL; ++j) {
+        const int k = lane + 32 * j;
+        const bool v = k < half;
+        b0[j] = v ? to_f32(sb[2 * k]) : 0.f; b1[j] = v ? to_f32(sb[2 * k + 1]) : 0.f;
+        c0[j] = v ? to_f32(sc[2 * k]) : 0.f; c1[j] = v ? to_f32(sc[2 * k + 1]) : 0.f;
+        ssb = fmaf(b0[j], b0[j], fmaf(b1[j], b1[j], ssb));
+        ssc = fmaf(c0[j], c0[j], fmaf(c1[j], c1[j], ssc));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        ssb += __shfl_xor_sync(0xffffffffu, ssb, o);
+        ssc += __shfl_xor_sync(0xffffffffu, ssc, o);
+      }
+      const float rb = sqrtf(ssb / (float)D + a.eps), rc = sqrtf(ssc / (float)D + a.eps);
+#pragma unroll
+      for (int j = 0; j < PPL; ++j) {
+        b0[j] = b0[j] / rb * wb0[j]; b1[j] = b1[j] / rb * wb1[j];
+        c0[j] = c0[j] / rc * wc0[j]; c1[j] = c1[j] / rc * wc1[j];
+      }
+    }
+    const float* bb = a.B_bias + ((int64_t)h * R + r) * D;
+    const float* cb = a.C_bias + ((int64_t)h * R + r) * D;
+    const float* ang = a.angles + ((int64_t)rowo * H + h) * S;
+    TO* ob = reinterpret_cast<TO*>(a.Bp) + (((int64_t)rowo * R + r) * H + h) * D;
+    TO* oc = reinterpret_cast<TO*>(a.Cp) + (((int64_t)rowo * R + r) * H + h) * D;
+#pragma unroll
+    for (int j = 0; j < PPL; ++j) {
+      const int k = lane + 32 * j;
+      if (k < half) {
+        const int d0 = 2 * k;
+        float x0 = b0[j] + bb[d0], x1 = b1[j] + bb[d0 + 1];
+        float y0 = c0[j] + cb[d0], y1 = c1[j] + cb[d0 + 1];
+        if (k < npair) {
+          float sn, cs;
+          sincosf(ang[k], &sn, &cs);
+          const float t0 = x0 * cs - x1 * sn, u0 = y0 * cs - y1 * sn;
+          x1 = x0 * sn + x1 * cs;
+          y1 = y0 * sn + y1 * cs;
+          x0 = t0;
+          y0 = u0;
+        }
+        st_pair<TO>(ob + d0, x0, x1);
+        st_pair<TO>(oc + d0, y0, y1);
+      }
+    }
+  }
+}
+
+// thread = 8 consecutive elements of one (b, l, h) row (16-byte vectors when VEC)
+template <typename T>
+struct alignas(16) V8 {
+  T e[8];
+};
+
+template <typename TY, typename TZ, typename TO, bool VEC>
 __global__ void __launch_bounds__(256) gate_kernel(GateParams a) {
-  const int64_t n = (int64_t)a.rows * a.P;
+  const int nv = (a.P + 7) / 8;
+  const int64_t n = a.rows * nv;
+  const int LH = a.L * a.H;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / a.P;
-    const int p = (int)(i - r * a.P);
-    const int64_t b = r / ((int64_t)a.L * a.H), rem = r - b * a.L * a.H;
-    const int64_t l = rem / a.H, h = rem - l * a.H;
-    const float y = to_f32(reinterpret_cast<const TY*>(a.y)[b * a.sy.b + l * a.sy.l + h * a.sy.h + p]);
-    const float z = to_f32(reinterpret_cast<const TZ*>(a.z)[b * a.sz.b + l * a.sz.l + h * a.sz.h + p]);
-    reinterpret_cast<TO*>(a.out)[b * a.so.b + l * a.so.l + h * a.so.h + p] = from_f32<TO>(y * (z * sigmoidf_(z)));
+    const int64_t r = i / nv;
+    const int p0 = (int)(i - r * nv) * 8;
+    const int64_t b = r / LH;
+    const int rem = (int)(r - b * LH);
+    const int l = rem / a.H, h = rem - l * a.H;
+    const TY* y = reinterpret_cast<const TY*>(a.y) + b * a.sy.b + (int64_t)l * a.sy.l + (int64_t)h * a.sy.h + p0;
+    const TZ* z = reinterpret_cast<const TZ*>(a.z) + b * a.sz.b + (int64_t)l * a.sz.l + (int64_t)h * a.sz.h + p0;
+    TO* o = reinterpret_cast<TO*>(a.out) + b * a.so.b + (int64_t)l * a.so.l + (int64_t)h * a.so.h + p0;
+    if (VEC) {
+      const V8<TY> yv = *reinterpret_cast<const V8<TY>*>(y);
+      const V8<TZ> zv = *reinterpret_cast<const V8<TZ>*>(z);
+      V8<TO> ov;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float zz = to_f32(zv.e[k]);
+        ov.e[k] = from_f32<TO>(to_f32(yv.e[k]) * (zz * sigmoidf_(zz)));
+      }
+      *reinterpret_cast<V8<TO>*>(o) = ov;
+    } else {
+      for (int k = 0; k < 8 && p0 + k < a.P; ++k) {
+        const float zz = to_f32(z[k]);
+        o[k] = from_f32<TO>(to_f32(y[k]) * (zz * sigmoidf_(zz)));
+      }
+    }
   }
 }
 
@@ -124,18 +202,20 @@ __global__ void __launch_bounds__(256) gate_kernel(GateParams a) {
 
 int launch_prologue(const PrologueParams& p, int zdt, int odt, cudaStream_t s) {
   if (p.S > 64) return fail(M3_ERR_UNSUPPORTED, "prologue: more than 64 rope angles");
-  if (p.D % 2) return fail(M3_ERR_UNSUPPORTED, "prologue: odd d_state");
-  const size_t smem = sizeof(float) * (2 * (size_t)p.R * p.G * p.D + 2 * (size_t)p.R * p.G);
-  if (smem > 48 * 1024) return fail(M3_ERR_UNSUPPORTED, "prologue: B/C rows too wide for shared memory");
-  if (p.L > 65535) return fail(M3_ERR_UNSUPPORTED, "prologue: sequence above 65535");
-  const unsigned ga = (unsigned)((p.Bn * p.H + kWarps - 1) / kWarps);
-  const dim3 gb(p.L, p.Bn);
-#define M3_PRO(TZ, TO)                                                        \
-  do {                                                                        \
-    prologue_angle_kernel<TZ><<<ga, 32 * kWarps, 0, s>>>(p);                  \
-    M3_TRY(check_launch("prologue_angle_kernel"));                            \
-    prologue_bc_kernel<TZ, TO><<<gb, 128, smem, s>>>(p);                      \
-    return check_launch("prologue_bc_kernel");                                \
+  if (p.D % 2 || p.D > 256 || p.R > 8) return fail(M3_ERR_UNSUPPORTED, "prologue: d_state odd or above 256, or rank above 8");
+  const unsigned ga = (unsigned)(p.Bn * p.H);
+  if ((int64_t)p.Bn * p.L > 2147483647LL) return fail(M3_ERR_UNSUPPORTED, "prologue: batch * seqlen too large");
+  const dim3 gb((unsigned)((int64_t)p.Bn * p.L), (unsigned)((p.R + 7) / 8));
+  const int ppl = (p.D / 2 + 31) / 32;
+#define M3_PRO(TZ, TO)                                                                  \
+  do {                                                                                  \
+    prologue_angle_kernel<TZ><<<ga, kAT, 0, s>>>(p);                                    \
+    M3_TRY(check_launch("prologue_angle_kernel"));                                      \
+    const int th = 32 * (p.R < 8 ? p.R : 8);                                            \
+    if (ppl == 1) prologue_bc_kernel<TZ, TO, 1><<<gb, th, 0, s>>>(p);                   \
+    else if (ppl == 2) prologue_bc_kernel<TZ, TO, 2><<<gb, th, 0, s>>>(p);              \
+    else prologue_bc_kernel<TZ, TO, 4><<<gb, th, 0, s>>>(p);                            \
+    return check_launch("prologue_bc_kernel");                                          \
   } while (0)
   if (zdt == M3_BFLOAT16 && odt == M3_BFLOAT16) M3_PRO(__nv_bfloat16, __nv_bfloat16);
   if (zdt == M3_BFLOAT16 && odt == M3_FLOAT32) M3_PRO(__nv_bfloat16, float);
@@ -148,13 +228,20 @@ int launch_prologue(const PrologueParams& p, int zdt, int odt, cudaStream_t s) {
 }
 
 int launch_gate(const GateParams& p, int ydt, int zdt, int odt, cudaStream_t s) {
-  const int64_t n = (int64_t)p.rows * p.P;
+  const int64_t n = p.rows * ((p.P + 7) / 8);
   if (n == 0) return M3_OK;
-  const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 32);
-#define M3_GATE(TY, TZ, TO)                                          \
-  do {                                                               \
-    gate_kernel<TY, TZ, TO><<<grid, 256, 0, s>>>(p);                 \
-    return check_launch("gate_kernel");                              \
+  const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  auto al = [](const void* ptr, const Str3& st, int es) {
+    return (reinterpret_cast<uintptr_t>(ptr) % 16 == 0) && (st.b * es) % 16 == 0 && (st.l * es) % 16 == 0 &&
+           (st.h * es) % 16 == 0;
+  };
+#define M3_GATE(TY, TZ, TO)                                                                          \
+  do {                                                                                               \
+    const bool vec = p.P % 8 == 0 && al(p.y, p.sy, sizeof(TY)) && al(p.z, p.sz, sizeof(TZ)) &&       \
+                     al(p.out, p.so, sizeof(TO));                                                    \
+    if (vec) gate_kernel<TY, TZ, TO, true><<<grid, 256, 0, s>>>(p);                                  \
+    else gate_kernel<TY, TZ, TO, false><<<grid, 256, 0, s>>>(p);                                     \
+    return check_launch("gate_kernel");                                                              \
   } while (0)
   if (ydt == M3_BFLOAT16 && zdt == M3_BFLOAT16 && odt == M3_BFLOAT16) M3_GATE(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
   if (ydt == M3_FLOAT32 && zdt == M3_FLOAT32 && odt == M3_FLOAT32) M3_GATE(float, float, float);
