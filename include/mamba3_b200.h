@@ -101,7 +101,11 @@ int m3_siso_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
 /* SISO scan, backward. The reference has no backward kernel (its CUDA tier drops the
  * gradient; cuda_backend.py:327); this returns the gradients autograd produces through
  * the loop of ops.py:166-175.
- * workspace: f32 buffer of at least m3_siso_scan_bwd_workspace_size() bytes.
+ * workspace: buffer of at least m3_siso_scan_bwd_workspace_size() bytes, 256-byte
+ * aligned. For bf16 inputs with headdim 64 and d_state 128 a workspace of that size lets
+ * the call take the chunked tensor-core path (it recomputes the forward's chunk states
+ * into the workspace first); a workspace of only 4 * batch * nheads * seqlen bytes selects
+ * the CUDA-core path, which every shape supports.
  * dD (H) f32 is overwritten. dh0 / dbx0 optional (B,H,P,D) f32 outputs. */
 size_t m3_siso_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads,
                                        int64_t headdim, int64_t dstate);
@@ -133,6 +137,37 @@ int m3_siso_scan_bwd_noalloc(const m3_tensor* x, const m3_tensor* B, const m3_te
                              const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB, m3_tensor* dC,
                              m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD,
                              m3_tensor* dh0, m3_tensor* dbx0, void* stream);
+
+/* SISO scan with saved chunk states (no counterpart in the reference; replaces the pair
+ * ssm_scan_siso forward / autograd backward of ops.py:145-181 when the forward is run for
+ * training). The forward additionally writes the carried state at the start of every
+ * 128-step chunk (bf16, m3_siso_scan_kstates_size bytes, 256-byte aligned); the backward
+ * reads them instead of recomputing the forward.
+ *   m3_siso_scan_kstates_size  bytes of the state array; 0 when the chunked kernels do not
+ *                              cover the request (then use m3_siso_scan_fwd / _bwd).
+ *                              x_dtype / bc_dtype are m3_dtype codes.
+ *   m3_siso_scan_fwd_kstates   as m3_siso_scan_fwd, plus the state array (output).
+ *   m3_siso_scan_bwd_kstates   as m3_siso_scan_bwd, with the state array of the forward on
+ *                              the same inputs and a workspace of
+ *                              m3_siso_scan_bwd_kstates_workspace_size bytes.
+ * M3_ERR_UNSUPPORTED when the inputs are outside the chunked kernels (dtype, headdim 64,
+ * d_state 128, 16-byte aligned rows). */
+size_t m3_siso_scan_kstates_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                                 int64_t dstate, int x_dtype, int bc_dtype);
+size_t m3_siso_scan_bwd_kstates_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads);
+int m3_siso_scan_fwd_kstates(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                             const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,
+                             const m3_tensor* D, const m3_tensor* h0, const m3_tensor* bx0,
+                             m3_tensor* y, m3_tensor* h_last, m3_tensor* bx_last,
+                             void* kstates, size_t kstates_bytes, void* stream);
+int m3_siso_scan_bwd_kstates(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                             const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,
+                             const m3_tensor* D, const m3_tensor* h0, const m3_tensor* bx0,
+                             const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB, m3_tensor* dC,
+                             m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD,
+                             m3_tensor* dh0, m3_tensor* dbx0, const void* kstates,
+                             size_t kstates_bytes, void* workspace, size_t workspace_bytes,
+                             void* stream);
 
 /* ---------------------------------------------------------------------------------
  * MIMO scan, forward.  Replaces mimo_state_cuda (cuda_backend.py:419-463: einsum ->

@@ -208,17 +208,46 @@ int m3_siso_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
   return launch_siso_fwd_recurrent(p, x->dtype, B->dtype, s);
 }
 
-size_t m3_siso_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
-                                       int64_t dstate) {
-  (void)headdim; (void)dstate;
-  return sizeof(float) * (size_t)(batch * nheads * seqlen);
+// Bytes of the workspace the chunked tensor-core backward needs: the forward's chunk states
+// (recomputed inside m3_siso_scan_bwd) followed by three per-position scratch arrays.
+static size_t chunked_bwd_ws_bytes(int64_t Bn, int64_t L, int64_t H) {
+  const size_t ks = (siso_chunk_kstate_bytes(Bn, L, H) + 255) & ~size_t(255);
+  return ks + siso_chunk_bwd_scratch_bytes(Bn, L, H);
 }
 
-int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
-                     const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* h0,
-                     const m3_tensor* bx0, const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB, m3_tensor* dC,
-                     m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dh0,
-                     m3_tensor* dbx0, void* workspace, size_t workspace_bytes, void* stream) {
+size_t m3_siso_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                                       int64_t dstate) {
+  const size_t rec = sizeof(float) * (size_t)(batch * nheads * seqlen);
+  // headdim 64 / d_state 128 may take the chunked path (bf16); size for it
+  if (headdim == 64 && dstate == 128) {
+    const size_t ch = chunked_bwd_ws_bytes(batch, seqlen, nheads);
+    return ch > rec ? ch : rec;
+  }
+  return rec;
+}
+
+size_t m3_siso_scan_kstates_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                                 int64_t dstate, int x_dtype, int bc_dtype) {
+  if (headdim != 64 || dstate != 128 || x_dtype != M3_BFLOAT16 || bc_dtype != M3_BFLOAT16 || seqlen <= 0 ||
+      batch * nheads <= 0)
+    return 0;
+  return siso_chunk_kstate_bytes(batch, seqlen, nheads);
+}
+
+size_t m3_siso_scan_bwd_kstates_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads) {
+  return siso_chunk_bwd_scratch_bytes(batch, seqlen, nheads);
+}
+
+namespace m3 {
+namespace {
+// Shared argument checks and parameter fill of the SISO backward entries. Returns M3_OK
+// with *done set when nothing is left to launch (empty shapes).
+int prep_siso_bwd(SisoParams& p, const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                  const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* h0,
+                  const m3_tensor* bx0, const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB, m3_tensor* dC,
+                  m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dh0,
+                  m3_tensor* dbx0, cudaStream_t s, bool* done) {
+  *done = false;
   int64_t Bn, L, H, P, Ds, R;
   M3_TRY(check_scan_inputs(x, B, C, ADT, DT, trap, D, 4, &Bn, &L, &H, &P, &Ds, &R));
   const bool empty = Bn * L * H * P == 0;
@@ -235,18 +264,21 @@ int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
   M3_TRY(check(dD, "dD", 1, hs, kF32, true, false, false));
   M3_TRY(check(dh0, "dh0", 4, st, kF32, true, true, false));
   M3_TRY(check(dbx0, "dbx0", 4, st, kF32, true, true, false));
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   M3_TRY(memset_async(dD->data, sizeof(float) * H, s, "dD"));
-  if (Bn * H * P * Ds == 0) return M3_OK;
+  if (Bn * H * P * Ds == 0) {
+    *done = true;
+    return M3_OK;
+  }
   if (L == 0) {
     const size_t bytes = sizeof(float) * Bn * H * P * Ds;
     M3_TRY(copy_or_zero(fptr<void>(dh0), nullptr, bytes, s, "dh0"));
-    return copy_or_zero(fptr<void>(dbx0), nullptr, bytes, s, "dbx0");
+    M3_TRY(copy_or_zero(fptr<void>(dbx0), nullptr, bytes, s, "dbx0"));
+    *done = true;
+    return M3_OK;
   }
-  const size_t need = m3_siso_scan_bwd_workspace_size(Bn, L, H, P, Ds);
-  if (workspace == nullptr || workspace_bytes < need)
-    return fail(M3_ERR_WORKSPACE, "siso backward: workspace of " + std::to_string(need) + " bytes required");
-  SisoParams p{};
+  if (Bn > INT32_MAX || L > INT32_MAX || H > INT32_MAX || P > 65535)
+    return fail(M3_ERR_UNSUPPORTED, "siso scan: dimension too large");
+  p = SisoParams{};
   p.Bn = (int)Bn; p.L = (int)L; p.H = (int)H; p.P = (int)P; p.D = (int)Ds;
   p.x = x->data; p.sx = s3(x);
   p.Bm = B->data; p.sB = s3(B);
@@ -265,8 +297,100 @@ int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
   p.dtrap = fptr<float>(dtrap); p.sdtrap = s3_scal(dtrap);
   p.dD = fptr<float>(dD);
   p.dh0 = fptr<float>(dh0); p.dbx0 = fptr<float>(dbx0);
+  return M3_OK;
+}
+}  // namespace
+}  // namespace m3
+
+int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                     const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* h0,
+                     const m3_tensor* bx0, const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB, m3_tensor* dC,
+                     m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dh0,
+                     m3_tensor* dbx0, void* workspace, size_t workspace_bytes, void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  SisoParams p;
+  bool done = false;
+  M3_TRY(prep_siso_bwd(p, x, B, C, ADT, DT, trap, D, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0, s,
+                       &done));
+  if (done) return M3_OK;
+  const size_t need = sizeof(float) * (size_t)p.Bn * p.H * p.L;
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(M3_ERR_WORKSPACE, "siso backward: workspace of " + std::to_string(need) + " bytes required");
+  // chunked tensor-core path: recompute the forward's chunk states into the workspace, then
+  // the reverse-chunk kernel (taken when the workspace has room for both)
+  if (siso_chunk_bwd_supported(p, x->dtype, B->dtype) && workspace_bytes >= chunked_bwd_ws_bytes(p.Bn, p.L, p.H) &&
+      (reinterpret_cast<uintptr_t>(workspace) & 255) == 0) {
+    const size_t ks = (siso_chunk_kstate_bytes(p.Bn, p.L, p.H) + 255) & ~size_t(255);
+    SisoParams f = p;
+    f.y = nullptr; f.sy = Str3{0, 0, 0};
+    f.h_last = nullptr; f.bx_last = nullptr;
+    f.kstates = workspace;
+    M3_TRY(launch_siso_fwd_chunked(f, x->dtype, B->dtype, s));
+    p.kstates = workspace;
+    return launch_siso_bwd_chunked(p, reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ks), s);
+  }
   p.q = reinterpret_cast<float*>(workspace);
   return launch_siso_bwd_recurrent(p, x->dtype, B->dtype, s);
+}
+
+int m3_siso_scan_fwd_kstates(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                             const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* h0,
+                             const m3_tensor* bx0, m3_tensor* y, m3_tensor* h_last, m3_tensor* bx_last,
+                             void* kstates, size_t kstates_bytes, void* stream) {
+  int64_t Bn, L, H, P, Ds, R;
+  M3_TRY(check_scan_inputs(x, B, C, ADT, DT, trap, D, 4, &Bn, &L, &H, &P, &Ds, &R));
+  const size_t need = m3_siso_scan_kstates_size(Bn, L, H, P, Ds, x->dtype, B->dtype);
+  if (need == 0) return fail(M3_ERR_UNSUPPORTED, "siso scan: no chunk states for this shape / dtype");
+  if (kstates == nullptr || kstates_bytes < need || (reinterpret_cast<uintptr_t>(kstates) & 255) != 0)
+    return fail(M3_ERR_WORKSPACE, "siso scan: kstates of " + std::to_string(need) + " bytes (256-byte aligned) required");
+  const int64_t xs[4] = {Bn, L, H, P}, st[4] = {Bn, H, P, Ds};
+  M3_TRY(check(y, "y", 4, xs, 1u << x->dtype, false, false, true));
+  M3_TRY(check(h0, "h0", 4, st, kF32, true, true, false));
+  M3_TRY(check(bx0, "bx0", 4, st, kF32, true, true, false));
+  M3_TRY(check(h_last, "h_last", 4, st, kF32, true, true, false));
+  M3_TRY(check(bx_last, "bx_last", 4, st, kF32, true, true, false));
+  if (Bn > INT32_MAX || L > INT32_MAX || H > INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "siso scan: dimension too large");
+  SisoParams p{};
+  p.Bn = (int)Bn; p.L = (int)L; p.H = (int)H; p.P = (int)P; p.D = (int)Ds;
+  p.x = x->data; p.sx = s3(x);
+  p.Bm = B->data; p.sB = s3(B);
+  p.Cm = C->data; p.sC = s3(C);
+  p.adt = fptr<const float>(ADT); p.sadt = s3_scal(ADT);
+  p.dt = fptr<const float>(DT); p.sdt = s3_scal(DT);
+  p.trap = fptr<const float>(trap); p.strap = s3_scal(trap);
+  p.Dskip = fptr<const float>(D); p.sD = D->stride[0];
+  p.h0 = fptr<const float>(h0); p.bx0 = fptr<const float>(bx0);
+  p.y = y->data; p.sy = s3(y);
+  p.h_last = fptr<float>(h_last); p.bx_last = fptr<float>(bx_last);
+  p.kstates = kstates;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (!siso_chunk_supported(p, x->dtype, B->dtype))
+    return fail(M3_ERR_UNSUPPORTED, "siso scan: inputs not eligible for the chunked kernel (alignment / strides)");
+  return launch_siso_fwd_chunked(p, x->dtype, B->dtype, s);
+}
+
+int m3_siso_scan_bwd_kstates(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                             const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* h0,
+                             const m3_tensor* bx0, const m3_tensor* dy, m3_tensor* dx, m3_tensor* dB,
+                             m3_tensor* dC, m3_tensor* dADT, m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD,
+                             m3_tensor* dh0, m3_tensor* dbx0, const void* kstates, size_t kstates_bytes,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  SisoParams p;
+  bool done = false;
+  M3_TRY(prep_siso_bwd(p, x, B, C, ADT, DT, trap, D, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0, s,
+                       &done));
+  if (done) return M3_OK;
+  const size_t kneed = m3_siso_scan_kstates_size(p.Bn, p.L, p.H, p.P, p.D, x->dtype, B->dtype);
+  if (kneed == 0 || !siso_chunk_bwd_supported(p, x->dtype, B->dtype))
+    return fail(M3_ERR_UNSUPPORTED, "siso backward: inputs not eligible for the chunked kernel");
+  if (kstates == nullptr || kstates_bytes < kneed || (reinterpret_cast<uintptr_t>(kstates) & 255) != 0)
+    return fail(M3_ERR_INVALID_ARGUMENT, "siso backward: kstates of " + std::to_string(kneed) + " bytes required");
+  const size_t need = siso_chunk_bwd_scratch_bytes(p.Bn, p.L, p.H);
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15) != 0)
+    return fail(M3_ERR_WORKSPACE, "siso backward: workspace of " + std::to_string(need) + " bytes required");
+  p.kstates = const_cast<void*>(kstates);
+  return launch_siso_bwd_chunked(p, reinterpret_cast<float*>(workspace), s);
 }
 
 // Device address of g_noalloc_scratch, looked up once per device with that device
@@ -596,7 +720,11 @@ int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* w
 
 int m3_device_timeouts(int reset, int* flag_out) {
   if (!flag_out) return fail(M3_ERR_INVALID_ARGUMENT, "flag_out: missing");
-  return chunk_error_word(reset != 0, flag_out);
+  int f = 0, b = 0;
+  M3_TRY(chunk_error_word(reset != 0, &f));
+  M3_TRY(chunk_bwd_error_word(reset != 0, &b));
+  *flag_out = f | b;
+  return M3_OK;
 }
 
 

@@ -127,6 +127,7 @@ struct ChunkArgs {
   __nv_bfloat16* y; Str3 sy;
   float* h_last;
   float* bx_last;
+  __nv_bfloat16* kst;  // optional: bf16 k_c^T of every chunk, [unit][chunk][d][p]
 };
 
 __device__ __forceinline__ uint32_t lane_addr(uint32_t base, int warp, uint32_t col) {
@@ -453,7 +454,7 @@ __device__ __forceinline__ void epilogue(const ChunkArgs& a, Smem& s, uint32_t t
     for (int e = 0; e < 8; ++e)
       outp[e] = pack_bf16(fmaf(sc, __uint_as_float(y1[2 * e]), __uint_as_float(y2[2 * e])),
                           fmaf(sc, __uint_as_float(y1[2 * e + 1]), __uint_as_float(y2[2 * e + 1])));
-    if (valid) {
+    if (valid && a.y) {
       dst[2 * qt] = make_uint4(outp[0], outp[1], outp[2], outp[3]);
       dst[2 * qt + 1] = make_uint4(outp[4], outp[5], outp[6], outp[7]);
     }
@@ -555,6 +556,17 @@ __device__ __forceinline__ void store_final(const ChunkArgs& a, const Smem& s, i
 }
 
 
+// chunk-start state row d (bf16, plain [d][p] rows of 128 B) for the backward
+__device__ __forceinline__ void store_kstate(const ChunkArgs& a, const ChunkPos& cp, int nch, int d,
+                                             const float (&k)[kP]) {
+  const int64_t u = (int64_t)cp.b * a.H + cp.h;
+  uint4* dst = reinterpret_cast<uint4*>(a.kst + (((u * nch + cp.c) * kD) + d) * kP);
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc)
+    dst[cc] = make_uint4(pack_bf16(k[8 * cc + 0], k[8 * cc + 1]), pack_bf16(k[8 * cc + 2], k[8 * cc + 3]),
+                         pack_bf16(k[8 * cc + 4], k[8 * cc + 5]), pack_bf16(k[8 * cc + 6], k[8 * cc + 7]));
+}
+
 // k = dec * k + dK, read in quarters
 __device__ __forceinline__ void add_dk(uint32_t tbase, int warp, float dec, float (&k)[kP]) {
 #pragma unroll
@@ -604,6 +616,7 @@ __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, i
     write_kbuf(s, d, k);
     fence_proxy_async_smem();
     mbar_arrive(&s.k_ready);
+    if (a.kst) store_kstate(a, cp, nch, d, k);
     prev_dec = sl.decay_end;
     prev_last = cp.last;
     prev_b = cp.b;
@@ -882,6 +895,12 @@ int num_sms() {
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 chunk_encode_fn() { return get_encode(); }
+int chunk_tmap_4d(CUtensorMap* m, const void* base, int64_t inner, int64_t H, int64_t L, int64_t Bn, const Str3& st) {
+  return make_map(m, base, inner, H, L, Bn, st);
+}
+int chunk_sm_count() { return num_sms(); }
+
 bool siso_chunk_supported(const SisoParams& p, int xdt, int bcdt) {
   if (xdt != M3_BFLOAT16 || bcdt != M3_BFLOAT16) return false;
   if (p.P != kP || (p.D != kD && p.D != 64)) return false;
@@ -922,6 +941,7 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
   a.h0 = p.h0; a.bx0 = p.bx0;
   a.y = reinterpret_cast<__nv_bfloat16*>(p.y); a.sy = p.sy;
   a.h_last = p.h_last; a.bx_last = p.bx_last;
+  a.kst = reinterpret_cast<__nv_bfloat16*>(p.kstates);
   const size_t smem = sizeof(Smem) + 1024;
   static bool attr_set = false;
   if (!attr_set) {

@@ -38,6 +38,9 @@ struct SisoParams {
   float* dh0;        // (B,H,P,D) or null
   float* dbx0;
   float* q;          // workspace (B,H,L): <dy_t, C_t h_t>
+  // chunked tensor-core path only: bf16 k_c^T [d][p] of every 128-step chunk, per (b, h)
+  // unit in chunk order (written by the forward, read by the backward)
+  void* kstates;
 };
 
 // Launchers (siso_scan.cu). xdt / bcdt are m3_dtype codes.

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(_HERE, "libmamba3_b200.so")
 MAX_DIMS = 6
 
 M3_FLOAT32, M3_BFLOAT16, M3_FLOAT16 = 0, 1, 2
+M3_OK, M3_ERR_INVALID_ARGUMENT, M3_ERR_UNSUPPORTED, M3_ERR_CUDA, M3_ERR_WORKSPACE = 0, 1, 2, 3, 4
 _DTYPE_CODE = {torch.float32: M3_FLOAT32, torch.bfloat16: M3_BFLOAT16, torch.float16: M3_FLOAT16}
 _STATUS = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "workspace"}
 
@@ -57,6 +58,11 @@ _SIGS = {
     "m3_siso_scan_bwd_workspace_size": ([ctypes.c_int64] * 5, ctypes.c_size_t),
     "m3_siso_scan_bwd": ([_P] * 19 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "m3_siso_scan_bwd_noalloc": ([_P] * 19 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_siso_scan_kstates_size": ([ctypes.c_int64] * 5 + [ctypes.c_int, ctypes.c_int], ctypes.c_size_t),
+    "m3_siso_scan_bwd_kstates_workspace_size": ([ctypes.c_int64] * 3, ctypes.c_size_t),
+    "m3_siso_scan_fwd_kstates": ([_P] * 12 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+    "m3_siso_scan_bwd_kstates": ([_P] * 19 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+                                              ctypes.c_void_p], ctypes.c_int),
     "m3_mimo_scan_fwd": ([_P] * 14 + [ctypes.c_void_p], ctypes.c_int),
     "m3_mimo_scan_fwd_workspace_size": ([ctypes.c_int64] * 4, ctypes.c_size_t),
     "m3_mimo_scan_fwd_ws": ([_P] * 14 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),

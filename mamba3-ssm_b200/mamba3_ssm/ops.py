@@ -115,8 +115,24 @@ class _SisoScanFn(torch.autograd.Function):
             hl = _empty((Bn, H, P, Ds), torch.float32, x.device)
             bl = _empty((Bn, H, P, Ds), torch.float32, x.device)
         a = L.pack(x, B, C, ADT, DT, trap, D, h0, bx0, y, hl, bl)
+        # when gradients will be needed and the chunked kernels cover the shape, keep the
+        # chunk-start states of the forward for the backward instead of recomputing them
+        ks = None
+        if any(ctx.needs_input_grad[:9]):
+            nb = lib.m3_siso_scan_kstates_size(Bn, Ln, H, P, Ds, L._DTYPE_CODE.get(x.dtype, -1),
+                                               L._DTYPE_CODE.get(B.dtype, -1))
+            if nb:
+                ks = torch.empty(int(nb), dtype=torch.uint8, device=x.device)
         with torch.cuda.device(x.device):
-            L.check(lib.m3_siso_scan_fwd(*a.ptrs, L.stream_of(x)), "m3_siso_scan_fwd")
+            if ks is not None:
+                rc = lib.m3_siso_scan_fwd_kstates(*a.ptrs, ks.data_ptr(), ks.numel(), L.stream_of(x))
+                if rc == L.M3_ERR_UNSUPPORTED:
+                    ks = None  # e.g. unaligned strided views: the plain forward below
+                else:
+                    L.check(rc, "m3_siso_scan_fwd_kstates")
+            if ks is None:
+                L.check(lib.m3_siso_scan_fwd(*a.ptrs, L.stream_of(x)), "m3_siso_scan_fwd")
+        ctx.kstates = ks
         ctx.save_for_backward(x, B, C, ADT, DT, trap, D, h0, bx0)
         ctx.mark_non_differentiable(*[t for t in (hl, bl) if t is not None])
         return y, hl, bl
@@ -140,13 +156,25 @@ class _SisoScanFn(torch.autograd.Function):
         dD = _empty((H,), torch.float32, dev)
         dh0 = _empty(h0.shape, torch.float32, dev) if (h0 is not None and ctx.needs_input_grad[7]) else None
         dbx0 = _empty(bx0.shape, torch.float32, dev) if (bx0 is not None and ctx.needs_input_grad[8]) else None
-        nbytes = lib.m3_siso_scan_bwd_workspace_size(Bn, Ln, H, P, Ds)
-        ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
         a = L.pack(x, B, C, ADT, DT, trap, D, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD,
                     dh0, dbx0)
+        ks = ctx.kstates
+        ctx.kstates = None
         with torch.cuda.device(dev):
-            L.check(lib.m3_siso_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)),
-                    "m3_siso_scan_bwd")
+            rc = None
+            if ks is not None:
+                nbytes = lib.m3_siso_scan_bwd_kstates_workspace_size(Bn, Ln, H)
+                ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
+                rc = lib.m3_siso_scan_bwd_kstates(*a.ptrs, ks.data_ptr(), ks.numel(), ws.data_ptr(),
+                                                  ws.numel(), L.stream_of(x))
+                if rc != L.M3_ERR_UNSUPPORTED:  # e.g. an unaligned dy view: the general path
+                    L.check(rc, "m3_siso_scan_bwd_kstates")
+                del ws
+            if ks is None or rc == L.M3_ERR_UNSUPPORTED:
+                nbytes = lib.m3_siso_scan_bwd_workspace_size(Bn, Ln, H, P, Ds)
+                ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
+                L.check(lib.m3_siso_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)),
+                        "m3_siso_scan_bwd")
         return dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0, None
 
 

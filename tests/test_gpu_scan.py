@@ -272,3 +272,95 @@ def test_mimo_chunked_backward_with_states(L, R, D, P):
         assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < 5e-4, k
     assert rel_err(h0.grad.double().cpu().numpy(), go["dh0"]) < 5e-4
     assert rel_err(b0.grad.double().cpu().numpy(), go["dbx0"]) < 5e-4
+
+
+def _siso_grads(ins, h0=None, b0=None):
+    from mamba3_ssm import ssm_scan_siso
+    from mamba3_ssm.ops import ssm_scan_siso_states
+    if h0 is None:
+        y = ssm_scan_siso(*ins)
+    else:
+        y, _, _ = ssm_scan_siso_states(*ins, h0, b0)
+    torch.manual_seed(1)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    return y, dy
+
+
+@pytest.mark.parametrize("L", [1, 77, 128, 129, 300, 700])
+@pytest.mark.parametrize("states", [False, True])
+def test_siso_bf16_chunked_backward_against_oracle(L, states):
+    """The chunked tensor-core backward (bf16, headdim 64, d_state 128; the forward keeps its
+    chunk-start states for it) on ragged lengths, with and without initial states, against
+    the float64 adjoint of the loop."""
+    Bn = 2 if L <= 300 else 1
+    arrs, t = _inputs(500 + L, Bn, L, 2, 64, 128, dtype=torch.bfloat16)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D")
+    ins = [t[k].requires_grad_(True) for k in keys]
+    h0 = b0 = None
+    if states:
+        rng = np.random.default_rng(L)
+        h0 = torch.tensor(rng.standard_normal((Bn, 2, 64, 128)), dtype=torch.float32, device=DEV).requires_grad_(True)
+        b0 = torch.tensor(rng.standard_normal((Bn, 2, 64, 128)), dtype=torch.float32, device=DEV).requires_grad_(True)
+    y, dy = _siso_grads(ins, h0, b0)
+    npy = lambda v: None if v is None else v.detach().double().cpu().numpy()
+    go = O.siso_scan_bwd(*[arrs[k] for k in keys], npy(dy), npy(h0), npy(b0))
+    for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
+        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
+        assert rel_err(npy(tt.grad), go[k]) < 2e-2 * f, k
+    if states:
+        assert rel_err(npy(h0.grad), go["dh0"]) < 2e-2
+        assert rel_err(npy(b0.grad), go["dbx0"]) < 2e-2
+
+
+@pytest.mark.parametrize("case", ["strong_decay", "mixed_sign"])
+def test_siso_bf16_chunked_backward_extreme_decay(case):
+    """Per-step decays whose in-chunk products leave the fp32 range (ADT down to -13) and
+    isolated growth steps (ADT up to +0.7) through the chunked backward."""
+    arrs, t = _inputs(11 if case == "strong_decay" else 12, 1, 300, 2, 64, 128, dtype=torch.bfloat16)
+    rng = np.random.default_rng(5)
+    if case == "strong_decay":
+        adt = -rng.uniform(0.0, 13.0, arrs["ADT"].shape)
+    else:
+        adt = -rng.uniform(0.0, 3.0, arrs["ADT"].shape)
+        grow = rng.random(adt.shape) < 0.05
+        adt[grow] = rng.uniform(0.0, 0.7, grow.sum())
+    t["ADT"] = torch.tensor(adt, dtype=torch.float32, device=DEV)
+    arrs["ADT"] = t["ADT"].double().cpu().numpy()
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D")
+    ins = [t[k].requires_grad_(True) for k in keys]
+    y, dy = _siso_grads(ins)
+    go = O.siso_scan_bwd(*[arrs[k] for k in keys], dy.detach().double().cpu().numpy())
+    for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
+        g = tt.grad.detach().double().cpu().numpy()
+        assert np.isfinite(g).all(), k
+        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
+        assert rel_err(g, go[k]) < 2e-2 * f, k
+
+
+def test_siso_bwd_entry_points_agree():
+    """The three ways into the SISO backward on one bf16 problem: the state-carrying pair
+    (autograd), m3_siso_scan_bwd with a full workspace (chunk states recomputed) and with
+    the minimal workspace (CUDA-core path)."""
+    from mamba3_ssm import _lib as L
+    Bn, Ln, H = 2, 333, 3
+    arrs, t = _inputs(77, Bn, Ln, H, 64, 128, dtype=torch.bfloat16)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D")
+    ins = [t[k].requires_grad_(True) for k in keys]
+    y, dy = _siso_grads(ins)
+    ref = [tt.grad.detach().clone() for tt in ins]
+    lib = L.load()
+    for ws_bytes in (lib.m3_siso_scan_bwd_workspace_size(Bn, Ln, H, 64, 128), 4 * Bn * Ln * H):
+        outs = [torch.empty_like(t["x"]), torch.empty_like(t["B"]), torch.empty_like(t["C"]),
+                torch.empty_like(t["ADT"]), torch.empty_like(t["DT"]), torch.empty_like(t["trap"]),
+                torch.empty(H, device=DEV)]
+        ws = torch.empty(int(ws_bytes), dtype=torch.uint8, device=DEV)
+        a = L.pack(*[t[k].detach() for k in keys], None, None, dy, *outs, None, None)
+        rc = lib.m3_siso_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+        L.check(rc, "m3_siso_scan_bwd")
+        torch.cuda.synchronize()
+        for k, o, r in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), outs, ref):
+            # same chunked kernels: equal up to the order of the dD atomics; the CUDA-core
+            # path: within the bf16 bar
+            tol = 1e-5 if ws_bytes > 4 * Bn * Ln * H else 2e-2 * (5 if k in ("dADT", "dDT", "dtrap", "dD") else 1)
+            assert rel_err(o.double().cpu().numpy(), r.double().cpu().numpy()) < tol, (k, ws_bytes)
