@@ -54,14 +54,22 @@ constexpr int kThreads = 512;
 constexpr uint32_t kTile = Q * 64 * 2;  // one SW128 tile: 128 rows x 128 B
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kSafeExp2 = 120.f;  // split-exponent factors stay within fp32 below 2^120
 
 // TMEM columns. Phase 1: G, S, Y1, dK, T. Phase 2 writes U, dC, dB over G / S / Y1 (read
 // by then); T stays for the phase-2 epilogue; dK is read by the state warps.
 constexpr uint32_t kColG = 0, kColS = 128, kColY1 = 256, kColDK = 320, kColT = 448;
 constexpr uint32_t kColU = 0, kColDC = 64, kColDB = 192;
+// dY rows as packed bf16 pairs (32 columns), copied by the phase-1 epilogue so that the dY
+// tile is free for the next chunk once phase 2 has read it
+constexpr uint32_t kColDY = 384;
 
 struct __align__(16) BScal {
   float lam2[Q + 4];  // lambda_i log2(e), i = 0..Q
+  float lnx[Q];       // lam2[i + 1] (aligned for vector reads by column)
+  float colf[Q];      // e^{lambda_{32b+1} - lambda_{j+1}}, b = j / 32 (split decay, column part)
+  float colfm[Q];     // colf[j] mu[j]
+  float lref[4];      // lam2[32 b + 1]
   float mu[Q];
   float beta[Q];
   float anext[Q];     // a_{i+1}
@@ -71,7 +79,8 @@ struct __align__(16) BScal {
   float dskip;
   float a0, g0;       // a and gamma of the chunk's first row (initial-state gradients)
   int n;              // valid rows
-  int pad[3];
+  int flags;          // bit b: block b takes the split-exponent path
+  int pad[2];
 };
 
 struct __align__(1024) BSmem {
@@ -89,7 +98,7 @@ struct __align__(1024) BSmem {
   float gdiag[Q], sdiag[Q];
   float red[4];
   uint64_t ld_full, dy_full, sc_full[2], sc_empty[2], edy_ready, dkn_ready;
-  uint64_t p1_done, ep1_done, p2_done, ep2_done, st_sync;
+  uint64_t p1_done, p1b_done, ep1_done, p2_done, ep2_done, st_sync, xread;
   uint32_t tmem_base;
 };
 
@@ -97,6 +106,8 @@ static_assert(sizeof(BSmem) + 1024 <= 232448, "shared memory budget");
 
 // consumers of a scalar slot: e^lambda o dY writers, epilogues, state warps
 constexpr uint32_t kScalReaders = 64 + 256 + 128;
+// arrivals that complete the phase-1 epilogue: the epilogue threads and the w o X writers
+constexpr uint32_t kEp1Arrivals = 256 + 64;
 
 __device__ int g_bwd_error;  // set when a bounded wait gives up
 
@@ -147,6 +158,17 @@ __device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// The control thread's waits: polling, so that it resumes as soon as the phase completes
+// (a suspended try_wait can resume late); bounded like bwait.
+__device__ __forceinline__ bool cwait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if (i > 64) __nanosleep(20);
+  }
+  atomicExch(&g_bwd_error, 1);
+  return false;
+}
+
 __device__ __forceinline__ float ld_scal(const float* p, const Str3& s, int b, int t, int h) {
   return p[(int64_t)b * s.b + (int64_t)t * s.l + (int64_t)h * s.h];
 }
@@ -165,7 +187,7 @@ __device__ __forceinline__ float2 bf2(uint32_t v) {
 // ------------------------------------------------------------------------------------
 // warp 1: per-chunk scalars, rows i = lane + 32 k, plus row Q (the next chunk's first)
 // ------------------------------------------------------------------------------------
-__device__ void scalar_role(const BwdArgs& a, BSmem& s, int G, int lane) {
+__device__ __forceinline__ void scalar_role(const BwdArgs& a, BSmem& s, int G, int lane) {
   for (int g = 0; g < G; ++g) {
     const int q = g & 1;
     const BPos cp = bpos(a, g);
@@ -224,12 +246,41 @@ __device__ void scalar_role(const BwdArgs& a, BSmem& s, int G, int lane) {
       gn[k] = lane < 31 ? g1 : gw;
       ln[k] = lane < 31 ? l1 : lw;
     }
+    // Split decay of the mask, per 32-column block b with reference lam2[32b+1]:
+    // E_ij = e^{lambda_i - lambda_{32b+1}} e^{lambda_{32b+1} - lambda_{j+1}}. A block is
+    // factorised when its column exponents and the row exponents of rows i >= 32b stay
+    // below 2^120; otherwise its elements take one exp2 each.
+    float ref[4], lmax[4];
+    int flags = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      ref[k] = __shfl_sync(0xffffffffu, lam[k], 1);
+      float cm = ref[k] - ln[k], lm = lam[k];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+        lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, o));
+      }
+      lmax[k] = lm;
+      if (cm <= kSafeExp2) flags |= 1 << k;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float rm = lmax[k];
+#pragma unroll
+      for (int k2 = k + 1; k2 < 4; ++k2) rm = fmaxf(rm, lmax[k2]);
+      if (!(rm - ref[k] <= kSafeExp2)) flags &= ~(1 << k);
+    }
     if (!bwait(&s.sc_empty[q], ((g >> 1) & 1) ^ 1)) return;
     BScal& sl = s.sc[q];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int j = lane + 32 * k;
       sl.lam2[j] = lam[k];
+      sl.lnx[j] = ln[k];
+      const float cf = exp2f(ref[k] - ln[k]);
+      sl.colf[j] = cf;
+      sl.colfm[j] = cf * fmaf(an[k], be[k], gn[k]);
       sl.mu[j] = fmaf(an[k], be[k], gn[k]);
       sl.beta[j] = be[k];
       sl.anext[j] = an[k];
@@ -243,40 +294,63 @@ __device__ void scalar_role(const BwdArgs& a, BSmem& s, int G, int lane) {
       sl.a0 = av[0];
       sl.g0 = ga[0];
       sl.n = cp.n;
+      sl.flags = flags;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sl.lref[k] = ref[k];
     }
     mbar_arrive(&s.sc_full[q]);
   }
 }
 
 // ------------------------------------------------------------------------------------
-// warps 2-3: e^{lambda_i} dY_i for the dK^T and dC MMAs (thread e: rows e and e + 64).
-// dY(g) lands only after the phase-2 epilogue of g-1, so e^lambda o dY(g-1) has been read.
+// e^{lambda_r} dY_r for the dK^T and dC MMAs, row r (the phase-2 epilogue threads of half 1
+// write the next chunk's rows once its dY has landed)
 // ------------------------------------------------------------------------------------
-__device__ void edy_role(BSmem& s, int G, int e) {
+__device__ __forceinline__ void write_edy_row(BSmem& s, const BScal& sl, int r) {
+  const float f = sl.el[r];
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc) {
+    const uint4 v = *reinterpret_cast<const uint4*>(s.dy + sw128_off(r, 8 * cc));
+    const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int z = 0; z < 4; ++z) {
+      const float2 f2 = bf2(vv[z]);
+      o[z] = pack_bf16(f2.x * f, f2.y * f);
+    }
+    *reinterpret_cast<uint4*>(s.edy + sw128_off(r, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// warps 2-3: w o X in place of X (thread e: rows e and e + 64) for the dB MMA of phase 2,
+// once S (phase 1) is complete and the epilogue threads have taken their X rows
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void wx_role(BSmem& s, int G, int e) {
   for (int g = 0; g < G; ++g) {
     const int q = g & 1;
     if (!bwait(&s.sc_full[q], (g >> 1) & 1)) return;
-    if (!bwait(&s.dy_full, g & 1)) return;
+    if (!bwait(&s.xread, g & 1)) return;
     const BScal& sl = s.sc[q];
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
       const int r = e + 64 * rr;
-      const float f = sl.el[r];
+      const float wi = sl.wdec[r] * sl.mu[r];
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
-        const uint4 v = *reinterpret_cast<const uint4*>(s.dy + sw128_off(r, 8 * cc));
+        const uint4 v = *reinterpret_cast<const uint4*>(s.x + sw128_off(r, 8 * cc));
         const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
         uint32_t o[4];
 #pragma unroll
         for (int z = 0; z < 4; ++z) {
-          const float2 f2 = bf2(vv[z]);
-          o[z] = pack_bf16(f2.x * f, f2.y * f);
+          const float2 f = bf2(vv[z]);
+          o[z] = pack_bf16(f.x * wi, f.y * wi);
         }
-        *reinterpret_cast<uint4*>(s.edy + sw128_off(r, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(s.x + sw128_off(r, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
     fence_proxy_async_smem();
-    mbar_arrive(&s.edy_ready);
+    mbar_arrive(&s.ep1_done);
     mbar_arrive(&s.sc_empty[q]);
   }
 }
@@ -293,17 +367,63 @@ __device__ __forceinline__ void zero_block(uint8_t* t, int i, int c0) {
   for (int cc = 0; cc < 4; ++cc) *reinterpret_cast<uint4*>(t + sw128_off(i, c0 + 8 * cc)) = make_uint4(0u, 0u, 0u, 0u);
 }
 
-__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_t (&r)[32]) {
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
+// 32 fp32 values -> bf16 at columns c0 .. c0 + 31 of row i of a SW128 staging tile
+__device__ __forceinline__ void stage_row_bf16(uint8_t* tile, int i, int c0, const uint32_t (&r)[32]) {
 #pragma unroll
   for (int cc = 0; cc < 4; ++cc)
-    d4[cc] = make_uint4(pack_bf16(__uint_as_float(r[8 * cc + 0]), __uint_as_float(r[8 * cc + 1])),
+    *reinterpret_cast<uint4*>(tile + sw128_off(i, c0 + 8 * cc)) = make_uint4(pack_bf16(__uint_as_float(r[8 * cc + 0]), __uint_as_float(r[8 * cc + 1])),
                         pack_bf16(__uint_as_float(r[8 * cc + 2]), __uint_as_float(r[8 * cc + 3])),
                         pack_bf16(__uint_as_float(r[8 * cc + 4]), __uint_as_float(r[8 * cc + 5])),
                         pack_bf16(__uint_as_float(r[8 * cc + 6]), __uint_as_float(r[8 * cc + 7])));
 }
 
-__device__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int warp, int i, int hf) {
+// One 32-column block of row i of Ghat (pg) and M o S (pm), packed bf16, and the block's
+// part of q. kMode 0: below the diagonal, split decay rowf * colf; 1: the diagonal block,
+// split decay; 2: any block, one exp2 per element (blocks whose split factors could leave
+// the fp32 range). gd / sd receive G_ii / S_ii when the diagonal is in the block.
+template <int kMode>
+__device__ __forceinline__ void mask_block(const uint32_t (&rg)[32], const uint32_t (&rs)[32], uint32_t (&pg)[16],
+                                           uint32_t (&pm)[16], const BScal& sl, int qd, int il, float li,
+                                           float rowf, float bi, float& qacc, float& gd, float& sd) {
+  const float4* c4 = reinterpret_cast<const float4*>(kMode == 2 ? sl.lnx + 32 * qd : sl.colf + 32 * qd);
+  const float4* m4 = reinterpret_cast<const float4*>(kMode == 2 ? sl.mu + 32 * qd : sl.colfm + 32 * qd);
+#pragma unroll
+  for (int e4 = 0; e4 < 8; ++e4) {
+    const float4 cv = c4[e4], mv = m4[e4];
+    const float ck[4] = {cv.x, cv.y, cv.z, cv.w}, mk[4] = {mv.x, mv.y, mv.z, mv.w};
+    float vg[4], vm[4];
+#pragma unroll
+    for (int z = 0; z < 4; ++z) {
+      const int jl = 4 * e4 + z;
+      const float gij = __uint_as_float(rg[jl]), sij = __uint_as_float(rs[jl]);
+      if (kMode == 0) {
+        vg[z] = gij * (rowf * ck[z]);
+        vm[z] = sij * (rowf * mk[z]);
+      } else {
+        float e, em;
+        if (kMode == 1) {
+          e = rowf * ck[z];
+          em = rowf * mk[z];
+        } else {
+          e = exp2f(li - ck[z]);
+          em = e * mk[z];
+        }
+        const bool lo = jl < il, dg = jl == il;
+        vg[z] = lo ? gij * e : 0.f;
+        vm[z] = lo ? sij * em : (dg ? bi * sij : 0.f);
+        gd = dg ? gij : gd;
+        sd = dg ? sij : sd;
+      }
+      qacc = fmaf(gij, vm[z], qacc);
+    }
+    pg[2 * e4] = pack_bf16(vg[0], vg[1]);
+    pg[2 * e4 + 1] = pack_bf16(vg[2], vg[3]);
+    pm[2 * e4] = pack_bf16(vm[0], vm[1]);
+    pm[2 * e4 + 1] = pack_bf16(vm[2], vm[3]);
+  }
+}
+
+__device__ __forceinline__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int warp, int i, int hf) {
   const int wr = warp & 3;  // this warp's rows are 32 wr .. 32 wr + 31
   const int lane = i & 31;
   uint4 xrow[8];            // X row i (half 0), from the phase-1 to the phase-2 epilogue
@@ -313,6 +433,13 @@ __device__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int w
     const uint32_t par = g & 1;
     const BPos cp = bpos(a, g);
     if (!bwait(&s.sc_full[q], (g >> 1) & 1)) return;
+    if (hf == 1 && g == 0) {
+      // e^lambda o dY of the first chunk (later chunks: after the phase-2 epilogue below)
+      if (!bwait(&s.dy_full, 0)) return;
+      write_edy_row(s, s.sc[0], i);
+      fence_proxy_async_smem();
+      mbar_arrive(&s.edy_ready);
+    }
     if (!bwait(&s.p1_done, par)) return;
     // the X and dY tiles this thread reads arrived by TMA: observe their barriers too
     if (!bwait(&s.ld_full, par) || !bwait(&s.dy_full, par)) return;
@@ -320,6 +447,12 @@ __device__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int w
     const BScal& sl = s.sc[q];
     const float li = sl.lam2[i], bi = sl.beta[i];
     float qacc = 0.f;
+    if (hf == 0) {
+      // X_i for dmu in the phase-2 epilogue; warps 2-3 then overwrite the tile with w o X
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) xrow[cc] = *reinterpret_cast<const uint4*>(s.x + sw128_off(i, 8 * cc));
+      mbar_arrive(&s.xread);
+    }
 #pragma unroll 1
     for (int t2 = 0; t2 < 2; ++t2) {
       const int qd = hf + 2 * t2;
@@ -337,31 +470,13 @@ __device__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int w
       tmem_wait_ld();
       const int il = i - 32 * qd;
       uint32_t pg[16], pm[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        float vg[2], vm[2];
-#pragma unroll
-        for (int z = 0; z < 2; ++z) {
-          const int jl = 2 * e + z, j = 32 * qd + jl;
-          const float gij = __uint_as_float(rg[jl]), sij = __uint_as_float(rs[jl]);
-          if (jl < il) {
-            const float ex = exp2f(li - sl.lam2[j + 1]);
-            vg[z] = gij * ex;
-            vm[z] = sij * ex * sl.mu[j];
-            qacc = fmaf(gij, vm[z], qacc);
-          } else if (jl == il) {
-            vg[z] = 0.f;
-            vm[z] = bi * sij;
-            qacc = fmaf(gij, vm[z], qacc);
-            s.gdiag[i] = gij;
-            s.sdiag[i] = sij;
-          } else {
-            vg[z] = 0.f;
-            vm[z] = 0.f;
-          }
-        }
-        pg[e] = pack_bf16(vg[0], vg[1]);
-        pm[e] = pack_bf16(vm[0], vm[1]);
+      float gd = 0.f, sd = 0.f;
+      if ((sl.flags >> qd) & 1) {
+        const float rowf = exp2f(li - sl.lref[qd]);
+        if (qd < wr) mask_block<0>(rg, rs, pg, pm, sl, qd, il, li, rowf, bi, qacc, gd, sd);
+        else mask_block<1>(rg, rs, pg, pm, sl, qd, il, li, rowf, bi, qacc, gd, sd);
+      } else {
+        mask_block<2>(rg, rs, pg, pm, sl, qd, il, li, 0.f, bi, qacc, gd, sd);
       }
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -370,43 +485,38 @@ __device__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int w
         *reinterpret_cast<uint4*>(mst + sw128_off(i, c0 + 8 * cc)) =
             make_uint4(pm[4 * cc], pm[4 * cc + 1], pm[4 * cc + 2], pm[4 * cc + 3]);
       }
+      if (il < 32) {
+        s.gdiag[i] = gd;
+        s.sdiag[i] = sd;
+      }
     }
     if (hf == 1) {
-      // q_i += e^{lambda_i} dY_i . Y1_i
+      // q_i += e^{lambda_i} dY_i . Y1_i; the dY row also goes to TMEM for the phase-2
+      // epilogue (the dY tile is reloaded before then)
       float dot = 0.f;
 #pragma unroll 1
       for (int qt = 0; qt < 2; ++qt) {
-        uint32_t r[32];
+        uint32_t r[32], w[16];
         tmem_ld32(lane_addr(tbase, warp, kColY1 + 32u * qt), r);
-        tmem_wait_ld();
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           const uint4 v = *reinterpret_cast<const uint4*>(s.dy + sw128_off(i, 32 * qt + 8 * cc));
-          const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+          w[4 * cc] = v.x;
+          w[4 * cc + 1] = v.y;
+          w[4 * cc + 2] = v.z;
+          w[4 * cc + 3] = v.w;
+        }
+        tmem_st16(lane_addr(tbase, warp, kColDY + 16u * qt), w);
+        tmem_wait_ld();
 #pragma unroll
-          for (int z = 0; z < 4; ++z) {
-            const float2 f = bf2(vv[z]);
-            dot = fmaf(f.x, __uint_as_float(r[8 * cc + 2 * z]), dot);
-            dot = fmaf(f.y, __uint_as_float(r[8 * cc + 2 * z + 1]), dot);
-          }
+        for (int z = 0; z < 16; ++z) {
+          const float2 f = bf2(w[z]);
+          dot = fmaf(f.x, __uint_as_float(r[2 * z]), dot);
+          dot = fmaf(f.y, __uint_as_float(r[2 * z + 1]), dot);
         }
       }
+      tmem_wait_st();
       qacc = fmaf(sl.el[i], dot, qacc);
-    } else {
-      // keep X_i, then w o X in place (S, its only reader, is complete)
-      const float wi = sl.wdec[i] * sl.mu[i];
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        xrow[cc] = *reinterpret_cast<const uint4*>(s.x + sw128_off(i, 8 * cc));
-        const uint32_t vv[4] = {xrow[cc].x, xrow[cc].y, xrow[cc].z, xrow[cc].w};
-        uint32_t o[4];
-#pragma unroll
-        for (int z = 0; z < 4; ++z) {
-          const float2 f = bf2(vv[z]);
-          o[z] = pack_bf16(f.x * wi, f.y * wi);
-        }
-        *reinterpret_cast<uint4*>(s.x + sw128_off(i, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
-      }
     }
     s.qpart[hf][i] = qacc;
     fence_proxy_async_smem();
@@ -430,16 +540,16 @@ __device__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int w
                                             (int64_t)cp.h * a.sdx.h);
 #pragma unroll
       for (int qt = 0; qt < 4; ++qt) {
-        uint32_t ru[16], rt[16];
+        uint32_t ru[16], rt[16], rd[8];
         tmem_ld16(lane_addr(tbase, warp, kColU + 16u * qt), ru);
         tmem_ld16(lane_addr(tbase, warp, kColT + 16u * qt), rt);
+        tmem_ld8(lane_addr(tbase, warp, kColDY + 8u * qt), rd);
         tmem_wait_ld();
         uint32_t out[8];
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          const uint4 dv = *reinterpret_cast<const uint4*>(s.dy + sw128_off(i, 16 * qt + 8 * h2));
           const uint4 xv = xrow[2 * qt + h2];
-          const uint32_t dvv[4] = {dv.x, dv.y, dv.z, dv.w};
+          const uint32_t dvv[4] = {rd[4 * h2], rd[4 * h2 + 1], rd[4 * h2 + 2], rd[4 * h2 + 3]};
           const uint32_t xvv[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
           for (int z = 0; z < 4; ++z) {
@@ -471,21 +581,30 @@ __device__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int w
         dd = 0.f;
       }
     } else {
-      __nv_bfloat16* dcr = a.dC + (int64_t)cp.b * a.sdC.b + (int64_t)t * a.sdC.l + (int64_t)cp.h * a.sdC.h;
-      __nv_bfloat16* dbr = a.dB + (int64_t)cp.b * a.sdB.b + (int64_t)t * a.sdB.l + (int64_t)cp.h * a.sdB.h;
+      // dC, dB rows -> the Ghat / M o S tiles (read by phase 2 only), stored by TMA
 #pragma unroll 1
       for (int qt = 0; qt < 4; ++qt) {
-        uint32_t r[32];
+        uint32_t r[32], r2[32];
         tmem_ld32(lane_addr(tbase, warp, kColDC + 32u * qt), r);
+        tmem_ld32(lane_addr(tbase, warp, kColDB + 32u * qt), r2);
         tmem_wait_ld();
-        if (valid) store_row_bf16(dcr + 32 * qt, r);
-        tmem_ld32(lane_addr(tbase, warp, kColDB + 32u * qt), r);
-        tmem_wait_ld();
-        if (valid) store_row_bf16(dbr + 32 * qt, r);
+        stage_row_bf16(s.gh[qt >> 1], i, (qt & 1) * 32, r);
+        stage_row_bf16(s.ms[qt >> 1], i, (qt & 1) * 32, r2);
       }
     }
+    fence_proxy_async_smem();
     tc_fence_before();
     mbar_arrive(&s.ep2_done);
+    if (hf == 1 && g + 1 < G) {
+      // e^lambda o dY of the next chunk, whose dY lands during this epilogue (the tile's
+      // previous readers, the MMAs of phase 2, are complete)
+      const int q1 = (g + 1) & 1;
+      if (!bwait(&s.sc_full[q1], ((g + 1) >> 1) & 1)) return;
+      if (!bwait(&s.dy_full, (g + 1) & 1)) return;
+      write_edy_row(s, s.sc[q1], i);
+      fence_proxy_async_smem();
+      mbar_arrive(&s.edy_ready);
+    }
     mbar_arrive(&s.sc_empty[q]);
   }
 }
@@ -496,7 +615,7 @@ __device__ void ep_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int w
 // it becomes dk_c = e^{lambda_Q} dk_next + dK^T. At a unit's first chunk dk_0 gives
 // dh0 = a_0 dk_0, dbx0 = gamma_0 dk_0 and dgamma_0 = <dk_0, bx0>.
 // ------------------------------------------------------------------------------------
-__device__ void state_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int warp, int d) {
+__device__ __forceinline__ void state_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, int warp, int d) {
   float dk[kP];
 #pragma unroll
   for (int p = 0; p < kP; ++p) dk[p] = 0.f;
@@ -521,7 +640,7 @@ __device__ void state_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, in
                      pack_bf16(dk[8 * cc + 4], dk[8 * cc + 5]), pack_bf16(dk[8 * cc + 6], dk[8 * cc + 7]));
     fence_proxy_async_smem();
     mbar_arrive(&s.dkn_ready);
-    if (!bwait(&s.p1_done, par)) return;
+    if (!bwait(&s.p1b_done, par)) return;
     tc_fence_after();
     const float dec = sl.decQ;
 #pragma unroll
@@ -555,15 +674,20 @@ __device__ void state_role(const BwdArgs& a, BSmem& s, uint32_t tbase, int G, in
 }
 
 // ------------------------------------------------------------------------------------
-// warp 0, lane 0: loads and MMA issue for every chunk, in order.
-//   C, B, X, k_c   after phase 2 of the previous chunk (their last MMA readers)
-//   dY             after the previous phase-2 epilogue (it reads dY rows)
-//   phase 1        after the loads, e^lambda o dY and the bf16 dk_next
-//   phase 2        after the phase-1 epilogue (Ghat, M o S, w o X in shared memory)
+// warp 0, lane 0: loads, MMA issue and output stores, in order. Per chunk g:
+//   phase 1(g)   once its inputs, e^lambda o dY(g) and dk_next(g) are in shared memory and
+//                the phase-2 epilogue of g-1 has read TMEM: G, S, Y1 (commit p1_done; the
+//                Ghat / M o S tiles are free once the TMA stores of g-1 have read them),
+//                then T and dK^T (commit p1b_done)
+//   phase 2(g)   after the phase-1 epilogue: U, dC, dB (commit p2_done)
+//   loads(g+1)   C, B, X, k_c, dY as soon as phase 2(g) has read the tiles, so they land
+//                during the phase-2 epilogue of g
+//   stores(g)    dC, dB by TMA from the Ghat / M o S tiles after the phase-2 epilogue
 // ------------------------------------------------------------------------------------
-__device__ void control_role(const CUtensorMap* tm_x, const CUtensorMap* tm_B, const CUtensorMap* tm_C,
-                             const CUtensorMap* tm_dy, const CUtensorMap* tm_k, const BwdArgs& a, BSmem& s,
-                             uint32_t tbase, int G) {
+__device__ __forceinline__ void control_role(const CUtensorMap* tm_x, const CUtensorMap* tm_B, const CUtensorMap* tm_C,
+                                             const CUtensorMap* tm_dy, const CUtensorMap* tm_k,
+                                             const CUtensorMap* tm_dB, const CUtensorMap* tm_dC, const BwdArgs& a,
+                                             BSmem& s, uint32_t tbase, int G) {
   constexpr uint32_t I_KK128 = idesc_bf16_f32(128, 128, false, false);  // A, B K-major, N = 128
   constexpr uint32_t I_KM64 = idesc_bf16_f32(128, 64, false, true);     // A K-major, B MN-major, N = 64
   constexpr uint32_t I_MM64 = idesc_bf16_f32(128, 64, true, true);      // both MN-major, N = 64
@@ -582,62 +706,77 @@ __device__ void control_role(const CUtensorMap* tm_x, const CUtensorMap* tm_B, c
   auto mn = [](uint32_t base, int kk) { return sdesc_sw128(base + (uint32_t)kk * 2048u, kTile, 1024); };
   // last chunk whose loads / MMA phases were issued: on a timeout, wait (bounded) for them
   // before leaving, so no copy or MMA is in flight when the CTA exits
-  int lg = -1, dg = -1, p1g = -1, p2g = -1;
+  int lg = -1, p1g = -1, p2g = -1;
   auto drain = [&]() {
-    if (lg >= 0) mbar_wait(&s.ld_full, lg & 1, 1u << 20);
-    if (dg >= 0) mbar_wait(&s.dy_full, dg & 1, 1u << 20);
-    if (p1g >= 0) mbar_wait(&s.p1_done, p1g & 1, 1u << 20);
+    bulk_wait0();
+    if (lg >= 0) {
+      mbar_wait(&s.ld_full, lg & 1, 1u << 20);
+      mbar_wait(&s.dy_full, lg & 1, 1u << 20);
+    }
+    if (p1g >= 0) mbar_wait(&s.p1b_done, p1g & 1, 1u << 20);
     if (p2g >= 0) mbar_wait(&s.p2_done, p2g & 1, 1u << 20);
   };
-  for (int g = 0; g < G; ++g) {
-    const BPos cp = bpos(a, g);
-    const uint32_t par = g & 1;
-    if (g > 0 && !bwait(&s.p2_done, par ^ 1)) return drain();
-    mbar_expect_tx(&s.ld_full, 6 * kTile);
+  auto load = [&](int gg) {
+    const BPos cp = bpos(a, gg);
+    // dY first: e^lambda o dY waits for it
+    mbar_expect_tx(&s.dy_full, kTile);
+    tma_load_4d(s.dy, tm_dy, &s.dy_full, 0, cp.h, cp.t0, cp.b);
+    mbar_expect_tx(&s.ld_full, 6 * kTile);  // C (2), B (2), X, k_c
     tma_load_4d(s.c[0], tm_C, &s.ld_full, 0, cp.h, cp.t0, cp.b);
     tma_load_4d(s.c[1], tm_C, &s.ld_full, 64, cp.h, cp.t0, cp.b);
     tma_load_4d(s.b[0], tm_B, &s.ld_full, 0, cp.h, cp.t0, cp.b);
     tma_load_4d(s.b[1], tm_B, &s.ld_full, 64, cp.h, cp.t0, cp.b);
     tma_load_4d(s.x, tm_x, &s.ld_full, 0, cp.h, cp.t0, cp.b);
     tma_load_2d(s.kc, tm_k, &s.ld_full, 0, (cp.u * a.nch + cp.c) * kD);
-    lg = g;
-    if (g > 0 && !bwait(&s.ep2_done, par ^ 1)) return drain();
-    mbar_expect_tx(&s.dy_full, kTile);
-    tma_load_4d(s.dy, tm_dy, &s.dy_full, 0, cp.h, cp.t0, cp.b);
-    dg = g;
-    if (g + 1 < G) {
-      // the next chunk into L2 while this one computes
-      const BPos nx = bpos(a, g + 1);
+    lg = gg;
+    if (gg + 1 < G) {
+      // the chunk after into L2
+      const BPos nx = bpos(a, gg + 1);
+      tma_prefetch_l2_4d(tm_dy, 0, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_4d(tm_C, 0, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_4d(tm_C, 64, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_4d(tm_B, 0, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_4d(tm_B, 64, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_4d(tm_x, 0, nx.h, nx.t0, nx.b);
-      tma_prefetch_l2_4d(tm_dy, 0, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_2d(tm_k, 0, (nx.u * a.nch + nx.c) * kD);
     }
-    if (!bwait(&s.ld_full, par) || !bwait(&s.dy_full, par) || !bwait(&s.edy_ready, par) ||
-        !bwait(&s.dkn_ready, par))
+  };
+  // dC, dB of chunk gg, staged in the Ghat and M o S tiles
+  auto store_outputs = [&](int gg) {
+    const BPos op = bpos(a, gg);
+    tma_store_4d(tm_dC, s.gh[0], 0, op.h, op.t0, op.b);
+    tma_store_4d(tm_dC, s.gh[1], 64, op.h, op.t0, op.b);
+    tma_store_4d(tm_dB, s.ms[0], 0, op.h, op.t0, op.b);
+    tma_store_4d(tm_dB, s.ms[1], 64, op.h, op.t0, op.b);
+    bulk_commit();
+  };
+  if (G > 0) load(0);
+  for (int g = 0; g < G; ++g) {
+    const uint32_t par = g & 1;
+    if (!cwait(&s.ld_full, par) || !cwait(&s.dy_full, par) || !cwait(&s.edy_ready, par) ||
+        !cwait(&s.dkn_ready, par))
       return drain();
+    // (the phase-2 epilogue of g-1, which read TMEM, completed before its stores below)
     tc_fence_after();
-    // phase 1
+    // phase 1: what the phase-1 epilogue reads first
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColG, k2(c0, kk), k2(b0, kk), I_KK128, kk > 0);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) mma_ss(tbase + kColS, k1(dya, kk), k1(xa, kk), I_KK128, kk > 0);
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColY1, k2(c0, kk), mn(ka, kk), I_KM64, kk > 0);
+    // the epilogue overwrites the staging tiles of g-1: their stores must have read them
+    if (g > 0) bulk_wait_read0();
+    mma_commit(&s.p1_done);
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColT, k2(b0, kk), mn(na, kk), I_KM64, kk > 0);
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColDK, mn(c0, kk), mn(ea, kk), I_MM64, kk > 0);
-    mma_commit(&s.p1_done);
+    mma_commit(&s.p1b_done);
     p1g = g;
     // phase 2
-    if (!bwait(&s.ep1_done, par)) return drain();
+    if (!cwait(&s.ep1_done, par)) return drain();
     tc_fence_after();
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColU, mn(ga, kk), mn(dya, kk), I_MM64, kk > 0);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) mma_ss(tbase + kColDC, k1(ea, kk), k1(ka, kk), I_KK128, kk > 0);
 #pragma unroll
@@ -646,18 +785,33 @@ __device__ void control_role(const CUtensorMap* tm_x, const CUtensorMap* tm_B, c
     for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColDB, mn(ma, kk), mn(c0, kk), I_MM128, kk > 0);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) mma_ss(tbase + kColDB, k1(xa, kk), k1(na, kk), I_KK128, 1u);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColU, mn(ga, kk), mn(dya, kk), I_MM64, kk > 0);
     mma_commit(&s.p2_done);
     p2g = g;
+    // the next chunk's tiles, once phase 2 has read these
+    if (g + 1 < G) {
+      if (!cwait(&s.p2_done, par)) return drain();
+      load(g + 1);
+    }
+    // this chunk's dC, dB once the phase-2 epilogue has staged them
+    if (!cwait(&s.ep2_done, par)) return drain();
+    store_outputs(g);
   }
+  bulk_wait0();
 }
 
 // ------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads, 1)
 siso_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_B,
                       const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_dy,
-                      const __grid_constant__ CUtensorMap tm_k, BwdArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  BSmem& s = *reinterpret_cast<BSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_dB,
+                      const __grid_constant__ CUtensorMap tm_dC,
+                      BwdArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte aligned base, derived from smem_raw so that accesses stay shared-space
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  BSmem& s = *reinterpret_cast<BSmem*>(smem_raw + pad);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int units = a.Bn * a.H;
   const int my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -670,13 +824,15 @@ siso_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
       mbar_init(&s.sc_full[i], 32);
       mbar_init(&s.sc_empty[i], kScalReaders);
     }
-    mbar_init(&s.edy_ready, 64);
+    mbar_init(&s.edy_ready, 128);
+    mbar_init(&s.xread, 128);
     mbar_init(&s.dkn_ready, 128);
     mbar_init(&s.p1_done, 1);
-    mbar_init(&s.ep1_done, 256);
+    mbar_init(&s.ep1_done, kEp1Arrivals);
     mbar_init(&s.p2_done, 1);
     mbar_init(&s.ep2_done, 256);
     mbar_init(&s.st_sync, 128);
+    mbar_init(&s.p1b_done, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -695,12 +851,14 @@ siso_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
       prefetch_tensormap(&tm_C);
       prefetch_tensormap(&tm_dy);
       prefetch_tensormap(&tm_k);
-      control_role(&tm_x, &tm_B, &tm_C, &tm_dy, &tm_k, a, s, tbase, G);
+      prefetch_tensormap(&tm_dB);
+      prefetch_tensormap(&tm_dC);
+      control_role(&tm_x, &tm_B, &tm_C, &tm_dy, &tm_k, &tm_dB, &tm_dC, a, s, tbase, G);
     }
   } else if (warp == 1) {
     scalar_role(a, s, G, lane);
   } else if (warp < 4) {
-    edy_role(s, G, tid - 64);
+    wx_role(s, G, tid - 64);
   } else if (warp < 12) {
     ep_role(a, s, tbase, G, warp, (tid - 128) & 127, (tid - 128) >> 7);
   } else {
@@ -805,7 +963,7 @@ bool siso_chunk_bwd_supported(const SisoParams& p, int xdt, int bcdt) {
 }
 
 int launch_siso_bwd_chunked(const SisoParams& p, float* scratch, cudaStream_t s) {
-  CUtensorMap mx, mb, mc, mdy, mk;
+  CUtensorMap mx, mb, mc, mdy, mk, mdb, mdc;
   const int nch = (p.L + Q - 1) / Q;
   const int units = p.Bn * p.H;
   M3_TRY(chunk_tmap_4d(&mx, p.x, p.P, p.H, p.L, p.Bn, p.sx));
@@ -813,6 +971,8 @@ int launch_siso_bwd_chunked(const SisoParams& p, float* scratch, cudaStream_t s)
   M3_TRY(chunk_tmap_4d(&mc, p.Cm, p.D, p.H, p.L, p.Bn, p.sC));
   M3_TRY(chunk_tmap_4d(&mdy, p.dy, p.P, p.H, p.L, p.Bn, p.sdy));
   M3_TRY(make_kstate_map(&mk, p.kstates, (int64_t)units * nch * kD));
+  M3_TRY(chunk_tmap_4d(&mdb, p.dB, p.D, p.H, p.L, p.Bn, p.sdB));
+  M3_TRY(chunk_tmap_4d(&mdc, p.dC, p.D, p.H, p.L, p.Bn, p.sdC));
   BwdArgs a{};
   a.Bn = p.Bn; a.L = p.L; a.H = p.H; a.nch = nch;
   a.adt = p.adt; a.sadt = p.sadt;
@@ -840,7 +1000,7 @@ int launch_siso_bwd_chunked(const SisoParams& p, float* scratch, cudaStream_t s)
   }
   const int sms = chunk_sm_count();
   const int grid = units < sms ? units : sms;
-  siso_chunk_bwd_kernel<<<grid, kThreads, smem, s>>>(mx, mb, mc, mdy, mk, a);
+  siso_chunk_bwd_kernel<<<grid, kThreads, smem, s>>>(mx, mb, mc, mdy, mk, mdb, mdc, a);
   M3_TRY(check_launch("siso_chunk_bwd_kernel"));
   siso_chunk_bwd_scal_kernel<<<units, 128, 0, s>>>(a);
   return check_launch("siso_chunk_bwd_scal_kernel");
