@@ -484,6 +484,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the forward+backward and decode figures")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the global batch (profiling runs on a smaller case)")
+    ap.add_argument("--fwd-bwd-only", action="store_true",
+                    help="only the ssm_scan_siso forward + backward figure (profiling the backward)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -513,6 +515,11 @@ def main():
     _, Bl = shard(Bt, world, rank)
     x, Bm, Cm, ADT, DT, trap, Dw = make_inputs(Bl, L, H, P, D, dev, 1234 + rank)
     torch.cuda.synchronize()
+    if args.fwd_bwd_only:
+        r = measure_fwd_bwd((x, Bm, Cm, ADT, DT, trap, Dw), steps=args.steps)
+        if rank == 0:
+            print(json.dumps({"fwd_bwd": r, "batch": Bl, "timeouts": _lib.device_timeouts(reset=True)}))
+        return
 
     def barrier():
         if pg is not None:
