@@ -486,6 +486,8 @@ def main():
                     help="override the global batch (profiling runs on a smaller case)")
     ap.add_argument("--fwd-bwd-only", action="store_true",
                     help="only the ssm_scan_siso forward + backward figure (profiling the backward)")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the decode figure (profiling the decode step)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -508,6 +510,11 @@ def main():
     from mamba3_ssm import ssm_scan_siso
     from mamba3_ssm import _lib
     _lib.load()
+    if args.decode_only:
+        r = measure_decode(dev)
+        if rank == 0:
+            print(json.dumps({"decode": r, "timeouts": _lib.device_timeouts(reset=True)}))
+        return
 
     if args.batch:
         C5["batch"] = args.batch

@@ -42,7 +42,8 @@ extern "C" {
 typedef enum m3_dtype {
   M3_FLOAT32 = 0,
   M3_BFLOAT16 = 1,
-  M3_FLOAT16 = 2
+  M3_FLOAT16 = 2,
+  M3_INT64 = 3 /* token ids (m3_argmax_rows) */
 } m3_dtype;
 
 typedef enum m3_status {
@@ -247,6 +248,16 @@ int m3_mimo_step(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_te
  * ------------------------------------------------------------------------------- */
 int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* weight, float eps,
                m3_tensor* out, m3_tensor* residual_out, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Greedy token choice of the decode step: out[r] = argmax over the last dimension of
+ * logits[r] (the logits.argmax(-1) of greedy decoding with MambaLMHeadModel, block.py /
+ * generate: first index of the maximum, NaN counting as the maximum, like torch.argmax).
+ *   logits (..., n) f32 / bf16 / f16, innermost stride 1, leading dims collapsible into
+ *   rows of one stride; out: int64, contiguous, one element per row.
+ * No counterpart in the reference's native code (a PyTorch reduction there).
+ * ------------------------------------------------------------------------------- */
+int m3_argmax_rows(const m3_tensor* logits, m3_tensor* out, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Fused forward prologue of Mamba3.forward (layer.py:180-244) for inference, from the

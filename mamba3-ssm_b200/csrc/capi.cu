@@ -4,6 +4,7 @@
 #include <mutex>
 #include <string>
 
+#include "argmax.cuh"
 #include "decode_step.cuh"
 #include "m3_common.cuh"
 #include "mimo_scan.cuh"
@@ -717,6 +718,34 @@ int m3_rmsnorm(const m3_tensor* x, const m3_tensor* residual, const m3_tensor* w
   return launch_rmsnorm(p, x->dtype, weight->dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
+
+int m3_argmax_rows(const m3_tensor* logits, m3_tensor* out, void* stream) {
+  if (!present(logits) || logits->ndim < 1) return fail(M3_ERR_INVALID_ARGUMENT, "logits: missing or 0-d");
+  if (!present(out)) return fail(M3_ERR_INVALID_ARGUMENT, "out: missing");
+  const int nd = logits->ndim;
+  const int64_t n = logits->shape[nd - 1];
+  int64_t rows = 1;
+  for (int i = 0; i < nd - 1; ++i) rows *= logits->shape[i];
+  M3_TRY(check(logits, "logits", nd, logits->shape, kAnyFloat, false, false, rows * n > 0));
+  if (n <= 0 && rows > 0) return fail(M3_ERR_INVALID_ARGUMENT, "logits: empty last dimension");
+  for (int i = 0; i + 2 < nd; ++i)
+    if (logits->shape[i] > 1 && logits->stride[i] != logits->stride[i + 1] * logits->shape[i + 1])
+      return fail(M3_ERR_INVALID_ARGUMENT, "logits: leading dims must collapse into rows");
+  if (out->dtype != M3_INT64) return fail(M3_ERR_INVALID_ARGUMENT, "out: expected int64");
+  int64_t on = 1, expect = 1;
+  for (int i = out->ndim - 1; i >= 0; --i) {
+    if (out->shape[i] > 1 && out->stride[i] != expect)
+      return fail(M3_ERR_INVALID_ARGUMENT, "out: must be contiguous");
+    expect *= out->shape[i];
+    on *= out->shape[i];
+  }
+  if (on != rows) return fail(M3_ERR_INVALID_ARGUMENT, "out: one element per logits row expected");
+  if (rows == 0) return M3_OK;
+  M3_TRY(check_device_ptr(out->data, "out"));
+  const int64_t sx = nd >= 2 ? logits->stride[nd - 2] : n;
+  return launch_argmax_rows(logits->data, logits->dtype, rows, n, sx, static_cast<int64_t*>(out->data),
+                            reinterpret_cast<cudaStream_t>(stream));
+}
 
 int m3_device_timeouts(int reset, int* flag_out) {
   if (!flag_out) return fail(M3_ERR_INVALID_ARGUMENT, "flag_out: missing");

@@ -1,9 +1,14 @@
 // Fused single-token decode step of one Mamba3 mixer: everything Mamba3.step
 // (mamba3_ssm/layer.py:298-371) does between in_proj and out_proj, in one kernel.
-// One CTA per (b, h). The prologue (split of the in_proj row, softplus / clamp /
-// sigmoid, RMSNorm + bias of B and C, angle update and RoPE) runs once per CTA in shared
-// memory; the state update and readout then stream the fp32 state exactly once
-// (read old state, write new state), which is what bounds the step on HBM.
+// Three layouts, chosen per shape:
+//   MIMO, d_state and headdim 64 / 128: a warp per (b, h), lane l owning the column pairs
+//     2l, 2l+1 (vector loads and stores, the RoPE partner in the same lane, one sincos per
+//     pair for every rank);
+//   other MIMO shapes with d_state 32 / 64 / 128: a warp per (b, h), lane = column;
+//   SISO and the remaining MIMO shapes: a CTA per (b, h) with the prologue (split of the
+//     in_proj row, softplus / clamp / sigmoid, RMSNorm + bias of B and C, angle update and
+//     RoPE) in shared memory.
+// Each streams the fp32 state once (read old state, write new state).
 #include "m3_common.cuh"
 #include "decode_step.cuh"
 
@@ -420,6 +425,225 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_warp_kernel(StepPara
   }
 }
 
+// ------------------------------------------------------------------------------------
+// Lean warp-per-(b, h) MIMO step for d_state 64 / 128 and headdim 64 / 128 (the shapes of
+// the LM presets): lane l owns the column pairs d = 2l, 2l+1 (+ 64 for d_state 128) and
+// p = 2l, 2l+1 (+ 64), so every load and store is a 4- or 8-byte vector, the RoPE partner
+// of a pair is in the same lane (no shuffles), and one sincos per lane and d-slot serves
+// every rank. Head parameters are read through the read-only cache (the CTA's 8 warps
+// are 8 batch rows of one head).
+// ------------------------------------------------------------------------------------
+template <typename T> struct Pair;
+template <> struct Pair<float> {
+  static __device__ __forceinline__ float2 ld(const float* p) { return *reinterpret_cast<const float2*>(p); }
+  static __device__ __forceinline__ void st(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
+};
+template <> struct Pair<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 ld(const __nv_bfloat16* p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, float2 v) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v.x, v.y);
+  }
+};
+template <> struct Pair<__half> {
+  static __device__ __forceinline__ float2 ld(const __half* p) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+  }
+  static __device__ __forceinline__ void st(__half* p, float2 v) {
+    *reinterpret_cast<__half2*>(p) = __floats2half2_rn(v.x, v.y);
+  }
+};
+__device__ __forceinline__ float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
+
+// Logistic function from the hardware exp / divide approximations (relative error a few
+// 1e-7), for the trapezoid weight and the output gate.
+__device__ __forceinline__ float fast_sigmoid(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
+
+// sin and cos of an angle of any size: Cody-Waite reduction by 2 pi with a two-part
+// constant (k = rint(x / 2pi), r = (x - k C1) - k C2, C1 = 2 pi rounded to fp32,
+// C2 = 2 pi - C1), then the hardware approximations on |r| <= pi (absolute error ~1e-6).
+__device__ __forceinline__ void sincos_reduced(float x, float* sn, float* cs) {
+  const float k = rintf(x * 0.159154943091895336f);
+  float r = fmaf(-k, 6.28318548202514648f, x);
+  r = fmaf(-k, -1.74845553146951715e-07f, r);
+  __sincosf(r, sn, cs);
+}
+
+template <typename TZ, int DP, int PP, int RM>
+__global__ void __launch_bounds__(32 * kWarpRows) mimo_step_pair_kernel(StepParams a) {
+  constexpr int D = 64 * DP, P = 64 * PP;
+  const int R = a.R, G = a.G, H = a.H, S = a.S;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  const int b = blockIdx.y * kWarpRows + (threadIdx.x >> 5);
+  if (b >= a.Bn) return;
+  const TZ* row = reinterpret_cast<const TZ*>(a.zxbcdt) + (int64_t)b * a.s_row;
+  const int g = (int)(((int64_t)h * G) / H);
+  const int off_B = 2 * a.d_inner, off_C = off_B + D * G * R, off_dt = off_C + D * G * R;
+  const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
+  // this row's operands (all loads independent)
+  float2 Bv[RM][DP], Cv[RM][DP], xv[PP], zv[PP], hs[DP], bp[DP];
+#pragma unroll
+  for (int r = 0; r < RM; ++r)
+#pragma unroll
+    for (int q = 0; q < DP; ++q) {
+      const int d0 = 2 * lane + 64 * q;
+      Bv[r][q] = r < R ? Pair<TZ>::ld(row + off_B + (r * G + g) * D + d0) : make_float2(0.f, 0.f);
+      Cv[r][q] = r < R ? Pair<TZ>::ld(row + off_C + (r * G + g) * D + d0) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+  for (int q = 0; q < PP; ++q) {
+    const int p0 = 2 * lane + 64 * q;
+    xv[q] = Pair<TZ>::ld(row + a.d_inner + h * P + p0);
+    zv[q] = Pair<TZ>::ld(row + h * P + p0);
+  }
+  const int64_t sbase = ((int64_t)b * H + h) * D;
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    hs[q] = *reinterpret_cast<const float2*>(a.ssm_in + sbase + 2 * lane + 64 * q);
+    bp[q] = *reinterpret_cast<const float2*>(a.bx_in + sbase + 2 * lane + 64 * q);
+  }
+  const int64_t abase = ((int64_t)b * H + h) * S;
+  float ang_in[DP], ang_raw[DP];
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    const int i = lane + 32 * q;  // the pair's angle
+    ang_in[q] = i < S ? a.angle_in[abase + i] : 0.f;
+    ang_raw[q] = i < S ? to_f32(row[off_ang + i]) : 0.f;
+  }
+  const float dt_raw = to_f32(row[off_dt + h]), A_raw = to_f32(row[off_A + h]), tr_raw = to_f32(row[off_tr + h]);
+
+  const float DT = softplusf_(dt_raw + __ldg(a.dt_bias + h));
+  const float A = -fminf(softplusf_(A_raw), -a.A_floor);  // layer.py:317
+  const float decay = expf(A * DT);
+  const float tr = fast_sigmoid(tr_raw);
+  const float Dk = __ldg(a.Dskip + h);
+  // RMSNorm per rank over D (ops.py:102-104)
+  float ss[2 * RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) {
+    float sb = 0.f, sc = 0.f;
+#pragma unroll
+    for (int q = 0; q < DP; ++q) {
+      sb = fmaf(Bv[r][q].x, Bv[r][q].x, fmaf(Bv[r][q].y, Bv[r][q].y, sb));
+      sc = fmaf(Cv[r][q].x, Cv[r][q].x, fmaf(Cv[r][q].y, Cv[r][q].y, sc));
+    }
+    ss[r] = sb;
+    ss[RM + r] = sc;
+  }
+  warp_sum_n<2 * RM>(ss, lane);
+  // angle update (layer.py:331-332) and the RoPE rotation of each owned pair
+  float sn[DP], cs[DP];
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    const int i = lane + 32 * q;
+    const float an = ang_in[q] + ang_raw[q] * DT;
+    sincos_reduced(an, &sn[q], &cs[q]);
+    if (i < S) a.angle_out[abase + i] = an;  // angle_out may alias angle_in: same lane, read above
+  }
+  // normalise, weight, bias, rotate
+  const float* Bb = a.B_bias + (int64_t)h * R * D;
+  const float* Cb = a.C_bias + (int64_t)h * R * D;
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    const int d0 = 2 * lane + 64 * q;
+    const bool rot = lane + 32 * q < S;
+    const float2 wb = ldg2(a.B_norm_w + d0), wc = ldg2(a.C_norm_w + d0);
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+      if (r >= R) break;
+      const float nb = rsqrtf(ss[r] * (1.0f / D) + a.eps), nc = rsqrtf(ss[RM + r] * (1.0f / D) + a.eps);
+      const float2 bb = ldg2(Bb + r * D + d0), cb = ldg2(Cb + r * D + d0);
+      float b0 = fmaf(Bv[r][q].x * nb, wb.x, bb.x), b1 = fmaf(Bv[r][q].y * nb, wb.y, bb.y);
+      float c0 = fmaf(Cv[r][q].x * nc, wc.x, cb.x), c1 = fmaf(Cv[r][q].y * nc, wc.y, cb.y);
+      if (rot) {
+        const float rb0 = b0 * cs[q] - b1 * sn[q], rb1 = b0 * sn[q] + b1 * cs[q];
+        const float rc0 = c0 * cs[q] - c1 * sn[q], rc1 = c0 * sn[q] + c1 * cs[q];
+        b0 = rb0; b1 = rb1; c0 = rc0; c1 = rc1;
+      }
+      Bv[r][q] = make_float2(b0, b1);
+      Cv[r][q] = make_float2(c0, c1);
+    }
+  }
+  // xr = mimo_x x (layer.py:346)
+  const float* mx = a.mimo_x + (int64_t)h * R * P;
+  const float* mo = a.mimo_o + (int64_t)h * R * P;
+  float xr[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) {
+    float acc = 0.f;
+    if (r < R) {
+#pragma unroll
+      for (int q = 0; q < PP; ++q) {
+        const float2 m = ldg2(mx + r * P + 2 * lane + 64 * q);
+        acc = fmaf(m.x, xv[q].x, fmaf(m.y, xv[q].y, acc));
+      }
+    }
+    xr[r] = acc;
+  }
+  warp_sum_n<RM>(xr, lane);
+  // state update (layer.py:347-351) and y_r = C_r h
+  float yr[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) yr[r] = 0.f;
+  const float w1 = 1.0f - 0.5f * tr, w2 = 0.5f * tr;  // blend = w1 bx + w2 bx_prev
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    float2 bxc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {  // zero B rows beyond R
+      bxc.x = fmaf(xr[r], Bv[r][q].x, bxc.x);
+      bxc.y = fmaf(xr[r], Bv[r][q].y, bxc.y);
+    }
+    float2 hn;
+    hn.x = fmaf(decay, hs[q].x, DT * fmaf(w1, bxc.x, w2 * bp[q].x));
+    hn.y = fmaf(decay, hs[q].y, DT * fmaf(w1, bxc.y, w2 * bp[q].y));
+    *reinterpret_cast<float2*>(a.ssm_out + sbase + 2 * lane + 64 * q) = hn;
+    *reinterpret_cast<float2*>(a.bx_out + sbase + 2 * lane + 64 * q) = bxc;
+#pragma unroll
+    for (int r = 0; r < RM; ++r) yr[r] = fmaf(Cv[r][q].x, hn.x, fmaf(Cv[r][q].y, hn.y, yr[r]));
+  }
+  warp_sum_n<RM>(yr, lane);
+  // y = mimo_o^T (y_r + D xr), gated by silu(z) (layer.py:352-356)
+  TZ* yo = reinterpret_cast<TZ*>(a.y) + (int64_t)b * a.s_y + h * P;
+#pragma unroll
+  for (int q = 0; q < PP; ++q) {
+    const int p0 = 2 * lane + 64 * q;
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+      if (r >= R) break;
+      const float2 m = ldg2(mo + r * P + p0);
+      const float yv = fmaf(Dk, xr[r], yr[r]);
+      acc.x = fmaf(yv, m.x, acc.x);
+      acc.y = fmaf(yv, m.y, acc.y);
+    }
+    const float2 z = zv[q];
+    Pair<TZ>::st(yo + p0, make_float2(acc.x * (z.x * fast_sigmoid(z.x)), acc.y * (z.y * fast_sigmoid(z.y))));
+  }
+}
+
+template <typename TZ, int DP, int PP>
+void launch_pair_pp(const StepParams& p, cudaStream_t s) {
+  const dim3 grid(p.H, (p.Bn + kWarpRows - 1) / kWarpRows);
+  if (p.R <= 1) mimo_step_pair_kernel<TZ, DP, PP, 1><<<grid, 32 * kWarpRows, 0, s>>>(p);
+  else if (p.R <= 2) mimo_step_pair_kernel<TZ, DP, PP, 2><<<grid, 32 * kWarpRows, 0, s>>>(p);
+  else if (p.R <= 4) mimo_step_pair_kernel<TZ, DP, PP, 4><<<grid, 32 * kWarpRows, 0, s>>>(p);
+  else mimo_step_pair_kernel<TZ, DP, PP, 8><<<grid, 32 * kWarpRows, 0, s>>>(p);
+}
+
+template <typename TZ>
+void launch_pair(const StepParams& p, cudaStream_t s) {
+  if (p.D == 64) {
+    if (p.P == 64) launch_pair_pp<TZ, 1, 1>(p, s);
+    else launch_pair_pp<TZ, 1, 2>(p, s);
+  } else {
+    if (p.P == 64) launch_pair_pp<TZ, 2, 1>(p, s);
+    else launch_pair_pp<TZ, 2, 2>(p, s);
+  }
+}
+
 template <typename TZ, int DL, int RM>
 void launch_warp_rm(const StepParams& p, cudaStream_t s) {
   const dim3 grid(p.H, (p.Bn + kWarpRows - 1) / kWarpRows);
@@ -446,6 +670,8 @@ void launch_warp(const StepParams& p, cudaStream_t s) {
 
 }  // namespace
 
+inline bool aligned_to(const void* p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
 int launch_step(const StepParams& p, int zdt, bool mimo, cudaStream_t s) {
   if (p.R * p.D > kMaxRD || p.R > 8 || p.S > 256) return fail(M3_ERR_UNSUPPORTED, "step: mimo_rank*d_state above 2048, rank above 8 or more than 256 angles");
   if (mimo && p.P > 1024) return fail(M3_ERR_UNSUPPORTED, "step: headdim above 1024");
@@ -456,9 +682,20 @@ int launch_step(const StepParams& p, int zdt, bool mimo, cudaStream_t s) {
   const int dl = p.D / 32;
   const bool warp_mimo = mimo && p.D % 32 == 0 && (dl == 1 || dl == 2 || dl == 4) && p.R * dl <= 16 &&
                          p.P <= 256 && p.split <= p.D;
+  // the vector-pair kernel: d_state and headdim 64 / 128, every row and state row starts on
+  // an 8-byte boundary (pairs of 16-bit or 32-bit values)
+  const int esz = zdt == M3_FLOAT32 ? 4 : 2;
+  const bool pair_mimo = mimo && (p.D == 64 || p.D == 128) && (p.P == 64 || p.P == 128) && p.R <= 8 &&
+                         2 * p.S <= p.D && p.split == 2 * p.S && (p.s_row % 2) == 0 && (p.s_y % 2) == 0 &&
+                         (p.d_inner % 2) == 0 && aligned_to(p.zxbcdt, 2 * esz) && aligned_to(p.y, 2 * esz) &&
+                         aligned_to(p.ssm_in, 8) && aligned_to(p.ssm_out, 8) && aligned_to(p.bx_in, 8) &&
+                         aligned_to(p.bx_out, 8) && aligned_to(p.B_bias, 8) && aligned_to(p.C_bias, 8) &&
+                         aligned_to(p.mimo_x, 8) && aligned_to(p.mimo_o, 8) && aligned_to(p.B_norm_w, 8) &&
+                         aligned_to(p.C_norm_w, 8);
 #define M3_STEP_LAUNCH(T)                                                          \
   do {                                                                             \
-    if (warp_mimo) launch_warp<T>(p, s);                                            \
+    if (pair_mimo) launch_pair<T>(p, s);                                            \
+    else if (warp_mimo) launch_warp<T>(p, s);                                       \
     else if (mimo) mimo_step_kernel<T><<<grid, kThreads, 0, s>>>(p);               \
     else siso_step_kernel<T><<<grid, kThreads, 0, s>>>(p);                         \
   } while (0)

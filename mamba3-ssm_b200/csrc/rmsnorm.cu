@@ -2,9 +2,11 @@
 // * weight, returned in x.dtype), with the block's residual add (block.py:20-29:
 // x + mixer(norm(x))) optionally fused in front: h = x + res is rounded to x.dtype exactly
 // as the eager add would, written out, and normalised.
-// One warp per row. Where every operand is 16-byte aligned (base, row stride, d) the row
-// moves in 16-byte vectors, all of a lane's loads issued together and the row kept in
-// registers between the two passes (up to 32 * kMaxVec vectors); otherwise element-wise.
+// Where every operand is 16-byte aligned (base, row stride, d): one CTA per row, one 16-byte
+// vector per thread and pass (the row stays in registers between the two passes, up to
+// kVecPerThread vectors a thread), the sum of squares reduced across the CTA; so a
+// decode-sized batch (a few hundred rows) still spreads over every SM. Otherwise one warp
+// per row, element-wise.
 #include "m3_common.cuh"
 #include "rmsnorm.cuh"
 
@@ -12,7 +14,6 @@ namespace m3 {
 namespace {
 
 constexpr int kRowsPerCta = 8;
-constexpr int kMaxVec = 8;
 
 template <typename T>
 struct alignas(16) Vec {
@@ -20,24 +21,42 @@ struct alignas(16) Vec {
   T e[N];
 };
 
+constexpr int kVecPerThread = 4;
+constexpr int kMaxRowThreads = 512;
+
+// N weights from element i0 (16-byte aligned): one vector when the weight has x's width,
+// else as float4s
 template <typename TX, typename TW>
-__global__ void __launch_bounds__(32 * kRowsPerCta) rmsnorm_vec_kernel(NormParams p) {
+__device__ __forceinline__ void load_w(const TW* w, int64_t i0, float (&out)[16 / sizeof(TX)]) {
+  constexpr int N = 16 / sizeof(TX);
+  if constexpr (sizeof(TW) == sizeof(TX)) {
+    const Vec<TW> v = *reinterpret_cast<const Vec<TW>*>(w + i0);
+#pragma unroll
+    for (int k = 0; k < N; ++k) out[k] = to_f32(v.e[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < N; ++k) out[k] = to_f32(w[i0 + k]);
+  }
+}
+
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(kMaxRowThreads) rmsnorm_vec_kernel(NormParams p) {
   using V = Vec<TX>;
   constexpr int N = V::N;
-  const int lane = threadIdx.x & 31;
-  const int64_t r = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
-  if (r >= p.rows) return;
+  __shared__ float red[32];
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t r = blockIdx.x;
   const int nv = (int)(p.d / N);
   const V* x = reinterpret_cast<const V*>(reinterpret_cast<const TX*>(p.x) + r * p.sx);
   const V* res = p.res ? reinterpret_cast<const V*>(reinterpret_cast<const TX*>(p.res) + r * p.sres) : nullptr;
   V* hout = p.hout ? reinterpret_cast<V*>(reinterpret_cast<TX*>(p.hout) + r * p.shout) : nullptr;
   V* out = reinterpret_cast<V*>(reinterpret_cast<TX*>(p.out) + r * p.sout);
   const TW* w = reinterpret_cast<const TW*>(p.w);
-  V hv[kMaxVec];
+  V hv[kVecPerThread];
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxVec; ++j) {
-    const int i = lane + 32 * j;
+  for (int j = 0; j < kVecPerThread; ++j) {
+    const int i = tid + nt * j;
     if (i < nv) {
       hv[j] = x[i];
       if (res) {
@@ -48,15 +67,15 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) rmsnorm_vec_kernel(NormParam
     }
   }
 #pragma unroll
-  for (int j = 0; j < kMaxVec; ++j) {
-    const int i = lane + 32 * j;
+  for (int j = 0; j < kVecPerThread; ++j) {
+    const int i = tid + nt * j;
     if (i < nv) {
       if (hout) hout[i] = hv[j];
 #pragma unroll
       for (int k = 0; k < N; ++k) ss = fmaf(to_f32(hv[j].e[k]), to_f32(hv[j].e[k]), ss);
     }
   }
-  for (int i = lane + 32 * kMaxVec; i < nv; i += 32) {  // rows longer than the register cache
+  for (int i = tid + nt * kVecPerThread; i < nv; i += nt) {  // rows longer than the register cache
     V v = x[i];
     if (res) {
       const V rv = res[i];
@@ -69,20 +88,31 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) rmsnorm_vec_kernel(NormParam
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float rms = sqrtf(ss / (float)p.d + p.eps);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < (nt >> 5) ? red[lane] : 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxVec; ++j) {
-    const int i = lane + 32 * j;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float rms = sqrtf(red[0] / (float)p.d + p.eps);
+#pragma unroll
+  for (int j = 0; j < kVecPerThread; ++j) {
+    const int i = tid + nt * j;
     if (i < nv) {
+      float wk[N];
+      load_w<TX, TW>(w, (int64_t)i * N, wk);
       V o;
 #pragma unroll
-      for (int k = 0; k < N; ++k) o.e[k] = from_f32<TX>(to_f32(hv[j].e[k]) / rms * to_f32(w[i * N + k]));
+      for (int k = 0; k < N; ++k) o.e[k] = from_f32<TX>(to_f32(hv[j].e[k]) / rms * wk[k]);
       out[i] = o;
     }
   }
-  for (int i = lane + 32 * kMaxVec; i < nv; i += 32) {
+  for (int i = tid + nt * kVecPerThread; i < nv; i += nt) {
     V v;
-    if (hout) v = hout[i];  // written above by this lane (hout may alias x)
+    if (hout) v = hout[i];  // written above by this thread (hout may alias x)
     else {
       v = x[i];
       if (res) {
@@ -91,9 +121,11 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) rmsnorm_vec_kernel(NormParam
         for (int k = 0; k < N; ++k) v.e[k] = from_f32<TX>(to_f32(v.e[k]) + to_f32(rv.e[k]));
       }
     }
+    float wk[N];
+    load_w<TX, TW>(w, (int64_t)i * N, wk);
     V o;
 #pragma unroll
-    for (int k = 0; k < N; ++k) o.e[k] = from_f32<TX>(to_f32(v.e[k]) / rms * to_f32(w[i * N + k]));
+    for (int k = 0; k < N; ++k) o.e[k] = from_f32<TX>(to_f32(v.e[k]) / rms * wk[k]);
     out[i] = o;
   }
 }
@@ -139,9 +171,18 @@ template <typename TX, typename TW>
 void launch_t(const NormParams& p, unsigned grid, cudaStream_t s) {
   const int es = (int)sizeof(TX);
   const bool vec = (p.d * es) % 16 == 0 && al16(p.x, p.sx, es) && al16(p.res, p.sres, es) &&
-                   al16(p.out, p.sout, es) && al16(p.hout, p.shout, es);
-  if (vec) rmsnorm_vec_kernel<TX, TW><<<grid, 32 * kRowsPerCta, 0, s>>>(p);
-  else rmsnorm_kernel<TX, TW><<<grid, 32 * kRowsPerCta, 0, s>>>(p);
+                   al16(p.out, p.sout, es) && al16(p.hout, p.shout, es) && al16(p.w, 0, es) &&
+                   p.rows <= INT32_MAX;
+  if (vec) {
+    // one thread per 16-byte vector, whole warps, at most kMaxRowThreads
+    const int64_t nv = p.d / (16 / es);
+    int nt = (int)((nv + 31) / 32 * 32);
+    if (nt > kMaxRowThreads) nt = kMaxRowThreads;
+    if (nt < 32) nt = 32;
+    rmsnorm_vec_kernel<TX, TW><<<(unsigned)p.rows, nt, 0, s>>>(p);
+  } else {
+    rmsnorm_kernel<TX, TW><<<grid, 32 * kRowsPerCta, 0, s>>>(p);
+  }
 }
 
 }  // namespace

@@ -17,7 +17,9 @@ MAX_DIMS = 6
 
 M3_FLOAT32, M3_BFLOAT16, M3_FLOAT16 = 0, 1, 2
 M3_OK, M3_ERR_INVALID_ARGUMENT, M3_ERR_UNSUPPORTED, M3_ERR_CUDA, M3_ERR_WORKSPACE = 0, 1, 2, 3, 4
-_DTYPE_CODE = {torch.float32: M3_FLOAT32, torch.bfloat16: M3_BFLOAT16, torch.float16: M3_FLOAT16}
+M3_INT64 = 3
+_DTYPE_CODE = {torch.float32: M3_FLOAT32, torch.bfloat16: M3_BFLOAT16, torch.float16: M3_FLOAT16,
+               torch.int64: M3_INT64}
 _STATUS = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "workspace"}
 
 
@@ -74,6 +76,7 @@ _SIGS = {
     "m3_device_timeouts": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "m3_layer_prologue": ([ctypes.c_void_p] + [_P] * 12 + [ctypes.c_void_p], ctypes.c_int),
     "m3_silu_gate": ([_P] * 3 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_argmax_rows": ([_P, _P, ctypes.c_void_p], ctypes.c_int),
 }
 
 _lib = None

@@ -11,7 +11,7 @@ import torch.nn.functional as F
 
 from .config import MambaConfig
 from .layer import Mamba3
-from .ops import RMSNorm, rmsnorm
+from .ops import RMSNorm, argmax_rows, rmsnorm
 
 
 class MambaBlock(nn.Module):
@@ -160,7 +160,7 @@ class DecodeGraph:
                 h = rmsnorm(x, nxt.weight, nxt.eps, residual=m.mlp_layers[i](h), residual_out=x)
         logits = m.lm_head(h)
         if self.greedy:
-            self.tokens.copy_(logits.argmax(-1))
+            argmax_rows(logits, out=self.tokens)
         return logits
 
     def reset(self):

@@ -68,6 +68,21 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.T
     return out
 
 
+def argmax_rows(logits: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """logits.argmax(-1) as int64 (first index of the maximum, NaN as the maximum) through
+    m3_argmax_rows; ``out`` (contiguous int64, one element per row) receives it in place."""
+    _require_cuda("argmax_rows", logits)
+    logits = _inner(logits)
+    if out is None:
+        out = torch.empty(logits.shape[:-1], dtype=torch.int64, device=logits.device)
+    lib = L.load()
+    a = L.pack(logits, out)
+    with torch.cuda.device(logits.device):
+        L.check(lib.m3_argmax_rows(a.ptrs[0], a.ptrs[1], torch.cuda.current_stream(logits.device).cuda_stream),
+                "m3_argmax_rows")
+    return out
+
+
 def build_rope_freqs(num_angles: int, device=None) -> torch.Tensor:
     i = torch.arange(num_angles, device=device, dtype=torch.float32)
     return 1.0 / (10000.0 ** (i / num_angles))

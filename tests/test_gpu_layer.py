@@ -147,13 +147,17 @@ def test_decode_graph_matches_step(name):
             assert torch.equal(gt, tok)
 
 
-# Shapes that route the decode step through each kernel variant: MIMO warp-per-(b,h)
-# kernel (d_state 32 / 64 / 128 with mimo_rank * d_state / 32 <= 16; rank rounded up to a
-# power of two; headdim <= 64 or up to 256) and the CTA-per-(b,h)
-# kernels (MIMO d_state 48 or 256; SISO).
+# Shapes that route the decode step through each kernel variant: the MIMO vector-pair
+# kernel (d_state and headdim 64 / 128; rank rounded up to a power of two), the MIMO
+# warp-per-(b,h) kernel (d_state 32 / 64 / 128 with mimo_rank * d_state / 32 <= 16, other
+# headdims up to 256) and the CTA-per-(b,h) kernels (MIMO d_state 48 or 256; SISO).
 STEP_SHAPES = [
     dict(d_state=64, headdim=32, is_mimo=True, mimo_rank=8),
     dict(d_state=128, headdim=64, is_mimo=True, mimo_rank=4),
+    dict(d_state=64, headdim=64, is_mimo=True, mimo_rank=4),
+    dict(d_state=128, headdim=128, is_mimo=True, mimo_rank=8),
+    dict(d_state=64, headdim=64, is_mimo=True, mimo_rank=1),
+    dict(d_state=64, headdim=64, is_mimo=True, mimo_rank=2, rope_fraction=1.0),
     dict(d_state=32, headdim=64, is_mimo=True, mimo_rank=1),
     dict(d_state=64, headdim=128, is_mimo=True, mimo_rank=3),
     dict(d_state=48, headdim=32, is_mimo=True, mimo_rank=2),

@@ -67,3 +67,26 @@ def test_rmsnorm_empty_and_errors():
     assert rmsnorm(torch.empty(0, 16, device=DEV), w, 1e-5).shape == (0, 16)
     with pytest.raises(RuntimeError, match="weight"):
         rmsnorm(torch.randn(4, 16, device=DEV), torch.ones(15, device=DEV), 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(256, 50000), (3, 7), (2, 5, 1003), (1, 64)])
+def test_argmax_rows_matches_torch(dtype, shape):
+    """m3_argmax_rows == torch.argmax(-1): first index of the maximum, ties and NaN rows
+    included, vector and element-wise paths."""
+    from mamba3_ssm.ops import argmax_rows
+    g = torch.Generator(device="cpu").manual_seed(sum(shape))
+    x = torch.randn(shape, generator=g).to(dtype)
+    flat = x.reshape(-1, shape[-1])
+    flat[0, :] = 1.0                       # all ties: index 0
+    if flat.shape[0] > 1:
+        flat[1, shape[-1] // 2] = float("nan")  # NaN counts as the maximum
+    if flat.shape[0] > 2 and shape[-1] > 3:
+        flat[2, 1] = flat[2, 3] = 100.0    # repeated maximum: the first
+    x = x.to(DEV)
+    got = argmax_rows(x)
+    assert got.dtype == torch.int64 and got.shape == x.shape[:-1]
+    assert torch.equal(got, x.argmax(-1))
+    out = torch.empty(x.shape[:-1], dtype=torch.int64, device=DEV)
+    argmax_rows(x, out=out)
+    assert torch.equal(out, x.argmax(-1))
