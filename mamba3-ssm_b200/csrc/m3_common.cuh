@@ -34,6 +34,20 @@ __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + expf
 // torch.nn.functional.softplus, beta = 1, threshold = 20
 __device__ __forceinline__ float softplusf_(float v) { return v > 20.0f ? v : log1pf(expf(v)); }
 
+// Logistic function from the hardware exp / divide approximations (relative error a few
+// 1e-7), for gates and the trapezoid weight of the inference paths.
+__device__ __forceinline__ float fast_sigmoid(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
+
+// sin and cos of an angle of any size: Cody-Waite reduction by 2 pi with a two-part
+// constant (k = rint(x / 2pi), r = (x - k C1) - k C2, C1 = 2 pi rounded to fp32,
+// C2 = 2 pi - C1), then the hardware approximations on |r| <= pi (absolute error ~1e-6).
+__device__ __forceinline__ void sincos_reduced(float x, float* sn, float* cs) {
+  const float k = rintf(x * 0.159154943091895336f);
+  float r = fmaf(-k, 6.28318548202514648f, x);
+  r = fmaf(-k, -1.74845553146951715e-07f, r);
+  __sincosf(r, sn, cs);
+}
+
 template <typename T> struct DT_;
 template <> struct DT_<float> { static constexpr int id = M3_FLOAT32; };
 template <> struct DT_<__nv_bfloat16> { static constexpr int id = M3_BFLOAT16; };

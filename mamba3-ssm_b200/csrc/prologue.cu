@@ -22,10 +22,15 @@ namespace {
 // from tile to tile
 constexpr int kAT = 128;
 
+// CTA per (b, h), thread = time step of a kAT-step tile. Each thread carries its step's
+// angles 16 at a time in registers: a warp scan over the tile, the warp totals through
+// shared memory (two barriers per 16 angles), then one (b, l, h) row of angles written as
+// 16-byte vectors (the S angles of a row are contiguous).
 template <typename TZ>
 __global__ void __launch_bounds__(kAT) prologue_angle_kernel(PrologueParams a) {
-  __shared__ float wsum[kAT / 32][64];
-  __shared__ float carry[64];
+  constexpr int kS = 16;
+  __shared__ float wsum[kAT / 32][kS];
+  __shared__ float carry[256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int u = blockIdx.x, b = u / a.H, h = u - b * a.H;
   const int H = a.H, S = a.S;
@@ -33,6 +38,7 @@ __global__ void __launch_bounds__(kAT) prologue_angle_kernel(PrologueParams a) {
   const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
   const float dtb = a.dt_bias[h];
   const TZ* base = reinterpret_cast<const TZ*>(a.zx) + (int64_t)b * a.s_zb;
+  const bool vec = (S % 4) == 0 && (reinterpret_cast<uintptr_t>(a.angles) & 15) == 0;
   for (int s0 = tid; s0 < S; s0 += kAT) carry[s0] = 0.f;
   __syncthreads();
   for (int l0 = 0; l0 < a.L; l0 += kAT) {
@@ -48,22 +54,44 @@ __global__ void __launch_bounds__(kAT) prologue_angle_kernel(PrologueParams a) {
       a.ADT[o] = A * dtv;
       a.trap[o] = to_f32(row[off_tr + h]);
     }
-    for (int s0 = 0; s0 < S; ++s0) {
-      float x = v ? to_f32(row[off_ang + s0]) * dtv : 0.f;
+    for (int s0 = 0; s0 < S; s0 += kS) {
+      float x[kS];
 #pragma unroll
-      for (int k = 1; k < 32; k <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, x, k);
-        if (lane >= k) x += y;
+      for (int k = 0; k < kS; ++k) x[k] = (v && s0 + k < S) ? to_f32(row[off_ang + s0 + k]) * dtv : 0.f;
+#pragma unroll
+      for (int of = 1; of < 32; of <<= 1) {
+#pragma unroll
+        for (int k = 0; k < kS; ++k) {
+          const float y = __shfl_up_sync(0xffffffffu, x[k], of);
+          if (lane >= of) x[k] += y;
+        }
       }
-      if (lane == 31) wsum[warp][s0] = x;
+      if (lane == 31)
+#pragma unroll
+        for (int k = 0; k < kS; ++k) wsum[warp][k] = x[k];
       __syncthreads();
-      float pre = carry[s0];
-      for (int w = 0; w < warp; ++w) pre += wsum[w][s0];
-      if (v) a.angles[o * S + s0] = pre + x;
-      __syncthreads();
-      if (tid == kAT - 1) carry[s0] = pre + x;
-      // the last thread's total (tile end) becomes the next tile's carry; readers of
-      // carry[s0] for this tile are past the barrier above
+#pragma unroll
+      for (int k = 0; k < kS; ++k) {
+        float pre = s0 + k < S ? carry[s0 + k] : 0.f;
+        for (int w = 0; w < warp; ++w) pre += wsum[w][k];
+        x[k] += pre;
+      }
+      if (v) {
+        float* dst = a.angles + o * S + s0;
+        if (vec && s0 + kS <= S) {
+#pragma unroll
+          for (int k = 0; k < kS; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(x[k], x[k + 1], x[k + 2], x[k + 3]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < kS; ++k)
+            if (s0 + k < S) dst[k] = x[k];
+        }
+      }
+      __syncthreads();  // carry and wsum read by every thread before they change
+      if (tid == kAT - 1)
+#pragma unroll
+        for (int k = 0; k < kS; ++k)
+          if (s0 + k < S) carry[s0 + k] = x[k];
     }
     __syncthreads();
   }
@@ -124,11 +152,11 @@ __global__ void __launch_bounds__(256) prologue_bc_kernel(PrologueParams a) {
         ssb += __shfl_xor_sync(0xffffffffu, ssb, o);
         ssc += __shfl_xor_sync(0xffffffffu, ssc, o);
       }
-      const float rb = sqrtf(ssb / (float)D + a.eps), rc = sqrtf(ssc / (float)D + a.eps);
+      const float rb = 1.0f / sqrtf(ssb / (float)D + a.eps), rc = 1.0f / sqrtf(ssc / (float)D + a.eps);
 #pragma unroll
       for (int j = 0; j < PPL; ++j) {
-        b0[j] = b0[j] / rb * wb0[j]; b1[j] = b1[j] / rb * wb1[j];
-        c0[j] = c0[j] / rc * wc0[j]; c1[j] = c1[j] / rc * wc1[j];
+        b0[j] = b0[j] * rb * wb0[j]; b1[j] = b1[j] * rb * wb1[j];
+        c0[j] = c0[j] * rc * wc0[j]; c1[j] = c1[j] * rc * wc1[j];
       }
     }
     const float* bb = a.B_bias + ((int64_t)h * R + r) * D;
@@ -141,11 +169,13 @@ __global__ void __launch_bounds__(256) prologue_bc_kernel(PrologueParams a) {
       const int k = lane + 32 * j;
       if (k < half) {
         const int d0 = 2 * k;
-        float x0 = b0[j] + bb[d0], x1 = b1[j] + bb[d0 + 1];
-        float y0 = c0[j] + cb[d0], y1 = c1[j] + cb[d0 + 1];
+        const float2 bv = __ldg(reinterpret_cast<const float2*>(bb + d0));
+        const float2 cv = __ldg(reinterpret_cast<const float2*>(cb + d0));
+        float x0 = b0[j] + bv.x, x1 = b1[j] + bv.y;
+        float y0 = c0[j] + cv.x, y1 = c1[j] + cv.y;
         if (k < npair) {
           float sn, cs;
-          sincosf(ang[k], &sn, &cs);
+          sincos_reduced(ang[k], &sn, &cs);
           const float t0 = x0 * cs - x1 * sn, u0 = y0 * cs - y1 * sn;
           x1 = x0 * sn + x1 * cs;
           y1 = y0 * sn + y1 * cs;
@@ -186,13 +216,13 @@ __global__ void __launch_bounds__(256) gate_kernel(GateParams a) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const float zz = to_f32(zv.e[k]);
-        ov.e[k] = from_f32<TO>(to_f32(yv.e[k]) * (zz * sigmoidf_(zz)));
+        ov.e[k] = from_f32<TO>(to_f32(yv.e[k]) * (zz * fast_sigmoid(zz)));
       }
       *reinterpret_cast<V8<TO>*>(o) = ov;
     } else {
       for (int k = 0; k < 8 && p0 + k < a.P; ++k) {
         const float zz = to_f32(z[k]);
-        o[k] = from_f32<TO>(to_f32(y[k]) * (zz * sigmoidf_(zz)));
+        o[k] = from_f32<TO>(to_f32(y[k]) * (zz * fast_sigmoid(zz)));
       }
     }
   }
@@ -203,6 +233,8 @@ __global__ void __launch_bounds__(256) gate_kernel(GateParams a) {
 int launch_prologue(const PrologueParams& p, int zdt, int odt, cudaStream_t s) {
   if (p.S > 64) return fail(M3_ERR_UNSUPPORTED, "prologue: more than 64 rope angles");
   if (p.D % 2 || p.D > 256 || p.R > 8) return fail(M3_ERR_UNSUPPORTED, "prologue: d_state odd or above 256, or rank above 8");
+  if ((reinterpret_cast<uintptr_t>(p.B_bias) | reinterpret_cast<uintptr_t>(p.C_bias)) & 7)
+    return fail(M3_ERR_UNSUPPORTED, "prologue: B_bias / C_bias must be 8-byte aligned");
   const unsigned ga = (unsigned)(p.Bn * p.H);
   if ((int64_t)p.Bn * p.L > 2147483647LL) return fail(M3_ERR_UNSUPPORTED, "prologue: batch * seqlen too large");
   const dim3 gb((unsigned)((int64_t)p.Bn * p.L), (unsigned)((p.R + 7) / 8));

@@ -2,11 +2,11 @@
 // * weight, returned in x.dtype), with the block's residual add (block.py:20-29:
 // x + mixer(norm(x))) optionally fused in front: h = x + res is rounded to x.dtype exactly
 // as the eager add would, written out, and normalised.
-// Where every operand is 16-byte aligned (base, row stride, d): one CTA per row, one 16-byte
-// vector per thread and pass (the row stays in registers between the two passes, up to
-// kVecPerThread vectors a thread), the sum of squares reduced across the CTA; so a
-// decode-sized batch (a few hundred rows) still spreads over every SM. Otherwise one warp
-// per row, element-wise.
+// Where every operand is 16-byte aligned (base, row stride, d) the row moves in 16-byte
+// vectors and stays in registers between the two passes: up to kCtaRowsMax rows (a decode
+// batch) one CTA per row, one vector per thread, the sum of squares reduced across the CTA,
+// so a few hundred rows still spread over every SM; beyond that one warp per row.
+// Otherwise one warp per row, element-wise.
 #include "m3_common.cuh"
 #include "rmsnorm.cuh"
 
@@ -23,6 +23,8 @@ struct alignas(16) Vec {
 
 constexpr int kVecPerThread = 4;
 constexpr int kMaxRowThreads = 512;
+// up to this many rows (a decode batch) one CTA per row; beyond, one warp per row
+constexpr int64_t kCtaRowsMax = 2048;
 
 // N weights from element i0 (16-byte aligned): one vector when the weight has x's width,
 // else as float4s
@@ -130,6 +132,92 @@ __global__ void __launch_bounds__(kMaxRowThreads) rmsnorm_vec_kernel(NormParams 
   }
 }
 
+// One warp per row (many rows: a CTA per row would leave too few rows per SM in flight
+// for the register budget); the row cached in registers up to 32 * kWarpVec vectors.
+constexpr int kWarpVec = 8;
+
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(32 * kRowsPerCta) rmsnorm_vec_warp_kernel(NormParams p) {
+  using V = Vec<TX>;
+  constexpr int N = V::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+  if (r >= p.rows) return;
+  const int nv = (int)(p.d / N);
+  const V* x = reinterpret_cast<const V*>(reinterpret_cast<const TX*>(p.x) + r * p.sx);
+  const V* res = p.res ? reinterpret_cast<const V*>(reinterpret_cast<const TX*>(p.res) + r * p.sres) : nullptr;
+  V* hout = p.hout ? reinterpret_cast<V*>(reinterpret_cast<TX*>(p.hout) + r * p.shout) : nullptr;
+  V* out = reinterpret_cast<V*>(reinterpret_cast<TX*>(p.out) + r * p.sout);
+  const TW* w = reinterpret_cast<const TW*>(p.w);
+  V hv[kWarpVec];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kWarpVec; ++j) {
+    const int i = lane + 32 * j;
+    if (i < nv) {
+      hv[j] = x[i];
+      if (res) {
+        const V rv = res[i];
+#pragma unroll
+        for (int k = 0; k < N; ++k) hv[j].e[k] = from_f32<TX>(to_f32(hv[j].e[k]) + to_f32(rv.e[k]));
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kWarpVec; ++j) {
+    const int i = lane + 32 * j;
+    if (i < nv) {
+      if (hout) hout[i] = hv[j];
+#pragma unroll
+      for (int k = 0; k < N; ++k) ss = fmaf(to_f32(hv[j].e[k]), to_f32(hv[j].e[k]), ss);
+    }
+  }
+  for (int i = lane + 32 * kWarpVec; i < nv; i += 32) {  // rows longer than the register cache
+    V v = x[i];
+    if (res) {
+      const V rv = res[i];
+#pragma unroll
+      for (int k = 0; k < N; ++k) v.e[k] = from_f32<TX>(to_f32(v.e[k]) + to_f32(rv.e[k]));
+      if (hout) hout[i] = v;
+    }
+#pragma unroll
+    for (int k = 0; k < N; ++k) ss = fmaf(to_f32(v.e[k]), to_f32(v.e[k]), ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rms = sqrtf(ss / (float)p.d + p.eps);
+#pragma unroll
+  for (int j = 0; j < kWarpVec; ++j) {
+    const int i = lane + 32 * j;
+    if (i < nv) {
+      float wk[N];
+      load_w<TX, TW>(w, (int64_t)i * N, wk);
+      V o;
+#pragma unroll
+      for (int k = 0; k < N; ++k) o.e[k] = from_f32<TX>(to_f32(hv[j].e[k]) / rms * wk[k]);
+      out[i] = o;
+    }
+  }
+  for (int i = lane + 32 * kWarpVec; i < nv; i += 32) {
+    V v;
+    if (hout) v = hout[i];  // written above by this lane (hout may alias x)
+    else {
+      v = x[i];
+      if (res) {
+        const V rv = res[i];
+#pragma unroll
+        for (int k = 0; k < N; ++k) v.e[k] = from_f32<TX>(to_f32(v.e[k]) + to_f32(rv.e[k]));
+      }
+    }
+    float wk[N];
+    load_w<TX, TW>(w, (int64_t)i * N, wk);
+    V o;
+#pragma unroll
+    for (int k = 0; k < N; ++k) o.e[k] = from_f32<TX>(to_f32(v.e[k]) / rms * wk[k]);
+    out[i] = o;
+  }
+}
+
 template <typename TX, typename TW>
 __global__ void __launch_bounds__(32 * kRowsPerCta) rmsnorm_kernel(NormParams p) {
   const int lane = threadIdx.x & 31;
@@ -173,7 +261,9 @@ void launch_t(const NormParams& p, unsigned grid, cudaStream_t s) {
   const bool vec = (p.d * es) % 16 == 0 && al16(p.x, p.sx, es) && al16(p.res, p.sres, es) &&
                    al16(p.out, p.sout, es) && al16(p.hout, p.shout, es) && al16(p.w, 0, es) &&
                    p.rows <= INT32_MAX;
-  if (vec) {
+  if (vec && p.rows > kCtaRowsMax) {
+    rmsnorm_vec_warp_kernel<TX, TW><<<grid, 32 * kRowsPerCta, 0, s>>>(p);
+  } else if (vec) {
     // one thread per 16-byte vector, whole warps, at most kMaxRowThreads
     const int64_t nv = p.d / (16 / es);
     int nt = (int)((nv + 31) / 32 * 32);
