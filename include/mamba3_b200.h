@@ -103,7 +103,7 @@ int m3_siso_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
  * gradient; cuda_backend.py:327); this returns the gradients autograd produces through
  * the loop of ops.py:166-175.
  * workspace: buffer of at least m3_siso_scan_bwd_workspace_size() bytes, 256-byte
- * aligned. For bf16 inputs with headdim 64 and d_state 128 a workspace of that size lets
+ * aligned. For bf16 inputs with headdim 64 and d_state 128 or 64 a workspace of that size lets
  * the call take the chunked tensor-core path (it recomputes the forward's chunk states
  * into the workspace first); a workspace of only 4 * batch * nheads * seqlen bytes selects
  * the CUDA-core path, which every shape supports.
@@ -152,7 +152,8 @@ int m3_siso_scan_bwd_noalloc(const m3_tensor* x, const m3_tensor* B, const m3_te
  *                              the same inputs and a workspace of
  *                              m3_siso_scan_bwd_kstates_workspace_size bytes.
  * M3_ERR_UNSUPPORTED when the inputs are outside the chunked kernels (dtype, headdim 64,
- * d_state 128, 16-byte aligned rows). */
+ * d_state 128 or 64, 16-byte aligned rows). The state array holds 128 rows per chunk
+ * for either d_state. */
 size_t m3_siso_scan_kstates_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
                                  int64_t dstate, int x_dtype, int bc_dtype);
 size_t m3_siso_scan_bwd_kstates_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads);

@@ -219,8 +219,8 @@ static size_t chunked_bwd_ws_bytes(int64_t Bn, int64_t L, int64_t H) {
 size_t m3_siso_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
                                        int64_t dstate) {
   const size_t rec = sizeof(float) * (size_t)(batch * nheads * seqlen);
-  // headdim 64 / d_state 128 may take the chunked path (bf16); size for it
-  if (headdim == 64 && dstate == 128) {
+  // headdim 64 / d_state 128 or 64 may take the chunked path (bf16); size for it
+  if (headdim == 64 && (dstate == 128 || dstate == 64)) {
     const size_t ch = chunked_bwd_ws_bytes(batch, seqlen, nheads);
     return ch > rec ? ch : rec;
   }
@@ -229,7 +229,7 @@ size_t m3_siso_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nh
 
 size_t m3_siso_scan_kstates_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
                                  int64_t dstate, int x_dtype, int bc_dtype) {
-  if (headdim != 64 || dstate != 128 || x_dtype != M3_BFLOAT16 || bc_dtype != M3_BFLOAT16 || seqlen <= 0 ||
+  if (headdim != 64 || (dstate != 128 && dstate != 64) || x_dtype != M3_BFLOAT16 || bc_dtype != M3_BFLOAT16 || seqlen <= 0 ||
       batch * nheads <= 0)
     return 0;
   return siso_chunk_kstate_bytes(batch, seqlen, nheads);

@@ -20,7 +20,7 @@ PFN_cuTensorMapEncodeTiled_v12000 chunk_encode_fn();
 int chunk_tmap_4d(CUtensorMap* m, const void* base, int64_t inner, int64_t H, int64_t L, int64_t Bn, const Str3& st);
 int chunk_sm_count();
 
-// Chunked tensor-core backward (siso_chunk_bwd.cu): bf16, P = 64, d_state 128.
+// Chunked tensor-core backward (siso_chunk_bwd.cu): bf16, P = 64, d_state 128 or 64.
 bool siso_chunk_bwd_supported(const SisoParams& p, int xdt, int bcdt);
 // bytes of the chunk-state array the forward writes for the backward
 size_t siso_chunk_kstate_bytes(int64_t Bn, int64_t L, int64_t H);

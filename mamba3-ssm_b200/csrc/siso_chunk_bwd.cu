@@ -1,5 +1,7 @@
 // Chunked SISO scan backward on the sm_100a tensor cores (tcgen05 + TMA), bf16 I/O,
-// headdim P = 64, d_state D = 128, fp32 accumulators. Gradients of ssm_scan_siso
+// headdim P = 64, d_state D = 128 or 64, fp32 accumulators. For d_state 64 the upper halves
+// of the C / B tiles stay zero (never loaded), the d-contractions take half the K steps,
+// and only the first 64 columns of dC / dB are stored. Gradients of ssm_scan_siso
 // (mamba3_ssm/ops.py:145-181, the loop :166-175) for the shapes of the chunked forward.
 //
 // Forward per chunk of Q = 128 steps (the k-formulation of the chunked forward): k_c is the
@@ -113,6 +115,8 @@ __device__ int g_bwd_error;  // set when a bounded wait gives up
 
 struct BwdArgs {
   int Bn, L, H, nch;
+  int D;    // d_state: 128, or 64
+  int nkd;  // K steps of 16 over d_state
   const float* adt; Str3 sadt;
   const float* dt; Str3 sdt;
   const float* trap; Str3 strap;
@@ -653,13 +657,15 @@ __device__ __forceinline__ void state_role(const BwdArgs& a, BSmem& s, uint32_t 
     }
     tc_fence_before();
     if (cp.first) {
-      const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * kD + d;
+      const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * a.D + d;
       float gsum = 0.f;
+      if (d < a.D) {
 #pragma unroll
-      for (int p = 0; p < kP; ++p) {
-        if (a.dh0) a.dh0[sb + (int64_t)p * kD] = sl.a0 * dk[p];
-        if (a.dbx0) a.dbx0[sb + (int64_t)p * kD] = sl.g0 * dk[p];
-        if (a.bx0) gsum = fmaf(dk[p], a.bx0[sb + (int64_t)p * kD], gsum);
+        for (int p = 0; p < kP; ++p) {
+          if (a.dh0) a.dh0[sb + (int64_t)p * a.D] = sl.a0 * dk[p];
+          if (a.dbx0) a.dbx0[sb + (int64_t)p * a.D] = sl.g0 * dk[p];
+          if (a.bx0) gsum = fmaf(dk[p], a.bx0[sb + (int64_t)p * a.D], gsum);
+        }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) gsum += __shfl_xor_sync(0xffffffffu, gsum, o);
@@ -721,11 +727,13 @@ __device__ __forceinline__ void control_role(const CUtensorMap* tm_x, const CUte
     // dY first: e^lambda o dY waits for it
     mbar_expect_tx(&s.dy_full, kTile);
     tma_load_4d(s.dy, tm_dy, &s.dy_full, 0, cp.h, cp.t0, cp.b);
-    mbar_expect_tx(&s.ld_full, 6 * kTile);  // C (2), B (2), X, k_c
+    mbar_expect_tx(&s.ld_full, (a.D == kD ? 6 : 4) * kTile);  // C (2 or 1), B (2 or 1), X, k_c
     tma_load_4d(s.c[0], tm_C, &s.ld_full, 0, cp.h, cp.t0, cp.b);
-    tma_load_4d(s.c[1], tm_C, &s.ld_full, 64, cp.h, cp.t0, cp.b);
     tma_load_4d(s.b[0], tm_B, &s.ld_full, 0, cp.h, cp.t0, cp.b);
-    tma_load_4d(s.b[1], tm_B, &s.ld_full, 64, cp.h, cp.t0, cp.b);
+    if (a.D == kD) {
+      tma_load_4d(s.c[1], tm_C, &s.ld_full, 64, cp.h, cp.t0, cp.b);
+      tma_load_4d(s.b[1], tm_B, &s.ld_full, 64, cp.h, cp.t0, cp.b);
+    }
     tma_load_4d(s.x, tm_x, &s.ld_full, 0, cp.h, cp.t0, cp.b);
     tma_load_2d(s.kc, tm_k, &s.ld_full, 0, (cp.u * a.nch + cp.c) * kD);
     lg = gg;
@@ -734,9 +742,11 @@ __device__ __forceinline__ void control_role(const CUtensorMap* tm_x, const CUte
       const BPos nx = bpos(a, gg + 1);
       tma_prefetch_l2_4d(tm_dy, 0, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_4d(tm_C, 0, nx.h, nx.t0, nx.b);
-      tma_prefetch_l2_4d(tm_C, 64, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_4d(tm_B, 0, nx.h, nx.t0, nx.b);
-      tma_prefetch_l2_4d(tm_B, 64, nx.h, nx.t0, nx.b);
+      if (a.D == kD) {
+        tma_prefetch_l2_4d(tm_C, 64, nx.h, nx.t0, nx.b);
+        tma_prefetch_l2_4d(tm_B, 64, nx.h, nx.t0, nx.b);
+      }
       tma_prefetch_l2_4d(tm_x, 0, nx.h, nx.t0, nx.b);
       tma_prefetch_l2_2d(tm_k, 0, (nx.u * a.nch + nx.c) * kD);
     }
@@ -745,9 +755,11 @@ __device__ __forceinline__ void control_role(const CUtensorMap* tm_x, const CUte
   auto store_outputs = [&](int gg) {
     const BPos op = bpos(a, gg);
     tma_store_4d(tm_dC, s.gh[0], 0, op.h, op.t0, op.b);
-    tma_store_4d(tm_dC, s.gh[1], 64, op.h, op.t0, op.b);
     tma_store_4d(tm_dB, s.ms[0], 0, op.h, op.t0, op.b);
-    tma_store_4d(tm_dB, s.ms[1], 64, op.h, op.t0, op.b);
+    if (a.D == kD) {
+      tma_store_4d(tm_dC, s.gh[1], 64, op.h, op.t0, op.b);
+      tma_store_4d(tm_dB, s.ms[1], 64, op.h, op.t0, op.b);
+    }
     bulk_commit();
   };
   if (G > 0) load(0);
@@ -760,16 +772,16 @@ __device__ __forceinline__ void control_role(const CUtensorMap* tm_x, const CUte
     tc_fence_after();
     // phase 1: what the phase-1 epilogue reads first
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColG, k2(c0, kk), k2(b0, kk), I_KK128, kk > 0);
+    for (int kk = 0; kk < a.nkd; ++kk) mma_ss(tbase + kColG, k2(c0, kk), k2(b0, kk), I_KK128, kk > 0);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) mma_ss(tbase + kColS, k1(dya, kk), k1(xa, kk), I_KK128, kk > 0);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColY1, k2(c0, kk), mn(ka, kk), I_KM64, kk > 0);
+    for (int kk = 0; kk < a.nkd; ++kk) mma_ss(tbase + kColY1, k2(c0, kk), mn(ka, kk), I_KM64, kk > 0);
     // the epilogue overwrites the staging tiles of g-1: their stores must have read them
     if (g > 0) bulk_wait_read0();
     mma_commit(&s.p1_done);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColT, k2(b0, kk), mn(na, kk), I_KM64, kk > 0);
+    for (int kk = 0; kk < a.nkd; ++kk) mma_ss(tbase + kColT, k2(b0, kk), mn(na, kk), I_KM64, kk > 0);
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColDK, mn(c0, kk), mn(ea, kk), I_MM64, kk > 0);
     mma_commit(&s.p1b_done);
@@ -838,6 +850,14 @@ siso_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
   if (warp == 1) {
     tmem_alloc(&s.tmem_base, kTmemCols);
     tmem_relinquish();
+  }
+  if (a.D < kD) {
+    // d_state 64: the upper halves of the C / B tiles are never loaded; they read as zero
+    for (int i = tid; i < 2 * (int)(kTile / 16); i += kThreads) {
+      uint8_t* t = i < (int)(kTile / 16) ? s.c[1] : s.b[1];
+      reinterpret_cast<uint4*>(t)[i % (kTile / 16)] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
   }
   tc_fence_before();
   __syncthreads();
@@ -951,7 +971,7 @@ size_t siso_chunk_bwd_scratch_bytes(int64_t Bn, int64_t L, int64_t H) {
 }
 
 bool siso_chunk_bwd_supported(const SisoParams& p, int xdt, int bcdt) {
-  if (p.D != kD) return false;
+  if (p.D != kD && p.D != 64) return false;
   SisoParams f = p;
   f.y = nullptr;
   f.sy = Str3{0, 0, 0};
@@ -975,6 +995,7 @@ int launch_siso_bwd_chunked(const SisoParams& p, float* scratch, cudaStream_t s)
   M3_TRY(chunk_tmap_4d(&mdc, p.dC, p.D, p.H, p.L, p.Bn, p.sdC));
   BwdArgs a{};
   a.Bn = p.Bn; a.L = p.L; a.H = p.H; a.nch = nch;
+  a.D = p.D; a.nkd = p.D / 16;
   a.adt = p.adt; a.sadt = p.sadt;
   a.dt = p.dt; a.sdt = p.sdt;
   a.trap = p.trap; a.strap = p.strap;

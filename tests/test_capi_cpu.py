@@ -47,6 +47,8 @@ def test_workspace_size_queries(lib):
     assert lib.m3_siso_scan_kstates_size(2, 300, 3, 64, 128, bf, bf) == 2 * 3 * 3 * 128 * 64 * 2
     assert lib.m3_siso_scan_kstates_size(2, 300, 3, 64, 128, _lib.M3_FLOAT32, bf) == 0
     assert lib.m3_siso_scan_kstates_size(2, 300, 3, 32, 128, bf, bf) == 0
+    assert lib.m3_siso_scan_kstates_size(2, 300, 3, 64, 64, bf, bf) == 2 * 3 * 3 * 128 * 64 * 2
+    assert lib.m3_siso_scan_kstates_size(2, 300, 3, 64, 32, bf, bf) == 0
     assert lib.m3_siso_scan_kstates_size(2, 0, 3, 64, 128, bf, bf) == 0
     assert lib.m3_siso_scan_bwd_kstates_workspace_size(2, 300, 3) == 12 * 2 * 300 * 3
     assert lib.m3_mimo_scan_bwd_workspace_size(2, 100, 3, 32, 64, 4) > 0

@@ -287,21 +287,22 @@ def _siso_grads(ins, h0=None, b0=None):
     return y, dy
 
 
+@pytest.mark.parametrize("Ds", [128, 64])
 @pytest.mark.parametrize("L", [1, 77, 128, 129, 300, 700])
 @pytest.mark.parametrize("states", [False, True])
-def test_siso_bf16_chunked_backward_against_oracle(L, states):
-    """The chunked tensor-core backward (bf16, headdim 64, d_state 128; the forward keeps its
-    chunk-start states for it) on ragged lengths, with and without initial states, against
-    the float64 adjoint of the loop."""
+def test_siso_bf16_chunked_backward_against_oracle(L, states, Ds):
+    """The chunked tensor-core backward (bf16, headdim 64, d_state 128 or 64; the forward
+    keeps its chunk-start states for it) on ragged lengths, with and without initial states,
+    against the float64 adjoint of the loop."""
     Bn = 2 if L <= 300 else 1
-    arrs, t = _inputs(500 + L, Bn, L, 2, 64, 128, dtype=torch.bfloat16)
+    arrs, t = _inputs(500 + L + Ds, Bn, L, 2, 64, Ds, dtype=torch.bfloat16)
     keys = ("x", "B", "C", "ADT", "DT", "trap", "D")
     ins = [t[k].requires_grad_(True) for k in keys]
     h0 = b0 = None
     if states:
         rng = np.random.default_rng(L)
-        h0 = torch.tensor(rng.standard_normal((Bn, 2, 64, 128)), dtype=torch.float32, device=DEV).requires_grad_(True)
-        b0 = torch.tensor(rng.standard_normal((Bn, 2, 64, 128)), dtype=torch.float32, device=DEV).requires_grad_(True)
+        h0 = torch.tensor(rng.standard_normal((Bn, 2, 64, Ds)), dtype=torch.float32, device=DEV).requires_grad_(True)
+        b0 = torch.tensor(rng.standard_normal((Bn, 2, 64, Ds)), dtype=torch.float32, device=DEV).requires_grad_(True)
     y, dy = _siso_grads(ins, h0, b0)
     npy = lambda v: None if v is None else v.detach().double().cpu().numpy()
     go = O.siso_scan_bwd(*[arrs[k] for k in keys], npy(dy), npy(h0), npy(b0))
