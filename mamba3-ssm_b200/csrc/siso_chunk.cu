@@ -167,15 +167,20 @@ __device__ __forceinline__ float ld_scal(const float* p, const Str3& s, int b, i
 }
 
 
-// xs[t][:] = w_t x[t][:] for the rows t = lane + 32 k
-__device__ __forceinline__ void write_xs_rows(const uint8_t* xt, uint8_t* xs, const float (&wk)[4], int lane) {
+// xs[t][:] = w_t x[t][:] for the rows t = lane + 32 k; each row's eight 16-byte chunks are
+// loaded before any store, so the loads are not held behind possibly aliasing stores
+__device__ __forceinline__ void write_xs_rows(const uint8_t* __restrict__ xt, uint8_t* __restrict__ xs,
+                                              const float (&wk)[4], int lane) {
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int t = lane + 32 * k;
     const float wt = wk[k];
+    uint4 row[8];
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) row[cc] = *reinterpret_cast<const uint4*>(xt + sw128_off(t, 8 * cc));
 #pragma unroll
     for (int cc = 0; cc < 8; ++cc) {
-      const uint4 v = *reinterpret_cast<const uint4*>(xt + sw128_off(t, 8 * cc));
+      const uint4 v = row[cc];
       const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
       uint32_t o[4];
 #pragma unroll
@@ -629,8 +634,10 @@ __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, i
 __global__ void __launch_bounds__(kThreads, 1)
 siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_B,
                       const __grid_constant__ CUtensorMap tm_C, ChunkArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte aligned base, derived from smem_raw so that accesses stay shared-space
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw + pad);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nch = (a.L + Q - 1) / Q;
   const int units = a.Bn * a.H;
