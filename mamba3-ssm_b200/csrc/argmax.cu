@@ -27,17 +27,36 @@ __global__ void __launch_bounds__(kThreads) argmax_rows_kernel(const T* __restri
   float best = -INFINITY;
   int64_t bi = n;  // beyond every index: any element beats it
   if (vec) {
-    constexpr int N = 16 / sizeof(T);
+    // four independent running maxima per thread, so four vector loads are in flight
+    constexpr int N = 16 / sizeof(T), kCh = 4;
     const int64_t nv = n / N;
-    for (int64_t j = threadIdx.x; j < nv; j += kThreads) {
-      const uint4 u = reinterpret_cast<const uint4*>(row)[j];
-      const T* e = reinterpret_cast<const T*>(&u);
+    float cb[kCh];
+    int64_t ci[kCh];
 #pragma unroll
-      for (int k = 0; k < N; ++k) {
-        const float v = to_f32(e[k]);
-        if (beats(v, j * N + k, best, bi)) { best = v; bi = j * N + k; }
+    for (int c = 0; c < kCh; ++c) { cb[c] = -INFINITY; ci[c] = n; }
+    for (int64_t j0 = threadIdx.x; j0 < nv; j0 += (int64_t)kThreads * kCh) {
+      uint4 u[kCh];
+#pragma unroll
+      for (int c = 0; c < kCh; ++c) {
+        const int64_t j = j0 + (int64_t)c * kThreads;
+        u[c] = j < nv ? reinterpret_cast<const uint4*>(row)[j] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int c = 0; c < kCh; ++c) {
+        const int64_t j = j0 + (int64_t)c * kThreads;
+        if (j < nv) {
+          const T* e = reinterpret_cast<const T*>(&u[c]);
+#pragma unroll
+          for (int k = 0; k < N; ++k) {
+            const float v = to_f32(e[k]);
+            if (beats(v, j * N + k, cb[c], ci[c])) { cb[c] = v; ci[c] = j * N + k; }
+          }
+        }
       }
     }
+#pragma unroll
+    for (int c = 0; c < kCh; ++c)
+      if (beats(cb[c], ci[c], best, bi)) { best = cb[c]; bi = ci[c]; }
   } else {
     for (int64_t j = threadIdx.x; j < n; j += kThreads) {
       const float v = to_f32(row[j]);

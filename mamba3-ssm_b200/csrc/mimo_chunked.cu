@@ -172,16 +172,33 @@ __global__ void __launch_bounds__(kCT) mimo_out_kernel(MimoParams a, const float
     if (c == nch - 1 && a.bx_last) a.bx_last[(int64_t)u * D + d] = bxp;
   }
   __syncthreads();
-  // yr_t[r] = C_t[r, :] . h_t + D xr_t[r]: one warp per (t, r), lanes over d
+  // yr_t[r] = C_t[r, :] . h_t + D xr_t[r]: a warp takes four (t, r) items at a time, lanes
+  // over d, so four items' loads of C are in flight together
   const float Dk = a.Dskip[h * a.sD];
   const int warp = tid >> 5, lane = tid & 31;
-  for (int pr = warp; pr < n * R; pr += kCT / 32) {
-    const int t = pr / R, r = pr - t * R;
-    float acc = 0.f;
-    for (int d = lane; d < D; d += 32) acc = fmaf(ldbcc<TB>(a.Cm, a.sC, b, t0 + t, r, h, d), s.H[t * D + d], acc);
+  constexpr int kIt = 4;
+  for (int pr0 = warp * kIt; pr0 < n * R; pr0 += (kCT / 32) * kIt) {
+    float acc[kIt];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) s.yr[pr] = fmaf(Dk, s.xr[(t + 1) * R + r], acc);
+    for (int j = 0; j < kIt; ++j) {
+      const int pr = pr0 + j;
+      acc[j] = 0.f;
+      if (pr < n * R) {
+        const int t = pr / R, r = pr - t * R;
+        for (int d = lane; d < D; d += 32) acc[j] = fmaf(ldbcc<TB>(a.Cm, a.sC, b, t0 + t, r, h, d), s.H[t * D + d], acc[j]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < kIt; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    if (lane < kIt && pr0 + lane < n * R) {
+      float v = acc[0];
+#pragma unroll
+      for (int j = 1; j < kIt; ++j) v = lane == j ? acc[j] : v;
+      const int pr = pr0 + lane, t = pr / R, r = pr - t * R;
+      s.yr[pr] = fmaf(Dk, s.xr[(t + 1) * R + r], v);
+    }
   }
   __syncthreads();
   // y_t = mimo_o^T yr_t
