@@ -611,6 +611,190 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_pair_kernel(StepPara
   }
 }
 
+// ------------------------------------------------------------------------------------
+// The same vector-pair layout with one B / C group (G = 1): a CTA takes one batch row and 8
+// consecutive heads (warp = head). Work every head of the row shares is done once per CTA:
+// warp 0 computes the RMSNorm factors of the row's B and C ranks and, on lanes 0-7, the
+// per-head scalars (two softplus, decay, trapezoid weights), handed over through shared
+// memory. RoPE is applied once per state pair instead of once per rank: the rotation is
+// linear and the same for every rank, so Bx = rot(sum_r xr_r b_r) and
+// C_r . h = c_r . rot^T(h), with b_r, c_r the normalised, weighted, biased rows.
+// ------------------------------------------------------------------------------------
+template <typename TZ, int DP, int PP, int RM>
+__global__ void __launch_bounds__(32 * kWarpRows) mimo_step_row_kernel(StepParams a) {
+  constexpr int D = 64 * DP, P = 64 * PP;
+  __shared__ float s_nrm[2 * 8];
+  __shared__ float s_sc[kWarpRows][5];  // DT, decay, w1, w2, D skip
+  const int R = a.R, H = a.H, S = a.S;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.y;
+  const int h0 = blockIdx.x * kWarpRows, h = h0 + warp;
+  const bool hv = h < H;
+  const int hh = hv ? h : h0;
+  const TZ* row = reinterpret_cast<const TZ*>(a.zxbcdt) + (int64_t)b * a.s_row;
+  const int off_B = 2 * a.d_inner, off_C = off_B + D * R, off_dt = off_C + D * R;
+  const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
+  // this (row, head)'s operands (all loads independent)
+  float2 Bv[RM][DP], Cv[RM][DP], xv[PP], zv[PP], hs[DP], bp[DP];
+#pragma unroll
+  for (int r = 0; r < RM; ++r)
+#pragma unroll
+    for (int q = 0; q < DP; ++q) {
+      const int d0 = 2 * lane + 64 * q;
+      Bv[r][q] = r < R ? Pair<TZ>::ld(row + off_B + r * D + d0) : make_float2(0.f, 0.f);
+      Cv[r][q] = r < R ? Pair<TZ>::ld(row + off_C + r * D + d0) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+  for (int q = 0; q < PP; ++q) {
+    const int p0 = 2 * lane + 64 * q;
+    xv[q] = Pair<TZ>::ld(row + a.d_inner + hh * P + p0);
+    zv[q] = Pair<TZ>::ld(row + hh * P + p0);
+  }
+  const int64_t sbase = ((int64_t)b * H + hh) * D;
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    hs[q] = *reinterpret_cast<const float2*>(a.ssm_in + sbase + 2 * lane + 64 * q);
+    bp[q] = *reinterpret_cast<const float2*>(a.bx_in + sbase + 2 * lane + 64 * q);
+  }
+  const int64_t abase = ((int64_t)b * H + hh) * S;
+  float ang_in[DP], ang_raw[DP];
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    const int i = lane + 32 * q;
+    ang_in[q] = i < S ? a.angle_in[abase + i] : 0.f;
+    ang_raw[q] = i < S ? to_f32(row[off_ang + i]) : 0.f;
+  }
+  if (warp == 0) {
+    // shared by the CTA's heads: the row's norm factors and, lanes 0-7, the heads' scalars
+    float ss[2 * RM];
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+      float sb = 0.f, sc = 0.f;
+#pragma unroll
+      for (int q = 0; q < DP; ++q) {
+        sb = fmaf(Bv[r][q].x, Bv[r][q].x, fmaf(Bv[r][q].y, Bv[r][q].y, sb));
+        sc = fmaf(Cv[r][q].x, Cv[r][q].x, fmaf(Cv[r][q].y, Cv[r][q].y, sc));
+      }
+      ss[r] = sb;
+      ss[RM + r] = sc;
+    }
+    warp_sum_n<2 * RM>(ss, lane);
+    if (lane < 2 * RM) {
+      float v = ss[0];
+#pragma unroll
+      for (int k = 1; k < 2 * RM; ++k) v = lane == k ? ss[k] : v;
+      s_nrm[lane < RM ? lane : 8 + lane - RM] = rsqrtf(v * (1.0f / D) + a.eps);
+    }
+    const int hl = h0 + lane;
+    if (lane < kWarpRows && hl < H) {
+      const float DT = softplusf_(to_f32(row[off_dt + hl]) + __ldg(a.dt_bias + hl));
+      const float A = -fminf(softplusf_(to_f32(row[off_A + hl])), -a.A_floor);  // layer.py:317
+      const float tr = fast_sigmoid(to_f32(row[off_tr + hl]));
+      s_sc[lane][0] = DT;
+      s_sc[lane][1] = expf(A * DT);
+      s_sc[lane][2] = 1.0f - 0.5f * tr;
+      s_sc[lane][3] = 0.5f * tr;
+      s_sc[lane][4] = __ldg(a.Dskip + hl);
+    }
+  }
+  __syncthreads();
+  if (!hv) return;
+  const float DT = s_sc[warp][0], decay = s_sc[warp][1], w1 = s_sc[warp][2], w2 = s_sc[warp][3],
+              Dk = s_sc[warp][4];
+  // angle update (layer.py:331-332); angle_out may alias angle_in: same lane, read above
+  float sn[DP], cs[DP];
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    const int i = lane + 32 * q;
+    const float an = ang_in[q] + ang_raw[q] * DT;
+    sincos_reduced(an, &sn[q], &cs[q]);
+    if (i < S) a.angle_out[abase + i] = an;
+  }
+  // normalise, weight, bias (the rotation comes once per pair below)
+  const float* Bb = a.B_bias + (int64_t)h * R * D;
+  const float* Cb = a.C_bias + (int64_t)h * R * D;
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    const int d0 = 2 * lane + 64 * q;
+    const float2 wb = ldg2(a.B_norm_w + d0), wc = ldg2(a.C_norm_w + d0);
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+      if (r >= R) break;
+      const float nb = s_nrm[r], nc = s_nrm[8 + r];
+      const float2 bb = ldg2(Bb + r * D + d0), cb = ldg2(Cb + r * D + d0);
+      Bv[r][q] = make_float2(fmaf(Bv[r][q].x * nb, wb.x, bb.x), fmaf(Bv[r][q].y * nb, wb.y, bb.y));
+      Cv[r][q] = make_float2(fmaf(Cv[r][q].x * nc, wc.x, cb.x), fmaf(Cv[r][q].y * nc, wc.y, cb.y));
+    }
+  }
+  // xr = mimo_x x (layer.py:346)
+  const float* mx = a.mimo_x + (int64_t)h * R * P;
+  const float* mo = a.mimo_o + (int64_t)h * R * P;
+  float xr[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) {
+    float acc = 0.f;
+    if (r < R) {
+#pragma unroll
+      for (int q = 0; q < PP; ++q) {
+        const float2 m = ldg2(mx + r * P + 2 * lane + 64 * q);
+        acc = fmaf(m.x, xv[q].x, fmaf(m.y, xv[q].y, acc));
+      }
+    }
+    xr[r] = acc;
+  }
+  warp_sum_n<RM>(xr, lane);
+  // state update (layer.py:347-351) and y_r = C_r h = c_r . rot^T(h)
+  float yr[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) yr[r] = 0.f;
+#pragma unroll
+  for (int q = 0; q < DP; ++q) {
+    const bool rot = lane + 32 * q < S;
+    float2 bxc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {  // zero B rows beyond R
+      bxc.x = fmaf(xr[r], Bv[r][q].x, bxc.x);
+      bxc.y = fmaf(xr[r], Bv[r][q].y, bxc.y);
+    }
+    if (rot) bxc = make_float2(bxc.x * cs[q] - bxc.y * sn[q], bxc.x * sn[q] + bxc.y * cs[q]);
+    float2 hn;
+    hn.x = fmaf(decay, hs[q].x, DT * fmaf(w1, bxc.x, w2 * bp[q].x));
+    hn.y = fmaf(decay, hs[q].y, DT * fmaf(w1, bxc.y, w2 * bp[q].y));
+    *reinterpret_cast<float2*>(a.ssm_out + sbase + 2 * lane + 64 * q) = hn;
+    *reinterpret_cast<float2*>(a.bx_out + sbase + 2 * lane + 64 * q) = bxc;
+    const float2 ht = rot ? make_float2(hn.x * cs[q] + hn.y * sn[q], hn.y * cs[q] - hn.x * sn[q]) : hn;
+#pragma unroll
+    for (int r = 0; r < RM; ++r) yr[r] = fmaf(Cv[r][q].x, ht.x, fmaf(Cv[r][q].y, ht.y, yr[r]));
+  }
+  warp_sum_n<RM>(yr, lane);
+  // y = mimo_o^T (y_r + D xr), gated by silu(z) (layer.py:352-356)
+  TZ* yo = reinterpret_cast<TZ*>(a.y) + (int64_t)b * a.s_y + h * P;
+#pragma unroll
+  for (int q = 0; q < PP; ++q) {
+    const int p0 = 2 * lane + 64 * q;
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+      if (r >= R) break;
+      const float2 m = ldg2(mo + r * P + p0);
+      const float yv = fmaf(Dk, xr[r], yr[r]);
+      acc.x = fmaf(yv, m.x, acc.x);
+      acc.y = fmaf(yv, m.y, acc.y);
+    }
+    const float2 z = zv[q];
+    Pair<TZ>::st(yo + p0, make_float2(acc.x * (z.x * fast_sigmoid(z.x)), acc.y * (z.y * fast_sigmoid(z.y))));
+  }
+}
+
+template <typename TZ, int DP, int PP>
+void launch_row_pp(const StepParams& p, cudaStream_t s) {
+  const dim3 grid((p.H + kWarpRows - 1) / kWarpRows, p.Bn);
+  if (p.R <= 1) mimo_step_row_kernel<TZ, DP, PP, 1><<<grid, 32 * kWarpRows, 0, s>>>(p);
+  else if (p.R <= 2) mimo_step_row_kernel<TZ, DP, PP, 2><<<grid, 32 * kWarpRows, 0, s>>>(p);
+  else if (p.R <= 4) mimo_step_row_kernel<TZ, DP, PP, 4><<<grid, 32 * kWarpRows, 0, s>>>(p);
+  else mimo_step_row_kernel<TZ, DP, PP, 8><<<grid, 32 * kWarpRows, 0, s>>>(p);
+}
+
 template <typename TZ, int DP, int PP>
 void launch_pair_pp(const StepParams& p, cudaStream_t s) {
   const dim3 grid(p.H, (p.Bn + kWarpRows - 1) / kWarpRows);
@@ -622,6 +806,16 @@ void launch_pair_pp(const StepParams& p, cudaStream_t s) {
 
 template <typename TZ>
 void launch_pair(const StepParams& p, cudaStream_t s) {
+  if (p.G == 1) {  // the row-per-CTA layout shares the group's norms between heads
+    if (p.D == 64) {
+      if (p.P == 64) launch_row_pp<TZ, 1, 1>(p, s);
+      else launch_row_pp<TZ, 1, 2>(p, s);
+    } else {
+      if (p.P == 64) launch_row_pp<TZ, 2, 1>(p, s);
+      else launch_row_pp<TZ, 2, 2>(p, s);
+    }
+    return;
+  }
   if (p.D == 64) {
     if (p.P == 64) launch_pair_pp<TZ, 1, 1>(p, s);
     else launch_pair_pp<TZ, 1, 2>(p, s);
