@@ -92,7 +92,7 @@ def max_over_ranks(values, dist=None, device=None):
 class ClockSampler:
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,clocks.mem")
 
     def __init__(self, gpu_ids):
         self.idx = ",".join(str(i) for i in gpu_ids)
@@ -130,7 +130,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.th.join(timeout=2)
-        sm, mx, reasons = [], [], set()
+        sm, mx, mem, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             f = [v.strip() for v in ln.split(",")]
@@ -144,10 +144,18 @@ class ClockSampler:
             for n, v in zip(names, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
+            if len(f) > 9:
+                try:
+                    mem.append(float(f[9]))
+                except ValueError:
+                    pass
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+               "samples": len(sm)}
+        if mem:
+            out["mem_mhz"] = statistics.median(mem)
+        return out
 
 
 # ----------------------------------------------------------------------------------
@@ -536,9 +544,16 @@ def main():
     def step():
         return ssm_scan_siso(x, Bm, Cm, ADT, DT, trap, Dw)
 
-    for _ in range(max(3, args.warmup)):
+    # untimed warm-up: at least W steps and at least ~1 s of work, so that the first timed
+    # step does not see the GPU's clocks still ramping up from idle
+    n_warm, t_w = 0, time.time()
+    while n_warm < max(3, args.warmup) or time.time() - t_w < 1.0:
         step()
+        n_warm += 1
+        if n_warm % 8 == 0:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
+    n_warm, = max_over_ranks([n_warm], pg, dev)
     K = args.steps
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     t_beg, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -652,7 +667,7 @@ def main():
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
-                "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+                "warmup": int(n_warm), "ms_per_step": ms_step, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": workload_config(world),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",

@@ -26,14 +26,17 @@
 //   C, B (64 KB)  2-stage ring; read by G, Y1 and dK, freed after dK (issued early)
 //   X    (16 KB)  per chunk parity; read by the scalar warps (w o X) and by Y2 after the mask
 //   w o X (16 KB) per chunk parity;  k_c^T (16 KB) one buffer
-// Roles:
-//   warp 0      TMA producer (one thread polling the C/B ring and the X ring, plus the L2
+// Roles (warp w issues from SM sub-partition w % 4, and TMEM lanes 32 (w % 4) .. +31 are
+// the only ones it can reach, so the mask warps of quadrant 3, whose rows have four blocks
+// on or below the diagonal, load sub-partition 3 four times as much as quadrant 0's; the
+// two scalar warps sit on sub-partitions 0 and 2 and the light producer on 3):
+//   warp 3      TMA producer (one thread polling the C/B ring and the X ring, plus the L2
 //               prefetch of later chunks)
 //   warp 1      tcgen05 MMA issuer (one thread polling three streams: G fed by the loads;
 //               dK and Y1 fed by the scalar and state warps; Y2 gated by the mask) and TMEM
 //               owner (512 columns: per chunk parity G (128, G' packed in place) and Y2
 //               (64); one Y1 (64) and one dK (64))
-//   warps 2-3   per-chunk scalars (decay cumsum, mu, block factors, state weights) into a
+//   warps 2, 0  per-chunk scalars (decay cumsum, mu, block factors, state weights) into a
 //               4-slot ring, even / odd chunks, running ahead of the consumers; then the
 //               chunk's w o X tile for dK (lane l owns rows l + 32 k, whose w it holds)
 //   warps 4-7   even chunks: G -> G' in TMEM (in place, packed bf16), then the epilogue
@@ -201,7 +204,7 @@ __device__ __noinline__ void stash_last_row(Smem& s, const uint8_t* xt, const ui
 }
 
 // ------------------------------------------------------------------------------------
-// warps 2 and 3: per-chunk scalars. Warp 2 takes the even chunks, warp 3 the odd ones;
+// warps 2 and 0: per-chunk scalars. Warp 2 takes the even chunks, warp 0 the odd ones;
 // each loads the raw ADT / DT / trap of its next chunk before computing the current one.
 // ------------------------------------------------------------------------------------
 struct RawScal {
@@ -691,7 +694,7 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
   tc_fence_after();
   const uint32_t tbase = s.tmem_base;
 
-  if (warp == 0) {
+  if (warp == 3) {
     // one producer thread polling two independent streams: the C/B ring (waits for dK of
     // two chunks back) and the X ring with the L2 prefetch (waits for Y2 of three back)
     if (lane == 0) {
@@ -838,8 +841,8 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
         }
       }
     }
-  } else if (warp == 2 || warp == 3) {
-    scalar_role(a, s, G, nch, lane, warp - 2);
+  } else if (warp == 2 || warp == 0) {
+    scalar_role(a, s, G, nch, lane, warp == 2 ? 0 : 1);
   } else if (warp >= 4 && warp < 8) {
     mask_role(a, s, tbase, G, nch, warp, tid - 128, 0);
   } else if (warp >= 8 && warp < 12) {
