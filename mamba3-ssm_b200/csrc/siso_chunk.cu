@@ -100,8 +100,6 @@ struct __align__(1024) Smem {
   uint8_t xs[2][kTileBytes];         // (w o x)[t][p], per chunk parity
   uint8_t kbuf[kTileBytes];          // k_c^T[d][p]
   ScalSlot sc[NSC];
-  float side_x[kP];                  // last row of a unit (for the final B*x)
-  float side_b[kD];
   uint64_t cb_full[NS], cb_empty[NS], x_full[2], x_empty[2];
   uint64_t xs_full[2], xs_empty[2], k_ready;
   uint64_t g_full[2], gp_ready[2], y_full[2], y2_free[2];
@@ -129,7 +127,6 @@ struct ChunkArgs {
   const float* bx0;
   __nv_bfloat16* y; Str3 sy;
   float* h_last;
-  float* bx_last;
   __nv_bfloat16* kst;  // optional: bf16 k_c^T of every chunk, [unit][chunk][d][p]
 };
 
@@ -196,11 +193,20 @@ __device__ __forceinline__ void write_xs_rows(const uint8_t* __restrict__ xt, ui
   }
 }
 
-__device__ __noinline__ void stash_last_row(Smem& s, const uint8_t* xt, const uint8_t* bt0, const uint8_t* bt1, int i) {
-  for (int pp = 0; pp < kP; ++pp)
-    s.side_x[pp] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(xt + sw128_off(i, pp)));
-  for (int d = 0; d < kD; ++d)
-    s.side_b[d] = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>((d < 64 ? bt0 : bt1) + sw128_off(i, d & 63)));
+// bx_last[b][h][p][d] = x[b][L-1][h][p] B[b][L-1][h][d]: the carried B x of the last step,
+// a function of the inputs alone, so it is written by this small kernel after the scan
+// (block = (b, h) unit, thread = d) and the scan kernel does not carry it
+__global__ void __launch_bounds__(128) bx_last_kernel(const __nv_bfloat16* __restrict__ x, Str3 sx,
+                                                      const __nv_bfloat16* __restrict__ Bm, Str3 sB, int H, int L,
+                                                      int D, float* __restrict__ bx_last) {
+  const int u = blockIdx.x, b = u / H, h = u - b * H, d = threadIdx.x;
+  if (d >= D) return;
+  const int64_t t = L - 1;
+  const float bd = __bfloat162float(Bm[(int64_t)b * sB.b + t * sB.l + (int64_t)h * sB.h + d]);
+  const __nv_bfloat16* xr = x + (int64_t)b * sx.b + t * sx.l + (int64_t)h * sx.h;
+  float* out = bx_last + (int64_t)u * kP * D + d;
+#pragma unroll 4
+  for (int pp = 0; pp < kP; ++pp) out[(int64_t)pp * D] = __bfloat162float(xr[pp]) * bd;
 }
 
 // ------------------------------------------------------------------------------------
@@ -371,16 +377,6 @@ __device__ void scalar_role(const ChunkArgs& a, Smem& s, int G, int nch, int lan
     if (!wait_or_flag(&s.x_full[p], (g >> 1) & 1)) return;
     if (!wait_or_flag(&s.xs_empty[p], ((g >> 1) & 1) ^ 1)) return;
     write_xs_rows(s.xr[p], s.xs[p], wk, lane);
-    if (cp.last && a.bx_last) {
-      // the C/B stage stays valid until Y1(g), which waits for the state warps; they read
-      // the stash after named barrier 2 + p (160 threads: this warp arrives, they sync)
-      if ((e & 31) == lane) {
-        const int st = g % NS;
-        stash_last_row(s, s.xr[p], s.cb[st][2], s.cb[st][3], e);
-      }
-      __syncwarp();
-      asm volatile("bar.arrive %0, 160;" ::"r"(2 + p) : "memory");
-    }
     fence_proxy_async_smem();
     mbar_arrive(&s.xs_full[p]);
   }
@@ -551,16 +547,10 @@ __device__ __forceinline__ void init_state(const ChunkArgs& a, const ChunkPos& c
   }
 }
 
-__device__ __forceinline__ void store_final(const ChunkArgs& a, const Smem& s, int b, int h, int d,
-                                            const float (&k)[kP]) {
+__device__ __forceinline__ void store_h_last(const ChunkArgs& a, int b, int h, int d, const float (&k)[kP]) {
   if (d >= a.D) return;
   const int64_t sb = ((int64_t)b * a.H + h) * kP * a.D;
-  if (a.h_last)
-    for (int pp = 0; pp < kP; ++pp) a.h_last[sb + (int64_t)pp * a.D + d] = k[pp];
-  if (a.bx_last) {
-    const float bd = s.side_b[d];
-    for (int pp = 0; pp < kP; ++pp) a.bx_last[sb + (int64_t)pp * a.D + d] = s.side_x[pp] * bd;
-  }
+  for (int pp = 0; pp < kP; ++pp) a.h_last[sb + (int64_t)pp * a.D + d] = k[pp];
 }
 
 
@@ -594,14 +584,10 @@ __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, i
   for (int g = 0; g <= G; ++g) {
     // (1) fold dK(g-1) into the carried state (or finish the unit that g-1 closed)
     if (g > 0) {
-      const int pp = (g - 1) & 1;
       if (!wait_or_flag(&s.dk_full, (g - 1) & 1)) return;
       tc_fence_after();
       add_dk(tbase, warp, prev_dec, k);
-      if (prev_last && (a.h_last || a.bx_last)) {
-        if (a.bx_last) asm volatile("bar.sync %0, 160;" ::"r"(2 + pp) : "memory");  // the stash of g-1
-        store_final(a, s, prev_b, prev_h, d, k);
-      }
+      if (prev_last && a.h_last) store_h_last(a, prev_b, prev_h, d, k);
       tc_fence_before();
       mbar_arrive(&s.dk_free);
     }
@@ -950,7 +936,7 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
   a.Dskip = p.Dskip; a.sD = p.sD;
   a.h0 = p.h0; a.bx0 = p.bx0;
   a.y = reinterpret_cast<__nv_bfloat16*>(p.y); a.sy = p.sy;
-  a.h_last = p.h_last; a.bx_last = p.bx_last;
+  a.h_last = p.h_last;
   a.kst = reinterpret_cast<__nv_bfloat16*>(p.kstates);
   const size_t smem = sizeof(Smem) + 1024;
   static bool attr_set = false;
@@ -962,7 +948,11 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
   const int units = p.Bn * p.H;
   const int grid = units < num_sms() ? units : num_sms();
   siso_chunk_fwd_kernel<<<grid, kThreads, smem, s>>>(mx, mb, mc, a);
-  return check_launch("siso_chunk_fwd_kernel");
+  M3_TRY(check_launch("siso_chunk_fwd_kernel"));
+  if (!p.bx_last) return M3_OK;
+  bx_last_kernel<<<units, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(p.x), p.sx,
+                                       reinterpret_cast<const __nv_bfloat16*>(p.Bm), p.sB, p.H, p.L, p.D, p.bx_last);
+  return check_launch("bx_last_kernel");
 }
 
 }  // namespace m3

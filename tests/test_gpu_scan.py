@@ -206,6 +206,22 @@ def test_siso_bf16_headdim64_dstate128_against_oracle(L, Ds):
     assert rel_err(b2.detach().double().cpu().numpy(), bo2) < 2e-2
 
 
+@pytest.mark.parametrize("L", [100, 128, 200])
+def test_siso_bf16_chunked_final_states_many_units(L):
+    """More (b, h) units than SMs with one or two chunks each, so that one CTA closes a unit
+    on consecutive chunks: the final states h_last and bx_last = x_{L-1} B_{L-1}^T of every
+    unit against the oracle (tensor-core path, bf16, P=64, d_state 128)."""
+    from mamba3_ssm.ops import ssm_scan_siso_states
+    arrs, t = _inputs(900 + L, 64, L, 4, 64, 128, dtype=torch.bfloat16)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D")
+    y, h, bx = ssm_scan_siso_states(*[t[k] for k in keys])
+    yo, ho, bo = O.siso_scan_fwd(*[arrs[k] for k in keys])
+    assert rel_err(y.double().cpu().numpy(), yo) < 2e-2
+    assert rel_err(h.double().cpu().numpy(), ho) < 2e-2
+    # bx_last is a product of two bf16 inputs, exact in fp32
+    assert rel_err(bx.double().cpu().numpy(), bo) < 1e-6
+
+
 @pytest.mark.parametrize("case", ["strong_decay", "mixed_sign"])
 def test_siso_bf16_chunked_exact_mask_path(case):
     """Decays outside the split-exponent range of the chunked kernel: strong per-step decay
