@@ -330,6 +330,28 @@ def test_siso_bf16_chunked_backward_against_oracle(L, states, Ds):
         assert rel_err(npy(b0.grad), go["dbx0"]) < 2e-2
 
 
+@pytest.mark.parametrize("L,Ds", [(100, 128), (160, 64)])
+def test_siso_bf16_chunked_backward_many_units(L, Ds):
+    """The chunked backward with more (b, h) units than SMs (152 > 148) and one or two
+    chunks per unit, so that a CTA moves from unit to unit on consecutive chunks, with
+    initial states."""
+    Bn, H = 38, 4
+    arrs, t = _inputs(700 + L, Bn, L, H, 64, Ds, dtype=torch.bfloat16)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D")
+    ins = [t[k].requires_grad_(True) for k in keys]
+    rng = np.random.default_rng(L + 1)
+    h0 = torch.tensor(rng.standard_normal((Bn, H, 64, Ds)), dtype=torch.float32, device=DEV).requires_grad_(True)
+    b0 = torch.tensor(rng.standard_normal((Bn, H, 64, Ds)), dtype=torch.float32, device=DEV).requires_grad_(True)
+    y, dy = _siso_grads(ins, h0, b0)
+    npy = lambda v: None if v is None else v.detach().double().cpu().numpy()
+    go = O.siso_scan_bwd(*[arrs[k] for k in keys], npy(dy), npy(h0), npy(b0))
+    for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
+        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
+        assert rel_err(npy(tt.grad), go[k]) < 2e-2 * f, k
+    assert rel_err(npy(h0.grad), go["dh0"]) < 2e-2
+    assert rel_err(npy(b0.grad), go["dbx0"]) < 2e-2
+
+
 @pytest.mark.parametrize("case", ["strong_decay", "mixed_sign"])
 def test_siso_bf16_chunked_backward_extreme_decay(case):
     """Per-step decays whose in-chunk products leave the fp32 range (ADT down to -13) and
