@@ -13,6 +13,9 @@
 
 namespace m3 {
 
+// CUDA devices one process may drive (per-device launch settings are tracked up to this)
+constexpr int kMaxDevices = 64;
+
 // ------------------------------------------------------------------------------------
 // element conversion
 // ------------------------------------------------------------------------------------

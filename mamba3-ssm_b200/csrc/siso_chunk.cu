@@ -939,11 +939,14 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
   a.h_last = p.h_last;
   a.kst = reinterpret_cast<__nv_bfloat16*>(p.kstates);
   const size_t smem = sizeof(Smem) + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the shared-memory opt-in belongs to each device's context: set it once per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(M3_ERR_CUDA, "cudaGetDevice failed");
+  static bool attr_set[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices || !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(siso_chunk_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    attr_set = true;
+    if (dev >= 0 && dev < kMaxDevices) attr_set[dev] = true;
   }
   const int units = p.Bn * p.H;
   const int grid = units < num_sms() ? units : num_sms();

@@ -1013,11 +1013,14 @@ int launch_siso_bwd_chunked(const SisoParams& p, float* scratch, cudaStream_t s)
   a.sbeta = scratch + npos;
   a.sgam = scratch + 2 * npos;
   const size_t smem = sizeof(BSmem) + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the shared-memory opt-in belongs to each device's context: set it once per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(M3_ERR_CUDA, "cudaGetDevice failed");
+  static bool attr_set[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices || !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(siso_chunk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    attr_set = true;
+    if (dev >= 0 && dev < kMaxDevices) attr_set[dev] = true;
   }
   const int sms = chunk_sm_count();
   const int grid = units < sms ? units : sms;
