@@ -30,8 +30,8 @@
 // the only ones it can reach, so the mask warps of quadrant 3, whose rows have four blocks
 // on or below the diagonal, load sub-partition 3 four times as much as quadrant 0's; the
 // two scalar warps sit on sub-partitions 0 and 2 and the light producer on 3):
-//   warp 3      TMA producer (one thread polling the C/B ring and the X ring, plus the L2
-//               prefetch of later chunks)
+//   warp 3      TMA producer (one thread polling the C/B ring and the X ring; no L2
+//               prefetch of later chunks: measured 2% slower with it)
 //   warp 1      tcgen05 MMA issuer (one thread polling three streams: G fed by the loads;
 //               dK and Y1 fed by the scalar and state warps; Y2 gated by the mask) and TMEM
 //               owner (512 columns: per chunk parity G (128, G' packed in place) and Y2
@@ -66,7 +66,6 @@ constexpr int kD = 128;
 constexpr int kThreads = 512;
 constexpr int NS = 2;    // C/B stages
 constexpr int NSC = 4;   // scalar slots
-constexpr int kPrefetch = 2;  // chunks streamed into L2 ahead of their TMA load
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTileBytes = Q * 64 * 2;       // one SW128 tile: 128 rows x 128 B
 constexpr uint32_t kCBBytes = 4 * kTileBytes;     // C(2) + B(2)
@@ -682,7 +681,7 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
 
   if (warp == 3) {
     // one producer thread polling two independent streams: the C/B ring (waits for dK of
-    // two chunks back) and the X ring with the L2 prefetch (waits for Y2 of three back)
+    // two chunks back) and the X ring (waits for Y2 of two back)
     if (lane == 0) {
       prefetch_tensormap(&tm_x);
       prefetch_tensormap(&tm_B);
@@ -709,16 +708,6 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
           const ChunkPos cp = chunk_pos(a, gx, nch);
           mbar_expect_tx(&s.x_full[xi], kTileBytes);
           tma_load_4d(s.xr[xi], &tm_x, &s.x_full[xi], 0, cp.h, cp.t0, cp.b);
-          // stream the following chunks into L2 so the loads above are L2 hits
-          for (int ahead = (gx == 0 ? 1 : kPrefetch); ahead <= kPrefetch; ++ahead) {
-            if (gx + ahead >= G) break;
-            const ChunkPos pf = chunk_pos(a, gx + ahead, nch);
-            tma_prefetch_l2_4d(&tm_C, 0, pf.h, pf.t0, pf.b);
-            tma_prefetch_l2_4d(&tm_C, 64, pf.h, pf.t0, pf.b);
-            tma_prefetch_l2_4d(&tm_B, 0, pf.h, pf.t0, pf.b);
-            tma_prefetch_l2_4d(&tm_B, 64, pf.h, pf.t0, pf.b);
-            tma_prefetch_l2_4d(&tm_x, 0, pf.h, pf.t0, pf.b);
-          }
           ++gx;
           moved = true;
         }

@@ -737,19 +737,6 @@ __device__ __forceinline__ void control_role(const CUtensorMap* tm_x, const CUte
     tma_load_4d(s.x, tm_x, &s.ld_full, 0, cp.h, cp.t0, cp.b);
     tma_load_2d(s.kc, tm_k, &s.ld_full, 0, (cp.u * a.nch + cp.c) * kD);
     lg = gg;
-    if (gg + 1 < G) {
-      // the chunk after into L2
-      const BPos nx = bpos(a, gg + 1);
-      tma_prefetch_l2_4d(tm_dy, 0, nx.h, nx.t0, nx.b);
-      tma_prefetch_l2_4d(tm_C, 0, nx.h, nx.t0, nx.b);
-      tma_prefetch_l2_4d(tm_B, 0, nx.h, nx.t0, nx.b);
-      if (a.D == kD) {
-        tma_prefetch_l2_4d(tm_C, 64, nx.h, nx.t0, nx.b);
-        tma_prefetch_l2_4d(tm_B, 64, nx.h, nx.t0, nx.b);
-      }
-      tma_prefetch_l2_4d(tm_x, 0, nx.h, nx.t0, nx.b);
-      tma_prefetch_l2_2d(tm_k, 0, (nx.u * a.nch + nx.c) * kD);
-    }
   };
   // dC, dB of chunk gg, staged in the Ghat and M o S tiles
   auto store_outputs = [&](int gg) {
