@@ -228,6 +228,35 @@ def cpu_baseline(target_s=12.0, L_s=4096):
                       f"run {reps} times in {dt:.1f} s"}, (L_s, per_2s)
 
 
+def check_units(inputs, y, units):
+    """Max rel error (max|y - ref| / max|ref|) of the kernel's y on a few (b, h) units
+    against a float64 restatement of the scan recurrence run on the host here (the
+    exponential-trapezoidal update of the reference loop, ops.py:166-175):
+    h_t = e^{ADT_t} h_{t-1} + dt_t ((1 - tr_t) x_t B_t + tr_t (x_t B_t + x_{t-1} B_{t-1}) / 2),
+    y_t = h_t C_t + D x_t, tr = sigmoid(trap). Independent of the kernels."""
+    import numpy as np
+    x, Bm, Cm, ADT, DT, trap, Dw = inputs
+    sel = lambda t: np.stack([t[b, :, h].double().cpu().numpy() for b, h in units], axis=1)  # noqa: E731
+    xs, bs, cs = sel(x), sel(Bm), sel(Cm)          # (L, n, P|D)
+    a = np.exp(sel(ADT))                            # (L, n)
+    dt = sel(DT)
+    tr = 1.0 / (1.0 + np.exp(-sel(trap)))
+    dsk = np.array([float(Dw[h]) for _, h in units])
+    n, P, D = xs.shape[1], xs.shape[2], bs.shape[2]
+    h = np.zeros((n, P, D))
+    bxp = np.zeros((n, P, D))
+    ref = np.empty_like(xs)
+    for t in range(xs.shape[0]):
+        bx = xs[t][:, :, None] * bs[t][:, None, :]
+        w1 = (dt[t] * (1.0 - 0.5 * tr[t]))[:, None, None]
+        w2 = (dt[t] * 0.5 * tr[t])[:, None, None]
+        h = a[t][:, None, None] * h + w1 * bx + w2 * bxp
+        ref[t] = np.einsum("npd,nd->np", h, cs[t]) + dsk[:, None] * xs[t]
+        bxp = bx
+    got = sel(y)
+    return float(np.max(np.abs(got - ref)) / np.max(np.abs(ref)))
+
+
 def workload_config(world):
     return {"workload": "raw SISO scan op forward, long context (ssm_scan_siso)", "batch": C5["batch"],
             "seq_len": C5["seqlen"], "nheads": C5["nheads"], "headdim": C5["headdim"], "d_state": C5["dstate"],
@@ -491,6 +520,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the forward+backward and decode figures")
+    ap.add_argument("--no-check", action="store_true", help="skip the host check of the timed output")
+    ap.add_argument("--no-sustained", action="store_true", help="skip the ~2 s sustained run")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the global batch (profiling runs on a smaller case)")
     ap.add_argument("--fwd-bwd-only", action="store_true",
@@ -583,6 +614,40 @@ def main():
     total_ms = t_beg.elapsed_time(t_end)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     total_ms, kern_ms = max_over_ranks([total_ms, kern_ms], pg, dev)
+
+    # the timed output, checked on two (b, h) units of this rank against a float64
+    # recurrence on the host (first and last unit of the shard)
+    check = None
+    if not args.no_check:
+        units = [(0, 0), (Bl - 1, H - 1)]
+        err = check_units((x, Bm, Cm, ADT, DT, trap, Dw), y, units)
+        (err,) = max_over_ranks([err], pg, dev)
+        check = {"max_rel_err": err, "bar": 2e-2, "ok": err < 2e-2,
+                 "what": "y of the last timed step on units (b, h) = (0, 0) and (last, last) of every rank's "
+                         "shard against a float64 host recurrence, max|y - ref| / max|ref|"}
+
+    # a sustained run of at least ~2 s after the timed region, with its own clock record
+    # (K steps of the timed region can be well under a second)
+    sustained = None
+    if not args.no_sustained:
+        n_s = max(K, int(math.ceil(2000.0 / max(total_ms / K, 1e-3))))
+        sampler2 = ClockSampler(uids) if rank == 0 else None
+        if sampler2:
+            sampler2.start()
+        barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(n_s):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+        barrier()
+        clk2 = sampler2.stop() if sampler2 else None
+        (s_ms,) = max_over_ranks([s0.elapsed_time(s1)], pg, dev)
+        sustained = {"steps": n_s, "seconds": s_ms / 1e3, "ms_per_step": s_ms / n_s,
+                     "value": Bt * L / (s_ms / n_s / 1e3), "clocks": clk2,
+                     "what": "the same step repeated for ~2 s right after the timed region"}
     ms_step = total_ms / K
     tokens = Bt * L
     value = tokens / (ms_step / 1e3)
@@ -674,7 +739,7 @@ def main():
                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
                              "algorithmic_bytes_per_launch": launch_bytes, "kernel_ms": kern_ms},
                 "cpu_baseline": base, "e2e": e2e, "gpu_launches": K, "clocks": clocks,
-                "secondary": extra}
+                "check": check, "sustained": sustained, "secondary": extra}
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()

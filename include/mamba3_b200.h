@@ -130,7 +130,15 @@ int m3_siso_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
  *     with that device current); make that first call before any stream capture.
  *   - Every call on a GPU shares the one array: calls whose kernels overlap on that GPU
  *     (different streams, or host threads) race and produce wrong gradients. Serialise them.
- *   - Nothing carries over between calls: each call writes every scratch entry it reads. */
+ *   - Nothing carries over between calls: each call writes every scratch entry it reads.
+ *   - Which backward runs depends on the size, because the array is the whole workspace:
+ *     for bf16 inputs with headdim 64 and d_state 128 or 64 the tensor-core backward runs
+ *     while its chunk states plus scratch fit, i.e. while
+ *       (16384 * chunks rounded up to 256) + 12 * positions + 16 * chunks,
+ *       chunks = batch * nheads * ceil(seqlen / 128),
+ *     is at most 8 MiB (about 59K positions); above that, and for every other shape, the
+ *     CUDA-core backward runs (several times slower at those sizes, and it rounds bf16
+ *     gradients differently, within the same bf16 tolerance). */
 #define M3_NOALLOC_MAX_POSITIONS (2 * 1024 * 1024)
 int m3_siso_scan_bwd_noalloc(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
                              const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,

@@ -1,5 +1,6 @@
 // extern "C" entry points of libmamba3_b200: argument validation, dispatch to the
 // kernels, and the thread-local error string. Nothing here allocates device memory.
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -27,6 +28,39 @@ int fail(int code, const std::string& msg) {
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return M3_OK;
+}
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(M3_ERR_UNSUPPORTED, "device ordinal beyond the supported range");
+  return M3_OK;
+}
+
+int device_sm_count(int* sms) {
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  M3_TRY(current_device(&dev));
+  int n = cache[dev].load(std::memory_order_acquire);
+  if (n <= 0) {
+    cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess || n <= 0)
+      return fail(M3_ERR_CUDA, std::string("multiprocessor count: ") + cudaGetErrorString(e));
+    cache[dev].store(n, std::memory_order_release);  // concurrent first callers store the same value
+  }
+  *sms = n;
+  return M3_OK;
+}
+
+int ensure_dynamic_smem(const void* kernel, size_t bytes, std::atomic<bool>* done) {
+  int dev = 0;
+  M3_TRY(current_device(&dev));
+  if (done[dev].load(std::memory_order_acquire)) return M3_OK;
+  // idempotent: two threads that both get here set the same attribute twice
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  done[dev].store(true, std::memory_order_release);
   return M3_OK;
 }
 

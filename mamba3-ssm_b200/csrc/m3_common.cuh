@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "mamba3_b200.h"
@@ -62,6 +63,13 @@ template <> struct DT_<__half> { static constexpr int id = M3_FLOAT16; };
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int check_launch(const char* what);
+// The current device's ordinal (M3_ERR_UNSUPPORTED beyond kMaxDevices).
+int current_device(int* dev);
+// SM count of the current device, cached per device; safe from several host threads.
+int device_sm_count(int* sms);
+// Sets a kernel's dynamic shared-memory opt-in once per device (done[] has kMaxDevices
+// entries, one per device context); safe from several host threads.
+int ensure_dynamic_smem(const void* kernel, size_t bytes, std::atomic<bool>* done);
 
 inline size_t dtype_size(int dt) { return dt == M3_FLOAT32 ? 4 : 2; }
 

@@ -23,27 +23,24 @@
 // Warp-specialised, persistent CTA (one per SM, 16 warps), walking its (b, h) units
 // chunk by chunk. Shared-memory buffers are split by lifetime so that the large C / B
 // tiles are released as soon as the early MMAs have read them:
-//   C, B (64 KB)  2-stage ring; read by G, Y1 and dK, freed after dK (issued early)
-//   X    (16 KB)  per chunk parity; read by the scalar warps (w o X) and by Y2 after the mask
+//   C, B (64 KB)  2-stage ring; read by G, Y1 and dK, freed after Y1
+//   X    (16 KB)  per chunk parity; read by the mask warpgroup (w o X) and by Y2
 //   w o X (16 KB) per chunk parity;  k_c^T (16 KB) one buffer
 // Roles (warp w issues from SM sub-partition w % 4, and TMEM lanes 32 (w % 4) .. +31 are
-// the only ones it can reach, so the mask warps of quadrant 3, whose rows have four blocks
-// on or below the diagonal, load sub-partition 3 four times as much as quadrant 0's; the
-// two scalar warps sit on sub-partitions 0 and 2 and the light producer on 3):
-//   warp 3      TMA producer (one thread polling the C/B ring and the X ring; no L2
-//               prefetch of later chunks: measured 2% slower with it)
+// the only ones it can reach):
+//   warp 3      TMA producer (one thread polling the C/B ring and the X ring)
 //   warp 1      tcgen05 MMA issuer (one thread polling three streams: G fed by the loads;
-//               dK and Y1 fed by the scalar and state warps; Y2 gated by the mask) and TMEM
+//               dK and Y1 fed by the mask and state warps; Y2 gated by the mask) and TMEM
 //               owner (512 columns: per chunk parity G (128, G' packed in place) and Y2
 //               (64); one Y1 (64) and one dK (64))
-//   warps 2, 0  per-chunk scalars (decay cumsum, mu, block factors, state weights) into a
-//               4-slot ring, even / odd chunks, running ahead of the consumers; then the
-//               chunk's w o X tile for dK (lane l owns rows l + 32 k, whose w it holds)
-//   warps 4-7   even chunks: G -> G' in TMEM (in place, packed bf16), then the epilogue
-//               y = e^{lambda} Y1 + Y2 -> global (bf16)
+//   warps 4-7   even chunks, thread = row: the chunk's scalars (decay cumsum across the
+//               four warps, mu, block factors, state weights) into a 4-slot ring, the
+//               w o X rows for dK, G -> G' in TMEM (in place, packed bf16), then the
+//               epilogue y = e^{lambda} Y1 + Y2 -> global (bf16)
 //   warps 12-15 odd chunks: the same
 //   warps 8-11  state: k^T (fp32, registers) <- decay k^T + dK^T and its bf16 copy for
 //               the next Y1
+//   warps 0, 2  idle
 // All hand-offs are mbarriers; every wait is bounded (blocking waits by a poll count, the
 // polling producer and issuer by an idle count), and on a timeout the kernel records an
 // error and drains.
@@ -83,8 +80,6 @@ constexpr uint32_t kColDK = 448u;
 struct __align__(16) ScalSlot {
   float colf[Q];      // e^{lambda_{32b+1} - lambda_{j+1}} mu_j (read as float4)
   float mu[Q];
-  float beta[Q];
-  float w[Q];         // state-update weights
   float lam2[Q + 1];  // lambda_i * log2(e)
   float decay_end;
   float dskip;        // D of the unit's head (added on the diagonal of G')
@@ -93,12 +88,23 @@ struct __align__(16) ScalSlot {
   int flags;          // bit0 first chunk of unit, bit1 last, bits 4..7 block b factorisable
 };
 
+// Values one warp of a mask warpgroup hands to the other three while the chunk's scalars
+// are formed (index 4: the row after the chunk, t0 + Q).
+struct WgXch {
+  float tot[4];                          // warp sums of the decay exponents
+  float a0[5], g0[5], adt0[5];           // a, gamma and ADT of each warp's first row
+  float amax[5], pmax[5];                // max |ADT| and max ADT per warp
+  float m[4], gmax[4], rm[4], ref[4];    // split-exponent bounds per 32-row block
+};
+
 struct __align__(1024) Smem {
   uint8_t cb[NS][4][kTileBytes];     // C(d 0-63), C(d 64-127), B(0-63), B(64-127)
   uint8_t xr[2][kTileBytes];         // x[t][p], per chunk parity
   uint8_t xs[2][kTileBytes];         // (w o x)[t][p], per chunk parity
   uint8_t kbuf[kTileBytes];          // k_c^T[d][p]
   ScalSlot sc[NSC];
+  WgXch xch[2];                      // per mask warpgroup: cross-warp scalar exchange
+  uint64_t wg_bar[2];                // per mask warpgroup: 128-thread barrier (bounded waits)
   uint64_t cb_full[NS], cb_empty[NS], x_full[2], x_empty[2];
   uint64_t xs_full[2], xs_empty[2], k_ready;
   uint64_t g_full[2], gp_ready[2], y_full[2], y2_free[2];
@@ -166,29 +172,24 @@ __device__ __forceinline__ float ld_scal(const float* p, const Str3& s, int b, i
 }
 
 
-// xs[t][:] = w_t x[t][:] for the rows t = lane + 32 k; each row's eight 16-byte chunks are
-// loaded before any store, so the loads are not held behind possibly aliasing stores
-__device__ __forceinline__ void write_xs_rows(const uint8_t* __restrict__ xt, uint8_t* __restrict__ xs,
-                                              const float (&wk)[4], int lane) {
+// xs[i][:] = w_i x[i][:] for row i; the row's eight 16-byte chunks are loaded before any
+// store, so the loads are not held behind possibly aliasing stores
+__device__ __forceinline__ void write_xs_row(const uint8_t* __restrict__ xt, uint8_t* __restrict__ xs, float wt,
+                                             int i) {
+  uint4 row[8];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int t = lane + 32 * k;
-    const float wt = wk[k];
-    uint4 row[8];
+  for (int cc = 0; cc < 8; ++cc) row[cc] = *reinterpret_cast<const uint4*>(xt + sw128_off(i, 8 * cc));
 #pragma unroll
-    for (int cc = 0; cc < 8; ++cc) row[cc] = *reinterpret_cast<const uint4*>(xt + sw128_off(t, 8 * cc));
+  for (int cc = 0; cc < 8; ++cc) {
+    const uint4 v = row[cc];
+    const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
 #pragma unroll
-    for (int cc = 0; cc < 8; ++cc) {
-      const uint4 v = row[cc];
-      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[e]));
-        o[e] = pack_bf16(f.x * wt, f.y * wt);
-      }
-      *reinterpret_cast<uint4*>(xs + sw128_off(t, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[e]));
+      o[e] = pack_bf16(f.x * wt, f.y * wt);
     }
+    *reinterpret_cast<uint4*>(xs + sw128_off(i, 8 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -209,176 +210,165 @@ __global__ void __launch_bounds__(128) bx_last_kernel(const __nv_bfloat16* __res
 }
 
 // ------------------------------------------------------------------------------------
-// warps 2 and 0: per-chunk scalars. Warp 2 takes the even chunks, warp 0 the odd ones;
-// each loads the raw ADT / DT / trap of its next chunk before computing the current one.
+// Per-chunk scalars, formed by the chunk's mask warpgroup: thread i owns row i. The raw
+// ADT / DT / trap of a row are loaded two chunks ahead (the warpgroup's next chunk);
+// thread Q-1 also loads row t0 + Q, whose a, gamma and ADT close the chunk.
 // ------------------------------------------------------------------------------------
-struct RawScal {
-  float adt[4], dt[4], tr[4];  // rows lane + 32k
-  float adtQ, dtQ, trQ;        // row t0 + Q (lane 0)
+struct RawRow {
+  float adt, dt, tr;     // row t0 + i
+  float adtQ, dtQ, trQ;  // row t0 + Q (thread Q-1 only)
 };
 
-__device__ __forceinline__ void load_raw(const ChunkArgs& a, const ChunkPos& cp, int lane, RawScal& r) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int t = cp.t0 + lane + 32 * k;
-    const bool v = t < a.L;
-    r.adt[k] = v ? ld_scal(a.adt, a.sadt, cp.b, t, cp.h) : 0.f;
-    r.dt[k] = v ? ld_scal(a.dt, a.sdt, cp.b, t, cp.h) : 0.f;
-    r.tr[k] = v ? ld_scal(a.trap, a.strap, cp.b, t, cp.h) : 0.f;
+__device__ __forceinline__ void load_raw_row(const ChunkArgs& a, const ChunkPos& cp, int i, RawRow& r) {
+  const int t = cp.t0 + i;
+  const bool v = t < a.L;
+  r.adt = v ? ld_scal(a.adt, a.sadt, cp.b, t, cp.h) : 0.f;
+  r.dt = v ? ld_scal(a.dt, a.sdt, cp.b, t, cp.h) : 0.f;
+  r.tr = v ? ld_scal(a.trap, a.strap, cp.b, t, cp.h) : 0.f;
+  r.adtQ = r.dtQ = r.trQ = 0.f;
+  if (i == Q - 1 && cp.t0 + Q < a.L) {
+    r.adtQ = ld_scal(a.adt, a.sadt, cp.b, cp.t0 + Q, cp.h);
+    r.dtQ = ld_scal(a.dt, a.sdt, cp.b, cp.t0 + Q, cp.h);
+    r.trQ = ld_scal(a.trap, a.strap, cp.b, cp.t0 + Q, cp.h);
   }
-  const int t = cp.t0 + Q;
-  const bool v = lane == 0 && t < a.L;
-  r.adtQ = v ? ld_scal(a.adt, a.sadt, cp.b, t, cp.h) : 0.f;
-  r.dtQ = v ? ld_scal(a.dt, a.sdt, cp.b, t, cp.h) : 0.f;
-  r.trQ = v ? ld_scal(a.trap, a.strap, cp.b, t, cp.h) : 0.f;
 }
 
-__device__ void scalar_role(const ChunkArgs& a, Smem& s, int G, int nch, int lane, int g_first) {
-  RawScal raw;
-  if (g_first < G) load_raw(a, chunk_pos(a, g_first, nch), lane, raw);
-  for (int g = g_first; g < G; g += 2) {
-    const int q = g % NSC;
-    const ChunkPos cp = chunk_pos(a, g, nch);
-    float adt[4], av[4], be[4], ga[4];
+// 128-thread barrier of one mask warpgroup on an mbarrier, with a bounded wait (a thread
+// that gave up elsewhere cannot leave the others blocked for good).
+__device__ __forceinline__ bool wg_sync(uint64_t* bar, uint32_t& phase) {
+  mbar_arrive(bar);
+  const bool ok = wait_or_flag(bar, phase);
+  phase ^= 1u;
+  return ok;
+}
+
+// Row i's values for the chunk: lambda_i (log2 units), beta_i and the state weight w_i in
+// registers; colf, mu and lambda of every row in the scalar slot; the chunk's decay, the
+// first row's a / gamma, and the split-exponent flags in the slot (thread 0). Returns false
+// after a timed-out wait.
+__device__ __forceinline__ bool scal_phase(const ChunkArgs& a, Smem& s, int g, int nch, int i, const RawRow& raw,
+                                           uint32_t& wg_phase, float& li, float& bi, float& wk) {
+  const int p = g & 1, q = g % NSC, lane = i & 31, wq = i >> 5;
+  const ChunkPos cp = chunk_pos(a, g, nch);
+  WgXch& X = s.xch[p];
+  const bool v = cp.t0 + i < a.L;
+  const float adt = raw.adt;
+  const float tr = v ? sigmoidf_(raw.tr) : 0.f;
+  const float be = raw.dt * (1.0f - tr) + 0.5f * raw.dt * tr;
+  const float ga = 0.5f * raw.dt * tr;
+  const float av = v ? exp2f(adt * kLog2e) : 0.f;
+  // lambda: inclusive scan of (row 0 ? 0 : ADT_r), per warp here and across warps below
+  float incl = (i == 0) ? 0.f : adt;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const bool v = cp.t0 + lane + 32 * k < a.L;
-      adt[k] = raw.adt[k];
-      const float dt = raw.dt[k];
-      const float tr = v ? sigmoidf_(raw.tr[k]) : 0.f;
-      be[k] = dt * (1.0f - tr) + 0.5f * dt * tr;
-      ga[k] = 0.5f * dt * tr;
-      av[k] = v ? exp2f(adt[k] * kLog2e) : 0.f;
-    }
-    float adtQ, aQ, gQ;
-    {
-      const bool v = cp.t0 + Q < a.L;
-      adtQ = __shfl_sync(0xffffffffu, raw.adtQ, 0);
-      aQ = v ? exp2f(adtQ * kLog2e) : 0.f;
-      const float trQ = v ? sigmoidf_(__shfl_sync(0xffffffffu, raw.trQ, 0)) : 0.f;
-      gQ = 0.5f * __shfl_sync(0xffffffffu, raw.dtQ, 0) * trQ;
-    }
-    if (g + 2 < G) load_raw(a, chunk_pos(a, g + 2, nch), lane, raw);  // next chunk of this warp
-    // lambda: inclusive scan of (r == 0 ? 0 : ADT_r) over r = lane + 32k
-    float lam[4];
-    float carry = 0.f;
+  for (int o = 1; o < 32; o <<= 1) {
+    const float u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  float amax = fabsf(adt), pmax = adt;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float v = (k == 0 && lane == 0) ? 0.f : adt[k];
+  for (int o = 16; o > 0; o >>= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, o));
+  }
+  if (lane == 31) X.tot[wq] = incl;
+  if (lane == 0) {
+    X.a0[wq] = av;
+    X.g0[wq] = ga;
+    X.adt0[wq] = adt;
+    X.amax[wq] = amax;
+    X.pmax[wq] = pmax;
+  }
+  if (i == Q - 1) {
+    const bool vq = cp.t0 + Q < a.L;
+    const float trq = vq ? sigmoidf_(raw.trQ) : 0.f;
+    X.a0[4] = vq ? exp2f(raw.adtQ * kLog2e) : 0.f;
+    X.g0[4] = 0.5f * raw.dtQ * trq;
+    X.adt0[4] = raw.adtQ;
+    X.amax[4] = fabsf(raw.adtQ);
+    X.pmax[4] = raw.adtQ;
+  }
+  if (!wg_sync(&s.wg_bar[p], wg_phase)) return false;
+  float pre = 0.f, total = 0.f;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += u;
-      }
-      lam[k] = (v + carry) * kLog2e;
-      carry += __shfl_sync(0xffffffffu, v, 31);
-    }
-    const float lamQ = (carry + adtQ) * kLog2e;
-    // next-row values: a_{r+1}, gamma_{r+1}, lam2_{r+1}
-    float an[4], gn[4], ln[4];
+  for (int w = 0; w < 4; ++w) {
+    const float tw = X.tot[w];
+    if (w < wq) pre += tw;
+    total += tw;
+  }
+  const float lam = (incl + pre) * kLog2e;
+  const float lamQ = (total + X.adt0[4]) * kLog2e;
+  // next-row values a_{i+1}, gamma_{i+1}, lambda_{i+1}
+  float l1 = __shfl_down_sync(0xffffffffu, lam, 1);
+  float a1 = __shfl_down_sync(0xffffffffu, av, 1);
+  float g1 = __shfl_down_sync(0xffffffffu, ga, 1);
+  if (lane == 31) {
+    l1 = (pre + X.tot[wq] + X.adt0[wq + 1]) * kLog2e;  // row 32 (wq + 1), or t0 + Q
+    a1 = X.a0[wq + 1];
+    g1 = X.g0[wq + 1];
+  }
+  const float mu = a1 * be + g1;
+  const float ref = __shfl_sync(0xffffffffu, lam, 1);  // lambda_{32 wq + 1}: block wq's reference
+  float am = X.amax[4], pm = X.pmax[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float a1 = __shfl_down_sync(0xffffffffu, av[k], 1);
-      const float g1 = __shfl_down_sync(0xffffffffu, ga[k], 1);
-      const float l1 = __shfl_down_sync(0xffffffffu, lam[k], 1);
-      float aw, gw, lw;
-      if (k < 3) {
-        aw = __shfl_sync(0xffffffffu, av[k + 1 < 4 ? k + 1 : 3], 0);
-        gw = __shfl_sync(0xffffffffu, ga[k + 1 < 4 ? k + 1 : 3], 0);
-        lw = __shfl_sync(0xffffffffu, lam[k + 1 < 4 ? k + 1 : 3], 0);
-      } else {
-        aw = aQ; gw = gQ; lw = lamQ;
-      }
-      an[k] = lane < 31 ? a1 : aw;
-      gn[k] = lane < 31 ? g1 : gw;
-      ln[k] = lane < 31 ? l1 : lw;
-    }
-    const int e = cp.n - 1;  // last valid row
-    const int eg = (e >> 5) & 3;
-    const float lam_sel = eg == 0 ? lam[0] : (eg == 1 ? lam[1] : (eg == 2 ? lam[2] : lam[3]));
-    const float lam_e = __shfl_sync(0xffffffffu, lam_sel, e & 31);
-    const float lam_end = cp.last ? lam_e : lamQ;
-    // Split-exponent safety. Column factors span at most 32 steps, row factors at most
-    // 128: with |ADT| <= 2.5 and ADT <= 0.6 everywhere in the chunk all blocks are safe.
-    float amax = fabsf(adtQ), pmax = adtQ;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      amax = fmaxf(amax, fabsf(adt[k]));
-      pmax = fmaxf(pmax, adt[k]);
-    }
+  for (int w = 0; w < 4; ++w) {
+    am = fmaxf(am, X.amax[w]);
+    pm = fmaxf(pm, X.pmax[w]);
+  }
+  // Split-exponent safety. Column factors span at most 32 steps, row factors at most 128:
+  // with |ADT| <= 2.5 and ADT <= 0.6 everywhere in the chunk every block is safe.
+  const bool all_safe = am <= 2.5f && pm <= 0.6f;
+  if (!wait_or_flag(&s.scal_empty[q], ((g / NSC) & 1) ^ 1)) return false;
+  ScalSlot& sl = s.sc[q];
+  sl.lam2[i] = lam;
+  sl.mu[i] = mu;
+  sl.colf[i] = exp2f(ref - l1) * mu;
+  if (i == Q - 1) sl.lam2[Q] = lamQ;
+  const int e = cp.n - 1;  // last valid row
+  float lam_end = lamQ;
+  if (cp.last) {  // uniform over the warpgroup
+    if (!wg_sync(&s.wg_bar[p], wg_phase)) return false;
+    lam_end = sl.lam2[e];
+  }
+  wk = !cp.last ? exp2f(lamQ - l1) * mu : (i < e ? exp2f(lam_end - l1) * mu : (i == e ? be : 0.f));
+  int flags = (cp.first ? 1 : 0) | (cp.last ? 2 : 0);
+  if (all_safe) {  // uniform over the warpgroup
+    flags |= 0xF0;
+  } else {
+    // per block: |column exponents| bounded, and row factors bounded above
+    float m = fabsf(ref - l1), gmax = lam, rm = lane >= 1 ? lam : -INFINITY;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, o));
-    }
-    const bool all_safe = amax <= 2.5f && pmax <= 0.6f;
-    int flags = (cp.first ? 1 : 0) | (cp.last ? 2 : 0);
-    ScalSlot& sl = s.sc[q];
-    float wk[4];
-    if (!wait_or_flag(&s.scal_empty[q], ((g / NSC) & 1) ^ 1)) return;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int j = lane + 32 * k;
-      const float mu = an[k] * be[k] + gn[k];
-      const float ref = __shfl_sync(0xffffffffu, lam[k], 1);  // lambda_{32k+1}
-      const float ex = ref - ln[k];
-      sl.lam2[j] = lam[k];
-      sl.mu[j] = mu;
-      sl.beta[j] = be[k];
-      sl.colf[j] = exp2f(ex) * mu;
-      float wj;
-      if (!cp.last) wj = exp2f(lamQ - ln[k]) * mu;
-      else wj = (j < e) ? exp2f(lam_e - ln[k]) * mu : (j == e ? be[k] : 0.f);
-      sl.w[j] = wj;
-      wk[k] = wj;
-    }
-    if (all_safe) {
-      flags |= 0xF0;
-    } else {
-      // per block: |column exponents| bounded, and row factors bounded above
-      float gmax[4], mx_grp[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float v = lam[k], rm = lane >= 1 ? lam[k] : -INFINITY;
-        const float ref = __shfl_sync(0xffffffffu, lam[k], 1);
-        float m = fabsf(ref - ln[k]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-          rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, o));
-          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        }
-        gmax[k] = v;
-        mx_grp[k] = rm;
-        if (m <= kSafeExp2) flags |= 1 << (4 + k);
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float mx = mx_grp[k];
-#pragma unroll
-        for (int k2 = k + 1; k2 < 4; ++k2) mx = fmaxf(mx, gmax[k2]);
-        const float ref = __shfl_sync(0xffffffffu, lam[k], 1);
-        if (!(mx - ref <= kSafeExp2)) flags &= ~(1 << (4 + k));
-      }
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
+      rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, o));
     }
     if (lane == 0) {
-      sl.lam2[Q] = lamQ;
-      sl.decay_end = exp2f(lam_end);
-      sl.dskip = a.Dskip[cp.h * a.sD];
-      sl.a0 = av[0];
-      sl.g0 = ga[0];
-      sl.n = cp.n;
-      sl.flags = flags;
+      X.m[wq] = m;
+      X.gmax[wq] = gmax;
+      X.rm[wq] = rm;
+      X.ref[wq] = ref;
     }
-    mbar_arrive(&s.scal_full[q]);
-    // (w o x) rows lane + 32 k of this chunk, for dK(g)
-    const int p = g & 1;
-    if (!wait_or_flag(&s.x_full[p], (g >> 1) & 1)) return;
-    if (!wait_or_flag(&s.xs_empty[p], ((g >> 1) & 1) ^ 1)) return;
-    write_xs_rows(s.xr[p], s.xs[p], wk, lane);
-    fence_proxy_async_smem();
-    mbar_arrive(&s.xs_full[p]);
+    if (!wg_sync(&s.wg_bar[p], wg_phase)) return false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float mx = X.rm[k];
+#pragma unroll
+      for (int k2 = k + 1; k2 < 4; ++k2) mx = fmaxf(mx, X.gmax[k2]);
+      if (X.m[k] <= kSafeExp2 && mx - X.ref[k] <= kSafeExp2) flags |= 1 << (4 + k);
+    }
   }
+  if (i == 0) {
+    sl.decay_end = exp2f(lam_end);
+    sl.dskip = a.Dskip[cp.h * a.sD];
+    sl.a0 = av;
+    sl.g0 = ga;
+    sl.n = cp.n;
+    sl.flags = flags;
+  }
+  mbar_arrive(&s.scal_full[q]);
+  li = lam;
+  bi = be;
+  return true;
 }
 
 // ------------------------------------------------------------------------------------
@@ -465,23 +455,35 @@ __device__ __forceinline__ void epilogue(const ChunkArgs& a, Smem& s, uint32_t t
 }
 
 // ------------------------------------------------------------------------------------
-// G -> G' (TMEM, in place), then the epilogue. Warps 4-7 take the even chunks, warps
-// 12-15 the odd ones (each chunk parity has its own TMEM columns), so two chunks are
-// masked concurrently. Thread i owns row i. Warp r (rows 32r..32r+31) sees column blocks
-// b < r entirely below the diagonal, block r on it and blocks b > r above it (zeros, not
-// read). The packed bf16 G' of block b lands in columns 16b..16b+15, which this thread has
+// One chunk per mask warpgroup iteration: the chunk's scalars (scal_phase), the w o X tile
+// for dK, G -> G' (TMEM, in place), then the epilogue. Warps 4-7 take the even chunks,
+// warps 12-15 the odd ones (each chunk parity has its own TMEM columns), so two chunks are
+// in flight. Thread i owns row i. Warp r (rows 32r..32r+31) sees column blocks b < r
+// entirely below the diagonal, block r on it and blocks b > r above it (zeros, not read).
+// The packed bf16 G' of block b lands in columns 16b..16b+15, which this thread has
 // already read.
 // ------------------------------------------------------------------------------------
 __device__ void mask_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, int nch, int warp, int i, int parity) {
   const int wr = warp & 3;
+  uint32_t wg_phase = 0;
+  RawRow raw;
+  if (parity < G) load_raw_row(a, chunk_pos(a, parity, nch), i, raw);
   for (int g = parity; g < G; g += 2) {
     const int p = g & 1, q = g % NSC;
+    float li, bi, wk;
+    if (!scal_phase(a, s, g, nch, i, raw, wg_phase, li, bi, wk)) return;
+    if (g + 2 < G) load_raw_row(a, chunk_pos(a, g + 2, nch), i, raw);  // this warpgroup's next chunk
+    // (w o x) row i of this chunk, for dK(g)
+    if (!wait_or_flag(&s.x_full[p], (g >> 1) & 1)) return;
+    if (!wait_or_flag(&s.xs_empty[p], ((g >> 1) & 1) ^ 1)) return;
+    write_xs_row(s.xr[p], s.xs[p], wk, i);
+    fence_proxy_async_smem();
+    mbar_arrive(&s.xs_full[p]);
+    // every row's slot entries written
     if (!wait_or_flag(&s.scal_full[q], (g / NSC) & 1)) return;
     if (!wait_or_flag(&s.g_full[p], (g >> 1) & 1)) return;
     tc_fence_after();
     const ScalSlot& sl = s.sc[q];
-    const float li = sl.lam2[i];
-    const float bi = sl.beta[i];
     const float dk = sl.dskip;
     const int flags = sl.flags;
 #pragma unroll 1
@@ -640,8 +642,9 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.x_full[i], 1);
       mbar_init(&s.x_empty[i], 1);
-      mbar_init(&s.xs_full[i], 32);
+      mbar_init(&s.xs_full[i], 128);
       mbar_init(&s.xs_empty[i], 1);
+      mbar_init(&s.wg_bar[i], 128);
     }
     mbar_init(&s.k_ready, 128);
     mbar_init(&s.y1_full[0], 1);
@@ -656,7 +659,7 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
       mbar_init(&s.y2_free[i], 128);
     }
     for (int i = 0; i < NSC; ++i) {
-      mbar_init(&s.scal_full[i], 32);
+      mbar_init(&s.scal_full[i], 128);
       mbar_init(&s.scal_empty[i], 2 * 128);
     }
     fence_barrier_init();
@@ -816,8 +819,6 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
         }
       }
     }
-  } else if (warp == 2 || warp == 0) {
-    scalar_role(a, s, G, nch, lane, warp == 2 ? 0 : 1);
   } else if (warp >= 4 && warp < 8) {
     mask_role(a, s, tbase, G, nch, warp, tid - 128, 0);
   } else if (warp >= 8 && warp < 12) {
@@ -836,17 +837,16 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
 // ------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 lookup_encode() {
+  cudaDriverEntryPointQueryResult q;
+  void* p = nullptr;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  return nullptr;
+}
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = lookup_encode();  // thread-safe static init
   return fn;
 }
 
@@ -868,15 +868,6 @@ int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t H, int64_t
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 bool strides_ok(const Str3& s) { return (s.b % 8 == 0) && (s.l % 8 == 0) && (s.h % 8 == 0); }
 
-int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      n = 148;
-  }
-  return n;
-}
 
 }  // namespace
 
@@ -884,7 +875,10 @@ PFN_cuTensorMapEncodeTiled_v12000 chunk_encode_fn() { return get_encode(); }
 int chunk_tmap_4d(CUtensorMap* m, const void* base, int64_t inner, int64_t H, int64_t L, int64_t Bn, const Str3& st) {
   return make_map(m, base, inner, H, L, Bn, st);
 }
-int chunk_sm_count() { return num_sms(); }
+int chunk_sm_count() {
+  int n = 0;
+  return device_sm_count(&n) == M3_OK ? n : 148;
+}
 
 bool siso_chunk_supported(const SisoParams& p, int xdt, int bcdt) {
   if (xdt != M3_BFLOAT16 || bcdt != M3_BFLOAT16) return false;
@@ -929,16 +923,12 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
   a.kst = reinterpret_cast<__nv_bfloat16*>(p.kstates);
   const size_t smem = sizeof(Smem) + 1024;
   // the shared-memory opt-in belongs to each device's context: set it once per device
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return fail(M3_ERR_CUDA, "cudaGetDevice failed");
-  static bool attr_set[kMaxDevices] = {};
-  if (dev < 0 || dev >= kMaxDevices || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(siso_chunk_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    if (dev >= 0 && dev < kMaxDevices) attr_set[dev] = true;
-  }
+  static std::atomic<bool> smem_set[kMaxDevices];
+  M3_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(siso_chunk_fwd_kernel), smem, smem_set));
+  int sms = 0;
+  M3_TRY(device_sm_count(&sms));
   const int units = p.Bn * p.H;
-  const int grid = units < num_sms() ? units : num_sms();
+  const int grid = units < sms ? units : sms;
   siso_chunk_fwd_kernel<<<grid, kThreads, smem, s>>>(mx, mb, mc, a);
   M3_TRY(check_launch("siso_chunk_fwd_kernel"));
   if (!p.bx_last) return M3_OK;

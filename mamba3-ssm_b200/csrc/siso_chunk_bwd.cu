@@ -22,8 +22,13 @@
 //   dmu_j        = X_j . V_j                  (= <g_{j+1}, u_j>)
 //   dbeta_i      = G_ii S_ii + a_{i+1} dmu_i  (= <g_i, u_i>)
 //   dgamma_{j+1} = dmu_j                      (= <g_{j+1}, u_j>)
-// A second kernel forms dADT_r = sum_{s>=r} (q_s - beta_s dbeta_s - gamma_s dgamma_s) with
-// fp64 suffix sums, dDT and dtrap (the identity of the CUDA-core backward).
+// A second kernel forms dADT_r = sum_{s>=r} (q_s - beta_s dbeta_s - gamma_s dgamma_s) (the
+// identity of the CUDA-core backward), dDT and dtrap. The suffix sum runs inside one chunk
+// only and starts from the exact value at the next chunk's first row t0,
+//   dADT_{t0} = a_{t0} <g_{t0}, h_{t0-1}> = <dk_c, k_c> - gamma_{t0} dgamma_{t0}
+// (k_c = a_{t0} h_{t0-1} + gamma_{t0} u_{t0-1}, dk_c = g_{t0}), which the state warps form
+// per chunk: a suffix over the whole sequence would add up the bf16-level errors of every
+// later term (at L = 32768 that drifted to several percent of max|dADT|).
 //
 // Ten MMAs per chunk (M = 128, fp32 accumulators in TMEM):
 //   phase 1: G = C B^T, S = dY X^T, Y1 = C k_c^T, T = B dk_next^T, dK^T = C^T (e^lambda o dY)
@@ -34,7 +39,8 @@
 //   warp 1      per-chunk scalars into two slots; TMEM owner
 //   warps 2-3   e^lambda o dY
 //   warps 4-11  epilogues, thread = row i; warps 4-7 and 8-11 split the columns
-//   warps 12-15 the carried adjoint dk^T (thread = state row d, fp32 registers)
+//   warps 12-15 the carried adjoint dk^T (thread = state row d, fp32 registers) and the
+//               chunk-start dot product <dk_c, k_c>
 // Every wait is bounded; on a timeout the kernel records an error and returns.
 #include <cudaTypedefs.h>
 
@@ -108,8 +114,9 @@ static_assert(sizeof(BSmem) + 1024 <= 232448, "shared memory budget");
 
 // consumers of a scalar slot: e^lambda o dY writers, epilogues, state warps
 constexpr uint32_t kScalReaders = 64 + 256 + 128;
-// arrivals that complete the phase-1 epilogue: the epilogue threads and the w o X writers
-constexpr uint32_t kEp1Arrivals = 256 + 64;
+// arrivals that complete the phase-1 epilogue: the epilogue threads, the w o X writers and
+// the state warps (done reading the k_c tile, which the next chunk's load overwrites)
+constexpr uint32_t kEp1Arrivals = 256 + 64 + 128;
 
 __device__ int g_bwd_error;  // set when a bounded wait gives up
 
@@ -135,6 +142,7 @@ struct BwdArgs {
   float* sq;     // per position [unit][t]: q_t
   float* sbeta;  //                         dbeta_t
   float* sgam;   //                         dgamma_t
+  float* skdot;  // per (unit, chunk): <dk_c, k_c> as four per-warp partials
 };
 
 struct BPos {
@@ -656,6 +664,25 @@ __device__ __forceinline__ void state_role(const BwdArgs& a, BSmem& s, uint32_t 
       for (int e = 0; e < 16; ++e) dk[16 * qt + e] = fmaf(dec, dk[16 * qt + e], __uint_as_float(r[e]));
     }
     tc_fence_before();
+    {
+      // <dk_c, k_c>, row d of this warp's part (k_c^T row d: the chunk-start state in bf16)
+      float kd = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        const uint4 v = *reinterpret_cast<const uint4*>(s.kc + sw128_off(d, 8 * cc));
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[e]));
+          kd = fmaf(dk[8 * cc + 2 * e], f.x, kd);
+          kd = fmaf(dk[8 * cc + 2 * e + 1], f.y, kd);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) kd += __shfl_xor_sync(0xffffffffu, kd, o);
+      if (lane == 0) a.skdot[((int64_t)cp.u * a.nch + cp.c) * 4 + (warp & 3)] = kd;
+      mbar_arrive(&s.ep1_done);  // the k_c tile is read
+    }
     if (cp.first) {
       const int64_t sb = ((int64_t)cp.b * a.H + cp.h) * kP * a.D + d;
       float gsum = 0.f;
@@ -880,51 +907,54 @@ siso_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
 }
 
 // ------------------------------------------------------------------------------------
-// dADT (fp64 suffix sums of q - beta dbeta - gamma dgamma), dDT, dtrap; CTA per unit,
-// 128-step tiles from the end
+// dADT, dDT, dtrap; CTA per (unit, chunk), thread = row. dADT_r is the suffix sum of
+// q - beta dbeta - gamma dgamma over the rest of the chunk (fp64) plus the exact value at
+// the next chunk's first row t0: <dk, k> of that chunk - gamma_{t0} dgamma_{t0}.
 // ------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) siso_chunk_bwd_scal_kernel(BwdArgs a) {
-  const int u = blockIdx.x, b = u / a.H, h = u - b * a.H;
+  const int u = (int)(blockIdx.x / (unsigned)a.nch), tt = (int)(blockIdx.x - (unsigned)u * a.nch);
+  const int b = u / a.H, h = u - b * a.H;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   __shared__ double wsum[4];
-  double carry = 0.0;
-  const int ntile = (a.L + 127) / 128;
-  for (int tt = ntile - 1; tt >= 0; --tt) {
-    const int t = tt * 128 + tid;
-    const bool v = t < a.L;
-    double e = 0.0;
-    float dbe = 0.f, dga = 0.f, tr = 0.f, dt = 0.f;
-    if (v) {
-      const int64_t pos = (int64_t)u * a.L + t;
-      const float qv = a.sq[pos];
-      dbe = a.sbeta[pos];
-      dga = a.sgam[pos];
-      dt = ld_scal(a.dt, a.sdt, b, t, h);
-      tr = sigmoidf_(ld_scal(a.trap, a.strap, b, t, h));
-      const float be = dt * (1.0f - tr) + 0.5f * dt * tr;
-      const float ga = 0.5f * dt * tr;
-      e = (double)qv - (double)be * dbe - (double)ga * dga;
-    }
-    double sfx = e;  // suffix sum within the warp
+  const int t = tt * 128 + tid;
+  const bool v = t < a.L;
+  double e = 0.0;
+  float dbe = 0.f, dga = 0.f, tr = 0.f, dt = 0.f;
+  if (v) {
+    const int64_t pos = (int64_t)u * a.L + t;
+    const float qv = a.sq[pos];
+    dbe = a.sbeta[pos];
+    dga = a.sgam[pos];
+    dt = ld_scal(a.dt, a.sdt, b, t, h);
+    tr = sigmoidf_(ld_scal(a.trap, a.strap, b, t, h));
+    const float be = dt * (1.0f - tr) + 0.5f * dt * tr;
+    const float ga = 0.5f * dt * tr;
+    e = (double)qv - (double)be * dbe - (double)ga * dga;
+  }
+  double sfx = e;  // suffix sum within the warp
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double y = __shfl_down_sync(0xffffffffu, sfx, o);
-      if (lane + o < 32) sfx += y;
-    }
-    if (lane == 0) wsum[w] = sfx;
-    __syncthreads();
-    double hi = 0.0;
-    for (int w2 = w + 1; w2 < 4; ++w2) hi += wsum[w2];
-    const double tot = (wsum[0] + wsum[1]) + (wsum[2] + wsum[3]);
-    if (v) {
-      a.dadt[(int64_t)b * a.sdadt.b + (int64_t)t * a.sdadt.l + (int64_t)h * a.sdadt.h] = (float)(carry + hi + sfx);
-      a.ddt[(int64_t)b * a.sddt.b + (int64_t)t * a.sddt.l + (int64_t)h * a.sddt.h] =
-          dbe * (1.0f - 0.5f * tr) + dga * 0.5f * tr;
-      a.dtrap[(int64_t)b * a.sdtrap.b + (int64_t)t * a.sdtrap.l + (int64_t)h * a.sdtrap.h] =
-          0.5f * dt * (dga - dbe) * tr * (1.0f - tr);
-    }
-    carry += tot;
-    __syncthreads();
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_down_sync(0xffffffffu, sfx, o);
+    if (lane + o < 32) sfx += y;
+  }
+  if (lane == 0) wsum[w] = sfx;
+  __syncthreads();
+  double hi = 0.0;
+  for (int w2 = w + 1; w2 < 4; ++w2) hi += wsum[w2];
+  double carry = 0.0;  // dADT at the next chunk's first row (none after the last chunk)
+  if (tt + 1 < a.nch) {
+    const int t1 = (tt + 1) * 128;
+    const float* kd = a.skdot + ((int64_t)u * a.nch + tt + 1) * 4;
+    const float tr1 = sigmoidf_(ld_scal(a.trap, a.strap, b, t1, h));
+    const float ga1 = 0.5f * ld_scal(a.dt, a.sdt, b, t1, h) * tr1;
+    carry = ((double)kd[0] + kd[1]) + ((double)kd[2] + kd[3]) - (double)ga1 * a.sgam[(int64_t)u * a.L + t1];
+  }
+  if (v) {
+    a.dadt[(int64_t)b * a.sdadt.b + (int64_t)t * a.sdadt.l + (int64_t)h * a.sdadt.h] = (float)(carry + hi + sfx);
+    a.ddt[(int64_t)b * a.sddt.b + (int64_t)t * a.sddt.l + (int64_t)h * a.sddt.h] =
+        dbe * (1.0f - 0.5f * tr) + dga * 0.5f * tr;
+    a.dtrap[(int64_t)b * a.sdtrap.b + (int64_t)t * a.sdtrap.l + (int64_t)h * a.sdtrap.h] =
+        0.5f * dt * (dga - dbe) * tr * (1.0f - tr);
   }
 }
 
@@ -954,7 +984,8 @@ size_t siso_chunk_kstate_bytes(int64_t Bn, int64_t L, int64_t H) {
 }
 
 size_t siso_chunk_bwd_scratch_bytes(int64_t Bn, int64_t L, int64_t H) {
-  return 3 * sizeof(float) * (size_t)(Bn * H * L);
+  const int64_t nch = (L + Q - 1) / Q;
+  return 3 * sizeof(float) * (size_t)(Bn * H * L) + 4 * sizeof(float) * (size_t)(Bn * H * nch);
 }
 
 bool siso_chunk_bwd_supported(const SisoParams& p, int xdt, int bcdt) {
@@ -999,21 +1030,19 @@ int launch_siso_bwd_chunked(const SisoParams& p, float* scratch, cudaStream_t s)
   a.sq = scratch;
   a.sbeta = scratch + npos;
   a.sgam = scratch + 2 * npos;
+  a.skdot = scratch + 3 * npos;
   const size_t smem = sizeof(BSmem) + 1024;
   // the shared-memory opt-in belongs to each device's context: set it once per device
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return fail(M3_ERR_CUDA, "cudaGetDevice failed");
-  static bool attr_set[kMaxDevices] = {};
-  if (dev < 0 || dev >= kMaxDevices || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(siso_chunk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    if (dev >= 0 && dev < kMaxDevices) attr_set[dev] = true;
-  }
-  const int sms = chunk_sm_count();
+  static std::atomic<bool> smem_set[kMaxDevices];
+  M3_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(siso_chunk_bwd_kernel), smem, smem_set));
+  int sms = 0;
+  M3_TRY(device_sm_count(&sms));
   const int grid = units < sms ? units : sms;
   siso_chunk_bwd_kernel<<<grid, kThreads, smem, s>>>(mx, mb, mc, mdy, mk, mdb, mdc, a);
   M3_TRY(check_launch("siso_chunk_bwd_kernel"));
-  siso_chunk_bwd_scal_kernel<<<units, 128, 0, s>>>(a);
+  const int64_t tiles = (int64_t)units * a.nch;
+  if (tiles > INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "siso backward: too many (unit, chunk) tiles");
+  siso_chunk_bwd_scal_kernel<<<(unsigned)tiles, 128, 0, s>>>(a);
   return check_launch("siso_chunk_bwd_scal_kernel");
 }
 

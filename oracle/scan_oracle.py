@@ -11,7 +11,10 @@ algorithm of the upstream package Aiyoniganmaaiya/mamba3-ssm v0.2.1:
   reference has no backward kernel; its gradients come from autograd through the loops,
   and the golden fixtures record those gradients.
 * ``rmsnorm`` (``ops.py:96-104``), ``apply_rope`` (``ops.py:116-119``).
-* ``mamba3_forward`` (``mamba3_ssm/layer.py:168-266``), ``mamba3_step``
+* ``siso_scan_bwd_segmented`` -- the SISO adjoint with per-segment recomputation (bounded
+  memory for long sequences).
+* ``mamba3_forward`` (``mamba3_ssm/layer.py:168-266``), ``mamba3_forward_backward`` (its
+  exact adjoint, the gradients autograd returns through it), ``mamba3_step``
   (``layer.py:272-374``), ``allocate_inference_cache`` (``layer.py:380-412``).
 * ``lm_forward`` / ``lm_step`` (``mamba3_ssm/block.py:93-139``).
 
@@ -121,6 +124,68 @@ def siso_scan_bwd(x, B, C, ADT, DT, trap, D, dy, h0=None, bx0=None):
     dbx0 = gam_next[..., None, None] * g_next
     return dict(dx=dx, dB=dB, dC=dC, dADT=dADT, dDT=dDT, dtrap=dtrap, dD=dD,
                 dh0=dh0, dbx0=dbx0)
+
+
+def siso_scan_bwd_segmented(x, B, C, ADT, DT, trap, D, dy, h0=None, bx0=None, seg=512):
+    """The same adjoint as ``siso_scan_bwd`` with bounded memory, for long sequences: the
+    forward keeps the state only at every ``seg``-th step, and the reverse pass recomputes
+    each segment's states from its checkpoint before walking it backwards. Same results
+    (float64, same operation order per step)."""
+    x = x.astype(f64); B = B.astype(f64); C = C.astype(f64); dy = dy.astype(f64)
+    Bn, L, H, P = x.shape
+    Ds = B.shape[-1]
+    a, dt, tr, beta, gamma = _coeffs(ADT, DT, trap)
+    starts = list(range(0, L, seg))
+    ck_h, ck_u = [], []
+    h = np.zeros((Bn, H, P, Ds)) if h0 is None else h0.astype(f64).copy()
+    up = np.zeros((Bn, H, P, Ds)) if bx0 is None else bx0.astype(f64).copy()
+    for t in range(L):
+        if t % seg == 0:
+            ck_h.append(h.copy())
+            ck_u.append(up.copy())
+        u = x[:, t][..., :, None] * B[:, t][..., None, :]
+        h = a[:, t][..., None, None] * h + beta[:, t][..., None, None] * u + gamma[:, t][..., None, None] * up
+        up = u
+    dx = np.empty_like(x); dB = np.empty_like(B); dC = np.empty_like(C)
+    dADT = np.empty((Bn, L, H)); dDT = np.empty((Bn, L, H)); dtrap = np.empty((Bn, L, H))
+    dD = np.zeros(H)
+    g_next = np.zeros((Bn, H, P, Ds))
+    a_next = np.zeros((Bn, H))
+    gam_next = np.zeros((Bn, H))
+    for si in range(len(starts) - 1, -1, -1):
+        t0 = starts[si]
+        t1 = min(L, t0 + seg)
+        n = t1 - t0
+        hs = np.empty((n + 1, Bn, H, P, Ds))
+        us = np.empty((n + 1, Bn, H, P, Ds))
+        hs[0] = ck_h[si]
+        us[0] = ck_u[si]
+        for j in range(n):
+            t = t0 + j
+            u = x[:, t][..., :, None] * B[:, t][..., None, :]
+            us[j + 1] = u
+            hs[j + 1] = (a[:, t][..., None, None] * hs[j] + beta[:, t][..., None, None] * u
+                         + gamma[:, t][..., None, None] * us[j])
+        for j in range(n - 1, -1, -1):
+            t = t0 + j
+            g = a_next[..., None, None] * g_next + dy[:, t][..., :, None] * C[:, t][..., None, :]
+            dC[:, t] = np.einsum("bhp,bhpd->bhd", dy[:, t], hs[j + 1])
+            v = beta[:, t][..., None, None] * g + gam_next[..., None, None] * g_next
+            dx[:, t] = D[None, :, None] * dy[:, t] + np.einsum("bhpd,bhd->bhp", v, B[:, t])
+            dB[:, t] = np.einsum("bhpd,bhp->bhd", v, x[:, t])
+            dbeta = np.einsum("bhpd,bhpd->bh", g, us[j + 1])
+            dgam = np.einsum("bhpd,bhpd->bh", g, us[j])
+            da = np.einsum("bhpd,bhpd->bh", g, hs[j])
+            dADT[:, t] = da * a[:, t]
+            trt = tr[:, t]
+            dDT[:, t] = dbeta * (1.0 - 0.5 * trt) + dgam * 0.5 * trt
+            dtrap[:, t] = 0.5 * dt[:, t] * (dgam - dbeta) * trt * (1.0 - trt)
+            dD += np.einsum("bhp,bhp->h", dy[:, t], x[:, t])
+            g_next = g
+            a_next = a[:, t]
+            gam_next = gamma[:, t]
+    return dict(dx=dx, dB=dB, dC=dC, dADT=dADT, dDT=dDT, dtrap=dtrap, dD=dD,
+                dh0=a_next[..., None, None] * g_next, dbx0=gam_next[..., None, None] * g_next)
 
 
 # ----------------------------------------------------------------------------------
@@ -299,6 +364,104 @@ def mamba3_forward(w, dims, u):
     y = y * (z * sigmoid(z))
     y = y.reshape(Bn, L, dims.d_inner)
     return y @ w["out_proj.weight"].astype(f64).T
+
+
+def _softplus_grad(v):
+    """Derivative of torch's softplus (beta 1, threshold 20): 1 above the threshold."""
+    return np.where(v > 20.0, 1.0, sigmoid(np.minimum(v, 20.0)))
+
+
+def _rope_bwd(dims, dout, out, ang):
+    """Adjoint of ``_rope_bc``: the rotation transposed for the input, and the angle
+    gradient d(ang) = sum over ranks of (-do1 * o2 + do2 * o1) from the rotated output."""
+    k = dims.split
+    a = ang[..., None, :, :]  # (..., 1, H, S)
+    c, s = np.cos(a), np.sin(a)
+    d1, d2 = dout[..., 0:k:2], dout[..., 1:k:2]
+    o1, o2 = out[..., 0:k:2], out[..., 1:k:2]
+    din = dout.copy()
+    din[..., 0:k:2] = d1 * c + d2 * s
+    din[..., 1:k:2] = -d1 * s + d2 * c
+    dang = np.sum(-d1 * o2 + d2 * o1, axis=-3)  # sum over R
+    return din, dang
+
+
+def _bc_heads_bwd(dims, raw, norm_w, dh, lead, eps=1e-5):
+    """Adjoint of ``_bc_heads``: returns (d raw (..., R*G*D), d norm weight (D,),
+    d bias (H, R, D)) from the gradient ``dh`` (..., R, H, D) of the biased heads."""
+    R, G, Ds, H = dims.R, dims.ngroups, dims.d_state, dims.H
+    r = raw.reshape(*lead, R, G, Ds).astype(f64)
+    rms = np.sqrt(np.mean(r * r, axis=-1, keepdims=True) + eps)
+    nb = len(lead)
+    dbias = np.swapaxes(dh.sum(axis=tuple(range(nb))), 0, 1)  # (R,H,D) -> (H,R,D)
+    dn = dh.reshape(*lead, R, G, H // G, Ds).sum(axis=-2)  # heads of each group
+    w = norm_w.astype(f64)
+    dw = np.sum(dn * r / rms, axis=tuple(range(nb + 2)))
+    wdn = w * dn
+    dr = wdn / rms - r * np.sum(wdn * r, axis=-1, keepdims=True) / (Ds * rms ** 3)
+    return dr.reshape(*lead, R * G * Ds), dw, dbias
+
+
+def mamba3_forward_backward(w, dims, u, dout):
+    """layer.py:168-266 in float64 with its exact adjoint: the output and the gradients
+    autograd returns through the reference's forward for the upstream gradient ``dout``.
+    Returns (out, grads) with grads keyed by state_dict name plus "u"."""
+    u = u.astype(f64)
+    dout = dout.astype(f64)
+    Bn, L, dm = u.shape
+    H, P, Ds = dims.H, dims.headdim, dims.d_state
+    Win = w["in_proj.weight"].astype(f64)
+    Wout = w["out_proj.weight"].astype(f64)
+    allp = u @ Win.T
+    z, x, Braw, Craw, ddt, dA, trap, angr = dims.split_proj(allp)
+    z = z.reshape(Bn, L, H, P)
+    x = x.reshape(Bn, L, H, P)
+    A = -np.minimum(softplus(dA), -dims.A_floor)
+    pre = ddt + w["dt_bias"].astype(f64)
+    DT = softplus(pre)
+    ADT = A * DT
+    Bh = _bc_heads(dims, Braw, w["B_norm.weight"], w["B_bias"], (Bn, L))
+    Ch = _bc_heads(dims, Craw, w["C_norm.weight"], w["C_bias"], (Bn, L))
+    ang = np.cumsum(angr[:, :, None, :] * DT[..., None], axis=1)
+    Bp = _rope_bc(dims, Bh, ang)
+    Cp = _rope_bc(dims, Ch, ang)
+    if dims.is_mimo:
+        y, _, _ = mimo_scan_fwd(x, Bp, Cp, ADT, DT, trap, w["D"], w["mimo_x"], w["mimo_o"])
+    else:
+        y, _, _ = siso_scan_fwd(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, w["D"])
+    sz = sigmoid(z)
+    g = y * (z * sz)
+    out = g.reshape(Bn, L, dims.d_inner) @ Wout.T
+    # ---- adjoint
+    grads = {}
+    grads["out_proj.weight"] = dout.reshape(-1, dm).T @ g.reshape(-1, dims.d_inner)
+    dg = (dout @ Wout).reshape(Bn, L, H, P)
+    dy = dg * (z * sz)
+    dz = dg * y * (sz * (1.0 + z * (1.0 - sz)))
+    if dims.is_mimo:
+        sg = mimo_scan_bwd(x, Bp, Cp, ADT, DT, trap, w["D"], w["mimo_x"], w["mimo_o"], dy)
+        dBp, dCp = sg["dB"], sg["dC"]
+        grads["mimo_x"] = sg["dmimo_x"]
+        grads["mimo_o"] = sg["dmimo_o"]
+    else:
+        sg = siso_scan_bwd(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, w["D"], dy)
+        dBp, dCp = sg["dB"][:, :, None], sg["dC"][:, :, None]
+    grads["D"] = sg["dD"]
+    dDT = sg["dDT"] + A * sg["dADT"]  # the clamp makes A constant: dd_A gets no gradient
+    dBh, dangB = _rope_bwd(dims, dBp, Bp, ang)
+    dCh, dangC = _rope_bwd(dims, dCp, Cp, ang)
+    q = np.cumsum((dangB + dangC)[:, ::-1], axis=1)[:, ::-1]  # suffix sums over L
+    dangr = np.einsum("blhs,blh->bls", q, DT)
+    dDT = dDT + np.einsum("blhs,bls->blh", q, angr)
+    dBraw, grads["B_norm.weight"], grads["B_bias"] = _bc_heads_bwd(dims, Braw, w["B_norm.weight"], dBh, (Bn, L))
+    dCraw, grads["C_norm.weight"], grads["C_bias"] = _bc_heads_bwd(dims, Craw, w["C_norm.weight"], dCh, (Bn, L))
+    dpre = dDT * _softplus_grad(pre)
+    grads["dt_bias"] = dpre.sum(axis=(0, 1))
+    dallp = np.concatenate([dz.reshape(Bn, L, -1), sg["dx"].reshape(Bn, L, -1), dBraw, dCraw, dpre,
+                            np.zeros((Bn, L, H)), sg["dtrap"], dangr], axis=-1)
+    grads["in_proj.weight"] = dallp.reshape(-1, dims.d_in_proj).T @ u.reshape(-1, dm)
+    grads["u"] = dallp @ Win
+    return out, grads
 
 
 def allocate_inference_cache(dims, batch):

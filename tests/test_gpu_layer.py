@@ -3,7 +3,8 @@ reference's own outputs (golden fixtures recorded from layer.py / block.py on th
 forward, backward (every parameter gradient and du), the fused decode step replayed
 token by token, and the reference's invariant step == forward (tests.py:67-108).
 
-Tolerances: rel 1e-4 in fp32, rel 2e-2 in bf16 (max|a - ref| / max|ref|)."""
+Tolerances: rel 1e-4 in fp32, rel 2e-2 in bf16 (max|a - ref| / max|ref|). bf16 layer
+gradients are measured against the float64 adjoint of the oracle (see _grad_bar)."""
 
 import numpy as np
 import pytest
@@ -34,6 +35,26 @@ LAYERS = ["layer_c1_siso_f32", "layer_siso_f32_grad", "layer_siso_rope1_f32", "l
           "layer_c2_mimo_bf16", "layer_siso_bf16"]
 
 
+def _grad_bar(g, name, tol):
+    """Bars for the gradients of a layer fixture: the parity bar itself in fp32. In bf16 the
+    fixture is the reference's own bf16 result, which can sit near 2e-2 from the exact
+    gradient (bf16 parameters and activations); there this build's gradient is compared
+    with the float64 adjoint of the oracle instead, within max(2e-2, 1.5x the reference's
+    own distance from it). Returns {key: (target array, bar)}."""
+    keys = ["du"] + [k for k in g if k.startswith("g.")]
+    if str(g["dtype"]) != "bfloat16":
+        return {k: (g[k], tol) for k in keys}
+    from oracle import scan_oracle as O
+    cfg = {k[4:]: g[k].item() for k in g if k.startswith("cfg.")}
+    w = {k[2:]: g[k] for k in g if k.startswith("w.")}
+    _, og = O.mamba3_forward_backward(w, O.LayerDims(**cfg), g["u"], g["dy"])
+    out = {}
+    for k in keys:
+        ok = "u" if k == "du" else k[2:]
+        out[k] = (og[ok], max(tol, 1.5 * rel_err(g[k], og[ok])))
+    return out
+
+
 @pytest.mark.parametrize("name", LAYERS)
 def test_layer_forward_backward_step(name):
     g = load_golden(name)
@@ -46,11 +67,14 @@ def test_layer_forward_backward_step(name):
     assert rel_err(y.float().detach().cpu().numpy(), g["y"]) < tol
     if "du" in g:
         y.backward(_t(g, "dy"))
-        assert rel_err(u.grad.detach().float().cpu().numpy(), g["du"]) < tol
+        bars = _grad_bar(g, name, tol)
+        ref, bar = bars["du"]
+        assert rel_err(u.grad.detach().float().cpu().numpy(), ref) < bar
         for k, p in m.named_parameters():
             gk = "g." + k
             if gk in g:
-                assert rel_err(p.grad.detach().float().cpu().numpy(), g[gk]) < tol * 5, k
+                ref, bar = bars[gk]
+                assert rel_err(p.grad.detach().float().cpu().numpy(), ref) < bar, k
     n = g["step_y"].shape[1]
     with torch.no_grad():
         a, s, b = m.allocate_inference_cache(u.shape[0])

@@ -2,8 +2,7 @@
 reference's own outputs (golden fixtures) and with the float64 oracle.
 
 Tolerances (max|a - ref| / max|ref| per tensor): rel 1e-4 for fp32 I/O, rel 2e-2 for bf16
-I/O, the bars of the parity target; parameter-like gradients that sum over the whole
-sequence (dADT, dDT, dtrap, dD) get 5x that.
+I/O, the bars of the parity target, for every output and every gradient.
 """
 
 import numpy as np
@@ -52,9 +51,8 @@ def test_siso_fwd_bwd_matches_reference(name):
     assert rel_err(y.detach().float().cpu().numpy(), g["y"]) < tol
     y.backward(_t(g, "dy"))
     for k, t in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
-        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
         assert t.grad.dtype == t.dtype
-        assert rel_err(t.grad.detach().float().cpu().numpy(), g[k]) < tol * f, k
+        assert rel_err(t.grad.detach().float().cpu().numpy(), g[k]) < tol, k
 
 
 @pytest.mark.parametrize("name", MIMO)
@@ -67,8 +65,7 @@ def test_mimo_fwd_bwd_matches_reference(name):
     assert rel_err(y.detach().float().cpu().numpy(), g["y"]) < tol
     y.backward(_t(g, "dy"))
     for k, t in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
-        f = 5 if k in ("dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o") else 1
-        assert rel_err(t.grad.detach().float().cpu().numpy(), g[k]) < tol * f, k
+        assert rel_err(t.grad.detach().float().cpu().numpy(), g[k]) < tol, k
 
 
 def _inputs(seed, Bn, L, H, P, D, R=None, dtype=torch.float32):
@@ -109,8 +106,7 @@ def test_siso_sweep_against_oracle(D, P, L, dtype):
     y.backward(dy)
     go = O.siso_scan_bwd(*[arrs[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")], dy.detach().double().cpu().numpy())
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
-        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
-        assert rel_err(tt.grad.detach().double().cpu().numpy(), go[k]) < tol * f, k
+        assert rel_err(tt.grad.detach().double().cpu().numpy(), go[k]) < tol, k
 
 
 @pytest.mark.parametrize("R,D,P", [(1, 16, 16), (2, 32, 64), (4, 64, 32), (8, 128, 64), (4, 64, 64)])
@@ -128,8 +124,7 @@ def test_mimo_sweep_against_oracle(R, D, P, dtype):
     y.backward(dy)
     go = O.mimo_scan_bwd(*[arrs[k] for k in keys], dy.detach().double().cpu().numpy())
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
-        f = 5 if k in ("dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o") else 1
-        assert rel_err(tt.grad.detach().double().cpu().numpy(), go[k]) < tol * f, k
+        assert rel_err(tt.grad.detach().double().cpu().numpy(), go[k]) < tol, k
 
 
 def test_siso_strided_views_and_state_continuation():
@@ -285,9 +280,9 @@ def test_mimo_chunked_backward_with_states(L, R, D, P):
     go = O.mimo_scan_bwd(*[arrs[k] for k in keys], dy.double().cpu().numpy(),
                          h0.detach().double().cpu().numpy(), b0.detach().double().cpu().numpy())
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
-        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < 5e-4, k
-    assert rel_err(h0.grad.double().cpu().numpy(), go["dh0"]) < 5e-4
-    assert rel_err(b0.grad.double().cpu().numpy(), go["dbx0"]) < 5e-4
+        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < 1e-4, k
+    assert rel_err(h0.grad.double().cpu().numpy(), go["dh0"]) < 1e-4
+    assert rel_err(b0.grad.double().cpu().numpy(), go["dbx0"]) < 1e-4
 
 
 def _siso_grads(ins, h0=None, b0=None):
@@ -323,8 +318,7 @@ def test_siso_bf16_chunked_backward_against_oracle(L, states, Ds):
     npy = lambda v: None if v is None else v.detach().double().cpu().numpy()
     go = O.siso_scan_bwd(*[arrs[k] for k in keys], npy(dy), npy(h0), npy(b0))
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
-        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
-        assert rel_err(npy(tt.grad), go[k]) < 2e-2 * f, k
+        assert rel_err(npy(tt.grad), go[k]) < 2e-2, k
     if states:
         assert rel_err(npy(h0.grad), go["dh0"]) < 2e-2
         assert rel_err(npy(b0.grad), go["dbx0"]) < 2e-2
@@ -346,8 +340,7 @@ def test_siso_bf16_chunked_backward_many_units(L, Ds):
     npy = lambda v: None if v is None else v.detach().double().cpu().numpy()
     go = O.siso_scan_bwd(*[arrs[k] for k in keys], npy(dy), npy(h0), npy(b0))
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
-        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
-        assert rel_err(npy(tt.grad), go[k]) < 2e-2 * f, k
+        assert rel_err(npy(tt.grad), go[k]) < 2e-2, k
     assert rel_err(npy(h0.grad), go["dh0"]) < 2e-2
     assert rel_err(npy(b0.grad), go["dbx0"]) < 2e-2
 
@@ -373,8 +366,7 @@ def test_siso_bf16_chunked_backward_extreme_decay(case):
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), ins):
         g = tt.grad.detach().double().cpu().numpy()
         assert np.isfinite(g).all(), k
-        f = 5 if k in ("dADT", "dDT", "dtrap", "dD") else 1
-        assert rel_err(g, go[k]) < 2e-2 * f, k
+        assert rel_err(g, go[k]) < 2e-2, k
 
 
 def test_siso_bwd_entry_points_agree():
@@ -401,5 +393,5 @@ def test_siso_bwd_entry_points_agree():
         for k, o, r in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"), outs, ref):
             # same chunked kernels: equal up to the order of the dD atomics; the CUDA-core
             # path: within the bf16 bar
-            tol = 1e-5 if ws_bytes > 4 * Bn * Ln * H else 2e-2 * (5 if k in ("dADT", "dDT", "dtrap", "dD") else 1)
+            tol = 1e-5 if ws_bytes > 4 * Bn * Ln * H else 2e-2
             assert rel_err(o.double().cpu().numpy(), r.double().cpu().numpy()) < tol, (k, ws_bytes)

@@ -29,7 +29,7 @@ def test_siso_scan_oracle_matches_reference(name):
     assert rel_err(y, g["y"]) < _tol(g)
     grads = O.siso_scan_bwd(*args, g["dy"])
     for k in ("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD"):
-        assert rel_err(grads[k], g[k]) < _tol(g) * (5 if k in ("dADT", "dDT", "dtrap", "dD") else 1), k
+        assert rel_err(grads[k], g[k]) < _tol(g), k
 
 
 @pytest.mark.parametrize("name", MIMO_OPS)
@@ -40,7 +40,7 @@ def test_mimo_scan_oracle_matches_reference(name):
     assert rel_err(y, g["y"]) < _tol(g)
     grads = O.mimo_scan_bwd(*args, g["dy"])
     for k in ("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"):
-        assert rel_err(grads[k], g[k]) < _tol(g) * (5 if k in ("dADT", "dDT", "dtrap", "dD") else 1), k
+        assert rel_err(grads[k], g[k]) < _tol(g), k
 
 
 def _weights(g):
@@ -139,3 +139,37 @@ def test_c_restatement_matches_reference(name):
     g = load_golden(name)
     y = cpu_ref.siso_fwd(*[g[k] for k in ("x", "B", "C", "ADT", "DT", "trap", "D")])
     assert rel_err(y, g["y"]) < (2e-2 if str(g["dtype"]) == "bfloat16" else 1e-5)
+
+
+@pytest.mark.parametrize("name", ["layer_siso_f32_grad", "layer_mimo_f32_grad", "layer_c2_mimo_bf16"])
+def test_layer_adjoint_matches_reference(name):
+    """The oracle's layer adjoint (mamba3_forward_backward) against the gradients autograd
+    returned through the reference's Mamba3.forward (fixtures recorded from the reference)."""
+    g = load_golden(name)
+    dims = O.LayerDims(**_cfg(g, "cfg."))
+    w = _weights(g)
+    out, grads = O.mamba3_forward_backward(w, dims, g["u"], g["dy"])
+    bf = str(g["dtype"]) == "bfloat16"
+    tol = 2e-2 if bf else 1e-5
+    assert rel_err(out, g["y"]) < tol
+    assert rel_err(grads["u"], g["du"]) < tol
+    for k in w:
+        if ("g." + k) in g:
+            assert grads[k].shape == g["g." + k].shape, k
+            assert rel_err(grads[k], g["g." + k]) < tol, k
+
+
+def test_segmented_adjoint_equals_full_adjoint():
+    """siso_scan_bwd_segmented (checkpointed, bounded memory) gives the adjoint of
+    siso_scan_bwd on a ragged length with initial states."""
+    rng = np.random.default_rng(3)
+    Bn, L, H, P, D = 2, 37, 2, 4, 6
+    x = rng.standard_normal((Bn, L, H, P)); Bm = rng.standard_normal((Bn, L, H, D))
+    C = rng.standard_normal((Bn, L, H, D)); ADT = -rng.uniform(0.01, 1, (Bn, L, H))
+    DT = rng.uniform(0.01, 0.1, (Bn, L, H)); trap = rng.standard_normal((Bn, L, H))
+    Dw = rng.standard_normal(H); dy = rng.standard_normal((Bn, L, H, P))
+    h0 = rng.standard_normal((Bn, H, P, D)); b0 = rng.standard_normal((Bn, H, P, D))
+    full = O.siso_scan_bwd(x, Bm, C, ADT, DT, trap, Dw, dy, h0, b0)
+    seg = O.siso_scan_bwd_segmented(x, Bm, C, ADT, DT, trap, Dw, dy, h0, b0, seg=8)
+    for k in full:
+        assert np.array_equal(full[k], seg[k]), k
