@@ -110,6 +110,7 @@ struct __align__(1024) Smem {
   uint64_t g_full[2], gp_ready[2], y_full[2], y2_free[2];
   uint64_t y1_full[2], y1_free, dk_full, dk_free;  // y1_full per parity: its two waiters
                                                    // are a chunk apart
+                                                   // are a chunk apart
   uint64_t scal_full[NSC], scal_empty[NSC];
   uint32_t tmem_base;
 };
@@ -123,7 +124,6 @@ __device__ int g_chunk_error;  // set when a bounded wait gives up
 struct ChunkArgs {
   int Bn, L, H;
   int D;     // d_state: 128, or 64 (the second halves of the C / B tiles then stay zero)
-  int nkd;   // K steps of 16 over d_state in G and Y1
   const float* adt; Str3 sadt;
   const float* dt; Str3 sdt;
   const float* trap; Str3 strap;
@@ -467,12 +467,14 @@ __device__ void mask_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, in
   const int wr = warp & 3;
   uint32_t wg_phase = 0;
   RawRow raw;
-  if (parity < G) load_raw_row(a, chunk_pos(a, parity, nch), i, raw);
+  float li = 0.f, bi = 0.f, wk = 0.f;  // row i's lambda, beta and state weight of chunk g
+  if (parity < G) {
+    load_raw_row(a, chunk_pos(a, parity, nch), i, raw);
+    if (!scal_phase(a, s, parity, nch, i, raw, wg_phase, li, bi, wk)) return;
+    if (parity + 2 < G) load_raw_row(a, chunk_pos(a, parity + 2, nch), i, raw);
+  }
   for (int g = parity; g < G; g += 2) {
     const int p = g & 1, q = g % NSC;
-    float li, bi, wk;
-    if (!scal_phase(a, s, g, nch, i, raw, wg_phase, li, bi, wk)) return;
-    if (g + 2 < G) load_raw_row(a, chunk_pos(a, g + 2, nch), i, raw);  // this warpgroup's next chunk
     // (w o x) row i of this chunk, for dK(g)
     if (!wait_or_flag(&s.x_full[p], (g >> 1) & 1)) return;
     if (!wait_or_flag(&s.xs_empty[p], ((g >> 1) & 1) ^ 1)) return;
@@ -511,12 +513,22 @@ __device__ void mask_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, in
     tmem_wait_st();
     tc_fence_before();
     mbar_arrive(&s.gp_ready[p]);
+    // the scalars of this warpgroup's next chunk, while Y1 / Y2 of this one run (its slot
+    // was released by chunk g - 2)
+    float li_n = 0.f, bi_n = 0.f, wk_n = 0.f;
+    if (g + 2 < G) {
+      if (!scal_phase(a, s, g + 2, nch, i, raw, wg_phase, li_n, bi_n, wk_n)) return;
+      if (g + 4 < G) load_raw_row(a, chunk_pos(a, g + 4, nch), i, raw);
+    }
     // this chunk's outputs
     if (!wait_or_flag(&s.y_full[p], (g >> 1) & 1)) return;
     if (!wait_or_flag(&s.y1_full[p], (g >> 1) & 1)) return;
     tc_fence_after();
     epilogue(a, s, tbase, g, nch, warp, i);
     mbar_arrive(&s.scal_empty[q]);
+    li = li_n;
+    bi = bi_n;
+    wk = wk_n;
   }
 }
 
@@ -621,6 +633,127 @@ __device__ void state_role(const ChunkArgs& a, Smem& s, uint32_t tbase, int G, i
 }
 
 // ------------------------------------------------------------------------------------
+// warp 1, one thread: the tcgen05 MMAs, in three streams, each in chunk order:
+//   G  : G(c) = C B^T                 needs the C/B stage, and Y2(c-2) issued (G'(c-2) read:
+//                                     the tensor pipe runs MMAs in issue order)
+//   K  : dK(c) = B^T (w o X), then Y1(c) = C k_c^T
+//        dK(c) needs w o X(c), the dK columns read (dK(c-1) consumed) and G(c) issued;
+//        Y1(c) needs k_c and the Y1 columns read (epilogue of c-1); Y1(c) is the last
+//        reader of the stage, so its commit frees it
+//   Y2 : Y2(c) = G' X                 needs the mask of c, X(c) and w o X(c), the Y2
+//                                     columns of c-2 read
+// A single thread issuing dependent integer work runs at instruction latency, so the issue
+// path is kept short: shared-memory descriptors are formed once and advanced by constant
+// offsets, every group is unrolled, and a stream's readiness conditions are polled only
+// until each has been seen to hold (sticky bits, reset when the group is issued).
+// ------------------------------------------------------------------------------------
+template <int NKD>
+__device__ __forceinline__ void mma_role(Smem& s, uint32_t tbase, int G) {
+  constexpr uint32_t I_G = idesc_bf16_f32(128, 128, false, false);
+  constexpr uint32_t I_Y = idesc_bf16_f32(128, 64, false, true);
+  constexpr uint32_t I_DK = idesc_bf16_f32(128, 64, true, true);
+  // K-major tiles: +32 B per K step of 16, +one tile per 64 K elements; MN-major tiles:
+  // +2048 B (16 rows) per K step. Descriptor addresses are in 16-byte units.
+  constexpr uint64_t kTileU = kTileBytes >> 4;
+  const uint64_t dC0 = sdesc_sw128(smem_u32(s.cb[0][0]), 16, 1024), dC1 = sdesc_sw128(smem_u32(s.cb[1][0]), 16, 1024);
+  const uint64_t dB0 = sdesc_sw128(smem_u32(s.cb[0][2]), 16, 1024), dB1 = sdesc_sw128(smem_u32(s.cb[1][2]), 16, 1024);
+  const uint64_t dBt0 = sdesc_sw128(smem_u32(s.cb[0][2]), kTileBytes, 1024);
+  const uint64_t dBt1 = sdesc_sw128(smem_u32(s.cb[1][2]), kTileBytes, 1024);
+  const uint64_t dXs0 = sdesc_sw128(smem_u32(s.xs[0]), kTileBytes, 1024);
+  const uint64_t dXs1 = sdesc_sw128(smem_u32(s.xs[1]), kTileBytes, 1024);
+  const uint64_t dX0 = sdesc_sw128(smem_u32(s.xr[0]), kTileBytes, 1024);
+  const uint64_t dX1 = sdesc_sw128(smem_u32(s.xr[1]), kTileBytes, 1024);
+  const uint64_t dKb = sdesc_sw128(smem_u32(s.kbuf), kTileBytes, 1024);
+  int cg = 0, ck = 0, sk = 0, gb = 0;
+  uint32_t rk = 0, ry = 0;  // sticky readiness bits of the K and Y2 streams
+  uint32_t idle = 0;
+  while (cg < G || ck < G || gb < G) {
+    bool moved = false;
+    if (cg < G && gb >= cg - 1 && mbar_test(&s.cb_full[cg & 1], (cg >> 1) & 1)) {
+      const int p = cg & 1;
+      const uint64_t a0 = p ? dC1 : dC0, b0 = p ? dB1 : dB0;
+      const uint32_t d = tbase + col_g(p);
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < NKD; ++kk) {
+        const uint64_t off = (uint64_t)(kk >> 2) * kTileU + (uint64_t)(kk & 3) * 2u;
+        mma_ss(d, a0 + off, b0 + off, I_G, kk > 0);
+      }
+      mma_commit(&s.g_full[p]);
+      ++cg;
+      moved = true;
+    }
+    if (ck < G) {
+      const int p = ck & 1;
+      if (sk == 0) {
+        if (!(rk & 1) && mbar_test(&s.xs_full[p], (ck >> 1) & 1)) rk |= 1;
+        if (!(rk & 2) && mbar_test(&s.dk_free, (ck & 1) ^ 1)) rk |= 2;
+        if (rk == 3 && cg > ck) {
+          const uint64_t a0 = p ? dBt1 : dBt0, b0 = p ? dXs1 : dXs0;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) mma_ss(tbase + kColDK, a0 + (uint64_t)kk * 128u, b0 + (uint64_t)kk * 128u, I_DK, kk > 0);
+          mma_commit(&s.dk_full);
+          mma_commit(&s.xs_empty[p]);
+          sk = 1;
+          rk = 0;
+          moved = true;
+        }
+      } else {
+        if (!(rk & 1) && mbar_test(&s.k_ready, ck & 1)) rk |= 1;
+        if (!(rk & 2) && mbar_test(&s.y1_free, (ck & 1) ^ 1)) rk |= 2;
+        if (rk == 3) {
+          const uint64_t a0 = p ? dC1 : dC0;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < NKD; ++kk)
+            mma_ss(tbase + kColY1, a0 + (uint64_t)(kk >> 2) * kTileU + (uint64_t)(kk & 3) * 2u, dKb + (uint64_t)kk * 128u,
+                   I_Y, kk > 0);
+          mma_commit(&s.y1_full[p]);
+          mma_commit(&s.cb_empty[p]);  // last reader of this C/B stage
+          sk = 0;
+          rk = 0;
+          ++ck;
+          moved = true;
+        }
+      }
+    }
+    if (gb < G) {
+      const int p = gb & 1;
+      const uint32_t ph = (gb >> 1) & 1;
+      // (w o X(gb) written implies the mask warps are past their wait on X(gb), so X(gb+2)
+      // cannot land in this slot before that wait)
+      if (!(ry & 1) && mbar_test(&s.gp_ready[p], ph)) ry |= 1;
+      if (!(ry & 2) && mbar_test(&s.x_full[p], ph)) ry |= 2;
+      if (!(ry & 4) && mbar_test(&s.xs_full[p], ph)) ry |= 4;
+      if (!(ry & 8) && mbar_test(&s.y2_free[p], ph ^ 1)) ry |= 8;
+      if (ry == 15) {
+        const uint64_t b0 = p ? dX1 : dX0;
+        const uint32_t d = tbase + col_y2(p), a = tbase + col_g(p);
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) mma_ts(d, a + 8u * kk, b0 + (uint64_t)kk * 128u, I_Y, kk > 0);
+        mma_commit(&s.y_full[p]);
+        mma_commit(&s.x_empty[p]);
+        ry = 0;
+        ++gb;
+        moved = true;
+      }
+    }
+    if (moved) {
+      idle = 0;
+    } else {
+      if (++idle > kIdleLimit) {
+        atomicExch(&g_chunk_error, 1);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+template <int NKD>
 __global__ void __launch_bounds__(kThreads, 1)
 siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_B,
                       const __grid_constant__ CUtensorMap tm_C, ChunkArgs a) {
@@ -726,99 +859,7 @@ siso_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_con
       }
     }
   } else if (warp == 1) {
-    // one MMA issuer thread polling three streams, each in chunk order:
-    //   G  : G(c) = C B^T                 needs the C/B stage, and Y2(c-2) issued (G'(c-2)
-    //                                     read: the tensor pipe runs MMAs in issue order)
-    //   K  : dK(c) = B^T (w o X), then Y1(c) = C k_c^T
-    //        dK(c) needs w o X(c), the dK columns read (dK(c-1) consumed) and G(c) issued;
-    //        Y1(c) needs k_c and the Y1 columns read (epilogue of c-1); Y1(c) is the last
-    //        reader of the stage, so its commit frees it
-    //   Y2 : Y2(c) = G' X                 needs the mask of c, X(c) and w o X(c), the Y2
-    //                                     columns of c-2 read
-    if (lane == 0) {
-      constexpr uint32_t I_G = idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t I_Y = idesc_bf16_f32(128, 64, false, true);
-      constexpr uint32_t I_DK = idesc_bf16_f32(128, 64, true, true);
-      const uint32_t a_kb = smem_u32(s.kbuf);
-      auto cb_addr = [&](int st, int t) { return smem_u32(s.cb[st][t]); };
-      int cg = 0, ck = 0, sk = 0, gb = 0;
-      uint32_t idle = 0;
-      while (cg < G || ck < G || gb < G) {
-        bool moved = false;
-        if (cg < G && gb >= cg - 1 && mbar_test(&s.cb_full[cg % NS], (cg / NS) & 1)) {
-          const int st = cg % NS, p = cg & 1;
-          tc_fence_after();
-          const uint32_t c0 = cb_addr(st, 0), b0 = cb_addr(st, 2);
-#pragma unroll 4
-          for (int kk = 0; kk < a.nkd; ++kk) {
-            const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
-            mma_ss(tbase + col_g(p), sdesc_sw128(c0 + koff, 16, 1024), sdesc_sw128(b0 + koff, 16, 1024), I_G,
-                   kk > 0);
-          }
-          mma_commit(&s.g_full[p]);
-          ++cg;
-          moved = true;
-        }
-        if (ck < G) {
-          const int st = ck % NS, p = ck & 1;
-          if (sk == 0) {
-            if (cg > ck && mbar_test(&s.xs_full[p], (ck >> 1) & 1) && mbar_test(&s.dk_free, (ck & 1) ^ 1)) {
-              tc_fence_after();
-              const uint32_t ba = cb_addr(st, 2), xsa = smem_u32(s.xs[p]);
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk)
-                mma_ss(tbase + kColDK, sdesc_sw128(ba + (uint32_t)kk * 2048u, kTileBytes, 1024),
-                       sdesc_sw128(xsa + (uint32_t)kk * 2048u, kTileBytes, 1024), I_DK, kk > 0);
-              mma_commit(&s.dk_full);
-              mma_commit(&s.xs_empty[p]);
-              sk = 1;
-              moved = true;
-            }
-          } else if (mbar_test(&s.k_ready, ck & 1) && mbar_test(&s.y1_free, (ck & 1) ^ 1)) {
-            tc_fence_after();
-            const uint32_t c0 = cb_addr(st, 0);
-#pragma unroll 4
-            for (int kk = 0; kk < a.nkd; ++kk) {
-              const uint32_t koff = (uint32_t)(kk >> 2) * kTileBytes + (uint32_t)(kk & 3) * 32u;
-              mma_ss(tbase + kColY1, sdesc_sw128(c0 + koff, 16, 1024),
-                     sdesc_sw128(a_kb + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
-            }
-            mma_commit(&s.y1_full[p]);
-            mma_commit(&s.cb_empty[st]);  // last reader of this C/B stage
-            sk = 0;
-            ++ck;
-            moved = true;
-          }
-        }
-        if (gb < G) {
-          const int p = gb & 1, xi = p;
-          // (w o X(gb) written implies the scalar warp is past its wait on X(gb), so X(gb+2)
-          // cannot land in this slot before that wait)
-          if (mbar_test(&s.gp_ready[p], (gb >> 1) & 1) && mbar_test(&s.x_full[xi], (gb >> 1) & 1) &&
-              mbar_test(&s.xs_full[p], (gb >> 1) & 1) && mbar_test(&s.y2_free[p], ((gb >> 1) & 1) ^ 1)) {
-            tc_fence_after();
-            const uint32_t xa = smem_u32(s.xr[xi]);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              mma_ts(tbase + col_y2(p), tbase + col_g(p) + 8u * kk,
-                     sdesc_sw128(xa + (uint32_t)kk * 2048u, kTileBytes, 1024), I_Y, kk > 0);
-            mma_commit(&s.y_full[p]);
-            mma_commit(&s.x_empty[xi]);
-            ++gb;
-            moved = true;
-          }
-        }
-        if (moved) {
-          idle = 0;
-        } else {
-          if (++idle > kIdleLimit) {
-            atomicExch(&g_chunk_error, 1);
-            break;
-          }
-          __nanosleep(32);
-        }
-      }
-    }
+    if (lane == 0) mma_role<NKD>(s, tbase, G);
   } else if (warp >= 4 && warp < 8) {
     mask_role(a, s, tbase, G, nch, warp, tid - 128, 0);
   } else if (warp >= 8 && warp < 12) {
@@ -912,7 +953,7 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
   M3_TRY(make_map(&mc, p.Cm, p.D, p.H, p.L, p.Bn, p.sC));
   ChunkArgs a{};
   a.Bn = p.Bn; a.L = p.L; a.H = p.H;
-  a.D = p.D; a.nkd = p.D / 16;
+  a.D = p.D;
   a.adt = p.adt; a.sadt = p.sadt;
   a.dt = p.dt; a.sdt = p.sdt;
   a.trap = p.trap; a.strap = p.strap;
@@ -923,13 +964,16 @@ int launch_siso_fwd_chunked(const SisoParams& p, int xdt, int bcdt, cudaStream_t
   a.kst = reinterpret_cast<__nv_bfloat16*>(p.kstates);
   const size_t smem = sizeof(Smem) + 1024;
   // the shared-memory opt-in belongs to each device's context: set it once per device
-  static std::atomic<bool> smem_set[kMaxDevices];
-  M3_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(siso_chunk_fwd_kernel), smem, smem_set));
+  static std::atomic<bool> smem_set[2][kMaxDevices];
+  const void* kfn = p.D == kD ? reinterpret_cast<const void*>(siso_chunk_fwd_kernel<8>)
+                              : reinterpret_cast<const void*>(siso_chunk_fwd_kernel<4>);
+  M3_TRY(ensure_dynamic_smem(kfn, smem, smem_set[p.D == kD ? 0 : 1]));
   int sms = 0;
   M3_TRY(device_sm_count(&sms));
   const int units = p.Bn * p.H;
   const int grid = units < sms ? units : sms;
-  siso_chunk_fwd_kernel<<<grid, kThreads, smem, s>>>(mx, mb, mc, a);
+  if (p.D == kD) siso_chunk_fwd_kernel<8><<<grid, kThreads, smem, s>>>(mx, mb, mc, a);
+  else siso_chunk_fwd_kernel<4><<<grid, kThreads, smem, s>>>(mx, mb, mc, a);
   M3_TRY(check_launch("siso_chunk_fwd_kernel"));
   if (!p.bx_last) return M3_OK;
   bx_last_kernel<<<units, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(p.x), p.sx,
