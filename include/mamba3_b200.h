@@ -278,11 +278,15 @@ int m3_argmax_rows(const m3_tensor* logits, m3_tensor* out, void* stream);
  *   (eps = dims->norm_eps) * weight + bias per head, pairs (2i, 2i+1) with 2i < rope_split
  *   rotated by angles. Parameters fp32 as in m3_siso_step. Replaces the PyTorch prologue
  *   of the reference (layer.py:198-244), which materialises the per-head B / C in fp32.
+ *   angle0 (batch, nheads, S) f32, optional: the angle state of a decode cache to continue
+ *   from (the cumulative angles then start there, as they would after that many step()s);
+ *   absent = zeros, as in the reference's forward.
  * ------------------------------------------------------------------------------- */
 int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
                       const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
-                      const m3_tensor* C_norm_w, m3_tensor* B_proj, m3_tensor* C_proj, m3_tensor* ADT,
-                      m3_tensor* DT, m3_tensor* trap, m3_tensor* angles, void* stream);
+                      const m3_tensor* C_norm_w, const m3_tensor* angle0, m3_tensor* B_proj,
+                      m3_tensor* C_proj, m3_tensor* ADT, m3_tensor* DT, m3_tensor* trap,
+                      m3_tensor* angles, void* stream);
 
 /* out = y * silu(z), (B, L, H, P) views with innermost stride 1; the gate of
  * Mamba3.forward between the scan and out_proj (layer.py:262-266). */

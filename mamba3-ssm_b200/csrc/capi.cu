@@ -793,8 +793,8 @@ int m3_device_timeouts(int reset, int* flag_out) {
 
 int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
                       const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
-                      const m3_tensor* C_norm_w, m3_tensor* B_proj, m3_tensor* C_proj, m3_tensor* ADT,
-                      m3_tensor* DT, m3_tensor* trap, m3_tensor* angles, void* stream) {
+                      const m3_tensor* C_norm_w, const m3_tensor* angle0, m3_tensor* B_proj, m3_tensor* C_proj,
+                      m3_tensor* ADT, m3_tensor* DT, m3_tensor* trap, m3_tensor* angles, void* stream) {
   if (!dims) return fail(M3_ERR_INVALID_ARGUMENT, "dims: missing");
   const int64_t H = dims->nheads, P = dims->headdim, Ds = dims->d_state, G = dims->ngroups,
                 R = dims->mimo_rank, S = dims->num_rope_angles, di = dims->d_inner;
@@ -819,6 +819,8 @@ int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const 
   M3_TRY(check(C_bias, "C_bias", 3, hrd, kF32, true, false, false));
   M3_TRY(check(B_norm_w, "B_norm_w", 1, d1, kF32, true, false, false));
   M3_TRY(check(C_norm_w, "C_norm_w", 1, d1, kF32, true, false, false));
+  const int64_t a0s[3] = {Bn, H, S};
+  M3_TRY(check(angle0, "angle0", 3, a0s, kF32, true, true, false));
   if (empty) return M3_OK;
   if (Bn > INT32_MAX || L > INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "prologue: dimension too large");
   PrologueParams p{};
@@ -830,6 +832,7 @@ int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const 
   p.B_norm_w = fptr<const float>(B_norm_w); p.C_norm_w = fptr<const float>(C_norm_w);
   p.Bp = B_proj->data; p.Cp = C_proj->data;
   p.ADT = fptr<float>(ADT); p.DT = fptr<float>(DT); p.trap = fptr<float>(trap); p.angles = fptr<float>(angles);
+  p.angle0 = S > 0 ? fptr<const float>(angle0) : nullptr;
   return launch_prologue(p, zxbcdt->dtype, B_proj->dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 

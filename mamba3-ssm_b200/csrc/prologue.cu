@@ -4,7 +4,8 @@
 //
 //   angle kernel (one CTA per (b, h), thread = step, block scans over tiles of 128 steps):
 //     DT = softplus(dd_dt + dt_bias), A = -min(softplus(dd_A), -A_floor) (layer.py:207),
-//     ADT = A DT, trap logit copied to fp32, angles[b,l,h,i] = sum_{l'<=l} angle_raw[b,l',i] DT
+//     ADT = A DT, trap logit copied to fp32, angles[b,l,h,i] = angle0[b,h,i] (the decode
+//     cache's angle state, zero when absent) + sum_{l'<=l} angle_raw[b,l',i] DT
 //   bc kernel (one warp per output row (b, l, B|C, r, h)): RMSNorm over d_state of the
 //     row's group (ops.py:94-102), the head's bias, and the rotation of the pairs
 //     (2i, 2i+1), i < rope_split / 2, by angles[b,l,h,i]
@@ -39,7 +40,7 @@ __global__ void __launch_bounds__(kAT) prologue_angle_kernel(PrologueParams a) {
   const float dtb = a.dt_bias[h];
   const TZ* base = reinterpret_cast<const TZ*>(a.zx) + (int64_t)b * a.s_zb;
   const bool vec = (S % 4) == 0 && (reinterpret_cast<uintptr_t>(a.angles) & 15) == 0;
-  for (int s0 = tid; s0 < S; s0 += kAT) carry[s0] = 0.f;
+  for (int s0 = tid; s0 < S; s0 += kAT) carry[s0] = a.angle0 ? a.angle0[(int64_t)u * S + s0] : 0.f;
   __syncthreads();
   for (int l0 = 0; l0 < a.L; l0 += kAT) {
     const int l = l0 + tid;

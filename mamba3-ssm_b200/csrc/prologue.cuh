@@ -18,6 +18,7 @@ struct PrologueParams {
   void* Bp; void* Cp;                       // (Bn, L, R, H, D) contiguous, operand dtype
   float* ADT; float* DT; float* trap;       // (Bn, L, H) contiguous
   float* angles;                            // (Bn, L, H, S) contiguous
+  const float* angle0;                      // (Bn, H, S) contiguous or null: angles before step 0
 };
 
 struct GateParams {

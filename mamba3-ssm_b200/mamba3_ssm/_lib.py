@@ -74,7 +74,7 @@ _SIGS = {
     "m3_mimo_step": ([ctypes.c_void_p] + [_P] * 16 + [ctypes.c_void_p], ctypes.c_int),
     "m3_rmsnorm": ([_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_void_p], ctypes.c_int),
     "m3_device_timeouts": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
-    "m3_layer_prologue": ([ctypes.c_void_p] + [_P] * 12 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_layer_prologue": ([ctypes.c_void_p] + [_P] * 13 + [ctypes.c_void_p], ctypes.c_int),
     "m3_silu_gate": ([_P] * 3 + [ctypes.c_void_p], ctypes.c_int),
     "m3_argmax_rows": ([_P, _P, ctypes.c_void_p], ctypes.c_int),
 }

@@ -80,6 +80,23 @@ class MambaLMHeadModel(nn.Module):
     def allocate_inference_cache(self, batch_size: int) -> List[Tuple[torch.Tensor, ...]]:
         return [blk.mixer.allocate_inference_cache(batch_size) for blk in self.layers]
 
+    def prefill(self, input_ids: torch.Tensor, cache=None):
+        """Run a whole prompt (B, L) through the chunked scans and return (logits (B, L, V),
+        cache), the decode cache after the last token (a list of (angle, ssm, bx_prev) per
+        layer, as allocate_inference_cache lays it out), ready for step(). Continues from
+        ``cache`` when given (chunked prefill of a long prompt). Not in the reference, whose
+        generate loop prefills one step() per prompt token; the result is that of stepping
+        through the prompt."""
+        x = self.embedding(input_ids)
+        new_cache = []
+        for i, block in enumerate(self.layers):
+            out, c = block.mixer(block.norm(x), cache=None if cache is None else cache[i], return_cache=True)
+            x = x + out
+            new_cache.append(c)
+            if self.mlp_layers is not None:
+                x = x + self.mlp_layers[i](self.mlp_norms[i](x))
+        return self.lm_head(self.norm_f(x)), new_cache
+
     def _norms_after(self, i):
         """The norm that follows layer i's mixer residual add: the MLP norm of layer i,
         the next block's norm, or norm_f."""
@@ -122,9 +139,9 @@ class DecodeGraph:
     ``tokens`` are static buffers overwritten by every call.
 
         g = model.decode_graph(batch)          # captures on the current device
-        g.reset()                              # zero cache
-        for t in prompt.T: g.feed(t)           # prefill token by token, like step()
+        g.prefill(prompt)                      # whole prompt through the chunked scans
         for _ in range(n): tok = g.next()      # greedy: the argmax becomes the next input
+    (``g.reset()`` then ``g.feed(t)`` per prompt token also works, like step().)
     """
 
     def __init__(self, model: "MambaLMHeadModel", batch_size: int, greedy: bool = True):
@@ -168,6 +185,20 @@ class DecodeGraph:
             a.zero_()
             s.zero_()
             b.zero_()
+
+    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+        """Replace the cache by that of the prompt (B, L), computed by MambaLMHeadModel.prefill
+        (chunked scans, not one replay per token), and return the last position's logits
+        (B, V); with ``greedy`` the next input token is their argmax."""
+        with torch.no_grad():
+            logits, cache = self.model.prefill(prompt.reshape(self.tokens.shape[0], -1))
+            for dst, src in zip(self.cache, cache):
+                for d, s_ in zip(dst, src):
+                    d.copy_(s_)
+            last = logits[:, -1]
+            if self.greedy:
+                argmax_rows(last, out=self.tokens)
+        return last
 
     def feed(self, tokens: torch.Tensor) -> torch.Tensor:
         """One step on the given tokens (B,) or (B, 1); returns the static logits."""

@@ -18,7 +18,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib as L
-from .ops import RMSNorm, apply_rope, ssm_scan_mimo, ssm_scan_siso
+from .ops import (RMSNorm, _bc_dtype, _inner, _MimoScanFn, apply_rope, ssm_scan_mimo, ssm_scan_siso,
+                  ssm_scan_siso_states)
 
 
 class _StepNoGrad(torch.autograd.Function):
@@ -103,12 +104,23 @@ class Mamba3(nn.Module):
         n = n.expand(*n.shape[:-2], self.nheads, self.d_state)
         return n + bias.transpose(0, 1)  # (H,R,D) -> (R,H,D)
 
-    def forward(self, u: torch.Tensor) -> torch.Tensor:
-        if not (torch.is_grad_enabled() and (u.requires_grad or any(p.requires_grad for p in self.parameters()))):
-            return self._forward_fused(u)
-        return self._forward_autograd(u)
+    def forward(self, u: torch.Tensor, cache=None, return_cache: bool = False):
+        """Mamba3.forward of the reference (layer.py:168-266) for ``forward(u)``.
 
-    def _forward_fused(self, u: torch.Tensor) -> torch.Tensor:
+        Not in the reference (whose generate prefills one step() per prompt token): with
+        ``cache`` (an (angle, ssm, bx_prev) triple as allocate_inference_cache returns) the
+        sequence continues from that decode state, and with ``return_cache`` the call returns
+        ``(out, cache)``, the cache after the last token, from the chunked scan. Feeding a
+        prompt through forward(..., return_cache=True) then decoding with step() reproduces
+        stepping through the prompt token by token."""
+        want = return_cache or cache is not None
+        if not (torch.is_grad_enabled() and (u.requires_grad or any(p.requires_grad for p in self.parameters()))):
+            out, new = self._forward_fused(u, cache, want)
+        else:
+            out, new = self._forward_autograd(u, cache, want)
+        return (out, new) if return_cache else out
+
+    def _forward_fused(self, u: torch.Tensor, cache=None, want_cache: bool = False):
         """Inference forward: in_proj, the fused prologue kernel (m3_layer_prologue: dt /
         decay / trap, RMSNorm + bias + RoPE of B and C per head, the angle cumsum), the scan,
         the fused silu gate (m3_silu_gate), out_proj. bf16 layers give the scan bf16 B / C
@@ -128,26 +140,50 @@ class Mamba3(nn.Module):
         Cp = torch.empty(batch, Ln, R, H, Ds, dtype=op, device=dev)
         ADT, DT, trap = (torch.empty(batch, Ln, H, dtype=torch.float32, device=dev) for _ in range(3))
         ang = torch.empty(batch, Ln, H, S, dtype=torch.float32, device=dev)
+        ang0 = cache[0].float().contiguous() if cache is not None else None
         lib = L.load()
-        a = L.pack(zx, *vals[:5], Bp, Cp, ADT, DT, trap, ang)
+        a = L.pack(zx, *vals[:5], ang0, Bp, Cp, ADT, DT, trap, ang)
         with torch.cuda.device(dev):
             rc = lib.m3_layer_prologue(ctypes.byref(dims), *a.ptrs, torch.cuda.current_stream(dev).cuda_stream)
         L.check(rc, "m3_layer_prologue")
         di = self.d_inner
         z = zx[..., :di].unflatten(-1, (H, P))
         x = zx[..., di:2 * di].unflatten(-1, (H, P))
-        if self.is_mimo:
-            y = ssm_scan_mimo(x, Bp, Cp, ADT, DT, trap, self.D, self.mimo_x, self.mimo_o)
-        else:
-            y = ssm_scan_siso(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, self.D)
+        y, new = self._scan(x, Bp, Cp, ADT, DT, trap, ang, cache, want_cache)
         g = torch.empty(batch, Ln, H, P, dtype=zx.dtype, device=dev)
         a = L.pack(y, z, g)
         with torch.cuda.device(dev):
             rc = lib.m3_silu_gate(*a.ptrs, torch.cuda.current_stream(dev).cuda_stream)
         L.check(rc, "m3_silu_gate")
-        return self.out_proj(g.flatten(-2))
+        return self.out_proj(g.flatten(-2)), new
 
-    def _forward_autograd(self, u: torch.Tensor) -> torch.Tensor:
+    def _scan(self, x, Bp, Cp, ADT, DT, trap, ang, cache, want_cache):
+        """The scan of forward; with ``want_cache`` it starts from ``cache`` (or zeros) and
+        also returns the cache after the last token (angle state = the last angles)."""
+        if not want_cache:
+            if self.is_mimo:
+                return ssm_scan_mimo(x, Bp, Cp, ADT, DT, trap, self.D, self.mimo_x, self.mimo_o), None
+            return ssm_scan_siso(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, self.D), None
+        h0 = b0 = None
+        if cache is not None:
+            h0 = cache[1].float().contiguous()
+            b0 = cache[2].float().contiguous()
+        if self.is_mimo:
+            B_, C_ = _bc_dtype(x, Bp, Cp)
+            y, hl, bl = _MimoScanFn.apply(_inner(x), _inner(B_), _inner(C_), ADT.float(), DT.float(), trap.float(),
+                                          self.D.float(), _inner(self.mimo_x.float()), _inner(self.mimo_o.float()),
+                                          h0, b0, True)
+        else:
+            y, hl, bl = ssm_scan_siso_states(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, self.D, h0, b0)
+        if ang.shape[1] > 0:
+            a_last = ang[:, -1].float().contiguous()
+        elif cache is not None:
+            a_last = cache[0].float().clone()
+        else:
+            a_last = torch.zeros(x.shape[0], self.nheads, self.num_rope_angles, device=x.device)
+        return y, (a_last, hl, bl)
+
+    def _forward_autograd(self, u: torch.Tensor, cache=None, want_cache: bool = False):
         """Training forward: the reference's PyTorch prologue (differentiated by autograd)
         around the scan kernels."""
         batch, Ln, _ = u.shape
@@ -162,17 +198,16 @@ class Mamba3(nn.Module):
         ADT = A * DT
         Bh = self._bc(B_raw, self.B_norm, self.B_bias)
         Ch = self._bc(C_raw, self.C_norm, self.C_bias)
-        ang = torch.cumsum(angle_raw.float().unsqueeze(2) * DT.unsqueeze(-1), dim=1)  # (B,L,H,S)
-        ang = ang.unsqueeze(2).expand(batch, Ln, R, H, self.num_rope_angles)
+        ang_h = torch.cumsum(angle_raw.float().unsqueeze(2) * DT.unsqueeze(-1), dim=1)  # (B,L,H,S)
+        if cache is not None:
+            ang_h = ang_h + cache[0].float().unsqueeze(1)
+        ang = ang_h.unsqueeze(2).expand(batch, Ln, R, H, self.num_rope_angles)
         k = self.split_tensor_size
         B_proj = torch.cat([apply_rope(Bh[..., :k], ang), Bh[..., k:]], dim=-1)
         C_proj = torch.cat([apply_rope(Ch[..., :k], ang), Ch[..., k:]], dim=-1)
-        if self.is_mimo:
-            y = ssm_scan_mimo(x, B_proj, C_proj, ADT, DT, trap_raw.float(), self.D, self.mimo_x, self.mimo_o)
-        else:
-            y = ssm_scan_siso(x, B_proj[:, :, 0], C_proj[:, :, 0], ADT, DT, trap_raw.float(), self.D)
+        y, new = self._scan(x, B_proj, C_proj, ADT, DT, trap_raw.float(), ang_h, cache, want_cache)
         y = y * F.silu(z.float())
-        return self.out_proj(y.flatten(-2).to(x.dtype))
+        return self.out_proj(y.flatten(-2).to(x.dtype)), new
 
     # ------------------------------------------------------------------------------
     def _dims(self):

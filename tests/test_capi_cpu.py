@@ -41,8 +41,10 @@ def test_workspace_size_queries(lib):
     # CUDA-core backward: one float per position
     assert lib.m3_siso_scan_bwd_workspace_size(2, 100, 3, 32, 64) == 4 * 2 * 100 * 3
     # headdim 64 / d_state 128 may take the chunked path: room for the chunk states
-    # (bf16 128 x 64 per 128-step chunk, rounded to 256 bytes) and three floats per position
-    assert lib.m3_siso_scan_bwd_workspace_size(2, 100, 3, 64, 128) == 2 * 3 * 1 * 128 * 64 * 2 + 12 * 2 * 100 * 3
+    # (bf16 128 x 64 per 128-step chunk, rounded to 256 bytes), three floats per position
+    # and four per (unit, chunk) (the chunk-boundary dot products of dADT)
+    assert lib.m3_siso_scan_bwd_workspace_size(2, 100, 3, 64, 128) == (2 * 3 * 1 * 128 * 64 * 2 + 12 * 2 * 100 * 3
+                                                                        + 16 * 2 * 3 * 1)
     bf = _lib.M3_BFLOAT16
     assert lib.m3_siso_scan_kstates_size(2, 300, 3, 64, 128, bf, bf) == 2 * 3 * 3 * 128 * 64 * 2
     assert lib.m3_siso_scan_kstates_size(2, 300, 3, 64, 128, _lib.M3_FLOAT32, bf) == 0
@@ -50,7 +52,7 @@ def test_workspace_size_queries(lib):
     assert lib.m3_siso_scan_kstates_size(2, 300, 3, 64, 64, bf, bf) == 2 * 3 * 3 * 128 * 64 * 2
     assert lib.m3_siso_scan_kstates_size(2, 300, 3, 64, 32, bf, bf) == 0
     assert lib.m3_siso_scan_kstates_size(2, 0, 3, 64, 128, bf, bf) == 0
-    assert lib.m3_siso_scan_bwd_kstates_workspace_size(2, 300, 3) == 12 * 2 * 300 * 3
+    assert lib.m3_siso_scan_bwd_kstates_workspace_size(2, 300, 3) == 12 * 2 * 300 * 3 + 16 * 2 * 3 * 3
     assert lib.m3_mimo_scan_bwd_workspace_size(2, 100, 3, 32, 64, 4) > 0
 
 
