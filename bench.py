@@ -510,6 +510,109 @@ def measure_lm_forward(dev, steps=5):
             "what": "MambaLMHeadModel.forward, SISO preset d_model 1024 x 16 layers, bf16, 32 x 512 tokens"}
 
 
+def measure_lm_dp(dev, world, rank, pg, steps=4, dec_steps=32):
+    """The two LM workloads data-parallel over the job's ranks: each rank holds a full
+    weight replica (same seed) and its share of the batch; no collective runs inside a
+    timed region, which is bracketed by barriers and taken as the max over ranks.
+      c3_lm_forward   MambaLMHeadModel.forward, SISO preset (d_model 1024, 16 layers, vocab
+                      50000), bf16, global batch 32 x 512 tokens;
+      c4_decode       greedy decode of the MIMO preset (d_model 1536, 20 layers, R=4, vocab
+                      50000), bf16, global batch 256, one whole step replayed as a CUDA
+                      graph after a 16-token prefill;
+      c4_step_kernel  the fused decode-step kernel alone (20 layers at the rank's batch
+                      share, caches cycled), the state-bound part of the decode step.
+    Full-LM decode carries the replicated weights (761 MB per step on every GPU), so it
+    cannot scale like the state-bound step kernel; both are reported."""
+    from mamba3_ssm import MambaConfig, MambaLMHeadModel
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = ev(), ev()
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        (ms,) = max_over_ranks([e0.elapsed_time(e1) / n], pg, dev)
+        return ms
+
+    out = {}
+    _, b3 = shard(32, world, rank)
+    torch.manual_seed(0)
+    cfg3 = MambaConfig(d_model=1024, n_layer=16, vocab_size=50000, ssm_cfg=dict(d_state=64, expand=2, headdim=64))
+    m3 = MambaLMHeadModel(cfg3, device=dev, dtype=torch.bfloat16).eval()
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321 + rank)
+    ids = torch.randint(0, 50000, (b3, 512), device=dev, generator=g)
+    with torch.no_grad():
+        for _ in range(2):
+            m3(ids)
+        ms3 = timed(lambda: m3(ids), steps)
+    out["c3_lm_forward"] = {"value": 32 * 512 / (ms3 / 1e3), "unit": "tokens/s", "ms_per_step": ms3,
+                            "batch_per_rank": b3, "global_batch": 32, "seq_len": 512, "steps": steps}
+    del m3, ids
+    torch.cuda.empty_cache()
+
+    _, b4 = shard(256, world, rank)
+    torch.manual_seed(0)
+    cfg4 = MambaConfig(d_model=1536, n_layer=20, vocab_size=50000,
+                       ssm_cfg=dict(d_state=64, expand=2, headdim=64, is_mimo=True, mimo_rank=4))
+    m4 = MambaLMHeadModel(cfg4, device=dev, dtype=torch.bfloat16).eval()
+    prompt = torch.randint(0, 50000, (b4, 16), device=dev, generator=g)
+    with torch.no_grad():
+        dg = m4.decode_graph(b4, greedy=True)
+        for t in range(16):
+            dg.feed(prompt[:, t])
+        for _ in range(3):
+            dg.next()
+        ms4 = timed(dg.next, dec_steps)
+        del dg
+        mixers = [blk.mixer for blk in m4.layers]
+        u = torch.randn(b4, cfg4.d_model, device=dev, dtype=torch.bfloat16, generator=g)
+        zs = [mx.in_proj(u).contiguous() for mx in mixers]
+        caches = [mx.allocate_inference_cache(b4) for mx in mixers]
+        ys = [torch.empty(b4, mx.d_inner, device=dev, dtype=torch.bfloat16) for mx in mixers]
+
+        def sweep():
+            for mx, z, c, y in zip(mixers, zs, caches, ys):
+                mx._fused_step(z, *c, *c, y)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                sweep()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()  # replayed, so the host-side binding cost is not timed
+        with torch.cuda.graph(graph):
+            sweep()
+        graph.replay()
+        us_k = timed(graph.replay, 10) * 1e3 / len(mixers)
+        del graph
+    kbytes = (2 * _state_bytes(mixers[0], b4) + zs[0].numel() * zs[0].element_size()
+              + ys[0].numel() * ys[0].element_size())
+    peak = peaks()[0]
+    out["c4_decode"] = {"value": 256 / (ms4 / 1e3), "unit": "tokens/s", "ms_per_step": ms4, "batch_per_rank": b4,
+                        "global_batch": 256, "steps": dec_steps,
+                        "what": "whole greedy decode step (CUDA graph): embedding, 20 layers, norm_f, lm_head, argmax"}
+    out["c4_step_kernel"] = {"value": 256 / (len(mixers) * us_k * 1e-6), "unit": "tokens/s", "us_per_launch": us_k,
+                             "batch_per_rank": b4, "bytes_per_launch": kbytes,
+                             "achieved_gbs_per_gpu": kbytes / (us_k * 1e-6) / 1e9,
+                             "frac_hbm_per_gpu": kbytes / (us_k * 1e-6) / 1e9 / peak,
+                             "what": "fused decode-step kernel only (m3_mimo_step), 20 layers per token step replayed "
+                                     "from a CUDA graph; value = tokens/s of the job if a decode step were these 20 "
+                                     "launches"}
+    del m4, zs, caches, ys, u
+    torch.cuda.empty_cache()
+    return out
+
+
 # ----------------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
@@ -522,6 +625,7 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the forward+backward and decode figures")
     ap.add_argument("--no-check", action="store_true", help="skip the host check of the timed output")
     ap.add_argument("--no-sustained", action="store_true", help="skip the ~2 s sustained run")
+    ap.add_argument("--no-lm", action="store_true", help="skip the data-parallel LM forward / decode figures")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the global batch (profiling runs on a smaller case)")
     ap.add_argument("--fwd-bwd-only", action="store_true",
@@ -718,9 +822,14 @@ def main():
         del hosts, y_host
 
     extra = {}
+    if not args.no_extra and not args.no_lm:
+        del y
+        extra["lm_dp"] = measure_lm_dp(dev, world, rank, pg)
+        y = None
     if world == 1 and not args.no_extra:
         extra["fwd_bwd"] = measure_fwd_bwd((x, Bm, Cm, ADT, DT, trap, Dw))
-        del x, Bm, Cm, ADT, DT, trap, Dw, y
+        del x, Bm, Cm, ADT, DT, trap, Dw
+        y = None
         torch.cuda.empty_cache()
         extra["decode"] = measure_decode(dev)
         extra["mimo"] = measure_mimo(dev)

@@ -623,14 +623,12 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_pair_kernel(StepPara
 template <typename TZ, int DP, int PP, int RM>
 __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_row_kernel(StepParams a) {
   constexpr int D = 64 * DP, P = 64 * PP;
-  __shared__ float s_nrm[2 * 8];
-  __shared__ float s_sc[kWarpRows][5];  // DT, decay, w1, w2, D skip
   const int R = a.R, H = a.H, S = a.S;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.y;
-  const int h0 = blockIdx.x * kWarpRows, h = h0 + warp;
-  const bool hv = h < H;
-  const int hh = hv ? h : h0;
+  const int h = blockIdx.x * kWarpRows + warp;
+  if (h >= H) return;
+  const int hh = h;
   const TZ* row = reinterpret_cast<const TZ*>(a.zxbcdt) + (int64_t)b * a.s_row;
   const int off_B = 2 * a.d_inner, off_C = off_B + D * R, off_dt = off_C + D * R;
   const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
@@ -664,43 +662,28 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_row_kernel(StepParam
     ang_in[q] = i < S ? a.angle_in[abase + i] : 0.f;
     ang_raw[q] = i < S ? to_f32(row[off_ang + i]) : 0.f;
   }
-  if (warp == 0) {
-    // shared by the CTA's heads: the row's norm factors and, lanes 0-7, the heads' scalars
-    float ss[2 * RM];
+  // the row's norm factors, formed by every warp from the B / C rows it holds (no barrier:
+  // the CTA's warps never wait on one another)
+  float nrm[2 * RM];
 #pragma unroll
-    for (int r = 0; r < RM; ++r) {
-      float sb = 0.f, sc = 0.f;
+  for (int r = 0; r < RM; ++r) {
+    float sb = 0.f, sc = 0.f;
 #pragma unroll
-      for (int q = 0; q < DP; ++q) {
-        sb = fmaf(Bv[r][q].x, Bv[r][q].x, fmaf(Bv[r][q].y, Bv[r][q].y, sb));
-        sc = fmaf(Cv[r][q].x, Cv[r][q].x, fmaf(Cv[r][q].y, Cv[r][q].y, sc));
-      }
-      ss[r] = sb;
-      ss[RM + r] = sc;
+    for (int q = 0; q < DP; ++q) {
+      sb = fmaf(Bv[r][q].x, Bv[r][q].x, fmaf(Bv[r][q].y, Bv[r][q].y, sb));
+      sc = fmaf(Cv[r][q].x, Cv[r][q].x, fmaf(Cv[r][q].y, Cv[r][q].y, sc));
     }
-    warp_sum_n<2 * RM>(ss, lane);
-    if (lane < 2 * RM) {
-      float v = ss[0];
-#pragma unroll
-      for (int k = 1; k < 2 * RM; ++k) v = lane == k ? ss[k] : v;
-      s_nrm[lane < RM ? lane : 8 + lane - RM] = rsqrtf(v * (1.0f / D) + a.eps);
-    }
-    const int hl = h0 + lane;
-    if (lane < kWarpRows && hl < H) {
-      const float DT = softplusf_(to_f32(row[off_dt + hl]) + __ldg(a.dt_bias + hl));
-      const float A = -fminf(softplusf_(to_f32(row[off_A + hl])), -a.A_floor);  // layer.py:317
-      const float tr = fast_sigmoid(to_f32(row[off_tr + hl]));
-      s_sc[lane][0] = DT;
-      s_sc[lane][1] = expf(A * DT);
-      s_sc[lane][2] = 1.0f - 0.5f * tr;
-      s_sc[lane][3] = 0.5f * tr;
-      s_sc[lane][4] = __ldg(a.Dskip + hl);
-    }
+    nrm[r] = sb;
+    nrm[RM + r] = sc;
   }
-  __syncthreads();
-  if (!hv) return;
-  const float DT = s_sc[warp][0], decay = s_sc[warp][1], w1 = s_sc[warp][2], w2 = s_sc[warp][3],
-              Dk = s_sc[warp][4];
+  warp_sum_n<2 * RM>(nrm, lane);
+#pragma unroll
+  for (int k = 0; k < 2 * RM; ++k) nrm[k] = rsqrtf(nrm[k] * (1.0f / D) + a.eps);
+  // this head's scalars (every lane, from broadcast loads)
+  const float DT = softplusf_(to_f32(row[off_dt + hh]) + __ldg(a.dt_bias + hh));
+  const float A = -fminf(softplusf_(to_f32(row[off_A + hh])), -a.A_floor);  // layer.py:317
+  const float tr = fast_sigmoid(to_f32(row[off_tr + hh]));
+  const float decay = expf(A * DT), w1 = 1.0f - 0.5f * tr, w2 = 0.5f * tr, Dk = __ldg(a.Dskip + hh);
   // angle update (layer.py:331-332); angle_out may alias angle_in: same lane, read above
   float sn[DP], cs[DP];
 #pragma unroll
@@ -720,7 +703,7 @@ __global__ void __launch_bounds__(32 * kWarpRows) mimo_step_row_kernel(StepParam
 #pragma unroll
     for (int r = 0; r < RM; ++r) {
       if (r >= R) break;
-      const float nb = s_nrm[r], nc = s_nrm[8 + r];
+      const float nb = nrm[r], nc = nrm[RM + r];
       const float2 bb = ldg2(Bb + r * D + d0), cb = ldg2(Cb + r * D + d0);
       Bv[r][q] = make_float2(fmaf(Bv[r][q].x * nb, wb.x, bb.x), fmaf(Bv[r][q].y * nb, wb.y, bb.y));
       Cv[r][q] = make_float2(fmaf(Cv[r][q].x * nc, wc.x, cb.x), fmaf(Cv[r][q].y * nc, wc.y, cb.y));
