@@ -608,6 +608,31 @@ def measure_lm_dp(dev, world, rank, pg, steps=4, dec_steps=32):
                              "what": "fused decode-step kernel only (m3_mimo_step), 20 layers per token step replayed "
                                      "from a CUDA graph; value = tokens/s of the job if a decode step were these 20 "
                                      "launches"}
+    # weak scaling of the same kernel: the full batch of 256 on every rank
+    with torch.no_grad():
+        if world > 1:
+            uw = torch.randn(256, cfg4.d_model, device=dev, dtype=torch.bfloat16, generator=g)
+            zw = [mx.in_proj(uw).contiguous() for mx in mixers]
+            cw = [mx.allocate_inference_cache(256) for mx in mixers]
+            yw = [torch.empty(256, mx.d_inner, device=dev, dtype=torch.bfloat16) for mx in mixers]
+
+            def sweep_w():
+                for mx, z, c, y in zip(mixers, zw, cw, yw):
+                    mx._fused_step(z, *c, *c, y)
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    sweep_w()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            gw = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gw):
+                sweep_w()
+            gw.replay()
+            us_w = timed(gw.replay, 10) * 1e3 / len(mixers)
+            del gw, zw, cw, yw, uw
+            out["c4_step_kernel_weak"] = {"value": 256 * world / (len(mixers) * us_w * 1e-6), "unit": "tokens/s",
+                                          "us_per_launch": us_w, "batch_per_rank": 256, "global_batch": 256 * world,
+                                          "scaling": "weak",
+                                          "what": "the same kernel with the full batch of 256 on every rank"}
     del m4, zs, caches, ys, u
     torch.cuda.empty_cache()
     return out
@@ -632,6 +657,8 @@ def main():
                     help="only the ssm_scan_siso forward + backward figure (profiling the backward)")
     ap.add_argument("--decode-only", action="store_true",
                     help="only the decode figure (profiling the decode step)")
+    ap.add_argument("--mimo-only", action="store_true",
+                    help="only the MIMO op / layer figures (profiling the MIMO kernels)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -658,6 +685,11 @@ def main():
         r = measure_decode(dev)
         if rank == 0:
             print(json.dumps({"decode": r, "timeouts": _lib.device_timeouts(reset=True)}))
+        return
+    if args.mimo_only:
+        r = measure_mimo(dev)
+        if rank == 0:
+            print(json.dumps({"mimo": r, "timeouts": _lib.device_timeouts(reset=True)}))
         return
 
     if args.batch:

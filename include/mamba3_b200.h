@@ -293,6 +293,32 @@ int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const 
 int m3_silu_gate(const m3_tensor* y, const m3_tensor* z, m3_tensor* out, void* stream);
 
 /* ---------------------------------------------------------------------------------
+ * Backward of the prologue and of the gate, for training (the gradients autograd returns
+ * through layer.py:198-266; the reference differentiates its PyTorch prologue).
+ * m3_layer_prologue_bwd: from the forward's in_proj output zxbcdt, DT and angles (as
+ *   m3_layer_prologue wrote them) and the scan's gradients dB_proj / dC_proj (batch,
+ *   seqlen, R, H, D, the scan operand dtype), dADT, dDT, dtrap (batch, seqlen, H) f32,
+ *   writes the B, C, dt, A (zeros: the clamp of layer.py:207 passes no gradient), trap and
+ *   angle columns of d_zxbcdt (zxbcdt's shape and dtype; the z and x columns are left to
+ *   m3_silu_gate_bwd and the scan backward) and overwrites the parameter gradients
+ *   d_dt_bias (H), d_B_bias / d_C_bias (H, R, D), d_B_norm_w / d_C_norm_w (D), all f32.
+ *   workspace: m3_layer_prologue_bwd_workspace_size bytes, 16-byte aligned.
+ * m3_silu_gate_bwd: dy = dout * silu(z), dz = dout * y * silu'(z), all (B, L, H, P) views of
+ *   one dtype with innermost stride 1.
+ * ------------------------------------------------------------------------------- */
+size_t m3_layer_prologue_bwd_workspace_size(const m3_layer_dims* dims, int64_t batch, int64_t seqlen);
+int m3_layer_prologue_bwd(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
+                          const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                          const m3_tensor* C_norm_w, const m3_tensor* DT, const m3_tensor* angles,
+                          const m3_tensor* dB_proj, const m3_tensor* dC_proj, const m3_tensor* dADT,
+                          const m3_tensor* dDT, const m3_tensor* dtrap, m3_tensor* d_zxbcdt,
+                          m3_tensor* d_dt_bias, m3_tensor* d_B_bias, m3_tensor* d_C_bias,
+                          m3_tensor* d_B_norm_w, m3_tensor* d_C_norm_w, void* workspace,
+                          size_t workspace_bytes, void* stream);
+int m3_silu_gate_bwd(const m3_tensor* y, const m3_tensor* z, const m3_tensor* dout, m3_tensor* dy,
+                     m3_tensor* dz, void* stream);
+
+/* ---------------------------------------------------------------------------------
  * Health word of the warp-specialised kernels on the current device: *flag_out is
  * nonzero once any bounded inter-warp wait gave up (the kernel then drained and its
  * outputs are invalid); reset != 0 clears it. Synchronises the device. No reference

@@ -836,6 +836,103 @@ int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const 
   return launch_prologue(p, zxbcdt->dtype, B_proj->dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
+size_t m3_layer_prologue_bwd_workspace_size(const m3_layer_dims* dims, int64_t batch, int64_t seqlen) {
+  if (!dims || batch < 0 || seqlen < 0) return 0;
+  return prologue_bwd_workspace_bytes(batch, seqlen, dims->nheads, dims->num_rope_angles);
+}
+
+int m3_layer_prologue_bwd(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
+                          const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                          const m3_tensor* C_norm_w, const m3_tensor* DT, const m3_tensor* angles,
+                          const m3_tensor* dB_proj, const m3_tensor* dC_proj, const m3_tensor* dADT,
+                          const m3_tensor* dDT, const m3_tensor* dtrap, m3_tensor* d_zxbcdt, m3_tensor* d_dt_bias,
+                          m3_tensor* d_B_bias, m3_tensor* d_C_bias, m3_tensor* d_B_norm_w, m3_tensor* d_C_norm_w,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dims) return fail(M3_ERR_INVALID_ARGUMENT, "dims: missing");
+  const int64_t H = dims->nheads, P = dims->headdim, Ds = dims->d_state, G = dims->ngroups,
+                R = dims->mimo_rank, S = dims->num_rope_angles, di = dims->d_inner;
+  if (H <= 0 || P <= 0 || Ds <= 0 || G <= 0 || R <= 0 || S < 0 || di != H * P || dims->rope_split != 2 * S ||
+      dims->rope_split > Ds || (G != 1 && G != H))
+    return fail(M3_ERR_INVALID_ARGUMENT, "dims: inconsistent layer dimensions");
+  if (!present(zxbcdt) || zxbcdt->ndim != 3) return fail(M3_ERR_INVALID_ARGUMENT, "zxbcdt: expected (batch, seqlen, d_in_proj)");
+  const int64_t Bn = zxbcdt->shape[0], L = zxbcdt->shape[1];
+  const int64_t dproj = 2 * di + 2 * Ds * G * R + 3 * H + S;
+  const bool empty = Bn * L == 0;
+  const int64_t zs[3] = {Bn, L, dproj}, bs[5] = {Bn, L, R, H, Ds}, ss[3] = {Bn, L, H}, as[4] = {Bn, L, H, S},
+                h1[1] = {H}, hrd[3] = {H, R, Ds}, d1[1] = {Ds};
+  M3_TRY(check(zxbcdt, "zxbcdt", 3, zs, kAnyFloat, false, false, !empty));
+  M3_TRY(check(d_zxbcdt, "d_zxbcdt", 3, zs, 1u << zxbcdt->dtype, false, false, !empty));
+  M3_TRY(check(dB_proj, "dB_proj", 5, bs, kAnyFloat, true, false, !empty));
+  M3_TRY(check(dC_proj, "dC_proj", 5, bs, 1u << dB_proj->dtype, true, false, !empty));
+  M3_TRY(check(DT, "DT", 3, ss, kF32, true, false, false));
+  M3_TRY(check(dADT, "dADT", 3, ss, kF32, true, false, false));
+  M3_TRY(check(dDT, "dDT", 3, ss, kF32, true, false, false));
+  M3_TRY(check(dtrap, "dtrap", 3, ss, kF32, true, false, false));
+  M3_TRY(check(angles, "angles", 4, as, kF32, true, S == 0, false));
+  M3_TRY(check(dt_bias, "dt_bias", 1, h1, kF32, true, false, false));
+  M3_TRY(check(B_bias, "B_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(C_bias, "C_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(B_norm_w, "B_norm_w", 1, d1, kF32, true, false, false));
+  M3_TRY(check(C_norm_w, "C_norm_w", 1, d1, kF32, true, false, false));
+  M3_TRY(check(d_dt_bias, "d_dt_bias", 1, h1, kF32, true, false, false));
+  M3_TRY(check(d_B_bias, "d_B_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(d_C_bias, "d_C_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(d_B_norm_w, "d_B_norm_w", 1, d1, kF32, true, false, false));
+  M3_TRY(check(d_C_norm_w, "d_C_norm_w", 1, d1, kF32, true, false, false));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (empty) {
+    // no positions: every parameter gradient is zero
+    M3_TRY(memset_async(d_dt_bias->data, sizeof(float) * H, s, "d_dt_bias"));
+    M3_TRY(memset_async(d_B_bias->data, sizeof(float) * H * R * Ds, s, "d_B_bias"));
+    M3_TRY(memset_async(d_C_bias->data, sizeof(float) * H * R * Ds, s, "d_C_bias"));
+    M3_TRY(memset_async(d_B_norm_w->data, sizeof(float) * Ds, s, "d_B_norm_w"));
+    return memset_async(d_C_norm_w->data, sizeof(float) * Ds, s, "d_C_norm_w");
+  }
+  if (Bn > INT32_MAX || L > INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "prologue backward: dimension too large");
+  const size_t need = prologue_bwd_workspace_bytes(Bn, L, H, S);
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15) != 0)
+    return fail(M3_ERR_WORKSPACE, "prologue backward: workspace of " + std::to_string(need) + " bytes required");
+  PrologueBwdParams p{};
+  p.Bn = (int)Bn; p.L = (int)L; p.H = (int)H; p.P = (int)P; p.D = (int)Ds; p.R = (int)R; p.G = (int)G;
+  p.S = (int)S; p.split = dims->rope_split; p.d_inner = (int)di; p.A_floor = dims->A_floor; p.eps = dims->norm_eps;
+  p.zx = zxbcdt->data; p.s_zb = zxbcdt->stride[0]; p.s_zl = zxbcdt->stride[1];
+  p.dzx = d_zxbcdt->data; p.s_dzb = d_zxbcdt->stride[0]; p.s_dzl = d_zxbcdt->stride[1];
+  p.dt_bias = fptr<const float>(dt_bias);
+  p.B_bias = fptr<const float>(B_bias); p.C_bias = fptr<const float>(C_bias);
+  p.B_norm_w = fptr<const float>(B_norm_w); p.C_norm_w = fptr<const float>(C_norm_w);
+  p.angles = fptr<const float>(angles); p.DT = fptr<const float>(DT);
+  p.dBp = dB_proj->data; p.dCp = dC_proj->data;
+  p.dADT = fptr<const float>(dADT); p.dDT = fptr<const float>(dDT); p.dtrap = fptr<const float>(dtrap);
+  p.dB_bias = fptr<float>(d_B_bias); p.dC_bias = fptr<float>(d_C_bias);
+  p.dB_norm_w = fptr<float>(d_B_norm_w); p.dC_norm_w = fptr<float>(d_C_norm_w);
+  p.ddt_bias = fptr<float>(d_dt_bias);
+  return launch_prologue_bwd(p, reinterpret_cast<float*>(workspace), zxbcdt->dtype, dB_proj->dtype, s);
+}
+
+int m3_silu_gate_bwd(const m3_tensor* y, const m3_tensor* z, const m3_tensor* dout, m3_tensor* dy, m3_tensor* dz,
+                     void* stream) {
+  if (!present(y) || y->ndim != 4) return fail(M3_ERR_INVALID_ARGUMENT, "y: expected (B, L, H, P)");
+  const int64_t* sh = y->shape;
+  const bool empty = sh[0] * sh[1] * sh[2] * sh[3] == 0;
+  M3_TRY(check(y, "y", 4, sh, kAnyFloat, false, false, !empty));
+  M3_TRY(check(z, "z", 4, sh, 1u << y->dtype, false, false, !empty));
+  M3_TRY(check(dout, "dout", 4, sh, 1u << y->dtype, false, false, !empty));
+  M3_TRY(check(dy, "dy", 4, sh, 1u << y->dtype, false, false, !empty));
+  M3_TRY(check(dz, "dz", 4, sh, 1u << y->dtype, false, false, !empty));
+  if (empty) return M3_OK;
+  if (sh[1] > INT32_MAX || sh[2] > INT32_MAX || sh[3] > INT32_MAX)
+    return fail(M3_ERR_UNSUPPORTED, "gate backward: dimension too large");
+  GateBwdParams p{};
+  p.rows = sh[0] * sh[1] * sh[2];
+  p.L = (int)sh[1]; p.H = (int)sh[2]; p.P = (int)sh[3];
+  p.y = y->data; p.sy = s3(y);
+  p.z = z->data; p.sz = s3(z);
+  p.dout = dout->data; p.sd = s3(dout);
+  p.dy = dy->data; p.sdy = s3(dy);
+  p.dz = dz->data; p.sdz = s3(dz);
+  return launch_gate_bwd(p, y->dtype, z->dtype, dout->dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int m3_silu_gate(const m3_tensor* y, const m3_tensor* z, m3_tensor* out, void* stream) {
   if (!present(y) || y->ndim != 4) return fail(M3_ERR_INVALID_ARGUMENT, "y: expected (B, L, H, P)");
   const int64_t* sh = y->shape;

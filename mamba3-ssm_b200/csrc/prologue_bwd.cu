@@ -1,0 +1,406 @@
+// Backward of the fused prologue and of the silu gate of Mamba3.forward (the training path;
+// mamba3_ssm/layer.py:180-266): the gradients autograd returns through the reference's
+// prologue, given the scan's gradients.
+//
+//   bc kernel (CTA per tile of kRowsBC (b, l) rows, warp r = rank r, heads in a loop):
+//     recompute the group row n = raw / rms * w and, per head, v = n + bias_h and the rotated
+//     o = rot_theta(v) on the pairs i < S (theta = the forward's angles[b,l,h,i]); then
+//       dv        = rot_theta^T(dB_proj)             the gradient before the rotation
+//       dtheta_i += -dv1' o2 + dv2' o1               over B and C (dv' = dB_proj), ranks summed in
+//                                                    shared memory, one write per (b, l, h, i)
+//       dbias    += dv                               summed over the tile in shared memory,
+//                                                    then atomics per CTA
+//       dn        = sum_h dv (one group) / dv (group per head)
+//       draw      = (w dn) / rms - raw sum_d(w dn raw) / (D rms^3)   into d zxbcdt
+//       dw       += dn raw / rms                     registers, then atomics per CTA
+//   angle kernel (CTA per (b, h), tiles of 128 steps from the end): q = suffix sums over l
+//     of dtheta; dDT_ang[b,l,h] = sum_i q angle_raw[b,l,i]; dangle_raw[b,l,i] += q DT[b,l,h]
+//     (atomics over heads into an fp32 buffer)
+//   dt kernel (thread per (b, l, h)): dDT_total = dDT + A dADT + dDT_ang, with A the clamped
+//     constant of layer.py:207 (so dd_A gets no gradient); dpre = dDT_total softplus'(dd_dt +
+//     dt_bias) into d zxbcdt (dt column), the trap logit's gradient into its column, and the
+//     dt_bias gradient (block sums, then atomics); the angle_raw columns from the fp32 buffer
+//   gate kernel: dy = dout silu(z), dz = dout y silu'(z)
+#include "m3_common.cuh"
+#include "prologue.cuh"
+
+namespace m3 {
+namespace {
+
+constexpr int kRowsBC = 16;  // (b, l) rows per CTA of the bc kernel
+constexpr int kAT = 128;     // steps per tile of the angle kernel
+
+template <typename T>
+__device__ __forceinline__ float2 ld_pair(const T* p) {
+  return make_float2(to_f32(p[0]), to_f32(p[1]));
+}
+template <>
+__device__ __forceinline__ float2 ld_pair<float>(const float* p) {
+  return *reinterpret_cast<const float2*>(p);
+}
+template <>
+__device__ __forceinline__ float2 ld_pair<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+template <typename T>
+__device__ __forceinline__ void st_pair2(T* p, float a, float b) {
+  p[0] = from_f32<T>(a);
+  p[1] = from_f32<T>(b);
+}
+
+// Shared memory of the bc kernel: the bias gradients of the tile (H, R, D) for B and C and
+// one row's angle gradients (H, S).
+template <typename TZ, typename TO, int PPL>
+__global__ void __launch_bounds__(256) prologue_bwd_bc_kernel(PrologueBwdParams a) {
+  extern __shared__ float sm[];
+  const int R = a.R, G = a.G, D = a.D, H = a.H, S = a.S;
+  const int half = D / 2, npair = a.split / 2;
+  const int lane = threadIdx.x & 31, r = threadIdx.x >> 5;
+  const int HRD = H * R * D;
+  float* sbB = sm;                 // (H, R, D)
+  float* sbC = sm + HRD;           // (H, R, D)
+  float* sang = sm + 2 * HRD;      // (H, S) of the current row
+  float* swb = sang + H * S;       // (R, D) dw partials of B
+  float* swc = swb + R * D;        // (R, D) of C
+  for (int i = threadIdx.x; i < 2 * HRD + H * S; i += blockDim.x) sm[i] = 0.f;
+  __syncthreads();
+  const int64_t nrows = (int64_t)a.Bn * a.L;
+  const int64_t RGD = (int64_t)R * G * D;
+  float wb0[PPL], wb1[PPL], wc0[PPL], wc1[PPL];
+  float dwb0[PPL], dwb1[PPL], dwc0[PPL], dwc1[PPL];
+#pragma unroll
+  for (int j = 0; j < PPL; ++j) {
+    const int k = min(lane + 32 * j, half - 1);
+    wb0[j] = a.B_norm_w[2 * k]; wb1[j] = a.B_norm_w[2 * k + 1];
+    wc0[j] = a.C_norm_w[2 * k]; wc1[j] = a.C_norm_w[2 * k + 1];
+    dwb0[j] = dwb1[j] = dwc0[j] = dwc1[j] = 0.f;
+  }
+  for (int t = 0; t < kRowsBC; ++t) {
+    const int64_t rowo = (int64_t)blockIdx.x * kRowsBC + t;  // b * L + l
+    const bool rv = rowo < nrows;                              // uniform over the CTA
+    if (rv) {
+      const int64_t b = rowo / a.L, l = rowo - b * a.L;
+      const TZ* zrow = reinterpret_cast<const TZ*>(a.zx) + b * a.s_zb + l * a.s_zl + 2 * a.d_inner;
+      TZ* drow = reinterpret_cast<TZ*>(a.dzx) + b * a.s_dzb + l * a.s_dzl + 2 * a.d_inner;
+      float rb0[PPL], rb1[PPL], rc0[PPL], rc1[PPL];  // raw group rows
+      float rsb = 0.f, rsc = 0.f;                    // 1 / rms
+      float db0[PPL], db1[PPL], dc0[PPL], dc1[PPL];  // dn (sum over the group's heads)
+      for (int h = 0; h < H; ++h) {
+        const int g = G == 1 ? 0 : h;
+        if (h == 0 || G != 1) {
+          const TZ* sb = zrow + (int64_t)(r * G + g) * D;
+          const TZ* sc = sb + RGD;
+          float ssb = 0.f, ssc = 0.f;
+#pragma unroll
+          for (int j = 0; j < PPL; ++j) {
+            const int k = lane + 32 * j;
+            const bool v = k < half;
+            rb0[j] = v ? to_f32(sb[2 * k]) : 0.f; rb1[j] = v ? to_f32(sb[2 * k + 1]) : 0.f;
+            rc0[j] = v ? to_f32(sc[2 * k]) : 0.f; rc1[j] = v ? to_f32(sc[2 * k + 1]) : 0.f;
+            ssb = fmaf(rb0[j], rb0[j], fmaf(rb1[j], rb1[j], ssb));
+            ssc = fmaf(rc0[j], rc0[j], fmaf(rc1[j], rc1[j], ssc));
+            db0[j] = db1[j] = dc0[j] = dc1[j] = 0.f;
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            ssb += __shfl_xor_sync(0xffffffffu, ssb, o);
+            ssc += __shfl_xor_sync(0xffffffffu, ssc, o);
+          }
+          rsb = 1.0f / sqrtf(ssb / (float)D + a.eps);
+          rsc = 1.0f / sqrtf(ssc / (float)D + a.eps);
+        }
+        const float* bb = a.B_bias + ((int64_t)h * R + r) * D;
+        const float* cb = a.C_bias + ((int64_t)h * R + r) * D;
+        const float* ang = a.angles + (rowo * H + h) * S;
+        const TO* gB = reinterpret_cast<const TO*>(a.dBp) + ((rowo * R + r) * H + h) * D;
+        const TO* gC = reinterpret_cast<const TO*>(a.dCp) + ((rowo * R + r) * H + h) * D;
+        float* sbBh = sbB + ((int64_t)h * R + r) * D;
+        float* sbCh = sbC + ((int64_t)h * R + r) * D;
+#pragma unroll
+        for (int j = 0; j < PPL; ++j) {
+          const int k = lane + 32 * j;
+          if (k < half) {
+            const int d0 = 2 * k;
+            float2 gb = ld_pair(gB + d0), gc = ld_pair(gC + d0);
+            if (k < npair) {
+              // o = rot(v) with v = n + bias; dtheta = -g1 o2 + g2 o1; dv = rot^T(g)
+              const float2 bv = __ldg(reinterpret_cast<const float2*>(bb + d0));
+              const float2 cv = __ldg(reinterpret_cast<const float2*>(cb + d0));
+              const float x0 = rb0[j] * rsb * wb0[j] + bv.x, x1 = rb1[j] * rsb * wb1[j] + bv.y;
+              const float y0 = rc0[j] * rsc * wc0[j] + cv.x, y1 = rc1[j] * rsc * wc1[j] + cv.y;
+              float sn, cs;
+              sincos_reduced(ang[k], &sn, &cs);
+              const float ob0 = x0 * cs - x1 * sn, ob1 = x0 * sn + x1 * cs;
+              const float oc0 = y0 * cs - y1 * sn, oc1 = y0 * sn + y1 * cs;
+              const float dth = (-gb.x * ob1 + gb.y * ob0) + (-gc.x * oc1 + gc.y * oc0);
+              atomicAdd(&sang[h * S + k], dth);  // ranks of the row add up
+              gb = make_float2(gb.x * cs + gb.y * sn, -gb.x * sn + gb.y * cs);
+              gc = make_float2(gc.x * cs + gc.y * sn, -gc.x * sn + gc.y * cs);
+            }
+            sbBh[d0] += gb.x; sbBh[d0 + 1] += gb.y;  // warp r owns (h, r, :)
+            sbCh[d0] += gc.x; sbCh[d0 + 1] += gc.y;
+            db0[j] += gb.x; db1[j] += gb.y;
+            dc0[j] += gc.x; dc1[j] += gc.y;
+          }
+        }
+        if (h == H - 1 || G != 1) {
+          // RMSNorm backward of group (r, g): draw = (w dn)/rms - raw sum(w dn raw)/(D rms^3)
+          float pb = 0.f, pc = 0.f;
+#pragma unroll
+          for (int j = 0; j < PPL; ++j) {
+            pb = fmaf(wb0[j] * db0[j], rb0[j], fmaf(wb1[j] * db1[j], rb1[j], pb));
+            pc = fmaf(wc0[j] * dc0[j], rc0[j], fmaf(wc1[j] * dc1[j], rc1[j], pc));
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            pb += __shfl_xor_sync(0xffffffffu, pb, o);
+            pc += __shfl_xor_sync(0xffffffffu, pc, o);
+          }
+          const float kb = pb * rsb * rsb * rsb / (float)D, kc = pc * rsc * rsc * rsc / (float)D;
+          TZ* ob = drow + (int64_t)(r * G + g) * D;
+          TZ* oc = ob + RGD;
+#pragma unroll
+          for (int j = 0; j < PPL; ++j) {
+            const int k = lane + 32 * j;
+            if (k < half) {
+              st_pair2(ob + 2 * k, wb0[j] * db0[j] * rsb - rb0[j] * kb, wb1[j] * db1[j] * rsb - rb1[j] * kb);
+              st_pair2(oc + 2 * k, wc0[j] * dc0[j] * rsc - rc0[j] * kc, wc1[j] * dc1[j] * rsc - rc1[j] * kc);
+              dwb0[j] = fmaf(db0[j], rb0[j] * rsb, dwb0[j]); dwb1[j] = fmaf(db1[j], rb1[j] * rsb, dwb1[j]);
+              dwc0[j] = fmaf(dc0[j], rc0[j] * rsc, dwc0[j]); dwc1[j] = fmaf(dc1[j], rc1[j] * rsc, dwc1[j]);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();  // the row's angle gradients complete
+    if (rv) {
+      float* dst = a.dtheta + rowo * H * S;
+      for (int i = threadIdx.x; i < H * S; i += blockDim.x) {
+        dst[i] = sang[i];
+        sang[i] = 0.f;
+      }
+    }
+    __syncthreads();
+  }
+  // tile partials to global: bias gradients (H, R, D) and the norm-weight gradients (D)
+#pragma unroll
+  for (int j = 0; j < PPL; ++j) {
+    const int k = lane + 32 * j;
+    if (k < half) {
+      swb[r * D + 2 * k] = dwb0[j]; swb[r * D + 2 * k + 1] = dwb1[j];
+      swc[r * D + 2 * k] = dwc0[j]; swc[r * D + 2 * k + 1] = dwc1[j];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < HRD; i += blockDim.x) {
+    atomicAdd(a.dB_bias + i, sbB[i]);
+    atomicAdd(a.dC_bias + i, sbC[i]);
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float sb = 0.f, sc = 0.f;
+    for (int rr = 0; rr < R; ++rr) {
+      sb += swb[rr * D + d];
+      sc += swc[rr * D + d];
+    }
+    atomicAdd(a.dB_norm_w + d, sb);
+    atomicAdd(a.dC_norm_w + d, sc);
+  }
+}
+
+// CTA per (b, h); thread = step of a 128-step tile walked from the end; suffix sums over l
+// of dtheta[b,l,h,i] for the S angles, 16 at a time, carried between tiles
+template <typename TZ>
+__global__ void __launch_bounds__(kAT) prologue_bwd_angle_kernel(PrologueBwdParams a) {
+  constexpr int kS = 16;
+  __shared__ float wsum[kAT / 32][kS];
+  __shared__ float carry[64];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int u = blockIdx.x, b = u / a.H, h = u - b * a.H;
+  const int H = a.H, S = a.S;
+  const int off_ang = 2 * a.d_inner + 2 * a.D * a.G * a.R + 3 * H;
+  const TZ* base = reinterpret_cast<const TZ*>(a.zx) + (int64_t)b * a.s_zb;
+  for (int s0 = tid; s0 < S; s0 += kAT) carry[s0] = 0.f;
+  __syncthreads();
+  const int ntile = (a.L + kAT - 1) / kAT;
+  for (int tt = ntile - 1; tt >= 0; --tt) {
+    const int l = tt * kAT + tid;
+    const bool v = l < a.L;
+    const int64_t o = ((int64_t)b * a.L + (v ? l : 0)) * H + h;
+    const TZ* row = base + (int64_t)(v ? l : 0) * a.s_zl;
+    const float dtv = v ? a.DT[o] : 0.f;
+    float ddt = 0.f;
+    for (int s0 = 0; s0 < S; s0 += kS) {
+      float x[kS];
+#pragma unroll
+      for (int k = 0; k < kS; ++k) x[k] = (v && s0 + k < S) ? a.dtheta[o * S + s0 + k] : 0.f;
+#pragma unroll
+      for (int of = 1; of < 32; of <<= 1) {
+#pragma unroll
+        for (int k = 0; k < kS; ++k) {
+          const float y = __shfl_down_sync(0xffffffffu, x[k], of);
+          if (lane + of < 32) x[k] += y;
+        }
+      }
+      if (lane == 0)
+#pragma unroll
+        for (int k = 0; k < kS; ++k) wsum[warp][k] = x[k];
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < kS; ++k) {
+        float post = s0 + k < S ? carry[s0 + k] : 0.f;
+        for (int w = warp + 1; w < kAT / 32; ++w) post += wsum[w][k];
+        x[k] += post;
+      }
+      if (v) {
+#pragma unroll
+        for (int k = 0; k < kS; ++k) {
+          if (s0 + k < S) {
+            ddt = fmaf(x[k], to_f32(row[off_ang + s0 + k]), ddt);
+            atomicAdd(a.dangle_raw + ((int64_t)b * a.L + l) * S + s0 + k, x[k] * dtv);
+          }
+        }
+      }
+      __syncthreads();  // carry and wsum read by every thread before they change
+      if (tid == 0)
+#pragma unroll
+        for (int k = 0; k < kS; ++k)
+          if (s0 + k < S) carry[s0 + k] = x[k];
+    }
+    if (v) a.dDT_ang[o] = ddt;
+    __syncthreads();
+  }
+}
+
+// thread per (b, l, h)
+template <typename TZ>
+__global__ void __launch_bounds__(256) prologue_bwd_dt_kernel(PrologueBwdParams a) {
+  __shared__ float sdb[256];
+  const int64_t n = (int64_t)a.Bn * a.L * a.H;
+  const int H = a.H, S = a.S;
+  const int off_dt = 2 * a.d_inner + 2 * a.D * a.G * a.R;
+  const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float dpre = 0.f;
+  int h = 0;
+  if (i < n) {
+    const int64_t bl = i / H;
+    h = (int)(i - bl * H);
+    const int64_t b = bl / a.L, l = bl - b * a.L;
+    const TZ* row = reinterpret_cast<const TZ*>(a.zx) + b * a.s_zb + l * a.s_zl;
+    TZ* drow = reinterpret_cast<TZ*>(a.dzx) + b * a.s_dzb + l * a.s_dzl;
+    const float A = -fminf(softplusf_(to_f32(row[off_A + h])), -a.A_floor);
+    const float pre = to_f32(row[off_dt + h]) + a.dt_bias[h];
+    const float dDT = a.dDT[i] + A * a.dADT[i] + a.dDT_ang[i];
+    dpre = dDT * (pre > 20.0f ? 1.0f : sigmoidf_(pre));
+    drow[off_dt + h] = from_f32<TZ>(dpre);
+    drow[off_A + h] = from_f32<TZ>(0.f);  // the clamp of layer.py:207 passes no gradient
+    drow[off_tr + h] = from_f32<TZ>(a.dtrap[i]);
+    if (h == 0)
+      for (int k = 0; k < S; ++k) drow[off_ang + k] = from_f32<TZ>(a.dangle_raw[bl * S + k]);
+  }
+  // dt_bias: the block's sums per head (thread t of the block holds head (start + t) mod H),
+  // then one atomic per head and block
+  sdb[threadIdx.x] = dpre;
+  __syncthreads();
+  const int64_t start = (int64_t)blockIdx.x * blockDim.x;
+  const int s0 = (int)(start % H);
+  for (int hh = threadIdx.x; hh < H; hh += blockDim.x) {
+    float sum = 0.f;
+    for (int t = (hh - s0 + H) % H; t < (int)blockDim.x; t += H)
+      if (start + t < n) sum += sdb[t];
+    atomicAdd(a.ddt_bias + hh, sum);
+  }
+  (void)h;
+}
+
+template <typename TY, typename TZ, typename TD>
+__global__ void __launch_bounds__(256) gate_bwd_kernel(GateBwdParams a) {
+  const int64_t n = a.rows * a.P;
+  const int LH = a.L * a.H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / a.P;
+    const int p = (int)(i - r * a.P);
+    const int64_t b = r / LH;
+    const int rem = (int)(r - b * LH);
+    const int l = rem / a.H, h = rem - l * a.H;
+    const float yv = to_f32(reinterpret_cast<const TY*>(a.y)[b * a.sy.b + (int64_t)l * a.sy.l + (int64_t)h * a.sy.h + p]);
+    const float zv = to_f32(reinterpret_cast<const TZ*>(a.z)[b * a.sz.b + (int64_t)l * a.sz.l + (int64_t)h * a.sz.h + p]);
+    const float g = to_f32(reinterpret_cast<const TD*>(a.dout)[b * a.sd.b + (int64_t)l * a.sd.l + (int64_t)h * a.sd.h + p]);
+    const float sg = sigmoidf_(zv);
+    reinterpret_cast<TY*>(a.dy)[b * a.sdy.b + (int64_t)l * a.sdy.l + (int64_t)h * a.sdy.h + p] =
+        from_f32<TY>(g * zv * sg);
+    reinterpret_cast<TZ*>(a.dz)[b * a.sdz.b + (int64_t)l * a.sdz.l + (int64_t)h * a.sdz.h + p] =
+        from_f32<TZ>(g * yv * sg * (1.0f + zv * (1.0f - sg)));
+  }
+}
+
+}  // namespace
+
+size_t prologue_bwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t S) {
+  // dtheta (B, L, H, S), dDT_ang (B, L, H), dangle_raw (B, L, S), all fp32
+  return sizeof(float) * (size_t)(Bn * L * (H * S + H + S));
+}
+
+int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt, cudaStream_t s) {
+  PrologueBwdParams p = p0;
+  if (p.S > 64) return fail(M3_ERR_UNSUPPORTED, "prologue backward: more than 64 rope angles");
+  if (p.D % 2 || p.D > 256 || p.R > 8) return fail(M3_ERR_UNSUPPORTED, "prologue backward: d_state or rank");
+  if ((reinterpret_cast<uintptr_t>(p.B_bias) | reinterpret_cast<uintptr_t>(p.C_bias)) & 7)
+    return fail(M3_ERR_UNSUPPORTED, "prologue backward: B_bias / C_bias must be 8-byte aligned");
+  const int64_t rows = (int64_t)p.Bn * p.L;
+  p.dtheta = ws;
+  p.dDT_ang = ws + rows * p.H * p.S;
+  p.dangle_raw = p.dDT_ang + rows * p.H;
+  const size_t zero_bytes = sizeof(float) * (size_t)(rows * p.S);
+  cudaError_t e = cudaMemsetAsync(p.dangle_raw, 0, zero_bytes, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.dB_bias, 0, sizeof(float) * (size_t)p.H * p.R * p.D, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.dC_bias, 0, sizeof(float) * (size_t)p.H * p.R * p.D, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.dB_norm_w, 0, sizeof(float) * (size_t)p.D, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.dC_norm_w, 0, sizeof(float) * (size_t)p.D, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.ddt_bias, 0, sizeof(float) * (size_t)p.H, s);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("prologue backward memset: ") + cudaGetErrorString(e));
+  const size_t smem = sizeof(float) * (size_t)(2 * p.H * p.R * p.D + p.H * p.S + 2 * p.R * p.D);
+  if (smem > 200 * 1024) return fail(M3_ERR_UNSUPPORTED, "prologue backward: nheads * rank * d_state too large");
+  const unsigned gbc = (unsigned)((rows + kRowsBC - 1) / kRowsBC);
+  const int ppl = (p.D / 2 + 31) / 32;
+  const unsigned gdt = (unsigned)((rows * p.H + 255) / 256);
+#define M3_PBWD(TZ, TO)                                                                                  \
+  do {                                                                                                   \
+    auto kbc = ppl == 1 ? prologue_bwd_bc_kernel<TZ, TO, 1>                                              \
+                        : (ppl == 2 ? prologue_bwd_bc_kernel<TZ, TO, 2> : prologue_bwd_bc_kernel<TZ, TO, 4>); \
+    if (smem > 48 * 1024) {                                                                              \
+      cudaError_t ea = cudaFuncSetAttribute(kbc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+      if (ea != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ea)); \
+    }                                                                                                    \
+    kbc<<<gbc, 32 * p.R, smem, s>>>(p);                                                                  \
+    M3_TRY(check_launch("prologue_bwd_bc_kernel"));                                                      \
+    prologue_bwd_angle_kernel<TZ><<<(unsigned)(p.Bn * p.H), kAT, 0, s>>>(p);                             \
+    M3_TRY(check_launch("prologue_bwd_angle_kernel"));                                                   \
+    prologue_bwd_dt_kernel<TZ><<<gdt, 256, 0, s>>>(p);                                                   \
+    return check_launch("prologue_bwd_dt_kernel");                                                       \
+  } while (0)
+  if (zdt == M3_BFLOAT16 && odt == M3_BFLOAT16) M3_PBWD(__nv_bfloat16, __nv_bfloat16);
+  if (zdt == M3_BFLOAT16 && odt == M3_FLOAT32) M3_PBWD(__nv_bfloat16, float);
+  if (zdt == M3_FLOAT32 && odt == M3_FLOAT32) M3_PBWD(float, float);
+  if (zdt == M3_FLOAT16 && odt == M3_FLOAT32) M3_PBWD(__half, float);
+#undef M3_PBWD
+  return fail(M3_ERR_UNSUPPORTED, "prologue backward: unsupported dtype pair");
+}
+
+int launch_gate_bwd(const GateBwdParams& p, int ydt, int zdt, int ddt, cudaStream_t s) {
+  const int64_t n = p.rows * p.P;
+  if (n == 0) return M3_OK;
+  const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16);
+#define M3_GB(TY, TZ, TD)                                \
+  do {                                                   \
+    gate_bwd_kernel<TY, TZ, TD><<<grid, 256, 0, s>>>(p); \
+    return check_launch("gate_bwd_kernel");              \
+  } while (0)
+  if (ydt == M3_BFLOAT16 && zdt == M3_BFLOAT16 && ddt == M3_BFLOAT16) M3_GB(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
+  if (ydt == M3_FLOAT32 && zdt == M3_FLOAT32 && ddt == M3_FLOAT32) M3_GB(float, float, float);
+  if (ydt == M3_FLOAT16 && zdt == M3_FLOAT16 && ddt == M3_FLOAT16) M3_GB(__half, __half, __half);
+#undef M3_GB
+  return fail(M3_ERR_UNSUPPORTED, "gate backward: unsupported dtype combination");
+}
+
+}  // namespace m3

@@ -76,6 +76,10 @@ _SIGS = {
     "m3_device_timeouts": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "m3_layer_prologue": ([ctypes.c_void_p] + [_P] * 13 + [ctypes.c_void_p], ctypes.c_int),
     "m3_silu_gate": ([_P] * 3 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_layer_prologue_bwd_workspace_size": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64], ctypes.c_size_t),
+    "m3_layer_prologue_bwd": ([ctypes.c_void_p] + [_P] * 19 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p],
+                              ctypes.c_int),
+    "m3_silu_gate_bwd": ([_P] * 5 + [ctypes.c_void_p], ctypes.c_int),
     "m3_argmax_rows": ([_P, _P, ctypes.c_void_p], ctypes.c_int),
 }
 

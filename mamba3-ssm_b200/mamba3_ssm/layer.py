@@ -18,8 +18,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib as L
-from .ops import (RMSNorm, _bc_dtype, _inner, _MimoScanFn, apply_rope, ssm_scan_mimo, ssm_scan_siso,
-                  ssm_scan_siso_states)
+from .ops import (RMSNorm, _bc_dtype, _inner, _mimo_bwd_raw, _mimo_fwd_raw, _MimoScanFn, _siso_bwd_raw,
+                  _siso_fwd_raw, apply_rope, ssm_scan_mimo, ssm_scan_siso, ssm_scan_siso_states)
 
 
 class _StepNoGrad(torch.autograd.Function):
@@ -34,6 +34,95 @@ class _StepNoGrad(torch.autograd.Function):
     def backward(ctx, *grads):
         raise RuntimeError("Mamba3.step is inference-only in the B200 build: its fused kernel has no "
                            "backward. Differentiate through Mamba3.forward instead.")
+
+
+def _f32(t):
+    return None if t is None else t.detach().float().contiguous()
+
+
+class _LayerCoreFn(torch.autograd.Function):
+    """Everything Mamba3.forward does between in_proj and out_proj (layer.py:180-262), for
+    training, on the fused kernels. Forward: m3_layer_prologue (dt / decay / trap, RMSNorm +
+    bias + RoPE of B and C per head, the angle cumsum), the scan (the SISO tensor-core pair
+    keeps its chunk states), m3_silu_gate. Backward: m3_silu_gate_bwd, the scan backward
+    and m3_layer_prologue_bwd, which together fill the gradient of the in_proj output and
+    of every mixer parameter. Returns the gated output (B, L, H, P) in zx's dtype."""
+
+    @staticmethod
+    def forward(ctx, zx, dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, Dskip, mimo_x, mimo_o, layer):
+        lib = L.load()
+        batch, Ln, _ = zx.shape
+        R, Ds, H, P, S, di = (layer.mimo_rank, layer.d_state, layer.nheads, layer.headdim, layer.num_rope_angles,
+                              layer.d_inner)
+        dev = zx.device
+        dims = layer._dims()
+        pb = [_f32(t) for t in (dt_bias, B_bias, C_bias, B_norm_w, C_norm_w)]
+        op = torch.bfloat16 if zx.dtype == torch.bfloat16 else torch.float32
+        Bp = torch.empty(batch, Ln, R, H, Ds, dtype=op, device=dev)
+        Cp = torch.empty(batch, Ln, R, H, Ds, dtype=op, device=dev)
+        ADT, DT, trap = (torch.empty(batch, Ln, H, dtype=torch.float32, device=dev) for _ in range(3))
+        ang = torch.empty(batch, Ln, H, S, dtype=torch.float32, device=dev)
+        a = L.pack(zx, *pb, None, Bp, Cp, ADT, DT, trap, ang)
+        with torch.cuda.device(dev):
+            L.check(lib.m3_layer_prologue(ctypes.byref(dims), *a.ptrs, L.stream_of(zx)), "m3_layer_prologue")
+        z = zx[..., :di].unflatten(-1, (H, P))
+        x = zx[..., di:2 * di].unflatten(-1, (H, P))
+        Dv = _f32(Dskip)
+        ks = None
+        mx = mo = None
+        if layer.is_mimo:
+            mx, mo = _f32(mimo_x), _f32(mimo_o)
+            y, _, _ = _mimo_fwd_raw(x, Bp, Cp, ADT, DT, trap, Dv, mx, mo)
+        else:
+            y, _, _, ks = _siso_fwd_raw(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, Dv, keep_states=True)
+        g = torch.empty(batch, Ln, H, P, dtype=zx.dtype, device=dev)
+        a = L.pack(y, z, g)
+        with torch.cuda.device(dev):
+            L.check(lib.m3_silu_gate(*a.ptrs, L.stream_of(zx)), "m3_silu_gate")
+        ctx.save_for_backward(zx, Bp, Cp, ADT, DT, trap, ang, y, Dv, *pb, mx, mo)
+        ctx.ks = ks
+        ctx.layer = layer
+        ctx.dtypes = [None if t is None else t.dtype for t in (dt_bias, B_bias, C_bias, B_norm_w, C_norm_w, Dskip,
+                                                               mimo_x, mimo_o)]
+        return g
+
+    @staticmethod
+    def backward(ctx, dg):
+        zx, Bp, Cp, ADT, DT, trap, ang, y, Dv, dtb, Bb, Cb, Bw, Cw, mx, mo = ctx.saved_tensors
+        layer = ctx.layer
+        lib = L.load()
+        H, P, di = layer.nheads, layer.headdim, layer.d_inner
+        dev = zx.device
+        dzx = torch.empty_like(zx)
+        z = zx[..., :di].unflatten(-1, (H, P))
+        x = zx[..., di:2 * di].unflatten(-1, (H, P))
+        dg = _inner(dg.to(zx.dtype))
+        dy = torch.empty_like(y)
+        a = L.pack(y, z, dg, dy, dzx[..., :di].unflatten(-1, (H, P)))
+        with torch.cuda.device(dev):
+            L.check(lib.m3_silu_gate_bwd(*a.ptrs, L.stream_of(zx)), "m3_silu_gate_bwd")
+        dmx = dmo = None
+        if layer.is_mimo:
+            dx, dBp, dCp, dADT, dDT, dtrap, dD, dmx, dmo, _, _ = _mimo_bwd_raw(x, Bp, Cp, ADT, DT, trap, Dv, mx, mo,
+                                                                             None, None, dy)
+        else:
+            ks = ctx.ks
+            ctx.ks = None
+            dx, dB, dC, dADT, dDT, dtrap, dD, _, _ = _siso_bwd_raw(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, Dv,
+                                                                   None, None, ks, dy)
+            dBp, dCp = dB.unsqueeze(2), dC.unsqueeze(2)
+        dzx[..., di:2 * di].copy_(dx.flatten(-2))
+        grads = [torch.empty(t.shape, dtype=torch.float32, device=dev) for t in (dtb, Bb, Cb, Bw, Cw)]
+        dims = layer._dims()
+        nbytes = lib.m3_layer_prologue_bwd_workspace_size(ctypes.byref(dims), zx.shape[0], zx.shape[1])
+        ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
+        a = L.pack(zx, dtb, Bb, Cb, Bw, Cw, DT, ang, dBp, dCp, dADT, dDT, dtrap, dzx, *grads)
+        with torch.cuda.device(dev):
+            L.check(lib.m3_layer_prologue_bwd(ctypes.byref(dims), *a.ptrs, ws.data_ptr(), ws.numel(),
+                                              L.stream_of(zx)), "m3_layer_prologue_bwd")
+        out = grads + [dD, dmx, dmo]
+        out = [None if (gv is None or dt is None) else gv.to(dt) for gv, dt in zip(out, ctx.dtypes)]
+        return (dzx, *out, None)
 
 
 class Mamba3(nn.Module):
@@ -184,8 +273,20 @@ class Mamba3(nn.Module):
         return y, (a_last, hl, bl)
 
     def _forward_autograd(self, u: torch.Tensor, cache=None, want_cache: bool = False):
-        """Training forward: the reference's PyTorch prologue (differentiated by autograd)
-        around the scan kernels."""
+        """Training forward. Without a decode cache: in_proj, the fused prologue / scan / gate
+        with their backward kernels (_LayerCoreFn), out_proj. With one (continuing from, or
+        returning, decode states): the reference's PyTorch prologue, differentiated by
+        autograd, around the scan kernels."""
+        if cache is None and not want_cache:
+            zx = self.in_proj(u)
+            if not zx.is_cuda:
+                raise RuntimeError("Mamba3.forward: the B200 build runs on CUDA tensors only (no CPU path)")
+            if zx.stride(-1) != 1:
+                zx = zx.contiguous()
+            g = _LayerCoreFn.apply(zx, self.dt_bias, self.B_bias, self.C_bias, self.B_norm.weight, self.C_norm.weight,
+                                   self.D, self.mimo_x if self.is_mimo else None,
+                                   self.mimo_o if self.is_mimo else None, self)
+            return self.out_proj(g.flatten(-2)), None
         batch, Ln, _ = u.shape
         R, G, Ds, H, P = self.mimo_rank, self.num_bc_heads, self.d_state, self.nheads, self.headdim
         z, x, B_raw, C_raw, dd_dt, dd_A, trap_raw, angle_raw = torch.split(self.in_proj(u), self._splits, dim=-1)

@@ -118,35 +118,125 @@ def _empty(shape, dtype, dev):
     return torch.empty(tuple(shape), dtype=dtype, device=dev)
 
 
+def _siso_fwd_raw(x, B, C, ADT, DT, trap, D, h0=None, bx0=None, want_state=False, keep_states=False):
+    """SISO forward on the C ABI. Returns (y, h_last, bx_last, kstates): the final states
+    with ``want_state``; with ``keep_states`` and when the chunked kernels cover the shape,
+    the forward's bf16 chunk-start states for the tensor-core backward (else None)."""
+    lib = L.load()
+    Bn, Ln, H, P = x.shape
+    Ds = B.shape[-1]
+    y = _empty(x.shape, x.dtype, x.device)
+    hl = bl = None
+    if want_state:
+        hl = _empty((Bn, H, P, Ds), torch.float32, x.device)
+        bl = _empty((Bn, H, P, Ds), torch.float32, x.device)
+    a = L.pack(x, B, C, ADT, DT, trap, D, h0, bx0, y, hl, bl)
+    ks = None
+    if keep_states:
+        nb = lib.m3_siso_scan_kstates_size(Bn, Ln, H, P, Ds, L._DTYPE_CODE.get(x.dtype, -1),
+                                           L._DTYPE_CODE.get(B.dtype, -1))
+        if nb:
+            ks = torch.empty(int(nb), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        if ks is not None:
+            rc = lib.m3_siso_scan_fwd_kstates(*a.ptrs, ks.data_ptr(), ks.numel(), L.stream_of(x))
+            if rc == L.M3_ERR_UNSUPPORTED:
+                ks = None  # e.g. unaligned strided views: the plain forward below
+            else:
+                L.check(rc, "m3_siso_scan_fwd_kstates")
+        if ks is None:
+            L.check(lib.m3_siso_scan_fwd(*a.ptrs, L.stream_of(x)), "m3_siso_scan_fwd")
+    return y, hl, bl, ks
+
+
+def _siso_bwd_raw(x, B, C, ADT, DT, trap, D, h0, bx0, ks, dy, need_h0=False, need_bx0=False):
+    """SISO backward on the C ABI: the tensor-core pair when ``ks`` holds the forward's chunk
+    states, else m3_siso_scan_bwd. Returns dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0."""
+    lib = L.load()
+    Bn, Ln, H, P = x.shape
+    Ds = B.shape[-1]
+    dev = x.device
+    dy = _inner(dy.to(x.dtype))
+    dx = _empty(x.shape, x.dtype, dev)
+    dB = _empty(B.shape, B.dtype, dev)
+    dC = _empty(C.shape, C.dtype, dev)
+    dADT = _empty(ADT.shape, torch.float32, dev)
+    dDT = _empty(DT.shape, torch.float32, dev)
+    dtrap = _empty(trap.shape, torch.float32, dev)
+    dD = _empty((H,), torch.float32, dev)
+    dh0 = _empty(h0.shape, torch.float32, dev) if (h0 is not None and need_h0) else None
+    dbx0 = _empty(bx0.shape, torch.float32, dev) if (bx0 is not None and need_bx0) else None
+    a = L.pack(x, B, C, ADT, DT, trap, D, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0)
+    with torch.cuda.device(dev):
+        rc = None
+        if ks is not None:
+            nbytes = lib.m3_siso_scan_bwd_kstates_workspace_size(Bn, Ln, H)
+            ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
+            rc = lib.m3_siso_scan_bwd_kstates(*a.ptrs, ks.data_ptr(), ks.numel(), ws.data_ptr(), ws.numel(),
+                                              L.stream_of(x))
+            if rc != L.M3_ERR_UNSUPPORTED:  # e.g. an unaligned dy view: the general path
+                L.check(rc, "m3_siso_scan_bwd_kstates")
+            del ws
+        if ks is None or rc == L.M3_ERR_UNSUPPORTED:
+            nbytes = lib.m3_siso_scan_bwd_workspace_size(Bn, Ln, H, P, Ds)
+            ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
+            L.check(lib.m3_siso_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)), "m3_siso_scan_bwd")
+    return dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0
+
+
+def _mimo_fwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0=None, bx0=None, want_state=False):
+    """MIMO forward (chunk-parallel kernels) on the C ABI. Returns (y, h_last, bx_last)."""
+    lib = L.load()
+    Bn, Ln, H, P = x.shape
+    Ds = B.shape[-1]
+    y = _empty(x.shape, x.dtype, x.device)
+    hl = bl = None
+    if want_state:
+        hl = _empty((Bn, H, Ds), torch.float32, x.device)
+        bl = _empty((Bn, H, Ds), torch.float32, x.device)
+    a = L.pack(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, y, hl, bl)
+    nbytes = lib.m3_mimo_scan_fwd_workspace_size(Bn, Ln, H, Ds)
+    ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        L.check(lib.m3_mimo_scan_fwd_ws(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)), "m3_mimo_scan_fwd_ws")
+    return y, hl, bl
+
+
+def _mimo_bwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, need_h0=False, need_bx0=False):
+    """MIMO backward on the C ABI. Returns dx, dB, dC, dADT, dDT, dtrap, dD, dmimo_x,
+    dmimo_o, dh0, dbx0."""
+    lib = L.load()
+    Bn, Ln, H, P = x.shape
+    R, Ds = B.shape[2], B.shape[-1]
+    dev = x.device
+    dy = _inner(dy.to(x.dtype))
+    dx = _empty(x.shape, x.dtype, dev)
+    dB = _empty(B.shape, B.dtype, dev)
+    dC = _empty(C.shape, C.dtype, dev)
+    dADT = _empty(ADT.shape, torch.float32, dev)
+    dDT = _empty(DT.shape, torch.float32, dev)
+    dtrap = _empty(trap.shape, torch.float32, dev)
+    dD = _empty((H,), torch.float32, dev)
+    dmx = _empty((H, R, P), torch.float32, dev)
+    dmo = _empty((H, R, P), torch.float32, dev)
+    dh0 = _empty(h0.shape, torch.float32, dev) if (h0 is not None and need_h0) else None
+    dbx0 = _empty(bx0.shape, torch.float32, dev) if (bx0 is not None and need_bx0) else None
+    nbytes = lib.m3_mimo_scan_bwd_workspace_size(Bn, Ln, H, P, Ds, R)
+    ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
+    a = L.pack(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD, dmx, dmo,
+               dh0, dbx0)
+    with torch.cuda.device(dev):
+        L.check(lib.m3_mimo_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)), "m3_mimo_scan_bwd")
+    return dx, dB, dC, dADT, dDT, dtrap, dD, dmx, dmo, dh0, dbx0
+
+
 class _SisoScanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, B, C, ADT, DT, trap, D, h0, bx0, want_state):
-        lib = L.load()
-        Bn, Ln, H, P = x.shape
-        Ds = B.shape[-1]
-        y = _empty(x.shape, x.dtype, x.device)
-        hl = bl = None
-        if want_state:
-            hl = _empty((Bn, H, P, Ds), torch.float32, x.device)
-            bl = _empty((Bn, H, P, Ds), torch.float32, x.device)
-        a = L.pack(x, B, C, ADT, DT, trap, D, h0, bx0, y, hl, bl)
         # when gradients will be needed and the chunked kernels cover the shape, keep the
         # chunk-start states of the forward for the backward instead of recomputing them
-        ks = None
-        if any(ctx.needs_input_grad[:9]):
-            nb = lib.m3_siso_scan_kstates_size(Bn, Ln, H, P, Ds, L._DTYPE_CODE.get(x.dtype, -1),
-                                               L._DTYPE_CODE.get(B.dtype, -1))
-            if nb:
-                ks = torch.empty(int(nb), dtype=torch.uint8, device=x.device)
-        with torch.cuda.device(x.device):
-            if ks is not None:
-                rc = lib.m3_siso_scan_fwd_kstates(*a.ptrs, ks.data_ptr(), ks.numel(), L.stream_of(x))
-                if rc == L.M3_ERR_UNSUPPORTED:
-                    ks = None  # e.g. unaligned strided views: the plain forward below
-                else:
-                    L.check(rc, "m3_siso_scan_fwd_kstates")
-            if ks is None:
-                L.check(lib.m3_siso_scan_fwd(*a.ptrs, L.stream_of(x)), "m3_siso_scan_fwd")
+        y, hl, bl, ks = _siso_fwd_raw(x, B, C, ADT, DT, trap, D, h0, bx0, want_state,
+                                      keep_states=any(ctx.needs_input_grad[:9]))
         ctx.kstates = ks
         ctx.save_for_backward(x, B, C, ADT, DT, trap, D, h0, bx0)
         ctx.mark_non_differentiable(*[t for t in (hl, bl) if t is not None])
@@ -155,61 +245,19 @@ class _SisoScanFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy, _dh, _dbx):
         x, B, C, ADT, DT, trap, D, h0, bx0 = ctx.saved_tensors
-        lib = L.load()
-        Bn, Ln, H, P = x.shape
-        Ds = B.shape[-1]
-        dev = x.device
         if dy is None:
             dy = torch.zeros_like(x)
-        dy = _inner(dy.to(x.dtype))
-        dx = _empty(x.shape, x.dtype, dev)
-        dB = _empty(B.shape, B.dtype, dev)
-        dC = _empty(C.shape, C.dtype, dev)
-        dADT = _empty(ADT.shape, torch.float32, dev)
-        dDT = _empty(DT.shape, torch.float32, dev)
-        dtrap = _empty(trap.shape, torch.float32, dev)
-        dD = _empty((H,), torch.float32, dev)
-        dh0 = _empty(h0.shape, torch.float32, dev) if (h0 is not None and ctx.needs_input_grad[7]) else None
-        dbx0 = _empty(bx0.shape, torch.float32, dev) if (bx0 is not None and ctx.needs_input_grad[8]) else None
-        a = L.pack(x, B, C, ADT, DT, trap, D, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD,
-                    dh0, dbx0)
         ks = ctx.kstates
         ctx.kstates = None
-        with torch.cuda.device(dev):
-            rc = None
-            if ks is not None:
-                nbytes = lib.m3_siso_scan_bwd_kstates_workspace_size(Bn, Ln, H)
-                ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
-                rc = lib.m3_siso_scan_bwd_kstates(*a.ptrs, ks.data_ptr(), ks.numel(), ws.data_ptr(),
-                                                  ws.numel(), L.stream_of(x))
-                if rc != L.M3_ERR_UNSUPPORTED:  # e.g. an unaligned dy view: the general path
-                    L.check(rc, "m3_siso_scan_bwd_kstates")
-                del ws
-            if ks is None or rc == L.M3_ERR_UNSUPPORTED:
-                nbytes = lib.m3_siso_scan_bwd_workspace_size(Bn, Ln, H, P, Ds)
-                ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
-                L.check(lib.m3_siso_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)),
-                        "m3_siso_scan_bwd")
-        return dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0, None
+        g = _siso_bwd_raw(x, B, C, ADT, DT, trap, D, h0, bx0, ks, dy, ctx.needs_input_grad[7],
+                          ctx.needs_input_grad[8])
+        return (*g, None)
 
 
 class _MimoScanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, want_state):
-        lib = L.load()
-        Bn, Ln, H, P = x.shape
-        Ds = B.shape[-1]
-        y = _empty(x.shape, x.dtype, x.device)
-        hl = bl = None
-        if want_state:
-            hl = _empty((Bn, H, Ds), torch.float32, x.device)
-            bl = _empty((Bn, H, Ds), torch.float32, x.device)
-        a = L.pack(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, y, hl, bl)
-        nbytes = lib.m3_mimo_scan_fwd_workspace_size(Bn, Ln, H, Ds)
-        ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=x.device)
-        with torch.cuda.device(x.device):
-            L.check(lib.m3_mimo_scan_fwd_ws(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)),
-                    "m3_mimo_scan_fwd_ws")
+        y, hl, bl = _mimo_fwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, want_state)
         ctx.save_for_backward(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0)
         ctx.mark_non_differentiable(*[t for t in (hl, bl) if t is not None])
         return y, hl, bl
@@ -217,32 +265,11 @@ class _MimoScanFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy, _dh, _dbx):
         x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0 = ctx.saved_tensors
-        lib = L.load()
-        Bn, Ln, H, P = x.shape
-        R, Ds = B.shape[2], B.shape[-1]
-        dev = x.device
         if dy is None:
             dy = torch.zeros_like(x)
-        dy = _inner(dy.to(x.dtype))
-        dx = _empty(x.shape, x.dtype, dev)
-        dB = _empty(B.shape, B.dtype, dev)
-        dC = _empty(C.shape, C.dtype, dev)
-        dADT = _empty(ADT.shape, torch.float32, dev)
-        dDT = _empty(DT.shape, torch.float32, dev)
-        dtrap = _empty(trap.shape, torch.float32, dev)
-        dD = _empty((H,), torch.float32, dev)
-        dmx = _empty((H, R, P), torch.float32, dev)
-        dmo = _empty((H, R, P), torch.float32, dev)
-        dh0 = _empty(h0.shape, torch.float32, dev) if (h0 is not None and ctx.needs_input_grad[9]) else None
-        dbx0 = _empty(bx0.shape, torch.float32, dev) if (bx0 is not None and ctx.needs_input_grad[10]) else None
-        nbytes = lib.m3_mimo_scan_bwd_workspace_size(Bn, Ln, H, P, Ds, R)
-        ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
-        a = L.pack(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap,
-                    dD, dmx, dmo, dh0, dbx0)
-        with torch.cuda.device(dev):
-            L.check(lib.m3_mimo_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)),
-                    "m3_mimo_scan_bwd")
-        return dx, dB, dC, dADT, dDT, dtrap, dD, dmx, dmo, dh0, dbx0, None
+        g = _mimo_bwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, ctx.needs_input_grad[9],
+                          ctx.needs_input_grad[10])
+        return (*g, None)
 
 
 def _prep_siso(x, B_proj, C_proj, ADT, DT, trap, D):
