@@ -529,7 +529,7 @@ int m3_mimo_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
 
 size_t m3_mimo_scan_fwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t dstate) {
   if (batch < 0 || seqlen < 0 || nheads < 0 || dstate < 0) return 0;
-  return sizeof(float) * mimo_fwd_workspace_floats(batch, seqlen, nheads, dstate);
+  return mimo_fwd_workspace_bytes(batch, seqlen, nheads, dstate);
 }
 
 int m3_mimo_scan_fwd_ws(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
@@ -554,14 +554,14 @@ int m3_mimo_scan_fwd_ws(const m3_tensor* x, const m3_tensor* B, const m3_tensor*
       return copy_or_zero(fptr<void>(bx_last), fptr<void>(bx0), bytes, s, "bx_last");
     }
   }
-  const size_t need = sizeof(float) * mimo_fwd_workspace_floats(d[0], d[1], d[2], d[4]);
+  const size_t need = mimo_fwd_workspace_bytes(d[0], d[1], d[2], d[4]);
   if (!workspace || workspace_bytes < need)
     return fail(M3_ERR_WORKSPACE, "workspace: need " + std::to_string(need) + " bytes");
   if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0) return fail(M3_ERR_INVALID_ARGUMENT, "workspace: not 16-byte aligned");
   M3_TRY(check_device_ptr(workspace, "workspace"));
   p.y = y->data; p.sy = s3(y);
   p.h_last = fptr<float>(h_last); p.bx_last = fptr<float>(bx_last);
-  return launch_mimo_fwd_chunked(p, x->dtype, B->dtype, reinterpret_cast<float*>(workspace), s);
+  return launch_mimo_fwd_chunked(p, x->dtype, B->dtype, workspace, s);
 }
 
 size_t m3_mimo_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
@@ -783,10 +783,11 @@ int m3_argmax_rows(const m3_tensor* logits, m3_tensor* out, void* stream) {
 
 int m3_device_timeouts(int reset, int* flag_out) {
   if (!flag_out) return fail(M3_ERR_INVALID_ARGUMENT, "flag_out: missing");
-  int f = 0, b = 0;
+  int f = 0, b = 0, m = 0;
   M3_TRY(chunk_error_word(reset != 0, &f));
   M3_TRY(chunk_bwd_error_word(reset != 0, &b));
-  *flag_out = f | b;
+  M3_TRY(mimo_error_word(reset != 0, &m));
+  *flag_out = f | b | m;
   return M3_OK;
 }
 

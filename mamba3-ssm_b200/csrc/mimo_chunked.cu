@@ -14,8 +14,11 @@
 // x_{t0-1} and B_{t0-1} (bx0 for the first chunk). The kernels read x and B twice and C
 // once; the per-chunk work is a few hundred steps of independent FMAs instead of one
 // serial walk of the whole sequence per (b, h).
+#include <algorithm>
+
 #include "m3_common.cuh"
 #include "mimo_scan.cuh"
+#include "sm100.cuh"
 
 namespace m3 {
 namespace {
@@ -513,6 +516,291 @@ __global__ void __launch_bounds__(kCT) mimo_bwd_dadt_kernel(MimoParams a, const 
   }
 }
 
+// ------------------------------------------------------------------------------------
+// Single-pass forward. One CTA per (b, h, chunk) takes its chunk from a ticket counter
+// (chunk-major, so every chunk it waits for belongs to a CTA that started earlier), pulls
+// the chunk's rows of B and C into shared memory with bulk copies, scans the chunk from a
+// zero state, publishes that local end state S_c and the chunk's decay product A_c, and
+// then finds its carry (the state entering the chunk) by looking back over the chunks
+// before it: a chunk whose inclusive state I_j (the true state at its end) is published
+// ends the walk; one with only (A_j, S_j) is folded in and the walk goes on,
+//   carry_c = S_{c-1} + A_{c-1} (S_{c-2} + A_{c-2} ( ... + I_j)).
+// Its own I_c = S_c + A_c carry_c is published as soon as the carry is known, and the
+// states of the chunk are h_t = hloc_t + (a_t0 ... a_t) carry_c. B, C and x are read once.
+// Every wait (bulk copies, predecessors' flags) is bounded; a wait that gives up sets the
+// error word and the kernel finishes with its outputs invalid.
+// ------------------------------------------------------------------------------------
+constexpr int kFT = 128;                 // threads per CTA
+constexpr int kLkMax = 8;                // state columns per lane in the look-back (d_state <= 256)
+constexpr uint32_t kSpinLimit = 1u << 22;  // flag polls (about 64 ns apart) before giving up
+
+__device__ int g_mimo_error;  // set when a bounded wait gives up
+
+// Workspace of the single-pass forward: ticket counter, chunk flags (0 none, 1 local
+// aggregate, 2 inclusive state), then per chunk A_c, S_c[D], I_c[D]. The counter and the
+// flags are cleared before every launch.
+struct FusedWs {
+  unsigned* ticket;
+  int* flag;
+  float *A, *S, *I;
+};
+inline int64_t align16(int64_t v) { return (v + 15) & ~int64_t(15); }
+inline int64_t fused_flag_bytes(int64_t cells) { return 16 + align16(4 * cells); }
+inline int64_t fused_ws_bytes(int64_t cells, int64_t D) { return fused_flag_bytes(cells) + align16(4 * cells) + 8 * cells * D; }
+inline FusedWs fused_ws(void* base, int64_t cells, int64_t D) {
+  char* p = static_cast<char*>(base);
+  FusedWs w;
+  w.ticket = reinterpret_cast<unsigned*>(p);
+  w.flag = reinterpret_cast<int*>(p + 16);
+  w.A = reinterpret_cast<float*>(p + fused_flag_bytes(cells));
+  w.S = reinterpret_cast<float*>(p + fused_flag_bytes(cells) + align16(4 * cells));
+  w.I = w.S + cells * D;
+  return w;
+}
+
+// Shared-memory layout (byte offsets, each 16-byte aligned): two mbarriers and the ticket,
+// B rows t0-1 .. t0+n-1 ([row][r][d], row 0 = t0-1), C rows t0 .. t0+n-1, the chunk's
+// states (fp32 [t][d]), x rows t0-1 .. t0+n-1 (fp32), their rank projections, the step
+// coefficients and their running product, mimo_x, mimo_o, the readouts yr and the carry.
+struct FusedSmem {
+  uint32_t bs, cs, hs, xs, xr, a, be, ga, cum, mx, mo, yr, carry, total;
+};
+__host__ __device__ inline uint32_t a16(uint32_t v) { return (v + 15u) & ~15u; }
+__host__ __device__ inline FusedSmem fused_smem(int Q, int P, int R, int D, int eb) {
+  FusedSmem L;
+  uint32_t o = 32;
+  L.bs = o; o = a16(o + (uint32_t)((Q + 1) * R * D * eb));
+  L.cs = o; o = a16(o + (uint32_t)(Q * R * D * eb));
+  L.hs = o; o = a16(o + (uint32_t)(Q * D * 4));
+  L.xs = o; o = a16(o + (uint32_t)((Q + 1) * P * 4));
+  L.xr = o; o = a16(o + (uint32_t)((Q + 1) * R * 4));
+  L.a = o; o = a16(o + (uint32_t)(Q * 4));
+  L.be = o; o = a16(o + (uint32_t)(Q * 4));
+  L.ga = o; o = a16(o + (uint32_t)(Q * 4));
+  L.cum = o; o = a16(o + (uint32_t)(Q * 4));
+  L.mx = o; o = a16(o + (uint32_t)(R * P * 4));
+  L.mo = o; o = a16(o + (uint32_t)(R * P * 4));
+  L.yr = o; o = a16(o + (uint32_t)(Q * R * 4));
+  L.carry = o; o = a16(o + (uint32_t)(D * 4));
+  L.total = o;
+  return L;
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ float2 ld2f(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 ld2f(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+__device__ __forceinline__ float2 ld2f(const __half* p) { return __half22float2(*reinterpret_cast<const __half2*>(p)); }
+
+// Bounded wait for this CTA's bulk copies; on giving up, set the error word and wait once
+// more (also bounded) so that no copy is still writing shared memory when the CTA ends.
+__device__ __forceinline__ void wait_copies(uint64_t* bar) {
+  if (sm100::mbar_wait(bar, 0, 1u << 24)) return;
+  atomicExch(&g_mimo_error, 1);
+  sm100::mbar_wait(bar, 0, 1u << 24);
+}
+
+template <typename TX, typename TB, int Q>
+__global__ void __launch_bounds__(kFT) mimo_fused_fwd_kernel(MimoParams a, FusedWs w, int nch, int units) {
+  extern __shared__ __align__(128) unsigned char fsm[];
+  const int P = a.P, R = a.R, D = a.D, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const FusedSmem L = fused_smem(Q, P, R, D, (int)sizeof(TB));
+  uint64_t* barB = reinterpret_cast<uint64_t*>(fsm);
+  uint64_t* barC = barB + 1;
+  int* tk_s = reinterpret_cast<int*>(fsm + 16);
+  TB* Bs = reinterpret_cast<TB*>(fsm + L.bs);
+  TB* Cs = reinterpret_cast<TB*>(fsm + L.cs);
+  float* hs = reinterpret_cast<float*>(fsm + L.hs);
+  float* cum = reinterpret_cast<float*>(fsm + L.cum);
+  float* carry = reinterpret_cast<float*>(fsm + L.carry);
+  CSmem s;
+  s.x = reinterpret_cast<float*>(fsm + L.xs);
+  s.xr = reinterpret_cast<float*>(fsm + L.xr);
+  s.a = reinterpret_cast<float*>(fsm + L.a);
+  s.be = reinterpret_cast<float*>(fsm + L.be);
+  s.ga = reinterpret_cast<float*>(fsm + L.ga);
+  s.mx = reinterpret_cast<float*>(fsm + L.mx);
+  s.mo = reinterpret_cast<float*>(fsm + L.mo);
+  s.H = hs;
+  s.yr = reinterpret_cast<float*>(fsm + L.yr);
+
+  if (tid == 0) {
+    *tk_s = (int)atomicAdd(w.ticket, 1u);
+    sm100::mbar_init(barB, 1);
+    sm100::mbar_init(barC, 1);
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
+  const int tk = *tk_s;
+  const int c = tk / units, u = tk - c * units, b = u / a.H, h = u - b * a.H;
+  const int t0 = c * Q, n = min(Q, a.L - t0);
+  const int hb = c > 0 ? 1 : 0;  // the row t0-1 of B, for the first step's gamma term
+  const uint32_t rowb = (uint32_t)(D * sizeof(TB));
+  if (warp == 0) {
+    if (lane == 0) {
+      sm100::mbar_expect_tx(barB, (uint32_t)((n + hb) * R) * rowb);
+      sm100::mbar_expect_tx(barC, (uint32_t)(n * R) * rowb);
+    }
+    __syncwarp();
+    const TB* gB = reinterpret_cast<const TB*>(a.Bm) + (int64_t)b * a.sB.b + (int64_t)h * a.sB.h;
+    for (int i = lane; i < (n + hb) * R; i += 32) {
+      const int tt = i / R, r = i - tt * R;
+      sm100::bulk_load(Bs + ((size_t)(tt + 1 - hb) * R + r) * D, gB + (int64_t)(t0 - hb + tt) * a.sB.l + (int64_t)r * a.sB.r,
+                       rowb, barB);
+    }
+    const TB* gC = reinterpret_cast<const TB*>(a.Cm) + (int64_t)b * a.sC.b + (int64_t)h * a.sC.h;
+    for (int i = lane; i < n * R; i += 32) {
+      const int tt = i / R, r = i - tt * R;
+      sm100::bulk_load(Cs + (size_t)i * D, gC + (int64_t)(t0 + tt) * a.sC.l + (int64_t)r * a.sC.r, rowb, barC);
+    }
+  }
+  stage<TX>(a, s, b, h, t0, n, true);
+  if (tid == kFT - 1) {
+    float pr = 1.f;
+    for (int t = 0; t < n; ++t) cum[t] = pr *= s.a[t];
+  }
+  // local scan from a zero state
+  wait_copies(barB);
+  for (int d = tid; d < D; d += kFT) {
+    float bxp = 0.f;
+    if (hb) {
+      for (int r = 0; r < R; ++r) bxp = fmaf(s.xr[r], to_f32(Bs[(size_t)r * D + d]), bxp);
+    } else if (a.bx0) {
+      bxp = a.bx0[(int64_t)u * D + d];
+    }
+    float hv = 0.f;
+#pragma unroll 4
+    for (int t = 0; t < n; ++t) {
+      const float* xr = s.xr + (t + 1) * R;
+      const TB* brow = Bs + (size_t)(t + 1) * R * D + d;
+      float bx = 0.f;
+      for (int r = 0; r < R; ++r) bx = fmaf(xr[r], to_f32(brow[(size_t)r * D]), bx);
+      hv = fmaf(s.a[t], hv, fmaf(s.be[t], bx, s.ga[t] * bxp));
+      hs[t * D + d] = hv;
+      bxp = bx;
+    }
+    if (c == nch - 1 && a.bx_last) a.bx_last[(int64_t)u * D + d] = bxp;
+  }
+  __syncthreads();
+  // publish, then the carry
+  const int64_t cell = (int64_t)u * nch + c;
+  const float Ac = cum[n - 1];
+  if (c == 0) {
+    for (int d = tid; d < D; d += kFT) {
+      const float cv = a.h0 ? a.h0[(int64_t)u * D + d] : 0.f;
+      carry[d] = cv;
+      w.I[cell * D + d] = fmaf(Ac, cv, hs[(n - 1) * D + d]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release(w.flag + cell, 2);
+  } else {
+    for (int d = tid; d < D; d += kFT) w.S[cell * D + d] = hs[(n - 1) * D + d];
+    if (tid == 0) w.A[cell] = Ac;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release(w.flag + cell, 1);
+    if (warp == 0) {
+      float accA = 1.f, acc[kLkMax];
+#pragma unroll
+      for (int k = 0; k < kLkMax; ++k) acc[k] = 0.f;
+      bool ok = true;
+      for (int j = c - 1;; --j) {
+        const int64_t cj = (int64_t)u * nch + j;
+        int f = 0;
+        if (lane == 0) {
+          for (uint32_t i = 0; i < kSpinLimit; ++i) {
+            f = ld_acquire(w.flag + cj);
+            if (f != 0) break;
+            __nanosleep(64);
+          }
+        }
+        f = __shfl_sync(0xffffffffu, f, 0);
+        __syncwarp();
+        if (f == 0) {
+          ok = false;
+          break;
+        }
+        if (f == 2) {
+#pragma unroll
+          for (int k = 0; k < kLkMax; ++k) {
+            const int d = lane + 32 * k;
+            if (d < D) acc[k] = fmaf(accA, __ldcg(w.I + cj * D + d), acc[k]);
+          }
+          break;
+        }
+#pragma unroll
+        for (int k = 0; k < kLkMax; ++k) {
+          const int d = lane + 32 * k;
+          if (d < D) acc[k] = fmaf(accA, __ldcg(w.S + cj * D + d), acc[k]);
+        }
+        accA *= __ldcg(w.A + cj);
+        if (j == 0) {  // chunk 0 always publishes its inclusive state: unreachable
+          ok = false;
+          break;
+        }
+      }
+      if (!ok && lane == 0) atomicExch(&g_mimo_error, 1);
+#pragma unroll
+      for (int k = 0; k < kLkMax; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) {
+          const float cv = ok ? acc[k] : 0.f;
+          carry[d] = cv;
+          w.I[cell * D + d] = fmaf(Ac, cv, hs[(n - 1) * D + d]);
+        }
+      }
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) st_release(w.flag + cell, 2);
+    }
+    __syncthreads();
+  }
+  // the chunk's states from its carry
+  for (int i = tid; i < n * D; i += kFT) {
+    const int t = i / D, d = i - t * D;
+    hs[i] = fmaf(cum[t], carry[d], hs[i]);
+  }
+  wait_copies(barC);
+  __syncthreads();
+  if (c == nch - 1 && a.h_last)
+    for (int d = tid; d < D; d += kFT) a.h_last[(int64_t)u * D + d] = hs[(n - 1) * D + d];
+  // yr_t[r] = C_t[r, :] . h_t + D xr_t[r]: a thread per (t, r), two columns per step, each
+  // lane starting at its own column pair so that a warp's reads fall in distinct banks
+  const float Dk = a.Dskip[h * a.sD];
+  const int D2 = D >> 1;
+  for (int it = tid; it < n * R; it += kFT) {
+    const int t = it / R, r = it - t * R;
+    const TB* crow = Cs + (size_t)it * D;
+    const float* hrow = hs + (size_t)t * D;
+    float acc0 = 0.f, acc1 = 0.f;
+    int k = lane % D2;
+    for (int e = 0; e < D2; ++e) {
+      const float2 cv = ld2f(crow + 2 * k), hv = ld2f(hrow + 2 * k);
+      acc0 = fmaf(cv.x, hv.x, acc0);
+      acc1 = fmaf(cv.y, hv.y, acc1);
+      k = k + 1 == D2 ? 0 : k + 1;
+    }
+    s.yr[it] = fmaf(Dk, s.xr[(t + 1) * R + r], acc0 + acc1);
+  }
+  __syncthreads();
+  // y_t = mimo_o^T yr_t
+  for (int i = tid; i < n * P; i += kFT) {
+    const int t = i / P, p = i - t * P;
+    float acc = 0.f;
+    for (int r = 0; r < R; ++r) acc = fmaf(s.yr[t * R + r], s.mo[r * P + p], acc);
+    st(reinterpret_cast<TX*>(a.y) + (int64_t)b * a.sy.b + (int64_t)(t0 + t) * a.sy.l + (int64_t)h * a.sy.h + p, acc);
+  }
+}
+
 template <typename K>
 int opt_in(K k, size_t smem) {
   if (smem <= 48 * 1024) return M3_OK;
@@ -521,8 +809,51 @@ int opt_in(K k, size_t smem) {
   return M3_OK;
 }
 
+// The single-pass forward applies when every row of B and C that it copies starts on a
+// 16-byte boundary and is a whole number of 16-byte units, and d_state <= 256.
+template <typename TB>
+bool fused_applies(const MimoParams& p) {
+  const int64_t eb = sizeof(TB);
+  auto al = [&](const void* ptr, const Str4& st) {
+    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && (st.b * eb) % 16 == 0 && (st.l * eb) % 16 == 0 &&
+           (st.r * eb) % 16 == 0 && (st.h * eb) % 16 == 0;
+  };
+  return p.D % 2 == 0 && p.D <= 32 * kLkMax && (p.D * eb) % 16 == 0 && al(p.Bm, p.sB) && al(p.Cm, p.sC);
+}
+
+// Chunk length of the single-pass forward: the longest of 64 / 32 / 16 steps whose shared
+// memory lets four CTAs share an SM, else the shortest that fits at all.
+template <typename TB>
+int fused_chunk(const MimoParams& p) {
+  for (int q : {64, 32, 16})
+    if (fused_smem(q, p.P, p.R, p.D, (int)sizeof(TB)).total <= 55u * 1024u) return q;
+  return fused_smem(16, p.P, p.R, p.D, (int)sizeof(TB)).total <= 200u * 1024u ? 16 : 0;
+}
+
+template <typename TX, typename TB, int Q>
+int run_fused(const MimoParams& p, void* ws, cudaStream_t s) {
+  const int64_t nch = (p.L + Q - 1) / Q, units = (int64_t)p.Bn * p.H, cells = units * nch;
+  if (cells >= INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "mimo scan: too many chunks for the grid");
+  const FusedWs w = fused_ws(ws, cells, p.D);
+  const size_t smem = fused_smem(Q, p.P, p.R, p.D, (int)sizeof(TB)).total;
+  M3_TRY(opt_in(mimo_fused_fwd_kernel<TX, TB, Q>, smem));
+  cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)fused_flag_bytes(cells), s);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  mimo_fused_fwd_kernel<TX, TB, Q><<<(unsigned)cells, kFT, smem, s>>>(p, w, (int)nch, (int)units);
+  return check_launch("mimo_fused_fwd_kernel");
+}
+
 template <typename TX, typename TB>
-int run_chunked(const MimoParams& p, float* ws, cudaStream_t s) {
+int run_chunked(const MimoParams& p, void* ws_raw, cudaStream_t s) {
+  if (fused_applies<TB>(p)) {
+    switch (fused_chunk<TB>(p)) {
+      case 64: return run_fused<TX, TB, 64>(p, ws_raw, s);
+      case 32: return run_fused<TX, TB, 32>(p, ws_raw, s);
+      case 16: return run_fused<TX, TB, 16>(p, ws_raw, s);
+      default: break;
+    }
+  }
+  float* ws = static_cast<float*>(ws_raw);
   const int nch = (p.L + kTcF - 1) / kTcF;
   const int units = p.Bn * p.H;
   float* S = ws;
@@ -594,12 +925,27 @@ int launch_mimo_bwd_chunked(const MimoParams& p, int xdt, int bcdt, void* ws, cu
   return fail(M3_ERR_UNSUPPORTED, "unsupported dtype combination for x / B,C");
 }
 
-size_t mimo_fwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t D) {
-  const int64_t nch = (L + kTcF - 1) / kTcF;
-  return (size_t)(Bn * H * nch * (D + 1));
+size_t mimo_fwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D) {
+  // the larger of the three-pass layout (64-step chunks: a state and a decay each) and the
+  // single-pass one at its shortest chunk (16 steps)
+  const int64_t three = 4 * Bn * H * ((L + kTcF - 1) / kTcF) * (D + 1);
+  const int64_t single = fused_ws_bytes(Bn * H * ((L + 15) / 16), D);
+  return (size_t)std::max(three, single);
 }
 
-int launch_mimo_fwd_chunked(const MimoParams& p, int xdt, int bcdt, float* ws, cudaStream_t s) {
+int mimo_error_word(bool reset, int* out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_mimo_error, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_mimo_error, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("mimo error word: ") + cudaGetErrorString(e));
+  *out = v;
+  return M3_OK;
+}
+
+int launch_mimo_fwd_chunked(const MimoParams& p, int xdt, int bcdt, void* ws, cudaStream_t s) {
   if (p.L >= (int64_t)65535 * kTcF) return fail(M3_ERR_UNSUPPORTED, "mimo scan: sequence too long for the chunk grid");
   if (xdt == M3_FLOAT32 && bcdt == M3_FLOAT32) return run_chunked<float, float>(p, ws, s);
   if (xdt == M3_BFLOAT16 && bcdt == M3_BFLOAT16) return run_chunked<__nv_bfloat16, __nv_bfloat16>(p, ws, s);

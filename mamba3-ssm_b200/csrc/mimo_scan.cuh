@@ -44,9 +44,11 @@ struct MimoParams {
 
 size_t mimo_bwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t P, int64_t D, int64_t R);
 int launch_mimo(const MimoParams& p, int xdt, int bcdt, bool bwd, cudaStream_t s);
-// Chunk-parallel forward (mimo_chunked.cu): workspace of mimo_fwd_workspace_floats floats.
-size_t mimo_fwd_workspace_floats(int64_t Bn, int64_t L, int64_t H, int64_t D);
-int launch_mimo_fwd_chunked(const MimoParams& p, int xdt, int bcdt, float* ws, cudaStream_t s);
+// Chunk-parallel forward (mimo_chunked.cu): workspace of mimo_fwd_workspace_bytes bytes.
+size_t mimo_fwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D);
+int launch_mimo_fwd_chunked(const MimoParams& p, int xdt, int bcdt, void* ws, cudaStream_t s);
+// the word the single-pass forward sets when a bounded wait gives up
+int mimo_error_word(bool reset, int* out);
 // Chunk-parallel backward (mimo_chunked.cu), used when its shared-memory layout fits.
 bool mimo_bwd_chunked_fits(int P, int R, int D);
 size_t mimo_bwd_chunked_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D);

@@ -241,16 +241,45 @@ def test_siso_bf16_chunked_exact_mask_path(case):
     assert rel_err(y.detach().double().cpu().numpy(), yo) < 2e-2
 
 
-@pytest.mark.parametrize("L", [1, 63, 64, 65, 300])
-@pytest.mark.parametrize("R,D,P", [(4, 64, 32), (8, 256, 16)])
-def test_mimo_chunked_forward_with_states(L, R, D, P):
-    """The chunk-parallel MIMO forward (64-step chunks: local states, carry pass, outputs)
-    on chunk-boundary lengths, with carried-in states h0 / bx0 and the returned h_last /
-    bx_last, against the fp64 oracle."""
+@pytest.mark.parametrize("L", [1, 15, 16, 17, 33, 63, 64, 65, 300, 2500])
+@pytest.mark.parametrize("R,D,P", [(4, 64, 32), (8, 256, 16), (2, 16, 8)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mimo_chunked_forward_with_states(L, R, D, P, dtype):
+    """The single-pass MIMO forward (16 / 32 / 64-step chunks by shared-memory size, carries
+    found by looking back over earlier chunks) on chunk-boundary lengths and a long
+    sequence of many chunks, with carried-in states h0 / bx0 and the returned h_last /
+    bx_last, against the fp64 oracle; no bounded wait may give up."""
+    from mamba3_ssm import _lib
     from mamba3_ssm.ops import _MimoScanFn
-    arrs, t = _inputs(1000 + L + D, 2, L, 3, P, D, R=R, dtype=torch.float32)
+    arrs, t = _inputs(1000 + L + D, 2, L, 3, P, D, R=R, dtype=dtype)
     keys = ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")
     rng = np.random.default_rng(L + 7)
+    h0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV)
+    b0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV)
+    _lib.device_timeouts(reset=True)
+    y, hl, bl = _MimoScanFn.apply(*[t[k] for k in keys], h0, b0, True)
+    yo, ho, bo = O.mimo_scan_fwd(*[arrs[k] for k in keys], h0.double().cpu().numpy(), b0.double().cpu().numpy())
+    tol = _tol(dtype)
+    assert rel_err(y.detach().double().cpu().numpy(), yo) < tol
+    assert rel_err(hl.double().cpu().numpy(), ho) < 1e-4
+    assert rel_err(bl.double().cpu().numpy(), bo) < 1e-4
+    assert _lib.device_timeouts(reset=True) == 0
+
+
+@pytest.mark.parametrize("L", [65, 300])
+def test_mimo_forward_unaligned_rows_three_pass(L):
+    """B / C whose rows do not start on 16-byte boundaries (a view of a wider d axis) take
+    the three-pass forward (local states, carry pass, outputs); same results."""
+    from mamba3_ssm.ops import _MimoScanFn
+    R, D, P = 4, 64, 32
+    arrs, t = _inputs(3000 + L, 2, L, 3, P, D, R=R, dtype=torch.float32)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")
+    for k in ("B", "C"):
+        wide = torch.zeros(*t[k].shape[:-1], D + 1, dtype=t[k].dtype, device=DEV)
+        wide[..., :D] = t[k]
+        t[k] = wide[..., :D]
+        assert (t[k].stride(3) * 4) % 16 != 0
+    rng = np.random.default_rng(L + 9)
     h0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV)
     b0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV)
     y, hl, bl = _MimoScanFn.apply(*[t[k] for k in keys], h0, b0, True)
