@@ -195,11 +195,14 @@ int m3_mimo_scan_fwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
  * overwritten. */
 /* Chunk-parallel MIMO forward: same operands and results as m3_mimo_scan_fwd, plus a
  * caller-provided device workspace (16-byte aligned) of at least
- * m3_mimo_scan_fwd_workspace_size(...) bytes (per (b, h, 64-step chunk) one state and one
- * decay: 4 * batch * nheads * ceil(seqlen / 64) * (dstate + 1) bytes). The time axis is cut
- * into 64-step chunks processed in parallel (local states, a carry pass, then the outputs),
- * instead of one serial walk per (b, h). Replaces the same reference path as
- * m3_mimo_scan_fwd (cuda_backend.py:419-463, ops.py:226-240). */
+ * m3_mimo_scan_fwd_workspace_size(...) bytes (about 8 * batch * nheads * ceil(seqlen / 16)
+ * * (dstate + 1) bytes: per (b, h, chunk) the published states and decay with their status
+ * words). The time axis is cut into 16 / 32 / 64-step chunks; one pass reads x, B and C
+ * once (TMA boxes), each chunk finding the state that enters it by looking back over the
+ * chunks before it. Inputs whose rows the TMA cannot describe (x / B / C not 16-byte
+ * aligned or with strides that are not whole 16-byte units) take a three-pass form (local
+ * states, carry pass, outputs). Replaces the same reference path as m3_mimo_scan_fwd
+ * (cuda_backend.py:419-463, ops.py:226-240). */
 size_t m3_mimo_scan_fwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t dstate);
 int m3_mimo_scan_fwd_ws(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
                         const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D,
@@ -319,8 +322,9 @@ int m3_silu_gate_bwd(const m3_tensor* y, const m3_tensor* z, const m3_tensor* do
                      m3_tensor* dz, void* stream);
 
 /* ---------------------------------------------------------------------------------
- * Health word of the warp-specialised kernels on the current device: *flag_out is
- * nonzero once any bounded inter-warp wait gave up (the kernel then drained and its
+ * Health word of the warp-specialised kernels and of the single-pass MIMO forward on the
+ * current device: *flag_out is nonzero once any bounded wait (between warps, on a TMA
+ * box, or on an earlier chunk's published state) gave up (the kernel then drained and its
  * outputs are invalid); reset != 0 clears it. Synchronises the device. No reference
  * counterpart (the reference checks no launch at all, cuda_backend.py:403-405).
  * ------------------------------------------------------------------------------- */

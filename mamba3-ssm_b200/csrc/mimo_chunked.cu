@@ -18,6 +18,7 @@
 
 #include "m3_common.cuh"
 #include "mimo_scan.cuh"
+#include "siso_chunk.cuh"
 #include "sm100.cuh"
 
 namespace m3 {
@@ -518,286 +519,359 @@ __global__ void __launch_bounds__(kCT) mimo_bwd_dadt_kernel(MimoParams a, const 
 
 // ------------------------------------------------------------------------------------
 // Single-pass forward. One CTA per (b, h, chunk) takes its chunk from a ticket counter
-// (chunk-major, so every chunk it waits for belongs to a CTA that started earlier), pulls
-// the chunk's rows of B and C into shared memory with bulk copies, scans the chunk from a
-// zero state, publishes that local end state S_c and the chunk's decay product A_c, and
-// then finds its carry (the state entering the chunk) by looking back over the chunks
-// before it: a chunk whose inclusive state I_j (the true state at its end) is published
-// ends the walk; one with only (A_j, S_j) is folded in and the walk goes on,
+// (chunk-major, so every chunk it waits for belongs to a CTA that started earlier) and
+// pulls the chunk's B and C tiles into shared memory with one TMA box each. Each state
+// column d is then one thread's: it scans the chunk from a zero state, publishes that
+// local end state S_c[d] (and, once per chunk, the decay product A_c), finds its carry
+// (the state entering the chunk) by looking back over the chunks before it, publishes its
+// inclusive state I_c[d] = S_c[d] + A_c carry[d], and adds (a_t0 ... a_t) carry[d] to the
+// chunk's states. A chunk whose I_j[d] is published ends the walk; one with only S_j[d]
+// is folded in and the walk goes on,
 //   carry_c = S_{c-1} + A_{c-1} (S_{c-2} + A_{c-2} ( ... + I_j)).
-// Its own I_c = S_c + A_c carry_c is published as soon as the carry is known, and the
-// states of the chunk are h_t = hloc_t + (a_t0 ... a_t) carry_c. B, C and x are read once.
-// Every wait (bulk copies, predecessors' flags) is bounded; a wait that gives up sets the
-// error word and the kernel finishes with its outputs invalid.
+// Every published value shares a 64-bit word with its status (1: S, 2: I), written and
+// read with single-copy-atomic 64-bit accesses, so no fence is needed between a value and
+// its flag. B, C and x are read once. Every wait (TMA boxes, predecessors' words) is
+// bounded; a wait that gives up sets the error word and the kernel finishes with its
+// outputs invalid.
 // ------------------------------------------------------------------------------------
-constexpr int kFT = 128;                 // threads per CTA
-constexpr int kLkMax = 8;                // state columns per lane in the look-back (d_state <= 256)
-constexpr uint32_t kSpinLimit = 1u << 22;  // flag polls (about 64 ns apart) before giving up
+constexpr int kFT = 256;                   // threads per CTA
+constexpr uint32_t kSpinLimit = 1u << 22;  // polls of a predecessor's word before giving up
 
 __device__ int g_mimo_error;  // set when a bounded wait gives up
 
-// Workspace of the single-pass forward: ticket counter, chunk flags (0 none, 1 local
-// aggregate, 2 inclusive state), then per chunk A_c, S_c[D], I_c[D]. The counter and the
-// flags are cleared before every launch.
-struct FusedWs {
-  unsigned* ticket;
-  int* flag;
-  float *A, *S, *I;
+// x / d for 0 <= x < 2^31 by a multiply-high and a shift (Granlund and Montgomery,
+// "Division by invariant integers using multiplication", 1994: the round-up multiplier
+// m = floor(2^32 (2^s - d) / d) + 1 with s = ceil(log2 d), q = (mulhi(x, m) + x) >> s).
+struct FastDiv {
+  uint32_t m, s;
 };
-inline int64_t align16(int64_t v) { return (v + 15) & ~int64_t(15); }
-inline int64_t fused_flag_bytes(int64_t cells) { return 16 + align16(4 * cells); }
-inline int64_t fused_ws_bytes(int64_t cells, int64_t D) { return fused_flag_bytes(cells) + align16(4 * cells) + 8 * cells * D; }
-inline FusedWs fused_ws(void* base, int64_t cells, int64_t D) {
-  char* p = static_cast<char*>(base);
-  FusedWs w;
-  w.ticket = reinterpret_cast<unsigned*>(p);
-  w.flag = reinterpret_cast<int*>(p + 16);
-  w.A = reinterpret_cast<float*>(p + fused_flag_bytes(cells));
-  w.S = reinterpret_cast<float*>(p + fused_flag_bytes(cells) + align16(4 * cells));
-  w.I = w.S + cells * D;
-  return w;
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  f.s = s;
+  f.m = (uint32_t)(((1ull << 32) * ((1ull << s) - d)) / d + 1);
+  return f;
+}
+__device__ __forceinline__ int fdiv(int x, FastDiv f) {
+  return (int)((__umulhi((uint32_t)x, f.m) + (uint32_t)x) >> f.s);
 }
 
-// Shared-memory layout (byte offsets, each 16-byte aligned): two mbarriers and the ticket,
-// B rows t0-1 .. t0+n-1 ([row][r][d], row 0 = t0-1), C rows t0 .. t0+n-1, the chunk's
-// states (fp32 [t][d]), x rows t0-1 .. t0+n-1 (fp32), their rank projections, the step
-// coefficients and their running product, mimo_x, mimo_o, the readouts yr and the carry.
-struct FusedSmem {
-  uint32_t bs, cs, hs, xs, xr, a, be, ga, cum, mx, mo, yr, carry, total;
+struct FusedArgs {
+  FastDiv fP4, fD4, fR, fU, fH;  // divisors headdim / 4, d_state / 4, rank, units, heads
+  int nch, units;
+  int ahead;  // CTAs resident on the device: a CTA prefetches the chunk of ticket + ahead into L2
+  int yvec;   // y rows start on 16-byte boundaries: four outputs per store
+  unsigned* ticket;
+  unsigned long long* rec;   // [unit][chunk][d]: S or I value | status << 32
+  unsigned long long* arec;  // [unit][chunk]: A value | 1 << 32
 };
-__host__ __device__ inline uint32_t a16(uint32_t v) { return (v + 15u) & ~15u; }
-__host__ __device__ inline FusedSmem fused_smem(int Q, int P, int R, int D, int eb) {
+
+// Workspace of the single-pass forward: the ticket counter, then the value words and the
+// decay words, all cleared before every launch.
+inline int64_t fused_ws_bytes(int64_t cells, int64_t D) { return 16 + 8 * cells * (D + 1); }
+
+// Shared-memory layout (byte offsets from a 128-byte aligned base): two mbarriers and the
+// ticket, the B box (rows t0-1 .. t0+Q-1, [row][r][d], row 0 = t0-1), the C box (rows
+// t0 .. t0+Q-1), the x box (rows t0-1 .. t0+Q-1, [row][p]), the chunk's bx and then states
+// (fp32 [t][d]), the rank projections of x, the step coefficients (a, beta, gamma, -) and
+// the running decay products, mimo_x and mimo_o (rows padded to P + 4 floats), the
+// readouts and the carries.
+struct FusedSmem {
+  uint32_t bs, cs, xs, hs, xr, coef, cum, mx, mo, yr, carry, total;
+};
+__host__ __device__ inline uint32_t aup(uint32_t v, uint32_t k) { return (v + k - 1) / k * k; }
+__host__ __device__ inline FusedSmem fused_smem(int Q, int P, int R, int D, int eb, int ex) {
   FusedSmem L;
-  uint32_t o = 32;
-  L.bs = o; o = a16(o + (uint32_t)((Q + 1) * R * D * eb));
-  L.cs = o; o = a16(o + (uint32_t)(Q * R * D * eb));
-  L.hs = o; o = a16(o + (uint32_t)(Q * D * 4));
-  L.xs = o; o = a16(o + (uint32_t)((Q + 1) * P * 4));
-  L.xr = o; o = a16(o + (uint32_t)((Q + 1) * R * 4));
-  L.a = o; o = a16(o + (uint32_t)(Q * 4));
-  L.be = o; o = a16(o + (uint32_t)(Q * 4));
-  L.ga = o; o = a16(o + (uint32_t)(Q * 4));
-  L.cum = o; o = a16(o + (uint32_t)(Q * 4));
-  L.mx = o; o = a16(o + (uint32_t)(R * P * 4));
-  L.mo = o; o = a16(o + (uint32_t)(R * P * 4));
-  L.yr = o; o = a16(o + (uint32_t)(Q * R * 4));
-  L.carry = o; o = a16(o + (uint32_t)(D * 4));
-  L.total = o;
+  uint32_t o = 128;
+  L.bs = o; o = aup(o + (uint32_t)((Q + 1) * R * D * eb), 128);
+  L.cs = o; o = aup(o + (uint32_t)(Q * R * D * eb), 128);
+  L.xs = o; o = aup(o + (uint32_t)((Q + 1) * P * ex), 128);
+  L.hs = o; o = aup(o + (uint32_t)(Q * D * 4), 16);
+  L.xr = o; o = aup(o + (uint32_t)((Q + 1) * R * 4), 16);
+  L.coef = o; o = aup(o + (uint32_t)(Q * 16), 16);
+  L.cum = o; o = aup(o + (uint32_t)(Q * 4), 16);
+  L.mx = o; o = aup(o + (uint32_t)(R * (P + 4) * 4), 16);
+  L.mo = o; o = aup(o + (uint32_t)(R * (P + 4) * 4), 16);
+  L.yr = o; o = aup(o + (uint32_t)(Q * R * 4), 16);
+  L.carry = o; o = aup(o + (uint32_t)(D * 4), 16);
+  L.total = o + 128;  // slack for aligning the dynamic shared-memory base
   return L;
 }
 
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release(int* p, int v) {
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed64(unsigned long long* p, float v, uint32_t status) {
+  const unsigned long long w = ((unsigned long long)status << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ float2 ld2f(const float* p) { return *reinterpret_cast<const float2*>(p); }
-__device__ __forceinline__ float2 ld2f(const __nv_bfloat16* p) {
-  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+// four consecutive elements (16-byte aligned for fp32, 8-byte for 16-bit types) as floats
+__device__ __forceinline__ float4 ld4f(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4f(const __nv_bfloat16* p) {
+  const uint2 w = *reinterpret_cast<const uint2*>(p);
+  const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+  const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
 }
-__device__ __forceinline__ float2 ld2f(const __half* p) { return __half22float2(*reinterpret_cast<const __half2*>(p)); }
+__device__ __forceinline__ float4 ld4f(const __half* p) {
+  const uint2 w = *reinterpret_cast<const uint2*>(p);
+  const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+  const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void st4(__nv_bfloat16* p, float4 v) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+  uint2 w;
+  w.x = *reinterpret_cast<const uint32_t*>(&lo);
+  w.y = *reinterpret_cast<const uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(p) = w;
+}
+__device__ __forceinline__ void st4(__half* p, float4 v) {
+  const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+  uint2 w;
+  w.x = *reinterpret_cast<const uint32_t*>(&lo);
+  w.y = *reinterpret_cast<const uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(p) = w;
+}
+__device__ __forceinline__ void fma4(float4& acc, float s, float4 v) {
+  acc.x = fmaf(s, v.x, acc.x);
+  acc.y = fmaf(s, v.y, acc.y);
+  acc.z = fmaf(s, v.z, acc.z);
+  acc.w = fmaf(s, v.w, acc.w);
+}
+__device__ __forceinline__ void fma4(float4& acc, float4 u, float4 v) {
+  acc.x = fmaf(u.x, v.x, acc.x);
+  acc.y = fmaf(u.y, v.y, acc.y);
+  acc.z = fmaf(u.z, v.z, acc.z);
+  acc.w = fmaf(u.w, v.w, acc.w);
+}
 
-// Bounded wait for this CTA's bulk copies; on giving up, set the error word and wait once
-// more (also bounded) so that no copy is still writing shared memory when the CTA ends.
+// Bounded wait for a TMA box; on giving up, set the error word and wait once more (also
+// bounded) so that no copy is still writing shared memory when the CTA ends.
 __device__ __forceinline__ void wait_copies(uint64_t* bar) {
   if (sm100::mbar_wait(bar, 0, 1u << 24)) return;
   atomicExch(&g_mimo_error, 1);
   sm100::mbar_wait(bar, 0, 1u << 24);
 }
 
+// The carry of column d of chunk c of unit u from the words of the chunks before it.
+__device__ __forceinline__ float look_back(const FusedArgs& f, int u, int c, int d, int D, bool& ok) {
+  const int64_t base = (int64_t)u * f.nch;
+  float acc = 0.f, accA = 1.f;
+  int j = c - 1;
+  for (uint32_t spins = 0; spins < kSpinLimit; ++spins) {
+    const unsigned long long w = ld_relaxed64(f.rec + (base + j) * D + d);
+    const unsigned long long av = ld_relaxed64(f.arec + base + j);
+    const uint32_t st = (uint32_t)(w >> 32);
+    if (st == 2) return fmaf(accA, __uint_as_float((uint32_t)w), acc);
+    if (st == 1 && (av >> 32) != 0) {
+      acc = fmaf(accA, __uint_as_float((uint32_t)w), acc);
+      accA *= __uint_as_float((uint32_t)av);
+      if (--j < 0) break;  // chunk 0 publishes its inclusive state only: unreachable
+      continue;
+    }
+    __nanosleep(32);
+  }
+  ok = false;
+  return 0.f;
+}
+
 template <typename TX, typename TB, int Q>
-__global__ void __launch_bounds__(kFT) mimo_fused_fwd_kernel(MimoParams a, FusedWs w, int nch, int units) {
-  extern __shared__ __align__(128) unsigned char fsm[];
-  const int P = a.P, R = a.R, D = a.D, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const FusedSmem L = fused_smem(Q, P, R, D, (int)sizeof(TB));
+__global__ void __launch_bounds__(kFT)
+    mimo_fused_fwd_kernel(const __grid_constant__ CUtensorMap mapB, const __grid_constant__ CUtensorMap mapC,
+                          const __grid_constant__ CUtensorMap mapX, MimoParams a, FusedArgs f) {
+  static_assert(Q <= kFT, "a thread per step of the chunk");
+  extern __shared__ __align__(128) unsigned char fsm_raw[];
+  unsigned char* fsm = fsm_raw + ((128u - (sm100::smem_u32(fsm_raw) & 127u)) & 127u);
+  const int P = a.P, R = a.R, D = a.D, tid = threadIdx.x, lane = tid & 31;
+  const int P4 = P >> 2, D4 = D >> 2, MS = P + 4;
+  const FusedSmem L = fused_smem(Q, P, R, D, (int)sizeof(TB), (int)sizeof(TX));
   uint64_t* barB = reinterpret_cast<uint64_t*>(fsm);
   uint64_t* barC = barB + 1;
   int* tk_s = reinterpret_cast<int*>(fsm + 16);
-  TB* Bs = reinterpret_cast<TB*>(fsm + L.bs);
-  TB* Cs = reinterpret_cast<TB*>(fsm + L.cs);
+  const TB* Bs = reinterpret_cast<const TB*>(fsm + L.bs);
+  const TB* Cs = reinterpret_cast<const TB*>(fsm + L.cs);
+  const TX* xs = reinterpret_cast<const TX*>(fsm + L.xs);
   float* hs = reinterpret_cast<float*>(fsm + L.hs);
+  float* xr = reinterpret_cast<float*>(fsm + L.xr);
+  float4* coef = reinterpret_cast<float4*>(fsm + L.coef);
   float* cum = reinterpret_cast<float*>(fsm + L.cum);
-  float* carry = reinterpret_cast<float*>(fsm + L.carry);
-  CSmem s;
-  s.x = reinterpret_cast<float*>(fsm + L.xs);
-  s.xr = reinterpret_cast<float*>(fsm + L.xr);
-  s.a = reinterpret_cast<float*>(fsm + L.a);
-  s.be = reinterpret_cast<float*>(fsm + L.be);
-  s.ga = reinterpret_cast<float*>(fsm + L.ga);
-  s.mx = reinterpret_cast<float*>(fsm + L.mx);
-  s.mo = reinterpret_cast<float*>(fsm + L.mo);
-  s.H = hs;
-  s.yr = reinterpret_cast<float*>(fsm + L.yr);
+  float* mx = reinterpret_cast<float*>(fsm + L.mx);
+  float* mo = reinterpret_cast<float*>(fsm + L.mo);
+  float* yr = reinterpret_cast<float*>(fsm + L.yr);
+  float* carry_s = reinterpret_cast<float*>(fsm + L.carry);
 
   if (tid == 0) {
-    *tk_s = (int)atomicAdd(w.ticket, 1u);
+    *tk_s = (int)atomicAdd(f.ticket, 1u);
     sm100::mbar_init(barB, 1);
     sm100::mbar_init(barC, 1);
     sm100::fence_barrier_init();
   }
   __syncthreads();
   const int tk = *tk_s;
-  const int c = tk / units, u = tk - c * units, b = u / a.H, h = u - b * a.H;
+  const int c = fdiv(tk, f.fU), u = tk - c * f.units, b = fdiv(u, f.fH), h = u - b * a.H;
   const int t0 = c * Q, n = min(Q, a.L - t0);
-  const int hb = c > 0 ? 1 : 0;  // the row t0-1 of B, for the first step's gamma term
-  const uint32_t rowb = (uint32_t)(D * sizeof(TB));
-  if (warp == 0) {
-    if (lane == 0) {
-      sm100::mbar_expect_tx(barB, (uint32_t)((n + hb) * R) * rowb);
-      sm100::mbar_expect_tx(barC, (uint32_t)(n * R) * rowb);
+  // the step scalars first: their loads are in flight while the boxes are requested
+  float s_adt = 0.f, s_dt = 0.f, s_tr = 0.f;
+  if (tid < n) {
+    s_adt = scalc(a.adt, a.sadt, b, t0 + tid, h);
+    s_dt = scalc(a.dt, a.sdt, b, t0 + tid, h);
+    s_tr = scalc(a.trap, a.strap, b, t0 + tid, h);
+  }
+  if (tid == 0) {
+    // whole boxes: rows outside the sequence (t0-1 of the first chunk, the tail of the
+    // last) arrive as zeros and still count toward the transaction bytes
+    sm100::mbar_expect_tx(barB, (uint32_t)((Q + 1) * (R * D * sizeof(TB) + P * sizeof(TX))));
+    sm100::tma_load_5d(fsm + L.bs, &mapB, barB, 0, h, 0, t0 - 1, b);
+    sm100::tma_load_4d(fsm + L.xs, &mapX, barB, 0, h, t0 - 1, b);
+    sm100::mbar_expect_tx(barC, (uint32_t)(Q * R * D * sizeof(TB)));
+    sm100::tma_load_5d(fsm + L.cs, &mapC, barC, 0, h, 0, t0, b);
+  }
+  // the inputs of the chunk that the CTA `ahead` tickets later will take, into L2
+  const int tf = tk + f.ahead;
+  if (tf < f.units * f.nch && tid < 32) {
+    const int cf = fdiv(tf, f.fU), uf = tf - cf * f.units, bf = fdiv(uf, f.fH), hf = uf - bf * a.H;
+    const int tf0 = cf * Q;
+    if (tid == 0) {  // rows from max(t0 - 1, 0): no prefetch starts outside the tensor
+      sm100::tma_prefetch_l2_5d(&mapB, 0, hf, 0, max(tf0 - 1, 0), bf);
+      sm100::tma_prefetch_l2_5d(&mapC, 0, hf, 0, tf0, bf);
+      sm100::tma_prefetch_l2_4d(&mapX, 0, hf, max(tf0 - 1, 0), bf);
     }
-    __syncwarp();
-    const TB* gB = reinterpret_cast<const TB*>(a.Bm) + (int64_t)b * a.sB.b + (int64_t)h * a.sB.h;
-    for (int i = lane; i < (n + hb) * R; i += 32) {
-      const int tt = i / R, r = i - tt * R;
-      sm100::bulk_load(Bs + ((size_t)(tt + 1 - hb) * R + r) * D, gB + (int64_t)(t0 - hb + tt) * a.sB.l + (int64_t)r * a.sB.r,
-                       rowb, barB);
-    }
-    const TB* gC = reinterpret_cast<const TB*>(a.Cm) + (int64_t)b * a.sC.b + (int64_t)h * a.sC.h;
-    for (int i = lane; i < n * R; i += 32) {
-      const int tt = i / R, r = i - tt * R;
-      sm100::bulk_load(Cs + (size_t)i * D, gC + (int64_t)(t0 + tt) * a.sC.l + (int64_t)r * a.sC.r, rowb, barC);
+    for (int t = tf0 + tid; t < min(tf0 + Q, a.L); t += 32) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a.adt + (int64_t)bf * a.sadt.b + (int64_t)t * a.sadt.l + (int64_t)hf * a.sadt.h));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a.dt + (int64_t)bf * a.sdt.b + (int64_t)t * a.sdt.l + (int64_t)hf * a.sdt.h));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a.trap + (int64_t)bf * a.strap.b + (int64_t)t * a.strap.l + (int64_t)hf * a.strap.h));
     }
   }
-  stage<TX>(a, s, b, h, t0, n, true);
-  if (tid == kFT - 1) {
-    float pr = 1.f;
-    for (int t = 0; t < n; ++t) cum[t] = pr *= s.a[t];
+  for (int i = tid; i < R * P; i += kFT) {
+    const int r = fdiv(i >> 2, f.fP4), p = i - r * P;
+    mx[r * MS + p] = a.mimo_x[(int64_t)h * a.smx_h + (int64_t)r * a.smx_r + p];
+    mo[r * MS + p] = a.mimo_o[(int64_t)h * a.smo_h + (int64_t)r * a.smo_r + p];
   }
-  // local scan from a zero state
+  if (tid < n) {
+    const float tr = sigmoidf_(s_tr);
+    coef[tid] = make_float4(expf(s_adt), s_dt * (1.0f - tr) + 0.5f * s_dt * tr, 0.5f * s_dt * tr, 0.f);
+  }
+  __syncthreads();
   wait_copies(barB);
+  // xr_t[k] = mimo_x[k, :] . x_t, four p per step, each row starting at its own p block
+  for (int i = tid; i < (n + 1) * R; i += kFT) {
+    const int row = fdiv(i, f.fR), k = i - row * R;
+    const TX* xrow = xs + row * P;
+    const float* mrow = mx + k * MS;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int pb = row % P4;
+    for (int e = 0; e < P4; ++e) {
+      fma4(acc, ld4f(xrow + 4 * pb), ld4f(mrow + 4 * pb));
+      pb = pb + 1 == P4 ? 0 : pb + 1;
+    }
+    xr[i] = (acc.x + acc.y) + (acc.z + acc.w);
+  }
+  __syncthreads();
+  // bx_t[d] = sum_r xr_t[r] B_t[r, d] for t0 .. t0+n-1 (four columns a thread), into the
+  // state array
+  for (int i = tid; i < n * D4; i += kFT) {
+    const int t = fdiv(i, f.fD4), d = 4 * (i - t * D4);
+    const float* xrow = xr + (t + 1) * R;
+    const TB* brow = Bs + (size_t)(t + 1) * R * D + d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < R; ++r) fma4(acc, xrow[r], ld4f(brow + (size_t)r * D));
+    *reinterpret_cast<float4*>(hs + t * D + d) = acc;
+  }
+  __syncthreads();
+  const int64_t cell = (int64_t)u * f.nch + c;
+  bool ok = true;
   for (int d = tid; d < D; d += kFT) {
     float bxp = 0.f;
-    if (hb) {
-      for (int r = 0; r < R; ++r) bxp = fmaf(s.xr[r], to_f32(Bs[(size_t)r * D + d]), bxp);
+    if (c > 0) {
+      for (int r = 0; r < R; ++r) bxp = fmaf(xr[r], to_f32(Bs[(size_t)r * D + d]), bxp);
     } else if (a.bx0) {
       bxp = a.bx0[(int64_t)u * D + d];
     }
-    float hv = 0.f;
-#pragma unroll 4
-    for (int t = 0; t < n; ++t) {
-      const float* xr = s.xr + (t + 1) * R;
-      const TB* brow = Bs + (size_t)(t + 1) * R * D + d;
-      float bx = 0.f;
-      for (int r = 0; r < R; ++r) bx = fmaf(xr[r], to_f32(brow[(size_t)r * D]), bx);
-      hv = fmaf(s.a[t], hv, fmaf(s.be[t], bx, s.ga[t] * bxp));
-      hs[t * D + d] = hv;
-      bxp = bx;
+    // the chunk from a zero state, eight steps per batch of shared-memory reads; column 0
+    // also records the running decay products
+    float hv = 0.f, pr = 1.f;
+    for (int tb = 0; tb < n; tb += 8) {
+      float bxv[8];
+      float4 cf[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool in = tb + j < n;
+        bxv[j] = in ? hs[(tb + j) * D + d] : 0.f;
+        cf[j] = in ? coef[tb + j] : make_float4(1.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        hv = fmaf(cf[j].x, hv, fmaf(cf[j].y, bxv[j], cf[j].z * bxp));
+        pr *= cf[j].x;
+        if (tb + j < n) {
+          bxp = bxv[j];
+          hs[(tb + j) * D + d] = hv;
+          if (d == 0) cum[tb + j] = pr;
+        }
+      }
     }
-    if (c == nch - 1 && a.bx_last) a.bx_last[(int64_t)u * D + d] = bxp;
+    if (c == f.nch - 1 && a.bx_last) a.bx_last[(int64_t)u * D + d] = bxp;
+    float carry;
+    if (c == 0) {
+      carry = a.h0 ? a.h0[(int64_t)u * D + d] : 0.f;
+    } else {
+      st_relaxed64(f.rec + cell * D + d, hv, 1);
+      if (d == 0) st_relaxed64(f.arec + cell, pr, 1);
+      carry = look_back(f, u, c, d, D, ok);
+    }
+    const float incl = fmaf(pr, carry, hv);
+    st_relaxed64(f.rec + cell * D + d, incl, 2);
+    if (c == f.nch - 1 && a.h_last) a.h_last[(int64_t)u * D + d] = incl;
+    carry_s[d] = carry;
   }
+  if (!ok) atomicExch(&g_mimo_error, 1);
   __syncthreads();
-  // publish, then the carry
-  const int64_t cell = (int64_t)u * nch + c;
-  const float Ac = cum[n - 1];
-  if (c == 0) {
-    for (int d = tid; d < D; d += kFT) {
-      const float cv = a.h0 ? a.h0[(int64_t)u * D + d] : 0.f;
-      carry[d] = cv;
-      w.I[cell * D + d] = fmaf(Ac, cv, hs[(n - 1) * D + d]);
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) st_release(w.flag + cell, 2);
-  } else {
-    for (int d = tid; d < D; d += kFT) w.S[cell * D + d] = hs[(n - 1) * D + d];
-    if (tid == 0) w.A[cell] = Ac;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) st_release(w.flag + cell, 1);
-    if (warp == 0) {
-      float accA = 1.f, acc[kLkMax];
-#pragma unroll
-      for (int k = 0; k < kLkMax; ++k) acc[k] = 0.f;
-      bool ok = true;
-      for (int j = c - 1;; --j) {
-        const int64_t cj = (int64_t)u * nch + j;
-        int f = 0;
-        if (lane == 0) {
-          for (uint32_t i = 0; i < kSpinLimit; ++i) {
-            f = ld_acquire(w.flag + cj);
-            if (f != 0) break;
-            __nanosleep(64);
-          }
-        }
-        f = __shfl_sync(0xffffffffu, f, 0);
-        __syncwarp();
-        if (f == 0) {
-          ok = false;
-          break;
-        }
-        if (f == 2) {
-#pragma unroll
-          for (int k = 0; k < kLkMax; ++k) {
-            const int d = lane + 32 * k;
-            if (d < D) acc[k] = fmaf(accA, __ldcg(w.I + cj * D + d), acc[k]);
-          }
-          break;
-        }
-#pragma unroll
-        for (int k = 0; k < kLkMax; ++k) {
-          const int d = lane + 32 * k;
-          if (d < D) acc[k] = fmaf(accA, __ldcg(w.S + cj * D + d), acc[k]);
-        }
-        accA *= __ldcg(w.A + cj);
-        if (j == 0) {  // chunk 0 always publishes its inclusive state: unreachable
-          ok = false;
-          break;
-        }
-      }
-      if (!ok && lane == 0) atomicExch(&g_mimo_error, 1);
-#pragma unroll
-      for (int k = 0; k < kLkMax; ++k) {
-        const int d = lane + 32 * k;
-        if (d < D) {
-          const float cv = ok ? acc[k] : 0.f;
-          carry[d] = cv;
-          w.I[cell * D + d] = fmaf(Ac, cv, hs[(n - 1) * D + d]);
-        }
-      }
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) st_release(w.flag + cell, 2);
-    }
-    __syncthreads();
-  }
-  // the chunk's states from its carry
-  for (int i = tid; i < n * D; i += kFT) {
-    const int t = i / D, d = i - t * D;
-    hs[i] = fmaf(cum[t], carry[d], hs[i]);
+  // the chunk's states from the carries: h_t = hloc_t + (a_t0 ... a_t) carry
+  for (int i = tid; i < n * D4; i += kFT) {
+    const int t = fdiv(i, f.fD4), d = 4 * (i - t * D4);
+    float4 hv = *reinterpret_cast<const float4*>(hs + t * D + d);
+    fma4(hv, cum[t], *reinterpret_cast<const float4*>(carry_s + d));
+    *reinterpret_cast<float4*>(hs + t * D + d) = hv;
   }
   wait_copies(barC);
   __syncthreads();
-  if (c == nch - 1 && a.h_last)
-    for (int d = tid; d < D; d += kFT) a.h_last[(int64_t)u * D + d] = hs[(n - 1) * D + d];
-  // yr_t[r] = C_t[r, :] . h_t + D xr_t[r]: a thread per (t, r), two columns per step, each
-  // lane starting at its own column pair so that a warp's reads fall in distinct banks
+  // yr_t[r] = C_t[r, :] . h_t + D xr_t[r]: a thread per (t, r), four columns per step, each
+  // lane starting at its own column block so that a warp's reads fall in distinct banks
   const float Dk = a.Dskip[h * a.sD];
-  const int D2 = D >> 1;
   for (int it = tid; it < n * R; it += kFT) {
-    const int t = it / R, r = it - t * R;
+    const int t = fdiv(it, f.fR), r = it - t * R;
     const TB* crow = Cs + (size_t)it * D;
     const float* hrow = hs + (size_t)t * D;
-    float acc0 = 0.f, acc1 = 0.f;
-    int k = lane % D2;
-    for (int e = 0; e < D2; ++e) {
-      const float2 cv = ld2f(crow + 2 * k), hv = ld2f(hrow + 2 * k);
-      acc0 = fmaf(cv.x, hv.x, acc0);
-      acc1 = fmaf(cv.y, hv.y, acc1);
-      k = k + 1 == D2 ? 0 : k + 1;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int k = lane % D4;
+#pragma unroll 4
+    for (int e = 0; e < D4; ++e) {
+      fma4(acc, ld4f(crow + 4 * k), ld4f(hrow + 4 * k));
+      k = k + 1 == D4 ? 0 : k + 1;
     }
-    s.yr[it] = fmaf(Dk, s.xr[(t + 1) * R + r], acc0 + acc1);
+    yr[it] = fmaf(Dk, xr[(t + 1) * R + r], (acc.x + acc.y) + (acc.z + acc.w));
   }
   __syncthreads();
-  // y_t = mimo_o^T yr_t
-  for (int i = tid; i < n * P; i += kFT) {
-    const int t = i / P, p = i - t * P;
-    float acc = 0.f;
-    for (int r = 0; r < R; ++r) acc = fmaf(s.yr[t * R + r], s.mo[r * P + p], acc);
-    st(reinterpret_cast<TX*>(a.y) + (int64_t)b * a.sy.b + (int64_t)(t0 + t) * a.sy.l + (int64_t)h * a.sy.h + p, acc);
+  // y_t = mimo_o^T yr_t, four outputs a thread
+  TX* yb = reinterpret_cast<TX*>(a.y) + (int64_t)b * a.sy.b + (int64_t)h * a.sy.h;
+  for (int i = tid; i < n * P4; i += kFT) {
+    const int t = fdiv(i, f.fP4), p = 4 * (i - t * P4);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < R; ++r) fma4(acc, yr[t * R + r], ld4f(mo + r * MS + p));
+    TX* yp = yb + (int64_t)(t0 + t) * a.sy.l + p;
+    if (f.yvec) {
+      st4(yp, acc);
+    } else {
+      st(yp, acc.x);
+      st(yp + 1, acc.y);
+      st(yp + 2, acc.z);
+      st(yp + 3, acc.w);
+    }
   }
 }
 
@@ -809,49 +883,121 @@ int opt_in(K k, size_t smem) {
   return M3_OK;
 }
 
-// The single-pass forward applies when every row of B and C that it copies starts on a
-// 16-byte boundary and is a whole number of 16-byte units, and d_state <= 256.
-template <typename TB>
+// The single-pass forward applies when its TMA boxes can be described: x, B and C 16-byte
+// aligned with strides of whole 16-byte units, rows of whole 16-byte units, headdim and
+// d_state at most 256 (one box dimension), d_state a multiple of 4, rank at most 8.
+template <typename TX, typename TB>
 bool fused_applies(const MimoParams& p) {
-  const int64_t eb = sizeof(TB);
+  const int64_t eb = sizeof(TB), ex = sizeof(TX);
   auto al = [&](const void* ptr, const Str4& st) {
     return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && (st.b * eb) % 16 == 0 && (st.l * eb) % 16 == 0 &&
-           (st.r * eb) % 16 == 0 && (st.h * eb) % 16 == 0;
+           (st.r * eb) % 16 == 0 && (st.h * eb) % 16 == 0 && st.b > 0 && st.l > 0 && st.r > 0 && st.h > 0;
   };
-  return p.D % 2 == 0 && p.D <= 32 * kLkMax && (p.D * eb) % 16 == 0 && al(p.Bm, p.sB) && al(p.Cm, p.sC);
+  const bool xal = reinterpret_cast<uintptr_t>(p.x) % 16 == 0 && (p.sx.b * ex) % 16 == 0 && (p.sx.l * ex) % 16 == 0 &&
+                   (p.sx.h * ex) % 16 == 0 && p.sx.b > 0 && p.sx.l > 0 && p.sx.h > 0 && (p.P * ex) % 16 == 0 &&
+                   p.P <= 256;
+  return p.D % 4 == 0 && p.D <= 256 && p.R <= 8 && (p.D * eb) % 16 == 0 && al(p.Bm, p.sB) && al(p.Cm, p.sC) &&
+         xal && chunk_encode_fn() != nullptr;
 }
 
 // Chunk length of the single-pass forward: the longest of 64 / 32 / 16 steps whose shared
 // memory lets four CTAs share an SM, else the shortest that fits at all.
-template <typename TB>
+template <typename TX, typename TB>
 int fused_chunk(const MimoParams& p) {
   for (int q : {64, 32, 16})
-    if (fused_smem(q, p.P, p.R, p.D, (int)sizeof(TB)).total <= 55u * 1024u) return q;
-  return fused_smem(16, p.P, p.R, p.D, (int)sizeof(TB)).total <= 200u * 1024u ? 16 : 0;
+    if (fused_smem(q, p.P, p.R, p.D, (int)sizeof(TB), (int)sizeof(TX)).total <= 55u * 1024u) return q;
+  return fused_smem(16, p.P, p.R, p.D, (int)sizeof(TB), (int)sizeof(TX)).total <= 200u * 1024u ? 16 : 0;
 }
 
+template <typename TB> constexpr CUtensorMapDataType tmap_type();
+template <> constexpr CUtensorMapDataType tmap_type<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+template <> constexpr CUtensorMapDataType tmap_type<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
+template <> constexpr CUtensorMapDataType tmap_type<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
+
+// 5-d map over (d, h, r, t, b) of a (B, L, R, H, D) tensor with a (D, 1, R, rows, 1) box,
+// no swizzle: the box lands in shared memory as [t][r][d].
+template <typename TB>
+bool make_bc_map(CUtensorMap* m, const void* base, const MimoParams& p, const Str4& st, int rows) {
+  auto enc = chunk_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t eb = sizeof(TB);
+  cuuint64_t dims[5] = {(cuuint64_t)p.D, (cuuint64_t)p.H, (cuuint64_t)p.R, (cuuint64_t)p.L, (cuuint64_t)p.Bn};
+  cuuint64_t strides[4] = {(cuuint64_t)st.h * eb, (cuuint64_t)st.r * eb, (cuuint64_t)st.l * eb, (cuuint64_t)st.b * eb};
+  cuuint32_t box[5] = {(cuuint32_t)p.D, 1, (cuuint32_t)p.R, (cuuint32_t)rows, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return enc(m, tmap_type<TB>(), 5, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 4-d map over (p, h, t, b) of a (B, L, H, P) tensor with a (P, 1, rows, 1) box: [t][p].
+template <typename TX>
+bool make_x_map(CUtensorMap* m, const MimoParams& p, int rows) {
+  auto enc = chunk_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t ex = sizeof(TX);
+  cuuint64_t dims[4] = {(cuuint64_t)p.P, (cuuint64_t)p.H, (cuuint64_t)p.L, (cuuint64_t)p.Bn};
+  cuuint64_t strides[3] = {(cuuint64_t)p.sx.h * ex, (cuuint64_t)p.sx.l * ex, (cuuint64_t)p.sx.b * ex};
+  cuuint32_t box[4] = {(cuuint32_t)p.P, 1, (cuuint32_t)rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, tmap_type<TX>(), 4, const_cast<void*>(p.x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Returns M3_ERR_UNSUPPORTED (nothing launched) when a tensor map cannot be made.
 template <typename TX, typename TB, int Q>
 int run_fused(const MimoParams& p, void* ws, cudaStream_t s) {
   const int64_t nch = (p.L + Q - 1) / Q, units = (int64_t)p.Bn * p.H, cells = units * nch;
-  if (cells >= INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "mimo scan: too many chunks for the grid");
-  const FusedWs w = fused_ws(ws, cells, p.D);
-  const size_t smem = fused_smem(Q, p.P, p.R, p.D, (int)sizeof(TB)).total;
+  if (cells >= INT32_MAX) return M3_ERR_UNSUPPORTED;
+  CUtensorMap mB, mC, mX;
+  if (!make_bc_map<TB>(&mB, p.Bm, p, p.sB, Q + 1) || !make_bc_map<TB>(&mC, p.Cm, p, p.sC, Q) ||
+      !make_x_map<TX>(&mX, p, Q + 1))
+    return M3_ERR_UNSUPPORTED;
+  FusedArgs f;
+  f.fP4 = make_fastdiv((uint32_t)(p.P / 4));
+  f.fD4 = make_fastdiv((uint32_t)(p.D / 4));
+  f.fR = make_fastdiv((uint32_t)p.R);
+  f.fU = make_fastdiv((uint32_t)units);
+  f.fH = make_fastdiv((uint32_t)p.H);
+  f.nch = (int)nch;
+  f.units = (int)units;
+  {
+    const int64_t ey = sizeof(TX);
+    f.yvec = reinterpret_cast<uintptr_t>(p.y) % 16 == 0 && (p.sy.b * ey) % 16 == 0 && (p.sy.l * ey) % 16 == 0 &&
+             (p.sy.h * ey) % 16 == 0;
+  }
+  char* w = static_cast<char*>(ws);
+  f.ticket = reinterpret_cast<unsigned*>(w);
+  f.rec = reinterpret_cast<unsigned long long*>(w + 16);
+  f.arec = f.rec + cells * p.D;
+  const size_t smem = fused_smem(Q, p.P, p.R, p.D, (int)sizeof(TB), (int)sizeof(TX)).total;
   M3_TRY(opt_in(mimo_fused_fwd_kernel<TX, TB, Q>, smem));
-  cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)fused_flag_bytes(cells), s);
+  // all of the unified L1 / shared array as shared memory, so that the CTAs that the
+  // registers allow are not limited by the carveout
+  cudaFuncSetAttribute(mimo_fused_fwd_kernel<TX, TB, Q>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  int per_sm = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mimo_fused_fwd_kernel<TX, TB, Q>, kFT, smem) != cudaSuccess)
+    per_sm = 1;
+  if (device_sm_count(&sms) != M3_OK) sms = 148;
+  f.ahead = std::max(1, per_sm * sms);
+  cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)fused_ws_bytes(cells, p.D), s);
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
-  mimo_fused_fwd_kernel<TX, TB, Q><<<(unsigned)cells, kFT, smem, s>>>(p, w, (int)nch, (int)units);
+  mimo_fused_fwd_kernel<TX, TB, Q><<<(unsigned)cells, kFT, smem, s>>>(mB, mC, mX, p, f);
   return check_launch("mimo_fused_fwd_kernel");
 }
 
 template <typename TX, typename TB>
 int run_chunked(const MimoParams& p, void* ws_raw, cudaStream_t s) {
-  if (fused_applies<TB>(p)) {
-    switch (fused_chunk<TB>(p)) {
-      case 64: return run_fused<TX, TB, 64>(p, ws_raw, s);
-      case 32: return run_fused<TX, TB, 32>(p, ws_raw, s);
-      case 16: return run_fused<TX, TB, 16>(p, ws_raw, s);
+  if (fused_applies<TX, TB>(p)) {
+    int rc = M3_ERR_UNSUPPORTED;
+    switch (fused_chunk<TX, TB>(p)) {
+      case 64: rc = run_fused<TX, TB, 64>(p, ws_raw, s); break;
+      case 32: rc = run_fused<TX, TB, 32>(p, ws_raw, s); break;
+      case 16: rc = run_fused<TX, TB, 16>(p, ws_raw, s); break;
       default: break;
     }
+    if (rc != M3_ERR_UNSUPPORTED) return rc;
   }
   float* ws = static_cast<float*>(ws_raw);
   const int nch = (p.L + kTcF - 1) / kTcF;
