@@ -557,16 +557,6 @@ __device__ __forceinline__ int fdiv(int x, FastDiv f) {
   return (int)((__umulhi((uint32_t)x, f.m) + (uint32_t)x) >> f.s);
 }
 
-struct FusedArgs {
-  FastDiv fP4, fD4, fR, fU, fH;  // divisors headdim / 4, d_state / 4, rank, units, heads
-  int nch, units;
-  int ahead;  // CTAs resident on the device: a CTA prefetches the chunk of ticket + ahead into L2
-  int yvec;   // y rows start on 16-byte boundaries: four outputs per store
-  unsigned* ticket;
-  unsigned long long* rec;   // [unit][chunk][d]: S or I value | status << 32
-  unsigned long long* arec;  // [unit][chunk]: A value | 1 << 32
-};
-
 // Workspace of the single-pass forward: the ticket counter, then the value words and the
 // decay words, all cleared before every launch.
 inline int64_t fused_ws_bytes(int64_t cells, int64_t D) { return 16 + 8 * cells * (D + 1); }
@@ -598,6 +588,17 @@ __host__ __device__ inline FusedSmem fused_smem(int Q, int P, int R, int D, int 
   L.total = o + 128;  // slack for aligning the dynamic shared-memory base
   return L;
 }
+
+struct FusedArgs {
+  FastDiv fP4, fD4, fR, fU, fH;  // divisors headdim / 4, d_state / 4, rank, units, heads
+  int nch, units;
+  int ahead;  // CTAs resident on the device: a CTA prefetches the chunk of ticket + ahead into L2
+  int yvec;   // y rows start on 16-byte boundaries: four outputs per store
+  FusedSmem L;  // shared-memory layout (computed on the host)
+  unsigned* ticket;
+  unsigned long long* rec;   // [unit][chunk][d]: S or I value | status << 32
+  unsigned long long* arec;  // [unit][chunk]: A value | 1 << 32
+};
 
 __device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long* p) {
   unsigned long long v;
@@ -689,7 +690,7 @@ __global__ void __launch_bounds__(kFT)
   unsigned char* fsm = fsm_raw + ((128u - (sm100::smem_u32(fsm_raw) & 127u)) & 127u);
   const int P = a.P, R = a.R, D = a.D, tid = threadIdx.x, lane = tid & 31;
   const int P4 = P >> 2, D4 = D >> 2, MS = P + 4;
-  const FusedSmem L = fused_smem(Q, P, R, D, (int)sizeof(TB), (int)sizeof(TX));
+  const FusedSmem& L = f.L;
   uint64_t* barB = reinterpret_cast<uint64_t*>(fsm);
   uint64_t* barC = barB + 1;
   int* tk_s = reinterpret_cast<int*>(fsm + 16);
@@ -764,7 +765,7 @@ __global__ void __launch_bounds__(kFT)
     const TX* xrow = xs + row * P;
     const float* mrow = mx + k * MS;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int pb = row % P4;
+    int pb = row - fdiv(row, f.fP4) * P4;
     for (int e = 0; e < P4; ++e) {
       fma4(acc, ld4f(xrow + 4 * pb), ld4f(mrow + 4 * pb));
       pb = pb + 1 == P4 ? 0 : pb + 1;
@@ -848,7 +849,7 @@ __global__ void __launch_bounds__(kFT)
     const TB* crow = Cs + (size_t)it * D;
     const float* hrow = hs + (size_t)t * D;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int k = lane % D4;
+    int k = lane - fdiv(lane, f.fD4) * D4;
 #pragma unroll 4
     for (int e = 0; e < D4; ++e) {
       fma4(acc, ld4f(crow + 4 * k), ld4f(hrow + 4 * k));
@@ -971,7 +972,8 @@ int run_fused(const MimoParams& p, void* ws, cudaStream_t s) {
   f.ticket = reinterpret_cast<unsigned*>(w);
   f.rec = reinterpret_cast<unsigned long long*>(w + 16);
   f.arec = f.rec + cells * p.D;
-  const size_t smem = fused_smem(Q, p.P, p.R, p.D, (int)sizeof(TB), (int)sizeof(TX)).total;
+  f.L = fused_smem(Q, p.P, p.R, p.D, (int)sizeof(TB), (int)sizeof(TX));
+  const size_t smem = f.L.total;
   M3_TRY(opt_in(mimo_fused_fwd_kernel<TX, TB, Q>, smem));
   // all of the unified L1 / shared array as shared memory, so that the CTAs that the
   // registers allow are not limited by the carveout
