@@ -839,7 +839,8 @@ int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const 
 
 size_t m3_layer_prologue_bwd_workspace_size(const m3_layer_dims* dims, int64_t batch, int64_t seqlen) {
   if (!dims || batch < 0 || seqlen < 0) return 0;
-  return prologue_bwd_workspace_bytes(batch, seqlen, dims->nheads, dims->num_rope_angles);
+  return prologue_bwd_workspace_bytes(batch, seqlen, dims->nheads, dims->num_rope_angles, dims->mimo_rank,
+                                      dims->d_state);
 }
 
 int m3_layer_prologue_bwd(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
@@ -890,7 +891,7 @@ int m3_layer_prologue_bwd(const m3_layer_dims* dims, const m3_tensor* zxbcdt, co
     return memset_async(d_C_norm_w->data, sizeof(float) * Ds, s, "d_C_norm_w");
   }
   if (Bn > INT32_MAX || L > INT32_MAX) return fail(M3_ERR_UNSUPPORTED, "prologue backward: dimension too large");
-  const size_t need = prologue_bwd_workspace_bytes(Bn, L, H, S);
+  const size_t need = prologue_bwd_workspace_bytes(Bn, L, H, S, R, Ds);
   if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15) != 0)
     return fail(M3_ERR_WORKSPACE, "prologue backward: workspace of " + std::to_string(need) + " bytes required");
   PrologueBwdParams p{};

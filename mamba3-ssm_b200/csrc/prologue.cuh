@@ -47,6 +47,7 @@ struct PrologueBwdParams {
   float* dB_norm_w; float* dC_norm_w;        // (D), overwritten
   float* ddt_bias;                           // (H), overwritten
   float* dtheta; float* dDT_ang; float* dangle_raw;  // scratch
+  float* bc_part;  // scratch: the bc kernel's per-CTA partial sums
 };
 
 struct GateBwdParams {
@@ -60,7 +61,7 @@ struct GateBwdParams {
 };
 
 int launch_prologue(const PrologueParams& p, int zdt, int odt, cudaStream_t s);
-size_t prologue_bwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t S);
+size_t prologue_bwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t S, int64_t R, int64_t D);
 int launch_prologue_bwd(const PrologueBwdParams& p, float* ws, int zdt, int odt, cudaStream_t s);
 int launch_gate_bwd(const GateBwdParams& p, int ydt, int zdt, int ddt, cudaStream_t s);
 int launch_gate(const GateParams& p, int ydt, int zdt, int odt, cudaStream_t s);

@@ -8,11 +8,12 @@
 //       dv        = rot_theta^T(dB_proj)             the gradient before the rotation
 //       dtheta_i += -dv1' o2 + dv2' o1               over B and C (dv' = dB_proj), ranks summed in
 //                                                    shared memory, one write per (b, l, h, i)
-//       dbias    += dv                               summed over the tile in shared memory,
-//                                                    then atomics per CTA
+//       dbias    += dv                               summed over the CTA's rows in shared memory,
+//                                                    then a workspace slot per CTA
 //       dn        = sum_h dv (one group) / dv (group per head)
 //       draw      = (w dn) / rms - raw sum_d(w dn raw) / (D rms^3)   into d zxbcdt
-//       dw       += dn raw / rms                     registers, then atomics per CTA
+//       dw       += dn raw / rms                     registers, then the CTA's slot
+//   reduce kernel: the slots summed (a thread per output, 64 slots each, one atomic each)
 //   angle kernel (CTA per (b, h), tiles of 128 steps from the end): q = suffix sums over l
 //     of dtheta; dDT_ang[b,l,h] = sum_i q angle_raw[b,l,i]; dangle_raw[b,l,i] += q DT[b,l,h]
 //     (atomics over heads into an fp32 buffer)
@@ -21,6 +22,8 @@
 //     dt_bias) into d zxbcdt (dt column), the trap logit's gradient into its column, and the
 //     dt_bias gradient (block sums, then atomics); the angle_raw columns from the fp32 buffer
 //   gate kernel: dy = dout silu(z), dz = dout y silu'(z)
+#include <algorithm>
+
 #include "m3_common.cuh"
 #include "prologue.cuh"
 
@@ -75,8 +78,10 @@ __global__ void __launch_bounds__(256) prologue_bwd_bc_kernel(PrologueBwdParams 
     wc0[j] = a.C_norm_w[2 * k]; wc1[j] = a.C_norm_w[2 * k + 1];
     dwb0[j] = dwb1[j] = dwc0[j] = dwc1[j] = 0.f;
   }
+  const int64_t ntiles = (nrows + kRowsBC - 1) / kRowsBC;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x)
   for (int t = 0; t < kRowsBC; ++t) {
-    const int64_t rowo = (int64_t)blockIdx.x * kRowsBC + t;  // b * L + l
+    const int64_t rowo = tile * kRowsBC + t;  // b * L + l
     const bool rv = rowo < nrows;                              // uniform over the CTA
     if (rv) {
       const int64_t b = rowo / a.L, l = rowo - b * a.L;
@@ -85,88 +90,110 @@ __global__ void __launch_bounds__(256) prologue_bwd_bc_kernel(PrologueBwdParams 
       float rb0[PPL], rb1[PPL], rc0[PPL], rc1[PPL];  // raw group rows
       float rsb = 0.f, rsc = 0.f;                    // 1 / rms
       float db0[PPL], db1[PPL], dc0[PPL], dc1[PPL];  // dn (sum over the group's heads)
-      for (int h = 0; h < H; ++h) {
-        const int g = G == 1 ? 0 : h;
-        if (h == 0 || G != 1) {
-          const TZ* sb = zrow + (int64_t)(r * G + g) * D;
-          const TZ* sc = sb + RGD;
-          float ssb = 0.f, ssc = 0.f;
+      // heads in batches of kHB: the batch's gradient pairs and angles are loaded into
+      // registers before any of them is used, so their latencies overlap
+      constexpr int kHB = 8 / PPL;
+      for (int h0 = 0; h0 < H; h0 += kHB) {
+        float2 gbv[kHB][PPL], gcv[kHB][PPL];
+        float angv[kHB][PPL];
+#pragma unroll
+        for (int hh = 0; hh < kHB; ++hh) {
+          const int h = h0 + hh;
+          const TO* gB = reinterpret_cast<const TO*>(a.dBp) + ((rowo * R + r) * H + h) * D;
+          const TO* gC = reinterpret_cast<const TO*>(a.dCp) + ((rowo * R + r) * H + h) * D;
+          const float* ang = a.angles + (rowo * H + h) * S;
 #pragma unroll
           for (int j = 0; j < PPL; ++j) {
             const int k = lane + 32 * j;
-            const bool v = k < half;
-            rb0[j] = v ? to_f32(sb[2 * k]) : 0.f; rb1[j] = v ? to_f32(sb[2 * k + 1]) : 0.f;
-            rc0[j] = v ? to_f32(sc[2 * k]) : 0.f; rc1[j] = v ? to_f32(sc[2 * k + 1]) : 0.f;
-            ssb = fmaf(rb0[j], rb0[j], fmaf(rb1[j], rb1[j], ssb));
-            ssc = fmaf(rc0[j], rc0[j], fmaf(rc1[j], rc1[j], ssc));
-            db0[j] = db1[j] = dc0[j] = dc1[j] = 0.f;
+            const bool v = h < H && k < half;
+            gbv[hh][j] = v ? ld_pair(gB + 2 * k) : make_float2(0.f, 0.f);
+            gcv[hh][j] = v ? ld_pair(gC + 2 * k) : make_float2(0.f, 0.f);
+            angv[hh][j] = v && k < npair ? __ldg(ang + k) : 0.f;
           }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            ssb += __shfl_xor_sync(0xffffffffu, ssb, o);
-            ssc += __shfl_xor_sync(0xffffffffu, ssc, o);
-          }
-          rsb = 1.0f / sqrtf(ssb / (float)D + a.eps);
-          rsc = 1.0f / sqrtf(ssc / (float)D + a.eps);
         }
-        const float* bb = a.B_bias + ((int64_t)h * R + r) * D;
-        const float* cb = a.C_bias + ((int64_t)h * R + r) * D;
-        const float* ang = a.angles + (rowo * H + h) * S;
-        const TO* gB = reinterpret_cast<const TO*>(a.dBp) + ((rowo * R + r) * H + h) * D;
-        const TO* gC = reinterpret_cast<const TO*>(a.dCp) + ((rowo * R + r) * H + h) * D;
-        float* sbBh = sbB + ((int64_t)h * R + r) * D;
-        float* sbCh = sbC + ((int64_t)h * R + r) * D;
 #pragma unroll
-        for (int j = 0; j < PPL; ++j) {
-          const int k = lane + 32 * j;
-          if (k < half) {
-            const int d0 = 2 * k;
-            float2 gb = ld_pair(gB + d0), gc = ld_pair(gC + d0);
-            if (k < npair) {
-              // o = rot(v) with v = n + bias; dtheta = -g1 o2 + g2 o1; dv = rot^T(g)
-              const float2 bv = __ldg(reinterpret_cast<const float2*>(bb + d0));
-              const float2 cv = __ldg(reinterpret_cast<const float2*>(cb + d0));
-              const float x0 = rb0[j] * rsb * wb0[j] + bv.x, x1 = rb1[j] * rsb * wb1[j] + bv.y;
-              const float y0 = rc0[j] * rsc * wc0[j] + cv.x, y1 = rc1[j] * rsc * wc1[j] + cv.y;
-              float sn, cs;
-              sincos_reduced(ang[k], &sn, &cs);
-              const float ob0 = x0 * cs - x1 * sn, ob1 = x0 * sn + x1 * cs;
-              const float oc0 = y0 * cs - y1 * sn, oc1 = y0 * sn + y1 * cs;
-              const float dth = (-gb.x * ob1 + gb.y * ob0) + (-gc.x * oc1 + gc.y * oc0);
-              atomicAdd(&sang[h * S + k], dth);  // ranks of the row add up
-              gb = make_float2(gb.x * cs + gb.y * sn, -gb.x * sn + gb.y * cs);
-              gc = make_float2(gc.x * cs + gc.y * sn, -gc.x * sn + gc.y * cs);
+        for (int hh = 0; hh < kHB; ++hh) {
+          const int h = h0 + hh;
+          if (h >= H) break;
+          const int g = G == 1 ? 0 : h;
+          if (h == 0 || G != 1) {
+            const TZ* sb = zrow + (int64_t)(r * G + g) * D;
+            const TZ* sc = sb + RGD;
+            float ssb = 0.f, ssc = 0.f;
+#pragma unroll
+            for (int j = 0; j < PPL; ++j) {
+              const int k = lane + 32 * j;
+              const bool v = k < half;
+              rb0[j] = v ? to_f32(sb[2 * k]) : 0.f; rb1[j] = v ? to_f32(sb[2 * k + 1]) : 0.f;
+              rc0[j] = v ? to_f32(sc[2 * k]) : 0.f; rc1[j] = v ? to_f32(sc[2 * k + 1]) : 0.f;
+              ssb = fmaf(rb0[j], rb0[j], fmaf(rb1[j], rb1[j], ssb));
+              ssc = fmaf(rc0[j], rc0[j], fmaf(rc1[j], rc1[j], ssc));
+              db0[j] = db1[j] = dc0[j] = dc1[j] = 0.f;
             }
-            sbBh[d0] += gb.x; sbBh[d0 + 1] += gb.y;  // warp r owns (h, r, :)
-            sbCh[d0] += gc.x; sbCh[d0 + 1] += gc.y;
-            db0[j] += gb.x; db1[j] += gb.y;
-            dc0[j] += gc.x; dc1[j] += gc.y;
-          }
-        }
-        if (h == H - 1 || G != 1) {
-          // RMSNorm backward of group (r, g): draw = (w dn)/rms - raw sum(w dn raw)/(D rms^3)
-          float pb = 0.f, pc = 0.f;
 #pragma unroll
-          for (int j = 0; j < PPL; ++j) {
-            pb = fmaf(wb0[j] * db0[j], rb0[j], fmaf(wb1[j] * db1[j], rb1[j], pb));
-            pc = fmaf(wc0[j] * dc0[j], rc0[j], fmaf(wc1[j] * dc1[j], rc1[j], pc));
+            for (int o = 16; o > 0; o >>= 1) {
+              ssb += __shfl_xor_sync(0xffffffffu, ssb, o);
+              ssc += __shfl_xor_sync(0xffffffffu, ssc, o);
+            }
+            rsb = 1.0f / sqrtf(ssb / (float)D + a.eps);
+            rsc = 1.0f / sqrtf(ssc / (float)D + a.eps);
           }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            pb += __shfl_xor_sync(0xffffffffu, pb, o);
-            pc += __shfl_xor_sync(0xffffffffu, pc, o);
-          }
-          const float kb = pb * rsb * rsb * rsb / (float)D, kc = pc * rsc * rsc * rsc / (float)D;
-          TZ* ob = drow + (int64_t)(r * G + g) * D;
-          TZ* oc = ob + RGD;
+          const float* bb = a.B_bias + ((int64_t)h * R + r) * D;
+          const float* cb = a.C_bias + ((int64_t)h * R + r) * D;
+          float* sbBh = sbB + ((int64_t)h * R + r) * D;
+          float* sbCh = sbC + ((int64_t)h * R + r) * D;
 #pragma unroll
           for (int j = 0; j < PPL; ++j) {
             const int k = lane + 32 * j;
             if (k < half) {
-              st_pair2(ob + 2 * k, wb0[j] * db0[j] * rsb - rb0[j] * kb, wb1[j] * db1[j] * rsb - rb1[j] * kb);
-              st_pair2(oc + 2 * k, wc0[j] * dc0[j] * rsc - rc0[j] * kc, wc1[j] * dc1[j] * rsc - rc1[j] * kc);
-              dwb0[j] = fmaf(db0[j], rb0[j] * rsb, dwb0[j]); dwb1[j] = fmaf(db1[j], rb1[j] * rsb, dwb1[j]);
-              dwc0[j] = fmaf(dc0[j], rc0[j] * rsc, dwc0[j]); dwc1[j] = fmaf(dc1[j], rc1[j] * rsc, dwc1[j]);
+              const int d0 = 2 * k;
+              float2 gb = gbv[hh][j], gc = gcv[hh][j];
+              if (k < npair) {
+                // o = rot(v) with v = n + bias; dtheta = -g1 o2 + g2 o1; dv = rot^T(g)
+                const float2 bv = __ldg(reinterpret_cast<const float2*>(bb + d0));
+                const float2 cv = __ldg(reinterpret_cast<const float2*>(cb + d0));
+                const float x0 = rb0[j] * rsb * wb0[j] + bv.x, x1 = rb1[j] * rsb * wb1[j] + bv.y;
+                const float y0 = rc0[j] * rsc * wc0[j] + cv.x, y1 = rc1[j] * rsc * wc1[j] + cv.y;
+                float sn, cs;
+                sincos_reduced(angv[hh][j], &sn, &cs);
+                const float ob0 = x0 * cs - x1 * sn, ob1 = x0 * sn + x1 * cs;
+                const float oc0 = y0 * cs - y1 * sn, oc1 = y0 * sn + y1 * cs;
+                const float dth = (-gb.x * ob1 + gb.y * ob0) + (-gc.x * oc1 + gc.y * oc0);
+                atomicAdd(&sang[h * S + k], dth);  // ranks of the row add up
+                gb = make_float2(gb.x * cs + gb.y * sn, -gb.x * sn + gb.y * cs);
+                gc = make_float2(gc.x * cs + gc.y * sn, -gc.x * sn + gc.y * cs);
+              }
+              sbBh[d0] += gb.x; sbBh[d0 + 1] += gb.y;  // warp r owns (h, r, :)
+              sbCh[d0] += gc.x; sbCh[d0 + 1] += gc.y;
+              db0[j] += gb.x; db1[j] += gb.y;
+              dc0[j] += gc.x; dc1[j] += gc.y;
+            }
+          }
+          if (h == H - 1 || G != 1) {
+            // RMSNorm backward of group (r, g): draw = (w dn)/rms - raw sum(w dn raw)/(D rms^3)
+            float pb = 0.f, pc = 0.f;
+#pragma unroll
+            for (int j = 0; j < PPL; ++j) {
+              pb = fmaf(wb0[j] * db0[j], rb0[j], fmaf(wb1[j] * db1[j], rb1[j], pb));
+              pc = fmaf(wc0[j] * dc0[j], rc0[j], fmaf(wc1[j] * dc1[j], rc1[j], pc));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              pb += __shfl_xor_sync(0xffffffffu, pb, o);
+              pc += __shfl_xor_sync(0xffffffffu, pc, o);
+            }
+            const float kb = pb * rsb * rsb * rsb / (float)D, kc = pc * rsc * rsc * rsc / (float)D;
+            TZ* ob = drow + (int64_t)(r * G + g) * D;
+            TZ* oc = ob + RGD;
+#pragma unroll
+            for (int j = 0; j < PPL; ++j) {
+              const int k = lane + 32 * j;
+              if (k < half) {
+                st_pair2(ob + 2 * k, wb0[j] * db0[j] * rsb - rb0[j] * kb, wb1[j] * db1[j] * rsb - rb1[j] * kb);
+                st_pair2(oc + 2 * k, wc0[j] * dc0[j] * rsc - rc0[j] * kc, wc1[j] * dc1[j] * rsc - rc1[j] * kc);
+                dwb0[j] = fmaf(db0[j], rb0[j] * rsb, dwb0[j]); dwb1[j] = fmaf(db1[j], rb1[j] * rsb, dwb1[j]);
+                dwc0[j] = fmaf(dc0[j], rc0[j] * rsc, dwc0[j]); dwc1[j] = fmaf(dc1[j], rc1[j] * rsc, dwc1[j]);
+              }
             }
           }
         }
@@ -182,7 +209,9 @@ __global__ void __launch_bounds__(256) prologue_bwd_bc_kernel(PrologueBwdParams 
     }
     __syncthreads();
   }
-  // tile partials to global: bias gradients (H, R, D) and the norm-weight gradients (D)
+  // the CTA's partials into its workspace slot: bias gradients (H, R, D) of B and C, then
+  // the norm-weight gradients (D) of B and C (summed over the ranks); plain stores, summed
+  // over the slots by bc_reduce_kernel
 #pragma unroll
   for (int j = 0; j < PPL; ++j) {
     const int k = lane + 32 * j;
@@ -192,19 +221,41 @@ __global__ void __launch_bounds__(256) prologue_bwd_bc_kernel(PrologueBwdParams 
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < HRD; i += blockDim.x) {
-    atomicAdd(a.dB_bias + i, sbB[i]);
-    atomicAdd(a.dC_bias + i, sbC[i]);
-  }
+  float* slot = a.bc_part + (int64_t)blockIdx.x * (2 * HRD + 2 * D);
+  for (int i = threadIdx.x; i < 2 * HRD; i += blockDim.x) slot[i] = sm[i];
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float sb = 0.f, sc = 0.f;
     for (int rr = 0; rr < R; ++rr) {
       sb += swb[rr * D + d];
       sc += swc[rr * D + d];
     }
-    atomicAdd(a.dB_norm_w + d, sb);
-    atomicAdd(a.dC_norm_w + d, sc);
+    slot[2 * HRD + d] = sb;
+    slot[2 * HRD + D + d] = sc;
   }
+}
+
+// Sum of the bc kernel's workspace slots: thread = output (B bias, C bias, B norm weight, C
+// norm weight, in slot order), grid.y = groups of kSlotsPerThread slots, one atomic per
+// (output, group) into outputs cleared beforehand.
+constexpr int kSlotsPerThread = 64;
+__global__ void __launch_bounds__(256) bc_reduce_kernel(PrologueBwdParams a, int nslots) {
+  const int HRD = a.H * a.R * a.D, W = 2 * HRD + 2 * a.D;
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= W) return;
+  const int s0 = blockIdx.y * kSlotsPerThread, s1 = min(s0 + kSlotsPerThread, nslots);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int sl = s0;
+  for (; sl + 4 <= s1; sl += 4) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] += a.bc_part[(int64_t)(sl + k) * W + o];
+  }
+  for (; sl < s1; ++sl) acc[0] += a.bc_part[(int64_t)sl * W + o];
+  const float v = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  float* dst = o < HRD ? a.dB_bias + o
+               : o < 2 * HRD ? a.dC_bias + (o - HRD)
+               : o < 2 * HRD + a.D ? a.dB_norm_w + (o - 2 * HRD)
+                                   : a.dC_norm_w + (o - 2 * HRD - a.D);
+  atomicAdd(dst, v);
 }
 
 // CTA per (b, h); thread = step of a 128-step tile walked from the end; suffix sums over l
@@ -336,9 +387,18 @@ __global__ void __launch_bounds__(256) gate_bwd_kernel(GateBwdParams a) {
 
 }  // namespace
 
-size_t prologue_bwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t S) {
-  // dtheta (B, L, H, S), dDT_ang (B, L, H), dangle_raw (B, L, S), all fp32
-  return sizeof(float) * (size_t)(Bn * L * (H * S + H + S));
+// Slots of the bc kernel's partial sums: one per CTA, at most 1024 and at most 32 MB.
+int64_t bc_slots(int64_t rows, int64_t H, int64_t R, int64_t D) {
+  const int64_t W = 2 * H * R * D + 2 * D;
+  const int64_t cap = std::max<int64_t>(1, std::min<int64_t>(1024, (int64_t(32) << 20) / (4 * W)));
+  return std::max<int64_t>(1, std::min<int64_t>((rows + kRowsBC - 1) / kRowsBC, cap));
+}
+
+size_t prologue_bwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t S, int64_t R, int64_t D) {
+  // dtheta (B, L, H, S), dDT_ang (B, L, H), dangle_raw (B, L, S), then the bc kernel's
+  // partial-sum slots, all fp32
+  const int64_t rows = Bn * L;
+  return sizeof(float) * (size_t)(rows * (H * S + H + S) + bc_slots(rows, H, R, D) * (2 * H * R * D + 2 * D));
 }
 
 int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt, cudaStream_t s) {
@@ -351,6 +411,9 @@ int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt
   p.dtheta = ws;
   p.dDT_ang = ws + rows * p.H * p.S;
   p.dangle_raw = p.dDT_ang + rows * p.H;
+  p.bc_part = p.dangle_raw + rows * p.S;
+  const int64_t nslots = bc_slots(rows, p.H, p.R, p.D);
+  const int W = 2 * p.H * p.R * p.D + 2 * p.D;
   const size_t zero_bytes = sizeof(float) * (size_t)(rows * p.S);
   cudaError_t e = cudaMemsetAsync(p.dangle_raw, 0, zero_bytes, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(p.dB_bias, 0, sizeof(float) * (size_t)p.H * p.R * p.D, s);
@@ -361,7 +424,7 @@ int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("prologue backward memset: ") + cudaGetErrorString(e));
   const size_t smem = sizeof(float) * (size_t)(2 * p.H * p.R * p.D + p.H * p.S + 2 * p.R * p.D);
   if (smem > 200 * 1024) return fail(M3_ERR_UNSUPPORTED, "prologue backward: nheads * rank * d_state too large");
-  const unsigned gbc = (unsigned)((rows + kRowsBC - 1) / kRowsBC);
+  const unsigned gbc = (unsigned)nslots;
   const int ppl = (p.D / 2 + 31) / 32;
   const unsigned gdt = (unsigned)((rows * p.H + 255) / 256);
 #define M3_PBWD(TZ, TO)                                                                                  \
@@ -374,6 +437,9 @@ int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt
     }                                                                                                    \
     kbc<<<gbc, 32 * p.R, smem, s>>>(p);                                                                  \
     M3_TRY(check_launch("prologue_bwd_bc_kernel"));                                                      \
+    bc_reduce_kernel<<<dim3((unsigned)((W + 255) / 256), (unsigned)((nslots + kSlotsPerThread - 1) / kSlotsPerThread)), \
+                       256, 0, s>>>(p, (int)nslots);                                                      \
+    M3_TRY(check_launch("bc_reduce_kernel"));                                                            \
     prologue_bwd_angle_kernel<TZ><<<(unsigned)(p.Bn * p.H), kAT, 0, s>>>(p);                             \
     M3_TRY(check_launch("prologue_bwd_angle_kernel"));                                                   \
     prologue_bwd_dt_kernel<TZ><<<gdt, 256, 0, s>>>(p);                                                   \
