@@ -221,6 +221,28 @@ int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
                      m3_tensor* dmimo_o, m3_tensor* dh0, m3_tensor* dbx0, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* MIMO backward from the forward's workspace: same operands and results as
+ * m3_mimo_scan_bwd, plus the device workspace a preceding m3_mimo_scan_fwd_ws call filled
+ * with the same inputs (x, B, C, ADT, DT, trap, D, mimo_x, h0, bx0). Where that forward ran
+ * its single-pass kernel, the backward is one pass too: it reads the forward's published
+ * chunk-end states instead of recomputing the forward, finds each chunk's adjoint carry by
+ * looking ahead over the chunks after it, and reads x, B, C and dy once (TMA boxes).
+ * Otherwise (inputs the TMA cannot describe, fwd_workspace NULL or too small) it runs the
+ * m3_mimo_scan_bwd kernels. workspace: at least m3_mimo_scan_bwd_ws_workspace_size(...)
+ * bytes, 16-byte aligned. Same reference path as m3_mimo_scan_bwd (the gradients of
+ * ops.py:226-240). */
+size_t m3_mimo_scan_bwd_ws_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads,
+                                          int64_t headdim, int64_t dstate, int64_t rank);
+int m3_mimo_scan_bwd_ws(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
+                        const m3_tensor* ADT, const m3_tensor* DT, const m3_tensor* trap,
+                        const m3_tensor* D, const m3_tensor* mimo_x, const m3_tensor* mimo_o,
+                        const m3_tensor* h0, const m3_tensor* bx0, const m3_tensor* dy,
+                        m3_tensor* dx, m3_tensor* dB, m3_tensor* dC, m3_tensor* dADT,
+                        m3_tensor* dDT, m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dmimo_x,
+                        m3_tensor* dmimo_o, m3_tensor* dh0, m3_tensor* dbx0,
+                        const void* fwd_workspace, size_t fwd_workspace_bytes, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Single-token decode step of one Mamba3 mixer, everything between in_proj and out_proj
  * of Mamba3.step (layer.py:298-371) in one kernel: split of the in_proj row, softplus /

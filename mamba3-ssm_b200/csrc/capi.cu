@@ -1,5 +1,6 @@
 // extern "C" entry points of libmamba3_b200: argument validation, dispatch to the
 // kernels, and the thread-local error string. Nothing here allocates device memory.
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <mutex>
@@ -569,12 +570,13 @@ size_t m3_mimo_scan_bwd_workspace_size(int64_t batch, int64_t seqlen, int64_t nh
   return sizeof(float) * mimo_bwd_workspace_floats(batch, seqlen, nheads, headdim, dstate, rank);
 }
 
-int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
-                     const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* mimo_x,
-                     const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, const m3_tensor* dy,
-                     m3_tensor* dx, m3_tensor* dB, m3_tensor* dC, m3_tensor* dADT, m3_tensor* dDT,
-                     m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dmimo_x, m3_tensor* dmimo_o, m3_tensor* dh0,
-                     m3_tensor* dbx0, void* workspace, size_t workspace_bytes, void* stream) {
+static int mimo_bwd_common(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                           const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* mimo_x,
+                           const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, const m3_tensor* dy,
+                           m3_tensor* dx, m3_tensor* dB, m3_tensor* dC, m3_tensor* dADT, m3_tensor* dDT,
+                           m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dmimo_x, m3_tensor* dmimo_o, m3_tensor* dh0,
+                           m3_tensor* dbx0, const void* fwd_workspace, size_t fwd_workspace_bytes, void* workspace,
+                           size_t workspace_bytes, void* stream) {
   MimoParams p{};
   int64_t d[6];
   M3_TRY(fill_mimo(p, x, B, C, ADT, DT, trap, D, mimo_x, mimo_o, h0, bx0, d));
@@ -604,12 +606,10 @@ int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
     M3_TRY(copy_or_zero(fptr<void>(dh0), nullptr, bytes, s, "dh0"));
     return copy_or_zero(fptr<void>(dbx0), nullptr, bytes, s, "dbx0");
   }
-  const size_t need = m3_mimo_scan_bwd_workspace_size(Bn, L, H, P, Ds, R);
-  if (need == 0) return fail(M3_ERR_UNSUPPORTED, "mimo backward: shapes too large for shared memory");
-  if (workspace == nullptr || workspace_bytes < need)
-    return fail(M3_ERR_WORKSPACE, "mimo backward: workspace of " + std::to_string(need) + " bytes required");
-  if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+  if (workspace && reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
     return fail(M3_ERR_INVALID_ARGUMENT, "mimo backward: workspace not 16-byte aligned");
+  if (fwd_workspace && reinterpret_cast<uintptr_t>(fwd_workspace) % 16 != 0)
+    return fail(M3_ERR_INVALID_ARGUMENT, "mimo backward: forward workspace not 16-byte aligned");
   p.dy = dy->data; p.sdy = s3(dy);
   p.dx = dx->data; p.sdx = s3(dx);
   p.dB = dB->data; p.sdB = s4(dB);
@@ -620,8 +620,47 @@ int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C,
   p.dD = fptr<float>(dD);
   p.dmx = fptr<float>(dmimo_x); p.dmo = fptr<float>(dmimo_o);
   p.dh0 = fptr<float>(dh0); p.dbx0 = fptr<float>(dbx0);
+  if (fwd_workspace) {
+    M3_TRY(check_device_ptr(fwd_workspace, "fwd_workspace"));
+    const int rc = launch_mimo_bwd_fused(p, x->dtype, B->dtype, fwd_workspace, fwd_workspace_bytes, workspace,
+                                         workspace_bytes, s);
+    if (rc != M3_ERR_UNSUPPORTED) return rc;
+  }
+  const size_t need = m3_mimo_scan_bwd_workspace_size(Bn, L, H, P, Ds, R);
+  if (need == 0) return fail(M3_ERR_UNSUPPORTED, "mimo backward: shapes too large for shared memory");
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(M3_ERR_WORKSPACE, "mimo backward: workspace of " + std::to_string(need) + " bytes required");
   p.work = reinterpret_cast<float*>(workspace);
   return launch_mimo(p, x->dtype, B->dtype, true, s);
+}
+
+int m3_mimo_scan_bwd(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                     const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* mimo_x,
+                     const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, const m3_tensor* dy,
+                     m3_tensor* dx, m3_tensor* dB, m3_tensor* dC, m3_tensor* dADT, m3_tensor* dDT,
+                     m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dmimo_x, m3_tensor* dmimo_o, m3_tensor* dh0,
+                     m3_tensor* dbx0, void* workspace, size_t workspace_bytes, void* stream) {
+  return mimo_bwd_common(x, B, C, ADT, DT, trap, D, mimo_x, mimo_o, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD,
+                         dmimo_x, dmimo_o, dh0, dbx0, nullptr, 0, workspace, workspace_bytes, stream);
+}
+
+size_t m3_mimo_scan_bwd_ws_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                                          int64_t dstate, int64_t rank) {
+  if (batch < 0 || seqlen < 0 || nheads < 0 || headdim < 0 || dstate < 0 || rank < 0) return 0;
+  return std::max(m3_mimo_scan_bwd_workspace_size(batch, seqlen, nheads, headdim, dstate, rank),
+                  mimo_bwd_fused_workspace_bytes(batch, seqlen, nheads, dstate));
+}
+
+int m3_mimo_scan_bwd_ws(const m3_tensor* x, const m3_tensor* B, const m3_tensor* C, const m3_tensor* ADT,
+                        const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* D, const m3_tensor* mimo_x,
+                        const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, const m3_tensor* dy,
+                        m3_tensor* dx, m3_tensor* dB, m3_tensor* dC, m3_tensor* dADT, m3_tensor* dDT,
+                        m3_tensor* dtrap, m3_tensor* dD, m3_tensor* dmimo_x, m3_tensor* dmimo_o, m3_tensor* dh0,
+                        m3_tensor* dbx0, const void* fwd_workspace, size_t fwd_workspace_bytes, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return mimo_bwd_common(x, B, C, ADT, DT, trap, D, mimo_x, mimo_o, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD,
+                         dmimo_x, dmimo_o, dh0, dbx0, fwd_workspace, fwd_workspace_bytes, workspace, workspace_bytes,
+                         stream);
 }
 
 static int step_common(bool mimo, const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,

@@ -503,11 +503,11 @@ __global__ void __launch_bounds__(kCT) mimo_bwd_full_kernel(MimoParams a, const 
 }
 
 // B4: add to every step's dADT the terms of all later chunks
-__global__ void __launch_bounds__(kCT) mimo_bwd_dadt_kernel(MimoParams a, const double* tot, int nch) {
+__global__ void __launch_bounds__(kCT) mimo_bwd_dadt_kernel(MimoParams a, const double* tot, int nch, int T) {
   const int u = blockIdx.x, b = u / a.H, h = u - b * a.H;
   double off = 0.0;
   for (int c = nch - 1; c >= 0; --c) {
-    const int t0 = c * kTcB, n = min(kTcB, a.L - t0);
+    const int t0 = c * T, n = min(T, a.L - t0);
     if (c < nch - 1)
       for (int t = threadIdx.x; t < n; t += kCT) {
         float* q = a.dadt + (int64_t)b * a.sdadt.b + (int64_t)(t0 + t) * a.sdadt.l + (int64_t)h * a.sdadt.h;
@@ -876,6 +876,388 @@ __global__ void __launch_bounds__(kFT)
   }
 }
 
+// ------------------------------------------------------------------------------------
+// Single-pass backward (the gradients of the single-pass forward, same chunks). The
+// adjoint of the state runs backwards in time,
+//   g_t = a_{t+1} g_{t+1} + E_t,   E_t[d] = sum_r dyr_t[r] C_t[r, d],   dyr_t = mimo_o dy_t,
+// so CTAs take chunks from the end (ticket order last chunk first) and look forward for
+// the adjoint entering their chunk from the right: a chunk publishes its local adjoint at
+// its first step, S_c = g_t0 from a zero adjoint after the chunk, and the decay product
+// A_c = a_{t0+1} .. a_{t0+n}; the carry of chunk c is g_{t0+n} = S_{c+1} + A_{c+1}(S_{c+2}
+// + ...). The forward states come from the forward's published chunk-end states (I_{c-1}
+// is the state entering chunk c), so nothing of the forward is recomputed but the chunk's
+// own steps. Per chunk one CTA then emits dx, dB, dC, dDT, dtrap, the per-step terms of
+// dADT with their chunk total (the cross-chunk suffix sums are mimo_bwd_dadt_kernel's),
+// and partial sums of dD, dmimo_x, dmimo_o (atomics). x, B, C and dy arrive as TMA boxes.
+// ------------------------------------------------------------------------------------
+struct FusedBwdSmem {
+  uint32_t bs, cs, xs, dys, bx, hs, gs, xr, dyr, dxr, yr, coef, trdt, dbg, red, mx, mo, total;
+};
+__host__ __device__ inline FusedBwdSmem fused_bwd_smem(int Q, int P, int R, int D, int eb, int ex) {
+  FusedBwdSmem L;
+  uint32_t o = 128;
+  L.bs = o; o = aup(o + (uint32_t)((Q + 1) * R * D * eb), 128);   // rows t0-1 .. t0+Q-1
+  L.cs = o; o = aup(o + (uint32_t)(Q * R * D * eb), 128);         // rows t0 .. t0+Q-1
+  L.xs = o; o = aup(o + (uint32_t)((Q + 1) * P * ex), 128);       // rows t0-1 .. t0+Q-1
+  L.dys = o; o = aup(o + (uint32_t)(Q * P * ex), 128);            // rows t0 .. t0+Q-1
+  L.bx = o; o = aup(o + (uint32_t)((Q + 1) * D * 4), 16);         // bx rows t0-1 .. t0+Q-1
+  L.hs = o; o = aup(o + (uint32_t)(Q * D * 4), 16);               // states t0 .. t0+Q-1
+  L.gs = o; o = aup(o + (uint32_t)((Q + 1) * D * 4), 16);         // E, then adjoints t0 .. t0+Q
+  L.xr = o; o = aup(o + (uint32_t)((Q + 1) * R * 4), 16);
+  L.dyr = o; o = aup(o + (uint32_t)(Q * R * 4), 16);
+  L.dxr = o; o = aup(o + (uint32_t)(Q * R * 4), 16);
+  L.yr = o; o = aup(o + (uint32_t)(Q * R * 4), 16);
+  L.coef = o; o = aup(o + (uint32_t)((Q + 1) * 16), 16);          // (a, beta, gamma, -) t0 .. t0+Q
+  L.trdt = o; o = aup(o + (uint32_t)(Q * 8), 16);                 // (sigmoid(trap), dt)
+  L.dbg = o; o = aup(o + (uint32_t)(Q * 8), 16);                  // (dbeta, dgamma)
+  L.red = o; o = aup(o + (uint32_t)(Q * 4), 16);                  // per-step dADT terms
+  L.mx = o; o = aup(o + (uint32_t)(R * (P + 4) * 4), 16);
+  L.mo = o; o = aup(o + (uint32_t)(R * (P + 4) * 4), 16);
+  L.total = o + 128;
+  return L;
+}
+
+struct FusedBwdArgs {
+  FastDiv fP4, fD4, fR, fU, fH;
+  int nch, units, ahead;
+  int bvec;  // dB / dC rows start on 16-byte boundaries (four gradients per store)
+  int xvec;  // dx rows likewise
+  FusedBwdSmem L;
+  const unsigned long long* fwd_rec;  // the forward's words: I_c = the state after chunk c
+  unsigned* ticket;
+  unsigned long long* rec;   // [unit][chunk][d]: adjoint S or I | status << 32
+  unsigned long long* arec;  // [unit][chunk]: A | 1 << 32
+  double* tot;               // [unit][chunk]: the chunk's dADT total
+};
+
+// The adjoint entering chunk c of unit u from the right (column d), from the words of the
+// chunks after it.
+__device__ __forceinline__ float look_ahead(const FusedBwdArgs& f, int u, int c, int d, int D, bool& ok) {
+  const int64_t base = (int64_t)u * f.nch;
+  float acc = 0.f, accA = 1.f;
+  int j = c + 1;
+  for (uint32_t spins = 0; spins < kSpinLimit; ++spins) {
+    const unsigned long long w = ld_relaxed64(f.rec + (base + j) * D + d);
+    const unsigned long long av = ld_relaxed64(f.arec + base + j);
+    const uint32_t st = (uint32_t)(w >> 32);
+    if (st == 2) return fmaf(accA, __uint_as_float((uint32_t)w), acc);
+    if (st == 1 && (av >> 32) != 0) {
+      acc = fmaf(accA, __uint_as_float((uint32_t)w), acc);
+      accA *= __uint_as_float((uint32_t)av);
+      if (++j >= f.nch) break;  // the last chunk publishes its inclusive adjoint only: unreachable
+      continue;
+    }
+    __nanosleep(32);
+  }
+  ok = false;
+  return 0.f;
+}
+
+template <typename T>
+__device__ __forceinline__ void st4v(T* p, float4 v, bool vec) {
+  if (vec) {
+    st4(p, v);
+  } else {
+    st(p, v.x);
+    st(p + 1, v.y);
+    st(p + 2, v.z);
+    st(p + 3, v.w);
+  }
+}
+
+template <typename TX, typename TB, int Q>
+__global__ void __launch_bounds__(kFT)
+    mimo_fused_bwd_kernel(const __grid_constant__ CUtensorMap mapB, const __grid_constant__ CUtensorMap mapC,
+                          const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapDY,
+                          MimoParams a, FusedBwdArgs f) {
+  static_assert(Q < kFT, "a thread per step of the chunk and the one after it");
+  extern __shared__ __align__(128) unsigned char fsm_raw[];
+  unsigned char* fsm = fsm_raw + ((128u - (sm100::smem_u32(fsm_raw) & 127u)) & 127u);
+  const int P = a.P, R = a.R, D = a.D, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int P4 = P >> 2, D4 = D >> 2, MS = P + 4;
+  const FusedBwdSmem& L = f.L;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(fsm);
+  int* tk_s = reinterpret_cast<int*>(fsm + 16);
+  const TB* Bs = reinterpret_cast<const TB*>(fsm + L.bs);
+  const TB* Cs = reinterpret_cast<const TB*>(fsm + L.cs);
+  const TX* xs = reinterpret_cast<const TX*>(fsm + L.xs);
+  const TX* dys = reinterpret_cast<const TX*>(fsm + L.dys);
+  float* bxs = reinterpret_cast<float*>(fsm + L.bx);
+  float* hs = reinterpret_cast<float*>(fsm + L.hs);
+  float* gs = reinterpret_cast<float*>(fsm + L.gs);
+  float* xr = reinterpret_cast<float*>(fsm + L.xr);
+  float* dyr = reinterpret_cast<float*>(fsm + L.dyr);
+  float* dxr = reinterpret_cast<float*>(fsm + L.dxr);
+  float* yr = reinterpret_cast<float*>(fsm + L.yr);
+  float4* coef = reinterpret_cast<float4*>(fsm + L.coef);
+  float2* trdt = reinterpret_cast<float2*>(fsm + L.trdt);
+  float2* dbg = reinterpret_cast<float2*>(fsm + L.dbg);
+  float* red = reinterpret_cast<float*>(fsm + L.red);
+  float* mx = reinterpret_cast<float*>(fsm + L.mx);
+  float* mo = reinterpret_cast<float*>(fsm + L.mo);
+
+  if (tid == 0) {
+    *tk_s = (int)atomicAdd(f.ticket, 1u);
+    sm100::mbar_init(bar, 1);
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
+  const int tk = *tk_s;
+  const int ci = fdiv(tk, f.fU), u = tk - ci * f.units, c = f.nch - 1 - ci;
+  const int b = fdiv(u, f.fH), h = u - b * a.H;
+  const int t0 = c * Q, n = min(Q, a.L - t0);
+  // the step scalars of t0 .. t0+n (the one after the chunk for the adjoint; zero past the
+  // end) and the state entering the chunk, first: their loads are in flight meanwhile
+  float s_adt = 0.f, s_dt = 0.f, s_tr = 0.f;
+  const bool sv = tid <= n && t0 + tid < a.L;
+  if (sv) {
+    s_adt = scalc(a.adt, a.sadt, b, t0 + tid, h);
+    s_dt = scalc(a.dt, a.sdt, b, t0 + tid, h);
+    s_tr = scalc(a.trap, a.strap, b, t0 + tid, h);
+  }
+  float hin = 0.f;
+  if (tid < D) {
+    if (c > 0)
+      hin = __uint_as_float((uint32_t)f.fwd_rec[((int64_t)u * f.nch + c - 1) * D + tid]);
+    else if (a.h0)
+      hin = a.h0[(int64_t)u * D + tid];
+  }
+  if (tid == 0) {
+    sm100::mbar_expect_tx(bar, (uint32_t)((Q + 1) * (R * D * sizeof(TB) + P * sizeof(TX)) +
+                                          Q * (R * D * sizeof(TB) + P * sizeof(TX))));
+    sm100::tma_load_5d(fsm + L.bs, &mapB, bar, 0, h, 0, t0 - 1, b);
+    sm100::tma_load_5d(fsm + L.cs, &mapC, bar, 0, h, 0, t0, b);
+    sm100::tma_load_4d(fsm + L.xs, &mapX, bar, 0, h, t0 - 1, b);
+    sm100::tma_load_4d(fsm + L.dys, &mapDY, bar, 0, h, t0, b);
+  }
+  const int tf = tk + f.ahead;
+  if (tf < f.units * f.nch && tid < 32) {
+    const int cif = fdiv(tf, f.fU), uf = tf - cif * f.units, bf = fdiv(uf, f.fH), hf = uf - bf * a.H;
+    const int tf0 = (f.nch - 1 - cif) * Q;
+    if (tid == 0) {  // rows from max(t0 - 1, 0): no prefetch starts outside the tensor
+      sm100::tma_prefetch_l2_5d(&mapB, 0, hf, 0, max(tf0 - 1, 0), bf);
+      sm100::tma_prefetch_l2_5d(&mapC, 0, hf, 0, tf0, bf);
+      sm100::tma_prefetch_l2_4d(&mapX, 0, hf, max(tf0 - 1, 0), bf);
+      sm100::tma_prefetch_l2_4d(&mapDY, 0, hf, tf0, bf);
+    }
+    for (int t = tf0 + tid; t < min(tf0 + Q + 1, a.L); t += 32) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a.adt + (int64_t)bf * a.sadt.b + (int64_t)t * a.sadt.l + (int64_t)hf * a.sadt.h));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a.dt + (int64_t)bf * a.sdt.b + (int64_t)t * a.sdt.l + (int64_t)hf * a.sdt.h));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a.trap + (int64_t)bf * a.strap.b + (int64_t)t * a.strap.l + (int64_t)hf * a.strap.h));
+    }
+  }
+  for (int i = tid; i < R * P; i += kFT) {
+    const int r = fdiv(i >> 2, f.fP4), p = i - r * P;
+    mx[r * MS + p] = a.mimo_x[(int64_t)h * a.smx_h + (int64_t)r * a.smx_r + p];
+    mo[r * MS + p] = a.mimo_o[(int64_t)h * a.smo_h + (int64_t)r * a.smo_r + p];
+  }
+  if (tid <= n) {
+    const float tr = sv ? sigmoidf_(s_tr) : 0.f;
+    coef[tid] = sv ? make_float4(expf(s_adt), s_dt * (1.0f - tr) + 0.5f * s_dt * tr, 0.5f * s_dt * tr, 0.f)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid < n) trdt[tid] = make_float2(tr, s_dt);
+  }
+  __syncthreads();
+  wait_copies(bar);
+  // xr for x rows t0-1 .. t0+n-1 and dyr for dy rows t0 .. t0+n-1, four p per step
+  for (int i = tid; i < (2 * n + 1) * R; i += kFT) {
+    const bool isx = i < (n + 1) * R;
+    const int j = isx ? i : i - (n + 1) * R;
+    const int row = fdiv(j, f.fR), k = j - row * R;
+    const TX* vrow = (isx ? xs : dys) + row * P;
+    const float* mrow = (isx ? mx : mo) + k * MS;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int pb = row - fdiv(row, f.fP4) * P4;
+    for (int e = 0; e < P4; ++e) {
+      fma4(acc, ld4f(vrow + 4 * pb), ld4f(mrow + 4 * pb));
+      pb = pb + 1 == P4 ? 0 : pb + 1;
+    }
+    (isx ? xr : dyr)[j] = (acc.x + acc.y) + (acc.z + acc.w);
+  }
+  __syncthreads();
+  // bx for rows t0-1 .. t0+n-1 and E for t0 .. t0+n-1, four columns a thread
+  for (int i = tid; i < (2 * n + 1) * D4; i += kFT) {
+    const bool isb = i < (n + 1) * D4;
+    const int j = isb ? i : i - (n + 1) * D4;
+    const int row = fdiv(j, f.fD4), d = 4 * (j - row * D4);
+    const float* wrow = (isb ? xr : dyr) + row * R;
+    const TB* mrow = (isb ? Bs : Cs) + (size_t)row * R * D + d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < R; ++r) fma4(acc, wrow[r], ld4f(mrow + (size_t)r * D));
+    *reinterpret_cast<float4*>((isb ? bxs : gs) + row * D + d) = acc;
+  }
+  __syncthreads();
+  // per column: the chunk's states from the entering state, its local adjoint from a zero
+  // adjoint after it, the adjoint carry from the chunks after it, the true adjoints
+  const int64_t cell = (int64_t)u * f.nch + c;
+  bool ok = true;
+  if (tid < D) {
+    const int d = tid;
+    if (c == 0) bxs[d] = a.bx0 ? a.bx0[(int64_t)u * D + d] : 0.f;
+    float hv = hin, bxp = bxs[d];
+    for (int tb = 0; tb < n; tb += 8) {
+      float bxv[8];
+      float4 cf[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool in = tb + j < n;
+        bxv[j] = in ? bxs[(tb + j + 1) * D + d] : 0.f;
+        cf[j] = in ? coef[tb + j] : make_float4(1.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        hv = fmaf(cf[j].x, hv, fmaf(cf[j].y, bxv[j], cf[j].z * bxp));
+        if (tb + j < n) {
+          bxp = bxv[j];
+          hs[(tb + j) * D + d] = hv;
+        }
+      }
+    }
+    float gl = 0.f, pr = 1.f;
+    for (int t = n - 1; t >= 0; --t) {
+      const float an = coef[t + 1].x;
+      gl = fmaf(an, gl, gs[t * D + d]);
+      pr *= an;
+      gs[t * D + d] = gl;
+    }
+    float carry = 0.f;
+    if (c < f.nch - 1) {
+      st_relaxed64(f.rec + cell * D + d, gl, 1);
+      if (d == 0) st_relaxed64(f.arec + cell, pr, 1);
+      carry = look_ahead(f, u, c, d, D, ok);
+    }
+    st_relaxed64(f.rec + cell * D + d, fmaf(pr, carry, gl), 2);
+    gs[n * D + d] = carry;
+    float q = 1.f;
+    for (int t = n - 1; t >= 0; --t) {
+      q *= coef[t + 1].x;
+      gs[t * D + d] = fmaf(q, carry, gs[t * D + d]);
+    }
+    if (c == 0) {
+      const float g0 = gs[d];
+      if (a.dh0) a.dh0[(int64_t)u * D + d] = coef[0].x * g0;
+      if (a.dbx0) a.dbx0[(int64_t)u * D + d] = coef[0].z * g0;
+    }
+  }
+  if (!ok) atomicExch(&g_mimo_error, 1);
+  __syncthreads();
+  // per (t, r): v = beta_t g_t + gamma_{t+1} g_{t+1}; dC = dyr h, dB = xr v, and the dots
+  // dxr = B . v + D dyr, yr = C . h + D xr; lpr lanes per row, four columns a lane
+  const float Dk = a.Dskip[h * a.sD];
+  int lpr = 1;
+  while (lpr * 2 <= 32 && lpr * 2 <= D4) lpr *= 2;
+  const int rpw = 32 / lpr, part = lane & (lpr - 1);
+  TB* dBb = reinterpret_cast<TB*>(a.dB) + (int64_t)b * a.sdB.b + (int64_t)h * a.sdB.h;
+  TB* dCb = reinterpret_cast<TB*>(a.dC) + (int64_t)b * a.sdC.b + (int64_t)h * a.sdC.h;
+  for (int it0 = warp * rpw; it0 < n * R; it0 += (kFT / 32) * rpw) {
+    const int it = it0 + lane / lpr;
+    float sx = 0.f, sy = 0.f;
+    if (it < n * R) {
+      const int t = fdiv(it, f.fR), r = it - t * R;
+      const float be = coef[t].y, gan = coef[t + 1].z, dv = dyr[it], xv = xr[(t + 1) * R + r];
+      const TB* brow = Bs + ((size_t)(t + 1) * R + r) * D;
+      const TB* crow = Cs + (size_t)it * D;
+      for (int blk = part; blk < D4; blk += lpr) {
+        const int d = 4 * blk;
+        const float4 h4 = *reinterpret_cast<const float4*>(hs + t * D + d);
+        const float4 g4 = *reinterpret_cast<const float4*>(gs + t * D + d);
+        const float4 g4n = *reinterpret_cast<const float4*>(gs + (t + 1) * D + d);
+        const float4 v4 = make_float4(fmaf(be, g4.x, gan * g4n.x), fmaf(be, g4.y, gan * g4n.y),
+                                      fmaf(be, g4.z, gan * g4n.z), fmaf(be, g4.w, gan * g4n.w));
+        const float4 b4 = ld4f(brow + d), c4 = ld4f(crow + d);
+        sx = fmaf(b4.x, v4.x, fmaf(b4.y, v4.y, fmaf(b4.z, v4.z, fmaf(b4.w, v4.w, sx))));
+        sy = fmaf(c4.x, h4.x, fmaf(c4.y, h4.y, fmaf(c4.z, h4.z, fmaf(c4.w, h4.w, sy))));
+        const int64_t tt = t0 + t;
+        st4v(dCb + tt * a.sdC.l + (int64_t)r * a.sdC.r + d,
+             make_float4(dv * h4.x, dv * h4.y, dv * h4.z, dv * h4.w), f.bvec);
+        st4v(dBb + tt * a.sdB.l + (int64_t)r * a.sdB.r + d,
+             make_float4(xv * v4.x, xv * v4.y, xv * v4.z, xv * v4.w), f.bvec);
+      }
+    }
+    for (int o = lpr >> 1; o > 0; o >>= 1) {
+      sx += __shfl_xor_sync(0xffffffffu, sx, o);
+      sy += __shfl_xor_sync(0xffffffffu, sy, o);
+    }
+    if (it < n * R && part == 0) {
+      const int t = fdiv(it, f.fR), r = it - t * R;
+      dxr[it] = fmaf(Dk, dyr[it], sx);
+      yr[it] = fmaf(Dk, xr[(t + 1) * R + r], sy);
+    }
+  }
+  // per t: dbeta = g_t . bx_t, dgamma = g_t . bx_{t-1}
+  for (int t0w = warp * rpw; t0w < n; t0w += (kFT / 32) * rpw) {
+    const int t = t0w + lane / lpr;
+    float sb = 0.f, sg = 0.f;
+    if (t < n)
+      for (int blk = part; blk < D4; blk += lpr) {
+        const int d = 4 * blk;
+        const float4 g4 = *reinterpret_cast<const float4*>(gs + t * D + d);
+        const float4 b1 = *reinterpret_cast<const float4*>(bxs + (t + 1) * D + d);
+        const float4 b0 = *reinterpret_cast<const float4*>(bxs + t * D + d);
+        sb = fmaf(g4.x, b1.x, fmaf(g4.y, b1.y, fmaf(g4.z, b1.z, fmaf(g4.w, b1.w, sb))));
+        sg = fmaf(g4.x, b0.x, fmaf(g4.y, b0.y, fmaf(g4.z, b0.z, fmaf(g4.w, b0.w, sg))));
+      }
+    for (int o = lpr >> 1; o > 0; o >>= 1) {
+      sb += __shfl_xor_sync(0xffffffffu, sb, o);
+      sg += __shfl_xor_sync(0xffffffffu, sg, o);
+    }
+    if (t < n && part == 0) dbg[t] = make_float2(sb, sg);
+  }
+  __syncthreads();
+  // per t: q = sum_r dyr (yr - D xr) = E_t . h_t, the dADT term, dDT and dtrap
+  if (tid < n) {
+    const int t = tid;
+    float qv = 0.f;
+    for (int r = 0; r < R; ++r) qv = fmaf(dyr[t * R + r], fmaf(-Dk, xr[(t + 1) * R + r], yr[t * R + r]), qv);
+    const float2 bg = dbg[t], td = trdt[t];
+    const float4 cf = coef[t];
+    red[t] = qv - cf.y * bg.x - cf.z * bg.y;
+    const int64_t tt = t0 + t;
+    a.ddt[(int64_t)b * a.sddt.b + tt * a.sddt.l + (int64_t)h * a.sddt.h] = bg.x * (1.0f - 0.5f * td.x) + bg.y * 0.5f * td.x;
+    a.dtrap[(int64_t)b * a.sdtrap.b + tt * a.sdtrap.l + (int64_t)h * a.sdtrap.h] =
+        0.5f * td.y * (bg.y - bg.x) * td.x * (1.0f - td.x);
+  }
+  // dx = mimo_x^T dxr, four p a thread
+  TX* dxb = reinterpret_cast<TX*>(a.dx) + (int64_t)b * a.sdx.b + (int64_t)h * a.sdx.h;
+  for (int i = tid; i < n * P4; i += kFT) {
+    const int t = fdiv(i, f.fP4), p = 4 * (i - t * P4);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < R; ++r) fma4(acc, dxr[t * R + r], ld4f(mx + r * MS + p));
+    st4v(dxb + (int64_t)(t0 + t) * a.sdx.l + p, acc, f.xvec);
+  }
+  // dmimo_x += dxr x^T, dmimo_o += yr dy^T, dD += <dyr, xr>
+  for (int i = tid; i < R * P; i += kFT) {
+    const int r = fdiv(i >> 2, f.fP4), p = i - r * P;
+    float ax = 0.f, ao = 0.f;
+    for (int t = 0; t < n; ++t) {
+      ax = fmaf(dxr[t * R + r], to_f32(xs[(t + 1) * P + p]), ax);
+      ao = fmaf(yr[t * R + r], to_f32(dys[t * P + p]), ao);
+    }
+    atomicAdd(a.dmx + (int64_t)h * R * P + i, ax);
+    atomicAdd(a.dmo + (int64_t)h * R * P + i, ao);
+  }
+  if (warp == kFT / 32 - 1) {
+    float v = 0.f;
+    for (int i = lane; i < n * R; i += 32) {
+      const int t = fdiv(i, f.fR), r = i - t * R;
+      v = fmaf(dyr[i], xr[(t + 1) * R + r], v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) atomicAdd(a.dD + h, v);
+  }
+  __syncthreads();
+  // within-chunk suffix sums of the dADT terms (fp64); the chunk total for the cross-chunk sums
+  if (tid == 0) {
+    double cum = 0.0;
+    for (int t = n - 1; t >= 0; --t) {
+      cum += (double)red[t];
+      a.dadt[(int64_t)b * a.sdadt.b + (int64_t)(t0 + t) * a.sdadt.l + (int64_t)h * a.sdadt.h] = (float)cum;
+    }
+    f.tot[cell] = cum;
+  }
+}
+
 template <typename K>
 int opt_in(K k, size_t smem) {
   if (smem <= 48 * 1024) return M3_OK;
@@ -933,17 +1315,33 @@ bool make_bc_map(CUtensorMap* m, const void* base, const MimoParams& p, const St
 
 // 4-d map over (p, h, t, b) of a (B, L, H, P) tensor with a (P, 1, rows, 1) box: [t][p].
 template <typename TX>
-bool make_x_map(CUtensorMap* m, const MimoParams& p, int rows) {
+bool make_row_map(CUtensorMap* m, const void* base, const Str3& st, const MimoParams& p, int rows) {
   auto enc = chunk_encode_fn();
   if (!enc) return false;
   const cuuint64_t ex = sizeof(TX);
   cuuint64_t dims[4] = {(cuuint64_t)p.P, (cuuint64_t)p.H, (cuuint64_t)p.L, (cuuint64_t)p.Bn};
-  cuuint64_t strides[3] = {(cuuint64_t)p.sx.h * ex, (cuuint64_t)p.sx.l * ex, (cuuint64_t)p.sx.b * ex};
+  cuuint64_t strides[3] = {(cuuint64_t)st.h * ex, (cuuint64_t)st.l * ex, (cuuint64_t)st.b * ex};
   cuuint32_t box[4] = {(cuuint32_t)p.P, 1, (cuuint32_t)rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  return enc(m, tmap_type<TX>(), 4, const_cast<void*>(p.x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  return enc(m, tmap_type<TX>(), 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+template <typename TX>
+bool make_x_map(CUtensorMap* m, const MimoParams& p, int rows) { return make_row_map<TX>(m, p.x, p.sx, p, rows); }
+
+// rows of 4 elements starting on 16-byte boundaries at every (b, t, h[, r]) and column 4k
+template <typename T>
+bool vec4_rows(const void* ptr, const Str3& st) {
+  const int64_t e = sizeof(T);
+  return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && (st.b * e) % 16 == 0 && (st.l * e) % 16 == 0 &&
+         (st.h * e) % 16 == 0;
+}
+template <typename T>
+bool vec4_rows(const void* ptr, const Str4& st) {
+  const int64_t e = sizeof(T);
+  return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && (st.b * e) % 16 == 0 && (st.l * e) % 16 == 0 &&
+         (st.r * e) % 16 == 0 && (st.h * e) % 16 == 0;
 }
 
 // Returns M3_ERR_UNSUPPORTED (nothing launched) when a tensor map cannot be made.
@@ -987,6 +1385,70 @@ int run_fused(const MimoParams& p, void* ws, cudaStream_t s) {
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   mimo_fused_fwd_kernel<TX, TB, Q><<<(unsigned)cells, kFT, smem, s>>>(mB, mC, mX, p, f);
   return check_launch("mimo_fused_fwd_kernel");
+}
+
+// Workspace of the single-pass backward: ticket, adjoint words and decay words (cleared
+// before each launch), then the per-chunk dADT totals.
+inline int64_t fused_bwd_ws_bytes(int64_t cells, int64_t D) { return fused_ws_bytes(cells, D) + 8 * cells + 16; }
+
+// Returns M3_ERR_UNSUPPORTED (nothing launched) when the single-pass pair does not apply.
+template <typename TX, typename TB, int Q>
+int run_fused_bwd(const MimoParams& p, const void* fwd_ws, size_t fwd_bytes, void* ws, size_t ws_bytes,
+                  cudaStream_t s) {
+  const int64_t nch = (p.L + Q - 1) / Q, units = (int64_t)p.Bn * p.H, cells = units * nch;
+  if (cells >= INT32_MAX || fwd_bytes < (size_t)fused_ws_bytes(cells, p.D) ||
+      ws_bytes < (size_t)fused_bwd_ws_bytes(cells, p.D))
+    return M3_ERR_UNSUPPORTED;
+  if (!vec4_rows<TX>(p.dy, p.sdy) || (p.P * (int64_t)sizeof(TX)) % 16 != 0) return M3_ERR_UNSUPPORTED;
+  const FusedBwdSmem L = fused_bwd_smem(Q, p.P, p.R, p.D, (int)sizeof(TB), (int)sizeof(TX));
+  if (L.total > 200u * 1024u) return M3_ERR_UNSUPPORTED;
+  CUtensorMap mB, mC, mX, mDY;
+  if (!make_bc_map<TB>(&mB, p.Bm, p, p.sB, Q + 1) || !make_bc_map<TB>(&mC, p.Cm, p, p.sC, Q) ||
+      !make_row_map<TX>(&mX, p.x, p.sx, p, Q + 1) || !make_row_map<TX>(&mDY, p.dy, p.sdy, p, Q))
+    return M3_ERR_UNSUPPORTED;
+  FusedBwdArgs f;
+  f.fP4 = make_fastdiv((uint32_t)(p.P / 4));
+  f.fD4 = make_fastdiv((uint32_t)(p.D / 4));
+  f.fR = make_fastdiv((uint32_t)p.R);
+  f.fU = make_fastdiv((uint32_t)units);
+  f.fH = make_fastdiv((uint32_t)p.H);
+  f.nch = (int)nch;
+  f.units = (int)units;
+  f.bvec = vec4_rows<TB>(p.dB, p.sdB) && vec4_rows<TB>(p.dC, p.sdC);
+  f.xvec = vec4_rows<TX>(p.dx, p.sdx);
+  f.L = L;
+  f.fwd_rec = reinterpret_cast<const unsigned long long*>(static_cast<const char*>(fwd_ws) + 16);
+  char* w = static_cast<char*>(ws);
+  f.ticket = reinterpret_cast<unsigned*>(w);
+  f.rec = reinterpret_cast<unsigned long long*>(w + 16);
+  f.arec = f.rec + cells * p.D;
+  f.tot = reinterpret_cast<double*>(w + ((fused_ws_bytes(cells, p.D) + 15) & ~int64_t(15)));
+  M3_TRY(opt_in(mimo_fused_bwd_kernel<TX, TB, Q>, L.total));
+  cudaFuncSetAttribute(mimo_fused_bwd_kernel<TX, TB, Q>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  int per_sm = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mimo_fused_bwd_kernel<TX, TB, Q>, kFT, L.total) !=
+      cudaSuccess)
+    per_sm = 1;
+  if (device_sm_count(&sms) != M3_OK) sms = 148;
+  f.ahead = std::max(1, per_sm * sms);
+  cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)fused_ws_bytes(cells, p.D), s);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  mimo_fused_bwd_kernel<TX, TB, Q><<<(unsigned)cells, kFT, L.total, s>>>(mB, mC, mX, mDY, p, f);
+  M3_TRY(check_launch("mimo_fused_bwd_kernel"));
+  mimo_bwd_dadt_kernel<<<(unsigned)units, kCT, 0, s>>>(p, f.tot, (int)nch, Q);
+  return check_launch("mimo_bwd_dadt_kernel");
+}
+
+template <typename TX, typename TB>
+int run_bwd_fused(const MimoParams& p, const void* fwd_ws, size_t fwd_bytes, void* ws, size_t ws_bytes,
+                  cudaStream_t s) {
+  if (!fused_applies<TX, TB>(p)) return M3_ERR_UNSUPPORTED;
+  switch (fused_chunk<TX, TB>(p)) {
+    case 64: return run_fused_bwd<TX, TB, 64>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+    case 32: return run_fused_bwd<TX, TB, 32>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+    case 16: return run_fused_bwd<TX, TB, 16>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+    default: return M3_ERR_UNSUPPORTED;
+  }
 }
 
 template <typename TX, typename TB>
@@ -1049,7 +1511,7 @@ int run_bwd_chunked(const MimoParams& p0, void* ws, cudaStream_t s) {
   M3_TRY(check_launch("mimo_bwd_carry_kernel"));
   mimo_bwd_full_kernel<TX, TB><<<grid, kCT, sm_full, s>>>(p, Hc, Gc, tot, nch);
   M3_TRY(check_launch("mimo_bwd_full_kernel"));
-  mimo_bwd_dadt_kernel<<<units, kCT, 0, s>>>(p, tot, nch);
+  mimo_bwd_dadt_kernel<<<units, kCT, 0, s>>>(p, tot, nch, kTcB);
   return check_launch("mimo_bwd_dadt_kernel");
 }
 
@@ -1079,6 +1541,26 @@ size_t mimo_fwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D) {
   const int64_t three = 4 * Bn * H * ((L + kTcF - 1) / kTcF) * (D + 1);
   const int64_t single = fused_ws_bytes(Bn * H * ((L + 15) / 16), D);
   return (size_t)std::max(three, single);
+}
+
+size_t mimo_bwd_fused_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D) {
+  return (size_t)fused_bwd_ws_bytes(Bn * H * ((L + 15) / 16), D);
+}
+
+int launch_mimo_bwd_fused(const MimoParams& p, int xdt, int bcdt, const void* fwd_ws, size_t fwd_bytes, void* ws,
+                          size_t ws_bytes, cudaStream_t s) {
+  if (!fwd_ws || !ws) return M3_ERR_UNSUPPORTED;
+  if (p.L >= (int64_t)65535 * 16 * 1024) return M3_ERR_UNSUPPORTED;
+  if (xdt == M3_FLOAT32 && bcdt == M3_FLOAT32) return run_bwd_fused<float, float>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+  if (xdt == M3_BFLOAT16 && bcdt == M3_BFLOAT16)
+    return run_bwd_fused<__nv_bfloat16, __nv_bfloat16>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+  if (xdt == M3_BFLOAT16 && bcdt == M3_FLOAT32)
+    return run_bwd_fused<__nv_bfloat16, float>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+  if (xdt == M3_FLOAT32 && bcdt == M3_BFLOAT16)
+    return run_bwd_fused<float, __nv_bfloat16>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+  if (xdt == M3_FLOAT16 && bcdt == M3_FLOAT16) return run_bwd_fused<__half, __half>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+  if (xdt == M3_FLOAT16 && bcdt == M3_FLOAT32) return run_bwd_fused<__half, float>(p, fwd_ws, fwd_bytes, ws, ws_bytes, s);
+  return M3_ERR_UNSUPPORTED;
 }
 
 int mimo_error_word(bool reset, int* out) {

@@ -47,7 +47,13 @@ int launch_mimo(const MimoParams& p, int xdt, int bcdt, bool bwd, cudaStream_t s
 // Chunk-parallel forward (mimo_chunked.cu): workspace of mimo_fwd_workspace_bytes bytes.
 size_t mimo_fwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D);
 int launch_mimo_fwd_chunked(const MimoParams& p, int xdt, int bcdt, void* ws, cudaStream_t s);
-// the word the single-pass forward sets when a bounded wait gives up
+// Single-pass backward (mimo_chunked.cu) from the single-pass forward's workspace (its
+// published chunk-end states): M3_ERR_UNSUPPORTED, nothing launched, when the pair does not
+// apply (the caller then runs launch_mimo_bwd_chunked).
+size_t mimo_bwd_fused_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D);
+int launch_mimo_bwd_fused(const MimoParams& p, int xdt, int bcdt, const void* fwd_ws, size_t fwd_bytes, void* ws,
+                          size_t ws_bytes, cudaStream_t s);
+// the word the single-pass kernels set when a bounded wait gives up
 int mimo_error_word(bool reset, int* out);
 // Chunk-parallel backward (mimo_chunked.cu), used when its shared-memory layout fits.
 bool mimo_bwd_chunked_fits(int P, int R, int D);

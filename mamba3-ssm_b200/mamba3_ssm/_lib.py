@@ -70,6 +70,9 @@ _SIGS = {
     "m3_mimo_scan_fwd_ws": ([_P] * 14 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "m3_mimo_scan_bwd_workspace_size": ([ctypes.c_int64] * 6, ctypes.c_size_t),
     "m3_mimo_scan_bwd": ([_P] * 23 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+    "m3_mimo_scan_bwd_ws_workspace_size": ([ctypes.c_int64] * 6, ctypes.c_size_t),
+    "m3_mimo_scan_bwd_ws": ([_P] * 23 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+                                         ctypes.c_void_p], ctypes.c_int),
     "m3_siso_step": ([ctypes.c_void_p] + [_P] * 14 + [ctypes.c_void_p], ctypes.c_int),
     "m3_mimo_step": ([ctypes.c_void_p] + [_P] * 16 + [ctypes.c_void_p], ctypes.c_int),
     "m3_rmsnorm": ([_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_void_p], ctypes.c_int),

@@ -72,7 +72,7 @@ class _LayerCoreFn(torch.autograd.Function):
         mx = mo = None
         if layer.is_mimo:
             mx, mo = _f32(mimo_x), _f32(mimo_o)
-            y, _, _ = _mimo_fwd_raw(x, Bp, Cp, ADT, DT, trap, Dv, mx, mo)
+            y, _, _, ks = _mimo_fwd_raw(x, Bp, Cp, ADT, DT, trap, Dv, mx, mo, keep_ws=True)
         else:
             y, _, _, ks = _siso_fwd_raw(x, Bp[:, :, 0], Cp[:, :, 0], ADT, DT, trap, Dv, keep_states=True)
         g = torch.empty(batch, Ln, H, P, dtype=zx.dtype, device=dev)
@@ -103,8 +103,10 @@ class _LayerCoreFn(torch.autograd.Function):
             L.check(lib.m3_silu_gate_bwd(*a.ptrs, L.stream_of(zx)), "m3_silu_gate_bwd")
         dmx = dmo = None
         if layer.is_mimo:
+            fws = ctx.ks
+            ctx.ks = None
             dx, dBp, dCp, dADT, dDT, dtrap, dD, dmx, dmo, _, _ = _mimo_bwd_raw(x, Bp, Cp, ADT, DT, trap, Dv, mx, mo,
-                                                                             None, None, dy)
+                                                                             None, None, dy, fwd_ws=fws)
         else:
             ks = ctx.ks
             ctx.ks = None

@@ -184,8 +184,9 @@ def _siso_bwd_raw(x, B, C, ADT, DT, trap, D, h0, bx0, ks, dy, need_h0=False, nee
     return dx, dB, dC, dADT, dDT, dtrap, dD, dh0, dbx0
 
 
-def _mimo_fwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0=None, bx0=None, want_state=False):
-    """MIMO forward (chunk-parallel kernels) on the C ABI. Returns (y, h_last, bx_last)."""
+def _mimo_fwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0=None, bx0=None, want_state=False, keep_ws=False):
+    """MIMO forward (chunk-parallel kernels) on the C ABI. Returns (y, h_last, bx_last), and
+    with keep_ws also the workspace (its published chunk-end states serve the backward)."""
     lib = L.load()
     Bn, Ln, H, P = x.shape
     Ds = B.shape[-1]
@@ -199,12 +200,14 @@ def _mimo_fwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0=None, bx0=None, want_sta
     ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=x.device)
     with torch.cuda.device(x.device):
         L.check(lib.m3_mimo_scan_fwd_ws(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)), "m3_mimo_scan_fwd_ws")
+    if keep_ws:
+        return y, hl, bl, ws
     return y, hl, bl
 
 
-def _mimo_bwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, need_h0=False, need_bx0=False):
-    """MIMO backward on the C ABI. Returns dx, dB, dC, dADT, dDT, dtrap, dD, dmimo_x,
-    dmimo_o, dh0, dbx0."""
+def _mimo_bwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, need_h0=False, need_bx0=False, fwd_ws=None):
+    """MIMO backward on the C ABI, from the forward's workspace when given (the single-pass
+    pair). Returns dx, dB, dC, dADT, dDT, dtrap, dD, dmimo_x, dmimo_o, dh0, dbx0."""
     lib = L.load()
     Bn, Ln, H, P = x.shape
     R, Ds = B.shape[2], B.shape[-1]
@@ -221,12 +224,18 @@ def _mimo_bwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, need_h0=False,
     dmo = _empty((H, R, P), torch.float32, dev)
     dh0 = _empty(h0.shape, torch.float32, dev) if (h0 is not None and need_h0) else None
     dbx0 = _empty(bx0.shape, torch.float32, dev) if (bx0 is not None and need_bx0) else None
-    nbytes = lib.m3_mimo_scan_bwd_workspace_size(Bn, Ln, H, P, Ds, R)
-    ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
     a = L.pack(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, dx, dB, dC, dADT, dDT, dtrap, dD, dmx, dmo,
                dh0, dbx0)
     with torch.cuda.device(dev):
-        L.check(lib.m3_mimo_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)), "m3_mimo_scan_bwd")
+        if fwd_ws is not None:
+            nbytes = lib.m3_mimo_scan_bwd_ws_workspace_size(Bn, Ln, H, P, Ds, R)
+            ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
+            L.check(lib.m3_mimo_scan_bwd_ws(*a.ptrs, fwd_ws.data_ptr(), fwd_ws.numel(), ws.data_ptr(), ws.numel(),
+                                            L.stream_of(x)), "m3_mimo_scan_bwd_ws")
+        else:
+            nbytes = lib.m3_mimo_scan_bwd_workspace_size(Bn, Ln, H, P, Ds, R)
+            ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
+            L.check(lib.m3_mimo_scan_bwd(*a.ptrs, ws.data_ptr(), ws.numel(), L.stream_of(x)), "m3_mimo_scan_bwd")
     return dx, dB, dC, dADT, dDT, dtrap, dD, dmx, dmo, dh0, dbx0
 
 
@@ -257,7 +266,12 @@ class _SisoScanFn(torch.autograd.Function):
 class _MimoScanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, want_state):
-        y, hl, bl = _mimo_fwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, want_state)
+        # when gradients will be needed, keep the forward's workspace (its chunk-end states)
+        # for the single-pass backward
+        keep = any(ctx.needs_input_grad[:11])
+        out = _mimo_fwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, want_state, keep_ws=keep)
+        y, hl, bl = out[:3]
+        ctx.fwd_ws = out[3] if keep else None
         ctx.save_for_backward(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0)
         ctx.mark_non_differentiable(*[t for t in (hl, bl) if t is not None])
         return y, hl, bl
@@ -267,8 +281,10 @@ class _MimoScanFn(torch.autograd.Function):
         x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0 = ctx.saved_tensors
         if dy is None:
             dy = torch.zeros_like(x)
+        fws = ctx.fwd_ws
+        ctx.fwd_ws = None
         g = _mimo_bwd_raw(x, B, C, ADT, DT, trap, D, mx, mo, h0, bx0, dy, ctx.needs_input_grad[9],
-                          ctx.needs_input_grad[10])
+                          ctx.needs_input_grad[10], fwd_ws=fws)
         return (*g, None)
 
 

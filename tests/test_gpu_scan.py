@@ -289,29 +289,60 @@ def test_mimo_forward_unaligned_rows_three_pass(L):
     assert rel_err(bl.double().cpu().numpy(), bo) < 1e-4
 
 
-@pytest.mark.parametrize("L", [1, 31, 32, 33, 200])
-@pytest.mark.parametrize("R,D,P", [(4, 64, 32), (2, 128, 64)])
-def test_mimo_chunked_backward_with_states(L, R, D, P):
-    """The chunk-parallel MIMO backward (32-step chunks: forward carries, reverse adjoint
-    carries, per-chunk gradients, cross-chunk dADT suffix sums) on chunk-boundary lengths,
-    with initial states, against the fp64 adjoint of the oracle (all gradients incl.
-    dh0 / dbx0)."""
+@pytest.mark.parametrize("L", [1, 15, 16, 17, 31, 32, 33, 200, 1500])
+@pytest.mark.parametrize("R,D,P", [(4, 64, 32), (2, 128, 64), (2, 16, 8)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mimo_chunked_backward_with_states(L, R, D, P, dtype):
+    """The single-pass MIMO backward (the forward's chunk-end states, adjoint carries found
+    by looking ahead over later chunks, per-chunk gradients, cross-chunk dADT suffix sums)
+    on chunk-boundary lengths and a long sequence, with initial states, against the fp64
+    adjoint of the oracle (all gradients incl. dh0 / dbx0); no bounded wait may give up."""
+    from mamba3_ssm import _lib
     from mamba3_ssm.ops import _MimoScanFn
-    arrs, t = _inputs(2000 + L + D, 2, L, 3, P, D, R=R, dtype=torch.float32)
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    arrs, t = _inputs(2000 + L + D, 2, L, 3, P, D, R=R, dtype=dtype)
     keys = ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")
     rng = np.random.default_rng(L + 11)
     h0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV).requires_grad_(True)
     b0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV).requires_grad_(True)
     ins = [t[k].requires_grad_(True) for k in keys]
+    _lib.device_timeouts(reset=True)
     y, _, _ = _MimoScanFn.apply(*ins, h0, b0, False)
     dy = torch.randn_like(y)
     y.backward(dy)
     go = O.mimo_scan_bwd(*[arrs[k] for k in keys], dy.double().cpu().numpy(),
                          h0.detach().double().cpu().numpy(), b0.detach().double().cpu().numpy())
     for k, tt in zip(("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o"), ins):
-        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < 1e-4, k
-    assert rel_err(h0.grad.double().cpu().numpy(), go["dh0"]) < 1e-4
-    assert rel_err(b0.grad.double().cpu().numpy(), go["dbx0"]) < 1e-4
+        assert rel_err(tt.grad.double().cpu().numpy(), go[k]) < tol, k
+    assert rel_err(h0.grad.double().cpu().numpy(), go["dh0"]) < tol
+    assert rel_err(b0.grad.double().cpu().numpy(), go["dbx0"]) < tol
+    assert _lib.device_timeouts(reset=True) == 0
+
+
+@pytest.mark.parametrize("L", [33, 300])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mimo_backward_without_forward_workspace(L, dtype):
+    """m3_mimo_scan_bwd (no forward workspace: the chunk-parallel kernels that recompute the
+    forward) and m3_mimo_scan_bwd_ws (the single-pass backward) on the same inputs, both
+    against the oracle's adjoint."""
+    from mamba3_ssm.ops import _mimo_bwd_raw, _mimo_fwd_raw
+    R, D, P = 4, 64, 32
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    arrs, t = _inputs(4000 + L, 2, L, 3, P, D, R=R, dtype=dtype)
+    keys = ("x", "B", "C", "ADT", "DT", "trap", "D", "mimo_x", "mimo_o")
+    rng = np.random.default_rng(L + 13)
+    h0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV)
+    b0 = torch.tensor(rng.standard_normal((2, 3, D)), dtype=torch.float32, device=DEV)
+    ins = [t[k] for k in keys]
+    _, _, _, fws = _mimo_fwd_raw(*ins, h0, b0, keep_ws=True)
+    dy = torch.randn(2, L, 3, P, device=DEV).to(dtype)
+    go = O.mimo_scan_bwd(*[arrs[k] for k in keys], dy.double().cpu().numpy(), h0.double().cpu().numpy(),
+                         b0.double().cpu().numpy())
+    names = ("dx", "dB", "dC", "dADT", "dDT", "dtrap", "dD", "dmimo_x", "dmimo_o", "dh0", "dbx0")
+    for fw in (None, fws):
+        g = _mimo_bwd_raw(*ins, h0, b0, dy, True, True, fwd_ws=fw)
+        for k, v in zip(names, g):
+            assert rel_err(v.double().cpu().numpy(), go[k]) < tol, (k, fw is None)
 
 
 def _siso_grads(ins, h0=None, b0=None):
