@@ -258,6 +258,149 @@ __global__ void __launch_bounds__(256) bc_reduce_kernel(PrologueBwdParams a, int
   atomicAdd(dst, v);
 }
 
+// The bc kernel for one B / C group (ngroups 1), a thread per (head, pair) slot of a row
+// for every rank: the angle's sin / cos once per (row, head, pair) for all ranks and both B
+// and C, dtheta summed in registers and written once, the bias gradients in thread-private
+// shared-memory slots, dn (the sum over heads) through shared-memory atomics, one per
+// (thread, rank, element) and row. CTAs stride over the rows; the RMSNorm backward of a
+// row is a warp per (B or C, rank). Partial sums go to the CTA's workspace slot as in the
+// general kernel.
+constexpr int kBC1 = 256;
+template <typename TZ, typename TO, int RT>
+__global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParams a) {
+  extern __shared__ float4 sm4[];
+  constexpr int R = RT;
+  const int D = a.D, H = a.H, S = a.S, half = D / 2, npair = a.split / 2;
+  const int np = H * half;  // (head, pair) slots of a row
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float4* sbias = sm4;                                          // [r][slot]: (dB0, dB1, dC0, dC1)
+  float* raw = reinterpret_cast<float*>(sm4 + (size_t)R * np);  // (2, R, D): the row's raw B, C group rows
+  float* rs = raw + 2 * R * D;                                  // (2, R): 1 / rms
+  float* sdn = rs + 2 * R;                                      // (2, R, D): dn = sum over heads of dv
+  float* swb = sdn + 2 * R * D;                                 // (2, R, D): norm-weight gradient partials
+  for (int i = tid; i < R * np; i += kBC1) sbias[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = tid; i < 2 * R * D; i += kBC1) swb[i] = 0.f;
+  const int64_t nrows = (int64_t)a.Bn * a.L;
+  const int64_t RD = (int64_t)R * D;
+  for (int64_t row = blockIdx.x; row < nrows; row += gridDim.x) {
+    const int64_t b = row / a.L, l = row - b * a.L;
+    const TZ* zrow = reinterpret_cast<const TZ*>(a.zx) + b * a.s_zb + l * a.s_zl + 2 * a.d_inner;
+    TZ* drow = reinterpret_cast<TZ*>(a.dzx) + b * a.s_dzb + l * a.s_dzl + 2 * a.d_inner;
+    __syncthreads();  // the previous row is done with raw, rs and sdn
+    for (int i = tid; i < 2 * R * D; i += kBC1) {
+      raw[i] = to_f32(zrow[i]);  // B rows (R, D), then C rows (R, D)
+      sdn[i] = 0.f;
+    }
+    __syncthreads();
+    for (int it = warp; it < 2 * R; it += kBC1 / 32) {
+      float ss = 0.f;
+      for (int d = lane; d < D; d += 32) ss = fmaf(raw[it * D + d], raw[it * D + d], ss);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) rs[it] = 1.0f / sqrtf(ss / (float)D + a.eps);
+    }
+    __syncthreads();
+    float dnb0[R], dnb1[R], dnc0[R], dnc1[R];
+    int kcur = -1;
+#pragma unroll
+    for (int r = 0; r < R; ++r) dnb0[r] = dnb1[r] = dnc0[r] = dnc1[r] = 0.f;
+    for (int sl = tid; sl < np; sl += kBC1) {
+      const int h = sl / half, k = sl - h * half, d0 = 2 * k;
+      if (k != kcur) {  // flush the running sums over heads of the previous pair
+        if (kcur >= 0) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            atomicAdd(&sdn[r * D + 2 * kcur], dnb0[r]); atomicAdd(&sdn[r * D + 2 * kcur + 1], dnb1[r]);
+            atomicAdd(&sdn[RD + r * D + 2 * kcur], dnc0[r]); atomicAdd(&sdn[RD + r * D + 2 * kcur + 1], dnc1[r]);
+            dnb0[r] = dnb1[r] = dnc0[r] = dnc1[r] = 0.f;
+          }
+        }
+        kcur = k;
+      }
+      const TO* gBh = reinterpret_cast<const TO*>(a.dBp) + (row * R * H + h) * D + d0;
+      const TO* gCh = reinterpret_cast<const TO*>(a.dCp) + (row * R * H + h) * D + d0;
+      float2 gb[R], gc[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        gb[r] = ld_pair(gBh + (int64_t)r * H * D);
+        gc[r] = ld_pair(gCh + (int64_t)r * H * D);
+      }
+      const bool rot = k < npair;
+      float sn = 0.f, cs = 1.f;
+      if (rot) sincos_reduced(__ldg(a.angles + (row * H + h) * S + k), &sn, &cs);
+      const float2 wb = __ldg(reinterpret_cast<const float2*>(a.B_norm_w + d0));
+      const float2 wc = __ldg(reinterpret_cast<const float2*>(a.C_norm_w + d0));
+      float dth = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float2 g1 = gb[r], g2 = gc[r];
+        if (rot) {
+          // o = rot(v), v = n + bias; dtheta = -g1 o2 + g2 o1; dv = rot^T(g)
+          const float2 bv = __ldg(reinterpret_cast<const float2*>(a.B_bias + ((int64_t)h * R + r) * D + d0));
+          const float2 cv = __ldg(reinterpret_cast<const float2*>(a.C_bias + ((int64_t)h * R + r) * D + d0));
+          const float rb = rs[r], rc = rs[R + r];
+          const float x0 = fmaf(raw[r * D + d0] * rb, wb.x, bv.x), x1 = fmaf(raw[r * D + d0 + 1] * rb, wb.y, bv.y);
+          const float y0 = fmaf(raw[RD + r * D + d0] * rc, wc.x, cv.x);
+          const float y1 = fmaf(raw[RD + r * D + d0 + 1] * rc, wc.y, cv.y);
+          const float ob0 = x0 * cs - x1 * sn, ob1 = x0 * sn + x1 * cs;
+          const float oc0 = y0 * cs - y1 * sn, oc1 = y0 * sn + y1 * cs;
+          dth += (-g1.x * ob1 + g1.y * ob0) + (-g2.x * oc1 + g2.y * oc0);
+          g1 = make_float2(g1.x * cs + g1.y * sn, -g1.x * sn + g1.y * cs);
+          g2 = make_float2(g2.x * cs + g2.y * sn, -g2.x * sn + g2.y * cs);
+        }
+        float4 acc = sbias[r * np + sl];
+        acc.x += g1.x; acc.y += g1.y; acc.z += g2.x; acc.w += g2.y;
+        sbias[r * np + sl] = acc;
+        dnb0[r] += g1.x; dnb1[r] += g1.y; dnc0[r] += g2.x; dnc1[r] += g2.y;
+      }
+      if (rot) a.dtheta[(row * H + h) * S + k] = dth;
+    }
+    if (kcur >= 0) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        atomicAdd(&sdn[r * D + 2 * kcur], dnb0[r]); atomicAdd(&sdn[r * D + 2 * kcur + 1], dnb1[r]);
+        atomicAdd(&sdn[RD + r * D + 2 * kcur], dnc0[r]); atomicAdd(&sdn[RD + r * D + 2 * kcur + 1], dnc1[r]);
+      }
+    }
+    __syncthreads();
+    // RMSNorm backward of (B or C, rank): draw = (w dn) / rms - raw sum(w dn raw) / (D rms^3)
+    for (int it = warp; it < 2 * R; it += kBC1 / 32) {
+      const float* w = it < R ? a.B_norm_w : a.C_norm_w;
+      const float rr = rs[it];
+      float pb = 0.f;
+      for (int d = lane; d < D; d += 32) pb = fmaf(__ldg(w + d) * sdn[it * D + d], raw[it * D + d], pb);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) pb += __shfl_xor_sync(0xffffffffu, pb, o);
+      const float kk = pb * rr * rr * rr / (float)D;
+      for (int d = lane; d < D; d += 32) {
+        const float dn = sdn[it * D + d], rv = raw[it * D + d];
+        drow[it * D + d] = from_f32<TZ>(fmaf(__ldg(w + d) * dn, rr, -rv * kk));
+        swb[it * D + d] = fmaf(dn, rv * rr, swb[it * D + d]);
+      }
+    }
+  }
+  // the CTA's partial sums into its slot: bias gradients (H, R, D) of B and C, then the
+  // norm-weight gradients (D) of B and C
+  __syncthreads();
+  const int HRD = H * R * D;
+  float* slot = a.bc_part + (int64_t)blockIdx.x * (2 * HRD + 2 * D);
+  for (int i = tid; i < HRD; i += kBC1) {
+    const int h = i / (R * D), rem = i - h * R * D, r = rem / D, d = rem - r * D;
+    const float4 v = sbias[r * np + h * half + (d >> 1)];
+    slot[i] = (d & 1) ? v.y : v.x;
+    slot[HRD + i] = (d & 1) ? v.w : v.z;
+  }
+  for (int d = tid; d < D; d += kBC1) {
+    float sb = 0.f, sc = 0.f;
+    for (int r = 0; r < R; ++r) {
+      sb += swb[r * D + d];
+      sc += swb[RD + r * D + d];
+    }
+    slot[2 * HRD + d] = sb;
+    slot[2 * HRD + D + d] = sc;
+  }
+}
+
 // CTA per (b, h); thread = step of a 128-step tile walked from the end; suffix sums over l
 // of dtheta[b,l,h,i] for the S angles, 16 at a time, carried between tiles
 template <typename TZ>
@@ -401,6 +544,22 @@ size_t prologue_bwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t S,
   return sizeof(float) * (size_t)(rows * (H * S + H + S) + bc_slots(rows, H, R, D) * (2 * H * R * D + 2 * D));
 }
 
+// Launch of the slot-per-thread bc kernel: as many CTAs as fit on the device at once, at
+// most `slots` (each CTA writes one slot); *used = the CTAs launched.
+template <typename K>
+int bc1_launch(K k, const PrologueBwdParams& p, size_t smem, unsigned slots, unsigned* used, cudaStream_t s) {
+  if (smem > 48 * 1024) {
+    cudaError_t ea = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (ea != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ea));
+  }
+  int per_sm = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kBC1, smem) != cudaSuccess || per_sm < 1) per_sm = 1;
+  if (device_sm_count(&sms) != M3_OK) sms = 148;
+  *used = std::min<unsigned>(slots, (unsigned)(per_sm * sms));
+  k<<<*used, kBC1, smem, s>>>(p);
+  return check_launch("prologue_bwd_bc1_kernel");
+}
+
 int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt, cudaStream_t s) {
   PrologueBwdParams p = p0;
   if (p.S > 64) return fail(M3_ERR_UNSUPPORTED, "prologue backward: more than 64 rope angles");
@@ -425,20 +584,32 @@ int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt
   const size_t smem = sizeof(float) * (size_t)(2 * p.H * p.R * p.D + p.H * p.S + 2 * p.R * p.D);
   if (smem > 200 * 1024) return fail(M3_ERR_UNSUPPORTED, "prologue backward: nheads * rank * d_state too large");
   const unsigned gbc = (unsigned)nslots;
+  // one B / C group and a power-of-two rank up to 8: the slot-per-thread kernel
+  const size_t smem1 = sizeof(float) * ((size_t)2 * p.H * p.R * p.D + 6 * (size_t)p.R * p.D + 2 * p.R);
+  const bool bc1 = p.G == 1 && (p.R == 1 || p.R == 2 || p.R == 4 || p.R == 8) && smem1 <= 200 * 1024 &&
+                   ((reinterpret_cast<uintptr_t>(p.B_norm_w) | reinterpret_cast<uintptr_t>(p.C_norm_w)) & 7) == 0;
   const int ppl = (p.D / 2 + 31) / 32;
   const unsigned gdt = (unsigned)((rows * p.H + 255) / 256);
 #define M3_PBWD(TZ, TO)                                                                                  \
   do {                                                                                                   \
-    auto kbc = ppl == 1 ? prologue_bwd_bc_kernel<TZ, TO, 1>                                              \
-                        : (ppl == 2 ? prologue_bwd_bc_kernel<TZ, TO, 2> : prologue_bwd_bc_kernel<TZ, TO, 4>); \
-    if (smem > 48 * 1024) {                                                                              \
-      cudaError_t ea = cudaFuncSetAttribute(kbc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-      if (ea != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ea)); \
+    unsigned used = gbc;                                                                                 \
+    if (bc1) {                                                                                           \
+      auto k1 = p.R == 1 ? prologue_bwd_bc1_kernel<TZ, TO, 1>                                            \
+                         : p.R == 2 ? prologue_bwd_bc1_kernel<TZ, TO, 2>                                 \
+                                    : p.R == 4 ? prologue_bwd_bc1_kernel<TZ, TO, 4> : prologue_bwd_bc1_kernel<TZ, TO, 8>; \
+      M3_TRY(bc1_launch(k1, p, smem1, gbc, &used, s));                                                   \
+    } else {                                                                                             \
+      auto kbc = ppl == 1 ? prologue_bwd_bc_kernel<TZ, TO, 1>                                            \
+                          : (ppl == 2 ? prologue_bwd_bc_kernel<TZ, TO, 2> : prologue_bwd_bc_kernel<TZ, TO, 4>); \
+      if (smem > 48 * 1024) {                                                                            \
+        cudaError_t ea = cudaFuncSetAttribute(kbc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+        if (ea != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ea)); \
+      }                                                                                                  \
+      kbc<<<gbc, 32 * p.R, smem, s>>>(p);                                                                \
+      M3_TRY(check_launch("prologue_bwd_bc_kernel"));                                                    \
     }                                                                                                    \
-    kbc<<<gbc, 32 * p.R, smem, s>>>(p);                                                                  \
-    M3_TRY(check_launch("prologue_bwd_bc_kernel"));                                                      \
-    bc_reduce_kernel<<<dim3((unsigned)((W + 255) / 256), (unsigned)((nslots + kSlotsPerThread - 1) / kSlotsPerThread)), \
-                       256, 0, s>>>(p, (int)nslots);                                                      \
+    bc_reduce_kernel<<<dim3((unsigned)((W + 255) / 256), (unsigned)((used + kSlotsPerThread - 1) / kSlotsPerThread)), \
+                       256, 0, s>>>(p, (int)used);                                                        \
     M3_TRY(check_launch("bc_reduce_kernel"));                                                            \
     prologue_bwd_angle_kernel<TZ><<<(unsigned)(p.Bn * p.H), kAT, 0, s>>>(p);                             \
     M3_TRY(check_launch("prologue_bwd_angle_kernel"));                                                   \
