@@ -822,11 +822,12 @@ int m3_argmax_rows(const m3_tensor* logits, m3_tensor* out, void* stream) {
 
 int m3_device_timeouts(int reset, int* flag_out) {
   if (!flag_out) return fail(M3_ERR_INVALID_ARGUMENT, "flag_out: missing");
-  int f = 0, b = 0, m = 0;
+  int f = 0, b = 0, m = 0, q = 0;
   M3_TRY(chunk_error_word(reset != 0, &f));
   M3_TRY(chunk_bwd_error_word(reset != 0, &b));
   M3_TRY(mimo_error_word(reset != 0, &m));
-  *flag_out = f | b | m;
+  M3_TRY(prologue_error_word(reset != 0, &q));
+  *flag_out = f | b | m | q;
   return M3_OK;
 }
 

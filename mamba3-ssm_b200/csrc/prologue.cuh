@@ -61,6 +61,8 @@ struct GateBwdParams {
 };
 
 int launch_prologue(const PrologueParams& p, int zdt, int odt, cudaStream_t s);
+// the word the prologue backward's bulk-copy waits set when they give up
+int prologue_error_word(bool reset, int* out);
 size_t prologue_bwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t S, int64_t R, int64_t D);
 int launch_prologue_bwd(const PrologueBwdParams& p, float* ws, int zdt, int odt, cudaStream_t s);
 int launch_gate_bwd(const GateBwdParams& p, int ydt, int zdt, int ddt, cudaStream_t s);

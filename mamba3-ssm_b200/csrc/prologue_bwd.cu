@@ -26,6 +26,7 @@
 
 #include "m3_common.cuh"
 #include "prologue.cuh"
+#include "sm100.cuh"
 
 namespace m3 {
 namespace {
@@ -262,39 +263,94 @@ __global__ void __launch_bounds__(256) bc_reduce_kernel(PrologueBwdParams a, int
 // for every rank: the angle's sin / cos once per (row, head, pair) for all ranks and both B
 // and C, dtheta summed in registers and written once, the bias gradients in thread-private
 // shared-memory slots, dn (the sum over heads) through shared-memory atomics, one per
-// (thread, rank, element) and row. CTAs stride over the rows; the RMSNorm backward of a
-// row is a warp per (B or C, rank). Partial sums go to the CTA's workspace slot as in the
-// general kernel.
+// (thread, rank, element) and row. CTAs stride over the rows; a row's dB / dC block, raw
+// B / C group rows and angles arrive by bulk copies into one of two buffers while the CTA
+// works on the row before (bounded waits). The RMSNorm backward of a row is a warp per
+// (B or C, rank). Partial sums go to the CTA's workspace slot as in the general kernel.
 constexpr int kBC1 = 256;
+__device__ int g_prologue_error;  // set when a bounded wait gives up
+
+struct Bc1Smem {
+  uint32_t bias, gb[2], gc[2], zr[2], an[2], rs, sdn, swb, total;
+};
+__host__ __device__ inline uint32_t bc1_up(uint32_t v) { return (v + 127u) & ~127u; }
+__host__ __device__ inline Bc1Smem bc1_smem(int H, int R, int D, int S, int ez, int eo) {
+  Bc1Smem L;
+  uint32_t o = 128;  // two mbarriers
+  L.bias = o; o = bc1_up(o + (uint32_t)(2 * H * R * D * 4));
+  for (int k = 0; k < 2; ++k) {
+    L.gb[k] = o; o = bc1_up(o + (uint32_t)(R * H * D * eo));
+    L.gc[k] = o; o = bc1_up(o + (uint32_t)(R * H * D * eo));
+    L.zr[k] = o; o = bc1_up(o + (uint32_t)(2 * R * D * ez));
+    L.an[k] = o; o = bc1_up(o + (uint32_t)(H * S * 4));
+  }
+  L.rs = o; o = bc1_up(o + (uint32_t)(2 * R * 4));
+  L.sdn = o; o = bc1_up(o + (uint32_t)(2 * R * D * 4));
+  L.swb = o; o = bc1_up(o + (uint32_t)(2 * R * D * 4));
+  L.total = o + 128;  // slack for aligning the base
+  return L;
+}
+
 template <typename TZ, typename TO, int RT>
-__global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParams a) {
-  extern __shared__ float4 sm4[];
+__global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParams a, Bc1Smem L) {
+  extern __shared__ __align__(128) unsigned char bsm_raw[];
+  unsigned char* bsm = bsm_raw + ((128u - (sm100::smem_u32(bsm_raw) & 127u)) & 127u);
   constexpr int R = RT;
   const int D = a.D, H = a.H, S = a.S, half = D / 2, npair = a.split / 2;
   const int np = H * half;  // (head, pair) slots of a row
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float4* sbias = sm4;                                          // [r][slot]: (dB0, dB1, dC0, dC1)
-  float* raw = reinterpret_cast<float*>(sm4 + (size_t)R * np);  // (2, R, D): the row's raw B, C group rows
-  float* rs = raw + 2 * R * D;                                  // (2, R): 1 / rms
-  float* sdn = rs + 2 * R;                                      // (2, R, D): dn = sum over heads of dv
-  float* swb = sdn + 2 * R * D;                                 // (2, R, D): norm-weight gradient partials
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bsm);
+  float4* sbias = reinterpret_cast<float4*>(bsm + L.bias);  // [r][slot]: (dB0, dB1, dC0, dC1)
+  float* rs = reinterpret_cast<float*>(bsm + L.rs);         // (2, R): 1 / rms
+  float* sdn = reinterpret_cast<float*>(bsm + L.sdn);       // (2, R, D): dn = sum over heads of dv
+  float* swb = reinterpret_cast<float*>(bsm + L.swb);       // (2, R, D): norm-weight gradient partials
+  const int64_t RD = (int64_t)R * D;
+  const uint32_t gbytes = (uint32_t)(R * H * D * sizeof(TO)), zbytes = (uint32_t)(2 * RD * sizeof(TZ)),
+                 abytes = (uint32_t)(H * S * 4);
+  const int64_t nrows = (int64_t)a.Bn * a.L;
+  auto issue = [&](int64_t row, int kb) {
+    const int64_t b = row / a.L, l = row - b * a.L;
+    uint64_t* bar = &bars[kb];
+    sm100::mbar_expect_tx(bar, 2 * gbytes + zbytes + abytes);
+    sm100::bulk_load(bsm + (kb ? L.gb[1] : L.gb[0]), reinterpret_cast<const TO*>(a.dBp) + row * R * H * D, gbytes, bar);
+    sm100::bulk_load(bsm + (kb ? L.gc[1] : L.gc[0]), reinterpret_cast<const TO*>(a.dCp) + row * R * H * D, gbytes, bar);
+    sm100::bulk_load(bsm + (kb ? L.zr[1] : L.zr[0]),
+                     reinterpret_cast<const TZ*>(a.zx) + b * a.s_zb + l * a.s_zl + 2 * a.d_inner, zbytes, bar);
+    sm100::bulk_load(bsm + (kb ? L.an[1] : L.an[0]), a.angles + row * H * S, abytes, bar);
+  };
+  if (tid == 0) {
+    sm100::mbar_init(&bars[0], 1);
+    sm100::mbar_init(&bars[1], 1);
+    sm100::fence_barrier_init();
+  }
   for (int i = tid; i < R * np; i += kBC1) sbias[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int i = tid; i < 2 * R * D; i += kBC1) swb[i] = 0.f;
-  const int64_t nrows = (int64_t)a.Bn * a.L;
-  const int64_t RD = (int64_t)R * D;
-  for (int64_t row = blockIdx.x; row < nrows; row += gridDim.x) {
-    const int64_t b = row / a.L, l = row - b * a.L;
-    const TZ* zrow = reinterpret_cast<const TZ*>(a.zx) + b * a.s_zb + l * a.s_zl + 2 * a.d_inner;
-    TZ* drow = reinterpret_cast<TZ*>(a.dzx) + b * a.s_dzb + l * a.s_dzl + 2 * a.d_inner;
-    __syncthreads();  // the previous row is done with raw, rs and sdn
-    for (int i = tid; i < 2 * R * D; i += kBC1) {
-      raw[i] = to_f32(zrow[i]);  // B rows (R, D), then C rows (R, D)
-      sdn[i] = 0.f;
+  __syncthreads();
+  if (tid == 0 && blockIdx.x < nrows) issue(blockIdx.x, 0);
+  uint32_t par0 = 0u, par1 = 0u;
+  int k = 0;
+  for (int64_t row = blockIdx.x; row < nrows; row += gridDim.x, k ^= 1) {
+    __syncthreads();  // the previous row is done with the other buffer, rs and sdn
+    if (tid == 0 && row + gridDim.x < nrows) issue(row + gridDim.x, k ^ 1);
+    const uint32_t pk = k ? par1 : par0;
+    if (!sm100::mbar_wait(&bars[k], pk, 1u << 24)) {  // give up: flag it, wait once more for the copies
+      atomicExch(&g_prologue_error, 1);
+      sm100::mbar_wait(&bars[k], pk, 1u << 24);
     }
-    __syncthreads();
+    if (k) par1 ^= 1u; else par0 ^= 1u;
+    const TO* gbs = reinterpret_cast<const TO*>(bsm + (k ? L.gb[1] : L.gb[0]));
+    const TO* gcs = reinterpret_cast<const TO*>(bsm + (k ? L.gc[1] : L.gc[0]));
+    const TZ* zr = reinterpret_cast<const TZ*>(bsm + (k ? L.zr[1] : L.zr[0]));  // B rows (R, D), then C rows (R, D)
+    const float* an = reinterpret_cast<const float*>(bsm + (k ? L.an[1] : L.an[0]));
+    const int64_t b = row / a.L, l = row - b * a.L;
+    TZ* drow = reinterpret_cast<TZ*>(a.dzx) + b * a.s_dzb + l * a.s_dzl + 2 * a.d_inner;
+    for (int i = tid; i < 2 * R * D; i += kBC1) sdn[i] = 0.f;
     for (int it = warp; it < 2 * R; it += kBC1 / 32) {
       float ss = 0.f;
-      for (int d = lane; d < D; d += 32) ss = fmaf(raw[it * D + d], raw[it * D + d], ss);
+      for (int d = lane; d < D; d += 32) {
+        const float v = to_f32(zr[it * D + d]);
+        ss = fmaf(v, v, ss);
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if (lane == 0) rs[it] = 1.0f / sqrtf(ss / (float)D + a.eps);
@@ -305,8 +361,8 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
 #pragma unroll
     for (int r = 0; r < R; ++r) dnb0[r] = dnb1[r] = dnc0[r] = dnc1[r] = 0.f;
     for (int sl = tid; sl < np; sl += kBC1) {
-      const int h = sl / half, k = sl - h * half, d0 = 2 * k;
-      if (k != kcur) {  // flush the running sums over heads of the previous pair
+      const int h = sl / half, kp = sl - h * half, d0 = 2 * kp;
+      if (kp != kcur) {  // flush the running sums over heads of the previous pair
         if (kcur >= 0) {
 #pragma unroll
           for (int r = 0; r < R; ++r) {
@@ -315,33 +371,25 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
             dnb0[r] = dnb1[r] = dnc0[r] = dnc1[r] = 0.f;
           }
         }
-        kcur = k;
+        kcur = kp;
       }
-      const TO* gBh = reinterpret_cast<const TO*>(a.dBp) + (row * R * H + h) * D + d0;
-      const TO* gCh = reinterpret_cast<const TO*>(a.dCp) + (row * R * H + h) * D + d0;
-      float2 gb[R], gc[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        gb[r] = ld_pair(gBh + (int64_t)r * H * D);
-        gc[r] = ld_pair(gCh + (int64_t)r * H * D);
-      }
-      const bool rot = k < npair;
+      const bool rot = kp < npair;
       float sn = 0.f, cs = 1.f;
-      if (rot) sincos_reduced(__ldg(a.angles + (row * H + h) * S + k), &sn, &cs);
+      if (rot) sincos_reduced(an[h * S + kp], &sn, &cs);
       const float2 wb = __ldg(reinterpret_cast<const float2*>(a.B_norm_w + d0));
       const float2 wc = __ldg(reinterpret_cast<const float2*>(a.C_norm_w + d0));
       float dth = 0.f;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        float2 g1 = gb[r], g2 = gc[r];
+        float2 g1 = ld_pair(gbs + ((int64_t)r * H + h) * D + d0), g2 = ld_pair(gcs + ((int64_t)r * H + h) * D + d0);
         if (rot) {
           // o = rot(v), v = n + bias; dtheta = -g1 o2 + g2 o1; dv = rot^T(g)
           const float2 bv = __ldg(reinterpret_cast<const float2*>(a.B_bias + ((int64_t)h * R + r) * D + d0));
           const float2 cv = __ldg(reinterpret_cast<const float2*>(a.C_bias + ((int64_t)h * R + r) * D + d0));
           const float rb = rs[r], rc = rs[R + r];
-          const float x0 = fmaf(raw[r * D + d0] * rb, wb.x, bv.x), x1 = fmaf(raw[r * D + d0 + 1] * rb, wb.y, bv.y);
-          const float y0 = fmaf(raw[RD + r * D + d0] * rc, wc.x, cv.x);
-          const float y1 = fmaf(raw[RD + r * D + d0 + 1] * rc, wc.y, cv.y);
+          const float2 zb = ld_pair(zr + r * D + d0), zc = ld_pair(zr + RD + r * D + d0);
+          const float x0 = fmaf(zb.x * rb, wb.x, bv.x), x1 = fmaf(zb.y * rb, wb.y, bv.y);
+          const float y0 = fmaf(zc.x * rc, wc.x, cv.x), y1 = fmaf(zc.y * rc, wc.y, cv.y);
           const float ob0 = x0 * cs - x1 * sn, ob1 = x0 * sn + x1 * cs;
           const float oc0 = y0 * cs - y1 * sn, oc1 = y0 * sn + y1 * cs;
           dth += (-g1.x * ob1 + g1.y * ob0) + (-g2.x * oc1 + g2.y * oc0);
@@ -353,7 +401,7 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
         sbias[r * np + sl] = acc;
         dnb0[r] += g1.x; dnb1[r] += g1.y; dnc0[r] += g2.x; dnc1[r] += g2.y;
       }
-      if (rot) a.dtheta[(row * H + h) * S + k] = dth;
+      if (rot) a.dtheta[(row * H + h) * S + kp] = dth;
     }
     if (kcur >= 0) {
 #pragma unroll
@@ -368,12 +416,12 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
       const float* w = it < R ? a.B_norm_w : a.C_norm_w;
       const float rr = rs[it];
       float pb = 0.f;
-      for (int d = lane; d < D; d += 32) pb = fmaf(__ldg(w + d) * sdn[it * D + d], raw[it * D + d], pb);
+      for (int d = lane; d < D; d += 32) pb = fmaf(__ldg(w + d) * sdn[it * D + d], to_f32(zr[it * D + d]), pb);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) pb += __shfl_xor_sync(0xffffffffu, pb, o);
       const float kk = pb * rr * rr * rr / (float)D;
       for (int d = lane; d < D; d += 32) {
-        const float dn = sdn[it * D + d], rv = raw[it * D + d];
+        const float dn = sdn[it * D + d], rv = to_f32(zr[it * D + d]);
         drow[it * D + d] = from_f32<TZ>(fmaf(__ldg(w + d) * dn, rr, -rv * kk));
         swb[it * D + d] = fmaf(dn, rv * rr, swb[it * D + d]);
       }
@@ -528,7 +576,87 @@ __global__ void __launch_bounds__(256) gate_bwd_kernel(GateBwdParams a) {
   }
 }
 
+// The gate backward on 16-byte groups of p (one dtype for all five tensors, rows and strides
+// in whole 16-byte units): index arithmetic once per group, 16-byte loads and stores.
+struct Div32 {
+  uint32_t m, s;
+};
+inline Div32 make_div32(uint32_t d) {
+  Div32 f;
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  f.s = s;
+  f.m = (uint32_t)(((1ull << 32) * ((1ull << s) - d)) / d + 1);  // round-up multiplier (Granlund-Montgomery)
+  return f;
+}
+__device__ __forceinline__ uint32_t div32(uint32_t x, Div32 f) { return (__umulhi(x, f.m) + x) >> f.s; }
+
+template <typename T>
+__global__ void __launch_bounds__(256) gate_bwd_vec_kernel(GateBwdParams a, Div32 fpc, Div32 fh, Div32 flh,
+                                                           uint32_t ngroups) {
+  constexpr int V = 16 / sizeof(T);
+  const uint32_t PC = (uint32_t)a.P / V;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += gridDim.x * blockDim.x) {
+    const uint32_t r = div32(i, fpc), j = i - r * PC;
+    const uint32_t b = div32(r, flh), rem = r - b * (uint32_t)(a.L * a.H);
+    const uint32_t l = div32(rem, fh), h = rem - l * (uint32_t)a.H;
+    const int64_t p = (int64_t)j * V;
+    auto at = [&](const Str3& st) { return (int64_t)b * st.b + (int64_t)l * st.l + (int64_t)h * st.h + p; };
+    const uint4 yw = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.y) + at(a.sy));
+    const uint4 zw = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.z) + at(a.sz));
+    const uint4 gw = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.dout) + at(a.sd));
+    const T* yv = reinterpret_cast<const T*>(&yw);
+    const T* zv = reinterpret_cast<const T*>(&zw);
+    const T* gv = reinterpret_cast<const T*>(&gw);
+    uint4 dyw, dzw;
+    T* dyv = reinterpret_cast<T*>(&dyw);
+    T* dzv = reinterpret_cast<T*>(&dzw);
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const float y = to_f32(yv[e]), z = to_f32(zv[e]), g = to_f32(gv[e]);
+      const float sg = sigmoidf_(z);
+      dyv[e] = from_f32<T>(g * z * sg);
+      dzv[e] = from_f32<T>(g * y * sg * (1.0f + z * (1.0f - sg)));
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.dy) + at(a.sdy)) = dyw;
+    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.dz) + at(a.sdz)) = dzw;
+  }
+}
+
+template <typename T>
+bool gate_vec_ok(const GateBwdParams& p) {
+  const int64_t e = sizeof(T), V = 16 / e;
+  auto al = [&](const void* q, const Str3& st) {
+    return reinterpret_cast<uintptr_t>(q) % 16 == 0 && (st.b * e) % 16 == 0 && (st.l * e) % 16 == 0 &&
+           (st.h * e) % 16 == 0;
+  };
+  return p.P % V == 0 && p.rows * (p.P / V) < (int64_t(1) << 31) && al(p.y, p.sy) && al(p.z, p.sz) &&
+         al(p.dout, p.sd) && al(p.dy, p.sdy) && al(p.dz, p.sdz);
+}
+
+template <typename T>
+int launch_gate_bwd_vec(const GateBwdParams& p, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  const uint32_t ng = (uint32_t)(p.rows * (p.P / V));
+  const unsigned grid = (unsigned)std::min<int64_t>((ng + 255) / 256, 148 * 16);
+  gate_bwd_vec_kernel<T><<<grid, 256, 0, s>>>(p, make_div32((uint32_t)(p.P / V)), make_div32((uint32_t)p.H),
+                                              make_div32((uint32_t)(p.L * p.H)), ng);
+  return check_launch("gate_bwd_vec_kernel");
+}
+
 }  // namespace
+
+int prologue_error_word(bool reset, int* out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_prologue_error, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_prologue_error, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("prologue error word: ") + cudaGetErrorString(e));
+  *out = v;
+  return M3_OK;
+}
 
 // Slots of the bc kernel's partial sums: one per CTA, at most 1024 and at most 32 MB.
 int64_t bc_slots(int64_t rows, int64_t H, int64_t R, int64_t D) {
@@ -547,7 +675,9 @@ size_t prologue_bwd_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t S,
 // Launch of the slot-per-thread bc kernel: as many CTAs as fit on the device at once, at
 // most `slots` (each CTA writes one slot); *used = the CTAs launched.
 template <typename K>
-int bc1_launch(K k, const PrologueBwdParams& p, size_t smem, unsigned slots, unsigned* used, cudaStream_t s) {
+int bc1_launch(K k, const PrologueBwdParams& p, const Bc1Smem& L, unsigned slots, unsigned* used,
+               cudaStream_t s) {
+  const size_t smem = L.total;
   if (smem > 48 * 1024) {
     cudaError_t ea = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (ea != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ea));
@@ -556,7 +686,7 @@ int bc1_launch(K k, const PrologueBwdParams& p, size_t smem, unsigned slots, uns
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kBC1, smem) != cudaSuccess || per_sm < 1) per_sm = 1;
   if (device_sm_count(&sms) != M3_OK) sms = 148;
   *used = std::min<unsigned>(slots, (unsigned)(per_sm * sms));
-  k<<<*used, kBC1, smem, s>>>(p);
+  k<<<*used, kBC1, smem, s>>>(p, L);
   return check_launch("prologue_bwd_bc1_kernel");
 }
 
@@ -585,9 +715,18 @@ int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt
   if (smem > 200 * 1024) return fail(M3_ERR_UNSUPPORTED, "prologue backward: nheads * rank * d_state too large");
   const unsigned gbc = (unsigned)nslots;
   // one B / C group and a power-of-two rank up to 8: the slot-per-thread kernel
-  const size_t smem1 = sizeof(float) * ((size_t)2 * p.H * p.R * p.D + 6 * (size_t)p.R * p.D + 2 * p.R);
-  const bool bc1 = p.G == 1 && (p.R == 1 || p.R == 2 || p.R == 4 || p.R == 8) && smem1 <= 200 * 1024 &&
-                   ((reinterpret_cast<uintptr_t>(p.B_norm_w) | reinterpret_cast<uintptr_t>(p.C_norm_w)) & 7) == 0;
+  // one B / C group, a power-of-two rank up to 8, and every row's blocks on 16-byte
+  // boundaries in whole 16-byte units (bulk copies): the slot-per-thread kernel
+  const int ez = zdt == M3_FLOAT32 ? 4 : 2, eo = odt == M3_FLOAT32 ? 4 : 2;
+  const Bc1Smem L1 = bc1_smem(p.H, p.R, p.D, p.S, ez, eo);
+  auto a16 = [](int64_t v) { return v % 16 == 0; };
+  const bool bc1 = p.G == 1 && (p.R == 1 || p.R == 2 || p.R == 4 || p.R == 8) && L1.total <= 200 * 1024 &&
+                   ((reinterpret_cast<uintptr_t>(p.B_norm_w) | reinterpret_cast<uintptr_t>(p.C_norm_w)) & 7) == 0 &&
+                   a16((int64_t)p.R * p.H * p.D * eo) && a16(2 * (int64_t)p.R * p.D * ez) &&
+                   a16((int64_t)p.H * p.S * 4) && p.S > 0 && a16(p.s_zb * ez) && a16(p.s_zl * ez) &&
+                   a16(2 * (int64_t)p.d_inner * ez) &&
+                   ((reinterpret_cast<uintptr_t>(p.zx) | reinterpret_cast<uintptr_t>(p.dBp) |
+                     reinterpret_cast<uintptr_t>(p.dCp) | reinterpret_cast<uintptr_t>(p.angles)) & 15) == 0;
   const int ppl = (p.D / 2 + 31) / 32;
   const unsigned gdt = (unsigned)((rows * p.H + 255) / 256);
 #define M3_PBWD(TZ, TO)                                                                                  \
@@ -597,7 +736,7 @@ int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt
       auto k1 = p.R == 1 ? prologue_bwd_bc1_kernel<TZ, TO, 1>                                            \
                          : p.R == 2 ? prologue_bwd_bc1_kernel<TZ, TO, 2>                                 \
                                     : p.R == 4 ? prologue_bwd_bc1_kernel<TZ, TO, 4> : prologue_bwd_bc1_kernel<TZ, TO, 8>; \
-      M3_TRY(bc1_launch(k1, p, smem1, gbc, &used, s));                                                   \
+      M3_TRY(bc1_launch(k1, p, L1, gbc, &used, s));                                                   \
     } else {                                                                                             \
       auto kbc = ppl == 1 ? prologue_bwd_bc_kernel<TZ, TO, 1>                                            \
                           : (ppl == 2 ? prologue_bwd_bc_kernel<TZ, TO, 2> : prologue_bwd_bc_kernel<TZ, TO, 4>); \
@@ -633,6 +772,11 @@ int launch_gate_bwd(const GateBwdParams& p, int ydt, int zdt, int ddt, cudaStrea
     gate_bwd_kernel<TY, TZ, TD><<<grid, 256, 0, s>>>(p); \
     return check_launch("gate_bwd_kernel");              \
   } while (0)
+  if (ydt == zdt && zdt == ddt && (int64_t)p.L * p.H < (int64_t(1) << 31)) {
+    if (ydt == M3_BFLOAT16 && gate_vec_ok<__nv_bfloat16>(p)) return launch_gate_bwd_vec<__nv_bfloat16>(p, s);
+    if (ydt == M3_FLOAT32 && gate_vec_ok<float>(p)) return launch_gate_bwd_vec<float>(p, s);
+    if (ydt == M3_FLOAT16 && gate_vec_ok<__half>(p)) return launch_gate_bwd_vec<__half>(p, s);
+  }
   if (ydt == M3_BFLOAT16 && zdt == M3_BFLOAT16 && ddt == M3_BFLOAT16) M3_GB(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
   if (ydt == M3_FLOAT32 && zdt == M3_FLOAT32 && ddt == M3_FLOAT32) M3_GB(float, float, float);
   if (ydt == M3_FLOAT16 && zdt == M3_FLOAT16 && ddt == M3_FLOAT16) M3_GB(__half, __half, __half);
