@@ -891,7 +891,7 @@ __global__ void __launch_bounds__(kFT)
 // and partial sums of dD, dmimo_x, dmimo_o (atomics). x, B, C and dy arrive as TMA boxes.
 // ------------------------------------------------------------------------------------
 struct FusedBwdSmem {
-  uint32_t bs, cs, xs, dys, bx, hs, gs, xr, dyr, dxr, yr, coef, trdt, dbg, red, mx, mo, total;
+  uint32_t bs, cs, xs, dys, bx, hs, gs, xr, dyr, dxr, yr, coef, trdt, dbg, red, mx, mo, rq, carry, total;
 };
 __host__ __device__ inline FusedBwdSmem fused_bwd_smem(int Q, int P, int R, int D, int eb, int ex) {
   FusedBwdSmem L;
@@ -913,6 +913,8 @@ __host__ __device__ inline FusedBwdSmem fused_bwd_smem(int Q, int P, int R, int 
   L.red = o; o = aup(o + (uint32_t)(Q * 4), 16);                  // per-step dADT terms
   L.mx = o; o = aup(o + (uint32_t)(R * (P + 4) * 4), 16);
   L.mo = o; o = aup(o + (uint32_t)(R * (P + 4) * 4), 16);
+  L.rq = o; o = aup(o + (uint32_t)(Q * 4), 16);                   // a_{t+1} .. a_{t0+n} per step
+  L.carry = o; o = aup(o + (uint32_t)(D * 4), 16);                // adjoint entering from the right
   L.total = o + 128;
   return L;
 }
@@ -995,6 +997,8 @@ __global__ void __launch_bounds__(kFT)
   float* red = reinterpret_cast<float*>(fsm + L.red);
   float* mx = reinterpret_cast<float*>(fsm + L.mx);
   float* mo = reinterpret_cast<float*>(fsm + L.mo);
+  float* rq = reinterpret_cast<float*>(fsm + L.rq);
+  float* carry_s = reinterpret_cast<float*>(fsm + L.carry);
 
   if (tid == 0) {
     *tk_s = (int)atomicAdd(f.ticket, 1u);
@@ -1113,12 +1117,27 @@ __global__ void __launch_bounds__(kFT)
         }
       }
     }
+    // the local adjoint from a zero adjoint after the chunk, eight steps per batch of
+    // shared-memory reads; column 0 records the decay from each step to the chunk's end
     float gl = 0.f, pr = 1.f;
-    for (int t = n - 1; t >= 0; --t) {
-      const float an = coef[t + 1].x;
-      gl = fmaf(an, gl, gs[t * D + d]);
-      pr *= an;
-      gs[t * D + d] = gl;
+    for (int te = n; te > 0; te -= 8) {
+      float ev[8], an[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int t = te - 1 - j;
+        ev[j] = t >= 0 ? gs[t * D + d] : 0.f;
+        an[j] = t >= 0 ? coef[t + 1].x : 1.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int t = te - 1 - j;
+        gl = fmaf(an[j], gl, ev[j]);
+        pr *= an[j];
+        if (t >= 0) {
+          gs[t * D + d] = gl;
+          if (d == 0) rq[t] = pr;
+        }
+      }
     }
     float carry = 0.f;
     if (c < f.nch - 1) {
@@ -1126,82 +1145,95 @@ __global__ void __launch_bounds__(kFT)
       if (d == 0) st_relaxed64(f.arec + cell, pr, 1);
       carry = look_ahead(f, u, c, d, D, ok);
     }
-    st_relaxed64(f.rec + cell * D + d, fmaf(pr, carry, gl), 2);
+    const float g0 = fmaf(pr, carry, gl);  // the true adjoint at the chunk's first step
+    st_relaxed64(f.rec + cell * D + d, g0, 2);
+    carry_s[d] = carry;
     gs[n * D + d] = carry;
-    float q = 1.f;
-    for (int t = n - 1; t >= 0; --t) {
-      q *= coef[t + 1].x;
-      gs[t * D + d] = fmaf(q, carry, gs[t * D + d]);
-    }
     if (c == 0) {
-      const float g0 = gs[d];
       if (a.dh0) a.dh0[(int64_t)u * D + d] = coef[0].x * g0;
       if (a.dbx0) a.dbx0[(int64_t)u * D + d] = coef[0].z * g0;
     }
   }
   if (!ok) atomicExch(&g_mimo_error, 1);
   __syncthreads();
-  // per (t, r): v = beta_t g_t + gamma_{t+1} g_{t+1}; dC = dyr h, dB = xr v, and the dots
-  // dxr = B . v + D dyr, yr = C . h + D xr; lpr lanes per row, four columns a lane
+  // the true adjoints g_t = gl_t + (a_{t+1} .. a_{t0+n}) carry, four columns a thread
+  for (int i = tid; i < n * D4; i += kFT) {
+    const int t = fdiv(i, f.fD4), d = 4 * (i - t * D4);
+    float4 g4 = *reinterpret_cast<const float4*>(gs + t * D + d);
+    fma4(g4, rq[t], *reinterpret_cast<const float4*>(carry_s + d));
+    *reinterpret_cast<float4*>(gs + t * D + d) = g4;
+  }
+  __syncthreads();
+  if (!ok) atomicExch(&g_mimo_error, 1);
+  __syncthreads();
+  // per (t, four-column block): v = beta_t g_t + gamma_{t+1} g_{t+1} once, then for each
+  // rank dC = dyr h, dB = xr v and the partial dots dxr = B . v, yr = C . h, and the step's
+  // dbeta = g_t . bx_t, dgamma = g_t . bx_{t-1}; lpr lanes per step, ranks four at a time
   const float Dk = a.Dskip[h * a.sD];
   int lpr = 1;
   while (lpr * 2 <= 32 && lpr * 2 <= D4) lpr *= 2;
   const int rpw = 32 / lpr, part = lane & (lpr - 1);
   TB* dBb = reinterpret_cast<TB*>(a.dB) + (int64_t)b * a.sdB.b + (int64_t)h * a.sdB.h;
   TB* dCb = reinterpret_cast<TB*>(a.dC) + (int64_t)b * a.sdC.b + (int64_t)h * a.sdC.h;
-  for (int it0 = warp * rpw; it0 < n * R; it0 += (kFT / 32) * rpw) {
-    const int it = it0 + lane / lpr;
-    float sx = 0.f, sy = 0.f;
-    if (it < n * R) {
-      const int t = fdiv(it, f.fR), r = it - t * R;
-      const float be = coef[t].y, gan = coef[t + 1].z, dv = dyr[it], xv = xr[(t + 1) * R + r];
-      const TB* brow = Bs + ((size_t)(t + 1) * R + r) * D;
-      const TB* crow = Cs + (size_t)it * D;
-      for (int blk = part; blk < D4; blk += lpr) {
-        const int d = 4 * blk;
-        const float4 h4 = *reinterpret_cast<const float4*>(hs + t * D + d);
-        const float4 g4 = *reinterpret_cast<const float4*>(gs + t * D + d);
-        const float4 g4n = *reinterpret_cast<const float4*>(gs + (t + 1) * D + d);
-        const float4 v4 = make_float4(fmaf(be, g4.x, gan * g4n.x), fmaf(be, g4.y, gan * g4n.y),
-                                      fmaf(be, g4.z, gan * g4n.z), fmaf(be, g4.w, gan * g4n.w));
-        const float4 b4 = ld4f(brow + d), c4 = ld4f(crow + d);
-        sx = fmaf(b4.x, v4.x, fmaf(b4.y, v4.y, fmaf(b4.z, v4.z, fmaf(b4.w, v4.w, sx))));
-        sy = fmaf(c4.x, h4.x, fmaf(c4.y, h4.y, fmaf(c4.z, h4.z, fmaf(c4.w, h4.w, sy))));
-        const int64_t tt = t0 + t;
-        st4v(dCb + tt * a.sdC.l + (int64_t)r * a.sdC.r + d,
-             make_float4(dv * h4.x, dv * h4.y, dv * h4.z, dv * h4.w), f.bvec);
-        st4v(dBb + tt * a.sdB.l + (int64_t)r * a.sdB.r + d,
-             make_float4(xv * v4.x, xv * v4.y, xv * v4.z, xv * v4.w), f.bvec);
-      }
-    }
-    for (int o = lpr >> 1; o > 0; o >>= 1) {
-      sx += __shfl_xor_sync(0xffffffffu, sx, o);
-      sy += __shfl_xor_sync(0xffffffffu, sy, o);
-    }
-    if (it < n * R && part == 0) {
-      const int t = fdiv(it, f.fR), r = it - t * R;
-      dxr[it] = fmaf(Dk, dyr[it], sx);
-      yr[it] = fmaf(Dk, xr[(t + 1) * R + r], sy);
-    }
-  }
-  // per t: dbeta = g_t . bx_t, dgamma = g_t . bx_{t-1}
-  for (int t0w = warp * rpw; t0w < n; t0w += (kFT / 32) * rpw) {
-    const int t = t0w + lane / lpr;
+  for (int tw = warp * rpw; tw < n; tw += (kFT / 32) * rpw) {
+    const int t = tw + lane / lpr;
+    const bool tv = t < n;
+    const int tc = tv ? t : 0;
+    const float be = coef[tc].y, gan = coef[tc + 1].z;
+    TB* dBt = dBb + (int64_t)(t0 + tc) * a.sdB.l;
+    TB* dCt = dCb + (int64_t)(t0 + tc) * a.sdC.l;
     float sb = 0.f, sg = 0.f;
-    if (t < n)
-      for (int blk = part; blk < D4; blk += lpr) {
-        const int d = 4 * blk;
-        const float4 g4 = *reinterpret_cast<const float4*>(gs + t * D + d);
-        const float4 b1 = *reinterpret_cast<const float4*>(bxs + (t + 1) * D + d);
-        const float4 b0 = *reinterpret_cast<const float4*>(bxs + t * D + d);
-        sb = fmaf(g4.x, b1.x, fmaf(g4.y, b1.y, fmaf(g4.z, b1.z, fmaf(g4.w, b1.w, sb))));
-        sg = fmaf(g4.x, b0.x, fmaf(g4.y, b0.y, fmaf(g4.z, b0.z, fmaf(g4.w, b0.w, sg))));
-      }
+    for (int r0 = 0; r0 < R; r0 += 4) {
+      float sx[4] = {0.f, 0.f, 0.f, 0.f}, sy[4] = {0.f, 0.f, 0.f, 0.f};
+      if (tv)
+        for (int blk = part; blk < D4; blk += lpr) {
+          const int d = 4 * blk;
+          const float4 h4 = *reinterpret_cast<const float4*>(hs + tc * D + d);
+          const float4 g4 = *reinterpret_cast<const float4*>(gs + tc * D + d);
+          const float4 g4n = *reinterpret_cast<const float4*>(gs + (tc + 1) * D + d);
+          const float4 v4 = make_float4(fmaf(be, g4.x, gan * g4n.x), fmaf(be, g4.y, gan * g4n.y),
+                                        fmaf(be, g4.z, gan * g4n.z), fmaf(be, g4.w, gan * g4n.w));
+          if (r0 == 0) {
+            const float4 b1 = *reinterpret_cast<const float4*>(bxs + (tc + 1) * D + d);
+            const float4 b0 = *reinterpret_cast<const float4*>(bxs + tc * D + d);
+            sb = fmaf(g4.x, b1.x, fmaf(g4.y, b1.y, fmaf(g4.z, b1.z, fmaf(g4.w, b1.w, sb))));
+            sg = fmaf(g4.x, b0.x, fmaf(g4.y, b0.y, fmaf(g4.z, b0.z, fmaf(g4.w, b0.w, sg))));
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int r = r0 + q;
+            if (r < R) {
+              const float4 b4 = ld4f(Bs + ((size_t)(tc + 1) * R + r) * D + d);
+              const float4 c4 = ld4f(Cs + ((size_t)tc * R + r) * D + d);
+              sx[q] = fmaf(b4.x, v4.x, fmaf(b4.y, v4.y, fmaf(b4.z, v4.z, fmaf(b4.w, v4.w, sx[q]))));
+              sy[q] = fmaf(c4.x, h4.x, fmaf(c4.y, h4.y, fmaf(c4.z, h4.z, fmaf(c4.w, h4.w, sy[q]))));
+              const float dv = dyr[tc * R + r], xv = xr[(tc + 1) * R + r];
+              st4v(dCt + (int64_t)r * a.sdC.r + d, make_float4(dv * h4.x, dv * h4.y, dv * h4.z, dv * h4.w), f.bvec);
+              st4v(dBt + (int64_t)r * a.sdB.r + d, make_float4(xv * v4.x, xv * v4.y, xv * v4.z, xv * v4.w), f.bvec);
+            }
+          }
+        }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        for (int o = lpr >> 1; o > 0; o >>= 1) {
+          sx[q] += __shfl_xor_sync(0xffffffffu, sx[q], o);
+          sy[q] += __shfl_xor_sync(0xffffffffu, sy[q], o);
+        }
+      if (tv && part == 0)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int r = r0 + q;
+          if (r < R) {
+            dxr[tc * R + r] = fmaf(Dk, dyr[tc * R + r], sx[q]);
+            yr[tc * R + r] = fmaf(Dk, xr[(tc + 1) * R + r], sy[q]);
+          }
+        }
+    }
     for (int o = lpr >> 1; o > 0; o >>= 1) {
       sb += __shfl_xor_sync(0xffffffffu, sb, o);
       sg += __shfl_xor_sync(0xffffffffu, sg, o);
     }
-    if (t < n && part == 0) dbg[t] = make_float2(sb, sg);
+    if (tv && part == 0) dbg[tc] = make_float2(sb, sg);
   }
   __syncthreads();
   // per t: q = sum_r dyr (yr - D xr) = E_t . h_t, the dADT term, dDT and dtrap
