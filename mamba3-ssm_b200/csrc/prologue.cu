@@ -18,16 +18,17 @@
 namespace m3 {
 namespace {
 
-// one CTA per (b, h); the sequence in tiles of 128 steps, thread = step; the angle
+// one CTA per (b, h); the sequence in tiles of kAT steps, thread = step; the angle
 // cumsums are block-wide inclusive scans (warp shuffles, then the warp totals) carried
-// from tile to tile
-constexpr int kAT = 128;
+// from tile to tile. kAT = 512 when there are few (b, h) units (a shorter serial walk per
+// CTA), 128 otherwise.
+constexpr int kATmax = 512;
 
 // CTA per (b, h), thread = time step of a kAT-step tile. Each thread carries its step's
 // angles 16 at a time in registers: a warp scan over the tile, the warp totals through
 // shared memory (two barriers per 16 angles), then one (b, l, h) row of angles written as
 // 16-byte vectors (the S angles of a row are contiguous).
-template <typename TZ>
+template <typename TZ, int kAT>
 __global__ void __launch_bounds__(kAT) prologue_angle_kernel(PrologueParams a) {
   constexpr int kS = 16;
   __shared__ float wsum[kAT / 32][kS];
@@ -240,9 +241,13 @@ int launch_prologue(const PrologueParams& p, int zdt, int odt, cudaStream_t s) {
   if ((int64_t)p.Bn * p.L > 2147483647LL) return fail(M3_ERR_UNSUPPORTED, "prologue: batch * seqlen too large");
   const dim3 gb((unsigned)((int64_t)p.Bn * p.L), (unsigned)((p.R + 7) / 8));
   const int ppl = (p.D / 2 + 31) / 32;
+  int sms = 148;
+  if (device_sm_count(&sms) != M3_OK) sms = 148;
+  const bool wide = (int64_t)ga < 4 * (int64_t)sms && p.L > 128;
 #define M3_PRO(TZ, TO)                                                                  \
   do {                                                                                  \
-    prologue_angle_kernel<TZ><<<ga, kAT, 0, s>>>(p);                                    \
+    if (wide) prologue_angle_kernel<TZ, kATmax><<<ga, kATmax, 0, s>>>(p);               \
+    else prologue_angle_kernel<TZ, 128><<<ga, 128, 0, s>>>(p);                          \
     M3_TRY(check_launch("prologue_angle_kernel"));                                      \
     const int th = 32 * (p.R < 8 ? p.R : 8);                                            \
     if (ppl == 1) prologue_bc_kernel<TZ, TO, 1><<<gb, th, 0, s>>>(p);                   \

@@ -32,7 +32,7 @@ namespace m3 {
 namespace {
 
 constexpr int kRowsBC = 16;  // (b, l) rows per CTA of the bc kernel
-constexpr int kAT = 128;     // steps per tile of the angle kernel
+constexpr int kATmax = 512;  // steps per tile of the angle kernel when (b, h) units are few (else 128)
 
 template <typename T>
 __device__ __forceinline__ float2 ld_pair(const T* p) {
@@ -451,7 +451,7 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
 
 // CTA per (b, h); thread = step of a 128-step tile walked from the end; suffix sums over l
 // of dtheta[b,l,h,i] for the S angles, 16 at a time, carried between tiles
-template <typename TZ>
+template <typename TZ, int kAT>
 __global__ void __launch_bounds__(kAT) prologue_bwd_angle_kernel(PrologueBwdParams a) {
   constexpr int kS = 16;
   __shared__ float wsum[kAT / 32][kS];
@@ -729,6 +729,9 @@ int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt
                      reinterpret_cast<uintptr_t>(p.dCp) | reinterpret_cast<uintptr_t>(p.angles)) & 15) == 0;
   const int ppl = (p.D / 2 + 31) / 32;
   const unsigned gdt = (unsigned)((rows * p.H + 255) / 256);
+  int nsm = 148;
+  if (device_sm_count(&nsm) != M3_OK) nsm = 148;
+  const bool wide = (int64_t)p.Bn * p.H < 4 * (int64_t)nsm && p.L > 128;
 #define M3_PBWD(TZ, TO)                                                                                  \
   do {                                                                                                   \
     unsigned used = gbc;                                                                                 \
@@ -750,7 +753,8 @@ int launch_prologue_bwd(const PrologueBwdParams& p0, float* ws, int zdt, int odt
     bc_reduce_kernel<<<dim3((unsigned)((W + 255) / 256), (unsigned)((used + kSlotsPerThread - 1) / kSlotsPerThread)), \
                        256, 0, s>>>(p, (int)used);                                                        \
     M3_TRY(check_launch("bc_reduce_kernel"));                                                            \
-    prologue_bwd_angle_kernel<TZ><<<(unsigned)(p.Bn * p.H), kAT, 0, s>>>(p);                             \
+    if (wide) prologue_bwd_angle_kernel<TZ, kATmax><<<(unsigned)(p.Bn * p.H), kATmax, 0, s>>>(p);         \
+    else prologue_bwd_angle_kernel<TZ, 128><<<(unsigned)(p.Bn * p.H), 128, 0, s>>>(p);                   \
     M3_TRY(check_launch("prologue_bwd_angle_kernel"));                                                   \
     prologue_bwd_dt_kernel<TZ><<<gdt, 256, 0, s>>>(p);                                                   \
     return check_launch("prologue_bwd_dt_kernel");                                                       \
