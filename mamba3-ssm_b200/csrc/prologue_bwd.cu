@@ -271,7 +271,7 @@ constexpr int kBC1 = 256;
 __device__ int g_prologue_error;  // set when a bounded wait gives up
 
 struct Bc1Smem {
-  uint32_t bias, gb[2], gc[2], zr[2], an[2], rs, sdn, swb, total;
+  uint32_t bias, gb[2], gc[2], zr[2], an[2], rs, sdn, swb, sdv, total;
 };
 __host__ __device__ inline uint32_t bc1_up(uint32_t v) { return (v + 127u) & ~127u; }
 __host__ __device__ inline Bc1Smem bc1_smem(int H, int R, int D, int S, int ez, int eo) {
@@ -287,12 +287,15 @@ __host__ __device__ inline Bc1Smem bc1_smem(int H, int R, int D, int S, int ez, 
   L.rs = o; o = bc1_up(o + (uint32_t)(2 * R * 4));
   L.sdn = o; o = bc1_up(o + (uint32_t)(2 * R * D * 4));
   L.swb = o; o = bc1_up(o + (uint32_t)(2 * R * D * 4));
+  // per thread group (the threads whose slots share a pair, when the pairs of a row divide
+  // the CTA): its sums over heads of dv, (group, B / C, R, D)
+  L.sdv = o; o = bc1_up(o + (uint32_t)((kBC1 % (D / 2) == 0 ? kBC1 / (D / 2) : 0) * 2 * R * D * 4));
   L.total = o + 128;  // slack for aligning the base
   return L;
 }
 
 template <typename TZ, typename TO, int RT>
-__global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParams a, Bc1Smem L) {
+__global__ void __launch_bounds__(kBC1, 3) prologue_bwd_bc1_kernel(PrologueBwdParams a, Bc1Smem L) {
   extern __shared__ __align__(128) unsigned char bsm_raw[];
   unsigned char* bsm = bsm_raw + ((128u - (sm100::smem_u32(bsm_raw) & 127u)) & 127u);
   constexpr int R = RT;
@@ -304,6 +307,11 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
   float* rs = reinterpret_cast<float*>(bsm + L.rs);         // (2, R): 1 / rms
   float* sdn = reinterpret_cast<float*>(bsm + L.sdn);       // (2, R, D): dn = sum over heads of dv
   float* swb = reinterpret_cast<float*>(bsm + L.swb);       // (2, R, D): norm-weight gradient partials
+  float* sdv = reinterpret_cast<float*>(bsm + L.sdv);       // (groups, 2, R, D): dn partials per group
+  // when the row's pairs divide the CTA, thread t's slots t, t + kBC1, ... share the pair
+  // t mod half, and the groups of half threads add their dn partials through sdv (no atomics)
+  const bool grouped = kBC1 % half == 0;
+  const int ngrp = grouped ? kBC1 / half : 0, grp = grouped ? tid / half : 0;
   const int64_t RD = (int64_t)R * D;
   const uint32_t gbytes = (uint32_t)(R * H * D * sizeof(TO)), zbytes = (uint32_t)(2 * RD * sizeof(TZ)),
                  abytes = (uint32_t)(H * S * 4);
@@ -344,7 +352,8 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
     const float* an = reinterpret_cast<const float*>(bsm + (k ? L.an[1] : L.an[0]));
     const int64_t b = row / a.L, l = row - b * a.L;
     TZ* drow = reinterpret_cast<TZ*>(a.dzx) + b * a.s_dzb + l * a.s_dzl + 2 * a.d_inner;
-    for (int i = tid; i < 2 * R * D; i += kBC1) sdn[i] = 0.f;
+    if (!grouped)
+      for (int i = tid; i < 2 * R * D; i += kBC1) sdn[i] = 0.f;
     for (int it = warp; it < 2 * R; it += kBC1 / 32) {
       float ss = 0.f;
       for (int d = lane; d < D; d += 32) {
@@ -360,10 +369,10 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
     int kcur = -1;
 #pragma unroll
     for (int r = 0; r < R; ++r) dnb0[r] = dnb1[r] = dnc0[r] = dnc1[r] = 0.f;
-    for (int sl = tid; sl < np; sl += kBC1) {
-      const int h = sl / half, kp = sl - h * half, d0 = 2 * kp;
+    for (int sl = tid, hg = grp; sl < np; sl += kBC1, hg += ngrp) {
+      const int h = grouped ? hg : sl / half, kp = sl - h * half, d0 = 2 * kp;
       if (kp != kcur) {  // flush the running sums over heads of the previous pair
-        if (kcur >= 0) {
+        if (kcur >= 0) {  // (only without groups: a grouped thread's slots share one pair)
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             atomicAdd(&sdn[r * D + 2 * kcur], dnb0[r]); atomicAdd(&sdn[r * D + 2 * kcur + 1], dnb1[r]);
@@ -383,18 +392,17 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
       for (int r = 0; r < R; ++r) {
         float2 g1 = ld_pair(gbs + ((int64_t)r * H + h) * D + d0), g2 = ld_pair(gcs + ((int64_t)r * H + h) * D + d0);
         if (rot) {
-          // o = rot(v), v = n + bias; dtheta = -g1 o2 + g2 o1; dv = rot^T(g)
+          // o = rot(v), v = n + bias; dv = rot^T(g); dtheta = -g1 o2 + g2 o1 = dv2 v1 - dv1 v2
+          // (the rotation commutes with the quarter turn)
+          g1 = make_float2(g1.x * cs + g1.y * sn, -g1.x * sn + g1.y * cs);
+          g2 = make_float2(g2.x * cs + g2.y * sn, -g2.x * sn + g2.y * cs);
           const float2 bv = __ldg(reinterpret_cast<const float2*>(a.B_bias + ((int64_t)h * R + r) * D + d0));
           const float2 cv = __ldg(reinterpret_cast<const float2*>(a.C_bias + ((int64_t)h * R + r) * D + d0));
           const float rb = rs[r], rc = rs[R + r];
           const float2 zb = ld_pair(zr + r * D + d0), zc = ld_pair(zr + RD + r * D + d0);
           const float x0 = fmaf(zb.x * rb, wb.x, bv.x), x1 = fmaf(zb.y * rb, wb.y, bv.y);
           const float y0 = fmaf(zc.x * rc, wc.x, cv.x), y1 = fmaf(zc.y * rc, wc.y, cv.y);
-          const float ob0 = x0 * cs - x1 * sn, ob1 = x0 * sn + x1 * cs;
-          const float oc0 = y0 * cs - y1 * sn, oc1 = y0 * sn + y1 * cs;
-          dth += (-g1.x * ob1 + g1.y * ob0) + (-g2.x * oc1 + g2.y * oc0);
-          g1 = make_float2(g1.x * cs + g1.y * sn, -g1.x * sn + g1.y * cs);
-          g2 = make_float2(g2.x * cs + g2.y * sn, -g2.x * sn + g2.y * cs);
+          dth += fmaf(g1.y, x0, -g1.x * x1) + fmaf(g2.y, y0, -g2.x * y1);
         }
         float4 acc = sbias[r * np + sl];
         acc.x += g1.x; acc.y += g1.y; acc.z += g2.x; acc.w += g2.y;
@@ -403,7 +411,15 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
       }
       if (rot) a.dtheta[(row * H + h) * S + kp] = dth;
     }
-    if (kcur >= 0) {
+    if (grouped) {
+      // the group's sums over its heads; every thread of the CTA owns one (group, pair)
+      const int kq = tid - grp * half;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        *reinterpret_cast<float2*>(&sdv[((size_t)grp * 2 * R + r) * D + 2 * kq]) = make_float2(dnb0[r], dnb1[r]);
+        *reinterpret_cast<float2*>(&sdv[((size_t)grp * 2 * R + R + r) * D + 2 * kq]) = make_float2(dnc0[r], dnc1[r]);
+      }
+    } else if (kcur >= 0) {
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         atomicAdd(&sdn[r * D + 2 * kcur], dnb0[r]); atomicAdd(&sdn[r * D + 2 * kcur + 1], dnb1[r]);
@@ -411,6 +427,14 @@ __global__ void __launch_bounds__(kBC1) prologue_bwd_bc1_kernel(PrologueBwdParam
       }
     }
     __syncthreads();
+    if (grouped) {
+      for (int i = tid; i < 2 * R * D; i += kBC1) {
+        float v = 0.f;
+        for (int g2 = 0; g2 < ngrp; ++g2) v += sdv[(size_t)g2 * 2 * R * D + i];
+        sdn[i] = v;
+      }
+      __syncthreads();
+    }
     // RMSNorm backward of (B or C, rank): draw = (w dn) / rms - raw sum(w dn raw) / (D rms^3)
     for (int it = warp; it < 2 * R; it += kBC1 / 32) {
       const float* w = it < R ? a.B_norm_w : a.C_norm_w;
