@@ -69,7 +69,7 @@ int ensure_dynamic_smem(const void* kernel, size_t bytes, std::atomic<bool>* don
 // the per-position workspace of up to M3_NOALLOC_MAX_POSITIONS (batch * heads * seqlen)
 // positions, 4 bytes each (8 MiB). Lives in every GPU that loads the library, for the
 // lifetime of the process, and is shared by all calls on that GPU.
-__device__ __align__(256) float g_noalloc_scratch[M3_NOALLOC_MAX_POSITIONS];
+static __device__ __align__(256) float g_noalloc_scratch[M3_NOALLOC_MAX_POSITIONS];
 
 namespace {
 
