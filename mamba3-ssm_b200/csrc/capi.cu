@@ -65,6 +65,39 @@ int ensure_dynamic_smem(const void* kernel, size_t bytes, std::atomic<bool>* don
   return M3_OK;
 }
 
+int kernel_residency(const void* kernel, int threads, size_t smem, LaunchCache* c, int* resident) {
+  int dev = 0;
+  M3_TRY(current_device(&dev));
+  const long long want = (long long)smem;
+  const long long w = c->word[dev].load(std::memory_order_acquire);
+  if (w > 0 && (w >> 32) == want) {
+    *resident = (int)(w & 0xffffffffLL);
+    return M3_OK;
+  }
+  // the opt-in only ever grows, so a launch of a larger size on another host thread never
+  // finds it lowered under it
+  long long cur = c->smem_max[dev].load(std::memory_order_acquire);
+  while (want > cur) {
+    if (c->smem_max[dev].compare_exchange_weak(cur, want)) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
+      if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      break;
+    }
+  }
+  // all of the unified L1 / shared array as shared memory: the CTAs that fit are then set by
+  // registers and shared memory, not by the carveout (a hint; its failure is not an error)
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    cudaGetLastError();
+  int per_sm = 0, sms = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
+  M3_TRY(device_sm_count(&sms));
+  const int n = std::max(1, per_sm * sms);
+  c->word[dev].store((want << 32) | (long long)n, std::memory_order_release);
+  *resident = n;
+  return M3_OK;
+}
+
 // Fixed scratch of the allocation-free SISO backward (m3_siso_scan_bwd_noalloc): room for
 // the per-position workspace of up to M3_NOALLOC_MAX_POSITIONS (batch * heads * seqlen)
 // positions, 4 bytes each (8 MiB). Lives in every GPU that loads the library, for the
@@ -138,12 +171,6 @@ int check(const m3_tensor* t, const char* name, int ndim, const int64_t* shape, 
 Str3 s3(const m3_tensor* t) { return Str3{t->stride[0], t->stride[1], t->stride[2]}; }
 Str3 s3_scal(const m3_tensor* t) { return Str3{t->stride[0], t->stride[1], t->stride[2]}; }
 Str4 s4(const m3_tensor* t) { return Str4{t->stride[0], t->stride[1], t->stride[2], t->stride[3]}; }
-
-int64_t numel(const m3_tensor* t) {
-  int64_t n = 1;
-  for (int i = 0; i < t->ndim; ++i) n *= t->shape[i];
-  return n;
-}
 
 template <typename T>
 T* fptr(const m3_tensor* t) { return present(t) ? reinterpret_cast<T*>(t->data) : nullptr; }

@@ -70,6 +70,15 @@ int device_sm_count(int* sms);
 // Sets a kernel's dynamic shared-memory opt-in once per device (done[] has kMaxDevices
 // entries, one per device context); safe from several host threads.
 int ensure_dynamic_smem(const void* kernel, size_t bytes, std::atomic<bool>* done);
+// Per kernel (one static LaunchCache each) and device: the dynamic shared-memory opt-in
+// (raised to the largest size asked so far), the preferred carveout, and the number of CTAs
+// of `threads` threads that fit on the whole device at `smem` bytes, recomputed only when
+// the size changes. Safe from several host threads.
+struct LaunchCache {
+  std::atomic<long long> word[kMaxDevices];      // (smem << 32) | resident CTAs, 0 = not yet
+  std::atomic<long long> smem_max[kMaxDevices];  // the opt-in set so far
+};
+int kernel_residency(const void* kernel, int threads, size_t smem, LaunchCache* c, int* resident);
 
 inline size_t dtype_size(int dt) { return dt == M3_FLOAT32 ? 4 : 2; }
 

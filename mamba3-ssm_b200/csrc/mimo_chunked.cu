@@ -1404,15 +1404,9 @@ int run_fused(const MimoParams& p, void* ws, cudaStream_t s) {
   f.arec = f.rec + cells * p.D;
   f.L = fused_smem(Q, p.P, p.R, p.D, (int)sizeof(TB), (int)sizeof(TX));
   const size_t smem = f.L.total;
-  M3_TRY(opt_in(mimo_fused_fwd_kernel<TX, TB, Q>, smem));
-  // all of the unified L1 / shared array as shared memory, so that the CTAs that the
-  // registers allow are not limited by the carveout
-  cudaFuncSetAttribute(mimo_fused_fwd_kernel<TX, TB, Q>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-  int per_sm = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mimo_fused_fwd_kernel<TX, TB, Q>, kFT, smem) != cudaSuccess)
-    per_sm = 1;
-  if (device_sm_count(&sms) != M3_OK) sms = 148;
-  f.ahead = std::max(1, per_sm * sms);
+  static LaunchCache lc;
+  M3_TRY(kernel_residency(reinterpret_cast<const void*>(mimo_fused_fwd_kernel<TX, TB, Q>), kFT, smem, &lc,
+                          &f.ahead));
   cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)fused_ws_bytes(cells, p.D), s);
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   mimo_fused_fwd_kernel<TX, TB, Q><<<(unsigned)cells, kFT, smem, s>>>(mB, mC, mX, p, f);
@@ -1455,14 +1449,9 @@ int run_fused_bwd(const MimoParams& p, const void* fwd_ws, size_t fwd_bytes, voi
   f.rec = reinterpret_cast<unsigned long long*>(w + 16);
   f.arec = f.rec + cells * p.D;
   f.tot = reinterpret_cast<double*>(w + ((fused_ws_bytes(cells, p.D) + 15) & ~int64_t(15)));
-  M3_TRY(opt_in(mimo_fused_bwd_kernel<TX, TB, Q>, L.total));
-  cudaFuncSetAttribute(mimo_fused_bwd_kernel<TX, TB, Q>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-  int per_sm = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mimo_fused_bwd_kernel<TX, TB, Q>, kFT, L.total) !=
-      cudaSuccess)
-    per_sm = 1;
-  if (device_sm_count(&sms) != M3_OK) sms = 148;
-  f.ahead = std::max(1, per_sm * sms);
+  static LaunchCache lc;
+  M3_TRY(kernel_residency(reinterpret_cast<const void*>(mimo_fused_bwd_kernel<TX, TB, Q>), kFT, L.total, &lc,
+                          &f.ahead));
   cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)fused_ws_bytes(cells, p.D), s);
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   mimo_fused_bwd_kernel<TX, TB, Q><<<(unsigned)cells, kFT, L.total, s>>>(mB, mC, mX, mDY, p, f);

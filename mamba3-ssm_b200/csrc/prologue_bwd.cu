@@ -702,14 +702,22 @@ template <typename K>
 int bc1_launch(K k, const PrologueBwdParams& p, const Bc1Smem& L, unsigned slots, unsigned* used,
                cudaStream_t s) {
   const size_t smem = L.total;
-  if (smem > 48 * 1024) {
-    cudaError_t ea = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (ea != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ea));
+  static LaunchCache lc[16];  // per instantiation of this launcher: one per kernel pointer below
+  static std::atomic<const void*> keys[16];
+  const void* kp = reinterpret_cast<const void*>(k);
+  int slot = -1;
+  for (int i = 0; i < 16 && slot < 0; ++i) {
+    const void* cur = keys[i].load(std::memory_order_acquire);
+    if (cur == kp) slot = i;
+    else if (cur == nullptr) {
+      const void* expect = nullptr;
+      if (keys[i].compare_exchange_strong(expect, kp) || expect == kp) slot = i;
+    }
   }
-  int per_sm = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kBC1, smem) != cudaSuccess || per_sm < 1) per_sm = 1;
-  if (device_sm_count(&sms) != M3_OK) sms = 148;
-  *used = std::min<unsigned>(slots, (unsigned)(per_sm * sms));
+  if (slot < 0) return fail(M3_ERR_UNSUPPORTED, "prologue backward: launch cache full");
+  int resident = 1;
+  M3_TRY(kernel_residency(kp, kBC1, smem, &lc[slot], &resident));
+  *used = std::min<unsigned>(slots, (unsigned)resident);
   k<<<*used, kBC1, smem, s>>>(p, L);
   return check_launch("prologue_bwd_bc1_kernel");
 }
