@@ -306,12 +306,45 @@ int m3_argmax_rows(const m3_tensor* logits, m3_tensor* out, void* stream);
  *   angle0 (batch, nheads, S) f32, optional: the angle state of a decode cache to continue
  *   from (the cumulative angles then start there, as they would after that many step()s);
  *   absent = zeros, as in the reference's forward.
+ *   B_proj and C_proj may both be NULL: only ADT, DT, trap and angles are written (the
+ *   inputs of m3_mimo_layer_scan_fwd, which forms B / C itself).
  * ------------------------------------------------------------------------------- */
 int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* dt_bias,
                       const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
                       const m3_tensor* C_norm_w, const m3_tensor* angle0, m3_tensor* B_proj,
                       m3_tensor* C_proj, m3_tensor* ADT, m3_tensor* DT, m3_tensor* trap,
                       m3_tensor* angles, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * MIMO scan of one Mamba3 layer straight from its in_proj output, for inference with one
+ * B / C group (ngroups 1): the per-head B / C of layer.py:214-244 (RMSNorm of the group
+ * rows * weight + per-head bias, pairs rotated by the angles) are formed inside the scan
+ * and never written, then the scan of ssm_scan_mimo (ops.py:184-242) and, with gate = 1,
+ * the gate y * silu(z) of layer.py:262-266. Equals m3_layer_prologue's B_proj / C_proj
+ * followed by m3_mimo_scan_fwd_ws and m3_silu_gate, up to rounding (B / C stay fp32 here).
+ *   zxbcdt (batch, seqlen, d_in_proj) f32 / bf16 / f16, innermost stride 1: z, x and the
+ *   group rows are read from it; its start, row strides, 2 * d_inner, headdim and d_state
+ *   in whole 16-byte units;
+ *   ADT, DT, trap (batch, seqlen, nheads) f32 and angles (batch, seqlen, nheads, S) f32
+ *   contiguous: m3_layer_prologue's outputs (B_proj / C_proj may be NULL there);
+ *   B_bias, C_bias (nheads, rank, d_state), B_norm_w, C_norm_w (d_state) f32 contiguous,
+ *   16-byte aligned; D (nheads), mimo_x, mimo_o (nheads, rank, headdim) f32;
+ *   h0, bx0 (batch, nheads, d_state) f32 optional: states to continue from;
+ *   out (batch, seqlen, nheads, headdim), zxbcdt's dtype: y, or y * silu(z) with gate = 1;
+ *   h_last, bx_last optional, as in m3_mimo_scan_fwd;
+ *   workspace: m3_mimo_scan_fwd_workspace_size(...) bytes, 16-byte aligned.
+ * M3_ERR_UNSUPPORTED (nothing launched) when ngroups > 1 or the layout does not allow
+ * the kernel's TMA boxes; the caller then runs m3_layer_prologue with B_proj / C_proj and
+ * m3_mimo_scan_fwd_ws. Replaces the PyTorch prologue of layer.py:214-244, whose per-head
+ * B / C are (batch, seqlen, rank, nheads, d_state) fp32 tensors, and the scan call.
+ * ------------------------------------------------------------------------------- */
+int m3_mimo_layer_scan_fwd(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* ADT,
+                           const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* angles,
+                           const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                           const m3_tensor* C_norm_w, const m3_tensor* D, const m3_tensor* mimo_x,
+                           const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, int32_t gate,
+                           m3_tensor* out, m3_tensor* h_last, m3_tensor* bx_last, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* out = y * silu(z), (B, L, H, P) views with innermost stride 1; the gate of
  * Mamba3.forward between the scan and out_proj (layer.py:262-266). */

@@ -876,8 +876,12 @@ int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const 
   const int64_t zs[3] = {Bn, L, dproj}, bs[5] = {Bn, L, R, H, Ds}, ss[3] = {Bn, L, H}, as[4] = {Bn, L, H, S},
                 h1[1] = {H}, hrd[3] = {H, R, Ds}, d1[1] = {Ds};
   M3_TRY(check(zxbcdt, "zxbcdt", 3, zs, kAnyFloat, false, false, !empty));
-  M3_TRY(check(B_proj, "B_proj", 5, bs, kAnyFloat, true, false, !empty));
-  M3_TRY(check(C_proj, "C_proj", 5, bs, 1u << B_proj->dtype, true, false, !empty));
+  // B_proj and C_proj: both present, or both absent (angles and step scalars only)
+  const bool with_bc = present(B_proj) || present(C_proj);
+  if (with_bc) {
+    M3_TRY(check(B_proj, "B_proj", 5, bs, kAnyFloat, true, false, !empty));
+    M3_TRY(check(C_proj, "C_proj", 5, bs, 1u << B_proj->dtype, true, false, !empty));
+  }
   M3_TRY(check(ADT, "ADT", 3, ss, kF32, true, false, false));
   M3_TRY(check(DT, "DT", 3, ss, kF32, true, false, false));
   M3_TRY(check(trap, "trap", 3, ss, kF32, true, false, false));
@@ -898,10 +902,87 @@ int m3_layer_prologue(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const 
   p.dt_bias = fptr<const float>(dt_bias);
   p.B_bias = fptr<const float>(B_bias); p.C_bias = fptr<const float>(C_bias);
   p.B_norm_w = fptr<const float>(B_norm_w); p.C_norm_w = fptr<const float>(C_norm_w);
-  p.Bp = B_proj->data; p.Cp = C_proj->data;
+  p.Bp = with_bc ? B_proj->data : nullptr;
+  p.Cp = with_bc ? C_proj->data : nullptr;
   p.ADT = fptr<float>(ADT); p.DT = fptr<float>(DT); p.trap = fptr<float>(trap); p.angles = fptr<float>(angles);
   p.angle0 = S > 0 ? fptr<const float>(angle0) : nullptr;
-  return launch_prologue(p, zxbcdt->dtype, B_proj->dtype, reinterpret_cast<cudaStream_t>(stream));
+  return launch_prologue(p, zxbcdt->dtype, with_bc ? B_proj->dtype : zxbcdt->dtype,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+int m3_mimo_layer_scan_fwd(const m3_layer_dims* dims, const m3_tensor* zxbcdt, const m3_tensor* ADT,
+                           const m3_tensor* DT, const m3_tensor* trap, const m3_tensor* angles,
+                           const m3_tensor* B_bias, const m3_tensor* C_bias, const m3_tensor* B_norm_w,
+                           const m3_tensor* C_norm_w, const m3_tensor* D, const m3_tensor* mimo_x,
+                           const m3_tensor* mimo_o, const m3_tensor* h0, const m3_tensor* bx0, int32_t gate,
+                           m3_tensor* out, m3_tensor* h_last, m3_tensor* bx_last, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!dims) return fail(M3_ERR_INVALID_ARGUMENT, "dims: missing");
+  const int64_t H = dims->nheads, P = dims->headdim, Ds = dims->d_state, G = dims->ngroups,
+                R = dims->mimo_rank, S = dims->num_rope_angles, di = dims->d_inner;
+  if (H <= 0 || P <= 0 || Ds <= 0 || G <= 0 || R <= 0 || S < 0 || di != H * P || dims->rope_split != 2 * S ||
+      dims->rope_split > Ds || (G != 1 && G != H))
+    return fail(M3_ERR_INVALID_ARGUMENT, "dims: inconsistent layer dimensions");
+  if (gate != 0 && gate != 1) return fail(M3_ERR_INVALID_ARGUMENT, "gate: must be 0 or 1");
+  if (!present(zxbcdt) || zxbcdt->ndim != 3) return fail(M3_ERR_INVALID_ARGUMENT, "zxbcdt: expected (batch, seqlen, d_in_proj)");
+  const int64_t Bn = zxbcdt->shape[0], L = zxbcdt->shape[1];
+  const int64_t dproj = 2 * di + 2 * Ds * G * R + 3 * H + S;
+  const bool empty = Bn * L == 0;
+  const int64_t zs[3] = {Bn, L, dproj}, ss[3] = {Bn, L, H}, as[4] = {Bn, L, H, S}, h1[1] = {H},
+                hrd[3] = {H, R, Ds}, d1[1] = {Ds}, ms[3] = {H, R, P}, st[3] = {Bn, H, Ds}, ys[4] = {Bn, L, H, P};
+  M3_TRY(check(zxbcdt, "zxbcdt", 3, zs, kAnyFloat, false, false, !empty));
+  M3_TRY(check(ADT, "ADT", 3, ss, kF32, false, false, false));
+  M3_TRY(check(DT, "DT", 3, ss, kF32, false, false, false));
+  M3_TRY(check(trap, "trap", 3, ss, kF32, false, false, false));
+  M3_TRY(check(angles, "angles", 4, as, kF32, true, S == 0, false));
+  M3_TRY(check(B_bias, "B_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(C_bias, "C_bias", 3, hrd, kF32, true, false, false));
+  M3_TRY(check(B_norm_w, "B_norm_w", 1, d1, kF32, true, false, false));
+  M3_TRY(check(C_norm_w, "C_norm_w", 1, d1, kF32, true, false, false));
+  M3_TRY(check(D, "D", 1, h1, kF32, false, false, false));
+  M3_TRY(check(mimo_x, "mimo_x", 3, ms, kF32, false, false, false));
+  M3_TRY(check(mimo_o, "mimo_o", 3, ms, kF32, false, false, false));
+  M3_TRY(check(h0, "h0", 3, st, kF32, true, true, false));
+  M3_TRY(check(bx0, "bx0", 3, st, kF32, true, true, false));
+  M3_TRY(check(out, "out", 4, ys, 1u << zxbcdt->dtype, false, false, !empty));
+  M3_TRY(check(h_last, "h_last", 3, st, kF32, true, true, false));
+  M3_TRY(check(bx_last, "bx_last", 3, st, kF32, true, true, false));
+  if (G != 1) return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: one B / C group only");
+  if (Bn > INT32_MAX || L > INT32_MAX || H > INT32_MAX || P > 65535 || R > 8)
+    return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: dimension too large (rank must be <= 8)");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (Bn * H * Ds == 0) return M3_OK;
+  if (L == 0) {
+    const size_t bytes = sizeof(float) * Bn * H * Ds;
+    M3_TRY(copy_or_zero(fptr<void>(h_last), fptr<void>(h0), bytes, s, "h_last"));
+    return copy_or_zero(fptr<void>(bx_last), fptr<void>(bx0), bytes, s, "bx_last");
+  }
+  const size_t need = mimo_fwd_workspace_bytes(Bn, L, H, Ds);
+  if (!workspace || workspace_bytes < need)
+    return fail(M3_ERR_WORKSPACE, "workspace: need " + std::to_string(need) + " bytes");
+  if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0) return fail(M3_ERR_INVALID_ARGUMENT, "workspace: not 16-byte aligned");
+  M3_TRY(check_device_ptr(workspace, "workspace"));
+  MimoParams p{};
+  p.Bn = (int)Bn; p.L = (int)L; p.H = (int)H; p.P = (int)P; p.D = (int)Ds; p.R = (int)R;
+  p.adt = fptr<const float>(ADT); p.sadt = s3_scal(ADT);
+  p.dt = fptr<const float>(DT); p.sdt = s3_scal(DT);
+  p.trap = fptr<const float>(trap); p.strap = s3_scal(trap);
+  p.Dskip = fptr<const float>(D); p.sD = D->stride[0];
+  p.mimo_x = fptr<const float>(mimo_x); p.smx_h = mimo_x->stride[0]; p.smx_r = mimo_x->stride[1];
+  p.mimo_o = fptr<const float>(mimo_o); p.smo_h = mimo_o->stride[0]; p.smo_r = mimo_o->stride[1];
+  p.h0 = fptr<const float>(h0); p.bx0 = fptr<const float>(bx0);
+  p.y = out->data; p.sy = s3(out);
+  p.h_last = fptr<float>(h_last); p.bx_last = fptr<float>(bx_last);
+  MimoGrpParams q{};
+  q.zx = zxbcdt->data; q.s_zb = zxbcdt->stride[0]; q.s_zl = zxbcdt->stride[1];
+  q.dtype = zxbcdt->dtype;
+  q.angles = S > 0 ? fptr<const float>(angles) : nullptr;
+  q.B_bias = fptr<const float>(B_bias); q.C_bias = fptr<const float>(C_bias);
+  q.B_norm_w = fptr<const float>(B_norm_w); q.C_norm_w = fptr<const float>(C_norm_w);
+  q.eps = dims->norm_eps;
+  q.S = (int)S;
+  q.gate = gate;
+  return launch_mimo_layer_fwd(p, q, workspace, s);
 }
 
 size_t m3_layer_prologue_bwd_workspace_size(const m3_layer_dims* dims, int64_t batch, int64_t seqlen) {

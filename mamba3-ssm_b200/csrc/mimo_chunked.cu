@@ -566,17 +566,22 @@ inline int64_t fused_ws_bytes(int64_t cells, int64_t D) { return 16 + 8 * cells 
 // t0 .. t0+Q-1), the x box (rows t0-1 .. t0+Q-1, [row][p]), the chunk's bx and then states
 // (fp32 [t][d]), the rank projections of x, the step coefficients (a, beta, gamma, -) and
 // the running decay products, mimo_x and mimo_o (rows padded to P + 4 floats), the
-// readouts and the carries.
+// readouts and the carries. The group-row form (grp) has no C box: its B box holds the raw
+// group rows of B and C ([row][2R][d], rows t0-1 .. t0+Q-1), and it adds the z box (rows
+// t0 .. t0+Q, when the gate is fused), the RMS factors of those rows ([row][2R]) and the
+// (cos, sin) table of the rotated pairs ([row][S]).
 struct FusedSmem {
-  uint32_t bs, cs, xs, hs, xr, coef, cum, mx, mo, yr, carry, total;
+  uint32_t bs, cs, xs, zs, hs, xr, coef, cum, mx, mo, yr, carry, rs, tab, total;
 };
 __host__ __device__ inline uint32_t aup(uint32_t v, uint32_t k) { return (v + k - 1) / k * k; }
-__host__ __device__ inline FusedSmem fused_smem(int Q, int P, int R, int D, int eb, int ex) {
+__host__ __device__ inline FusedSmem fused_smem(int Q, int P, int R, int D, int eb, int ex, bool grp = false,
+                                                int S = 0, bool gate = false) {
   FusedSmem L;
   uint32_t o = 128;
-  L.bs = o; o = aup(o + (uint32_t)((Q + 1) * R * D * eb), 128);
-  L.cs = o; o = aup(o + (uint32_t)(Q * R * D * eb), 128);
+  L.bs = o; o = aup(o + (uint32_t)((Q + 1) * (grp ? 2 * R : R) * D * eb), 128);
+  L.cs = o; o = aup(o + (uint32_t)(grp ? 0 : Q * R * D * eb), 128);
   L.xs = o; o = aup(o + (uint32_t)((Q + 1) * P * ex), 128);
+  L.zs = o; o = aup(o + (uint32_t)(grp && gate ? (Q + 1) * P * ex : 0), 128);
   L.hs = o; o = aup(o + (uint32_t)(Q * D * 4), 16);
   L.xr = o; o = aup(o + (uint32_t)((Q + 1) * R * 4), 16);
   L.coef = o; o = aup(o + (uint32_t)(Q * 16), 16);
@@ -585,9 +590,28 @@ __host__ __device__ inline FusedSmem fused_smem(int Q, int P, int R, int D, int 
   L.mo = o; o = aup(o + (uint32_t)(R * (P + 4) * 4), 16);
   L.yr = o; o = aup(o + (uint32_t)(Q * R * 4), 16);
   L.carry = o; o = aup(o + (uint32_t)(D * 4), 16);
+  L.rs = o; o = aup(o + (uint32_t)(grp ? (Q + 1) * 2 * R * 4 : 0), 16);
+  L.tab = o; o = aup(o + (uint32_t)(grp ? (Q + 1) * S * 8 : 0), 16);
   L.total = o + 128;  // slack for aligning the dynamic shared-memory base
   return L;
 }
+
+// Operands of the group-row form: B_t[r] and C_t[r] of head h are
+//   rot_{t,h}(RMSNorm(raw_t[r]) * w + bias[h, r]),
+// raw the group rows of the in_proj output, rot the rotation of pairs (2k, 2k+1), k < S,
+// by angles[b, t, h, k]. The rotation is the same for every rank of a (t, h), so
+//   Bx_t = rot(w o sum_r xr_t[r] rs_t[r] raw_t[r] + sum_r xr_t[r] bias[h, r]) and
+//   C_t[r] . h_t = rs_t[r] (raw_t[r] o w) . rot^T(h_t) + bias[h, r] . rot^T(h_t),
+// one rotation per (t, pair) for B and one for the states.
+struct GrpArgs {
+  const float* angles;                            // (Bn, L, H, S) contiguous
+  const float* B_bias; const float* C_bias;       // (H, R, D) contiguous, 16-byte aligned
+  const float* B_norm_w; const float* C_norm_w;   // (D), 16-byte aligned
+  float eps;                                      // RMSNorm epsilon
+  int S;                                          // rotated pairs
+  int gate;                                       // y * silu(z), z from the z box
+  FastDiv fS;                                     // divisor S (S > 0)
+};
 
 struct FusedArgs {
   FastDiv fP4, fD4, fR, fU, fH;  // divisors headdim / 4, d_state / 4, rank, units, heads
@@ -681,15 +705,31 @@ __device__ __forceinline__ float look_back(const FusedArgs& f, int u, int c, int
   return 0.f;
 }
 
-template <typename TX, typename TB, int Q>
+// rotation of the pair (u, v) by (cos, sin) = cs, and by its transpose
+__device__ __forceinline__ void rot2(float& u, float& v, float2 cs) {
+  const float t = u * cs.x - v * cs.y;
+  v = u * cs.y + v * cs.x;
+  u = t;
+}
+__device__ __forceinline__ void rot2t(float& u, float& v, float2 cs) {
+  const float t = u * cs.x + v * cs.y;
+  v = v * cs.x - u * cs.y;
+  u = t;
+}
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// GRP: the group-row form (GrpArgs): mapB covers the group rows of B and C of the in_proj
+// output, mapX its z and x columns as 2H heads (z heads first), mapC is unused.
+template <typename TX, typename TB, int Q, bool GRP>
 __global__ void __launch_bounds__(kFT)
     mimo_fused_fwd_kernel(const __grid_constant__ CUtensorMap mapB, const __grid_constant__ CUtensorMap mapC,
-                          const __grid_constant__ CUtensorMap mapX, MimoParams a, FusedArgs f) {
+                          const __grid_constant__ CUtensorMap mapX, MimoParams a, FusedArgs f, GrpArgs g) {
   static_assert(Q <= kFT, "a thread per step of the chunk");
   extern __shared__ __align__(128) unsigned char fsm_raw[];
   unsigned char* fsm = fsm_raw + ((128u - (sm100::smem_u32(fsm_raw) & 127u)) & 127u);
   const int P = a.P, R = a.R, D = a.D, tid = threadIdx.x, lane = tid & 31;
-  const int P4 = P >> 2, D4 = D >> 2, MS = P + 4;
+  const int P4 = P >> 2, D4 = D >> 2, MS = P + 4, R2 = 2 * R;
+  const int S = GRP ? g.S : 0;
   const FusedSmem& L = f.L;
   uint64_t* barB = reinterpret_cast<uint64_t*>(fsm);
   uint64_t* barC = barB + 1;
@@ -697,6 +737,7 @@ __global__ void __launch_bounds__(kFT)
   const TB* Bs = reinterpret_cast<const TB*>(fsm + L.bs);
   const TB* Cs = reinterpret_cast<const TB*>(fsm + L.cs);
   const TX* xs = reinterpret_cast<const TX*>(fsm + L.xs);
+  const TX* zs = reinterpret_cast<const TX*>(fsm + L.zs);
   float* hs = reinterpret_cast<float*>(fsm + L.hs);
   float* xr = reinterpret_cast<float*>(fsm + L.xr);
   float4* coef = reinterpret_cast<float4*>(fsm + L.coef);
@@ -705,6 +746,8 @@ __global__ void __launch_bounds__(kFT)
   float* mo = reinterpret_cast<float*>(fsm + L.mo);
   float* yr = reinterpret_cast<float*>(fsm + L.yr);
   float* carry_s = reinterpret_cast<float*>(fsm + L.carry);
+  float* rs = reinterpret_cast<float*>(fsm + L.rs);
+  float2* tab = reinterpret_cast<float2*>(fsm + L.tab);
 
   if (tid == 0) {
     *tk_s = (int)atomicAdd(f.ticket, 1u);
@@ -726,11 +769,22 @@ __global__ void __launch_bounds__(kFT)
   if (tid == 0) {
     // whole boxes: rows outside the sequence (t0-1 of the first chunk, the tail of the
     // last) arrive as zeros and still count toward the transaction bytes
-    sm100::mbar_expect_tx(barB, (uint32_t)((Q + 1) * (R * D * sizeof(TB) + P * sizeof(TX))));
-    sm100::tma_load_5d(fsm + L.bs, &mapB, barB, 0, h, 0, t0 - 1, b);
-    sm100::tma_load_4d(fsm + L.xs, &mapX, barB, 0, h, t0 - 1, b);
-    sm100::mbar_expect_tx(barC, (uint32_t)(Q * R * D * sizeof(TB)));
-    sm100::tma_load_5d(fsm + L.cs, &mapC, barC, 0, h, 0, t0, b);
+    if constexpr (GRP) {
+      sm100::mbar_expect_tx(barB, (uint32_t)((Q + 1) * (R2 * D * sizeof(TB) + P * sizeof(TX))));
+      sm100::tma_load_4d(fsm + L.bs, &mapB, barB, 0, 0, t0 - 1, b);
+      sm100::tma_load_4d(fsm + L.xs, &mapX, barB, 0, a.H + h, t0 - 1, b);
+      if (g.gate) {
+        // the x map's box: Q + 1 rows from t0, the last one unused
+        sm100::mbar_expect_tx(barC, (uint32_t)((Q + 1) * P * sizeof(TX)));
+        sm100::tma_load_4d(fsm + L.zs, &mapX, barC, 0, h, t0, b);
+      }
+    } else {
+      sm100::mbar_expect_tx(barB, (uint32_t)((Q + 1) * (R * D * sizeof(TB) + P * sizeof(TX))));
+      sm100::tma_load_5d(fsm + L.bs, &mapB, barB, 0, h, 0, t0 - 1, b);
+      sm100::tma_load_4d(fsm + L.xs, &mapX, barB, 0, h, t0 - 1, b);
+      sm100::mbar_expect_tx(barC, (uint32_t)(Q * R * D * sizeof(TB)));
+      sm100::tma_load_5d(fsm + L.cs, &mapC, barC, 0, h, 0, t0, b);
+    }
   }
   // the inputs of the chunk that the CTA `ahead` tickets later will take, into L2
   const int tf = tk + f.ahead;
@@ -738,14 +792,26 @@ __global__ void __launch_bounds__(kFT)
     const int cf = fdiv(tf, f.fU), uf = tf - cf * f.units, bf = fdiv(uf, f.fH), hf = uf - bf * a.H;
     const int tf0 = cf * Q;
     if (tid == 0) {  // rows from max(t0 - 1, 0): no prefetch starts outside the tensor
-      sm100::tma_prefetch_l2_5d(&mapB, 0, hf, 0, max(tf0 - 1, 0), bf);
-      sm100::tma_prefetch_l2_5d(&mapC, 0, hf, 0, tf0, bf);
-      sm100::tma_prefetch_l2_4d(&mapX, 0, hf, max(tf0 - 1, 0), bf);
+      if constexpr (GRP) {
+        sm100::tma_prefetch_l2_4d(&mapB, 0, 0, max(tf0 - 1, 0), bf);
+        sm100::tma_prefetch_l2_4d(&mapX, 0, a.H + hf, max(tf0 - 1, 0), bf);
+        if (g.gate) sm100::tma_prefetch_l2_4d(&mapX, 0, hf, tf0, bf);
+      } else {
+        sm100::tma_prefetch_l2_5d(&mapB, 0, hf, 0, max(tf0 - 1, 0), bf);
+        sm100::tma_prefetch_l2_5d(&mapC, 0, hf, 0, tf0, bf);
+        sm100::tma_prefetch_l2_4d(&mapX, 0, hf, max(tf0 - 1, 0), bf);
+      }
     }
     for (int t = tf0 + tid; t < min(tf0 + Q, a.L); t += 32) {
       asm volatile("prefetch.global.L2 [%0];" ::"l"(a.adt + (int64_t)bf * a.sadt.b + (int64_t)t * a.sadt.l + (int64_t)hf * a.sadt.h));
       asm volatile("prefetch.global.L2 [%0];" ::"l"(a.dt + (int64_t)bf * a.sdt.b + (int64_t)t * a.sdt.l + (int64_t)hf * a.sdt.h));
       asm volatile("prefetch.global.L2 [%0];" ::"l"(a.trap + (int64_t)bf * a.strap.b + (int64_t)t * a.strap.l + (int64_t)hf * a.strap.h));
+      if (GRP && S > 0) {  // the angle row of step t and of step t - 1 (the first's row t0 - 1)
+        const float* ar = g.angles + (((int64_t)bf * a.L + t) * a.H + hf) * S;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(ar));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(ar + S - 1));
+        if (t == tf0 && t > 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(ar - (int64_t)a.H * S));
+      }
     }
   }
   for (int i = tid; i < R * P; i += kFT) {
@@ -757,31 +823,78 @@ __global__ void __launch_bounds__(kFT)
     const float tr = sigmoidf_(s_tr);
     coef[tid] = make_float4(expf(s_adt), s_dt * (1.0f - tr) + 0.5f * s_dt * tr, 0.5f * s_dt * tr, 0.f);
   }
-  __syncthreads();
-  wait_copies(barB);
-  // xr_t[k] = mimo_x[k, :] . x_t, four p per step, each row starting at its own p block
-  for (int i = tid; i < (n + 1) * R; i += kFT) {
-    const int row = fdiv(i, f.fR), k = i - row * R;
-    const TX* xrow = xs + row * P;
-    const float* mrow = mx + k * MS;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int pb = row - fdiv(row, f.fP4) * P4;
-    for (int e = 0; e < P4; ++e) {
-      fma4(acc, ld4f(xrow + 4 * pb), ld4f(mrow + 4 * pb));
-      pb = pb + 1 == P4 ? 0 : pb + 1;
+  if constexpr (GRP) {
+    // (cos, sin) of the rotated pairs of rows t0-1 .. t0+n-1 (identity before the sequence)
+    const float* ab = g.angles + ((int64_t)b * a.L * a.H + h) * S;
+    for (int i = tid; i < (n + 1) * S; i += kFT) {
+      const int row = fdiv(i, g.fS), k = i - row * S, t = t0 - 1 + row;
+      float sn = 0.f, cs = 1.f;
+      if (t >= 0) sincos_reduced(ab[(int64_t)t * a.H * S + k], &sn, &cs);
+      tab[i] = make_float2(cs, sn);
     }
-    xr[i] = (acc.x + acc.y) + (acc.z + acc.w);
   }
   __syncthreads();
-  // bx_t[d] = sum_r xr_t[r] B_t[r, d] for t0 .. t0+n-1 (four columns a thread), into the
-  // state array
-  for (int i = tid; i < n * D4; i += kFT) {
-    const int t = fdiv(i, f.fD4), d = 4 * (i - t * D4);
-    const float* xrow = xr + (t + 1) * R;
-    const TB* brow = Bs + (size_t)(t + 1) * R * D + d;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r = 0; r < R; ++r) fma4(acc, xrow[r], ld4f(brow + (size_t)r * D));
-    *reinterpret_cast<float4*>(hs + t * D + d) = acc;
+  wait_copies(barB);
+  // xr_t[k] = mimo_x[k, :] . x_t, four p per step, each row starting at its own p block;
+  // GRP: also the RMS factors of the group rows, 1 / sqrt(mean(raw^2) + eps)
+  const int nxr = (n + 1) * R;
+  for (int i = tid; i < (GRP ? 3 * nxr : nxr); i += kFT) {
+    if (!GRP || i < nxr) {
+      const int row = fdiv(i, f.fR), k = i - row * R;
+      const TX* xrow = xs + row * P;
+      const float* mrow = mx + k * MS;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      int pb = row - fdiv(row, f.fP4) * P4;
+      for (int e = 0; e < P4; ++e) {
+        fma4(acc, ld4f(xrow + 4 * pb), ld4f(mrow + 4 * pb));
+        pb = pb + 1 == P4 ? 0 : pb + 1;
+      }
+      xr[i] = (acc.x + acc.y) + (acc.z + acc.w);
+    } else {
+      const int j = i - nxr;  // row * 2R + k
+      const TB* grow = Bs + (size_t)j * D;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      int kb = j - fdiv(j, f.fD4) * D4;
+      for (int e = 0; e < D4; ++e) {
+        const float4 v = ld4f(grow + 4 * kb);
+        fma4(acc, v, v);
+        kb = kb + 1 == D4 ? 0 : kb + 1;
+      }
+      rs[j] = 1.0f / sqrtf(((acc.x + acc.y) + (acc.z + acc.w)) / (float)D + g.eps);
+    }
+  }
+  __syncthreads();
+  if constexpr (GRP) {
+    // bx of rows t0-1 (only after the first chunk; into the carry array) .. t0+n-1 (into
+    // the state array): w o sum_r xr rs raw_r + sum_r xr bias_r, then the rotation
+    for (int i = tid + (c > 0 ? 0 : D4); i < (n + 1) * D4; i += kFT) {
+      const int row = fdiv(i, f.fD4), d = 4 * (i - row * D4);
+      const float* xrow = xr + row * R;
+      const float* rrow = rs + row * R2;
+      const TB* brow = Bs + (size_t)row * R2 * D + d;
+      const float* bb = g.B_bias + (size_t)h * R * D + d;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f), accb = acc;
+      for (int r = 0; r < R; ++r) {
+        fma4(acc, xrow[r] * rrow[r], ld4f(brow + (size_t)r * D));
+        fma4(accb, xrow[r], ldg4(bb + (size_t)r * D));
+      }
+      fma4(accb, acc, ldg4(g.B_norm_w + d));
+      const int j0 = d >> 1;
+      if (j0 < S) rot2(accb.x, accb.y, tab[row * S + j0]);
+      if (j0 + 1 < S) rot2(accb.z, accb.w, tab[row * S + j0 + 1]);
+      *reinterpret_cast<float4*>(row == 0 ? carry_s + d : hs + (row - 1) * D + d) = accb;
+    }
+  } else {
+    // bx_t[d] = sum_r xr_t[r] B_t[r, d] for t0 .. t0+n-1 (four columns a thread), into the
+    // state array
+    for (int i = tid; i < n * D4; i += kFT) {
+      const int t = fdiv(i, f.fD4), d = 4 * (i - t * D4);
+      const float* xrow = xr + (t + 1) * R;
+      const TB* brow = Bs + (size_t)(t + 1) * R * D + d;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < R; ++r) fma4(acc, xrow[r], ld4f(brow + (size_t)r * D));
+      *reinterpret_cast<float4*>(hs + t * D + d) = acc;
+    }
   }
   __syncthreads();
   const int64_t cell = (int64_t)u * f.nch + c;
@@ -789,7 +902,11 @@ __global__ void __launch_bounds__(kFT)
   for (int d = tid; d < D; d += kFT) {
     float bxp = 0.f;
     if (c > 0) {
-      for (int r = 0; r < R; ++r) bxp = fmaf(xr[r], to_f32(Bs[(size_t)r * D + d]), bxp);
+      if constexpr (GRP) {
+        bxp = carry_s[d];  // this thread's own column: read here, overwritten below
+      } else {
+        for (int r = 0; r < R; ++r) bxp = fmaf(xr[r], to_f32(Bs[(size_t)r * D + d]), bxp);
+      }
     } else if (a.bx0) {
       bxp = a.bx0[(int64_t)u * D + d];
     }
@@ -832,38 +949,68 @@ __global__ void __launch_bounds__(kFT)
   }
   if (!ok) atomicExch(&g_mimo_error, 1);
   __syncthreads();
-  // the chunk's states from the carries: h_t = hloc_t + (a_t0 ... a_t) carry
+  // the chunk's states from the carries: h_t = hloc_t + (a_t0 ... a_t) carry (GRP: stored
+  // rotated back, rot^T h_t, for the readouts against the unrotated C rows)
   for (int i = tid; i < n * D4; i += kFT) {
     const int t = fdiv(i, f.fD4), d = 4 * (i - t * D4);
     float4 hv = *reinterpret_cast<const float4*>(hs + t * D + d);
     fma4(hv, cum[t], *reinterpret_cast<const float4*>(carry_s + d));
+    if constexpr (GRP) {
+      const int j0 = d >> 1;
+      if (j0 < S) rot2t(hv.x, hv.y, tab[(t + 1) * S + j0]);
+      if (j0 + 1 < S) rot2t(hv.z, hv.w, tab[(t + 1) * S + j0 + 1]);
+    }
     *reinterpret_cast<float4*>(hs + t * D + d) = hv;
   }
-  wait_copies(barC);
+  if (!GRP || g.gate) wait_copies(barC);
   __syncthreads();
   // yr_t[r] = C_t[r, :] . h_t + D xr_t[r]: a thread per (t, r), four columns per step, each
   // lane starting at its own column block so that a warp's reads fall in distinct banks
   const float Dk = a.Dskip[h * a.sD];
   for (int it = tid; it < n * R; it += kFT) {
     const int t = fdiv(it, f.fR), r = it - t * R;
-    const TB* crow = Cs + (size_t)it * D;
     const float* hrow = hs + (size_t)t * D;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     int k = lane - fdiv(lane, f.fD4) * D4;
+    if constexpr (GRP) {
+      // rs (raw o w) . h' + bias . h', h' = rot^T h
+      const TB* crow = Bs + ((size_t)(t + 1) * R2 + R + r) * D;
+      const float* cb = g.C_bias + ((size_t)h * R + r) * D;
+      float4 accb = acc;
 #pragma unroll 4
-    for (int e = 0; e < D4; ++e) {
-      fma4(acc, ld4f(crow + 4 * k), ld4f(hrow + 4 * k));
-      k = k + 1 == D4 ? 0 : k + 1;
+      for (int e = 0; e < D4; ++e) {
+        const float4 hv = ld4f(hrow + 4 * k), wv = ldg4(g.C_norm_w + 4 * k);
+        fma4(acc, ld4f(crow + 4 * k), make_float4(wv.x * hv.x, wv.y * hv.y, wv.z * hv.z, wv.w * hv.w));
+        fma4(accb, ldg4(cb + 4 * k), hv);
+        k = k + 1 == D4 ? 0 : k + 1;
+      }
+      const float dot = fmaf(rs[(t + 1) * R2 + R + r], (acc.x + acc.y) + (acc.z + acc.w),
+                             (accb.x + accb.y) + (accb.z + accb.w));
+      yr[it] = fmaf(Dk, xr[(t + 1) * R + r], dot);
+    } else {
+      const TB* crow = Cs + (size_t)it * D;
+#pragma unroll 4
+      for (int e = 0; e < D4; ++e) {
+        fma4(acc, ld4f(crow + 4 * k), ld4f(hrow + 4 * k));
+        k = k + 1 == D4 ? 0 : k + 1;
+      }
+      yr[it] = fmaf(Dk, xr[(t + 1) * R + r], (acc.x + acc.y) + (acc.z + acc.w));
     }
-    yr[it] = fmaf(Dk, xr[(t + 1) * R + r], (acc.x + acc.y) + (acc.z + acc.w));
   }
   __syncthreads();
-  // y_t = mimo_o^T yr_t, four outputs a thread
+  // y_t = mimo_o^T yr_t, four outputs a thread (GRP with the gate: times silu(z_t))
   TX* yb = reinterpret_cast<TX*>(a.y) + (int64_t)b * a.sy.b + (int64_t)h * a.sy.h;
   for (int i = tid; i < n * P4; i += kFT) {
     const int t = fdiv(i, f.fP4), p = 4 * (i - t * P4);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int r = 0; r < R; ++r) fma4(acc, yr[t * R + r], ld4f(mo + r * MS + p));
+    if (GRP && g.gate) {
+      const float4 zv = ld4f(zs + t * P + p);
+      acc.x *= zv.x * fast_sigmoid(zv.x);
+      acc.y *= zv.y * fast_sigmoid(zv.y);
+      acc.z *= zv.z * fast_sigmoid(zv.z);
+      acc.w *= zv.w * fast_sigmoid(zv.w);
+    }
     TX* yp = yb + (int64_t)(t0 + t) * a.sy.l + p;
     if (f.yvec) {
       st4(yp, acc);
@@ -1405,11 +1552,81 @@ int run_fused(const MimoParams& p, void* ws, cudaStream_t s) {
   f.L = fused_smem(Q, p.P, p.R, p.D, (int)sizeof(TB), (int)sizeof(TX));
   const size_t smem = f.L.total;
   static LaunchCache lc;
-  M3_TRY(kernel_residency(reinterpret_cast<const void*>(mimo_fused_fwd_kernel<TX, TB, Q>), kFT, smem, &lc,
+  M3_TRY(kernel_residency(reinterpret_cast<const void*>(mimo_fused_fwd_kernel<TX, TB, Q, false>), kFT, smem, &lc,
                           &f.ahead));
   cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)fused_ws_bytes(cells, p.D), s);
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
-  mimo_fused_fwd_kernel<TX, TB, Q><<<(unsigned)cells, kFT, smem, s>>>(mB, mC, mX, p, f);
+  mimo_fused_fwd_kernel<TX, TB, Q, false><<<(unsigned)cells, kFT, smem, s>>>(mB, mC, mX, p, f, GrpArgs{});
+  return check_launch("mimo_fused_fwd_kernel");
+}
+
+// 4-d map with a (box0, box1, rows, 1) box over dims (n0, n1, L, Bn), element strides
+// (s1, s_l, s_b) for dims 1..3, no swizzle: the box lands as [row][i1][i0].
+template <typename T>
+bool make_map4(CUtensorMap* m, const void* base, int64_t n0, int64_t n1, int64_t L, int64_t Bn, int64_t s1,
+               int64_t s_l, int64_t s_b, int box0, int box1, int rows) {
+  auto enc = chunk_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t e = sizeof(T);
+  cuuint64_t dims[4] = {(cuuint64_t)n0, (cuuint64_t)n1, (cuuint64_t)L, (cuuint64_t)Bn};
+  cuuint64_t strides[3] = {(cuuint64_t)s1 * e, (cuuint64_t)s_l * e, (cuuint64_t)s_b * e};
+  cuuint32_t box[4] = {(cuuint32_t)box0, (cuuint32_t)box1, (cuuint32_t)rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, tmap_type<T>(), 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Chunk length of the group-row form: the longest of 64 / 32 / 16 steps whose shared memory
+// lets four CTAs share an SM, else 16 when it fits at all, else 0.
+inline int grp_chunk(const MimoParams& p, int e, int S, bool gate) {
+  for (int q : {64, 32, 16})
+    if (fused_smem(q, p.P, p.R, p.D, e, e, true, S, gate).total <= 55u * 1024u) return q;
+  return fused_smem(16, p.P, p.R, p.D, e, e, true, S, gate).total <= 200u * 1024u ? 16 : 0;
+}
+
+// Group-row form of the single-pass forward from the in_proj output zx (Bn, L, d_proj):
+// z at columns [0, H P), x at [H P, 2 H P), the B group rows at [2 H P, 2 H P + R D) and the
+// C rows right after. Returns M3_ERR_UNSUPPORTED (nothing launched) when a map cannot be
+// made.
+template <typename T, int Q>
+int run_fused_grp(const MimoParams& p, const GrpArgs& g0, const T* zx, int64_t s_zb, int64_t s_zl, void* ws,
+                  cudaStream_t s) {
+  const int64_t nch = (p.L + Q - 1) / Q, units = (int64_t)p.Bn * p.H, cells = units * nch;
+  if (cells >= INT32_MAX) return M3_ERR_UNSUPPORTED;
+  const int64_t di = (int64_t)p.H * p.P;
+  CUtensorMap mB, mX;
+  if (!make_map4<T>(&mB, zx + 2 * di, p.D, 2 * p.R, p.L, p.Bn, p.D, s_zl, s_zb, p.D, 2 * p.R, Q + 1) ||
+      !make_map4<T>(&mX, zx, p.P, 2 * p.H, p.L, p.Bn, p.P, s_zl, s_zb, p.P, 1, Q + 1))
+    return M3_ERR_UNSUPPORTED;
+  GrpArgs g = g0;
+  if (g.S > 0) g.fS = make_fastdiv((uint32_t)g.S);
+  FusedArgs f;
+  f.fP4 = make_fastdiv((uint32_t)(p.P / 4));
+  f.fD4 = make_fastdiv((uint32_t)(p.D / 4));
+  f.fR = make_fastdiv((uint32_t)p.R);
+  f.fU = make_fastdiv((uint32_t)units);
+  f.fH = make_fastdiv((uint32_t)p.H);
+  f.nch = (int)nch;
+  f.units = (int)units;
+  {
+    const int64_t ey = sizeof(T);
+    f.yvec = reinterpret_cast<uintptr_t>(p.y) % 16 == 0 && (p.sy.b * ey) % 16 == 0 && (p.sy.l * ey) % 16 == 0 &&
+             (p.sy.h * ey) % 16 == 0;
+  }
+  char* w = static_cast<char*>(ws);
+  f.ticket = reinterpret_cast<unsigned*>(w);
+  f.rec = reinterpret_cast<unsigned long long*>(w + 16);
+  f.arec = f.rec + cells * p.D;
+  f.L = fused_smem(Q, p.P, p.R, p.D, (int)sizeof(T), (int)sizeof(T), true, g.S, g.gate != 0);
+  const size_t smem = f.L.total;
+  static LaunchCache lc;
+  M3_TRY(kernel_residency(reinterpret_cast<const void*>(mimo_fused_fwd_kernel<T, T, Q, true>), kFT, smem, &lc,
+                          &f.ahead));
+  cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)fused_ws_bytes(cells, p.D), s);
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  // mapC is not read by the group-row form; mB stands in for it
+  mimo_fused_fwd_kernel<T, T, Q, true><<<(unsigned)cells, kFT, smem, s>>>(mB, mB, mX, p, f, g);
   return check_launch("mimo_fused_fwd_kernel");
 }
 
@@ -1605,6 +1822,46 @@ int launch_mimo_fwd_chunked(const MimoParams& p, int xdt, int bcdt, void* ws, cu
   if (xdt == M3_FLOAT16 && bcdt == M3_FLOAT16) return run_chunked<__half, __half>(p, ws, s);
   if (xdt == M3_FLOAT16 && bcdt == M3_FLOAT32) return run_chunked<__half, float>(p, ws, s);
   return fail(M3_ERR_UNSUPPORTED, "unsupported dtype combination for x / B,C");
+}
+
+template <typename T>
+static int grp_dispatch(const MimoParams& p, const GrpArgs& g, const MimoGrpParams& q, void* ws, cudaStream_t s) {
+  const T* zx = static_cast<const T*>(q.zx);
+  int rc = M3_ERR_UNSUPPORTED;
+  switch (grp_chunk(p, (int)sizeof(T), q.S, q.gate != 0)) {
+    case 64: rc = run_fused_grp<T, 64>(p, g, zx, q.s_zb, q.s_zl, ws, s); break;
+    case 32: rc = run_fused_grp<T, 32>(p, g, zx, q.s_zb, q.s_zl, ws, s); break;
+    case 16: rc = run_fused_grp<T, 16>(p, g, zx, q.s_zb, q.s_zl, ws, s); break;
+    default: break;
+  }
+  if (rc == M3_ERR_UNSUPPORTED) return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: tensor maps unavailable");
+  return rc;
+}
+
+int launch_mimo_layer_fwd(const MimoParams& p, const MimoGrpParams& q, void* ws, cudaStream_t s) {
+  const int64_t e = q.dtype == M3_FLOAT32 ? 4 : 2;
+  auto a16 = [](const void* v) { return reinterpret_cast<uintptr_t>(v) % 16 == 0; };
+  const int64_t di = (int64_t)p.H * p.P;
+  if (!(a16(q.zx) && (2 * di * e) % 16 == 0 && q.s_zb > 0 && q.s_zl > 0 && (q.s_zb * e) % 16 == 0 &&
+        (q.s_zl * e) % 16 == 0 && (p.P * e) % 16 == 0 && p.P <= 256 && (p.D * e) % 16 == 0 && p.D % 4 == 0 &&
+        p.D <= 256 && p.R <= 8 && 2 * q.S <= p.D && a16(q.B_bias) && a16(q.C_bias) && a16(q.B_norm_w) &&
+        a16(q.C_norm_w)))
+    return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: the in_proj output or the parameters are not laid out on "
+                                    "16-byte units (or d_state / headdim / rank out of range)");
+  if (grp_chunk(p, (int)e, q.S, q.gate != 0) == 0)
+    return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: shapes too large for shared memory");
+  if (!chunk_encode_fn()) return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: tensor-map encoder unavailable");
+  GrpArgs g{};
+  g.angles = q.angles;
+  g.B_bias = q.B_bias; g.C_bias = q.C_bias;
+  g.B_norm_w = q.B_norm_w; g.C_norm_w = q.C_norm_w;
+  g.eps = q.eps;
+  g.S = q.S;
+  g.gate = q.gate;
+  if (q.dtype == M3_FLOAT32) return grp_dispatch<float>(p, g, q, ws, s);
+  if (q.dtype == M3_BFLOAT16) return grp_dispatch<__nv_bfloat16>(p, g, q, ws, s);
+  if (q.dtype == M3_FLOAT16) return grp_dispatch<__half>(p, g, q, ws, s);
+  return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: unsupported dtype");
 }
 
 }  // namespace m3

@@ -55,6 +55,23 @@ int launch_mimo_bwd_fused(const MimoParams& p, int xdt, int bcdt, const void* fw
                           size_t ws_bytes, cudaStream_t s);
 // the word the single-pass kernels set when a bounded wait gives up
 int mimo_error_word(bool reset, int* out);
+// Single-pass forward of one layer's scan from its in_proj output (one B / C group): x
+// and z from zx, B / C from its group rows normalised, biased per head and rotated by the
+// angles inside the kernel, y optionally gated (y * silu(z)). p carries the step scalars,
+// D, mimo_x / mimo_o, the optional states and y (x, Bm, Cm unused). Workspace as for
+// launch_mimo_fwd_chunked. M3_ERR_UNSUPPORTED, nothing launched, when the layout does not
+// allow the tensor maps.
+struct MimoGrpParams {
+  const void* zx; int64_t s_zb, s_zl;  // (Bn, L, d_proj), innermost contiguous
+  int dtype;                           // of zx (and of y)
+  const float* angles;                 // (Bn, L, H, S) contiguous
+  const float* B_bias; const float* C_bias;      // (H, R, D) contiguous
+  const float* B_norm_w; const float* C_norm_w;  // (D)
+  float eps;
+  int S;     // rotated pairs
+  int gate;  // 1: y * silu(z)
+};
+int launch_mimo_layer_fwd(const MimoParams& p, const MimoGrpParams& q, void* ws, cudaStream_t s);
 // Chunk-parallel backward (mimo_chunked.cu), used when its shared-memory layout fits.
 bool mimo_bwd_chunked_fits(int P, int R, int D);
 size_t mimo_bwd_chunked_workspace_bytes(int64_t Bn, int64_t L, int64_t H, int64_t D);

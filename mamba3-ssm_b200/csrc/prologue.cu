@@ -249,6 +249,7 @@ int launch_prologue(const PrologueParams& p, int zdt, int odt, cudaStream_t s) {
     if (wide) prologue_angle_kernel<TZ, kATmax><<<ga, kATmax, 0, s>>>(p);               \
     else prologue_angle_kernel<TZ, 128><<<ga, 128, 0, s>>>(p);                          \
     M3_TRY(check_launch("prologue_angle_kernel"));                                      \
+    if (!p.Bp) return M3_OK; /* angles and step scalars only */                         \
     const int th = 32 * (p.R < 8 ? p.R : 8);                                            \
     if (ppl == 1) prologue_bc_kernel<TZ, TO, 1><<<gb, th, 0, s>>>(p);                   \
     else if (ppl == 2) prologue_bc_kernel<TZ, TO, 2><<<gb, th, 0, s>>>(p);              \

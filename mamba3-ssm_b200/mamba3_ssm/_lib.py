@@ -79,6 +79,8 @@ _SIGS = {
     "m3_device_timeouts": ([ctypes.c_int, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "m3_layer_prologue": ([ctypes.c_void_p] + [_P] * 13 + [ctypes.c_void_p], ctypes.c_int),
     "m3_silu_gate": ([_P] * 3 + [ctypes.c_void_p], ctypes.c_int),
+    "m3_mimo_layer_scan_fwd": ([ctypes.c_void_p] + [_P] * 14 + [ctypes.c_int32] + [_P] * 3 +
+                               [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "m3_layer_prologue_bwd_workspace_size": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64], ctypes.c_size_t),
     "m3_layer_prologue_bwd": ([ctypes.c_void_p] + [_P] * 19 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p],
                               ctypes.c_int),

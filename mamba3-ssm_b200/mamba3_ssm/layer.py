@@ -225,6 +225,10 @@ class Mamba3(nn.Module):
             zx = zx.contiguous()
         vals = self._step_params()
         dims = self._f32_cache[3]
+        if self.is_mimo and self.num_bc_heads == 1:
+            r = self._forward_mimo_rows(zx, vals, dims, cache, want_cache)
+            if r is not None:
+                return r
         dev = zx.device
         op = torch.bfloat16 if zx.dtype == torch.bfloat16 else torch.float32
         Bp = torch.empty(batch, Ln, R, H, Ds, dtype=op, device=dev)
@@ -246,6 +250,52 @@ class Mamba3(nn.Module):
         with torch.cuda.device(dev):
             rc = lib.m3_silu_gate(*a.ptrs, torch.cuda.current_stream(dev).cuda_stream)
         L.check(rc, "m3_silu_gate")
+        return self.out_proj(g.flatten(-2)), new
+
+    def _forward_mimo_rows(self, zx, vals, dims, cache, want_cache):
+        """Inference forward of a one-group MIMO layer without per-head B / C tensors:
+        m3_layer_prologue writes only the step scalars and angles, and
+        m3_mimo_layer_scan_fwd forms B / C from the group rows inside the scan and gates its
+        output. None (after the scalar prologue, nothing else launched) when that kernel does
+        not apply to this layout; the caller then runs the prologue with B / C and the scan."""
+        batch, Ln, _ = zx.shape
+        Ds, H, P, S = self.d_state, self.nheads, self.headdim, self.num_rope_angles
+        dev = zx.device
+        ADT, DT, trap = (torch.empty(batch, Ln, H, dtype=torch.float32, device=dev) for _ in range(3))
+        ang = torch.empty(batch, Ln, H, S, dtype=torch.float32, device=dev)
+        ang0 = cache[0].float().contiguous() if cache is not None else None
+        lib = L.load()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        a = L.pack(zx, *vals[:5], ang0, None, None, ADT, DT, trap, ang)
+        with torch.cuda.device(dev):
+            rc = lib.m3_layer_prologue(ctypes.byref(dims), *a.ptrs, stream)
+        L.check(rc, "m3_layer_prologue")
+        h0 = b0 = hl = bl = None
+        if want_cache:
+            if cache is not None:
+                h0 = cache[1].float().contiguous()
+                b0 = cache[2].float().contiguous()
+            hl = torch.empty(batch, H, Ds, dtype=torch.float32, device=dev)
+            bl = torch.empty(batch, H, Ds, dtype=torch.float32, device=dev)
+        g = torch.empty(batch, Ln, H, P, dtype=zx.dtype, device=dev)
+        ws = torch.empty(lib.m3_mimo_scan_fwd_workspace_size(batch, Ln, H, Ds), dtype=torch.uint8, device=dev)
+        a = L.pack(zx, ADT, DT, trap, ang, vals[1], vals[2], vals[3], vals[4], vals[5], vals[6], vals[7], h0, b0)
+        o = L.pack(g, hl, bl)
+        with torch.cuda.device(dev):
+            rc = lib.m3_mimo_layer_scan_fwd(ctypes.byref(dims), *a.ptrs, 1, *o.ptrs, ws.data_ptr(), ws.numel(),
+                                            stream)
+        if rc == L.M3_ERR_UNSUPPORTED:
+            return None
+        L.check(rc, "m3_mimo_layer_scan_fwd")
+        new = None
+        if want_cache:
+            if Ln > 0:
+                a_last = ang[:, -1].contiguous()
+            elif cache is not None:
+                a_last = cache[0].float().clone()
+            else:
+                a_last = torch.zeros(batch, H, S, device=dev)
+            new = (a_last, hl, bl)
         return self.out_proj(g.flatten(-2)), new
 
     def _scan(self, x, Bp, Cp, ADT, DT, trap, ang, cache, want_cache):

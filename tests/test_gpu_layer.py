@@ -257,3 +257,116 @@ def test_fused_forward_equals_autograd_forward(cfg, dtype):
         y = m(u)
     tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
     assert rel_err(y.float().cpu().numpy(), y_ref.detach().float().cpu().numpy()) < tol
+
+
+# one-group MIMO layers whose in_proj output rows are whole 16-byte units in fp32 and bf16
+# (d_in_proj a multiple of 8), so that m3_mimo_layer_scan_fwd applies
+ROW_SHAPES = [
+    dict(d_state=64, headdim=32, mimo_rank=4),
+    dict(d_state=128, headdim=32, mimo_rank=2),
+    dict(d_state=32, headdim=16, mimo_rank=8, rope_fraction=1.0),
+    dict(d_state=16, headdim=32, mimo_rank=1, rope_fraction=1.0),
+]
+
+
+def _row_layer(cfg, dtype):
+    from mamba3_ssm import Mamba3
+    torch.manual_seed(0)
+    m = Mamba3(d_model=128, expand=2, is_mimo=True, **cfg).to(dtype).to(DEV)
+    gen = torch.Generator().manual_seed(3)
+    with torch.no_grad():
+        m.dt_bias.add_(0.5)
+        for p in (m.B_bias, m.C_bias, m.B_norm.weight, m.C_norm.weight):
+            p.copy_((torch.randn(p.shape, generator=gen) * 0.5 + 1.0).to(p.dtype))
+    return m
+
+
+def _prologue(m, zx, with_bc):
+    import ctypes
+    from mamba3_ssm import _lib as L
+    b, n, _ = zx.shape
+    R, D, H, S = m.mimo_rank, m.d_state, m.nheads, m.num_rope_angles
+    vals = m._step_params()
+    dims = m._f32_cache[3]
+    f = dict(dtype=torch.float32, device=DEV)
+    Bp = torch.empty(b, n, R, H, D, **f) if with_bc else None
+    Cp = torch.empty(b, n, R, H, D, **f) if with_bc else None
+    ADT, DT, trap = (torch.empty(b, n, H, **f) for _ in range(3))
+    ang = torch.empty(b, n, H, S, **f)
+    lib = L.load()
+    a = L.pack(zx, *vals[:5], None, Bp, Cp, ADT, DT, trap, ang)
+    L.check(lib.m3_layer_prologue(ctypes.byref(dims), *a.ptrs, torch.cuda.current_stream().cuda_stream),
+            "m3_layer_prologue")
+    return Bp, Cp, ADT, DT, trap, ang
+
+
+def _row_scan(m, zx, scal, h0, b0, gate):
+    import ctypes
+    from mamba3_ssm import _lib as L
+    b, n, _ = zx.shape
+    H, P, D = m.nheads, m.headdim, m.d_state
+    vals = m._step_params()
+    dims = m._f32_cache[3]
+    lib = L.load()
+    out = torch.empty(b, n, H, P, dtype=zx.dtype, device=DEV)
+    hl = torch.empty(b, H, D, device=DEV)
+    bl = torch.empty(b, H, D, device=DEV)
+    ws = torch.empty(lib.m3_mimo_scan_fwd_workspace_size(b, n, H, D), dtype=torch.uint8, device=DEV)
+    a = L.pack(zx, *scal, *vals[1:8], h0, b0)
+    o = L.pack(out, hl, bl)
+    rc = lib.m3_mimo_layer_scan_fwd(ctypes.byref(dims), *a.ptrs, gate, *o.ptrs, ws.data_ptr(), ws.numel(),
+                                    torch.cuda.current_stream().cuda_stream)
+    return rc, out, hl, bl
+
+
+@pytest.mark.parametrize("gate", [1, 0])
+@pytest.mark.parametrize("Ln", [1, 31, 300])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("cfg", ROW_SHAPES, ids=lambda c: "_".join(f"{k}{v}" for k, v in c.items()))
+def test_mimo_layer_scan_matches_prologue_and_scan(cfg, dtype, Ln, gate):
+    """m3_mimo_layer_scan_fwd (per-head B / C formed from the group rows inside the scan,
+    gate fused) == m3_layer_prologue's per-head B / C (fp32) + the MIMO scan + the gate, from
+    carried states, with its end states; the fused entry must apply to these layouts.
+    Tolerances: rel 1e-4 fp32; bf16 outputs 1e-2 (the reference path rounds y to bf16
+    before the gate), end states 1e-4 (both fp32 from the same bf16 inputs)."""
+    import torch.nn.functional as F
+    from mamba3_ssm import _lib as L
+    from mamba3_ssm.ops import _mimo_fwd_raw
+    m = _row_layer(cfg, dtype)
+    H, P, D = m.nheads, m.headdim, m.d_state
+    gen = torch.Generator().manual_seed(Ln)
+    u = torch.randn(2, Ln, 128, generator=gen).to(dtype).to(DEV)
+    h0 = (torch.randn(2, H, D, generator=gen) * 0.5).to(DEV)
+    b0 = (torch.randn(2, H, D, generator=gen) * 0.5).to(DEV)
+    with torch.no_grad():
+        zx = m.in_proj(u).contiguous()
+        Bp, Cp, ADT, DT, trap, ang = _prologue(m, zx, True)
+        di = m.d_inner
+        z = zx[..., :di].unflatten(-1, (H, P))
+        x = zx[..., di:2 * di].unflatten(-1, (H, P))
+        y, hl_ref, bl_ref = _mimo_fwd_raw(x, Bp, Cp, ADT, DT, trap, m.D.float(), m.mimo_x.float(),
+                                          m.mimo_o.float(), h0, b0, True)
+        ref = y.float() * F.silu(z.float()) if gate else y.float()
+        rc, out, hl, bl = _row_scan(m, zx, (ADT, DT, trap, ang), h0, b0, gate)
+    assert rc == L.M3_OK, L.load().m3_last_error_string().decode()
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-4
+    assert rel_err(out.float().cpu().numpy(), ref.cpu().numpy()) < tol
+    assert rel_err(hl.cpu().numpy(), hl_ref.cpu().numpy()) < 1e-4
+    assert rel_err(bl.cpu().numpy(), bl_ref.cpu().numpy()) < 1e-4
+
+
+def test_mimo_layer_scan_unsupported_layout_falls_back():
+    """A bf16 layer whose in_proj rows are not whole 16-byte units: the fused entry
+    launches nothing and reports M3_ERR_UNSUPPORTED; Mamba3.forward then takes the prologue
+    with per-head B / C and gives the training forward's result."""
+    from mamba3_ssm import _lib as L
+    m = _row_layer(dict(d_state=64, headdim=128, mimo_rank=3), torch.bfloat16)  # d_in_proj 918
+    u = torch.randn(2, 40, 128, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).to(DEV)
+    with torch.no_grad():
+        zx = m.in_proj(u).contiguous()
+        _, _, ADT, DT, trap, ang = _prologue(m, zx, False)
+        rc, *_ = _row_scan(m, zx, (ADT, DT, trap, ang), None, None, 1)
+        y = m(u)
+    assert rc == L.M3_ERR_UNSUPPORTED
+    y_ref = m(u)  # autograd path
+    assert rel_err(y.float().cpu().numpy(), y_ref.detach().float().cpu().numpy()) < 2e-2
