@@ -2,7 +2,7 @@
 // everything between the in_proj GEMM and the scan, and the silu gate between the scan and
 // out_proj, read straight from the in_proj output.
 //
-//   angle kernel (one CTA per (b, h), thread = step, block scans over tiles of 128 steps):
+//   angle kernels (one CTA per (b, h); 128-step tiles, or segments when units are few):
 //     DT = softplus(dd_dt + dt_bias), A = -min(softplus(dd_A), -A_floor) (layer.py:207),
 //     ADT = A DT, trap logit copied to fp32, angles[b,l,h,i] = angle0[b,h,i] (the decode
 //     cache's angle state, zero when absent) + sum_{l'<=l} angle_raw[b,l',i] DT
@@ -18,18 +18,13 @@
 namespace m3 {
 namespace {
 
-// one CTA per (b, h); the sequence in tiles of kAT steps, thread = step; the angle
-// cumsums are block-wide inclusive scans (warp shuffles, then the warp totals) carried
-// from tile to tile. kAT = 512 when there are few (b, h) units (a shorter serial walk per
-// CTA), 128 otherwise.
-constexpr int kATmax = 512;
-
-// CTA per (b, h), thread = time step of a kAT-step tile. Each thread carries its step's
+// Many (b, h) units (four or more per SM): one CTA per (b, h), thread = time step of a
+// kAT-step tile. Each thread carries its step's
 // angles 16 at a time in registers: a warp scan over the tile, the warp totals through
 // shared memory (two barriers per 16 angles), then one (b, l, h) row of angles written as
 // 16-byte vectors (the S angles of a row are contiguous).
 template <typename TZ, int kAT>
-__global__ void __launch_bounds__(kAT) prologue_angle_kernel(PrologueParams a) {
+__global__ void __launch_bounds__(kAT) prologue_angle_tile_kernel(PrologueParams a) {
   constexpr int kS = 16;
   __shared__ float wsum[kAT / 32][kS];
   __shared__ float carry[256];
@@ -96,6 +91,91 @@ __global__ void __launch_bounds__(kAT) prologue_angle_kernel(PrologueParams a) {
           if (s0 + k < S) carry[s0 + k] = x[k];
     }
     __syncthreads();
+  }
+}
+
+// Few (b, h) units: one CTA per (b, h); warp w walks the w-th of the CTA's consecutive segments of T steps
+// (T a multiple of 32) in slabs of 32 steps. Per slab each lane forms DT of one step (lane
+// = step, one softplus per step); the walk over the slab's steps then runs with lane =
+// angle (32 angles at a time), DT of step j handed over by a warp shuffle, so each step's
+// angle_raw row and each row of angles is one contiguous access of the warp. Pass 1 sums
+// each angle's increments angle_raw[l, i] DT[l] over the warp's segment; the segment totals
+// meet in shared memory, where one thread per angle turns them into exclusive prefixes
+// (starting from angle0). Pass 2 walks the segment again from that prefix, writing the
+// running angles; its first angle group also writes DT, ADT and trap. No scratch memory, no
+// waits between CTAs.
+template <typename TZ>
+__global__ void __launch_bounds__(1024) prologue_angle_kernel(PrologueParams a, int T) {
+  constexpr int kB = 8;           // steps whose angle_raw loads are issued together
+  __shared__ float tot[32][65];  // [segment][angle]: totals, then exclusive prefixes
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, W = blockDim.x >> 5;
+  const int u = blockIdx.x, b = u / a.H, h = u - b * a.H;
+  const int H = a.H, S = a.S;
+  const int off_dt = 2 * a.d_inner + 2 * a.D * a.G * a.R;
+  const int off_A = off_dt + H, off_tr = off_A + H, off_ang = off_tr + H;
+  const float dtb = a.dt_bias[h];
+  const TZ* base = reinterpret_cast<const TZ*>(a.zx) + (int64_t)b * a.s_zb;
+  const int64_t szl = a.s_zl, HS = (int64_t)H * S;
+  const int l0 = w * T, l1 = min(l0 + T, a.L);
+  for (int s0 = 0; s0 < S; s0 += 32) {
+    const int s = s0 + lane;
+    float acc = 0.f;
+    for (int ls = l0; ls < l1; ls += 32) {
+      const int l = ls + lane, n = min(32, l1 - ls);
+      const float dtl = l < l1 ? softplusf_(to_f32(base[(int64_t)l * szl + off_dt + h]) + dtb) : 0.f;
+      const TZ* col = base + (int64_t)ls * szl + off_ang + (s < S ? s : 0);
+      for (int j0 = 0; j0 < n; j0 += kB) {
+        float xv[kB];
+#pragma unroll
+        for (int k = 0; k < kB; ++k) xv[k] = j0 + k < n ? to_f32(col[(int64_t)(j0 + k) * szl]) : 0.f;
+#pragma unroll
+        for (int k = 0; k < kB; ++k) acc = fmaf(xv[k], __shfl_sync(0xffffffffu, dtl, (j0 + k) & 31), acc);
+      }
+    }
+    if (s < S) tot[w][s] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x < S) {
+    const int i = threadIdx.x;
+    float run = a.angle0 ? a.angle0[(int64_t)u * S + i] : 0.f;
+    for (int j = 0; j < W; ++j) {
+      const float t = tot[j][i];
+      tot[j][i] = run;
+      run += t;
+    }
+  }
+  __syncthreads();
+  for (int s0 = 0; s0 < (S > 0 ? S : 1); s0 += 32) {  // S == 0: one pass for DT, ADT, trap
+    const int s = s0 + lane;
+    const bool sv = s < S;
+    float run = sv ? tot[w][s] : 0.f;
+    for (int ls = l0; ls < l1; ls += 32) {
+      const int l = ls + lane, n = min(32, l1 - ls);
+      const bool v = l < l1;
+      const TZ* row = base + (int64_t)(v ? l : l0) * szl;
+      const float dtl = v ? softplusf_(to_f32(row[off_dt + h]) + dtb) : 0.f;
+      if (s0 == 0 && v) {
+        const int64_t o = ((int64_t)b * a.L + l) * H + h;
+        const float A = -fminf(softplusf_(to_f32(row[off_A + h])), -a.A_floor);
+        a.DT[o] = dtl;
+        a.ADT[o] = A * dtl;
+        a.trap[o] = to_f32(row[off_tr + h]);
+      }
+      if (S == 0) continue;
+      const TZ* col = base + (int64_t)ls * szl + off_ang + (sv ? s : 0);
+      float* dst = a.angles + ((int64_t)b * a.L + ls) * HS + (int64_t)h * S + (sv ? s : 0);
+      // the batch's loads first: each is independent of the angles stored before it
+      for (int j0 = 0; j0 < n; j0 += kB) {
+        float xv[kB];
+#pragma unroll
+        for (int k = 0; k < kB; ++k) xv[k] = j0 + k < n ? to_f32(col[(int64_t)(j0 + k) * szl]) : 0.f;
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+          run = fmaf(xv[k], __shfl_sync(0xffffffffu, dtl, (j0 + k) & 31), run);
+          if (sv && j0 + k < n) dst[(int64_t)(j0 + k) * HS] = run;
+        }
+      }
+    }
   }
 }
 
@@ -243,11 +323,16 @@ int launch_prologue(const PrologueParams& p, int zdt, int odt, cudaStream_t s) {
   const int ppl = (p.D / 2 + 31) / 32;
   int sms = 148;
   if (device_sm_count(&sms) != M3_OK) sms = 148;
-  const bool wide = (int64_t)ga < 4 * (int64_t)sms && p.L > 128;
+  // fewer than four (b, h) units per SM: the segment kernel, about 64 warps per SM over the
+  // grid (at most 32 segments per unit, each whole slabs of 32 steps); else 128-step tiles
+  const bool seg = (int64_t)ga < 4 * (int64_t)sms && p.L > 128;
+  const int64_t want = std::min<int64_t>(32, std::max<int64_t>(1, ((int64_t)sms * 64 + ga - 1) / ga));
+  const int T = (int)(((p.L + want - 1) / want + 31) / 32 * 32);
+  const int nseg = (p.L + T - 1) / T;
 #define M3_PRO(TZ, TO)                                                                  \
   do {                                                                                  \
-    if (wide) prologue_angle_kernel<TZ, kATmax><<<ga, kATmax, 0, s>>>(p);               \
-    else prologue_angle_kernel<TZ, 128><<<ga, 128, 0, s>>>(p);                          \
+    if (seg) prologue_angle_kernel<TZ><<<ga, 32 * nseg, 0, s>>>(p, T);                  \
+    else prologue_angle_tile_kernel<TZ, 128><<<ga, 128, 0, s>>>(p);                     \
     M3_TRY(check_launch("prologue_angle_kernel"));                                      \
     if (!p.Bp) return M3_OK; /* angles and step scalars only */                         \
     const int th = 32 * (p.R < 8 ? p.R : 8);                                            \

@@ -370,3 +370,54 @@ def test_mimo_layer_scan_unsupported_layout_falls_back():
     assert rc == L.M3_ERR_UNSUPPORTED
     y_ref = m(u)  # autograd path
     assert rel_err(y.float().cpu().numpy(), y_ref.detach().float().cpu().numpy()) < 2e-2
+
+
+PROLOGUE_CASES = [(cfg, Ln, 1 if Ln > 1000 else 2)
+                  for cfg in (dict(d_state=64, headdim=32), dict(d_state=64, headdim=64, rope_fraction=1.0),
+                              dict(d_state=16, headdim=32, rope_fraction=1.0),
+                              dict(d_state=12, headdim=32, rope_fraction=1.0))
+                  for Ln in (1, 33, 700, 4100)]
+# 40 x 16 = 640 (b, h) units: the 128-step tile kernel instead of the segment kernel
+PROLOGUE_CASES += [(dict(d_state=16, headdim=8, rope_fraction=1.0), 300, 40),
+                   (dict(d_state=64, headdim=8), 1000, 40)]
+
+
+@pytest.mark.parametrize("cfg,Ln,batch", PROLOGUE_CASES,
+                         ids=[f"{'_'.join(f'{k}{v}' for k, v in c.items())}-L{n}-b{b}" for c, n, b in PROLOGUE_CASES])
+def test_prologue_scalars_and_angles_match_fp64(cfg, Ln, batch):
+    """m3_layer_prologue's DT, ADT, trap and cumulative angles (continuing from an angle
+    state) against the PyTorch prologue of layer.py:206-244 evaluated in float64, for 16,
+    32, 8 and 6 angles per head, lengths across the 32-step slabs and sequence segments of
+    the segment kernel (few (b, h) units) and across the tiles of the tile kernel (many).
+    Tolerance rel 1e-5 (fp32 sums)."""
+    import torch.nn.functional as F
+    from mamba3_ssm import Mamba3
+    torch.manual_seed(0)
+    m = Mamba3(d_model=64, expand=2, **cfg).to(DEV)
+    H, S, di = m.nheads, m.num_rope_angles, m.d_inner
+    gen = torch.Generator().manual_seed(Ln)
+    u = torch.randn(batch, Ln, 64, generator=gen).to(DEV)
+    ang0 = torch.randn(batch, H, S, generator=gen).to(DEV)
+    with torch.no_grad():
+        zx = m.in_proj(u).contiguous()
+        import ctypes
+        from mamba3_ssm import _lib as L
+        vals = m._step_params()
+        dims = m._f32_cache[3]
+        f = dict(dtype=torch.float32, device=DEV)
+        ADT, DT, trap = (torch.empty(batch, Ln, H, **f) for _ in range(3))
+        ang = torch.empty(batch, Ln, H, S, **f)
+        a = L.pack(zx, *vals[:5], ang0, None, None, ADT, DT, trap, ang)
+        L.check(L.load().m3_layer_prologue(ctypes.byref(dims), *a.ptrs, torch.cuda.current_stream().cuda_stream),
+                "m3_layer_prologue")
+        z64 = zx.double()
+        off = 2 * di + 2 * m.d_state * m.mimo_rank * m.num_bc_heads
+        dd_dt, dd_A, tr = z64[..., off:off + H], z64[..., off + H:off + 2 * H], z64[..., off + 2 * H:off + 3 * H]
+        ang_raw = z64[..., off + 3 * H:off + 3 * H + S]
+        A = -F.softplus(dd_A).clamp(max=-m.A_floor)
+        DT_ref = F.softplus(dd_dt + m.dt_bias.double())
+        ang_ref = ang0.double().unsqueeze(1) + torch.cumsum(ang_raw.unsqueeze(2) * DT_ref.unsqueeze(-1), dim=1)
+    assert rel_err(DT.cpu().numpy(), DT_ref.cpu().numpy()) < 1e-5
+    assert rel_err(ADT.cpu().numpy(), (A * DT_ref).cpu().numpy()) < 1e-5
+    assert rel_err(trap.cpu().numpy(), tr.cpu().numpy()) < 1e-6
+    assert rel_err(ang.cpu().numpy(), ang_ref.cpu().numpy()) < 1e-5
