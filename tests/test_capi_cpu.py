@@ -72,6 +72,79 @@ def test_host_validation_errors(lib):
     assert rc == 1 and b"dims" in lib.m3_last_error_string()
 
 
+def _view(shape, code, data=16):
+    """A descriptor of a contiguous tensor at a fake address (never dereferenced: every case
+    below fails, or finishes, on the host before any device access)."""
+    from mamba3_ssm import _lib
+    m = _lib.M3Tensor()
+    m.data, m.dtype, m.ndim = data, code, len(shape)
+    st = 1
+    for i in range(len(shape) - 1, -1, -1):
+        m.shape[i], m.stride[i] = shape[i], st
+        st *= max(shape[i], 1)
+    return m
+
+
+def test_mimo_layer_scan_and_prologue_host_validation(lib):
+    """m3_mimo_layer_scan_fwd and m3_layer_prologue reject bad arguments on the host: no
+    dims, inconsistent dims, a gate flag other than 0 / 1, B_proj without C_proj, and more
+    than one B / C group (M3_ERR_UNSUPPORTED); an empty sequence without states is a no-op."""
+    from mamba3_ssm import _lib
+    f32, bf = _lib.M3_FLOAT32, _lib.M3_BFLOAT16
+    B, L, H, P, D, R, S = 2, 0, 4, 8, 16, 2, 4
+    dp = 2 * H * P + 2 * D * R + 3 * H + S
+
+    def dims(G=1):
+        d = _lib.M3LayerDims()
+        d.d_model, d.d_inner, d.nheads, d.headdim, d.d_state = H * P // 2, H * P, H, P, D
+        d.ngroups, d.mimo_rank, d.num_rope_angles, d.rope_split = G, R, S, 2 * S
+        d.A_floor, d.norm_eps = 1e-4, 1e-5
+        return d
+
+    def args(G=1):
+        dpg = 2 * H * P + 2 * D * R * G + 3 * H + S
+        ins = [_view((B, L, dpg), bf), _view((B, L, H), f32), _view((B, L, H), f32), _view((B, L, H), f32),
+               _view((B, L, H, S), f32), _view((H, R, D), f32), _view((H, R, D), f32), _view((D,), f32),
+               _view((D,), f32), _view((H,), f32), _view((H, R, P), f32), _view((H, R, P), f32)]
+        return ins
+
+    null = _lib.M3Tensor()
+
+    def call(d, ins, gate):
+        refs = [ctypes.byref(t) for t in ins] + [ctypes.byref(null)] * 2
+        out = _view((B, L, H, P), bf)
+        return lib.m3_mimo_layer_scan_fwd(d, *refs, gate, ctypes.byref(out), ctypes.byref(null), ctypes.byref(null),
+                                          None, 0, None)
+
+    assert call(None, args(), 1) == _lib.M3_ERR_INVALID_ARGUMENT
+    assert b"dims: missing" in lib.m3_last_error_string()
+    assert call(ctypes.byref(_lib.M3LayerDims()), args(), 1) == _lib.M3_ERR_INVALID_ARGUMENT
+    assert b"inconsistent" in lib.m3_last_error_string()
+    assert call(ctypes.byref(dims()), args(), 2) == _lib.M3_ERR_INVALID_ARGUMENT
+    assert b"gate" in lib.m3_last_error_string()
+    bad = args()
+    bad[5] = _view((H, R, D + 1), f32)
+    assert call(ctypes.byref(dims()), bad, 1) == _lib.M3_ERR_INVALID_ARGUMENT
+    assert b"B_bias" in lib.m3_last_error_string()
+    assert call(ctypes.byref(dims(G=H)), args(G=H), 1) == _lib.M3_ERR_UNSUPPORTED
+    assert b"one B / C group" in lib.m3_last_error_string()
+    assert call(ctypes.byref(dims()), args(), 1) == _lib.M3_OK  # empty sequence, no states
+
+    # the prologue: B_proj and C_proj both present or both absent
+    zx = _view((B, L, dp), bf)
+    bc = _view((B, L, R, H, D), bf)
+    sc = [_view((B, L, H), f32) for _ in range(3)] + [_view((B, L, H, S), f32)]
+    pars = [_view((H,), f32), _view((H, R, D), f32), _view((H, R, D), f32), _view((D,), f32), _view((D,), f32)]
+    rc = lib.m3_layer_prologue(ctypes.byref(dims()), ctypes.byref(zx), *[ctypes.byref(t) for t in pars],
+                               ctypes.byref(null), ctypes.byref(bc), ctypes.byref(null),
+                               *[ctypes.byref(t) for t in sc], None)
+    assert rc == _lib.M3_ERR_INVALID_ARGUMENT and b"C_proj: missing" in lib.m3_last_error_string()
+    rc = lib.m3_layer_prologue(ctypes.byref(dims()), ctypes.byref(zx), *[ctypes.byref(t) for t in pars],
+                               ctypes.byref(null), ctypes.byref(null), ctypes.byref(null),
+                               *[ctypes.byref(t) for t in sc], None)
+    assert rc == _lib.M3_OK  # scalars and angles only, empty sequence
+
+
 def test_cpu_tensors_are_rejected():
     from mamba3_ssm import ssm_scan_siso, ssm_scan_mimo
     x = torch.randn(1, 4, 2, 8)
