@@ -1834,7 +1834,8 @@ static int grp_dispatch(const MimoParams& p, const GrpArgs& g, const MimoGrpPara
     case 16: rc = run_fused_grp<T, 16>(p, g, zx, q.s_zb, q.s_zl, ws, s); break;
     default: break;
   }
-  if (rc == M3_ERR_UNSUPPORTED) return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: tensor maps unavailable");
+  if (rc == M3_ERR_UNSUPPORTED)
+    return fail(M3_ERR_UNSUPPORTED, "mimo layer scan: too many chunks, or a tensor map could not be made");
   return rc;
 }
 
