@@ -109,14 +109,23 @@ def _sd(module):
     return {"w." + k: _np(v) for k, v in module.state_dict().items()}
 
 
-def gen_layer(name, cfg, batch, L, dtype, seed_w, seed_x, grad):
+def gen_layer(name, cfg, batch, L, dtype, seed_w, seed_x, grad, perturb=False):
     """Mamba3.forward (layer.py:168-266) at default init from torch.manual_seed(seed_w),
     optional backward with dy ~ N(0,1), and the token-by-token step() replay of the
-    first few positions from a zero cache (layer.py:272-374, 380-412)."""
+    first few positions from a zero cache (layer.py:272-374, 380-412). With ``perturb``
+    the parameters that init leaves constant (B_bias, C_bias and the B / C norm weights
+    are all ones, D ones) get distinct seeded values, so that a fixture tells heads,
+    ranks and state columns apart."""
     import torch
     from mamba3_ssm.layer import Mamba3
     torch.manual_seed(seed_w)
     m = Mamba3(**cfg)
+    if perturb:
+        pg = torch.Generator().manual_seed(seed_w + 1000)
+        with torch.no_grad():
+            for p in (m.B_bias, m.C_bias, m.B_norm.weight, m.C_norm.weight):
+                p.copy_(1.0 + 0.5 * torch.randn(p.shape, generator=pg))
+            m.D.copy_(torch.randn(m.D.shape, generator=pg))
     if dtype != torch.float32:
         m = m.to(dtype)
     gen = torch.Generator().manual_seed(seed_x)
@@ -189,7 +198,19 @@ def gen_lm(name, mcfg, batch, L, n_step, dtype, seed_w, seed_x):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", default="", help="comma-separated fixture names (without .npz) to write")
     args = ap.parse_args()
+    only = set(filter(None, args.only.split(",")))
+
+    def sel(fn):
+        def run(name, *a, **k):
+            if not only or name[:-4] in only:
+                fn(name, *a, **k)
+        return run
+
+    g = globals()
+    gen_siso_op, gen_mimo_op, gen_layer, gen_lm = (sel(g[n]) for n in ("gen_siso_op", "gen_mimo_op", "gen_layer",
+                                                                        "gen_lm"))
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.ref)
     import torch
@@ -219,6 +240,10 @@ def main():
     c2 = dict(d_model=256, d_state=64, expand=2, headdim=32, is_mimo=True, mimo_rank=4)
     gen_layer("layer_c2_mimo_bf16.npz", c2, 2, 32, bf16, 0, 1238, grad=True)
     gen_layer("layer_siso_bf16.npz", dict(d_model=128, d_state=64, expand=2, headdim=64), 2, 48, bf16, 3, 1239, grad=True)
+    # distinct per-head / per-rank / per-column biases, norm weights and D
+    gen_layer("layer_siso_f32_params.npz", small, 2, 40, f32, 10, 1243, grad=True, perturb=True)
+    gen_layer("layer_mimo_f32_params.npz", dict(small, is_mimo=True, mimo_rank=2, rope_fraction=1.0), 2, 40, f32,
+              11, 1244, grad=True, perturb=True)
     # language models
     lm_siso = dict(d_model=64, n_layer=2, vocab_size=300,
                    ssm_cfg=dict(d_state=32, expand=2, headdim=32, is_mimo=False))

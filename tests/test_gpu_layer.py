@@ -31,8 +31,10 @@ def _layer(g):
     return m.to(DEV)
 
 
+# the *_params fixtures carry distinct per-head / per-rank / per-column B / C biases, norm
+# weights and D (init leaves them constant), so that they tell heads, ranks and columns apart
 LAYERS = ["layer_c1_siso_f32", "layer_siso_f32_grad", "layer_siso_rope1_f32", "layer_mimo_f32_grad",
-          "layer_c2_mimo_bf16", "layer_siso_bf16"]
+          "layer_c2_mimo_bf16", "layer_siso_bf16", "layer_siso_f32_params", "layer_mimo_f32_params"]
 
 
 def _grad_bar(g, name, tol):

@@ -56,7 +56,8 @@ def _cfg(g, prefix):
 
 
 @pytest.mark.parametrize("name", ["layer_c1_siso_f32", "layer_siso_f32_grad", "layer_siso_rope1_f32",
-                                  "layer_mimo_f32_grad", "layer_c2_mimo_bf16", "layer_siso_bf16"])
+                                  "layer_mimo_f32_grad", "layer_c2_mimo_bf16", "layer_siso_bf16",
+                                  "layer_siso_f32_params", "layer_mimo_f32_params"])
 def test_layer_oracle_matches_reference(name):
     g = load_golden(name)
     dims = O.LayerDims(**_cfg(g, "cfg."))
@@ -141,7 +142,8 @@ def test_c_restatement_matches_reference(name):
     assert rel_err(y, g["y"]) < (2e-2 if str(g["dtype"]) == "bfloat16" else 1e-5)
 
 
-@pytest.mark.parametrize("name", ["layer_siso_f32_grad", "layer_mimo_f32_grad", "layer_c2_mimo_bf16"])
+@pytest.mark.parametrize("name", ["layer_siso_f32_grad", "layer_mimo_f32_grad", "layer_c2_mimo_bf16",
+                                  "layer_siso_f32_params", "layer_mimo_f32_params"])
 def test_layer_adjoint_matches_reference(name):
     """The oracle's layer adjoint (mamba3_forward_backward) against the gradients autograd
     returned through the reference's Mamba3.forward (fixtures recorded from the reference)."""
