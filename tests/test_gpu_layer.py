@@ -244,8 +244,11 @@ FUSED_SHAPES = [
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("cfg", FUSED_SHAPES, ids=lambda c: "_".join(f"{k}{v}" for k, v in c.items()))
 def test_fused_forward_equals_autograd_forward(cfg, dtype):
-    """Inference forward (fused kernels) == training forward (PyTorch prologue) on the same
-    weights and inputs; bf16 layers feed the scan bf16 B / C in the fused path."""
+    """Inference forward == autograd forward on the same weights and inputs. Inference: for a
+    one-group MIMO layer the group-row scan (B / C formed inside the scan, gate fused), else
+    the prologue with per-head B / C (bf16 for bf16 layers), the scan and the gate. Autograd:
+    the prologue with per-head B / C, the scan that keeps its states for the backward, the
+    gate (layer._LayerCoreFn)."""
     from mamba3_ssm import Mamba3
     torch.manual_seed(0)
     try:
