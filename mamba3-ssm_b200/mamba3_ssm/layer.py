@@ -1,9 +1,12 @@
 """Mamba3 mixer with the constructor, parameters (names, shapes, init order), forward,
 step and allocate_inference_cache of the reference's ``mamba3_ssm/layer.py`` (:61-412).
 
-* ``forward`` keeps the reference's prologue (in_proj split, softplus/clamp, RMSNorm + bias
-  of B/C, cumulative RoPE angles) and epilogue (silu gate, out_proj) and runs the scan
-  through ``ops.ssm_scan_siso`` / ``ops.ssm_scan_mimo`` (sm_100a kernels, with backward).
+* ``forward`` runs in_proj and out_proj (cuBLAS) around fused kernels for everything between
+  them (softplus / clamp, RMSNorm + bias + RoPE of B / C, the angle cumsum, the scan, the silu
+  gate), with their backward kernels under autograd; a one-group MIMO layer's inference
+  forward forms B / C inside the scan (``m3_mimo_layer_scan_fwd``). Continuing from, or
+  returning, a decode cache under autograd keeps the reference's PyTorch prologue around the
+  scan kernels.
 * ``step`` runs everything between in_proj and out_proj of one decode step
   (layer.py:298-371) as a single fused kernel (``m3_siso_step`` / ``m3_mimo_step``).
   Like the reference it returns new state tensors and leaves its inputs untouched.
@@ -212,10 +215,12 @@ class Mamba3(nn.Module):
         return (out, new) if return_cache else out
 
     def _forward_fused(self, u: torch.Tensor, cache=None, want_cache: bool = False):
-        """Inference forward: in_proj, the fused prologue kernel (m3_layer_prologue: dt /
-        decay / trap, RMSNorm + bias + RoPE of B and C per head, the angle cumsum), the scan,
-        the fused silu gate (m3_silu_gate), out_proj. bf16 layers give the scan bf16 B / C
-        (the tensor-core path); other dtypes keep them in fp32."""
+        """Inference forward: in_proj, then for a one-group MIMO layer the scalar prologue and
+        the group-row scan with the gate fused (_forward_mimo_rows); otherwise the fused
+        prologue kernel (m3_layer_prologue: dt / decay / trap, RMSNorm + bias + RoPE of B and C
+        per head, the angle cumsum), the scan and the fused silu gate (m3_silu_gate); out_proj.
+        bf16 layers give the scan bf16 B / C (the tensor-core path); other dtypes keep them in
+        fp32."""
         batch, Ln, _ = u.shape
         R, Ds, H, P, S = self.mimo_rank, self.d_state, self.nheads, self.headdim, self.num_rope_angles
         zx = self.in_proj(u)
